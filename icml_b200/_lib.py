@@ -1,0 +1,91 @@
+"""ctypes binding of the in-tree libpgf.so (declarations in include/pgf.h).
+
+There is no fallback: if the library is missing or cannot be loaded, every operator raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p, c_char_p
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libpgf.so")
+
+_lock = threading.Lock()
+_lib = None
+
+P = c_void_p
+I64 = c_int64
+
+
+class Epilogue(ctypes.Structure):
+    """pgf_epilogue of include/pgf.h."""
+    _fields_ = [
+        ("kind", c_int), ("alpha", c_float), ("bias", c_void_p),
+        ("aux", c_void_p), ("aux_dtype", c_int), ("ld_aux", c_int64),
+        ("aux_out", c_void_p), ("aux_out_dtype", c_int), ("ld_aux_out", c_int64),
+        ("addend", c_void_p), ("addend_dtype", c_int), ("ld_addend", c_int64),
+        ("accumulate", c_int),
+    ]
+
+
+# name -> (restype, argtypes); mirrors include/pgf.h
+SIGNATURES = {
+    "pgf_last_error": (c_char_p, []),
+    "pgf_version": (c_int, []),
+    "pgf_rmsnorm_fwd": (c_int, [P, P, P, I64, I64, c_float, c_int, P]),
+    "pgf_rmsnorm_bwd_workspace": (c_size_t, [I64, I64]),
+    "pgf_rmsnorm_bwd": (c_int, [P, P, P, P, P, c_int, I64, I64, c_float, c_int, P, c_size_t, P]),
+    "pgf_embedding_fwd": (c_int, [P, P, P, I64, I64, I64, c_int, P]),
+    "pgf_embedding_bwd_workspace": (c_size_t, [I64, I64, I64]),
+    "pgf_embedding_bwd": (c_int, [P, P, P, c_int, I64, I64, I64, c_int, P, c_size_t, P]),
+    "pgf_gemm": (c_int, [I64, I64, I64, P, c_int, I64, c_int, P, c_int, I64, c_int, P, c_int, I64,
+                         ctypes.POINTER(Epilogue), P]),
+    "pgf_colsum_workspace": (c_size_t, [I64, I64]),
+    "pgf_colsum": (c_int, [P, c_int, I64, I64, I64, P, c_int, P, c_size_t, P]),
+    "pgf_ffn_workspace": (c_size_t, [I64, I64, I64, I64, c_int, c_int]),
+    "pgf_ffn_fwd": (c_int, [P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P, c_size_t, P]),
+    "pgf_ffn_bwd": (c_int, [P, P, P, P, P, P, P, P, P, P, c_int, I64, I64, I64, I64, c_int, c_int,
+                            P, c_size_t, P]),
+    "pgf_lm_head_workspace": (c_size_t, [I64, I64, I64, c_int]),
+    "pgf_lm_head_fwd": (c_int, [P, P, P, I64, I64, I64, c_int, P, c_size_t, P]),
+    "pgf_lm_head_bwd": (c_int, [P, P, P, P, P, c_int, I64, I64, I64, c_int, P, c_size_t, P]),
+    "pgf_lm_head_ce_workspace": (c_size_t, [I64, I64, I64, c_int]),
+    "pgf_lm_head_ce_fwd": (c_int, [P, P, P, P, P, I64, I64, I64, c_int, P, c_size_t, P]),
+    "pgf_lm_head_ce_bwd": (c_int, [P, P, P, P, c_float, P, P, c_int, I64, I64, I64, c_int, P,
+                                   c_size_t, P]),
+    "pgf_ssm_workspace": (c_size_t, [I64, I64, I64, I64, c_int, c_int]),
+    "pgf_ssm_fwd": (c_int, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P,
+                            c_size_t, P]),
+    "pgf_ssm_bwd": (c_int, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, I64, I64,
+                            I64, I64, c_int, c_int, P, c_size_t, P]),
+}
+
+
+def lib():
+    """Load libpgf.so once and declare every exported symbol's signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m icml_b200.build`")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().pgf_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed (code {rc}): {last_error()}")

@@ -1,0 +1,437 @@
+// FFN and LM-head operators composed from the dense-product engine
+// (pgf_ffn.py:34-117, 183-307; pgf_lm_head.py:14-130; CE of test_multi_layer_grads.py:74-86).
+//
+// Rows (tokens) are processed in tiles whose scratch is bounded by the tile, not by the number
+// of rows, which is the block-streaming of the reference on the GPU.  In bf16 mode the fp32
+// master weights are converted once per call into bf16 operand copies in the workspace.
+#include "gemm.cuh"
+
+#include <math.h>
+
+namespace pgf {
+
+static const int64_t kTileBytes = int64_t(64) << 20;  // scratch budget for one row tile
+
+static int64_t ffn_tile_rows(int64_t rows, int64_t d_hidden, int backward) {
+  // hidden activations (and the pre-activation in backward) of one tile, in float32
+  int64_t per_row = d_hidden * 4 * (backward ? 2 : 1);
+  int64_t t = kTileBytes / (per_row > 0 ? per_row : 1);
+  t = (t / 128) * 128;
+  if (t < 128) t = 128;
+  return rows < t ? rows : t;
+}
+
+struct FfnWs {
+  void* h;      // tile hidden activations (dtype)
+  float* z;     // tile pre-activation (backward)
+  __nv_bfloat16 *W1b, *W2b;  // bf16 operand copies
+  void* cs;     // colsum scratch
+  size_t cs_bytes;
+};
+
+static size_t ffn_ws_bytes(int64_t rows, int64_t d_in, int64_t d_h, int64_t d_out, int dtype, int backward) {
+  int64_t tr = ffn_tile_rows(rows < 1 ? 1 : rows, d_h, backward);
+  size_t es = dtype ? 2 : 4;
+  size_t b = Workspace::round(size_t(tr) * d_h * es);
+  if (backward) b += Workspace::round(size_t(tr) * d_h * 4);
+  if (dtype) b += Workspace::round(size_t(d_h) * d_in * 2) + Workspace::round(size_t(d_out) * d_h * 2);
+  if (backward) {
+    size_t c1 = colsum_ws(tr, d_h), c2 = colsum_ws(tr, d_out);
+    b += Workspace::round(c1 > c2 ? c1 : c2);
+  }
+  return b + 1024;
+}
+
+static int ffn_carve(Workspace& W, FfnWs& f, int64_t rows, int64_t d_in, int64_t d_h, int64_t d_out,
+                     int dtype, int backward) {
+  int64_t tr = ffn_tile_rows(rows, d_h, backward);
+  size_t es = dtype ? 2 : 4;
+  f.h = W.take<char>(size_t(tr) * d_h * es);
+  f.z = backward ? W.take<float>(size_t(tr) * d_h) : nullptr;
+  f.W1b = dtype ? W.take<__nv_bfloat16>(size_t(d_h) * d_in) : nullptr;
+  f.W2b = dtype ? W.take<__nv_bfloat16>(size_t(d_out) * d_h) : nullptr;
+  if (backward) {
+    size_t c1 = colsum_ws(tr, d_h), c2 = colsum_ws(tr, d_out);
+    f.cs_bytes = c1 > c2 ? c1 : c2;
+    f.cs = W.take<char>(f.cs_bytes);
+  } else {
+    f.cs = nullptr;
+    f.cs_bytes = 0;
+  }
+  if (!f.h || (backward && (!f.z || !f.cs)) || (dtype && (!f.W1b || !f.W2b))) {
+    set_error("ffn: workspace too small (%zu)", W.cap);
+    return PGF_ERR_WORKSPACE;
+  }
+  return PGF_OK;
+}
+
+static int act_epi(int activation, int backward) {
+  if (activation == PGF_ACT_GELU) return backward ? PGF_EPI_DGELU : PGF_EPI_GELU;
+  return backward ? PGF_EPI_DRELU : PGF_EPI_RELU;
+}
+
+static Gemm mk(int64_t M, int64_t N, int64_t K, const void* A, int abf, int64_t lda, int at,
+               const void* B, int bbf, int64_t ldb, int bt, void* D, int dbf, int64_t ldd) {
+  Gemm g;
+  g.M = M; g.N = N; g.K = K;
+  g.A = A; g.a_bf16 = abf; g.lda = lda; g.a_trans = at;
+  g.B = B; g.b_bf16 = bbf; g.ldb = ldb; g.b_trans = bt;
+  g.D = D; g.d_bf16 = dbf; g.ldd = ldd;
+  g.epi = epi_default();
+  return g;
+}
+
+}  // namespace pgf
+
+using namespace pgf;
+
+extern "C" size_t pgf_ffn_workspace(int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out,
+                                    int dtype, int backward) {
+  return ffn_ws_bytes(rows, d_in, d_hidden, d_out, dtype, backward);
+}
+
+extern "C" int pgf_ffn_fwd(const void* x, const float* W1, const float* b1, const float* W2,
+                           const float* b2, void* y, int64_t rows, int64_t d_in, int64_t d_hidden,
+                           int64_t d_out, int activation, int dtype, void* ws, size_t ws_bytes,
+                           pgf_stream_t stream) {
+  PGF_CHECK_ARG(x && W1 && b1 && W2 && b2 && y, "ffn_fwd: null pointer");
+  PGF_CHECK_ARG(activation == PGF_ACT_GELU || activation == PGF_ACT_RELU, "ffn_fwd: bad activation");
+  PGF_CHECK_ARG(dtype == 0 || dtype == 1, "ffn_fwd: bad dtype");
+  if (rows == 0) return PGF_OK;
+  cudaStream_t s = as_stream(stream);
+  Workspace W(ws, ws_bytes);
+  FfnWs f;
+  PGF_TRY(ffn_carve(W, f, rows, d_in, d_hidden, d_out, dtype, 0));
+  const void* w1 = W1;
+  const void* w2 = W2;
+  if (dtype) {
+    PGF_TRY(to_bf16(W1, f.W1b, d_hidden * d_in, s));
+    PGF_TRY(to_bf16(W2, f.W2b, d_out * d_hidden, s));
+    w1 = f.W1b;
+    w2 = f.W2b;
+  }
+  const int64_t tr = ffn_tile_rows(rows, d_hidden, 0);
+  const size_t es = dtype ? 2 : 4;
+  for (int64_t r = 0; r < rows; r += tr) {
+    const int64_t m = rows - r < tr ? rows - r : tr;
+    const char* xt = static_cast<const char*>(x) + r * d_in * es;
+    char* yt = static_cast<char*>(y) + r * d_out * es;
+    Gemm g1 = mk(m, d_hidden, d_in, xt, dtype, d_in, 0, w1, dtype, d_in, 0, f.h, dtype, d_hidden);
+    g1.epi.bias = b1;
+    g1.epi.kind = act_epi(activation, 0);
+    PGF_TRY(run_gemm(g1, s));
+    Gemm g2 = mk(m, d_out, d_hidden, f.h, dtype, d_hidden, 0, w2, dtype, d_hidden, 0, yt, dtype, d_out);
+    g2.epi.bias = b2;
+    PGF_TRY(run_gemm(g2, s));
+  }
+  return PGF_OK;
+}
+
+extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const float* b1,
+                           const float* W2, float* gW1, float* gb1, float* gW2, float* gb2,
+                           void* gx, int accumulate, int64_t rows, int64_t d_in, int64_t d_h,
+                           int64_t d_out, int activation, int dtype, void* ws, size_t ws_bytes,
+                           pgf_stream_t stream) {
+  PGF_CHECK_ARG(x && g && W1 && b1 && W2 && gW1 && gb1 && gW2 && gb2, "ffn_bwd: null pointer");
+  PGF_CHECK_ARG(activation == PGF_ACT_GELU || activation == PGF_ACT_RELU, "ffn_bwd: bad activation");
+  PGF_CHECK_ARG(dtype == 0 || dtype == 1, "ffn_bwd: bad dtype");
+  cudaStream_t s = as_stream(stream);
+  if (rows == 0) {
+    if (!accumulate) {
+      PGF_CUDA(cudaMemsetAsync(gW1, 0, d_h * d_in * 4, s));
+      PGF_CUDA(cudaMemsetAsync(gb1, 0, d_h * 4, s));
+      PGF_CUDA(cudaMemsetAsync(gW2, 0, d_out * d_h * 4, s));
+      PGF_CUDA(cudaMemsetAsync(gb2, 0, d_out * 4, s));
+    }
+    return PGF_OK;
+  }
+  Workspace W(ws, ws_bytes);
+  FfnWs f;
+  PGF_TRY(ffn_carve(W, f, rows, d_in, d_h, d_out, dtype, 1));
+  const void* w1 = W1;
+  const void* w2 = W2;
+  int wbf = 0;
+  if (dtype) {
+    PGF_TRY(to_bf16(W1, f.W1b, d_h * d_in, s));
+    PGF_TRY(to_bf16(W2, f.W2b, d_out * d_h, s));
+    w1 = f.W1b;
+    w2 = f.W2b;
+    wbf = 1;
+  }
+  const int64_t tr = ffn_tile_rows(rows, d_h, 1);
+  const size_t es = dtype ? 2 : 4;
+  for (int64_t r = 0; r < rows; r += tr) {
+    const int64_t m = rows - r < tr ? rows - r : tr;
+    const int acc = (r > 0) || accumulate;
+    const char* xt = static_cast<const char*>(x) + r * d_in * es;
+    const char* gt = static_cast<const char*>(g) + r * d_out * es;
+    // z = x W1^T + b1 (kept in float32 for act'), h = act(z) (activation dtype)
+    Gemm g1 = mk(m, d_h, d_in, xt, dtype, d_in, 0, w1, wbf, d_in, 0, f.h, dtype, d_h);
+    g1.epi.bias = b1;
+    g1.epi.kind = act_epi(activation, 0);
+    g1.epi.aux_out = f.z;
+    g1.epi.aux_out_dtype = 0;
+    g1.epi.ld_aux_out = d_h;
+    PGF_TRY(run_gemm(g1, s));
+    // grad_W2 (+)= g^T h   (d_out x d_h, K = rows)
+    Gemm g2 = mk(d_out, d_h, m, gt, dtype, d_out, 1, f.h, dtype, d_h, 1, gW2, 0, d_h);
+    g2.epi.accumulate = acc;
+    PGF_TRY(run_gemm(g2, s));
+    PGF_TRY(colsum(gt, dtype, m, d_out, d_out, gb2, acc, f.cs, f.cs_bytes, s));
+    // grad_z = (g W2) * act'(z), written over h (no longer needed)
+    Gemm g3 = mk(m, d_h, d_out, gt, dtype, d_out, 0, w2, wbf, d_h, 1, f.h, dtype, d_h);
+    g3.epi.kind = act_epi(activation, 1);
+    g3.epi.aux = f.z;
+    g3.epi.aux_dtype = 0;
+    g3.epi.ld_aux = d_h;
+    PGF_TRY(run_gemm(g3, s));
+    // grad_W1 (+)= grad_z^T x   (d_h x d_in, K = rows)
+    Gemm g4 = mk(d_h, d_in, m, f.h, dtype, d_h, 1, xt, dtype, d_in, 1, gW1, 0, d_in);
+    g4.epi.accumulate = acc;
+    PGF_TRY(run_gemm(g4, s));
+    PGF_TRY(colsum(f.h, dtype, m, d_h, d_h, gb1, acc, f.cs, f.cs_bytes, s));
+    if (gx) {
+      // grad_x = grad_z W1
+      char* gxt = static_cast<char*>(gx) + r * d_in * es;
+      Gemm g5 = mk(m, d_in, d_h, f.h, dtype, d_h, 0, w1, wbf, d_in, 1, gxt, dtype, d_in);
+      PGF_TRY(run_gemm(g5, s));
+    }
+  }
+  return PGF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// LM head
+// ---------------------------------------------------------------------------
+extern "C" size_t pgf_lm_head_workspace(int64_t T, int64_t V, int64_t d, int dtype) {
+  (void)T;
+  return dtype ? Workspace::round(size_t(V) * d * 2) + 256 : 256;
+}
+
+extern "C" int pgf_lm_head_fwd(const void* h, const float* W, float* logits, int64_t T, int64_t V,
+                               int64_t d, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(h && W && logits, "lm_head_fwd: null pointer");
+  cudaStream_t s = as_stream(stream);
+  const void* w = W;
+  if (dtype) {
+    Workspace Wk(ws, ws_bytes);
+    __nv_bfloat16* wb = Wk.take<__nv_bfloat16>(size_t(V) * d);
+    if (!wb) { set_error("lm_head_fwd: workspace too small"); return PGF_ERR_WORKSPACE; }
+    PGF_TRY(to_bf16(W, wb, V * d, s));
+    w = wb;
+  }
+  Gemm g = mk(T, V, d, h, dtype, d, 0, w, dtype, d, 0, logits, 0, V);
+  return run_gemm(g, s);
+}
+
+extern "C" int pgf_lm_head_bwd(const void* h, const float* g_logits, const float* W, float* grad_W,
+                               void* grad_h, int accumulate, int64_t T, int64_t V, int64_t d,
+                               int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(h && g_logits && W && grad_W, "lm_head_bwd: null pointer");
+  (void)ws; (void)ws_bytes;
+  cudaStream_t s = as_stream(stream);
+  Gemm g1 = mk(V, d, T, g_logits, 0, V, 1, h, dtype, d, 1, grad_W, 0, d);
+  g1.epi.accumulate = accumulate;
+  PGF_TRY(run_gemm(g1, s));
+  if (grad_h) {
+    Gemm g2 = mk(T, d, V, g_logits, 0, V, 0, W, 0, d, 1, grad_h, dtype, d);
+    PGF_TRY(run_gemm(g2, s));
+  }
+  return PGF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// LM head + cross entropy, tiled over (tokens x vocab)
+// ---------------------------------------------------------------------------
+namespace pgf {
+
+constexpr int64_t CE_VT = 8192;  // vocab columns per tile
+
+static int64_t ce_tile_rows(int64_t T) {
+  int64_t t = kTileBytes / (CE_VT * 4);  // float32 logits tile
+  t = (t / 128) * 128;
+  if (t < 128) t = 128;
+  return T < t ? T : t;
+}
+
+// Online log-sum-exp over one vocab tile: run_m/run_s hold the running max and sum of
+// exp(logit - max) of each row; tgt_logit receives the target's logit when it lies in the tile.
+__global__ void ce_tile_stats_kernel(const float* __restrict__ tile, int64_t rows, int64_t cols,
+                                     int64_t v0, const int64_t* __restrict__ targets,
+                                     float* __restrict__ run_m, float* __restrict__ run_s,
+                                     float* __restrict__ tgt_logit, int first) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float* row = tile + r * cols;
+  float mx = -INFINITY;
+  for (int64_t c = lane; c < cols; c += 32) mx = fmaxf(mx, row[c]);
+  mx = warp_max(mx);
+  float se = 0.f;
+  for (int64_t c = lane; c < cols; c += 32) se += expf(row[c] - mx);
+  se = warp_sum(se);
+  if (lane == 0) {
+    const int64_t tg = targets[r];
+    if (tg >= v0 && tg < v0 + cols) tgt_logit[r] = row[tg - v0];
+    if (first) {
+      run_m[r] = mx;
+      run_s[r] = se;
+    } else {
+      const float m0 = run_m[r];
+      const float m1 = fmaxf(m0, mx);
+      run_s[r] = run_s[r] * expf(m0 - m1) + se * expf(mx - m1);
+      run_m[r] = m1;
+    }
+  }
+}
+
+__global__ void ce_finish_kernel(const float* __restrict__ run_m, const float* __restrict__ run_s,
+                                 const float* __restrict__ tgt_logit, int64_t rows,
+                                 float* __restrict__ loss_rows, float* __restrict__ lse) {
+  const int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const float l = run_m[r] + logf(run_s[r]);
+  lse[r] = l;
+  loss_rows[r] = l - tgt_logit[r];
+}
+
+// g = (exp(logit - lse) - onehot) * scale, in place (float32) and as a bf16 copy when asked.
+__global__ void ce_grad_tile_kernel(float* __restrict__ tile, __nv_bfloat16* __restrict__ tile_bf,
+                                    int64_t rows, int64_t cols, int64_t v0,
+                                    const int64_t* __restrict__ targets, const float* __restrict__ lse,
+                                    float scale) {
+  const int64_t r = blockIdx.y;
+  const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows || c >= cols) return;
+  const int64_t o = r * cols + c;
+  float p = expf(tile[o] - lse[r]);
+  if (targets[r] == v0 + c) p -= 1.0f;
+  p *= scale;
+  tile[o] = p;
+  if (tile_bf) tile_bf[o] = __float2bfloat16_rn(p);
+}
+
+struct CeWs {
+  float* tile;
+  __nv_bfloat16* tile_bf;
+  __nv_bfloat16* Wb;
+  float *run_m, *run_s, *tgt;
+  float* gh32;  // float32 grad_h accumulator of a bf16 run
+};
+
+static size_t ce_ws_bytes(int64_t T, int64_t V, int64_t d, int dtype) {
+  int64_t tr = ce_tile_rows(T < 1 ? 1 : T);
+  size_t b = Workspace::round(size_t(tr) * CE_VT * 4);
+  if (dtype) b += Workspace::round(size_t(tr) * CE_VT * 2) + Workspace::round(size_t(V) * d * 2);
+  b += 3 * Workspace::round(size_t(tr) * 4);
+  if (dtype) b += Workspace::round(size_t(tr) * d * 4);
+  return b + 1024;
+}
+
+static int ce_carve(Workspace& W, CeWs& c, int64_t T, int64_t V, int64_t d, int dtype) {
+  int64_t tr = ce_tile_rows(T);
+  c.tile = W.take<float>(size_t(tr) * CE_VT);
+  c.tile_bf = dtype ? W.take<__nv_bfloat16>(size_t(tr) * CE_VT) : nullptr;
+  c.Wb = dtype ? W.take<__nv_bfloat16>(size_t(V) * d) : nullptr;
+  c.run_m = W.take<float>(tr);
+  c.run_s = W.take<float>(tr);
+  c.tgt = W.take<float>(tr);
+  c.gh32 = dtype ? W.take<float>(size_t(tr) * d) : nullptr;
+  if ((dtype && !c.gh32) || !c.tile || !c.run_m || !c.run_s || !c.tgt || (dtype && (!c.tile_bf || !c.Wb))) {
+    set_error("lm_head_ce: workspace too small");
+    return PGF_ERR_WORKSPACE;
+  }
+  return PGF_OK;
+}
+
+}  // namespace pgf
+
+extern "C" size_t pgf_lm_head_ce_workspace(int64_t T, int64_t V, int64_t d, int dtype) {
+  return ce_ws_bytes(T, V, d, dtype);
+}
+
+extern "C" int pgf_lm_head_ce_fwd(const void* h, const float* W, const int64_t* targets,
+                                  float* loss_rows, float* lse, int64_t T, int64_t V, int64_t d,
+                                  int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(h && W && targets && loss_rows && lse, "lm_head_ce_fwd: null pointer");
+  PGF_CHECK_ARG(dtype == 0 || dtype == 1, "lm_head_ce_fwd: bad dtype");
+  if (T == 0) return PGF_OK;
+  cudaStream_t s = as_stream(stream);
+  Workspace Wk(ws, ws_bytes);
+  CeWs c;
+  PGF_TRY(ce_carve(Wk, c, T, V, d, dtype));
+  const void* w = W;
+  if (dtype) {
+    PGF_TRY(to_bf16(W, c.Wb, V * d, s));
+    w = c.Wb;
+  }
+  const int64_t tr = ce_tile_rows(T);
+  const size_t es = dtype ? 2 : 4;
+  for (int64_t r = 0; r < T; r += tr) {
+    const int64_t m = T - r < tr ? T - r : tr;
+    const char* ht = static_cast<const char*>(h) + r * d * es;
+    for (int64_t v0 = 0; v0 < V; v0 += CE_VT) {
+      const int64_t nv = V - v0 < CE_VT ? V - v0 : CE_VT;
+      const char* wt = static_cast<const char*>(w) + v0 * d * es;
+      Gemm g = mk(m, nv, d, ht, dtype, d, 0, wt, dtype, d, 0, c.tile, 0, nv);
+      PGF_TRY(run_gemm(g, s));
+      ce_tile_stats_kernel<<<ceil_div(m, 8), 256, 0, s>>>(c.tile, m, nv, v0, targets + r, c.run_m,
+                                                         c.run_s, c.tgt, v0 == 0);
+      PGF_LAUNCH_CHECK();
+    }
+    ce_finish_kernel<<<ceil_div(m, 256), 256, 0, s>>>(c.run_m, c.run_s, c.tgt, m, loss_rows + r, lse + r);
+    PGF_LAUNCH_CHECK();
+  }
+  return PGF_OK;
+}
+
+extern "C" int pgf_lm_head_ce_bwd(const void* h, const float* W, const int64_t* targets,
+                                  const float* lse, float grad_scale, float* grad_W, void* grad_h,
+                                  int accumulate, int64_t T, int64_t V, int64_t d, int dtype,
+                                  void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(h && W && targets && lse && grad_W, "lm_head_ce_bwd: null pointer");
+  PGF_CHECK_ARG(dtype == 0 || dtype == 1, "lm_head_ce_bwd: bad dtype");
+  cudaStream_t s = as_stream(stream);
+  if (T == 0) {
+    if (!accumulate) PGF_CUDA(cudaMemsetAsync(grad_W, 0, size_t(V) * d * 4, s));
+    return PGF_OK;
+  }
+  Workspace Wk(ws, ws_bytes);
+  CeWs c;
+  PGF_TRY(ce_carve(Wk, c, T, V, d, dtype));
+  const void* w = W;
+  if (dtype) {
+    PGF_TRY(to_bf16(W, c.Wb, V * d, s));
+    w = c.Wb;
+  }
+  const int64_t tr = ce_tile_rows(T);
+  const size_t es = dtype ? 2 : 4;
+  for (int64_t r = 0; r < T; r += tr) {
+    const int64_t m = T - r < tr ? T - r : tr;
+    const char* ht = static_cast<const char*>(h) + r * d * es;
+    char* ght = grad_h ? static_cast<char*>(grad_h) + r * d * es : nullptr;
+    for (int64_t v0 = 0; v0 < V; v0 += CE_VT) {
+      const int64_t nv = V - v0 < CE_VT ? V - v0 : CE_VT;
+      const char* wt = static_cast<const char*>(w) + v0 * d * es;
+      Gemm g = mk(m, nv, d, ht, dtype, d, 0, wt, dtype, d, 0, c.tile, 0, nv);
+      PGF_TRY(run_gemm(g, s));
+      dim3 gg(ceil_div(nv, 256), unsigned(m));
+      ce_grad_tile_kernel<<<gg, 256, 0, s>>>(c.tile, c.tile_bf, m, nv, v0, targets + r, lse + r, grad_scale);
+      PGF_LAUNCH_CHECK();
+      const void* gt = dtype ? (const void*)c.tile_bf : (const void*)c.tile;
+      // grad_W[v0:v0+nv] (+)= G^T h_tile
+      Gemm gw = mk(nv, d, m, gt, dtype, nv, 1, ht, dtype, d, 1, grad_W + v0 * d, 0, d);
+      gw.epi.accumulate = (r > 0) || accumulate;
+      PGF_TRY(run_gemm(gw, s));
+      if (ght) {
+        // grad_h_tile (+)= G W_tile, summed over vocab tiles in float32
+        float* acc32 = dtype ? c.gh32 : reinterpret_cast<float*>(ght);
+        Gemm gh = mk(m, d, nv, gt, dtype, nv, 0, wt, dtype, d, 1, acc32, 0, d);
+        gh.epi.accumulate = v0 > 0;
+        PGF_TRY(run_gemm(gh, s));
+      }
+    }
+    if (ght && dtype) PGF_TRY(to_bf16(c.gh32, reinterpret_cast<__nv_bfloat16*>(ght), m * d, s));
+  }
+  return PGF_OK;
+}

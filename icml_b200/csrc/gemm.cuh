@@ -1,0 +1,69 @@
+// Internal dense-product interface shared by the composite operators.
+#pragma once
+#include "common.cuh"
+
+namespace pgf {
+
+struct Gemm {
+  int64_t M, N, K;
+  const void* A; int a_bf16; int64_t lda; int a_trans;
+  const void* B; int b_bf16; int64_t ldb; int b_trans;
+  void* D; int d_bf16; int64_t ldd;
+  pgf_epilogue epi;
+};
+
+static inline pgf_epilogue epi_default() {
+  pgf_epilogue e;
+  e.kind = PGF_EPI_NONE; e.alpha = 1.f; e.bias = nullptr;
+  e.aux = nullptr; e.aux_dtype = 0; e.ld_aux = 0;
+  e.aux_out = nullptr; e.aux_out_dtype = 0; e.ld_aux_out = 0;
+  e.addend = nullptr; e.addend_dtype = 0; e.ld_addend = 0;
+  e.accumulate = 0;
+  return e;
+}
+
+// D = epi(opA * opB^T); picks the tensor-core path when the operands allow it.
+int run_gemm(const Gemm& g, cudaStream_t s);
+// SIMT path (any dtype mix, any layout): the float32 reference-precision engine.
+int run_gemm_simt(const Gemm& g, cudaStream_t s);
+// tcgen05 path; returns PGF_ERR_UNSUPPORTED when the call does not fit it.
+int run_gemm_tc(const Gemm& g, cudaStream_t s);
+
+// out[n] (+)= sum_m X[m*ld+n] with `ws` >= colsum_ws(M, N) bytes.
+size_t colsum_ws(int64_t M, int64_t N);
+int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out, int accumulate,
+           void* ws, size_t ws_bytes, cudaStream_t s);
+
+// dst[i] = bf16(src[i]) (weights to the tensor-core operand type)
+int to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s);
+
+// Epilogue applied to one accumulator element.
+__device__ __forceinline__ void epi_store(const pgf_epilogue& e, void* D, int d_bf16, int64_t ldd,
+                                          int64_t m, int64_t n, float acc) {
+  float v = e.alpha * acc;
+  if (e.bias) v += e.bias[n];
+  switch (e.kind) {
+    case PGF_EPI_GELU:
+      if (e.aux_out) stv(e.aux_out, e.aux_out_dtype, m * e.ld_aux_out + n, v);
+      v = gelu_f(v);
+      break;
+    case PGF_EPI_RELU:
+      if (e.aux_out) stv(e.aux_out, e.aux_out_dtype, m * e.ld_aux_out + n, v);
+      v = v > 0.f ? v : 0.f;
+      break;
+    case PGF_EPI_DGELU:
+      v *= gelu_prime_f(ldv(e.aux, e.aux_dtype, m * e.ld_aux + n));
+      break;
+    case PGF_EPI_DRELU:
+      v *= ldv(e.aux, e.aux_dtype, m * e.ld_aux + n) > 0.f ? 1.f : 0.f;
+      break;
+    default:
+      break;
+  }
+  if (e.addend) v += ldv(e.addend, e.addend_dtype, m * e.ld_addend + n);
+  const int64_t o = m * ldd + n;
+  if (e.accumulate) v += reinterpret_cast<float*>(D)[o];
+  stv(D, d_bf16, o, v);
+}
+
+}  // namespace pgf

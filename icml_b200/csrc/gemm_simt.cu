@@ -1,0 +1,198 @@
+// SIMT dense product (float32 FMA on the CUDA cores) with the fused epilogues, column sums and
+// the public pgf_gemm / pgf_colsum entry points.
+//
+// The SIMT engine is the reference-precision path: float32 inputs are multiplied and summed in
+// float32, which keeps the float32 operators within the 1e-5 parity bound.  bf16 operands go to
+// the tcgen05 engine (gemm_tc.cu) when their shapes fit it.
+#include "gemm.cuh"
+
+namespace pgf {
+
+constexpr int SG_BM = 64, SG_BN = 64, SG_BK = 16, SG_THREADS = 256;
+
+__global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g) {
+  __shared__ __align__(16) float As[SG_BK][SG_BM + 4];
+  __shared__ __align__(16) float Bs[SG_BK][SG_BN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = int64_t(blockIdx.y) * SG_BM, n0 = int64_t(blockIdx.x) * SG_BN;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  for (int64_t k0 = 0; k0 < g.K; k0 += SG_BK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int li = tid + i * SG_THREADS;
+      int mm, kk;
+      if (!g.a_trans) { kk = li % SG_BK; mm = li / SG_BK; } else { mm = li % SG_BM; kk = li / SG_BM; }
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      float v = 0.f;
+      if (gm < g.M && gk < g.K)
+        v = ldv(g.A, g.a_bf16, g.a_trans ? gk * g.lda + gm : gm * g.lda + gk);
+      As[kk][mm] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int li = tid + i * SG_THREADS;
+      int nn, kk;
+      if (!g.b_trans) { kk = li % SG_BK; nn = li / SG_BK; } else { nn = li % SG_BN; kk = li / SG_BN; }
+      const int64_t gn = n0 + nn, gk = k0 + kk;
+      float v = 0.f;
+      if (gn < g.N && gk < g.K)
+        v = ldv(g.B, g.b_bf16, g.b_trans ? gk * g.ldb + gn : gn * g.ldb + gk);
+      Bs[kk][nn] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < SG_BK; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t m = m0 + ty * 4 + i;
+    if (m >= g.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t n = n0 + tx * 4 + j;
+      if (n < g.N) epi_store(g.epi, g.D, g.d_bf16, g.ldd, m, n, acc[i][j]);
+    }
+  }
+}
+
+int run_gemm_simt(const Gemm& g, cudaStream_t s) {
+  if (g.M == 0 || g.N == 0) return PGF_OK;
+  dim3 grid(ceil_div(g.N, SG_BN), ceil_div(g.M, SG_BM));
+  if (grid.y > 65535u) {
+    // split M into launches of at most 65535 row tiles
+    const int64_t rows_per = int64_t(65535) * SG_BM;
+    for (int64_t r = 0; r < g.M; r += rows_per) {
+      Gemm h = g;
+      h.M = (g.M - r) < rows_per ? (g.M - r) : rows_per;
+      const int64_t ea = g.a_bf16 ? 2 : 4, ed = g.d_bf16 ? 2 : 4;
+      h.A = static_cast<const char*>(g.A) + (g.a_trans ? r : r * g.lda) * ea;
+      h.D = static_cast<char*>(g.D) + r * g.ldd * ed;
+      if (h.epi.aux) h.epi.aux = static_cast<const char*>(g.epi.aux) + r * g.epi.ld_aux * (g.epi.aux_dtype ? 2 : 4);
+      if (h.epi.aux_out) h.epi.aux_out = static_cast<char*>(g.epi.aux_out) + r * g.epi.ld_aux_out * (g.epi.aux_out_dtype ? 2 : 4);
+      if (h.epi.addend) h.epi.addend = static_cast<const char*>(g.epi.addend) + r * g.epi.ld_addend * (g.epi.addend_dtype ? 2 : 4);
+      PGF_TRY(run_gemm_simt(h, s));
+    }
+    return PGF_OK;
+  }
+  gemm_simt_kernel<<<grid, SG_THREADS, 0, s>>>(g);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+int run_gemm(const Gemm& g, cudaStream_t s) {
+  int rc = run_gemm_tc(g, s);
+  if (rc != PGF_ERR_UNSUPPORTED) return rc;
+  clear_error();
+  return run_gemm_simt(g, s);
+}
+
+// ---------------------------------------------------------------------------
+// column sums, fixed two-level order
+// ---------------------------------------------------------------------------
+constexpr int CS_ROWS = 256;
+
+__global__ void colsum_part_kernel(const void* __restrict__ X, int bf16, int64_t M, int64_t N,
+                                   int64_t ld, float* __restrict__ part) {
+  const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const int64_t r0 = int64_t(blockIdx.y) * CS_ROWS;
+  const int64_t r1 = r0 + CS_ROWS < M ? r0 + CS_ROWS : M;
+  float s = 0.f;
+  for (int64_t r = r0; r < r1; ++r) s += ldv(X, bf16, r * ld + n);
+  part[int64_t(blockIdx.y) * N + n] = s;
+}
+
+__global__ void colsum_final_kernel(const float* __restrict__ part, int64_t nparts, int64_t N,
+                                    float* __restrict__ out, int accumulate) {
+  const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float s = 0.f;
+  for (int64_t p = 0; p < nparts; ++p) s += part[p * N + n];
+  out[n] = accumulate ? out[n] + s : s;
+}
+
+size_t colsum_ws(int64_t M, int64_t N) {
+  return Workspace::round(size_t(ceil_div(M < 1 ? 1 : M, CS_ROWS)) * size_t(N) * 4);
+}
+
+int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out, int accumulate,
+           void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (N == 0) return PGF_OK;
+  if (M == 0) {
+    if (!accumulate) PGF_CUDA(cudaMemsetAsync(out, 0, N * 4, s));
+    return PGF_OK;
+  }
+  const int64_t np = ceil_div(M, CS_ROWS);
+  if (size_t(np) * N * 4 > ws_bytes) { set_error("colsum: workspace too small"); return PGF_ERR_WORKSPACE; }
+  if (np > 65535) { set_error("colsum: too many rows"); return PGF_ERR_UNSUPPORTED; }
+  float* part = static_cast<float*>(ws);
+  colsum_part_kernel<<<dim3(ceil_div(N, 128), unsigned(np)), 128, 0, s>>>(X, bf16, M, N, ld, part);
+  PGF_LAUNCH_CHECK();
+  colsum_final_kernel<<<ceil_div(N, 128), 128, 0, s>>>(part, np, N, out, accumulate);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+__global__ void to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n) {
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (; i < n; i += stride) dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+int to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s) {
+  if (n == 0) return PGF_OK;
+  int blocks = ceil_div(n, 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  to_bf16_kernel<<<blocks, 256, 0, s>>>(src, dst, n);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+}  // namespace pgf
+
+using namespace pgf;
+
+extern "C" int pgf_gemm(int64_t M, int64_t N, int64_t K, const void* A, int a_dtype, int64_t lda,
+                        int a_trans, const void* B, int b_dtype, int64_t ldb, int b_trans, void* D,
+                        int d_dtype, int64_t ldd, const pgf_epilogue* epi, pgf_stream_t stream) {
+  PGF_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "gemm: negative size");
+  PGF_CHECK_ARG((M == 0 || N == 0 || K == 0) || (A && B), "gemm: null operand");
+  PGF_CHECK_ARG(D || M == 0 || N == 0, "gemm: null output");
+  PGF_CHECK_ARG((a_dtype == 0 || a_dtype == 1) && (b_dtype == 0 || b_dtype == 1) &&
+                    (d_dtype == 0 || d_dtype == 1),
+                "gemm: bad dtype");
+  Gemm g;
+  g.M = M; g.N = N; g.K = K;
+  g.A = A; g.a_bf16 = a_dtype; g.lda = lda; g.a_trans = a_trans;
+  g.B = B; g.b_bf16 = b_dtype; g.ldb = ldb; g.b_trans = b_trans;
+  g.D = D; g.d_bf16 = d_dtype; g.ldd = ldd;
+  g.epi = epi ? *epi : epi_default();
+  PGF_CHECK_ARG(!g.epi.accumulate || d_dtype == PGF_DTYPE_F32, "gemm: accumulate needs float32 D");
+  PGF_CHECK_ARG(!(g.epi.kind == PGF_EPI_DGELU || g.epi.kind == PGF_EPI_DRELU) || g.epi.aux,
+                "gemm: DGELU/DRELU need aux");
+  return run_gemm(g, as_stream(stream));
+}
+
+extern "C" size_t pgf_colsum_workspace(int64_t M, int64_t N) { return colsum_ws(M, N); }
+
+extern "C" int pgf_colsum(const void* X, int dtype, int64_t M, int64_t N, int64_t ld, float* out,
+                          int accumulate, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(out && (X || M == 0), "colsum: null pointer");
+  return colsum(X, dtype, M, N, ld, out, accumulate, ws, ws_bytes, as_stream(stream));
+}

@@ -1,0 +1,644 @@
+// Selective-scan layer of SingleLayerMambaPGF (train_singlemamba_optimized.py:88-472) on sm_100a.
+//
+// Layout: u, y, g: (Bsz, L, D); proj = u W_cat^T + b_cat: (Bsz, L, P = D + 2N) float32 with
+// columns [dt_in | B | C].  The recurrence h_t = exp(dt_t A) h_{t-1} + phi_1(dt_t A) B_t u_t runs
+// per (batch, channel, state); a thread owns NS = 4 states of one channel, four adjacent lanes
+// cover the N = 16 states, a CTA covers DC = 64 channels of one time chunk of Tc tokens.
+//
+// Forward (3 kernels): chunk summaries from a zero state (local end state + sum of dt, because
+// prod_t exp(dt_t A_n) = exp(A_n sum_t dt_t)), a sequential compose over chunks giving every
+// chunk's start state (the PGF boundary states), and the output pass re-running each chunk from
+// its start state.
+// Backward (3 kernels + 2 reductions): reverse chunk summaries of the adjoint
+// delta_h_t = exp(dt_{t+1} A) delta_h_{t+1} + delta_in_t C_t from a zero carry, a reverse compose
+// giving each chunk's incoming carry, and the main kernel: it re-runs the chunk from its boundary
+// state keeping checkpoints every SUB tokens in shared memory, then walks the sub-chunks in
+// reverse, re-running each forward into registers and stepping the adjoint back through it while
+// it forms every gradient of _pass2_block_direct_grad (:350-472).  Sums over channels (grad B,
+// grad C) and over tokens (grad A_log, D, scale) go through fixed-order partial buffers.
+#include "gemm.cuh"
+
+namespace pgf {
+
+constexpr int NST = 16;              // d_state
+constexpr int NQ = 4;                // threads per channel
+constexpr int NS = NST / NQ;         // states per thread
+constexpr int DC = 64;               // channels per CTA
+constexpr int SSM_THREADS = DC * NQ; // 256
+constexpr int SSM_WARPS = SSM_THREADS / 32;
+constexpr int SUB = 8;               // backward sub-chunk (register trajectory length)
+constexpr int TC_MAX = 128;
+
+struct SsmArgs {
+  const void* u; int u_bf16;
+  const float* proj;
+  const void* g; int g_bf16;
+  const float* A_log; const float* Dp; const float* scale;
+  int act;
+  int64_t Bsz, L, D, P, Tc, nC, G;
+  const float* h_init;
+  float* hloc; float* sdt; float* hC;
+  float* dloc; float* sdt2; float* dt0; float* X;
+  void* y; int y_bf16;
+  float* actp;
+  float* gstack; float* gu_scan; float* dbc_part;
+  float* partA; float* partD; float* partS;
+};
+
+__device__ __forceinline__ float act_apply(int act, float x) {
+  if (act == PGF_ACT_RELU) return x > 0.f ? x : 0.f;
+  if (act == PGF_ACT_TANH) return tanhf(x);
+  return x;
+}
+__device__ __forceinline__ float act_deriv(int act, float x) {
+  if (act == PGF_ACT_RELU) return x > 0.f ? 1.f : 0.f;
+  if (act == PGF_ACT_TANH) { float t = tanhf(x); return 1.f - t * t; }
+  return 1.f;
+}
+
+struct Lane {
+  int tid, dl, nq;
+  int64_t c, b, d, s, e;
+  int grp;
+  bool ch;
+};
+
+__device__ __forceinline__ Lane lane_of(const SsmArgs& a) {
+  Lane l;
+  l.tid = threadIdx.x;
+  l.dl = l.tid / NQ;
+  l.nq = l.tid % NQ;
+  l.c = blockIdx.x;
+  l.b = blockIdx.y;
+  l.grp = blockIdx.z;
+  l.d = int64_t(l.grp) * DC + l.dl;
+  l.ch = l.d < a.D;
+  l.s = l.c * a.Tc;
+  l.e = l.s + a.Tc < a.L ? l.s + a.Tc : a.L;
+  return l;
+}
+
+__device__ __forceinline__ void load_A(const SsmArgs& a, int nq, float An[NS]) {
+#pragma unroll
+  for (int j = 0; j < NS; ++j) An[j] = -expf(a.A_log[nq * NS + j]);
+}
+
+// one forward step of the thread's NS states at token `row`
+__device__ __forceinline__ void fwd_step(const SsmArgs& a, const Lane& l, int64_t row,
+                                         const float An[NS], float h[NS], float& dt, float& uu) {
+  const float dtin = l.ch ? a.proj[row * a.P + l.d] : 0.f;
+  dt = softplus_f(dtin);
+  uu = l.ch ? ldv(a.u, a.u_bf16, row * a.D + l.d) : 0.f;
+  const float* Bp = a.proj + row * a.P + a.D + l.nq * NS;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const float z = dt * An[j];
+    const float ez = expf(z);
+    const float p1 = phi1_from_exp(z, ez);
+    h[j] = ez * h[j] + (p1 * Bp[j]) * uu;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArgs a) {
+  const Lane l = lane_of(a);
+  float An[NS];
+  load_A(a, l.nq, An);
+  float h[NS] = {0.f, 0.f, 0.f, 0.f};
+  float sdt = 0.f;
+  for (int64_t t = l.s; t < l.e; ++t) {
+    float dt, uu;
+    fwd_step(a, l, l.b * a.L + t, An, h, dt, uu);
+    sdt += dt;
+  }
+  if (!l.ch) return;
+  const int64_t cb = l.b * a.nC + l.c;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) a.hloc[(cb * a.D + l.d) * NST + l.nq * NS + j] = h[j];
+  if (l.nq == 0) a.sdt[cb * a.D + l.d] = sdt;
+}
+
+__global__ void ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_final) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= a.Bsz * a.D * NST) return;
+  const int n = int(idx % NST);
+  const int64_t d = (idx / NST) % a.D;
+  const int64_t b = idx / (NST * a.D);
+  const float An = -expf(a.A_log[n]);
+  float H = a.h_init ? a.h_init[(b * a.D + d) * NST + n] : 0.f;
+  a.hC[((b * (a.nC + 1)) * a.D + d) * NST + n] = H;
+  for (int64_t c = 0; c < a.nC; ++c) {
+    const int64_t cb = b * a.nC + c;
+    H = expf(An * a.sdt[cb * a.D + d]) * H + a.hloc[(cb * a.D + d) * NST + n];
+    a.hC[((b * (a.nC + 1) + c + 1) * a.D + d) * NST + n] = H;
+  }
+  if (h_final) h_final[(b * a.D + d) * NST + n] = H;
+}
+
+__global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs a) {
+  const Lane l = lane_of(a);
+  float An[NS];
+  load_A(a, l.nq, An);
+  float h[NS];
+#pragma unroll
+  for (int j = 0; j < NS; ++j)
+    h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
+  const float Dd = l.ch ? a.Dp[l.d] : 0.f;
+  const float sc = l.ch ? a.scale[l.d] : 0.f;
+  for (int64_t t = l.s; t < l.e; ++t) {
+    const int64_t row = l.b * a.L + t;
+    float dt, uu;
+    fwd_step(a, l, row, An, h, dt, uu);
+    const float* Cp = a.proj + row * a.P + a.D + NST + l.nq * NS;
+    float yc = 0.f;
+#pragma unroll
+    for (int j = 0; j < NS; ++j) yc = fmaf(Cp[j], h[j], yc);
+    yc += __shfl_xor_sync(0xffffffffu, yc, 1);
+    yc += __shfl_xor_sync(0xffffffffu, yc, 2);
+    if (l.nq == 0 && l.ch) {
+      if (a.y) stv(a.y, a.y_bf16, row * a.D + l.d, (act_apply(a.act, yc) + Dd * uu) * sc);
+      if (a.actp) a.actp[row * a.D + l.d] = act_deriv(a.act, yc);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float delta_in_h(const SsmArgs& a, const Lane& l, int64_t row, float sc,
+                                            float& gg, float& din) {
+  gg = l.ch ? ldv(a.g, a.g_bf16, row * a.D + l.d) : 0.f;
+  din = gg * sc;
+  float dh = din;
+  if (a.actp && l.ch) dh *= a.actp[row * a.D + l.d];
+  return dh;
+}
+
+__global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArgs a) {
+  const Lane l = lane_of(a);
+  float An[NS];
+  load_A(a, l.nq, An);
+  const float sc = l.ch ? a.scale[l.d] : 0.f;
+  float dlt[NS] = {0.f, 0.f, 0.f, 0.f};
+  float anext[NS] = {1.f, 1.f, 1.f, 1.f};
+  float sdt2 = 0.f, dt_first = 0.f;
+  for (int64_t t = l.e - 1; t >= l.s; --t) {
+    const int64_t row = l.b * a.L + t;
+    const float dt = softplus_f(l.ch ? a.proj[row * a.P + l.d] : 0.f);
+    float gg, din;
+    const float dh = delta_in_h(a, l, row, sc, gg, din);
+    const float* Cp = a.proj + row * a.P + a.D + NST + l.nq * NS;
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      dlt[j] = anext[j] * dlt[j] + dh * Cp[j];
+      anext[j] = expf(dt * An[j]);
+    }
+    if (t > l.s) sdt2 += dt;
+    dt_first = dt;
+  }
+  if (!l.ch) return;
+  const int64_t cb = l.b * a.nC + l.c;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) a.dloc[(cb * a.D + l.d) * NST + l.nq * NS + j] = dlt[j];
+  if (l.nq == 0) {
+    a.sdt2[cb * a.D + l.d] = sdt2;
+    a.dt0[cb * a.D + l.d] = dt_first;
+  }
+}
+
+__global__ void ssm_compose_bwd_kernel(const SsmArgs a, const float* __restrict__ dh_end,
+                                       const float* __restrict__ dA_end, float* __restrict__ dh_start,
+                                       float* __restrict__ dA_start) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= a.Bsz * a.D * NST) return;
+  const int n = int(idx % NST);
+  const int64_t d = (idx / NST) % a.D;
+  const int64_t b = idx / (NST * a.D);
+  const float An = -expf(a.A_log[n]);
+  const int64_t o = (b * a.D + d) * NST + n;
+  float G = dh_end ? dh_end[o] : 0.f;
+  float aE = dA_end ? dA_end[o] : 1.f;
+  for (int64_t c = a.nC - 1; c >= 0; --c) {
+    const int64_t cb = b * a.nC + c;
+    const float X = aE * G;
+    a.X[(cb * a.D + d) * NST + n] = X;
+    G = expf(An * a.sdt2[cb * a.D + d]) * X + a.dloc[(cb * a.D + d) * NST + n];
+    aE = expf(a.dt0[cb * a.D + d] * An);
+  }
+  if (dh_start) dh_start[o] = G;
+  if (dA_start) dA_start[o] = aE;
+}
+
+__global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs a) {
+  extern __shared__ float sm[];
+  const Lane l = lane_of(a);
+  const int K = int((a.Tc + SUB - 1) / SUB);
+  float* ckpt = sm;                                 // [K][SSM_THREADS][NS]
+  float* red = sm + size_t(K) * SSM_THREADS * NS;   // [SUB][SSM_WARPS][32]
+  const int lane = l.tid & 31, warp = l.tid >> 5;
+  float An[NS];
+  load_A(a, l.nq, An);
+  const float Dd = l.ch ? a.Dp[l.d] : 0.f;
+  const float sc = l.ch ? a.scale[l.d] : 0.f;
+  const int64_t cb = l.b * a.nC + l.c;
+
+  float h[NS], carry[NS];
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
+    carry[j] = l.ch ? a.X[(cb * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
+  }
+  // pass 1: checkpoints at every SUB tokens
+  for (int k = 0; k < K; ++k) {
+#pragma unroll
+    for (int j = 0; j < NS; ++j) ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j] = h[j];
+#pragma unroll
+    for (int i = 0; i < SUB; ++i) {
+      const int64_t t = l.s + int64_t(k) * SUB + i;
+      if (t < l.e) {
+        float dt, uu;
+        fwd_step(a, l, l.b * a.L + t, An, h, dt, uu);
+      }
+    }
+  }
+
+  float accA[NS] = {0.f, 0.f, 0.f, 0.f};
+  float accD = 0.f, accS = 0.f;
+  const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+
+  for (int k = K - 1; k >= 0; --k) {
+    float tr[SUB + 1][NS];
+#pragma unroll
+    for (int j = 0; j < NS; ++j) tr[0][j] = ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j];
+#pragma unroll
+    for (int i = 0; i < SUB; ++i) {
+#pragma unroll
+      for (int j = 0; j < NS; ++j) tr[i + 1][j] = tr[i][j];
+      const int64_t t = l.s + int64_t(k) * SUB + i;
+      if (t < l.e) {
+        float dt, uu;
+        fwd_step(a, l, l.b * a.L + t, An, tr[i + 1], dt, uu);
+      }
+    }
+#pragma unroll
+    for (int i = SUB - 1; i >= 0; --i) {
+      const int64_t t = l.s + int64_t(k) * SUB + i;
+      const bool valid = t < l.e;  // uniform across the CTA
+      float v8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float gdt = 0.f, gur = 0.f, hc = 0.f, sig = 0.f, uu = 0.f, gg = 0.f, din = 0.f;
+      const int64_t row = l.b * a.L + t;
+      if (valid) {
+        const float dtin = l.ch ? a.proj[row * a.P + l.d] : 0.f;
+        const float dt = softplus_f(dtin);
+        sig = sigmoid_f(dtin);
+        uu = l.ch ? ldv(a.u, a.u_bf16, row * a.D + l.d) : 0.f;
+        const float dh = delta_in_h(a, l, row, sc, gg, din);
+        const float* Bp = a.proj + row * a.P + a.D + l.nq * NS;
+        const float* Cp = Bp + NST;
+#pragma unroll
+        for (int j = 0; j < NS; ++j) {
+          hc = fmaf(Cp[j], tr[i + 1][j], hc);
+          const float dlt = carry[j] + dh * Cp[j];
+          const float z = dt * An[j];
+          const float ez = expf(z);
+          const float p1 = phi1_from_exp(z, ez);
+          const float p1p = phi1p_from_exp(z, ez);
+          const float q = ez * tr[i][j] + p1p * (Bp[j] * uu);
+          const float dq = dlt * q;
+          accA[j] = fmaf(dq, z, accA[j]);
+          gdt = fmaf(dq, An[j], gdt);
+          gur = fmaf(dlt, p1 * Bp[j], gur);
+          v8[j] = dlt * (p1 * uu);
+          v8[NS + j] = dh * tr[i + 1][j];
+          carry[j] = ez * dlt;
+        }
+      }
+      gdt += __shfl_xor_sync(0xffffffffu, gdt, 1);
+      gdt += __shfl_xor_sync(0xffffffffu, gdt, 2);
+      gur += __shfl_xor_sync(0xffffffffu, gur, 1);
+      gur += __shfl_xor_sync(0xffffffffu, gur, 2);
+      hc += __shfl_xor_sync(0xffffffffu, hc, 1);
+      hc += __shfl_xor_sync(0xffffffffu, hc, 2);
+      if (valid && l.nq == 0 && l.ch) {
+        a.gstack[row * a.P + l.d] = gdt * sig;
+        a.gu_scan[row * a.D + l.d] = din * Dd + gur;
+        accD = fmaf(din, uu, accD);
+        accS = fmaf(gg, act_apply(a.act, hc) + Dd * uu, accS);
+      }
+      // sum the 8 grad-B / grad-C partials over the warp's 8 channels (lane bits 2..4)
+      float w4[4], w2[2];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float keep = b4 ? v8[4 + q] : v8[q];
+        const float send = b4 ? v8[q] : v8[4 + q];
+        w4[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float keep = b3 ? w4[2 + q] : w4[q];
+        const float send = b3 ? w4[q] : w4[2 + q];
+        w2[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      const float keep = b2 ? w2[1] : w2[0];
+      const float send = b2 ? w2[0] : w2[1];
+      red[(i * SSM_WARPS + warp) * 32 + lane] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    __syncthreads();
+    for (int o = l.tid; o < SUB * 32; o += SSM_THREADS) {
+      const int i = o >> 5, ln = o & 31;
+      const int64_t t = l.s + int64_t(k) * SUB + i;
+      if (t < l.e) {
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < SSM_WARPS; ++w) sum += red[(i * SSM_WARPS + w) * 32 + ln];
+        const int vi = (ln >> 2) & 7, nqq = ln & 3;
+        const int n = nqq * NS + (vi & 3);
+        const int which = vi >> 2;
+        a.dbc_part[((int64_t(l.grp) * a.Bsz + l.b) * a.L + t) * 32 + which * NST + n] = sum;
+      }
+    }
+    __syncthreads();
+  }
+  // per-CTA parameter partials
+  float* sA = sm;  // [SSM_THREADS][NS]; checkpoints are no longer needed
+#pragma unroll
+  for (int j = 0; j < NS; ++j) sA[l.tid * NS + j] = l.ch ? accA[j] : 0.f;
+  __syncthreads();
+  if (l.tid < NST) {
+    const int n = l.tid, nqq = n / NS, j = n % NS;
+    float s = 0.f;
+    for (int dl = 0; dl < DC; ++dl) s += sA[(dl * NQ + nqq) * NS + j];
+    a.partA[((l.c * a.Bsz + l.b) * a.G + l.grp) * NST + n] = s;
+  }
+  if (l.nq == 0 && l.ch) {
+    a.partD[(l.c * a.Bsz + l.b) * a.D + l.d] = accD;
+    a.partS[(l.c * a.Bsz + l.b) * a.D + l.d] = accS;
+  }
+}
+
+// grad B / grad C columns of gstack: sum of the channel-group partials, in group order.
+__global__ void ssm_bc_reduce_kernel(const SsmArgs a) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t rows = a.Bsz * a.L;
+  if (idx >= rows * 32) return;
+  const int64_t row = idx / 32;
+  const int m = int(idx % 32);
+  float s = 0.f;
+  for (int64_t gi = 0; gi < a.G; ++gi) s += a.dbc_part[(gi * rows + row) * 32 + m];
+  a.gstack[row * a.P + a.D + m] = s;
+}
+
+// grad A_log / D / scale from the per-CTA partials, in a fixed order.
+__global__ void ssm_param_reduce_kernel(const SsmArgs a, float* __restrict__ gA,
+                                        float* __restrict__ gD, float* __restrict__ gS,
+                                        int accumulate) {
+  __shared__ float red[256];
+  if (blockIdx.x < NST) {
+    const int n = blockIdx.x;
+    const int64_t cnt = a.nC * a.Bsz * a.G;
+    float s = 0.f;
+    for (int64_t i = threadIdx.x; i < cnt; i += blockDim.x) s += a.partA[i * NST + n];
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+      if (int(threadIdx.x) < o) red[threadIdx.x] += red[threadIdx.x + o];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) gA[n] = accumulate ? gA[n] + red[0] : red[0];
+    return;
+  }
+  const int64_t d = int64_t(blockIdx.x - NST) * blockDim.x + threadIdx.x;
+  if (d >= a.D) return;
+  const int64_t cnt = a.nC * a.Bsz;
+  float sD = 0.f, sS = 0.f;
+  for (int64_t i = 0; i < cnt; ++i) {
+    sD += a.partD[i * a.D + d];
+    sS += a.partS[i * a.D + d];
+  }
+  gD[d] = accumulate ? gD[d] + sD : sD;
+  gS[d] = accumulate ? gS[d] + sS : sS;
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+static int64_t pick_tc(int64_t Bsz, int64_t L, int64_t G) {
+  int64_t tc = TC_MAX;
+  const int64_t target = 4 * 148;
+  while (tc > 32 && ((L + tc - 1) / tc) * Bsz * G < target) tc /= 2;
+  return tc;
+}
+
+struct SsmPlan {
+  int64_t Bsz, L, D, P, Tc, nC, G;
+};
+
+static SsmPlan plan_of(int64_t Bsz, int64_t L, int64_t D) {
+  SsmPlan p;
+  p.Bsz = Bsz; p.L = L; p.D = D; p.P = D + 2 * NST;
+  p.G = (D + DC - 1) / DC;
+  p.Tc = pick_tc(Bsz, L, p.G);
+  p.nC = (L + p.Tc - 1) / p.Tc;
+  return p;
+}
+
+static size_t ssm_ws(const SsmPlan& p, int dtype, int backward, int act) {
+  const size_t BL = size_t(p.Bsz) * p.L;
+  size_t b = 0;
+  b += Workspace::round(BL * p.P * 4);                                  // proj
+  b += Workspace::round(size_t(p.Bsz) * p.nC * p.D * NST * 4);          // hloc
+  b += Workspace::round(size_t(p.Bsz) * p.nC * p.D * 4);                // sdt
+  b += Workspace::round(size_t(p.Bsz) * (p.nC + 1) * p.D * NST * 4);    // hC
+  if (dtype) b += Workspace::round(size_t(p.P) * p.D * 2);              // W_cat bf16
+  if (backward) {
+    b += Workspace::round(BL * p.P * 4);                                // gstack
+    b += Workspace::round(BL * p.D * 4);                                // gu_scan
+    b += Workspace::round(size_t(p.G) * BL * 32 * 4);                   // dbc_part
+    if (act != PGF_ACT_NONE) b += Workspace::round(BL * p.D * 4);       // actp
+    b += Workspace::round(size_t(p.Bsz) * p.nC * p.D * NST * 4) * 2;    // dloc, X
+    b += Workspace::round(size_t(p.Bsz) * p.nC * p.D * 4) * 2;          // sdt2, dt0
+    b += Workspace::round(size_t(p.nC) * p.Bsz * p.G * NST * 4);        // partA
+    b += Workspace::round(size_t(p.nC) * p.Bsz * p.D * 4) * 2;          // partD, partS
+    b += colsum_ws(int64_t(BL), p.P);
+  }
+  return b + 4096;
+}
+
+static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u, int dtype,
+                      const float* W_cat, const float* b_cat, const void** wcat_op, cudaStream_t s) {
+  const size_t BL = size_t(p.Bsz) * p.L;
+  a.Bsz = p.Bsz; a.L = p.L; a.D = p.D; a.P = p.P; a.Tc = p.Tc; a.nC = p.nC; a.G = p.G;
+  a.u = u; a.u_bf16 = dtype;
+  float* proj = W.take<float>(BL * p.P);
+  a.hloc = W.take<float>(size_t(p.Bsz) * p.nC * p.D * NST);
+  a.sdt = W.take<float>(size_t(p.Bsz) * p.nC * p.D);
+  a.hC = W.take<float>(size_t(p.Bsz) * (p.nC + 1) * p.D * NST);
+  __nv_bfloat16* wb = dtype ? W.take<__nv_bfloat16>(size_t(p.P) * p.D) : nullptr;
+  if (!proj || !a.hloc || !a.sdt || !a.hC || (dtype && !wb)) {
+    set_error("ssm: workspace too small (%zu)", W.cap);
+    return PGF_ERR_WORKSPACE;
+  }
+  a.proj = proj;
+  const void* w = W_cat;
+  if (dtype) {
+    PGF_TRY(to_bf16(W_cat, wb, p.P * p.D, s));
+    w = wb;
+  }
+  *wcat_op = w;
+  // proj = u W_cat^T + b_cat   (train_singlemamba_optimized.py:116-124)
+  Gemm g;
+  g.M = int64_t(BL); g.N = p.P; g.K = p.D;
+  g.A = u; g.a_bf16 = dtype; g.lda = p.D; g.a_trans = 0;
+  g.B = w; g.b_bf16 = dtype; g.ldb = p.D; g.b_trans = 0;
+  g.D = proj; g.d_bf16 = 0; g.ldd = p.P;
+  g.epi = epi_default();
+  g.epi.bias = b_cat;
+  return run_gemm(g, s);
+}
+
+static int ssm_forward_states(const SsmArgs& a, const SsmPlan& p, float* h_final, cudaStream_t s) {
+  dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  ssm_chunk_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  const int64_t nth = p.Bsz * p.D * NST;
+  ssm_compose_fwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, h_final);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+static int check_common(int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype) {
+  PGF_CHECK_ARG(N == NST, "ssm: d_state must be %d (got %lld)", NST, (long long)N);
+  PGF_CHECK_ARG(Bsz > 0 && L >= 0 && D > 0, "ssm: bad shape");
+  PGF_CHECK_ARG(Bsz <= 65535, "ssm: batch too large");
+  PGF_CHECK_ARG(act == PGF_ACT_NONE || act == PGF_ACT_RELU || act == PGF_ACT_TANH, "ssm: bad act");
+  PGF_CHECK_ARG(dtype == 0 || dtype == 1, "ssm: bad dtype");
+  return PGF_OK;
+}
+
+}  // namespace pgf
+
+using namespace pgf;
+
+extern "C" size_t pgf_ssm_workspace(int64_t Bsz, int64_t L, int64_t D, int64_t N, int dtype,
+                                    int backward) {
+  (void)N;
+  SsmPlan p = plan_of(Bsz < 1 ? 1 : Bsz, L < 1 ? 1 : L, D < 1 ? 1 : D);
+  return ssm_ws(p, dtype, backward, PGF_ACT_TANH);
+}
+
+extern "C" int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat,
+                           const float* A_log, const float* Dp, const float* scale,
+                           const float* h_init, void* y, float* h_final, int64_t Bsz, int64_t L,
+                           int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                           pgf_stream_t stream) {
+  PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
+  PGF_CHECK_ARG(u && W_cat && b_cat && A_log && Dp && scale && y, "ssm_fwd: null pointer");
+  cudaStream_t s = as_stream(stream);
+  if (L == 0) {
+    if (h_final) {
+      if (h_init) PGF_CUDA(cudaMemcpyAsync(h_final, h_init, Bsz * D * NST * 4, cudaMemcpyDeviceToDevice, s));
+      else PGF_CUDA(cudaMemsetAsync(h_final, 0, Bsz * D * NST * 4, s));
+    }
+    return PGF_OK;
+  }
+  SsmPlan p = plan_of(Bsz, L, D);
+  Workspace W(ws, ws_bytes);
+  SsmArgs a = {};
+  a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act; a.h_init = h_init;
+  const void* wop;
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
+  PGF_TRY(ssm_forward_states(a, p, h_final, s));
+  a.y = y;
+  a.y_bf16 = dtype;
+  dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                           const float* A_log, const float* Dp, const float* scale,
+                           const float* h_init, const float* dh_end, const float* dA_end,
+                           float* gW_cat, float* gb_cat, float* gA_log, float* gDp, float* gscale,
+                           void* gu, float* dh_start, float* dA_start, int accumulate, int64_t Bsz,
+                           int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                           size_t ws_bytes, pgf_stream_t stream) {
+  PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
+  PGF_CHECK_ARG(u && g && W_cat && b_cat && A_log && Dp && scale && gW_cat && gb_cat && gA_log &&
+                    gDp && gscale && gu,
+                "ssm_bwd: null pointer");
+  PGF_CHECK_ARG(L > 0, "ssm_bwd: empty sequence");
+  cudaStream_t s = as_stream(stream);
+  SsmPlan p = plan_of(Bsz, L, D);
+  Workspace W(ws, ws_bytes);
+  SsmArgs a = {};
+  a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act; a.h_init = h_init;
+  a.g = g; a.g_bf16 = dtype;
+  const void* wop;
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
+  const size_t BL = size_t(Bsz) * L;
+  a.gstack = W.take<float>(BL * p.P);
+  a.gu_scan = W.take<float>(BL * p.D);
+  a.dbc_part = W.take<float>(size_t(p.G) * BL * 32);
+  a.actp = act != PGF_ACT_NONE ? W.take<float>(BL * p.D) : nullptr;
+  a.dloc = W.take<float>(size_t(Bsz) * p.nC * D * NST);
+  a.X = W.take<float>(size_t(Bsz) * p.nC * D * NST);
+  a.sdt2 = W.take<float>(size_t(Bsz) * p.nC * D);
+  a.dt0 = W.take<float>(size_t(Bsz) * p.nC * D);
+  a.partA = W.take<float>(size_t(p.nC) * Bsz * p.G * NST);
+  a.partD = W.take<float>(size_t(p.nC) * Bsz * D);
+  a.partS = W.take<float>(size_t(p.nC) * Bsz * D);
+  const size_t csb = colsum_ws(int64_t(BL), p.P);
+  void* cs = W.take<char>(csb);
+  if (!a.gstack || !a.gu_scan || !a.dbc_part || (act != PGF_ACT_NONE && !a.actp) || !a.dloc ||
+      !a.X || !a.sdt2 || !a.dt0 || !a.partA || !a.partD || !a.partS || !cs) {
+    set_error("ssm_bwd: workspace too small (%zu)", ws_bytes);
+    return PGF_ERR_WORKSPACE;
+  }
+  PGF_TRY(ssm_forward_states(a, p, nullptr, s));
+  dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  if (act != PGF_ACT_NONE) {
+    a.y = nullptr;
+    ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);  // act'(C h) per token and channel
+    PGF_LAUNCH_CHECK();
+  }
+  ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  const int64_t nth = Bsz * D * NST;
+  ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start);
+  PGF_LAUNCH_CHECK();
+  const int K = int((p.Tc + SUB - 1) / SUB);
+  const size_t smem = (size_t(K) * SSM_THREADS * NS + size_t(SUB) * SSM_WARPS * 32) * 4;
+  PGF_CUDA(cudaFuncSetAttribute(ssm_main_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(smem)));
+  ssm_main_bwd_kernel<<<grid, SSM_THREADS, smem, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  ssm_bc_reduce_kernel<<<ceil_div(int64_t(BL) * 32, 256), 256, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  ssm_param_reduce_kernel<<<NST + ceil_div(D, 256), 256, 0, s>>>(a, gA_log, gDp, gscale, accumulate);
+  PGF_LAUNCH_CHECK();
+  // grad W_cat (+)= gstack^T u ;  grad b_cat (+)= colsum(gstack)   (:438-451)
+  Gemm gw;
+  gw.M = p.P; gw.N = D; gw.K = int64_t(BL);
+  gw.A = a.gstack; gw.a_bf16 = 0; gw.lda = p.P; gw.a_trans = 1;
+  gw.B = u; gw.b_bf16 = dtype; gw.ldb = D; gw.b_trans = 1;
+  gw.D = gW_cat; gw.d_bf16 = 0; gw.ldd = D;
+  gw.epi = epi_default();
+  gw.epi.accumulate = accumulate;
+  PGF_TRY(run_gemm(gw, s));
+  PGF_TRY(colsum(a.gstack, 0, int64_t(BL), p.P, p.P, gb_cat, accumulate, cs, csb, s));
+  // grad_u = gstack W_cat + (delta_in*D + sum_n delta_h phi_1 B)   (:453-463)
+  Gemm gx;
+  gx.M = int64_t(BL); gx.N = D; gx.K = p.P;
+  gx.A = a.gstack; gx.a_bf16 = 0; gx.lda = p.P; gx.a_trans = 0;
+  gx.B = W_cat; gx.b_bf16 = 0; gx.ldb = D; gx.b_trans = 1;
+  gx.D = gu; gx.d_bf16 = dtype; gx.ldd = D;
+  gx.epi = epi_default();
+  gx.epi.addend = a.gu_scan;
+  gx.epi.addend_dtype = 0;
+  gx.epi.ld_addend = D;
+  PGF_TRY(run_gemm(gx, s));
+  return PGF_OK;
+}

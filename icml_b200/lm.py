@@ -1,0 +1,101 @@
+"""PGF language-model training step (the reference's ExternalPGFLanguageModel,
+train_wikitext_rebuttal.py:58-149) on libpgf.so.
+
+Differences from the reference's step, none of which changes the mathematics:
+* the LM head and cross entropy are fused and tiled over tokens and vocabulary, so the (T, V)
+  logits are never materialised (the reference builds them and their softmax in full);
+* activations between operators may be bfloat16 (``act_dtype``), parameters, gradients and the
+  optimizer state stay float32;
+* ``step()`` returns the loss as a device tensor, so a training loop need not synchronise.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .pgf_mamba_block import PGFMambaBlock, PGFMambaSequential
+
+
+class PGFLanguageModel:
+    def __init__(self, vocab_size: int, d_model: int, d_state: int, d_ff: int, n_layers: int,
+                 block_size: int, device, act_dtype=torch.float32, lr: float = 1e-3,
+                 weight_decay: float = 0.01, tie_embeddings: bool = False, init_std: float = 0.02):
+        self.vocab_size = vocab_size
+        self.d_model = d_model
+        self.block_size = block_size
+        self.n_layers = n_layers
+        self.device = torch.device(device)
+        self.act_dtype = act_dtype
+        self.emb_weight = nn.Parameter(torch.randn(vocab_size, d_model, device=device) * init_std)
+        self.tied = tie_embeddings
+        self.lm_head_weight = (self.emb_weight if tie_embeddings else
+                               nn.Parameter(torch.randn(vocab_size, d_model, device=device) * init_std))
+        blocks = [PGFMambaBlock(d_model, d_state, d_ff, block_size) for _ in range(n_layers)]
+        self.backbone = PGFMambaSequential(blocks).to(device)
+        self.params = [self.emb_weight] + ([] if tie_embeddings else [self.lm_head_weight]) + \
+            list(self.backbone.parameters())
+        self.optimizer = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay,
+                                           fused=self.device.type == "cuda")
+
+    @torch.no_grad()
+    def load_(self, emb: torch.Tensor, lm_head: torch.Tensor, backbone_state: Dict[str, torch.Tensor]):
+        self.emb_weight.copy_(emb)
+        if not self.tied:
+            self.lm_head_weight.copy_(lm_head)
+        self.backbone.load_state_dict(backbone_state)
+
+    @torch.no_grad()
+    def forward_backward(self, input_ids: torch.Tensor, targets: torch.Tensor):
+        """PGF pass 1 over all layers (stashing each layer's input), fused LM head + CE, pass 2 in
+        reverse.  Returns (loss tensor, {param name: grad})."""
+        B, L = input_ids.shape
+        d = self.d_model
+        x = ops.embedding_fwd(input_ids, self.emb_weight, dtype=self.act_dtype)
+        stash: List[torch.Tensor] = []
+        for layer in self.backbone.layers:
+            stash.append(x)
+            x = layer.pgf_forward(x)
+        h = x.reshape(-1, d)
+        tg = targets.reshape(-1)
+        loss_rows, lse = ops.lm_head_ce_fwd(h, self.lm_head_weight, tg)
+        loss = loss_rows.mean()
+        gW, gh = ops.lm_head_ce_bwd(h, self.lm_head_weight, tg, lse, 1.0 / h.shape[0])
+        grads = {"lm_head": gW}
+        g = gh.reshape(B, L, d)
+        del x, h, gh
+        for i in reversed(range(self.n_layers)):
+            res = self.backbone.layers[i].pgf_backward(stash.pop(), g)
+            for k, v in res["grads"].items():
+                grads[f"layers.{i}.{k}"] = v
+            g = res["grad_input"]
+            del res
+        grads["emb"] = ops.embedding_bwd(input_ids, g, self.vocab_size)
+        if self.tied:
+            grads["emb"] = grads["emb"] + grads.pop("lm_head")
+        return loss, grads
+
+    def _assign(self, grads):
+        self.emb_weight.grad = grads["emb"]
+        if not self.tied:
+            self.lm_head_weight.grad = grads["lm_head"]
+        for i, layer in enumerate(self.backbone.layers):
+            for name, p in layer.named_parameters():
+                p.grad = grads[f"layers.{i}.{name}"]
+
+    def step(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One training step (forward, backward, AdamW); returns the loss without syncing."""
+        self.optimizer.zero_grad(set_to_none=True)
+        loss, grads = self.forward_backward(input_ids, targets)
+        self._assign(grads)
+        self.optimizer.step()
+        return loss
+
+    def train_step_pgf(self, input_ids: torch.Tensor, targets: torch.Tensor) -> float:
+        """train_wikitext_rebuttal.py:98-149."""
+        return self.step(input_ids, targets).item()
+
+
+__all__ = ["PGFLanguageModel"]

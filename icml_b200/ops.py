@@ -1,0 +1,298 @@
+"""Tensor-level wrappers over the C-ABI of libpgf.so.
+
+Every function takes CUDA tensors, allocates outputs and scratch from the torch caching
+allocator (so peak-memory accounting stays in ``torch.cuda.max_memory_allocated``), launches on
+the current stream and returns new tensors.  Activations are float32 or bfloat16; parameters and
+parameter gradients are float32.  Nothing here runs on the CPU: a CPU tensor is an error.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from ._lib import Epilogue, check, lib
+
+F32, BF16 = 0, 1
+ACT = {None: 0, "none": 0, "gelu": 1, "relu": 2, "tanh": 3}
+EPI = {"none": 0, "gelu": 1, "relu": 2, "dgelu": 3, "drelu": 4}
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise TypeError(f"unsupported activation dtype {t.dtype} (float32 or bfloat16)")
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("icml_b200 operators run on CUDA tensors only (no CPU path)")
+
+
+def _c(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    return None if t is None else t.contiguous()
+
+
+def _p(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _f32(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    return None if t is None else t.detach().float().contiguous()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+# --------------------------------------------------------------------------- RMSNorm
+def rmsnorm_fwd(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    _cuda(x, w)
+    x = _c(x)
+    w = _f32(w)
+    dim = x.shape[-1]
+    rows = x.numel() // dim
+    y = torch.empty_like(x)
+    check(lib().pgf_rmsnorm_fwd(_p(x), _p(w), _p(y), rows, dim, eps, _dt(x), _stream()), "rmsnorm_fwd")
+    return y
+
+
+def rmsnorm_bwd(x: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float,
+                need_gx: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    _cuda(x, g, w)
+    x, g = _c(x), _c(g.to(x.dtype))
+    w = _f32(w)
+    dim = x.shape[-1]
+    rows = x.numel() // dim
+    gw = torch.empty(dim, dtype=torch.float32, device=x.device)
+    gx = torch.empty_like(x) if need_gx else None
+    L = lib()
+    nb = L.pgf_rmsnorm_bwd_workspace(rows, dim)
+    ws = _ws(nb, x.device)
+    check(L.pgf_rmsnorm_bwd(_p(x), _p(g), _p(w), _p(gx), _p(gw), 0, rows, dim, eps, _dt(x),
+                            _p(ws), ws.numel(), _stream()), "rmsnorm_bwd")
+    return gw, gx
+
+
+# --------------------------------------------------------------------------- embedding
+def embedding_fwd(ids: torch.Tensor, W: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+    _cuda(ids, W)
+    ids = _c(ids.long())
+    W = _f32(W)
+    V, d = W.shape
+    y = torch.empty(*ids.shape, d, dtype=dtype, device=W.device)
+    check(lib().pgf_embedding_fwd(_p(ids), _p(W), _p(y), ids.numel(), V, d, _dt(y), _stream()),
+          "embedding_fwd")
+    return y
+
+
+def embedding_bwd(ids: torch.Tensor, g: torch.Tensor, vocab: int) -> torch.Tensor:
+    _cuda(ids, g)
+    ids = _c(ids.long())
+    d = g.shape[-1]
+    g = _c(g)
+    n = ids.numel()
+    gw = torch.empty(vocab, d, dtype=torch.float32, device=g.device)
+    L = lib()
+    ws = _ws(L.pgf_embedding_bwd_workspace(n, vocab, d), g.device)
+    check(L.pgf_embedding_bwd(_p(ids), _p(g), _p(gw), 0, n, vocab, d, _dt(g), _p(ws), ws.numel(),
+                              _stream()), "embedding_bwd")
+    return gw
+
+
+# --------------------------------------------------------------------------- dense products
+def gemm(A: torch.Tensor, B: torch.Tensor, *, a_trans=False, b_trans=False, out_dtype=torch.float32,
+         bias=None, epilogue="none", aux=None, aux_out=None, addend=None, alpha=1.0,
+         out: Optional[torch.Tensor] = None, accumulate=False) -> torch.Tensor:
+    """D = epi(alpha * opA @ opB^T): opA = A (M,K) or A^T when a_trans; opB = B (N,K) or B^T."""
+    _cuda(A, B)
+    A, B = _c(A), _c(B)
+    M, K = (A.shape[1], A.shape[0]) if a_trans else A.shape
+    N, K2 = (B.shape[1], B.shape[0]) if b_trans else B.shape
+    assert K == K2, (A.shape, B.shape, a_trans, b_trans)
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=A.device)
+    e = Epilogue()
+    e.kind = EPI[epilogue]
+    e.alpha = alpha
+    keep = []  # keeps converted operands alive until the launch
+    if bias is not None:
+        keep.append(_f32(bias))
+        e.bias = keep[-1].data_ptr()
+    if aux is not None:
+        e.aux, e.aux_dtype, e.ld_aux = aux.data_ptr(), _dt(aux), aux.shape[-1]
+    if aux_out is not None:
+        e.aux_out, e.aux_out_dtype, e.ld_aux_out = aux_out.data_ptr(), _dt(aux_out), aux_out.shape[-1]
+    if addend is not None:
+        e.addend, e.addend_dtype, e.ld_addend = addend.data_ptr(), _dt(addend), addend.shape[-1]
+    e.accumulate = int(accumulate)
+    check(lib().pgf_gemm(M, N, K, _p(A), _dt(A), A.shape[1], int(a_trans), _p(B), _dt(B), B.shape[1],
+                         int(b_trans), _p(out), _dt(out), out.shape[1], e, _stream()), "gemm")
+    return out
+
+
+def colsum(X: torch.Tensor) -> torch.Tensor:
+    _cuda(X)
+    X = _c(X)
+    M, N = X.shape
+    out = torch.empty(N, dtype=torch.float32, device=X.device)
+    L = lib()
+    ws = _ws(L.pgf_colsum_workspace(M, N), X.device)
+    check(L.pgf_colsum(_p(X), _dt(X), M, N, N, _p(out), 0, _p(ws), ws.numel(), _stream()), "colsum")
+    return out
+
+
+# --------------------------------------------------------------------------- FFN
+def ffn_fwd(x, W1, b1, W2, b2, activation="gelu") -> torch.Tensor:
+    _cuda(x, W1)
+    x = _c(x)
+    W1, b1, W2, b2 = _f32(W1), _f32(b1), _f32(W2), _f32(b2)
+    rows, d_in = x.shape
+    d_h, d_out = W1.shape[0], W2.shape[0]
+    y = torch.empty(rows, d_out, dtype=x.dtype, device=x.device)
+    L = lib()
+    ws = _ws(L.pgf_ffn_workspace(rows, d_in, d_h, d_out, _dt(x), 0), x.device)
+    check(L.pgf_ffn_fwd(_p(x), _p(W1), _p(b1), _p(W2), _p(b2), _p(y), rows, d_in, d_h, d_out,
+                        ACT[activation], _dt(x), _p(ws), ws.numel(), _stream()), "ffn_fwd")
+    return y
+
+
+def ffn_bwd(x, g, W1, b1, W2, activation="gelu", need_gx=True) -> Dict[str, torch.Tensor]:
+    _cuda(x, g, W1)
+    x, g = _c(x), _c(g.to(x.dtype))
+    W1, b1, W2 = _f32(W1), _f32(b1), _f32(W2)
+    rows, d_in = x.shape
+    d_h, d_out = W1.shape[0], W2.shape[0]
+    dev = x.device
+    gW1 = torch.empty(d_h, d_in, device=dev)
+    gb1 = torch.empty(d_h, device=dev)
+    gW2 = torch.empty(d_out, d_h, device=dev)
+    gb2 = torch.empty(d_out, device=dev)
+    gx = torch.empty_like(x) if need_gx else None
+    L = lib()
+    ws = _ws(L.pgf_ffn_workspace(rows, d_in, d_h, d_out, _dt(x), 1), dev)
+    check(L.pgf_ffn_bwd(_p(x), _p(g), _p(W1), _p(b1), _p(W2), _p(gW1), _p(gb1), _p(gW2), _p(gb2),
+                        _p(gx), 0, rows, d_in, d_h, d_out, ACT[activation], _dt(x), _p(ws),
+                        ws.numel(), _stream()), "ffn_bwd")
+    r = {"grad_W1": gW1, "grad_b1": gb1, "grad_W2": gW2, "grad_b2": gb2}
+    if need_gx:
+        r["grad_x"] = gx
+    return r
+
+
+# --------------------------------------------------------------------------- LM head
+def lm_head_fwd(h, W) -> torch.Tensor:
+    _cuda(h, W)
+    h = _c(h)
+    W = _f32(W)
+    T, d = h.shape
+    V = W.shape[0]
+    logits = torch.empty(T, V, dtype=torch.float32, device=h.device)
+    L = lib()
+    ws = _ws(L.pgf_lm_head_workspace(T, V, d, _dt(h)), h.device)
+    check(L.pgf_lm_head_fwd(_p(h), _p(W), _p(logits), T, V, d, _dt(h), _p(ws), ws.numel(), _stream()),
+          "lm_head_fwd")
+    return logits
+
+
+def lm_head_bwd(h, g_logits, W, need_gh=True):
+    _cuda(h, g_logits, W)
+    h = _c(h)
+    g_logits = _f32(g_logits)
+    W = _f32(W)
+    T, d = h.shape
+    V = W.shape[0]
+    gW = torch.empty(V, d, dtype=torch.float32, device=h.device)
+    gh = torch.empty_like(h) if need_gh else None
+    L = lib()
+    ws = _ws(L.pgf_lm_head_workspace(T, V, d, _dt(h)), h.device)
+    check(L.pgf_lm_head_bwd(_p(h), _p(g_logits), _p(W), _p(gW), _p(gh), 0, T, V, d, _dt(h), _p(ws),
+                            ws.numel(), _stream()), "lm_head_bwd")
+    return gW, gh
+
+
+def lm_head_ce_fwd(h, W, targets):
+    """Per-row CE loss and log-sum-exp of logits = h W^T, vocab-tiled (logits never stored)."""
+    _cuda(h, W, targets)
+    h = _c(h)
+    W = _f32(W)
+    targets = _c(targets.long())
+    T, d = h.shape
+    V = W.shape[0]
+    loss_rows = torch.empty(T, dtype=torch.float32, device=h.device)
+    lse = torch.empty(T, dtype=torch.float32, device=h.device)
+    L = lib()
+    ws = _ws(L.pgf_lm_head_ce_workspace(T, V, d, _dt(h)), h.device)
+    check(L.pgf_lm_head_ce_fwd(_p(h), _p(W), _p(targets), _p(loss_rows), _p(lse), T, V, d, _dt(h),
+                               _p(ws), ws.numel(), _stream()), "lm_head_ce_fwd")
+    return loss_rows, lse
+
+
+def lm_head_ce_bwd(h, W, targets, lse, grad_scale: float, need_gh=True):
+    _cuda(h, W, targets, lse)
+    h = _c(h)
+    W = _f32(W)
+    targets = _c(targets.long())
+    T, d = h.shape
+    V = W.shape[0]
+    gW = torch.empty(V, d, dtype=torch.float32, device=h.device)
+    gh = torch.empty_like(h) if need_gh else None
+    L = lib()
+    ws = _ws(L.pgf_lm_head_ce_workspace(T, V, d, _dt(h)), h.device)
+    lse = _c(lse)
+    check(L.pgf_lm_head_ce_bwd(_p(h), _p(W), _p(targets), _p(lse), grad_scale, _p(gW), _p(gh), 0,
+                               T, V, d, _dt(h), _p(ws), ws.numel(), _stream()), "lm_head_ce_bwd")
+    return gW, gh
+
+
+# --------------------------------------------------------------------------- selective scan
+def ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, want_h_final=False):
+    """y (Bsz,L,D) in u's dtype, and the state after the last token when asked."""
+    _cuda(u, W_cat)
+    u = _c(u)
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    y = torch.empty_like(u)
+    hf = torch.empty(Bsz, D, N, dtype=torch.float32, device=u.device) if want_h_final else None
+    Lb = lib()
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 0), u.device)
+    W_cat, b_cat, A_log, Dp, scale, h_init = (_f32(t) for t in (W_cat, b_cat, A_log, Dp, scale, h_init))
+    check(Lb.pgf_ssm_fwd(_p(u), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp), _p(scale), _p(h_init),
+                         _p(y), _p(hf), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(),
+                         _stream()), "ssm_fwd")
+    return y, hf
+
+
+def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_end=None, act=None,
+            want_carry=False):
+    """All gradients of the SSM layer over [0, L) plus the carries (delta_h[0], dA[0])."""
+    _cuda(u, g, W_cat)
+    u, g = _c(u), _c(g.to(u.dtype))
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    dev = u.device
+    W_cat, b_cat = _f32(W_cat), _f32(b_cat)
+    gW = torch.empty_like(W_cat)
+    gb = torch.empty_like(b_cat)
+    gA = torch.empty(N, dtype=torch.float32, device=dev)
+    gD = torch.empty(D, dtype=torch.float32, device=dev)
+    gS = torch.empty(D, dtype=torch.float32, device=dev)
+    gu = torch.empty_like(u)
+    dh0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev) if want_carry else None
+    dA0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev) if want_carry else None
+    Lb = lib()
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 1), dev)
+    A_log, Dp, scale, h_init, dh_end, dA_end = (_f32(t) for t in (A_log, Dp, scale, h_init, dh_end, dA_end))
+    check(Lb.pgf_ssm_bwd(_p(u), _p(g), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp),
+                         _p(scale), _p(h_init), _p(dh_end), _p(dA_end),
+                         _p(gW), _p(gb), _p(gA), _p(gD), _p(gS), _p(gu), _p(dh0), _p(dA0), 0,
+                         Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(), _stream()), "ssm_bwd")
+    return {"W_cat": gW, "b_cat": gb, "A_log": gA, "D": gD, "scale": gS, "grad_u": gu,
+            "delta_h0": dh0, "dA0": dA0}

@@ -1,0 +1,146 @@
+"""PGFMambaBlock / PGFMambaSequential with the API of the reference's pgf_mamba_block.py
+(:16-322), on libpgf.so.
+
+pgf_forward runs the whole sequence through the chunked CUDA scan (the reference loops over
+blocks of ``block_size`` in Python; the kernels keep per-chunk boundary states instead of the
+(L, B, d, N) trajectory, which is the same O(1)-in-L state memory).  pgf_backward recomputes the
+forward from the layer input exactly as the reference does (:155-179) and returns the same
+gradient dictionary (:137-153) and ``grad_input``.
+"""
+from __future__ import annotations
+
+from typing import Any, Dict, List, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .pgf_ffn import FFNFunction, pgf_ffn_forward, pgf_ffn_grad
+from .pgf_rmsnorm import RMSNorm
+from .train_singlemamba_optimized import SingleLayerMambaPGF, _cat_weights
+
+
+class PGFMambaBlock(nn.Module):
+    """x -> RMSNorm -> SSM -> +x -> RMSNorm -> FFN -> +x (pgf_mamba_block.py:16-68)."""
+
+    def __init__(self, d_model: int, d_state: int = 16, d_ff: Optional[int] = None,
+                 block_size: int = 128, output_activation: Optional[str] = None,
+                 ffn_activation: str = "gelu"):
+        super().__init__()
+        self.d_model = d_model
+        self.d_state = d_state
+        self.d_ff = d_ff or 4 * d_model
+        self.block_size = block_size
+        self.ffn_activation = ffn_activation
+        self.norm1 = RMSNorm(d_model)
+        self.mamba = SingleLayerMambaPGF(d_model, d_state, output_activation=output_activation)
+        self.norm2 = RMSNorm(d_model)
+        self.W1 = nn.Parameter(torch.randn(self.d_ff, d_model) * 0.02)
+        self.b1 = nn.Parameter(torch.zeros(self.d_ff))
+        self.W2 = nn.Parameter(torch.randn(d_model, self.d_ff) * 0.02)
+        self.b2 = nn.Parameter(torch.zeros(d_model))
+        nn.init.xavier_uniform_(self.W1)
+        nn.init.xavier_uniform_(self.W2)
+
+    @property
+    def reference_scale_grad(self) -> bool:
+        return self.mamba.reference_scale_grad
+
+    @reference_scale_grad.setter
+    def reference_scale_grad(self, v: bool):
+        self.mamba.reference_scale_grad = bool(v)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """Autograd forward (pgf_mamba_block.py:51-68) through the CUDA autograd functions."""
+        res = x
+        x = self.norm1(x)
+        x = self.mamba.forward_standard(x)
+        x = x + res
+        res = x
+        h = self.norm2(x)
+        B, L, D = h.shape
+        f = FFNFunction.apply(h.reshape(-1, D), self.W1, self.b1, self.W2, self.b2, self.ffn_activation)
+        return f.reshape(B, L, D) + res
+
+    @torch.no_grad()
+    def pgf_forward(self, x: torch.Tensor) -> torch.Tensor:
+        """pgf_mamba_block.py:70-126."""
+        B, L, D = x.shape
+        xn = self.norm1.pgf_forward(x, block_size=self.block_size)
+        y, _ = self.mamba.ssm_forward(xn)
+        x1 = y + x
+        xn2 = self.norm2.pgf_forward(x1, block_size=self.block_size)
+        f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
+                            block_size=self.block_size, activation=self.ffn_activation)
+        return f.reshape(B, L, D) + x1
+
+    @torch.no_grad()
+    def pgf_backward(self, x: torch.Tensor, g_out: torch.Tensor, fp32_accum: bool = True) -> Dict[str, Any]:
+        """pgf_mamba_block.py:128-249."""
+        B, L, D = x.shape
+        g_out = g_out.to(x.dtype)
+        xn1 = self.norm1.pgf_forward(x, block_size=self.block_size)              # :157
+        y, _ = self.mamba.ssm_forward(xn1)                                       # :163-178
+        m_out = y + x
+        xn2 = self.norm2.pgf_forward(m_out, block_size=self.block_size)          # :179
+        fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
+                          block_size=self.block_size, activation=self.ffn_activation,
+                          compute_input_grads=True)                              # :183-192
+        n2 = self.norm2.pgf_grad(m_out, fr["grad_x"].reshape(B, L, D), compute_input_grads=True)  # :196
+        g_m = n2["grad_x"] + g_out                                               # :202
+        W, b = _cat_weights(self.mamba)
+        m = self.mamba
+        r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, act=m.output_activation)  # :206-234
+        n1 = self.norm1.pgf_grad(x, r["grad_u"], compute_input_grads=True)       # :237-242
+        d, N = self.d_model, self.d_state
+        gscale = r["scale"].sum().expand(d).clone() if m.reference_scale_grad else r["scale"]
+        grads = {
+            "W1": fr["grad_W1"], "b1": fr["grad_b1"], "W2": fr["grad_W2"], "b2": fr["grad_b2"],
+            "mamba.A_log": r["A_log"], "mamba.D": r["D"], "mamba.scale": gscale,
+            "mamba.dt_proj.weight": r["W_cat"][:d], "mamba.dt_proj.bias": r["b_cat"][:d],
+            "mamba.B_proj.weight": r["W_cat"][d:d + N], "mamba.B_proj.bias": r["b_cat"][d:d + N],
+            "mamba.C_proj.weight": r["W_cat"][d + N:], "mamba.C_proj.bias": r["b_cat"][d + N:],
+            "norm1.weight": n1["grad_weight"], "norm2.weight": n2["grad_weight"],
+        }
+        return {"grads": grads, "grad_input": n1["grad_x"] + g_m}               # :246-249
+
+    @torch.no_grad()
+    def pgf_forward_mamba_only(self, x_norm: torch.Tensor) -> torch.Tensor:
+        """pgf_mamba_block.py:251-275."""
+        y, _ = self.mamba.ssm_forward(x_norm)
+        return y
+
+
+class PGFMambaSequential(nn.Module):
+    """pgf_mamba_block.py:277-322."""
+
+    def __init__(self, layers: List[PGFMambaBlock]):
+        super().__init__()
+        self.layers = nn.ModuleList(layers)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        for layer in self.layers:
+            x = layer(x)
+        return x
+
+    @torch.no_grad()
+    def pgf_train_step(self, x: torch.Tensor, target: torch.Tensor, loss_fn: Any) -> Dict[str, Any]:
+        layer_inputs = []
+        cur = x
+        for layer in self.layers:
+            layer_inputs.append(cur.detach().clone())
+            cur = layer.pgf_forward(cur)
+        loss, g_out = loss_fn(cur, target)
+        all_grads = {}
+        g = g_out
+        for i in reversed(range(len(self.layers))):
+            res = self.layers[i].pgf_backward(layer_inputs.pop(), g)
+            for k, v in res["grads"].items():
+                all_grads[f"layers.{i}.{k}"] = v
+            g = res["grad_input"]
+            del res
+        return {"loss": loss, "grads": all_grads}
+
+
+__all__ = ["PGFMambaBlock", "PGFMambaSequential"]

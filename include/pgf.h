@@ -1,0 +1,197 @@
+/*
+ * pgf.h -- C-ABI of the B200 (sm_100a) PGF training-step library, libpgf.so.
+ *
+ * The reference (zhry915/icml) is pure Python: it has no FFI of its own.  Each entry point
+ * below replaces one block-streamed operator of its Python modules; the citation next to each
+ * names the reference function whose arguments and results it reproduces.  The Python
+ * modules in icml_b200/ keep the reference signatures and call these through ctypes.
+ *
+ * Conventions
+ *  - All tensor arguments are device pointers to contiguous row-major buffers; sizes are
+ *    element counts.  `dtype` selects the activation type (PGF_DTYPE_F32 or PGF_DTYPE_BF16);
+ *    parameters and parameter gradients are always float32, gradients accumulate in float32.
+ *  - Every call is stream-ordered on `stream` (a cudaStream_t), never synchronises, never
+ *    allocates device memory: scratch comes from the caller through (`ws`, `ws_bytes`), sized
+ *    by the matching *_workspace() function.
+ *  - Return value: PGF_OK (0) or a PGF_ERR_* code; pgf_last_error() (thread-local) describes
+ *    the last failure.  Nothing aborts, throws or exits.
+ *  - `accumulate` = 1 adds parameter gradients into the output buffers instead of overwriting.
+ *  - Results are deterministic: no floating-point atomics; reductions run in a fixed order.
+ */
+#ifndef PGF_H_
+#define PGF_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PGF_OK 0
+#define PGF_ERR_INVALID 1
+#define PGF_ERR_CUDA 2
+#define PGF_ERR_WORKSPACE 3
+#define PGF_ERR_UNSUPPORTED 4
+
+#define PGF_DTYPE_F32 0
+#define PGF_DTYPE_BF16 1
+
+/* activation codes: FFN (pgf_ffn.py:81-88) and SSM output activation
+   (train_singlemamba_optimized.py:103-114) */
+#define PGF_ACT_NONE 0
+#define PGF_ACT_GELU 1
+#define PGF_ACT_RELU 2
+#define PGF_ACT_TANH 3
+
+typedef void* pgf_stream_t; /* cudaStream_t */
+
+/* Last error message of the calling thread ("" if none). */
+const char* pgf_last_error(void);
+/* Library version, major*10000 + minor*100 + patch. */
+int pgf_version(void);
+
+/* ------------------------------------------------------------------------------------------
+ * RMSNorm.  Replaces RMSNorm.pgf_forward (pgf_rmsnorm.py:89-117, math :10-18) and
+ * RMSNorm.pgf_grad (pgf_rmsnorm.py:157-214, math :22-51).
+ *   y = x / sqrt(mean(x^2) + eps) * weight                      x, y: (rows, dim)
+ *   grad_weight = sum_rows g * x / rms;  grad_x = g*w/rms - x * sum(g*w*x) / (rms^3 * dim)
+ * ------------------------------------------------------------------------------------------ */
+int pgf_rmsnorm_fwd(const void* x, const float* weight, void* y, int64_t rows, int64_t dim,
+                    float eps, int dtype, pgf_stream_t stream);
+size_t pgf_rmsnorm_bwd_workspace(int64_t rows, int64_t dim);
+int pgf_rmsnorm_bwd(const void* x, const void* g, const float* weight, void* grad_x /* nullable */,
+                    float* grad_weight, int accumulate, int64_t rows, int64_t dim, float eps,
+                    int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Embedding.  Replaces pgf_embedding_forward (pgf_embedding.py:74-124) and
+ * pgf_embedding_grad (pgf_embedding.py:14-71).  The gradient is a deterministic
+ * sort-by-id then segment-sum (the reference's index_add_ is atomic on CUDA).
+ *   ids: (n_tokens,) int64 in [0, vocab);  weight, grad_weight: (vocab, dim) float32;
+ *   y, g: (n_tokens, dim) in `dtype`.
+ * ------------------------------------------------------------------------------------------ */
+int pgf_embedding_fwd(const int64_t* ids, const float* weight, void* y, int64_t n_tokens,
+                      int64_t vocab, int64_t dim, int dtype, pgf_stream_t stream);
+size_t pgf_embedding_bwd_workspace(int64_t n_tokens, int64_t vocab, int64_t dim);
+int pgf_embedding_bwd(const int64_t* ids, const void* g, float* grad_weight, int accumulate,
+                      int64_t n_tokens, int64_t vocab, int64_t dim, int dtype, void* ws,
+                      size_t ws_bytes, pgf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Dense product with fused epilogue (the matmuls of pgf_ffn.py:43-53, 90-112,
+ * pgf_lm_head.py:20-40 and train_singlemamba_optimized.py:120, 440-461).
+ *   D[m,n] = epi( alpha * sum_k opA[m,k] * opB[n,k] )
+ *   opA[m,k] = a_trans ? A[k*lda + m] : A[m*lda + k]       (M x K)
+ *   opB[n,k] = b_trans ? B[k*ldb + n] : B[n*ldb + k]       (N x K, i.e. nn.Linear weight layout)
+ * Epilogue order: v = alpha*acc (+ bias[n]); GELU/RELU: aux_out[m,n] = v (if given), v = act(v);
+ * DGELU/DRELU: v *= act'(aux[m,n]); v += addend[m,n] (if given); v += D[m,n] (if accumulate).
+ * ------------------------------------------------------------------------------------------ */
+#define PGF_EPI_NONE 0
+#define PGF_EPI_GELU 1
+#define PGF_EPI_RELU 2
+#define PGF_EPI_DGELU 3
+#define PGF_EPI_DRELU 4
+
+typedef struct pgf_epilogue {
+  int kind;
+  float alpha;
+  const float* bias;      /* (N,) or NULL */
+  const void* aux;        /* DGELU/DRELU pre-activation (M x N) */
+  int aux_dtype;
+  int64_t ld_aux;
+  void* aux_out;          /* GELU/RELU: pre-activation output (M x N) or NULL */
+  int aux_out_dtype;
+  int64_t ld_aux_out;
+  const void* addend;     /* (M x N) or NULL */
+  int addend_dtype;
+  int64_t ld_addend;
+  int accumulate;         /* D must be float32 */
+} pgf_epilogue;
+
+int pgf_gemm(int64_t M, int64_t N, int64_t K, const void* A, int a_dtype, int64_t lda, int a_trans,
+             const void* B, int b_dtype, int64_t ldb, int b_trans, void* D, int d_dtype,
+             int64_t ldd, const pgf_epilogue* epi, pgf_stream_t stream);
+
+/* Column sums: out[n] (+)= sum_m X[m*ld + n]; deterministic (fixed-order two-level sum).
+   The bias gradients of pgf_ffn.py:95,109 and train_singlemamba_optimized.py:443. */
+size_t pgf_colsum_workspace(int64_t M, int64_t N);
+int pgf_colsum(const void* X, int dtype, int64_t M, int64_t N, int64_t ld, float* out,
+               int accumulate, void* ws, size_t ws_bytes, pgf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * FFN.  Replaces pgf_ffn_forward (pgf_ffn.py:261-307, block math :34-55) and pgf_ffn_grad
+ * (pgf_ffn.py:183-258, block math :58-117 with the missing grad_W1 = grad_z^T x).
+ *   y = act(x W1^T + b1) W2^T + b2, x: (rows, d_in), W1: (d_hidden, d_in), W2: (d_out, d_hidden).
+ * Rows are processed in tiles so the workspace stays bounded by the tile, not by rows.
+ * ------------------------------------------------------------------------------------------ */
+size_t pgf_ffn_workspace(int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out, int dtype,
+                         int backward);
+int pgf_ffn_fwd(const void* x, const float* W1, const float* b1, const float* W2, const float* b2,
+                void* y, int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out,
+                int activation, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const float* b1, const float* W2,
+                float* grad_W1, float* grad_b1, float* grad_W2, float* grad_b2,
+                void* grad_x /* nullable */, int accumulate, int64_t rows, int64_t d_in,
+                int64_t d_hidden, int64_t d_out, int activation, int dtype, void* ws,
+                size_t ws_bytes, pgf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * LM head.  pgf_lm_head_forward (pgf_lm_head.py:96-130): logits (float32, T x V) = h W^T.
+ * pgf_lm_head_grad (pgf_lm_head.py:45-93): grad_W = g^T h, grad_h = g W.
+ * ------------------------------------------------------------------------------------------ */
+size_t pgf_lm_head_workspace(int64_t T, int64_t V, int64_t d, int dtype);
+int pgf_lm_head_fwd(const void* h, const float* W, float* logits, int64_t T, int64_t V, int64_t d,
+                    int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_lm_head_bwd(const void* h, const float* g_logits, const float* W, float* grad_W,
+                    void* grad_h /* nullable */, int accumulate, int64_t T, int64_t V, int64_t d,
+                    int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+
+/* LM head fused with the mean cross entropy of test_multi_layer_grads.py:74-86 /
+ * train_wikitext_rebuttal.py:116-125, tiled over tokens and vocabulary: the (T x V) logits and
+ * their gradient exist only one (token tile x vocab tile) at a time.
+ *   fwd: loss_rows[t] = lse_t - logit[t, target_t], lse[t] = logsumexp_v logit[t, v].
+ *   bwd: g = (softmax - onehot(target)) * grad_scale; grad_W (+)= g^T h; grad_h = g W. */
+size_t pgf_lm_head_ce_workspace(int64_t T, int64_t V, int64_t d, int dtype);
+int pgf_lm_head_ce_fwd(const void* h, const float* W, const int64_t* targets, float* loss_rows,
+                       float* lse, int64_t T, int64_t V, int64_t d, int dtype, void* ws,
+                       size_t ws_bytes, pgf_stream_t stream);
+int pgf_lm_head_ce_bwd(const void* h, const float* W, const int64_t* targets, const float* lse,
+                       float grad_scale, float* grad_W, void* grad_h, int accumulate, int64_t T,
+                       int64_t V, int64_t d, int dtype, void* ws, size_t ws_bytes,
+                       pgf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Selective-scan layer of SingleLayerMambaPGF (train_singlemamba_optimized.py:88-472).
+ * Parameters: W_cat = [dt_proj.weight; B_proj.weight; C_proj.weight] (D+2N, D),
+ * b_cat (D+2N,), A_log (N,), Dp = D (D,), scale (D,).  u, y, g, grad_u: (Bsz, L, D) in dtype.
+ *
+ * pgf_ssm_fwd: project (:116-124), discretise (:140-144), scan (:41-52), output map
+ *   y = (act(sum_n C h) + Dp*u) * scale (pgf_mamba_block.py:86-112), starting from h_init
+ *   (NULL = zeros).  h_final (nullable) receives the state after the last token.
+ * pgf_ssm_bwd: _pass2_block_direct_grad (:350-472) over the whole range [0, L): recompute from
+ *   h_init, reverse adjoint scan seeded by (dh_end, dA_end) (NULL = zeros / ones), all
+ *   parameter gradients and grad_u.  dh_start / dA_start (nullable) return the reference's
+ *   (delta_h_block[0], dA[0]).  grad_scale is the per-channel gradient sum(g*y_raw) over
+ *   (batch, time) -- autograd's value for the (D,) parameter; the reference's scalar
+ *   (:400) is recovered by summing it.
+ * N must be 16.  act in {NONE, RELU, TANH}.
+ * ------------------------------------------------------------------------------------------ */
+size_t pgf_ssm_workspace(int64_t Bsz, int64_t L, int64_t D, int64_t N, int dtype, int backward);
+int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                const float* Dp, const float* scale, const float* h_init, void* y,
+                float* h_final, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype,
+                void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                const float* A_log, const float* Dp, const float* scale, const float* h_init,
+                const float* dh_end, const float* dA_end, float* grad_W_cat, float* grad_b_cat,
+                float* grad_A_log, float* grad_Dp, float* grad_scale, void* grad_u,
+                float* dh_start, float* dA_start, int accumulate, int64_t Bsz, int64_t L,
+                int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                pgf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PGF_H_ */

@@ -1,0 +1,303 @@
+"""Parity of each CUDA operator (through the C-ABI) against the CPU oracle on seeded inputs."""
+import math
+
+import pytest
+import torch
+
+from oracle import pgf_oracle as O
+from tests.conftest import golden
+from tests.parity import BF16_RTOL, assert_close, rel_err
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from icml_b200 import ops as _ops
+    return _ops
+
+
+def _gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+# ----------------------------------------------------------------------------- RMSNorm
+@pytest.mark.parametrize("shape", [(3, 40, 48), (7, 1024), (5, 100), (1, 1, 4096), (0, 64)])
+@pytest.mark.parametrize("eps", [1e-6, 1e-5])
+def test_rmsnorm_f32(ops, shape, eps):
+    g = _gen(1)
+    x = torch.randn(*shape, generator=g)
+    gy = torch.randn(*shape, generator=g)
+    w = 1 + 0.02 * torch.randn(shape[-1], generator=g)
+    y = ops.rmsnorm_fwd(x.to(DEV), w.to(DEV), eps)
+    assert_close(y, O.rmsnorm_forward(x.double(), w.double(), eps), name="y")
+    gw, gx = ops.rmsnorm_bwd(x.to(DEV), gy.to(DEV), w.to(DEV), eps)
+    rgw, rgx = O.rmsnorm_grad(x.double(), gy.double(), w.double(), eps)
+    assert_close(gx, rgx, name="grad_x")
+    assert_close(gw, rgw, name="grad_weight")
+
+
+def test_rmsnorm_golden(ops):
+    for eps in ("1e-06", "1e-05"):
+        c = golden("components.pt")[f"rmsnorm_{eps}"]
+        y = ops.rmsnorm_fwd(c["x"].to(DEV), c["w"].to(DEV), c["eps"])
+        assert_close(y, c["y"])
+        gw, gx = ops.rmsnorm_bwd(c["x"].to(DEV), c["g"].to(DEV), c["w"].to(DEV), c["eps"])
+        assert_close(gw, c["grad_weight"])
+        assert_close(gx, c["grad_x"])
+
+
+def test_rmsnorm_bf16(ops):
+    g = _gen(2)
+    x = torch.randn(8, 256, 1024, generator=g)
+    gy = torch.randn(8, 256, 1024, generator=g)
+    w = 1 + 0.02 * torch.randn(1024, generator=g)
+    xb, gb = x.bfloat16(), gy.bfloat16()
+    y = ops.rmsnorm_fwd(xb.to(DEV), w.to(DEV), 1e-5)
+    assert y.dtype == torch.bfloat16
+    ref = O.rmsnorm_forward(xb.double(), w.double(), 1e-5)
+    assert rel_err(y, ref) < 1e-2
+    gw, gx = ops.rmsnorm_bwd(xb.to(DEV), gb.to(DEV), w.to(DEV), 1e-5)
+    rgw, rgx = O.rmsnorm_grad(xb.double(), gb.double(), w.double(), 1e-5)
+    assert rel_err(gx, rgx) < 1e-2
+    assert rel_err(gw, rgw) < 1e-3
+
+
+# ----------------------------------------------------------------------------- embedding
+@pytest.mark.parametrize("n,V,d", [(100, 30, 24), (5000, 300, 64), (20000, 50257, 32), (1, 7, 8),
+                                   (3000, 3, 16)])
+def test_embedding(ops, n, V, d):
+    g = _gen(3)
+    ids = O.zipf_tokens(n, V, generator=g)
+    W = torch.randn(V, d, generator=g)
+    gy = torch.randn(n, d, generator=g)
+    y = ops.embedding_fwd(ids.to(DEV), W.to(DEV))
+    assert torch.equal(y.cpu(), W[ids])
+    gw = ops.embedding_bwd(ids.to(DEV), gy.to(DEV), V)
+    assert_close(gw, O.embedding_grad(ids, gy.double(), W.double()), name="grad_weight")
+    gw2 = ops.embedding_bwd(ids.to(DEV), gy.to(DEV), V)
+    assert torch.equal(gw, gw2), "embedding gradient must be bitwise reproducible"
+
+
+def test_embedding_golden(ops):
+    c = golden("components.pt")["embedding"]
+    y = ops.embedding_fwd(c["ids"].to(DEV), c["W"].to(DEV))
+    assert torch.equal(y.cpu(), c["y"])
+    gw = ops.embedding_bwd(c["ids"].to(DEV), c["g"].to(DEV), c["W"].shape[0])
+    assert_close(gw, c["grad_weight"])
+
+
+def test_embedding_single_id_long_segment(ops):
+    """One id repeated across many segment tiles (the Zipf head): ordered multi-tile carry."""
+    n, d = 10000, 40
+    ids = torch.zeros(n, dtype=torch.long)
+    ids[::7] = 5
+    gy = torch.randn(n, d, generator=_gen(4))
+    gw = ops.embedding_bwd(ids.to(DEV), gy.to(DEV), 9)
+    ref = torch.zeros(9, d, dtype=torch.float64).index_add_(0, ids, gy.double())
+    assert_close(gw, ref)
+
+
+# ----------------------------------------------------------------------------- dense products
+@pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (67, 45, 33), (256, 288, 256), (130, 1000, 64)])
+def test_gemm_layouts_f32(ops, at, bt, M, N, K):
+    g = _gen(5)
+    A = torch.randn(K, M, generator=g) if at else torch.randn(M, K, generator=g)
+    B = torch.randn(K, N, generator=g) if bt else torch.randn(N, K, generator=g)
+    ref = (A.double().t() if at else A.double()) @ (B.double() if bt else B.double().t())
+    D = ops.gemm(A.to(DEV), B.to(DEV), a_trans=bool(at), b_trans=bool(bt))
+    assert_close(D, ref, rtol=1e-5)
+
+
+def test_gemm_epilogues(ops):
+    g = _gen(6)
+    M, N, K = 70, 90, 40
+    A, B = torch.randn(M, K, generator=g), torch.randn(N, K, generator=g)
+    bias, aux, add = torch.randn(N, generator=g), torch.randn(M, N, generator=g), torch.randn(M, N, generator=g)
+    z = A.double() @ B.double().t() + bias.double()
+    zo = torch.empty(M, N, device=DEV)
+    h = ops.gemm(A.to(DEV), B.to(DEV), bias=bias.to(DEV), epilogue="gelu", aux_out=zo)
+    assert_close(zo, z)
+    assert_close(h, O.gelu_tanh(z))
+    d = ops.gemm(A.to(DEV), B.to(DEV), epilogue="dgelu", aux=aux.to(DEV), addend=add.to(DEV))
+    assert_close(d, (A.double() @ B.double().t()) * O.gelu_tanh_prime(aux.double()) + add.double())
+    acc = torch.randn(M, N, generator=g)
+    out = acc.clone().to(DEV)
+    ops.gemm(A.to(DEV), B.to(DEV), out=out, accumulate=True, alpha=0.5)
+    assert_close(out, acc.double() + 0.5 * (A.double() @ B.double().t()))
+
+
+def test_colsum(ops):
+    X = torch.randn(1000, 77, generator=_gen(7))
+    assert_close(ops.colsum(X.to(DEV)), X.double().sum(0))
+
+
+# ----------------------------------------------------------------------------- FFN
+@pytest.mark.parametrize("act", ["gelu", "relu"])
+@pytest.mark.parametrize("rows,d,dh", [(70, 24, 64), (1000, 256, 1024), (1, 32, 32)])
+def test_ffn_f32(ops, act, rows, d, dh):
+    g = _gen(8)
+    x = torch.randn(rows, d, generator=g)
+    gy = torch.randn(rows, d, generator=g)
+    a1 = math.sqrt(6 / (d + dh))
+    W1 = (torch.rand(dh, d, generator=g) * 2 - 1) * a1
+    W2 = (torch.rand(d, dh, generator=g) * 2 - 1) * a1
+    b1, b2 = 0.1 * torch.randn(dh, generator=g), 0.1 * torch.randn(d, generator=g)
+    args = [t.to(DEV) for t in (W1, b1, W2, b2)]
+    y = ops.ffn_fwd(x.to(DEV), *args, activation=act)
+    dd = [t.double() for t in (W1, b1, W2, b2)]
+    assert_close(y, O.ffn_forward(x.double(), *dd, act), name="y")
+    r = ops.ffn_bwd(x.to(DEV), gy.to(DEV), args[0], args[1], args[2], activation=act)
+    ref = O.ffn_grad(x.double(), gy.double(), *dd, act)
+    for k in ("grad_W1", "grad_b1", "grad_W2", "grad_b2", "grad_x"):
+        assert_close(r[k], ref[k], name=k)
+
+
+def test_ffn_golden(ops):
+    for act in ("gelu", "relu"):
+        c = golden("components.pt")[f"ffn_{act}"]
+        args = [c[k].to(DEV) for k in ("W1", "b1", "W2", "b2")]
+        assert_close(ops.ffn_fwd(c["x"].to(DEV), *args, activation=act), c["y"])
+        r = ops.ffn_bwd(c["x"].to(DEV), c["g"].to(DEV), args[0], args[1], args[2], activation=act)
+        for k in ("grad_W1", "grad_b1", "grad_W2", "grad_b2", "grad_x"):
+            assert_close(r[k], c[k], name=k)
+
+
+# ----------------------------------------------------------------------------- LM head
+def test_lm_head_golden(ops):
+    c = golden("components.pt")["lm_head"]
+    assert_close(ops.lm_head_fwd(c["h"].to(DEV), c["W"].to(DEV)), c["logits"])
+    gW, gh = ops.lm_head_bwd(c["h"].to(DEV), c["g_logits"].to(DEV), c["W"].to(DEV))
+    assert_close(gW, c["grad_W_lm_head"])
+    assert_close(gh, c["grad_hidden"])
+
+
+@pytest.mark.parametrize("T,V,d", [(50, 40, 24), (300, 9000, 64), (17, 20000, 32)])
+def test_lm_head_ce_f32(ops, T, V, d):
+    g = _gen(9)
+    h = torch.randn(T, d, generator=g)
+    W = 0.3 * torch.randn(V, d, generator=g)
+    tg = torch.randint(0, V, (T,), generator=g)
+    loss_rows, lse = ops.lm_head_ce_fwd(h.to(DEV), W.to(DEV), tg.to(DEV))
+    logits = h.double() @ W.double().t()
+    ref_lse = torch.logsumexp(logits, -1)
+    assert_close(lse, ref_lse, name="lse")
+    assert_close(loss_rows, ref_lse - logits[torch.arange(T), tg], name="loss_rows")
+    loss, gl = O.ce_loss_and_grad(logits, tg)
+    assert abs(loss_rows.mean().item() - loss.item()) < 1e-5
+    gW, gh = ops.lm_head_ce_bwd(h.to(DEV), W.to(DEV), tg.to(DEV), lse, 1.0 / T)
+    rgW, rgh = O.lm_head_grad(h.double(), gl, W.double())
+    assert_close(gW, rgW, name="grad_W")
+    assert_close(gh, rgh, name="grad_h")
+
+
+# ----------------------------------------------------------------------------- selective scan
+def _ssm_case(Bsz, L, D, seed, carries=True):
+    g = _gen(seed)
+    p = O.ssm_init(D, 16, g)
+    p["scale"] = p["scale"] * (0.5 + torch.rand(D, generator=g))
+    p["D"] = p["D"] * (0.5 + torch.rand(D, generator=g))
+    p["A_log"] = p["A_log"] + 0.1 * torch.randn(16, generator=g)
+    u = torch.randn(Bsz, L, D, generator=g)
+    gy = torch.randn(Bsz, L, D, generator=g)
+    h0 = 0.5 * torch.randn(Bsz, D, 16, generator=g) if carries else torch.zeros(Bsz, D, 16)
+    dh = 0.3 * torch.randn(Bsz, D, 16, generator=g) if carries else torch.zeros(Bsz, D, 16)
+    dA = (0.5 + 0.5 * torch.rand(Bsz, D, 16, generator=g)) if carries else torch.ones(Bsz, D, 16)
+    return p, u, gy, h0, dh, dA
+
+
+def _wcat(p):
+    return torch.cat([p["dt_w"], p["B_w"], p["C_w"]], 0), torch.cat([p["dt_b"], p["B_b"], p["C_b"]], 0)
+
+
+def _run_ssm(ops, p, u, gy, h0, dh, dA, act=None, dtype=torch.float32):
+    W, b = _wcat(p)
+    dv = lambda t: t.to(DEV)  # noqa: E731
+    y, hf = ops.ssm_fwd(dv(u).to(dtype), dv(W), dv(b), dv(p["A_log"]), dv(p["D"]), dv(p["scale"]),
+                        h_init=dv(h0), act=act, want_h_final=True)
+    r = ops.ssm_bwd(dv(u).to(dtype), dv(gy).to(dtype), dv(W), dv(b), dv(p["A_log"]), dv(p["D"]),
+                    dv(p["scale"]), h_init=dv(h0), dh_end=dv(dh), dA_end=dv(dA), act=act, want_carry=True)
+    return y, hf, r
+
+
+def _ref_ssm(p, u, gy, h0, dh, dA, act=None):
+    pd = {k: v.double() for k, v in p.items()}
+    y, _, hf = O.ssm_forward(pd, u.double(), u.shape[1], h0=h0.double(), act=act)
+    r = O.ssm_block_grad(pd, u.double(), gy.double(), h0.double(), dh.double(), dA.double(), act=act)
+    return y, hf, r
+
+
+@pytest.mark.parametrize("Bsz,L,D", [(1, 1, 32), (2, 7, 32), (2, 100, 64), (3, 333, 100),
+                                     (1, 1000, 128), (2, 512, 128), (1, 4100, 256)])
+def test_ssm_f32(ops, Bsz, L, D):
+    p, u, gy, h0, dh, dA = _ssm_case(Bsz, L, D, seed=10 + L)
+    y, hf, r = _run_ssm(ops, p, u, gy, h0, dh, dA)
+    ry, rhf, rr = _ref_ssm(p, u, gy, h0, dh, dA)
+    assert_close(y, ry, name="y")
+    assert_close(hf, rhf, name="h_final")
+    W_ref = torch.cat([rr["dt_w"], rr["B_w"], rr["C_w"]], 0)
+    b_ref = torch.cat([rr["dt_b"], rr["B_b"], rr["C_b"]], 0)
+    assert_close(r["W_cat"], W_ref, name="grad_W_cat")
+    assert_close(r["b_cat"], b_ref, name="grad_b_cat")
+    assert_close(r["A_log"], rr["A_log"], name="grad_A_log")
+    assert_close(r["D"], rr["D"], name="grad_D")
+    assert_close(r["scale"], rr["scale"], name="grad_scale")
+    assert_close(r["grad_u"], rr["grad_u"], name="grad_u")
+    assert_close(r["delta_h0"], rr["delta_h0"], name="delta_h0")
+    assert_close(r["dA0"], rr["dA0"], name="dA0")
+
+
+@pytest.mark.parametrize("act", ["tanh", "relu"])
+def test_ssm_output_activation(ops, act):
+    p, u, gy, h0, dh, dA = _ssm_case(2, 200, 64, seed=21)
+    y, hf, r = _run_ssm(ops, p, u, gy, h0, dh, dA, act=act)
+    ry, rhf, rr = _ref_ssm(p, u, gy, h0, dh, dA, act=act)
+    assert_close(y, ry, name="y")
+    for k in ("A_log", "D", "scale"):
+        assert_close(r[k], rr[k], name=k)
+    assert_close(r["grad_u"], rr["grad_u"], name="grad_u")
+
+
+def test_ssm_golden_block(ops):
+    """The reference's own _pass2_block_direct_grad outputs (scale: reference scalar = sum)."""
+    G = golden("ssm_block.pt")
+    sd = G["params"]
+    p = {"A_log": sd["A_log"], "D": sd["D"], "scale": sd["scale"], "dt_w": sd["dt_proj.weight"],
+         "dt_b": sd["dt_proj.bias"], "B_w": sd["B_proj.weight"], "B_b": sd["B_proj.bias"],
+         "C_w": sd["C_proj.weight"], "C_b": sd["C_proj.bias"]}
+    _, _, r = _run_ssm(ops, p, G["u"], G["g"], G["h0"], G["delta_h_next"], G["dA_next"])
+    o = G["out"]
+    d, N = p["D"].shape[0], 16
+    assert_close(r["A_log"], o["A_log"], name="A_log")
+    assert_close(r["D"], o["D"], name="D")
+    assert_close(r["scale"].sum(), o["scale_ref"], name="scale(reference scalar)")
+    assert_close(r["W_cat"][:d], o["dt_w"], name="dt_w")
+    assert_close(r["W_cat"][d:d + N], o["B_w"], name="B_w")
+    assert_close(r["W_cat"][d + N:], o["C_w"], name="C_w")
+    assert_close(r["b_cat"][:d], o["dt_b"], name="dt_b")
+    assert_close(r["delta_h0"], o["delta_h0"], name="delta_h0")
+    assert_close(r["dA0"], o["dA0"], name="dA0")
+    assert_close(r["grad_u"], o["grad_u"], name="grad_u")
+
+
+def test_ssm_deterministic(ops):
+    p, u, gy, h0, dh, dA = _ssm_case(1, 3000, 128, seed=30)
+    _, _, r1 = _run_ssm(ops, p, u, gy, h0, dh, dA)
+    _, _, r2 = _run_ssm(ops, p, u, gy, h0, dh, dA)
+    for k in ("W_cat", "b_cat", "A_log", "D", "scale", "grad_u"):
+        assert torch.equal(r1[k], r2[k]), k
+
+
+def test_ssm_bf16_activations(ops):
+    p, u, gy, h0, dh, dA = _ssm_case(1, 2048, 256, seed=31, carries=False)
+    ub, gb = u.bfloat16().float(), gy.bfloat16().float()
+    y, _, r = _run_ssm(ops, p, ub, gb, h0, dh, dA, dtype=torch.bfloat16)
+    ry, _, rr = _ref_ssm(p, ub, gb, h0, dh, dA)
+    assert y.dtype == torch.bfloat16
+    assert rel_err(y, ry) < BF16_RTOL
+    assert rel_err(r["A_log"], rr["A_log"]) < BF16_RTOL
+    assert rel_err(r["grad_u"], rr["grad_u"]) < BF16_RTOL
+    W_ref = torch.cat([rr["dt_w"], rr["B_w"], rr["C_w"]], 0)
+    assert rel_err(r["W_cat"], W_ref) < BF16_RTOL
