@@ -1,0 +1,349 @@
+"""Benchmark of the PGF training step (fwd + bwd + AdamW) on B200.
+
+Workload (default): the 8-layer PGF Mamba language model of the reference's training scripts at
+d_model 256 / d_state 16 / d_ff 1024 / vocab 50257 (reference SSM variant, untied embedding and
+LM head as in train_wikitext_rebuttal.py:58-77), one sequence of L tokens per GPU, synthetic
+Zipf(1.1) token ids, bf16 activations, fp32 weights and AdamW.  N GPUs run N replicas with an NCCL
+gradient all-reduce (data parallel, per-GPU work fixed: weak scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--seq-len L] [--impl b200|reference]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "fwd+bwd tokens/s (8-layer PGF Mamba LM)"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--seq-len", type=int, default=65536)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--d-model", type=int, default=256)
+    ap.add_argument("--d-ff", type=int, default=1024)
+    ap.add_argument("--vocab", type=int, default=50257)
+    ap.add_argument("--block-size", type=int, default=4096)
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
+    ap.add_argument("--cpu-sample-len", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def config_of(a, world):
+    return {
+        "workload": f"8-layer PGF Mamba LM, d_model {a.d_model}, d_state 16, d_ff {a.d_ff}, vocab {a.vocab}, "
+                    f"B={a.batch} x L={a.seq_len} tokens per GPU, bf16 activations / fp32 weights + AdamW",
+        "layers": a.layers, "d_model": a.d_model, "d_state": 16, "d_ff": a.d_ff, "vocab": a.vocab,
+        "global_batch": a.batch * world, "seq_len": a.seq_len, "pgf_block_size": a.block_size,
+        "parallelism": f"dp{world}", "ssm_variant": "reference (d_inner = d_model, shared A)",
+        "l2": "per-step working set (weights, optimizer state, activations) > 126 MB L2; no explicit flush",
+    }
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        load = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(a, kind="port"):
+    """The oracle (CPU restatement of the reference PGF step, float32, all host threads) on a
+    bounded sample of the workload: the same model at L = cpu_sample_len tokens."""
+    from oracle import pgf_oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    blocks = [O.block_init(a.d_model, 16, a.d_ff, g) for _ in range(a.layers)]
+    emb = torch.randn(a.vocab, a.d_model, generator=g) * 0.02
+    lmw = torch.randn(a.vocab, a.d_model, generator=g) * 0.02
+    L = a.cpu_sample_len
+    ids = O.zipf_tokens(L + 1, a.vocab, generator=g).reshape(1, L + 1)
+    bs = min(a.block_size, 128)
+    O.lm_pgf_step(emb, lmw, blocks, ids[:, :-1], ids[:, 1:], bs)  # warm-up
+    times = []
+    t_end = time.time() + 20.0
+    while len(times) < 3 and (not times or time.time() < t_end):
+        t0 = time.perf_counter()
+        O.lm_pgf_step(emb, lmw, blocks, ids[:, :-1], ids[:, 1:], bs)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": L / med, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
+            "sample": f"oracle PGF step (fp32, no optimizer) of the same 8-layer model on B=1 x L={L} "
+                      f"tokens, pgf block {bs}, median of {len(times)} steps after 1 warm-up, "
+                      f"{threads} host threads"}
+
+
+def run_reference(a, rank, world):
+    if rank != 0:
+        return
+    cb = cpu_baseline(a)
+    line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": 1000.0 * a.cpu_sample_len / cb["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference", "config": config_of(a, world),
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def roofline_entry(name, ms_total, n, work_total):
+    """Achieved rate of one kernel (algorithmic work / its average launch time measured with CUDA
+    events in the timed region) against MEASURED_PEAKS.json (sustained bf16 figure: the kernels run
+    inside a long step)."""
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    src = "measured" if peaks else "fallback"
+    t = ms_total / n / 1e3
+    if name.startswith("gemm"):
+        peak = peaks.get("bf16_tflops_sustained", 1400.0)
+        ach = work_total / n / t / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "traffic": None, "kernel": name, "peak_source": src + " (bf16 sustained)",
+                "work_per_launch": work_total / n, "ms_per_launch": t * 1e3}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    ach = work_total / n / t / 1e9
+    return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+            "traffic": None, "kernel": name, "peak_source": src,
+            "work_per_launch": work_total / n, "ms_per_launch": t * 1e3}
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank, world)
+        return
+    run_gpu(a, rank, world, local_rank)
+
+
+def zipf_ids(n, vocab, seed, s=1.1):
+    g = torch.Generator().manual_seed(seed)
+    ranks = torch.arange(1, vocab + 1, dtype=torch.float64)
+    pmf = ranks.pow(-s)
+    cdf = torch.cumsum(pmf / pmf.sum(), 0)
+    return torch.searchsorted(cdf, torch.rand(n, generator=g, dtype=torch.float64)).clamp_(max=vocab - 1)
+
+
+PROF_NAMES = {0: "ssm_chunk_fwd", 1: "ssm_compose", 2: "ssm_out_fwd", 3: "ssm_chunk_bwd",
+              4: "ssm_main_bwd", 5: "gemm_tc", 6: "gemm_simt", 7: "rmsnorm_fwd", 8: "rmsnorm_bwd",
+              9: "embedding", 10: "ce"}
+
+
+def run_gpu(a, rank, world, local_rank):
+    import ctypes
+    from icml_b200 import _lib
+    from icml_b200.lm import PGFLanguageModel
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+        pg = torch.distributed.group.WORLD
+    L = _lib.lib()
+    act = torch.bfloat16 if a.dtype == "bf16" else torch.float32
+    torch.manual_seed(1234)
+    model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act)
+    for p in model.params:  # identical replicas
+        if pg is not None:
+            torch.distributed.broadcast(p.data, 0)
+
+    ids_host = zipf_ids(a.batch * (a.seq_len + 1), a.vocab, seed=100 + rank).reshape(a.batch, a.seq_len + 1)
+    inp_host = ids_host[:, :-1].contiguous().pin_memory()
+    tgt_host = ids_host[:, 1:].contiguous().pin_memory()
+    inp = inp_host.to(dev)
+    tgt = tgt_host.to(dev)
+
+    def allreduce_grads():
+        if pg is None:
+            return
+        grads = [p.grad for p in model.params]
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        torch.distributed.all_reduce(flat)
+        flat.div_(world)
+        o = 0
+        for g in grads:
+            n = g.numel()
+            g.copy_(flat[o:o + n].view_as(g))
+            o += n
+
+    def step(x, y):
+        model.optimizer.zero_grad(set_to_none=True)
+        loss, grads = model.forward_backward(x, y)
+        model._assign(grads)
+        allreduce_grads()
+        model.optimizer.step()
+        return loss
+
+    for _ in range(a.warmup):
+        step(inp, tgt)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if pg is not None:
+            torch.distributed.barrier()
+
+    # ---------------- device-timed region: inputs resident in HBM
+    torch.cuda.reset_peak_memory_stats(dev)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    n0 = L.pgf_launch_count()
+    L.pgf_profile(1)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        loss = step(inp, tgt)
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    L.pgf_profile(0)
+    launches = (L.pgf_launch_count() - n0) // a.steps
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    prof_ms, prof_n, prof_w = {}, {}, {}
+    for i, nm in PROF_NAMES.items():
+        c = ctypes.c_longlong(0)
+        t = ctypes.c_double(0.0)
+        w = ctypes.c_double(0.0)
+        L.pgf_profile_read(i, ctypes.byref(c), ctypes.byref(t), ctypes.byref(w))
+        if c.value:
+            prof_n[nm] = c.value
+            prof_ms[nm] = t.value
+            prof_w[nm] = w.value
+    t_all = torch.tensor([ms], device=dev)
+    if pg is not None:
+        torch.distributed.all_reduce(t_all, op=torch.distributed.ReduceOp.MAX)
+    ms = t_all.item()
+    ms_step = ms / a.steps
+    tokens = a.batch * a.seq_len * world * a.steps
+    value = tokens / (ms / 1e3)
+
+    # ---------------- end to end: host ids -> device each step, loss read back each step
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        x = inp_host.to(dev, non_blocking=True)
+        y = tgt_host.to(dev, non_blocking=True)
+        loss = step(x, y)
+        loss_val = loss.item()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if pg is not None:
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    e2e = tokens / (te.item() / 1e3)
+
+    if rank == 0:
+        dom = max(prof_ms, key=prof_ms.get) if prof_ms else None
+        kernels = {k: {"launches_per_step": prof_n[k] / a.steps, "ms_per_step": prof_ms[k] / a.steps,
+                       "share_of_step": prof_ms[k] / a.steps / ms_step if ms_step else None,
+                       "roofline": roofline_entry(k, prof_ms[k], prof_n[k], prof_w[k])}
+                   for k in prof_ms}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": a.dtype, "data": "synthetic (Zipf 1.1 token ids, random init)",
+            "config": config_of(a, world), "impl": "b200",
+            "peak_hbm_gb": peak_gb, "loss": loss_val, "clocks": clocks,
+            "e2e": {"value": e2e, "unit": UNIT,
+                    "h2d_bytes_per_step": inp_host.numel() * 8 * 2, "d2h_bytes_per_step": 4},
+            "gpu_launches": int(launches),
+            "kernels": kernels, "dominant_kernel": dom,
+            "roofline": kernels[dom]["roofline"] if dom else None,
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(a)
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -37,8 +37,19 @@ void clear_error();
     }                                                                         \
   } while (0)
 
+// Kernel-launch accounting and optional CUDA-event timing of selected kernels (abi.cu).
+enum ProfId {
+  PROF_SSM_CHUNK_FWD = 0, PROF_SSM_COMPOSE, PROF_SSM_OUT_FWD, PROF_SSM_CHUNK_BWD, PROF_SSM_MAIN_BWD,
+  PROF_GEMM_TC, PROF_GEMM_SIMT, PROF_RMSNORM_FWD, PROF_RMSNORM_BWD, PROF_EMBEDDING, PROF_CE, PROF_COUNT
+};
+void count_launch();
+void prof_begin(int id, cudaStream_t s);
+// `work`: algorithmic FLOPs (dense products) or bytes (bandwidth kernels) of the launch
+void prof_end(int id, cudaStream_t s, double work);
+
 #define PGF_LAUNCH_CHECK()                                                    \
   do {                                                                        \
+    ::pgf::count_launch();                                                    \
     cudaError_t e_ = cudaGetLastError();                                      \
     if (e_ != cudaSuccess) {                                                  \
       ::pgf::set_error("%s:%d kernel launch: %s", __FILE__, __LINE__,         \

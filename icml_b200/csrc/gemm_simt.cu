@@ -90,7 +90,9 @@ int run_gemm_simt(const Gemm& g, cudaStream_t s) {
     }
     return PGF_OK;
   }
+  prof_begin(PROF_GEMM_SIMT, s);
   gemm_simt_kernel<<<grid, SG_THREADS, 0, s>>>(g);
+  prof_end(PROF_GEMM_SIMT, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }

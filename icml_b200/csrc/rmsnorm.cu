@@ -114,7 +114,12 @@ static int rms_fwd_dispatch(const T* x, const float* w, T* y, int64_t rows, int 
                             cudaStream_t s) {
   dim3 grid(ceil_div(rows, RMS_WARPS)), block(RMS_WARPS * 32);
   int vpl = ceil_div(dim, 32);
-#define PGF_RMS_F(V) rmsnorm_fwd_kernel<V, T><<<grid, block, 0, s>>>(x, w, y, rows, dim, eps)
+#define PGF_RMS_F(V)                                                                  \
+  do {                                                                                \
+    prof_begin(PROF_RMSNORM_FWD, s);                                                  \
+    rmsnorm_fwd_kernel<V, T><<<grid, block, 0, s>>>(x, w, y, rows, dim, eps);         \
+    prof_end(PROF_RMSNORM_FWD, s, double(rows) * dim * 2.0 * sizeof(T) + dim * 4.0);    \
+  } while (0)
   if (vpl <= 1) PGF_RMS_F(1);
   else if (vpl <= 2) PGF_RMS_F(2);
   else if (vpl <= 4) PGF_RMS_F(4);
@@ -143,7 +148,9 @@ static int rms_bwd_dispatch(const T* x, const T* g, const float* w, T* gx, float
     if (smem > 48 * 1024)                                                                      \
       PGF_CUDA(cudaFuncSetAttribute(rmsnorm_bwd_kernel<V, T>,                                  \
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));  \
+    prof_begin(PROF_RMSNORM_BWD, s);                                                           \
     rmsnorm_bwd_kernel<V, T><<<grid, block, smem, s>>>(x, g, w, gx, part, rows, dim, eps);     \
+    prof_end(PROF_RMSNORM_BWD, s, double(rows) * dim * 3.0 * sizeof(T) + dim * 4.0);           \
   } while (0)
   if (vpl <= 1) PGF_RMS_B(1);
   else if (vpl <= 2) PGF_RMS_B(2);

@@ -424,6 +424,26 @@ __global__ void ssm_param_reduce_kernel(const SsmArgs a, float* __restrict__ gA,
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
+// Algorithmic HBM bytes of the scan kernels (each mandatory tensor once, activations at `es`
+// bytes, boundary states in float32): the denominators of their roofline.
+static double bytes_chunk_fwd(const SsmArgs& a, int es) {
+  const double T = double(a.Bsz) * a.L;
+  return T * es * (2.0 * a.D + NST) + double(a.Bsz) * a.nC * a.D * (NST + 1) * 4.0;
+}
+static double bytes_out_fwd(const SsmArgs& a, int es) {
+  const double T = double(a.Bsz) * a.L;
+  return T * es * (3.0 * a.D + 2.0 * NST) + double(a.Bsz) * a.nC * a.D * NST * 4.0;
+}
+static double bytes_chunk_bwd(const SsmArgs& a, int es) {
+  const double T = double(a.Bsz) * a.L;
+  return T * es * (2.0 * a.D + NST) + double(a.Bsz) * a.nC * a.D * (NST + 2) * 4.0;
+}
+static double bytes_main_bwd(const SsmArgs& a, int es) {
+  // read u, dt_in, g, B, C; write grad_dt_in, grad_u, grad_B, grad_C; boundary state + carry
+  const double T = double(a.Bsz) * a.L;
+  return T * es * (5.0 * a.D + 4.0 * NST) + double(a.Bsz) * a.nC * a.D * NST * 4.0 * 2.0;
+}
+static double bytes_compose(const SsmArgs& a) { return double(a.Bsz) * a.nC * a.D * NST * 4.0 * 2.0; }
 static int64_t pick_tc(int64_t Bsz, int64_t L, int64_t G) {
   int64_t tc = TC_MAX;
   const int64_t target = 4 * 148;
@@ -500,10 +520,14 @@ static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u,
 
 static int ssm_forward_states(const SsmArgs& a, const SsmPlan& p, float* h_final, cudaStream_t s) {
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  prof_begin(PROF_SSM_CHUNK_FWD, s);
   ssm_chunk_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_CHUNK_FWD, s, bytes_chunk_fwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   const int64_t nth = p.Bsz * p.D * NST;
+  prof_begin(PROF_SSM_COMPOSE, s);
   ssm_compose_fwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, h_final);
+  prof_end(PROF_SSM_COMPOSE, s, bytes_compose(a));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
@@ -553,7 +577,9 @@ extern "C" int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat
   a.y = y;
   a.y_bf16 = dtype;
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  prof_begin(PROF_SSM_OUT_FWD, s);
   ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_OUT_FWD, s, bytes_out_fwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
@@ -604,7 +630,9 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
     ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);  // act'(C h) per token and channel
     PGF_LAUNCH_CHECK();
   }
+  prof_begin(PROF_SSM_CHUNK_BWD, s);
   ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   const int64_t nth = Bsz * D * NST;
   ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start);
@@ -613,7 +641,9 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   const size_t smem = (size_t(K) * SSM_THREADS * NS + size_t(SUB) * SSM_WARPS * 32) * 4;
   PGF_CUDA(cudaFuncSetAttribute(ssm_main_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(smem)));
+  prof_begin(PROF_SSM_MAIN_BWD, s);
   ssm_main_bwd_kernel<<<grid, SSM_THREADS, smem, s>>>(a);
+  prof_end(PROF_SSM_MAIN_BWD, s, bytes_main_bwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   ssm_bc_reduce_kernel<<<ceil_div(int64_t(BL) * 32, 256), 256, 0, s>>>(a);
   PGF_LAUNCH_CHECK();

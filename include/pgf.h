@@ -51,6 +51,32 @@ const char* pgf_last_error(void);
 /* Library version, major*10000 + minor*100 + patch. */
 int pgf_version(void);
 
+/* Instrumentation (no counterpart in the reference, which has no native code).
+ * pgf_launch_count: number of kernels this library has launched in the process.
+ * pgf_profile(1) starts recording a CUDA-event pair around each launch of the kernels listed in
+ * PGF_PROF_* (stream-ordered, no synchronisation); pgf_profile(0) stops.  pgf_profile_read
+ * synchronises on the recorded events and returns, for one kernel since the last pgf_profile(1),
+ * its launch count, summed device time and summed algorithmic work: FLOPs (2*M*N*K) for the dense
+ * products, bytes that must cross HBM at least once for the bandwidth kernels. */
+#define PGF_PROF_SSM_CHUNK_FWD 0
+#define PGF_PROF_SSM_COMPOSE 1
+#define PGF_PROF_SSM_OUT_FWD 2
+#define PGF_PROF_SSM_CHUNK_BWD 3
+#define PGF_PROF_SSM_MAIN_BWD 4
+#define PGF_PROF_GEMM_TC 5
+#define PGF_PROF_GEMM_SIMT 6
+#define PGF_PROF_RMSNORM_FWD 7
+#define PGF_PROF_RMSNORM_BWD 8
+#define PGF_PROF_EMBEDDING 9
+#define PGF_PROF_CE 10
+long long pgf_launch_count(void);
+/* Reads and clears the fault flag of the tensor-core engine: 1 if a bounded mbarrier wait expired
+ * in a tcgen05 kernel since the last call (the kernel then skipped its epilogue and returned).
+ * Synchronous; -1 if the flag cannot be read. */
+int pgf_tc_fault(void);
+int pgf_profile(int enable);
+int pgf_profile_read(int id, long long* count, double* total_ms, double* total_work);
+
 /* ------------------------------------------------------------------------------------------
  * RMSNorm.  Replaces RMSNorm.pgf_forward (pgf_rmsnorm.py:89-117, math :10-18) and
  * RMSNorm.pgf_grad (pgf_rmsnorm.py:157-214, math :22-51).

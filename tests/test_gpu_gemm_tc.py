@@ -1,0 +1,62 @@
+"""The tcgen05/TMEM bf16 dense-product engine against a float64 product of the same bf16 inputs."""
+import ctypes
+
+import pytest
+import torch
+
+from tests.parity import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from icml_b200 import ops as _ops
+    return _ops
+
+
+def _tc_launches(fn):
+    from icml_b200 import _lib
+    L = _lib.lib()
+    L.pgf_profile(1)
+    out = fn()
+    torch.cuda.synchronize()
+    L.pgf_profile(0)
+    c, t, w = ctypes.c_longlong(0), ctypes.c_double(0), ctypes.c_double(0)
+    L.pgf_profile_read(5, ctypes.byref(c), ctypes.byref(t), ctypes.byref(w))
+    assert L.pgf_tc_fault() == 0, "tensor-core kernel reported an expired wait"
+    return out, c.value
+
+
+@pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 512), (200, 72, 40), (1000, 300, 1024),
+                                   (64, 1000, 8), (4096, 1024, 256)])
+def test_tc_gemm_layouts(ops, at, bt, M, N, K):
+    g = torch.Generator().manual_seed(M + N + K + 7 * at + 3 * bt)
+    A = (torch.randn(K, M, generator=g) if at else torch.randn(M, K, generator=g)).bfloat16()
+    B = (torch.randn(K, N, generator=g) if bt else torch.randn(N, K, generator=g)).bfloat16()
+    ref = (A.double().t() if at else A.double()) @ (B.double() if bt else B.double().t())
+    D, n = _tc_launches(lambda: ops.gemm(A.to(DEV), B.to(DEV), a_trans=bool(at), b_trans=bool(bt)))
+    assert n == 1, "expected the tcgen05 engine to run"
+    assert_close(D, ref, atol=1e-4, rtol=1e-5)
+
+
+def test_tc_gemm_epilogue_and_bf16_out(ops):
+    g = torch.Generator().manual_seed(3)
+    M, N, K = 300, 500, 256
+    A = torch.randn(M, K, generator=g).bfloat16()
+    B = torch.randn(N, K, generator=g).bfloat16()
+    bias = torch.randn(N, generator=g)
+    z = A.double() @ B.double().t() + bias.double()
+    zo = torch.empty(M, N, device=DEV)
+    h, n = _tc_launches(lambda: ops.gemm(A.to(DEV), B.to(DEV), bias=bias.to(DEV), epilogue="gelu",
+                                         aux_out=zo, out_dtype=torch.bfloat16))
+    assert n == 1 and h.dtype == torch.bfloat16
+    assert_close(zo, z, atol=1e-4)
+    from oracle import pgf_oracle as O
+    assert_close(h.float(), O.gelu_tanh(z), atol=2e-2, rtol=1e-2)
+    acc = torch.randn(M, N, generator=g)
+    out = acc.clone().to(DEV)
+    _tc_launches(lambda: ops.gemm(A.to(DEV), B.to(DEV), out=out, accumulate=True))
+    assert_close(out, acc.double() + A.double() @ B.double().t(), atol=1e-4)
