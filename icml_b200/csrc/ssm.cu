@@ -5,6 +5,12 @@
 // per (batch, channel, state); a thread owns NS = 4 states of one channel, four adjacent lanes
 // cover the N = 16 states, a CTA covers DC = 64 channels of one time chunk of Tc tokens.
 //
+// Inputs reach the kernels through shared memory, ST tokens at a time: the CTA loads the next
+// sub-chunk into registers while it computes the current one, then stores it, already
+// transformed once per (token, channel) -- dt = softplus(dt_in), 1/dt, delta_in -- so the four
+// lanes of a channel never repeat that work.  exp(dt A_n) is exp2(dt * A_n log2 e) and 1/(dt A_n)
+// is (1/dt)(1/A_n): no division per state.
+//
 // Forward (3 kernels): chunk summaries from a zero state (local end state + sum of dt, because
 // prod_t exp(dt_t A_n) = exp(A_n sum_t dt_t)), a sequential compose over chunks giving every
 // chunk's start state (the PGF boundary states), and the output pass re-running each chunk from
@@ -12,10 +18,11 @@
 // Backward (3 kernels + 2 reductions): reverse chunk summaries of the adjoint
 // delta_h_t = exp(dt_{t+1} A) delta_h_{t+1} + delta_in_t C_t from a zero carry, a reverse compose
 // giving each chunk's incoming carry, and the main kernel: it re-runs the chunk from its boundary
-// state keeping checkpoints every SUB tokens in shared memory, then walks the sub-chunks in
-// reverse, re-running each forward into registers and stepping the adjoint back through it while
-// it forms every gradient of _pass2_block_direct_grad (:350-472).  Sums over channels (grad B,
-// grad C) and over tokens (grad A_log, D, scale) go through fixed-order partial buffers.
+// state keeping a checkpoint every ST tokens in shared memory, then walks the sub-chunks in
+// reverse, re-running each one into registers (state and exp(dt A) per token) and stepping the
+// adjoint back through it while it forms every gradient of _pass2_block_direct_grad (:350-472).
+// Sums over channels (grad B, grad C) and over tokens (grad A_log, D, scale) go through
+// fixed-order partial buffers: results are bitwise reproducible.
 #include "gemm.cuh"
 
 namespace pgf {
@@ -26,8 +33,9 @@ constexpr int NS = NST / NQ;         // states per thread
 constexpr int DC = 64;               // channels per CTA
 constexpr int SSM_THREADS = DC * NQ; // 256
 constexpr int SSM_WARPS = SSM_THREADS / 32;
-constexpr int SUB = 8;               // backward sub-chunk (register trajectory length)
+constexpr int ST = 8;                // tokens per staged sub-chunk (= backward register trajectory)
 constexpr int TC_MAX = 128;
+constexpr float LOG2E = 1.4426950408889634f;
 
 struct SsmArgs {
   const void* u; int u_bf16;
@@ -42,7 +50,26 @@ struct SsmArgs {
   void* y; int y_bf16;
   float* actp;
   float* gstack; float* gu_scan; float* dbc_part;
+  __nv_bfloat16* gstack_bf;  // bf16 copy of gstack (bf16 runs), operand of the tensor-core GEMMs
   float* partA; float* partD; float* partS;
+};
+
+// One staged sub-chunk: ST tokens x DC channels (+ the token's B and C rows).
+struct Stage {
+  float dt[ST][DC];
+  float rdt[ST][DC];
+  float u[ST][DC];
+  float gg[ST][DC];    // backward: incoming gradient g
+  float dh[ST][DC];    // backward: delta_in_h = g * scale * act'(C h)
+  float sig[ST][DC];   // backward: sigmoid(dt_in)
+  float4 B[ST][NQ];
+  float4 C[ST][NQ];
+};
+
+// Registers that carry the next sub-chunk from global memory to the stage.
+struct Pref {
+  float dtin[2], u[2], g[2], ap[2], sc[2];
+  float bc;
 };
 
 __device__ __forceinline__ float act_apply(int act, float x) {
@@ -54,6 +81,16 @@ __device__ __forceinline__ float act_deriv(int act, float x) {
   if (act == PGF_ACT_RELU) return x > 0.f ? 1.f : 0.f;
   if (act == PGF_ACT_TANH) { float t = tanhf(x); return 1.f - t * t; }
   return 1.f;
+}
+
+// phi_1(z) and phi_1'(z) given e = e^z and rz = 1/z (series near 0, see common.cuh).
+__device__ __forceinline__ float phi1r(float z, float e, float rz) {
+  if (fabsf(z) < 0.25f) return phi1_from_exp(z, e);
+  return (e - 1.0f) * rz;
+}
+__device__ __forceinline__ float phi1pr(float z, float e, float rz) {
+  if (fabsf(z) < 0.5f) return phi1p_from_exp(z, e);
+  return fmaf(z - 1.0f, e, 1.0f) * (rz * rz);
 }
 
 struct Lane {
@@ -78,24 +115,83 @@ __device__ __forceinline__ Lane lane_of(const SsmArgs& a) {
   return l;
 }
 
-__device__ __forceinline__ void load_A(const SsmArgs& a, int nq, float An[NS]) {
-#pragma unroll
-  for (int j = 0; j < NS; ++j) An[j] = -expf(a.A_log[nq * NS + j]);
-}
-
-// one forward step of the thread's NS states at token `row`
-__device__ __forceinline__ void fwd_step(const SsmArgs& a, const Lane& l, int64_t row,
-                                         const float An[NS], float h[NS], float& dt, float& uu) {
-  const float dtin = l.ch ? a.proj[row * a.P + l.d] : 0.f;
-  dt = softplus_f(dtin);
-  uu = l.ch ? ldv(a.u, a.u_bf16, row * a.D + l.d) : 0.f;
-  const float* Bp = a.proj + row * a.P + a.D + l.nq * NS;
+// per-thread state constants: A_n, A_n log2(e), 1/A_n
+struct AConst {
+  float A[NS], A2[NS], rA[NS];
+};
+__device__ __forceinline__ AConst load_A(const SsmArgs& a, int nq) {
+  AConst c;
 #pragma unroll
   for (int j = 0; j < NS; ++j) {
-    const float z = dt * An[j];
-    const float ez = expf(z);
-    const float p1 = phi1_from_exp(z, ez);
-    h[j] = ez * h[j] + (p1 * Bp[j]) * uu;
+    c.A[j] = -expf(a.A_log[nq * NS + j]);
+    c.A2[j] = c.A[j] * LOG2E;
+    c.rA[j] = 1.0f / c.A[j];
+  }
+  return c;
+}
+
+__device__ __forceinline__ void pref_load(const SsmArgs& a, const Lane& l, int64_t s0, bool bwd, Pref& r) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * SSM_THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    const int64_t tok = s0 + t;
+    const int64_t d = int64_t(l.grp) * DC + dl;
+    const bool v = tok < l.e && d < a.D;
+    const int64_t row = l.b * a.L + tok;
+    r.dtin[q] = v ? a.proj[row * a.P + d] : 0.f;
+    r.u[q] = v ? ldv(a.u, a.u_bf16, row * a.D + d) : 0.f;
+    if (bwd) {
+      r.g[q] = v ? ldv(a.g, a.g_bf16, row * a.D + d) : 0.f;
+      r.ap[q] = (v && a.actp) ? a.actp[row * a.D + d] : 1.f;
+      r.sc[q] = v ? a.scale[d] : 0.f;
+    }
+  }
+  {
+    const int t = l.tid >> 5, j = l.tid & 31;
+    const int64_t tok = s0 + t;
+    r.bc = (t < ST && tok < l.e) ? a.proj[(l.b * a.L + tok) * a.P + a.D + j] : 0.f;
+  }
+}
+
+__device__ __forceinline__ void pref_store(const Pref& r, const Lane& l, bool bwd, Stage& st) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * SSM_THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    const float dt = softplus_f(r.dtin[q]);
+    st.dt[t][dl] = dt;
+    st.rdt[t][dl] = 1.0f / dt;
+    st.u[t][dl] = r.u[q];
+    if (bwd) {
+      st.gg[t][dl] = r.g[q];
+      st.dh[t][dl] = r.g[q] * r.sc[q] * r.ap[q];
+      st.sig[t][dl] = sigmoid_f(r.dtin[q]);
+    }
+  }
+  {
+    const int t = l.tid >> 5, j = l.tid & 31;
+    if (t < ST) {
+      float* dst = j < NST ? reinterpret_cast<float*>(&st.B[t][0]) + j
+                           : reinterpret_cast<float*>(&st.C[t][0]) + (j - NST);
+      *dst = r.bc;
+    }
+  }
+}
+
+// One forward step of the thread's NS states on staged token i; returns e = exp(dt A) per state.
+__device__ __forceinline__ void step_fwd(const Stage& st, int i, int dl, int nq, const AConst& K,
+                                         float h[NS], float e_out[NS]) {
+  const float dt = st.dt[i][dl], rdt = st.rdt[i][dl], uu = st.u[i][dl];
+  const float4 Bq = st.B[i][nq];
+  const float Bv[NS] = {Bq.x, Bq.y, Bq.z, Bq.w};
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const float z = dt * K.A[j];
+    const float ez = exp2f(dt * K.A2[j]);
+    const float p1 = phi1r(z, ez, rdt * K.rA[j]);
+    h[j] = ez * h[j] + (p1 * Bv[j]) * uu;
+    e_out[j] = ez;
   }
 }
 
@@ -103,15 +199,28 @@ __device__ __forceinline__ void fwd_step(const SsmArgs& a, const Lane& l, int64_
 // forward
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArgs a) {
+  __shared__ Stage stg[2];
   const Lane l = lane_of(a);
-  float An[NS];
-  load_A(a, l.nq, An);
-  float h[NS] = {0.f, 0.f, 0.f, 0.f};
+  const AConst K = load_A(a, l.nq);
+  float h[NS] = {0.f, 0.f, 0.f, 0.f}, e[NS];
   float sdt = 0.f;
-  for (int64_t t = l.s; t < l.e; ++t) {
-    float dt, uu;
-    fwd_step(a, l, l.b * a.L + t, An, h, dt, uu);
-    sdt += dt;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s, false, r);
+  pref_store(r, l, false, stg[0]);
+  __syncthreads();
+  for (int k = 0; k < nsub; ++k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    const Stage& S = stg[k & 1];
+#pragma unroll
+    for (int i = 0; i < ST; ++i) {
+      if (l.s + int64_t(k) * ST + i < l.e) {
+        step_fwd(S, i, l.dl, l.nq, K, h, e);
+        sdt += S.dt[i][l.dl];
+      }
+    }
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
@@ -120,46 +229,91 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
   if (l.nq == 0) a.sdt[cb * a.D + l.d] = sdt;
 }
 
+// H_{c+1} = exp(A_n * sum_dt_c) H_c + hloc_c, sequential over chunks; loads run 4 chunks ahead.
 __global__ void ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_final) {
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= a.Bsz * a.D * NST) return;
   const int n = int(idx % NST);
   const int64_t d = (idx / NST) % a.D;
   const int64_t b = idx / (NST * a.D);
-  const float An = -expf(a.A_log[n]);
+  const float A2 = -expf(a.A_log[n]) * LOG2E;
+  const float* __restrict__ sdt = a.sdt + b * a.nC * a.D + d;
+  const float* __restrict__ hloc = a.hloc + (b * a.nC * a.D + d) * NST + n;
+  float* __restrict__ hC = a.hC + (b * (a.nC + 1) * a.D + d) * NST + n;
+  const int64_t cs = a.D, hs = a.D * NST;
   float H = a.h_init ? a.h_init[(b * a.D + d) * NST + n] : 0.f;
-  a.hC[((b * (a.nC + 1)) * a.D + d) * NST + n] = H;
-  for (int64_t c = 0; c < a.nC; ++c) {
-    const int64_t cb = b * a.nC + c;
-    H = expf(An * a.sdt[cb * a.D + d]) * H + a.hloc[(cb * a.D + d) * NST + n];
-    a.hC[((b * (a.nC + 1) + c + 1) * a.D + d) * NST + n] = H;
+  hC[0] = H;
+  int64_t c = 0;
+  for (; c + 4 <= a.nC; c += 4) {
+    float sd[4], hl[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      sd[q] = sdt[(c + q) * cs];
+      hl[q] = hloc[(c + q) * hs];
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      H = exp2f(A2 * sd[q]) * H + hl[q];
+      hC[(c + q + 1) * hs] = H;
+    }
+  }
+  for (; c < a.nC; ++c) {
+    H = exp2f(A2 * sdt[c * cs]) * H + hloc[c * hs];
+    hC[(c + 1) * hs] = H;
   }
   if (h_final) h_final[(b * a.D + d) * NST + n] = H;
 }
 
 __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs a) {
+  __shared__ Stage stg[2];
+  __shared__ float ybuf[2][ST][DC];
   const Lane l = lane_of(a);
-  float An[NS];
-  load_A(a, l.nq, An);
-  float h[NS];
+  const AConst K = load_A(a, l.nq);
+  float h[NS], e[NS];
 #pragma unroll
   for (int j = 0; j < NS; ++j)
     h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
   const float Dd = l.ch ? a.Dp[l.d] : 0.f;
   const float sc = l.ch ? a.scale[l.d] : 0.f;
-  for (int64_t t = l.s; t < l.e; ++t) {
-    const int64_t row = l.b * a.L + t;
-    float dt, uu;
-    fwd_step(a, l, row, An, h, dt, uu);
-    const float* Cp = a.proj + row * a.P + a.D + NST + l.nq * NS;
-    float yc = 0.f;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s, false, r);
+  pref_store(r, l, false, stg[0]);
+  __syncthreads();
+  for (int k = 0; k < nsub; ++k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    const Stage& S = stg[k & 1];
 #pragma unroll
-    for (int j = 0; j < NS; ++j) yc = fmaf(Cp[j], h[j], yc);
-    yc += __shfl_xor_sync(0xffffffffu, yc, 1);
-    yc += __shfl_xor_sync(0xffffffffu, yc, 2);
-    if (l.nq == 0 && l.ch) {
-      if (a.y) stv(a.y, a.y_bf16, row * a.D + l.d, (act_apply(a.act, yc) + Dd * uu) * sc);
-      if (a.actp) a.actp[row * a.D + l.d] = act_deriv(a.act, yc);
+    for (int i = 0; i < ST; ++i) {
+      if (l.s + int64_t(k) * ST + i < l.e) {
+        step_fwd(S, i, l.dl, l.nq, K, h, e);
+        const float4 Cq = S.C[i][l.nq];
+        float yc = Cq.x * h[0];
+        yc = fmaf(Cq.y, h[1], yc);
+        yc = fmaf(Cq.z, h[2], yc);
+        yc = fmaf(Cq.w, h[3], yc);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 1);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 2);
+        if (l.nq == 0) {
+          ybuf[k & 1][i][l.dl] = a.y ? (act_apply(a.act, yc) + Dd * S.u[i][l.dl]) * sc
+                                     : act_deriv(a.act, yc);
+        }
+      }
+    }
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
+    // coalesced write-out of the sub-chunk (y, or act'(C h) for the backward)
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int idx = l.tid + q * SSM_THREADS;
+      const int t = idx / DC, dl = idx % DC;
+      const int64_t tok = l.s + int64_t(k) * ST + t;
+      const int64_t d = int64_t(l.grp) * DC + dl;
+      if (tok < l.e && d < a.D) {
+        const int64_t o = (l.b * a.L + tok) * a.D + d;
+        if (a.y) stv(a.y, a.y_bf16, o, ybuf[k & 1][t][dl]);
+        else a.actp[o] = ybuf[k & 1][t][dl];
+      }
     }
   }
 }
@@ -167,36 +321,40 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
 // ---------------------------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ float delta_in_h(const SsmArgs& a, const Lane& l, int64_t row, float sc,
-                                            float& gg, float& din) {
-  gg = l.ch ? ldv(a.g, a.g_bf16, row * a.D + l.d) : 0.f;
-  din = gg * sc;
-  float dh = din;
-  if (a.actp && l.ch) dh *= a.actp[row * a.D + l.d];
-  return dh;
-}
-
 __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArgs a) {
+  __shared__ Stage stg[2];
   const Lane l = lane_of(a);
-  float An[NS];
-  load_A(a, l.nq, An);
-  const float sc = l.ch ? a.scale[l.d] : 0.f;
+  const AConst K = load_A(a, l.nq);
   float dlt[NS] = {0.f, 0.f, 0.f, 0.f};
   float anext[NS] = {1.f, 1.f, 1.f, 1.f};
   float sdt2 = 0.f, dt_first = 0.f;
-  for (int64_t t = l.e - 1; t >= l.s; --t) {
-    const int64_t row = l.b * a.L + t;
-    const float dt = softplus_f(l.ch ? a.proj[row * a.P + l.d] : 0.f);
-    float gg, din;
-    const float dh = delta_in_h(a, l, row, sc, gg, din);
-    const float* Cp = a.proj + row * a.P + a.D + NST + l.nq * NS;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+  pref_store(r, l, true, stg[(nsub - 1) & 1]);
+  __syncthreads();
+  for (int k = nsub - 1; k >= 0; --k) {
+    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    const Stage& S = stg[k & 1];
 #pragma unroll
-    for (int j = 0; j < NS; ++j) {
-      dlt[j] = anext[j] * dlt[j] + dh * Cp[j];
-      anext[j] = expf(dt * An[j]);
+    for (int i = ST - 1; i >= 0; --i) {
+      const int64_t t = l.s + int64_t(k) * ST + i;
+      if (t < l.e) {
+        const float dt = S.dt[i][l.dl];
+        const float dh = S.dh[i][l.dl];
+        const float4 Cq = S.C[i][l.nq];
+        const float Cv[NS] = {Cq.x, Cq.y, Cq.z, Cq.w};
+#pragma unroll
+        for (int j = 0; j < NS; ++j) {
+          dlt[j] = anext[j] * dlt[j] + dh * Cv[j];
+          anext[j] = exp2f(dt * K.A2[j]);
+        }
+        if (t > l.s) sdt2 += dt;
+        dt_first = dt;
+      }
     }
-    if (t > l.s) sdt2 += dt;
-    dt_first = dt;
+    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
+    __syncthreads();
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
@@ -216,100 +374,131 @@ __global__ void ssm_compose_bwd_kernel(const SsmArgs a, const float* __restrict_
   const int n = int(idx % NST);
   const int64_t d = (idx / NST) % a.D;
   const int64_t b = idx / (NST * a.D);
-  const float An = -expf(a.A_log[n]);
+  const float A2 = -expf(a.A_log[n]) * LOG2E;
   const int64_t o = (b * a.D + d) * NST + n;
+  const float* __restrict__ sdt2 = a.sdt2 + b * a.nC * a.D + d;
+  const float* __restrict__ dt0 = a.dt0 + b * a.nC * a.D + d;
+  const float* __restrict__ dloc = a.dloc + (b * a.nC * a.D + d) * NST + n;
+  float* __restrict__ X = a.X + (b * a.nC * a.D + d) * NST + n;
+  const int64_t cs = a.D, hs = a.D * NST;
   float G = dh_end ? dh_end[o] : 0.f;
   float aE = dA_end ? dA_end[o] : 1.f;
-  for (int64_t c = a.nC - 1; c >= 0; --c) {
-    const int64_t cb = b * a.nC + c;
-    const float X = aE * G;
-    a.X[(cb * a.D + d) * NST + n] = X;
-    G = expf(An * a.sdt2[cb * a.D + d]) * X + a.dloc[(cb * a.D + d) * NST + n];
-    aE = expf(a.dt0[cb * a.D + d] * An);
+  int64_t c = a.nC - 1;
+  for (; c >= 3; c -= 4) {
+    float s2[4], d0[4], dl[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      s2[q] = sdt2[(c - q) * cs];
+      d0[q] = dt0[(c - q) * cs];
+      dl[q] = dloc[(c - q) * hs];
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float x = aE * G;
+      X[(c - q) * hs] = x;
+      G = exp2f(A2 * s2[q]) * x + dl[q];
+      aE = exp2f(d0[q] * A2);
+    }
+  }
+  for (; c >= 0; --c) {
+    const float x = aE * G;
+    X[c * hs] = x;
+    G = exp2f(A2 * sdt2[c * cs]) * x + dloc[c * hs];
+    aE = exp2f(dt0[c * cs] * A2);
   }
   if (dh_start) dh_start[o] = G;
   if (dA_start) dA_start[o] = aE;
 }
 
+// Main backward kernel.  Shared memory (dynamic): ckpt [Tc/ST][SSM_THREADS][NS] floats, then
+// red [ST][SSM_WARPS][32], then gbuf [2][ST][DC] (grad_dt_in, grad_u_scan of the sub-chunk).
 __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs a) {
   extern __shared__ float sm[];
+  __shared__ Stage stg[2];
   const Lane l = lane_of(a);
-  const int K = int((a.Tc + SUB - 1) / SUB);
-  float* ckpt = sm;                                 // [K][SSM_THREADS][NS]
-  float* red = sm + size_t(K) * SSM_THREADS * NS;   // [SUB][SSM_WARPS][32]
+  const int KS = int((a.Tc + ST - 1) / ST);
+  float* ckpt = sm;
+  float* red = ckpt + size_t(KS) * SSM_THREADS * NS;
+  float* gbuf = red + ST * SSM_WARPS * 32;  // [2][ST][DC]
   const int lane = l.tid & 31, warp = l.tid >> 5;
-  float An[NS];
-  load_A(a, l.nq, An);
+  const AConst K = load_A(a, l.nq);
   const float Dd = l.ch ? a.Dp[l.d] : 0.f;
-  const float sc = l.ch ? a.scale[l.d] : 0.f;
   const int64_t cb = l.b * a.nC + l.c;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
 
-  float h[NS], carry[NS];
+  float h[NS], carry[NS], e[NS];
 #pragma unroll
   for (int j = 0; j < NS; ++j) {
     h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
     carry[j] = l.ch ? a.X[(cb * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
   }
-  // pass 1: checkpoints at every SUB tokens
-  for (int k = 0; k < K; ++k) {
+  // ---- pass 1: forward through the chunk, checkpoint at the start of every sub-chunk
+  Pref r;
+  pref_load(a, l, l.s, false, r);
+  pref_store(r, l, false, stg[0]);
+  __syncthreads();
+  for (int k = 0; k < nsub; ++k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
 #pragma unroll
     for (int j = 0; j < NS; ++j) ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j] = h[j];
+    const Stage& S = stg[k & 1];
 #pragma unroll
-    for (int i = 0; i < SUB; ++i) {
-      const int64_t t = l.s + int64_t(k) * SUB + i;
-      if (t < l.e) {
-        float dt, uu;
-        fwd_step(a, l, l.b * a.L + t, An, h, dt, uu);
-      }
-    }
+    for (int i = 0; i < ST; ++i)
+      if (l.s + int64_t(k) * ST + i < l.e) step_fwd(S, i, l.dl, l.nq, K, h, e);
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
   }
 
+  // ---- pass 2: sub-chunks in reverse
   float accA[NS] = {0.f, 0.f, 0.f, 0.f};
   float accD = 0.f, accS = 0.f;
   const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
-
-  for (int k = K - 1; k >= 0; --k) {
-    float tr[SUB + 1][NS];
+  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+  pref_store(r, l, true, stg[(nsub - 1) & 1]);
+  __syncthreads();
+  for (int k = nsub - 1; k >= 0; --k) {
+    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    const Stage& S = stg[k & 1];
+    float* gb = gbuf + (k & 1) * (2 * ST * DC);
+    // re-run the sub-chunk into registers: tr[i] = state before token i, ex[i] = exp(dt_i A)
+    float tr[ST + 1][NS], ex[ST][NS];
 #pragma unroll
     for (int j = 0; j < NS; ++j) tr[0][j] = ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j];
 #pragma unroll
-    for (int i = 0; i < SUB; ++i) {
+    for (int i = 0; i < ST; ++i) {
 #pragma unroll
       for (int j = 0; j < NS; ++j) tr[i + 1][j] = tr[i][j];
-      const int64_t t = l.s + int64_t(k) * SUB + i;
-      if (t < l.e) {
-        float dt, uu;
-        fwd_step(a, l, l.b * a.L + t, An, tr[i + 1], dt, uu);
+      if (l.s + int64_t(k) * ST + i < l.e) step_fwd(S, i, l.dl, l.nq, K, tr[i + 1], ex[i]);
+      else {
+#pragma unroll
+        for (int j = 0; j < NS; ++j) ex[i][j] = 1.f;
       }
     }
 #pragma unroll
-    for (int i = SUB - 1; i >= 0; --i) {
-      const int64_t t = l.s + int64_t(k) * SUB + i;
-      const bool valid = t < l.e;  // uniform across the CTA
+    for (int i = ST - 1; i >= 0; --i) {
+      const bool valid = l.s + int64_t(k) * ST + i < l.e;  // uniform across the CTA
       float v8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      float gdt = 0.f, gur = 0.f, hc = 0.f, sig = 0.f, uu = 0.f, gg = 0.f, din = 0.f;
-      const int64_t row = l.b * a.L + t;
+      float gdt = 0.f, gur = 0.f, hc = 0.f;
+      const float dt = S.dt[i][l.dl], rdt = S.rdt[i][l.dl], uu = S.u[i][l.dl];
+      const float dh = S.dh[i][l.dl];
       if (valid) {
-        const float dtin = l.ch ? a.proj[row * a.P + l.d] : 0.f;
-        const float dt = softplus_f(dtin);
-        sig = sigmoid_f(dtin);
-        uu = l.ch ? ldv(a.u, a.u_bf16, row * a.D + l.d) : 0.f;
-        const float dh = delta_in_h(a, l, row, sc, gg, din);
-        const float* Bp = a.proj + row * a.P + a.D + l.nq * NS;
-        const float* Cp = Bp + NST;
+        const float4 Bq = S.B[i][l.nq], Cq = S.C[i][l.nq];
+        const float Bv[NS] = {Bq.x, Bq.y, Bq.z, Bq.w};
+        const float Cv[NS] = {Cq.x, Cq.y, Cq.z, Cq.w};
 #pragma unroll
         for (int j = 0; j < NS; ++j) {
-          hc = fmaf(Cp[j], tr[i + 1][j], hc);
-          const float dlt = carry[j] + dh * Cp[j];
-          const float z = dt * An[j];
-          const float ez = expf(z);
-          const float p1 = phi1_from_exp(z, ez);
-          const float p1p = phi1p_from_exp(z, ez);
-          const float q = ez * tr[i][j] + p1p * (Bp[j] * uu);
+          hc = fmaf(Cv[j], tr[i + 1][j], hc);
+          const float dlt = carry[j] + dh * Cv[j];
+          const float z = dt * K.A[j];
+          const float ez = ex[i][j];
+          const float rz = rdt * K.rA[j];
+          const float p1 = phi1r(z, ez, rz);
+          const float p1p = phi1pr(z, ez, rz);
+          const float q = ez * tr[i][j] + p1p * (Bv[j] * uu);
           const float dq = dlt * q;
           accA[j] = fmaf(dq, z, accA[j]);
-          gdt = fmaf(dq, An[j], gdt);
-          gur = fmaf(dlt, p1 * Bp[j], gur);
+          gdt = fmaf(dq, K.A[j], gdt);
+          gur = fmaf(dlt, p1 * Bv[j], gur);
           v8[j] = dlt * (p1 * uu);
           v8[NS + j] = dh * tr[i + 1][j];
           carry[j] = ez * dlt;
@@ -321,9 +510,11 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
       gur += __shfl_xor_sync(0xffffffffu, gur, 2);
       hc += __shfl_xor_sync(0xffffffffu, hc, 1);
       hc += __shfl_xor_sync(0xffffffffu, hc, 2);
-      if (valid && l.nq == 0 && l.ch) {
-        a.gstack[row * a.P + l.d] = gdt * sig;
-        a.gu_scan[row * a.D + l.d] = din * Dd + gur;
+      if (valid && l.nq == 0) {
+        const float gg = S.gg[i][l.dl];
+        const float din = l.ch ? gg * a.scale[l.d] : 0.f;
+        gb[i * DC + l.dl] = gdt * S.sig[i][l.dl];
+        gb[ST * DC + i * DC + l.dl] = din * Dd + gur;
         accD = fmaf(din, uu, accD);
         accS = fmaf(gg, act_apply(a.act, hc) + Dd * uu, accS);
       }
@@ -345,11 +536,13 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
       const float send = b2 ? w2[0] : w2[1];
       red[(i * SSM_WARPS + warp) * 32 + lane] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
     }
+    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
     __syncthreads();
-    for (int o = l.tid; o < SUB * 32; o += SSM_THREADS) {
-      const int i = o >> 5, ln = o & 31;
-      const int64_t t = l.s + int64_t(k) * SUB + i;
-      if (t < l.e) {
+    // grad B / grad C of the sub-chunk: sum over the CTA's warps, one partial per channel group
+    {
+      const int i = l.tid >> 5, ln = l.tid & 31;
+      const int64_t t = l.s + int64_t(k) * ST + i;
+      if (i < ST && t < l.e) {
         float sum = 0.f;
 #pragma unroll
         for (int w = 0; w < SSM_WARPS; ++w) sum += red[(i * SSM_WARPS + w) * 32 + ln];
@@ -357,6 +550,21 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
         const int n = nqq * NS + (vi & 3);
         const int which = vi >> 2;
         a.dbc_part[((int64_t(l.grp) * a.Bsz + l.b) * a.L + t) * 32 + which * NST + n] = sum;
+      }
+    }
+    // grad dt_in and grad_u (scan part) of the sub-chunk, coalesced
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int idx = l.tid + q * SSM_THREADS;
+      const int t = idx / DC, dl = idx % DC;
+      const int64_t tok = l.s + int64_t(k) * ST + t;
+      const int64_t d = int64_t(l.grp) * DC + dl;
+      if (tok < l.e && d < a.D) {
+        const int64_t row = l.b * a.L + tok;
+        const float gd = gb[t * DC + dl];
+        a.gstack[row * a.P + d] = gd;
+        if (a.gstack_bf) a.gstack_bf[row * a.P + d] = __float2bfloat16_rn(gd);
+        a.gu_scan[row * a.D + d] = gb[ST * DC + t * DC + dl];
       }
     }
     __syncthreads();
@@ -388,6 +596,7 @@ __global__ void ssm_bc_reduce_kernel(const SsmArgs a) {
   float s = 0.f;
   for (int64_t gi = 0; gi < a.G; ++gi) s += a.dbc_part[(gi * rows + row) * 32 + m];
   a.gstack[row * a.P + a.D + m] = s;
+  if (a.gstack_bf) a.gstack_bf[row * a.P + a.D + m] = __float2bfloat16_rn(s);
 }
 
 // grad A_log / D / scale from the per-CTA partials, in a fixed order.
@@ -474,6 +683,7 @@ static size_t ssm_ws(const SsmPlan& p, int dtype, int backward, int act) {
   if (dtype) b += Workspace::round(size_t(p.P) * p.D * 2);              // W_cat bf16
   if (backward) {
     b += Workspace::round(BL * p.P * 4);                                // gstack
+    if (dtype) b += Workspace::round(BL * p.P * 2);                     // gstack bf16 copy
     b += Workspace::round(BL * p.D * 4);                                // gu_scan
     b += Workspace::round(size_t(p.G) * BL * 32 * 4);                   // dbc_part
     if (act != PGF_ACT_NONE) b += Workspace::round(BL * p.D * 4);       // actp
@@ -606,6 +816,7 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
   const size_t BL = size_t(Bsz) * L;
   a.gstack = W.take<float>(BL * p.P);
+  a.gstack_bf = dtype ? W.take<__nv_bfloat16>(BL * p.P) : nullptr;
   a.gu_scan = W.take<float>(BL * p.D);
   a.dbc_part = W.take<float>(size_t(p.G) * BL * 32);
   a.actp = act != PGF_ACT_NONE ? W.take<float>(BL * p.D) : nullptr;
@@ -618,7 +829,7 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   a.partS = W.take<float>(size_t(p.nC) * Bsz * D);
   const size_t csb = colsum_ws(int64_t(BL), p.P);
   void* cs = W.take<char>(csb);
-  if (!a.gstack || !a.gu_scan || !a.dbc_part || (act != PGF_ACT_NONE && !a.actp) || !a.dloc ||
+  if (!a.gstack || (dtype && !a.gstack_bf) || !a.gu_scan || !a.dbc_part || (act != PGF_ACT_NONE && !a.actp) || !a.dloc ||
       !a.X || !a.sdt2 || !a.dt0 || !a.partA || !a.partD || !a.partS || !cs) {
     set_error("ssm_bwd: workspace too small (%zu)", ws_bytes);
     return PGF_ERR_WORKSPACE;
@@ -637,8 +848,8 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   const int64_t nth = Bsz * D * NST;
   ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start);
   PGF_LAUNCH_CHECK();
-  const int K = int((p.Tc + SUB - 1) / SUB);
-  const size_t smem = (size_t(K) * SSM_THREADS * NS + size_t(SUB) * SSM_WARPS * 32) * 4;
+  const int KS = int((p.Tc + ST - 1) / ST);
+  const size_t smem = (size_t(KS) * SSM_THREADS * NS + size_t(ST) * SSM_WARPS * 32 + 2 * 2 * ST * DC) * 4;
   PGF_CUDA(cudaFuncSetAttribute(ssm_main_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(smem)));
   prof_begin(PROF_SSM_MAIN_BWD, s);
@@ -652,7 +863,8 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   // grad W_cat (+)= gstack^T u ;  grad b_cat (+)= colsum(gstack)   (:438-451)
   Gemm gw;
   gw.M = p.P; gw.N = D; gw.K = int64_t(BL);
-  gw.A = a.gstack; gw.a_bf16 = 0; gw.lda = p.P; gw.a_trans = 1;
+  gw.A = dtype ? (const void*)a.gstack_bf : (const void*)a.gstack; gw.a_bf16 = dtype;
+  gw.lda = p.P; gw.a_trans = 1;
   gw.B = u; gw.b_bf16 = dtype; gw.ldb = D; gw.b_trans = 1;
   gw.D = gW_cat; gw.d_bf16 = 0; gw.ldd = D;
   gw.epi = epi_default();
@@ -662,8 +874,9 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   // grad_u = gstack W_cat + (delta_in*D + sum_n delta_h phi_1 B)   (:453-463)
   Gemm gx;
   gx.M = int64_t(BL); gx.N = D; gx.K = p.P;
-  gx.A = a.gstack; gx.a_bf16 = 0; gx.lda = p.P; gx.a_trans = 0;
-  gx.B = W_cat; gx.b_bf16 = 0; gx.ldb = D; gx.b_trans = 1;
+  gx.A = dtype ? (const void*)a.gstack_bf : (const void*)a.gstack; gx.a_bf16 = dtype;
+  gx.lda = p.P; gx.a_trans = 0;
+  gx.B = wop; gx.b_bf16 = dtype; gx.ldb = D; gx.b_trans = 1;
   gx.D = gu; gx.d_bf16 = dtype; gx.ldd = D;
   gx.epi = epi_default();
   gx.epi.addend = a.gu_scan;

@@ -30,7 +30,7 @@ def _tc_launches(fn):
 
 
 @pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
-@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 512), (200, 72, 40), (1000, 300, 1024),
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 512), (200, 72, 40), (1000, 304, 1024),
                                    (64, 1000, 8), (4096, 1024, 256)])
 def test_tc_gemm_layouts(ops, at, bt, M, N, K):
     g = torch.Generator().manual_seed(M + N + K + 7 * at + 3 * bt)
@@ -60,3 +60,14 @@ def test_tc_gemm_epilogue_and_bf16_out(ops):
     out = acc.clone().to(DEV)
     _tc_launches(lambda: ops.gemm(A.to(DEV), B.to(DEV), out=out, accumulate=True))
     assert_close(out, acc.double() + A.double() @ B.double().t(), atol=1e-4)
+
+
+def test_unaligned_pitch_falls_back_to_simt(ops):
+    """A row pitch that is not a multiple of 16 bytes cannot be a TMA operand: the SIMT engine runs."""
+    g = torch.Generator().manual_seed(9)
+    A = torch.randn(100, 64, generator=g).bfloat16()
+    B = torch.randn(64, 300, generator=g).bfloat16()  # stored K x N, pitch 600 B
+    ref = A.double() @ B.double()
+    D, n = _tc_launches(lambda: ops.gemm(A.to(DEV), B.to(DEV), b_trans=True))
+    assert n == 0
+    assert_close(D, ref, atol=1e-4, rtol=1e-5)
