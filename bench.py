@@ -167,7 +167,7 @@ def roofline_entry(name, ms_total, n, work_total):
         pass
     src = "measured" if peaks else "fallback"
     t = ms_total / n / 1e3
-    if name.startswith("gemm"):
+    if name.startswith("gemm") or name == "ce":
         peak = peaks.get("bf16_tflops_sustained", 1400.0)
         ach = work_total / n / t / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,

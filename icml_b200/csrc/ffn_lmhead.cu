@@ -257,13 +257,13 @@ static int64_t ce_tile_rows(int64_t T) {
 // Online log-sum-exp over one vocab tile: run_m/run_s hold the running max and sum of
 // exp(logit - max) of each row; tgt_logit receives the target's logit when it lies in the tile.
 __global__ void ce_tile_stats_kernel(const float* __restrict__ tile, int64_t rows, int64_t cols,
-                                     int64_t v0, const int64_t* __restrict__ targets,
+                                     int64_t ld, int64_t v0, const int64_t* __restrict__ targets,
                                      float* __restrict__ run_m, float* __restrict__ run_s,
                                      float* __restrict__ tgt_logit, int first) {
   const int lane = threadIdx.x & 31;
   const int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= rows) return;
-  const float* row = tile + r * cols;
+  const float* row = tile + r * ld;
   float mx = -INFINITY;
   for (int64_t c = lane; c < cols; c += 32) mx = fmaxf(mx, row[c]);
   mx = warp_max(mx);
@@ -297,13 +297,13 @@ __global__ void ce_finish_kernel(const float* __restrict__ run_m, const float* _
 
 // g = (exp(logit - lse) - onehot) * scale, in place (float32) and as a bf16 copy when asked.
 __global__ void ce_grad_tile_kernel(float* __restrict__ tile, __nv_bfloat16* __restrict__ tile_bf,
-                                    int64_t rows, int64_t cols, int64_t v0,
+                                    int64_t rows, int64_t cols, int64_t ld, int64_t v0,
                                     const int64_t* __restrict__ targets, const float* __restrict__ lse,
                                     float scale) {
   const int64_t r = blockIdx.y;
   const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (r >= rows || c >= cols) return;
-  const int64_t o = r * cols + c;
+  const int64_t o = r * ld + c;
   float p = expf(tile[o] - lse[r]);
   if (targets[r] == v0 + c) p -= 1.0f;
   p *= scale;
@@ -344,11 +344,105 @@ static int ce_carve(Workspace& W, CeWs& c, int64_t T, int64_t V, int64_t d, int 
   return PGF_OK;
 }
 
+// ---- tensor-core path (bf16): fused online-LSE forward, bf16 G written by the logits epilogue
+constexpr int CE_NG = 16;                 // 128-column tiles per forward work unit (2048 vocab ids)
+constexpr int64_t CE_BWD_ROWS = 16384;    // rows of G (bf16, rows x vocab) materialised at a time
+
+static int64_t ce_ngroups(int64_t V) { return ((V + 127) / 128 + CE_NG - 1) / CE_NG; }
+static int64_t ce_ldv(int64_t V) { return (V + 63) / 64 * 64; }
+
+static size_t ce_tc_ws_bytes(int64_t T, int64_t V, int64_t d) {
+  const int64_t R = T < CE_BWD_ROWS ? T : CE_BWD_ROWS;
+  size_t b = Workspace::round(size_t(V) * d * 2);                  // W bf16
+  b += 2 * Workspace::round(size_t(T) * ce_ngroups(V) * 4);        // part_m, part_s
+  b += Workspace::round(size_t(T) * 4);                            // target logits
+  b += Workspace::round(size_t(R < 1 ? 1 : R) * ce_ldv(V) * 2);    // G
+  return b + 1024;
+}
+
+// lse = M + log(sum_g s_g exp(m_g - M)), loss = lse - target logit, groups in fixed order.
+__global__ void ce_combine_kernel(const float* __restrict__ part_m, const float* __restrict__ part_s,
+                                  const float* __restrict__ tgt, int64_t rows, int64_t ng,
+                                  float* __restrict__ loss_rows, float* __restrict__ lse) {
+  const int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float M = -INFINITY;
+  for (int64_t g = 0; g < ng; ++g) M = fmaxf(M, part_m[r * ng + g]);
+  float S = 0.f;
+  for (int64_t g = 0; g < ng; ++g) S += part_s[r * ng + g] * expf(part_m[r * ng + g] - M);
+  const float l = M + logf(S);
+  lse[r] = l;
+  loss_rows[r] = l - tgt[r];
+}
+
 }  // namespace pgf
 
 extern "C" size_t pgf_lm_head_ce_workspace(int64_t T, int64_t V, int64_t d, int dtype) {
-  return ce_ws_bytes(T, V, d, dtype);
+  size_t a = ce_ws_bytes(T, V, d, dtype);
+  if (dtype) {
+    size_t b = ce_tc_ws_bytes(T, V, d);
+    if (b > a) a = b;
+  }
+  return a;
 }
+
+namespace pgf {
+
+static int ce_fwd_tc(const void* h, const float* W, const int64_t* targets, float* loss_rows, float* lse,
+                     int64_t T, int64_t V, int64_t d, void* ws, size_t ws_bytes, cudaStream_t s) {
+  Workspace Wk(ws, ws_bytes);
+  __nv_bfloat16* Wb = Wk.take<__nv_bfloat16>(size_t(V) * d);
+  const int64_t ng = ce_ngroups(V);
+  float* pm = Wk.take<float>(size_t(T) * ng);
+  float* ps = Wk.take<float>(size_t(T) * ng);
+  float* tg = Wk.take<float>(size_t(T));
+  if (!Wb || !pm || !ps || !tg) { set_error("lm_head_ce_fwd: workspace too small"); return PGF_ERR_WORKSPACE; }
+  Gemm g = mk(T, V, d, h, 1, d, 0, Wb, 1, d, 0, nullptr, 0, 0);
+  if (!tc_usable(g)) return PGF_ERR_UNSUPPORTED;
+  PGF_TRY(to_bf16(W, Wb, V * d, s));
+  PGF_CUDA(cudaMemsetAsync(tg, 0, size_t(T) * 4, s));
+  int ngo = 0;
+  PGF_TRY(tc_ce_fwd(g, CE_NG, targets, pm, ps, tg, &ngo, s));
+  ce_combine_kernel<<<ceil_div(T, 256), 256, 0, s>>>(pm, ps, tg, T, ngo, loss_rows, lse);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+static int ce_bwd_tc(const void* h, const float* W, const int64_t* targets, const float* lse, float scale,
+                     float* grad_W, void* grad_h, int accumulate, int64_t T, int64_t V, int64_t d,
+                     void* ws, size_t ws_bytes, cudaStream_t s) {
+  Workspace Wk(ws, ws_bytes);
+  __nv_bfloat16* Wb = Wk.take<__nv_bfloat16>(size_t(V) * d);
+  const int64_t ng = ce_ngroups(V);
+  Wk.take<float>(size_t(T) * ng);  // keep the forward layout: the same workspace serves both
+  Wk.take<float>(size_t(T) * ng);
+  Wk.take<float>(size_t(T));
+  const int64_t R = T < CE_BWD_ROWS ? T : CE_BWD_ROWS;
+  const int64_t ldv = ce_ldv(V);
+  __nv_bfloat16* G = Wk.take<__nv_bfloat16>(size_t(R) * ldv);
+  if (!Wb || !G) { set_error("lm_head_ce_bwd: workspace too small"); return PGF_ERR_WORKSPACE; }
+  Gemm probe = mk(R, V, d, h, 1, d, 0, Wb, 1, d, 0, G, 1, ldv);
+  if (!tc_usable(probe)) return PGF_ERR_UNSUPPORTED;
+  PGF_TRY(to_bf16(W, Wb, V * d, s));
+  for (int64_t r = 0; r < T; r += R) {
+    const int64_t m = T - r < R ? T - r : R;
+    const __nv_bfloat16* ht = static_cast<const __nv_bfloat16*>(h) + r * d;
+    Gemm g = mk(m, V, d, ht, 1, d, 0, Wb, 1, d, 0, G, 1, ldv);
+    PGF_TRY(tc_ce_bwd(g, targets + r, lse + r, scale, G, ldv, s));
+    // grad_W (+)= G^T h_rows
+    Gemm gw = mk(V, d, m, G, 1, ldv, 1, ht, 1, d, 1, grad_W, 0, d);
+    gw.epi.accumulate = (r > 0) || accumulate;
+    PGF_TRY(run_gemm(gw, s));
+    if (grad_h) {
+      // grad_h_rows = G W
+      Gemm gh = mk(m, d, V, G, 1, ldv, 0, Wb, 1, d, 1, static_cast<__nv_bfloat16*>(grad_h) + r * d, 1, d);
+      PGF_TRY(run_gemm(gh, s));
+    }
+  }
+  return PGF_OK;
+}
+
+}  // namespace pgf
 
 extern "C" int pgf_lm_head_ce_fwd(const void* h, const float* W, const int64_t* targets,
                                   float* loss_rows, float* lse, int64_t T, int64_t V, int64_t d,
@@ -357,6 +451,11 @@ extern "C" int pgf_lm_head_ce_fwd(const void* h, const float* W, const int64_t* 
   PGF_CHECK_ARG(dtype == 0 || dtype == 1, "lm_head_ce_fwd: bad dtype");
   if (T == 0) return PGF_OK;
   cudaStream_t s = as_stream(stream);
+  if (dtype) {
+    const int rc = ce_fwd_tc(h, W, targets, loss_rows, lse, T, V, d, ws, ws_bytes, s);
+    if (rc != PGF_ERR_UNSUPPORTED) return rc;
+    clear_error();
+  }
   Workspace Wk(ws, ws_bytes);
   CeWs c;
   PGF_TRY(ce_carve(Wk, c, T, V, d, dtype));
@@ -372,10 +471,11 @@ extern "C" int pgf_lm_head_ce_fwd(const void* h, const float* W, const int64_t* 
     const char* ht = static_cast<const char*>(h) + r * d * es;
     for (int64_t v0 = 0; v0 < V; v0 += CE_VT) {
       const int64_t nv = V - v0 < CE_VT ? V - v0 : CE_VT;
+      const int64_t ldt = (nv + 63) / 64 * 64;  // 128-byte aligned tile pitch (TMA operand rule)
       const char* wt = static_cast<const char*>(w) + v0 * d * es;
-      Gemm g = mk(m, nv, d, ht, dtype, d, 0, wt, dtype, d, 0, c.tile, 0, nv);
+      Gemm g = mk(m, nv, d, ht, dtype, d, 0, wt, dtype, d, 0, c.tile, 0, ldt);
       PGF_TRY(run_gemm(g, s));
-      ce_tile_stats_kernel<<<ceil_div(m, 8), 256, 0, s>>>(c.tile, m, nv, v0, targets + r, c.run_m,
+      ce_tile_stats_kernel<<<ceil_div(m, 8), 256, 0, s>>>(c.tile, m, nv, ldt, v0, targets + r, c.run_m,
                                                          c.run_s, c.tgt, v0 == 0);
       PGF_LAUNCH_CHECK();
     }
@@ -396,6 +496,12 @@ extern "C" int pgf_lm_head_ce_bwd(const void* h, const float* W, const int64_t* 
     if (!accumulate) PGF_CUDA(cudaMemsetAsync(grad_W, 0, size_t(V) * d * 4, s));
     return PGF_OK;
   }
+  if (dtype) {
+    const int rc = ce_bwd_tc(h, W, targets, lse, grad_scale, grad_W, grad_h, accumulate, T, V, d, ws,
+                             ws_bytes, s);
+    if (rc != PGF_ERR_UNSUPPORTED) return rc;
+    clear_error();
+  }
   Workspace Wk(ws, ws_bytes);
   CeWs c;
   PGF_TRY(ce_carve(Wk, c, T, V, d, dtype));
@@ -412,21 +518,23 @@ extern "C" int pgf_lm_head_ce_bwd(const void* h, const float* W, const int64_t* 
     char* ght = grad_h ? static_cast<char*>(grad_h) + r * d * es : nullptr;
     for (int64_t v0 = 0; v0 < V; v0 += CE_VT) {
       const int64_t nv = V - v0 < CE_VT ? V - v0 : CE_VT;
+      const int64_t ldt = (nv + 63) / 64 * 64;
       const char* wt = static_cast<const char*>(w) + v0 * d * es;
-      Gemm g = mk(m, nv, d, ht, dtype, d, 0, wt, dtype, d, 0, c.tile, 0, nv);
+      Gemm g = mk(m, nv, d, ht, dtype, d, 0, wt, dtype, d, 0, c.tile, 0, ldt);
       PGF_TRY(run_gemm(g, s));
       dim3 gg(ceil_div(nv, 256), unsigned(m));
-      ce_grad_tile_kernel<<<gg, 256, 0, s>>>(c.tile, c.tile_bf, m, nv, v0, targets + r, lse + r, grad_scale);
+      ce_grad_tile_kernel<<<gg, 256, 0, s>>>(c.tile, c.tile_bf, m, nv, ldt, v0, targets + r, lse + r,
+                                              grad_scale);
       PGF_LAUNCH_CHECK();
       const void* gt = dtype ? (const void*)c.tile_bf : (const void*)c.tile;
       // grad_W[v0:v0+nv] (+)= G^T h_tile
-      Gemm gw = mk(nv, d, m, gt, dtype, nv, 1, ht, dtype, d, 1, grad_W + v0 * d, 0, d);
+      Gemm gw = mk(nv, d, m, gt, dtype, ldt, 1, ht, dtype, d, 1, grad_W + v0 * d, 0, d);
       gw.epi.accumulate = (r > 0) || accumulate;
       PGF_TRY(run_gemm(gw, s));
       if (ght) {
         // grad_h_tile (+)= G W_tile, summed over vocab tiles in float32
         float* acc32 = dtype ? c.gh32 : reinterpret_cast<float*>(ght);
-        Gemm gh = mk(m, d, nv, gt, dtype, nv, 0, wt, dtype, d, 1, acc32, 0, d);
+        Gemm gh = mk(m, d, nv, gt, dtype, ldt, 0, wt, dtype, d, 1, acc32, 0, d);
         gh.epi.accumulate = v0 > 0;
         PGF_TRY(run_gemm(gh, s));
       }

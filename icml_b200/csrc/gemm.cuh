@@ -28,6 +28,15 @@ int run_gemm(const Gemm& g, cudaStream_t s);
 int run_gemm_simt(const Gemm& g, cudaStream_t s);
 // tcgen05 path; returns PGF_ERR_UNSUPPORTED when the call does not fit it.
 int run_gemm_tc(const Gemm& g, cudaStream_t s);
+bool tc_usable(const Gemm& g);
+// Fused LM-head + cross-entropy passes on the tcgen05 engine (g: logits = h W^T, N = vocab).
+// Forward: per row and per group of `ng` 128-column tiles, the running max / sum of exp of the
+// logits (part_m, part_s: (M, n_groups)) and the target logit; the logits are never stored.
+int tc_ce_fwd(const Gemm& g, int ng, const int64_t* targets, float* part_m, float* part_s,
+              float* tgt_logit, int* n_groups_out, cudaStream_t s);
+// Backward: G[m, v] = (exp(logit - lse[m]) - [v == target[m]]) * scale as bf16, pitch ldg.
+int tc_ce_bwd(const Gemm& g, const int64_t* targets, const float* lse, float scale, __nv_bfloat16* G,
+              int64_t ldg, cudaStream_t s);
 
 // out[n] (+)= sum_m X[m*ld+n] with `ws` >= colsum_ws(M, N) bytes.
 size_t colsum_ws(int64_t M, int64_t N);

@@ -1,43 +1,66 @@
 // tcgen05 / TMEM dense product for bf16 operands on sm_100a.
 //
-// One CTA computes a 128 x 128 output tile, fp32 accumulation in tensor memory (TMEM):
-//   * warp 0, one lane: TMA producer.  Operand tiles arrive 128B-swizzled through a TC_STAGES-deep
+// Persistent, warp-specialised kernel, one CTA per SM, 192 threads:
+//   * warp 0 (one lane): TMA producer.  Operand tiles arrive 128B-swizzled through a TC_STAGES-deep
 //     mbarrier ring.  A K-major operand is one box {64 k, 128 rows}; an MN-major operand (stored
 //     transposed) is two boxes {64 rows, 64 k} side by side, so no operand is ever transposed in
 //     memory.
-//   * warp 1, one lane: issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32, M=128, N=128, K=16)
-//     and frees each smem stage with tcgen05.commit onto its "empty" mbarrier.
-//   * all 4 warps: epilogue.  Warp w reads TMEM lanes 32w..32w+31 (tile rows) with tcgen05.ld and
-//     applies the shared epilogue (bias, GELU / GELU', addend, accumulate) from gemm.cuh.
+//   * warp 1 (one lane): issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32, M=128, N=128, K=16)
+//     into one of two TMEM accumulators (2 x 128 columns), frees smem stages with tcgen05.commit
+//     on their "empty" barriers and hands finished accumulators to the epilogue.
+//   * warps 2..5: epilogue.  Warp w reads TMEM lanes 32*(w%4).. (tile rows) with tcgen05.ld while
+//     the MMA warp already fills the other accumulator.  Modes:
+//       GENERIC  - 32x32 transposes through shared memory, then the shared epilogue (bias, GELU /
+//                  GELU', addend, accumulate) with coalesced row stores;
+//       CE_FWD   - online log-sum-exp of each row over the CTA's vocabulary range plus the target
+//                  logit; the logits never leave TMEM;
+//       CE_BWD   - g = (softmax - onehot) * scale from the recomputed logits and the saved lse,
+//                  stored as bf16 through the transpose.
+// Work unit = (128-row block, group of `ng` consecutive 128-column tiles); CTAs stride over units.
 // Every mbarrier wait is bounded by a clock budget; on expiry the kernel records a fault in
-// g_tc_fault, skips the epilogue, releases its TMEM and returns.
+// g_tc_fault and stops issuing work.
 #include "gemm.cuh"
 
 #include <cuda.h>
+#include <math.h>
 
 #include <mutex>
 
 namespace pgf {
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64;
-constexpr int TC_STAGES = 3;
-constexpr int TC_THREADS = 128;
+constexpr int TC_STAGES = 4;
+constexpr int TC_THREADS = 192;
 constexpr int TILE_A_BYTES = TC_BM * TC_BK * 2;
 constexpr int TILE_B_BYTES = TC_BN * TC_BK * 2;
 constexpr int STAGE_BYTES = TILE_A_BYTES + TILE_B_BYTES;
-constexpr uint32_t TMEM_COLS = 128;
-constexpr size_t TC_SMEM = size_t(TC_STAGES) * STAGE_BYTES + 1024 /* align */ + 256 /* barriers */;
+constexpr int EPI_BYTES = 4 * 32 * 33 * 4;  // one 32x33 float transpose buffer per epilogue warp
+constexpr uint32_t TMEM_COLS = 256;        // two 128-column fp32 accumulators
+constexpr size_t TC_SMEM = size_t(TC_STAGES) * STAGE_BYTES + EPI_BYTES + 256 /* barriers */ + 1024 /* align */;
 constexpr long long WAIT_CYCLES = 4000000000ll;  // about 2 s at the B200 clock
+
+enum { TC_GENERIC = 0, TC_CE_FWD = 1, TC_CE_BWD = 2 };
 
 __device__ int g_tc_fault;
 
 struct TcParams {
   int64_t M, N, K;
   int a_mn, b_mn;
+  int mode;
+  int ng;              // 128-column tiles per work unit
+  int n_groups;        // work units per row block
+  int64_t units;
   void* D;
   int d_bf16;
   int64_t ldd;
   pgf_epilogue epi;
+  // cross-entropy modes (columns are vocabulary ids)
+  const int64_t* targets;  // (M,)
+  const float* lse;        // (M,)  CE_BWD
+  float scale;             // CE_BWD
+  float* part_m;           // (M, n_groups)  CE_FWD
+  float* part_s;           // (M, n_groups)  CE_FWD
+  float* tgt_logit;        // (M,)  CE_FWD
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -51,6 +74,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Bounded wait for the phase of parity `parity` to complete; false on timeout.
@@ -121,21 +148,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + TC_STAGES * STAGE_BYTES);
+  float* epi_buf = reinterpret_cast<float*>(tiles + TC_STAGES * STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi_buf) + EPI_BYTES);
   uint64_t* empty = full + TC_STAGES;
-  uint64_t* accb = empty + TC_STAGES;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accb + 1);
+  uint64_t* tfull = empty + TC_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = int64_t(blockIdx.y) * TC_BM, n0 = int64_t(blockIdx.x) * TC_BN;
   const int nk = int((p.K + TC_BK - 1) / TC_BK);
+  const int n_tiles = int((p.N + TC_BN - 1) / TC_BN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accb, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
@@ -150,70 +182,160 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tslot;
 
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % TC_STAGES, r = kb / TC_STAGES;
-      if (r > 0 && !mbar_wait(&empty[s], uint32_t((r - 1) & 1))) break;
-      mbar_expect_tx(&full[s], STAGE_BYTES);
-      uint8_t* sa = tiles + s * STAGE_BYTES;
-      uint8_t* sb = sa + TILE_A_BYTES;
-      const int k0 = kb * TC_BK;
-      if (!p.a_mn) {
-        tma_load_2d(sa, &tmA, &full[s], k0, int(m0));
-      } else {
-        tma_load_2d(sa, &tmA, &full[s], int(m0), k0);
-        tma_load_2d(sa + TILE_A_BYTES / 2, &tmA, &full[s], int(m0) + 64, k0);
-      }
-      if (!p.b_mn) {
-        tma_load_2d(sb, &tmB, &full[s], k0, int(n0));
-      } else {
-        tma_load_2d(sb, &tmB, &full[s], int(n0), k0);
-        tma_load_2d(sb + TILE_B_BYTES / 2, &tmB, &full[s], int(n0) + 64, k0);
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer
-    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(p.a_mn) << 15) |
-                           (uint32_t(p.b_mn) << 16) | (uint32_t(TC_BN >> 3) << 17) |
-                           (uint32_t(TC_BM >> 4) << 24);
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % TC_STAGES, r = kb / TC_STAGES;
-      if (!mbar_wait(&full[s], uint32_t(r & 1))) break;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a_base = smem_u32(tiles + s * STAGE_BYTES);
-      const uint32_t b_base = a_base + TILE_A_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < TC_BK / 16; ++kk) {
-        // K-major: advance 16 elements (32 B) inside the 128B swizzle row;
-        // MN-major: advance 16 k-rows (2 KB), two 8-row atoms apart by SBO = 1 KB.
-        const uint64_t ad = p.a_mn ? sdesc(a_base + kk * 2048, TILE_A_BYTES / 2, 1024)
-                                   : sdesc(a_base + kk * 32, 16, 1024);
-        const uint64_t bd = p.b_mn ? sdesc(b_base + kk * 2048, TILE_B_BYTES / 2, 1024)
-                                   : sdesc(b_base + kk * 32, 16, 1024);
-        umma_bf16(tmem, ad, bd, idesc, (kb | kk) != 0);
-      }
-      umma_commit(&empty[s]);
-    }
-    umma_commit(accb);
-  }
-  __syncwarp();
-
-  // ---- epilogue
-  const bool ok = mbar_wait(accb, 0);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (ok) {
-    const int64_t m = m0 + warp * 32 + lane;
-#pragma unroll 1
-    for (int c = 0; c < TC_BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c * 32), r);
-      if (m < p.M) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int64_t n = n0 + c * 32 + j;
-          if (n < p.N) epi_store(p.epi, p.D, p.d_bf16, p.ldd, m, n, __uint_as_float(r[j]));
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const int mb = int(u / p.n_groups), ng = int(u % p.n_groups);
+        const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
+        const int m0 = mb * TC_BM;
+        for (int nt = nt0; nt < nt1 && ok; ++nt) {
+          const int n0 = nt * TC_BN;
+          for (int kb = 0; kb < nk; ++kb, ++it) {
+            const int s = int(it % TC_STAGES), r = int(it / TC_STAGES);
+            if (r > 0 && !mbar_wait(&empty[s], uint32_t((r - 1) & 1))) { ok = false; break; }
+            mbar_expect_tx(&full[s], STAGE_BYTES);
+            uint8_t* sa = tiles + s * STAGE_BYTES;
+            uint8_t* sb = sa + TILE_A_BYTES;
+            const int k0 = kb * TC_BK;
+            if (!p.a_mn) {
+              tma_load_2d(sa, &tmA, &full[s], k0, m0);
+            } else {
+              tma_load_2d(sa, &tmA, &full[s], m0, k0);
+              tma_load_2d(sa + TILE_A_BYTES / 2, &tmA, &full[s], m0 + 64, k0);
+            }
+            if (!p.b_mn) {
+              tma_load_2d(sb, &tmB, &full[s], k0, n0);
+            } else {
+              tma_load_2d(sb, &tmB, &full[s], n0, k0);
+              tma_load_2d(sb + TILE_B_BYTES / 2, &tmB, &full[s], n0 + 64, k0);
+            }
+          }
         }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(p.a_mn) << 15) |
+                             (uint32_t(p.b_mn) << 16) | (uint32_t(TC_BN >> 3) << 17) |
+                             (uint32_t(TC_BM >> 4) << 24);
+      uint32_t it = 0, tt = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const int ng = int(u % p.n_groups);
+        const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
+        for (int nt = nt0; nt < nt1 && ok; ++nt, ++tt) {
+          const uint32_t buf = tt & 1, use = tt >> 1;
+          if (use > 0 && !mbar_wait(&tempty[buf], (use - 1) & 1)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t dcol = tmem + buf * TC_BN;
+          for (int kb = 0; kb < nk; ++kb, ++it) {
+            const int s = int(it % TC_STAGES), r = int(it / TC_STAGES);
+            if (!mbar_wait(&full[s], uint32_t(r & 1))) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_base = smem_u32(tiles + s * STAGE_BYTES);
+            const uint32_t b_base = a_base + TILE_A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 16; ++kk) {
+              // K-major: advance 16 elements (32 B) inside the 128B swizzle row;
+              // MN-major: advance 16 k-rows (2 KB), two 8-row atoms apart by SBO = 1 KB.
+              const uint64_t ad = p.a_mn ? sdesc(a_base + kk * 2048, TILE_A_BYTES / 2, 1024)
+                                         : sdesc(a_base + kk * 32, 16, 1024);
+              const uint64_t bd = p.b_mn ? sdesc(b_base + kk * 2048, TILE_B_BYTES / 2, 1024)
+                                         : sdesc(b_base + kk * 32, 16, 1024);
+              umma_bf16(dcol, ad, bd, idesc, (kb | kk) != 0);
+            }
+            umma_commit(&empty[s]);
+          }
+          umma_commit(&tfull[buf]);
+        }
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5; TMEM lane quarter q = warp % 4
+    const int q = warp & 3;
+    float* tb = epi_buf + (warp - 2) * 32 * 33;
+    uint32_t tt = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      const int mb = int(u / p.n_groups), ng = int(u % p.n_groups);
+      const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
+      const int64_t row = int64_t(mb) * TC_BM + q * 32 + lane;  // this thread's row (CE modes)
+      const bool row_ok = row < p.M;
+      float run_m = -INFINITY, run_s = 0.f;
+      int64_t tgt = -1;
+      float row_lse = 0.f;
+      if (p.mode != TC_GENERIC && row_ok) {
+        tgt = p.targets[row];
+        if (p.mode == TC_CE_BWD) row_lse = p.lse[row];
+      }
+      for (int nt = nt0; nt < nt1; ++nt, ++tt) {
+        const uint32_t buf = tt & 1, use = tt >> 1;
+        if (!mbar_wait(&tfull[buf], use & 1)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int64_t n0 = int64_t(nt) * TC_BN;
+#pragma unroll 1
+        for (int c = 0; c < TC_BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + buf * TC_BN + (uint32_t(q * 32) << 16) + uint32_t(c * 32), r);
+          const int64_t nc = n0 + c * 32;
+          if (p.mode == TC_CE_FWD) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nc + j < p.N) mx = fmaxf(mx, __uint_as_float(r[j]));
+            if (mx > -INFINITY) {
+              const float m1 = fmaxf(run_m, mx);
+              float s = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < p.N) s += expf(__uint_as_float(r[j]) - m1);
+              run_s = run_s * expf(run_m - m1) + s;
+              run_m = m1;
+            }
+            if (tgt >= nc && tgt < nc + 32) {
+              float v = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (tgt == nc + j) v = __uint_as_float(r[j]);
+              if (row_ok) p.tgt_logit[row] = v;
+            }
+            continue;
+          }
+          if (p.mode == TC_CE_BWD) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float g = expf(__uint_as_float(r[j]) - row_lse);
+              if (tgt == nc + j) g -= 1.0f;
+              r[j] = __float_as_uint(g * p.scale);
+            }
+          }
+          // transpose the 32x32 block through shared memory, then store row segments
+#pragma unroll
+          for (int j = 0; j < 32; ++j) tb[lane * 33 + j] = __uint_as_float(r[j]);
+          __syncwarp();
+          const int64_t n = nc + lane;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const int64_t m = int64_t(mb) * TC_BM + q * 32 + rr;
+            if (m < p.M && n < p.N) {
+              const float v = tb[rr * 33 + lane];
+              if (p.mode == TC_GENERIC) epi_store(p.epi, p.D, p.d_bf16, p.ldd, m, n, v);
+              else reinterpret_cast<__nv_bfloat16*>(p.D)[m * p.ldd + n] = __float2bfloat16_rn(v);
+            }
+          }
+          __syncwarp();
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+      }
+      if (p.mode == TC_CE_FWD && row_ok && ok) {
+        p.part_m[row * p.n_groups + ng] = run_m;
+        p.part_s[row * p.n_groups + ng] = run_s;
       }
     }
   }
@@ -268,13 +390,25 @@ static bool tc_disabled() {
   return v == 1;
 }
 
-int run_gemm_tc(const Gemm& g, cudaStream_t s) {
-  if (tc_disabled() || !g.a_bf16 || !g.b_bf16) return PGF_ERR_UNSUPPORTED;
-  if (g.M == 0 || g.N == 0) return PGF_OK;
-  if (g.K == 0) return PGF_ERR_UNSUPPORTED;
-  if (!aligned(g.A, 16) || !aligned(g.B, 16) || (g.lda * 2) % 16 || (g.ldb * 2) % 16) return PGF_ERR_UNSUPPORTED;
-  if (g.M > (int64_t(1) << 31) || g.N > (int64_t(1) << 31) || g.K > (int64_t(1) << 31)) return PGF_ERR_UNSUPPORTED;
-  if (ceil_div(g.M, TC_BM) > 65535) return PGF_ERR_UNSUPPORTED;
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
+bool tc_usable(const Gemm& g) {
+  if (tc_disabled() || !g.a_bf16 || !g.b_bf16 || g.K == 0) return false;
+  if (!aligned(g.A, 16) || !aligned(g.B, 16) || (g.lda * 2) % 16 || (g.ldb * 2) % 16) return false;
+  if (g.M > (int64_t(1) << 31) || g.N > (int64_t(1) << 31) || g.K > (int64_t(1) << 31)) return false;
+  return true;
+}
+
+// Launch over the whole (M x N) output with the given mode; `ng` = column tiles per work unit.
+static int launch_tc(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
   CUtensorMap ma, mb;
   const bool oka = g.a_trans ? make_map(&ma, g.A, g.M, g.K, g.lda, 64, 64)
                              : make_map(&ma, g.A, g.K, g.M, g.lda, 64, TC_BM);
@@ -290,17 +424,53 @@ int run_gemm_tc(const Gemm& g, cudaStream_t s) {
     set_error("gemm_tc: smem attribute: %s", cudaGetErrorString(attr_err));
     return PGF_ERR_CUDA;
   }
-  TcParams p;
   p.M = g.M; p.N = g.N; p.K = g.K;
   p.a_mn = g.a_trans; p.b_mn = g.b_trans;
-  p.D = g.D; p.d_bf16 = g.d_bf16; p.ldd = g.ldd;
-  p.epi = g.epi;
-  dim3 grid(ceil_div(g.N, TC_BN), ceil_div(g.M, TC_BM));
-  prof_begin(PROF_GEMM_TC, s);
-  gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(ma, mb, p);
-  prof_end(PROF_GEMM_TC, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
+  const int64_t n_tiles = (g.N + TC_BN - 1) / TC_BN;
+  const int64_t m_blocks = (g.M + TC_BM - 1) / TC_BM;
+  p.n_groups = int((n_tiles + p.ng - 1) / p.ng);
+  p.units = m_blocks * p.n_groups;
+  const int64_t grid = p.units < sm_count() ? p.units : sm_count();
+  prof_begin(prof_id, s);
+  gemm_tc_kernel<<<unsigned(grid), TC_THREADS, TC_SMEM, s>>>(ma, mb, p);
+  prof_end(prof_id, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
+}
+
+int run_gemm_tc(const Gemm& g, cudaStream_t s) {
+  if (!tc_usable(g)) return PGF_ERR_UNSUPPORTED;
+  if (g.M == 0 || g.N == 0) return PGF_OK;
+  TcParams p = {};
+  p.mode = TC_GENERIC;
+  p.ng = 1;
+  p.D = g.D; p.d_bf16 = g.d_bf16; p.ldd = g.ldd;
+  p.epi = g.epi;
+  return launch_tc(g, p, s, PROF_GEMM_TC);
+}
+
+int tc_ce_fwd(const Gemm& g, int ng, const int64_t* targets, float* part_m, float* part_s,
+              float* tgt_logit, int* n_groups_out, cudaStream_t s) {
+  if (!tc_usable(g)) return PGF_ERR_UNSUPPORTED;
+  TcParams p = {};
+  p.mode = TC_CE_FWD;
+  p.ng = ng;
+  p.targets = targets;
+  p.part_m = part_m; p.part_s = part_s; p.tgt_logit = tgt_logit;
+  const int64_t n_tiles = (g.N + TC_BN - 1) / TC_BN;
+  *n_groups_out = int((n_tiles + ng - 1) / ng);
+  return launch_tc(g, p, s, PROF_CE);
+}
+
+int tc_ce_bwd(const Gemm& g, const int64_t* targets, const float* lse, float scale, __nv_bfloat16* G,
+              int64_t ldg, cudaStream_t s) {
+  if (!tc_usable(g)) return PGF_ERR_UNSUPPORTED;
+  TcParams p = {};
+  p.mode = TC_CE_BWD;
+  p.ng = 1;
+  p.targets = targets; p.lse = lse; p.scale = scale;
+  p.D = G; p.d_bf16 = 1; p.ldd = ldg;
+  return launch_tc(g, p, s, PROF_CE);
 }
 
 }  // namespace pgf

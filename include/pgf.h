@@ -68,7 +68,7 @@ int pgf_version(void);
 #define PGF_PROF_RMSNORM_FWD 7
 #define PGF_PROF_RMSNORM_BWD 8
 #define PGF_PROF_EMBEDDING 9
-#define PGF_PROF_CE 10
+#define PGF_PROF_CE 10 /* the fused LM-head + cross-entropy tensor-core passes */
 long long pgf_launch_count(void);
 /* Reads and clears the fault flag of the tensor-core engine: 1 if a bounded mbarrier wait expired
  * in a tcgen05 kernel since the last call (the kernel then skipped its epilogue and returned).

@@ -218,6 +218,17 @@ def gen_components(R):
     return out
 
 
+def gen_init(R):
+    """Freshly constructed modules under fixed seeds: the initial weights a drop-in must reproduce
+    (pgf_mamba_block.py:21-49, train_singlemamba_optimized.py:89-101, pgf_rmsnorm.py:77-81)."""
+    out = {}
+    torch.manual_seed(5)
+    out["block"] = _sd(R["blk"].PGFMambaBlock(32, 16, 64, 32))
+    torch.manual_seed(6)
+    out["ssm"] = _sd(R["tso"].SingleLayerMambaPGF(24, 16))
+    return out
+
+
 def main(ref_path="/root/reference"):
     R = _import_reference(ref_path)
     torch.set_num_threads(1)
@@ -228,6 +239,7 @@ def main(ref_path="/root/reference"):
                os.path.join(HERE, "block.pt"))
     torch.save(gen_lm(R), os.path.join(HERE, "lm.pt"))
     torch.save(gen_components(R), os.path.join(HERE, "components.pt"))
+    torch.save(gen_init(R), os.path.join(HERE, "init.pt"))
     print("golden fixtures written to", HERE)
 
 

@@ -1,0 +1,61 @@
+"""CPU checks of the drop-in surface: module names, signatures, parameter names and seeded init."""
+import inspect
+import os
+import subprocess
+import sys
+
+import torch
+
+from tests.conftest import ROOT, golden
+
+
+def test_dropin_modules_import_under_reference_names():
+    code = ("import pgf_mamba_block, pgf_rmsnorm, pgf_ffn, pgf_embedding, pgf_lm_head, "
+            "train_singlemamba_optimized as t;"
+            "assert hasattr(pgf_mamba_block, 'PGFMambaSequential');"
+            "assert hasattr(t, 'SingleLayerMambaPGF');"
+            "print(pgf_mamba_block.PGFMambaBlock.__module__)")
+    env = dict(os.environ, PYTHONPATH=os.path.join(ROOT, "icml_b200", "dropin"))
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, cwd="/")
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "icml_b200.pgf_mamba_block"
+
+
+def test_signatures_match_reference():
+    from icml_b200 import pgf_embedding, pgf_ffn, pgf_lm_head
+    from icml_b200.pgf_mamba_block import PGFMambaBlock
+    from icml_b200.pgf_rmsnorm import RMSNorm
+    from icml_b200.train_singlemamba_optimized import SingleLayerMambaPGF
+
+    def params(f):
+        return list(inspect.signature(f).parameters)
+
+    assert params(pgf_ffn.pgf_ffn_grad) == ["x", "g_out", "W1", "b1", "W2", "b2", "block_size", "activation",
+                                             "compute_input_grads", "fp32_accum"]
+    assert params(pgf_ffn.pgf_ffn_forward) == ["x", "W1", "b1", "W2", "b2", "block_size", "activation",
+                                                "streaming", "callback"]
+    assert params(pgf_lm_head.pgf_lm_head_grad) == ["hidden", "g_logits", "W_lm_head", "block_size",
+                                                     "compute_input_grads", "fp32_accum"]
+    assert params(pgf_embedding.pgf_embedding_grad) == ["input_ids", "g_out", "weight", "block_size",
+                                                         "compute_input_grads", "fp32_accum"]
+    assert params(RMSNorm.pgf_grad) == ["self", "x", "g_out", "block_size", "fp32_accum",
+                                        "compute_input_grads"]
+    assert params(PGFMambaBlock.__init__) == ["self", "d_model", "d_state", "d_ff", "block_size",
+                                              "output_activation", "ffn_activation"]
+    assert params(SingleLayerMambaPGF._pass2_block_direct_grad) == [
+        "self", "u_block", "g_out_block", "h0_block", "delta_h_next", "dA_next", "fp32_accum"]
+
+
+def test_seeded_init_matches_reference():
+    from icml_b200.pgf_mamba_block import PGFMambaBlock
+    from icml_b200.train_singlemamba_optimized import SingleLayerMambaPGF
+    G = golden("init.pt")
+    torch.manual_seed(5)
+    sd = PGFMambaBlock(32, 16, 64, 32).state_dict()
+    assert sorted(sd) == sorted(G["block"])
+    for k, v in G["block"].items():
+        assert torch.equal(sd[k], v), k
+    torch.manual_seed(6)
+    sd = SingleLayerMambaPGF(24, 16).state_dict()
+    for k, v in G["ssm"].items():
+        assert torch.equal(sd[k], v), k
