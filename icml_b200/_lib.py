@@ -42,6 +42,7 @@ SIGNATURES = {
     "pgf_rmsnorm_fwd": (c_int, [P, P, P, I64, I64, c_float, c_int, P]),
     "pgf_rmsnorm_bwd_workspace": (c_size_t, [I64, I64]),
     "pgf_rmsnorm_bwd": (c_int, [P, P, P, P, P, c_int, I64, I64, c_float, c_int, P, c_size_t, P]),
+    "pgf_rmsnorm_bwd_noalloc": (c_int, [P, P, P, P, P, c_int, I64, I64, c_float, c_int, P]),
     "pgf_embedding_fwd": (c_int, [P, P, P, I64, I64, I64, c_int, P]),
     "pgf_embedding_bwd_workspace": (c_size_t, [I64, I64, I64]),
     "pgf_embedding_bwd": (c_int, [P, P, P, c_int, I64, I64, I64, c_int, P, c_size_t, P]),

@@ -217,3 +217,80 @@ extern "C" int pgf_rmsnorm_bwd(const void* x, const void* g, const float* weight
   set_error("rmsnorm_bwd: bad dtype %d", dtype);
   return PGF_ERR_INVALID;
 }
+
+// ---------------------------------------------------------------------------------------------
+// RMSNorm backward without a caller workspace.
+//
+// For callers that cannot call cudaMalloc: a plugin inside an engine that plans and owns all
+// device memory and forbids allocation from its operators, or a latency-critical loop that must
+// not enter the allocator.  The grad-weight partials live in the file-scope array below instead
+// of a workspace: NOALLOC_RMS_FLOATS floats (4 MiB), held by every GPU that loads this library
+// until the process exits.  A call needs ceil(rows / 32) * dim of them.
+//
+// The host cannot pass the array's name to a kernel (in host code it is only a stand-in for the
+// device symbol): the first call on each device, with that device current, looks up the device
+// address with cudaGetSymbolAddress and caches it.  Make that first call before any stream
+// capture.  Every call overwrites all the partial slots it reads, so nothing needs clearing, but
+// the calls share the one array: calls that overlap on the GPU (other streams, other threads)
+// race on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace pgf {
+
+constexpr size_t NOALLOC_RMS_FLOATS = size_t(1) << 20;
+static __device__ __align__(256) float g_rms_noalloc_scratch[NOALLOC_RMS_FLOATS];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+// Device address of the scratch array on the current device (looked up once per device).
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  PGF_CUDA(cudaGetDevice(&dev));
+  PGF_CHECK_ARG(dev >= 0 && dev < NOALLOC_MAX_DEVICES, "rmsnorm_bwd_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_rms_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return PGF_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return PGF_OK;
+}
+
+}  // namespace pgf
+
+extern "C" int pgf_rmsnorm_bwd_noalloc(const void* x, const void* g, const float* weight, void* grad_x,
+                                       float* grad_weight, int accumulate, int64_t rows, int64_t dim,
+                                       float eps, int dtype, pgf_stream_t stream) {
+  PGF_CHECK_ARG(weight && grad_weight, "rmsnorm_bwd_noalloc: null pointer");
+  PGF_CHECK_ARG(rows >= 0 && dim > 0 && dim <= 4096, "rmsnorm_bwd_noalloc: bad shape");
+  const size_t need = size_t(rms_bwd_ctas(rows < 1 ? 1 : rows)) * size_t(dim);
+  PGF_CHECK_ARG(need <= NOALLOC_RMS_FLOATS,
+                "rmsnorm_bwd_noalloc: ceil(rows/32)*dim = %zu floats exceeds the static scratch of %zu "
+                "floats (4 MiB); use pgf_rmsnorm_bwd with a caller workspace",
+                need, NOALLOC_RMS_FLOATS);
+  cudaStream_t s = as_stream(stream);
+  if (rows == 0) {
+    if (!accumulate) PGF_CUDA(cudaMemsetAsync(grad_weight, 0, dim * sizeof(float), s));
+    return PGF_OK;
+  }
+  PGF_CHECK_ARG(x && g, "rmsnorm_bwd_noalloc: null pointer");
+  float* part = nullptr;
+  PGF_TRY(noalloc_scratch(&part));
+  if (dtype == PGF_DTYPE_F32)
+    return rms_bwd_dispatch((const float*)x, (const float*)g, weight, (float*)grad_x, grad_weight,
+                            accumulate, rows, int(dim), eps, part, s);
+  if (dtype == PGF_DTYPE_BF16)
+    return rms_bwd_dispatch((const __nv_bfloat16*)x, (const __nv_bfloat16*)g, weight,
+                            (__nv_bfloat16*)grad_x, grad_weight, accumulate, rows, int(dim), eps,
+                            part, s);
+  set_error("rmsnorm_bwd_noalloc: bad dtype %d", dtype);
+  return PGF_ERR_INVALID;
+}

@@ -89,6 +89,15 @@ size_t pgf_rmsnorm_bwd_workspace(int64_t rows, int64_t dim);
 int pgf_rmsnorm_bwd(const void* x, const void* g, const float* weight, void* grad_x /* nullable */,
                     float* grad_weight, int accumulate, int64_t rows, int64_t dim, float eps,
                     int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+/* Same results as pgf_rmsnorm_bwd, for callers that cannot allocate device memory (an engine that
+ * owns all device memory and forbids allocation from its operators, or a loop that must not enter
+ * the allocator).  No counterpart in the reference, which has no native layer.  Scratch is a 4 MiB
+ * static device array inside libpgf.so instead of `ws`: the call is rejected (PGF_ERR_INVALID) when
+ * ceil(rows/32)*dim > 1048576.  Its first call on a device looks the array up (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the GPU race; serialise them. */
+int pgf_rmsnorm_bwd_noalloc(const void* x, const void* g, const float* weight,
+                            void* grad_x /* nullable */, float* grad_weight, int accumulate,
+                            int64_t rows, int64_t dim, float eps, int dtype, pgf_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * Embedding.  Replaces pgf_embedding_forward (pgf_embedding.py:74-124) and
