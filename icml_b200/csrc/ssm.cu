@@ -230,7 +230,8 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
 }
 
 // H_{c+1} = exp(A_n * sum_dt_c) H_c + hloc_c, sequential over chunks; loads run 4 chunks ahead.
-__global__ void ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_final) {
+__global__ void ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_final,
+                                       float* __restrict__ sum_dt) {
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= a.Bsz * a.D * NST) return;
   const int n = int(idx % NST);
@@ -262,6 +263,11 @@ __global__ void ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_fi
     hC[(c + 1) * hs] = H;
   }
   if (h_final) h_final[(b * a.D + d) * NST + n] = H;
+  if (sum_dt && n == 0) {
+    float t = 0.f;
+    for (int64_t k = 0; k < a.nC; ++k) t += sdt[k * cs];
+    sum_dt[b * a.D + d] = t;
+  }
 }
 
 __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs a) {
@@ -368,7 +374,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArg
 
 __global__ void ssm_compose_bwd_kernel(const SsmArgs a, const float* __restrict__ dh_end,
                                        const float* __restrict__ dA_end, float* __restrict__ dh_start,
-                                       float* __restrict__ dA_start) {
+                                       float* __restrict__ dA_start, float* __restrict__ sum_dt_excl) {
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= a.Bsz * a.D * NST) return;
   const int n = int(idx % NST);
@@ -408,6 +414,12 @@ __global__ void ssm_compose_bwd_kernel(const SsmArgs a, const float* __restrict_
   }
   if (dh_start) dh_start[o] = G;
   if (dA_start) dA_start[o] = aE;
+  if (sum_dt_excl && n == 0) {
+    // sum of dt over every token but the first: within-chunk sums plus the later chunks' first dt
+    float t = 0.f;
+    for (int64_t k = 0; k < a.nC; ++k) t += sdt2[k * cs] + (k > 0 ? dt0[k * cs] : 0.f);
+    sum_dt_excl[b * a.D + d] = t;
+  }
 }
 
 // Main backward kernel.  Shared memory (dynamic): ckpt [Tc/ST][SSM_THREADS][NS] floats, then
@@ -728,7 +740,8 @@ static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u,
   return run_gemm(g, s);
 }
 
-static int ssm_forward_states(const SsmArgs& a, const SsmPlan& p, float* h_final, cudaStream_t s) {
+static int ssm_forward_states(const SsmArgs& a, const SsmPlan& p, float* h_final, cudaStream_t s,
+                              float* sum_dt = nullptr) {
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
   prof_begin(PROF_SSM_CHUNK_FWD, s);
   ssm_chunk_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
@@ -736,7 +749,7 @@ static int ssm_forward_states(const SsmArgs& a, const SsmPlan& p, float* h_final
   PGF_LAUNCH_CHECK();
   const int64_t nth = p.Bsz * p.D * NST;
   prof_begin(PROF_SSM_COMPOSE, s);
-  ssm_compose_fwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, h_final);
+  ssm_compose_fwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, h_final, sum_dt);
   prof_end(PROF_SSM_COMPOSE, s, bytes_compose(a));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
@@ -846,7 +859,8 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   const int64_t nth = Bsz * D * NST;
-  ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start);
+  ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start,
+                                                            nullptr);
   PGF_LAUNCH_CHECK();
   const int KS = int((p.Tc + ST - 1) / ST);
   const size_t smem = (size_t(KS) * SSM_THREADS * NS + size_t(ST) * SSM_WARPS * 32 + 2 * 2 * ST * DC) * 4;
@@ -883,5 +897,68 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   gx.epi.addend_dtype = 0;
   gx.epi.ld_addend = D;
   PGF_TRY(run_gemm(gx, s));
+  return PGF_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Segment summaries for a sequence sharded across ranks (affine-recurrence composition).
+// ---------------------------------------------------------------------------------------------
+extern "C" int pgf_ssm_summary(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                               const float* h_init, float* h_final, float* sum_dt, int64_t Bsz, int64_t L,
+                               int64_t D, int64_t N, int dtype, void* ws, size_t ws_bytes,
+                               pgf_stream_t stream) {
+  PGF_TRY(check_common(Bsz, L, D, N, PGF_ACT_NONE, dtype));
+  PGF_CHECK_ARG(u && W_cat && b_cat && A_log && h_final && sum_dt, "ssm_summary: null pointer");
+  PGF_CHECK_ARG(L > 0, "ssm_summary: empty segment");
+  cudaStream_t s = as_stream(stream);
+  SsmPlan p = plan_of(Bsz, L, D);
+  Workspace W(ws, ws_bytes);
+  SsmArgs a = {};
+  a.A_log = A_log; a.act = PGF_ACT_NONE; a.h_init = h_init;
+  const void* wop;
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
+  return ssm_forward_states(a, p, h_final, s, sum_dt);
+}
+
+extern "C" int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                                   const float* A_log, const float* scale, const float* h_init,
+                                   float* dh_start, float* dA_start, float* sum_dt_excl, int64_t Bsz,
+                                   int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                                   size_t ws_bytes, pgf_stream_t stream) {
+  PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
+  PGF_CHECK_ARG(u && g && W_cat && b_cat && A_log && scale && dh_start && dA_start && sum_dt_excl,
+                "ssm_bwd_summary: null pointer");
+  PGF_CHECK_ARG(L > 0, "ssm_bwd_summary: empty segment");
+  cudaStream_t s = as_stream(stream);
+  SsmPlan p = plan_of(Bsz, L, D);
+  Workspace W(ws, ws_bytes);
+  SsmArgs a = {};
+  a.A_log = A_log; a.scale = scale; a.act = act; a.h_init = h_init;
+  a.g = g; a.g_bf16 = dtype;
+  const void* wop;
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
+  const size_t BL = size_t(Bsz) * L;
+  a.actp = act != PGF_ACT_NONE ? W.take<float>(BL * p.D) : nullptr;
+  a.dloc = W.take<float>(size_t(Bsz) * p.nC * D * NST);
+  a.X = W.take<float>(size_t(Bsz) * p.nC * D * NST);
+  a.sdt2 = W.take<float>(size_t(Bsz) * p.nC * D);
+  a.dt0 = W.take<float>(size_t(Bsz) * p.nC * D);
+  if ((act != PGF_ACT_NONE && !a.actp) || !a.dloc || !a.X || !a.sdt2 || !a.dt0) {
+    set_error("ssm_bwd_summary: workspace too small (%zu)", ws_bytes);
+    return PGF_ERR_WORKSPACE;
+  }
+  dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  if (act != PGF_ACT_NONE) {
+    PGF_TRY(ssm_forward_states(a, p, nullptr, s));
+    a.y = nullptr;
+    ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+    PGF_LAUNCH_CHECK();
+  }
+  ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  const int64_t nth = Bsz * D * NST;
+  ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, nullptr, nullptr, dh_start, dA_start,
+                                                            sum_dt_excl);
+  PGF_LAUNCH_CHECK();
   return PGF_OK;
 }

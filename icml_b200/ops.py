@@ -296,3 +296,38 @@ def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_e
                          Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(), _stream()), "ssm_bwd")
     return {"W_cat": gW, "b_cat": gb, "A_log": gA, "D": gD, "scale": gS, "grad_u": gu,
             "delta_h0": dh0, "dA0": dA0}
+
+
+def ssm_summary(u, W_cat, b_cat, A_log, h_init=None):
+    """(state after the segment from h_init, sum of dt per (batch, channel))."""
+    _cuda(u, W_cat)
+    u = _c(u)
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    hf = torch.empty(Bsz, D, N, dtype=torch.float32, device=u.device)
+    sdt = torch.empty(Bsz, D, dtype=torch.float32, device=u.device)
+    Lb = lib()
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 0), u.device)
+    W_cat, b_cat, A_log, h_init = (_f32(t) for t in (W_cat, b_cat, A_log, h_init))
+    check(Lb.pgf_ssm_summary(_p(u), _p(W_cat), _p(b_cat), _p(A_log), _p(h_init), _p(hf), _p(sdt), Bsz, L_,
+                             D, N, _dt(u), _p(ws), ws.numel(), _stream()), "ssm_summary")
+    return hf, sdt
+
+
+def ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=None, act=None):
+    """(adjoint at the first token for a zero end carry, first token's decay, sum of dt but the first)."""
+    _cuda(u, g, W_cat)
+    u, g = _c(u), _c(g.to(u.dtype))
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    dev = u.device
+    dh0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev)
+    dA0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev)
+    sdx = torch.empty(Bsz, D, dtype=torch.float32, device=dev)
+    Lb = lib()
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 1), dev)
+    W_cat, b_cat, A_log, scale, h_init = (_f32(t) for t in (W_cat, b_cat, A_log, scale, h_init))
+    check(Lb.pgf_ssm_bwd_summary(_p(u), _p(g), _p(W_cat), _p(b_cat), _p(A_log), _p(scale), _p(h_init),
+                                 _p(dh0), _p(dA0), _p(sdx), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws),
+                                 ws.numel(), _stream()), "ssm_bwd_summary")
+    return dh0, dA0, sdx

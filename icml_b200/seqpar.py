@@ -1,0 +1,188 @@
+"""Sequence-sharded PGF training step: one long sequence split into contiguous segments, one per rank.
+
+Every operator of the block is token-local except the selective scan, whose recurrence
+h_t = exp(dt_t A) h_{t-1} + b_t is affine.  A rank's segment therefore summarises, from a zero
+start, to (h_loc, sum_dt): its end state and its total decay exp(A_n * sum_dt).  One all-gather of
+those per layer gives every rank the state entering its segment (an exclusive prefix over the
+ranks before it); it then runs its segment from that state.  The backward mirrors it: from a zero
+carry each rank computes the adjoint at its first token, its first token's decay and the decay of
+the rest of its segment; one all-gather per layer gives every rank the carry entering its segment
+from the right (the reference's block hand-off, pgf_mamba_block.py:86-112 and :207-234, across
+GPUs).  Parameter and embedding gradients are partial sums, all-reduced once per step.
+
+The functions take an `ops` namespace (default: the CUDA operators of icml_b200.ops) so the same
+host logic can be exercised with other implementations of the operators.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import ops as cuda_ops
+
+
+@dataclass
+class SeqGroup:
+    """A process group whose ranks hold consecutive segments of the same sequences."""
+    group: Any = None
+    rank: int = 0
+    world: int = 1
+
+    @staticmethod
+    def from_default() -> "SeqGroup":
+        if not dist.is_initialized():
+            return SeqGroup()
+        return SeqGroup(None, dist.get_rank(), dist.get_world_size())
+
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        """(world, *t.shape) stack of every rank's tensor, in rank order."""
+        t = t.contiguous()
+        if self.world == 1:
+            return t.unsqueeze(0)
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        dist.all_gather(out, t, group=self.group)
+        return torch.stack(out, 0)
+
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            dist.all_reduce(t, group=self.group)
+        return t
+
+
+def compose_forward_state(h_locs: torch.Tensor, sum_dts: torch.Tensor, A: torch.Tensor, rank: int) -> torch.Tensor:
+    """State entering segment `rank`: fold H <- exp(A * sum_dt_j) H + h_loc_j over ranks j < rank.
+    h_locs (P, B, d, N), sum_dts (P, B, d), A (N,) = -exp(A_log)."""
+    H = torch.zeros_like(h_locs[0])
+    for j in range(rank):
+        H = torch.exp(A * sum_dts[j].unsqueeze(-1)) * H + h_locs[j]
+    return H
+
+
+def compose_backward_carry(d_locs: torch.Tensor, dA_starts: torch.Tensor, sum_dt_excls: torch.Tensor,
+                           A: torch.Tensor, rank: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(dh_end, dA_end) for segment `rank`: the adjoint at the first token of the next segment and
+    that token's decay.  Folds from the last rank down to rank + 1:
+    X = a_E * G;  G <- exp(A * sum_dt_excl_j) X + d_loc_j;  a_E <- dA_start_j."""
+    P = d_locs.shape[0]
+    G = torch.zeros_like(d_locs[0])
+    aE = torch.ones_like(d_locs[0])
+    for j in range(P - 1, rank, -1):
+        X = aE * G
+        G = torch.exp(A * sum_dt_excls[j].unsqueeze(-1)) * X + d_locs[j]
+        aE = dA_starts[j]
+    return G, aE
+
+
+def _wb(m):
+    W = torch.cat([m.dt_proj.weight, m.B_proj.weight, m.C_proj.weight], 0)
+    b = torch.cat([m.dt_proj.bias, m.B_proj.bias, m.C_proj.bias], 0)
+    return W, b
+
+
+@torch.no_grad()
+def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
+    """PGFMambaBlock.pgf_forward on this rank's segment; returns (y, state entering the segment)."""
+    B, L, D = x.shape
+    m = block.mamba
+    W, b = _wb(m)
+    A = -torch.exp(m.A_log.detach().float())
+    xn = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
+    if sp.world > 1:
+        h_loc, sdt = ops.ssm_summary(xn, W, b, m.A_log)
+        h_in = compose_forward_state(sp.all_gather(h_loc), sp.all_gather(sdt), A, sp.rank)
+    else:
+        h_in = None
+    y, _ = ops.ssm_fwd(xn, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
+    x1 = y + x
+    xn2 = ops.rmsnorm_fwd(x1, block.norm2.weight, block.norm2.eps)
+    f = ops.ffn_fwd(xn2.reshape(-1, D), block.W1, block.b1, block.W2, block.b2, block.ffn_activation)
+    return f.reshape(B, L, D) + x1, h_in
+
+
+@torch.no_grad()
+def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[torch.Tensor], sp: SeqGroup,
+                   ops=cuda_ops) -> Dict[str, Any]:
+    """PGFMambaBlock.pgf_backward on this rank's segment (local partial parameter gradients)."""
+    B, L, D = x.shape
+    m = block.mamba
+    W, b = _wb(m)
+    A = -torch.exp(m.A_log.detach().float())
+    g_out = g_out.to(x.dtype)
+    xn1 = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
+    y, _ = ops.ssm_fwd(xn1, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
+    m_out = y + x
+    xn2 = ops.rmsnorm_fwd(m_out, block.norm2.weight, block.norm2.eps)
+    fr = ops.ffn_bwd(xn2.reshape(-1, D), g_out.reshape(-1, D), block.W1, block.b1, block.W2,
+                     block.ffn_activation, need_gx=True)
+    gn2w, gn2x = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), block.norm2.weight, block.norm2.eps)
+    g_m = gn2x + g_out
+    dh_end = dA_end = None
+    if sp.world > 1:
+        d_loc, dA0, sdx = ops.ssm_bwd_summary(xn1, g_m, W, b, m.A_log, m.scale, h_init=h_in,
+                                              act=m.output_activation)
+        dh_end, dA_end = compose_backward_carry(sp.all_gather(d_loc), sp.all_gather(dA0), sp.all_gather(sdx),
+                                                A, sp.rank)
+    r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, h_init=h_in, dh_end=dh_end, dA_end=dA_end,
+                    act=m.output_activation)
+    gn1w, gn1x = ops.rmsnorm_bwd(x, r["grad_u"], block.norm1.weight, block.norm1.eps)
+    d, N = m.d_model, m.d_state
+    gscale = r["scale"].sum().expand(d).clone() if m.reference_scale_grad else r["scale"]
+    grads = {
+        "W1": fr["grad_W1"], "b1": fr["grad_b1"], "W2": fr["grad_W2"], "b2": fr["grad_b2"],
+        "mamba.A_log": r["A_log"], "mamba.D": r["D"], "mamba.scale": gscale,
+        "mamba.dt_proj.weight": r["W_cat"][:d], "mamba.dt_proj.bias": r["b_cat"][:d],
+        "mamba.B_proj.weight": r["W_cat"][d:d + N], "mamba.B_proj.bias": r["b_cat"][d:d + N],
+        "mamba.C_proj.weight": r["W_cat"][d + N:], "mamba.C_proj.bias": r["b_cat"][d + N:],
+        "norm1.weight": gn1w, "norm2.weight": gn2w,
+    }
+    return {"grads": grads, "grad_input": gn1x + g_m}
+
+
+@torch.no_grad()
+def lm_forward_backward(model, input_ids: torch.Tensor, targets: torch.Tensor, sp: SeqGroup,
+                        ops=cuda_ops, total_tokens: Optional[int] = None):
+    """The PGF LM step on this rank's segment of every sequence.  Returns (global mean loss, grads):
+    gradients are summed over ranks (all-reduce), the loss is the mean over all ranks' tokens."""
+    B, L = input_ids.shape
+    d = model.d_model
+    T_total = total_tokens if total_tokens is not None else B * L * sp.world
+    x = ops.embedding_fwd(input_ids, model.emb_weight, dtype=model.act_dtype)
+    stash: List[Tuple[torch.Tensor, Optional[torch.Tensor]]] = []
+    for layer in model.backbone.layers:
+        y, h_in = block_forward(layer, x, sp, ops)
+        stash.append((x, h_in))
+        x = y
+    h = x.reshape(-1, d)
+    tg = targets.reshape(-1)
+    loss_rows, lse = ops.lm_head_ce_fwd(h, model.lm_head_weight, tg)
+    gW, gh = ops.lm_head_ce_bwd(h, model.lm_head_weight, tg, lse, 1.0 / T_total)
+    grads = {"lm_head": gW}
+    g = gh.reshape(B, L, d)
+    for i in reversed(range(model.n_layers)):
+        xi, h_in = stash.pop()
+        res = block_backward(model.backbone.layers[i], xi, g, h_in, sp, ops)
+        for k, v in res["grads"].items():
+            grads[f"layers.{i}.{k}"] = v
+        g = res["grad_input"]
+    grads["emb"] = ops.embedding_bwd(input_ids, g, model.vocab_size)
+    if getattr(model, "tied", False):
+        grads["emb"] = grads["emb"] + grads.pop("lm_head")
+    loss_sum = loss_rows.sum().reshape(1).float()
+    if sp.world > 1:
+        names = sorted(grads)
+        flat = torch.cat([grads[k].reshape(-1).float() for k in names] + [loss_sum])
+        sp.all_reduce_(flat)
+        o = 0
+        for k in names:
+            n = grads[k].numel()
+            grads[k] = flat[o:o + n].view_as(grads[k])
+            o += n
+        loss_sum = flat[o:o + 1]
+    return loss_sum[0] / T_total, grads
+
+
+__all__ = ["SeqGroup", "compose_forward_state", "compose_backward_carry", "block_forward", "block_backward",
+           "lm_forward_backward"]

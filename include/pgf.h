@@ -225,6 +225,29 @@ int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, const float* b
                 int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
                 pgf_stream_t stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Segment summaries for a sequence sharded across GPUs.  No single-function counterpart in the
+ * reference: they are the block hand-off of pgf_mamba_block.py:86-112 (forward, `curr_h`) and
+ * :207-234 (backward, `delta_h_next` / `dA_next`) made composable, using that the recurrence is
+ * affine.  Workspace: pgf_ssm_workspace(..., backward = 0 / 1).
+ *
+ * pgf_ssm_summary: state after the segment starting from h_init (NULL = zeros) -> h_final
+ *   (Bsz, D, N), and sum_dt (Bsz, D) = sum over the segment of softplus(dt_in), so that the
+ *   segment's total decay is exp(A_n * sum_dt).
+ * pgf_ssm_bwd_summary: adjoint at the segment's first token for a zero carry at its end ->
+ *   dh_start (Bsz, D, N), the first token's decay dA_start = exp(dt_first A) (Bsz, D, N), and
+ *   sum_dt_excl (Bsz, D) = sum of dt over every token but the first.  h_init is only read when
+ *   act != PGF_ACT_NONE (the output activation's derivative needs the states).
+ * ------------------------------------------------------------------------------------------ */
+int pgf_ssm_summary(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                    const float* h_init, float* h_final, float* sum_dt, int64_t Bsz, int64_t L,
+                    int64_t D, int64_t N, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                        const float* A_log, const float* scale, const float* h_init, float* dh_start,
+                        float* dA_start, float* sum_dt_excl, int64_t Bsz, int64_t L, int64_t D,
+                        int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                        pgf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

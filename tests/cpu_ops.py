@@ -1,0 +1,102 @@
+"""CPU implementation of the operator namespace that icml_b200.seqpar drives, built on the oracle.
+
+Test infrastructure: it lets the sequence-sharding host logic (segment summaries, all-gathers,
+carry composition, gradient all-reduce) run on gloo CPU ranks and be compared with the
+single-process oracle.  Signatures follow icml_b200.ops.
+"""
+import torch
+import torch.nn.functional as F
+
+from oracle import pgf_oracle as O
+
+
+def _params(W_cat, b_cat, A_log, Dp=None, scale=None):
+    N = A_log.shape[0]
+    d = W_cat.shape[1]
+    return {"A_log": A_log.detach(), "D": (Dp if Dp is not None else torch.ones(d)).detach(),
+            "scale": (scale if scale is not None else torch.ones(d)).detach(),
+            "dt_w": W_cat[:d].detach(), "dt_b": b_cat[:d].detach(), "B_w": W_cat[d:d + N].detach(),
+            "B_b": b_cat[d:d + N].detach(), "C_w": W_cat[d + N:].detach(), "C_b": b_cat[d + N:].detach()}
+
+
+def _dt(u, W_cat, b_cat):
+    d = W_cat.shape[1]
+    return F.softplus((u @ W_cat.t() + b_cat)[..., :d])
+
+
+def rmsnorm_fwd(x, w, eps):
+    return O.rmsnorm_forward(x, w.detach(), eps)
+
+
+def rmsnorm_bwd(x, g, w, eps, need_gx=True):
+    gw, gx = O.rmsnorm_grad(x, g, w.detach(), eps)
+    return gw, (gx if need_gx else None)
+
+
+def ssm_summary(u, W_cat, b_cat, A_log, h_init=None):
+    p = _params(W_cat, b_cat, A_log)
+    _, _, h = O.ssm_forward(p, u, u.shape[1], h0=h_init)
+    return h, _dt(u, W_cat, b_cat).sum(1)
+
+
+def ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, want_h_final=False):
+    p = _params(W_cat, b_cat, A_log, Dp, scale)
+    y, _, h = O.ssm_forward(p, u, u.shape[1], h0=h_init, act=act)
+    return y, (h if want_h_final else None)
+
+
+def ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=None, act=None):
+    p = _params(W_cat, b_cat, A_log, None, scale)
+    B, L, d = u.shape
+    N = A_log.shape[0]
+    h0 = h_init if h_init is not None else torch.zeros(B, d, N, dtype=u.dtype)
+    r = O.ssm_block_grad(p, u, g, h0, torch.zeros(B, d, N, dtype=u.dtype), torch.ones(B, d, N, dtype=u.dtype),
+                         act=act)
+    return r["delta_h0"], r["dA0"], _dt(u, W_cat, b_cat)[:, 1:].sum(1)
+
+
+def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_end=None, act=None,
+            want_carry=False):
+    p = _params(W_cat, b_cat, A_log, Dp, scale)
+    B, L, d = u.shape
+    N = A_log.shape[0]
+    z = torch.zeros(B, d, N, dtype=u.dtype)
+    r = O.ssm_block_grad(p, u, g, h_init if h_init is not None else z, dh_end if dh_end is not None else z,
+                         dA_end if dA_end is not None else torch.ones_like(z), act=act)
+    return {"W_cat": torch.cat([r["dt_w"], r["B_w"], r["C_w"]], 0),
+            "b_cat": torch.cat([r["dt_b"], r["B_b"], r["C_b"]], 0),
+            "A_log": r["A_log"], "D": r["D"], "scale": r["scale"], "grad_u": r["grad_u"],
+            "delta_h0": r["delta_h0"], "dA0": r["dA0"]}
+
+
+def ffn_fwd(x, W1, b1, W2, b2, activation="gelu"):
+    return O.ffn_forward(x, W1.detach(), b1.detach(), W2.detach(), b2.detach(), activation)
+
+
+def ffn_bwd(x, g, W1, b1, W2, activation="gelu", need_gx=True):
+    r = O.ffn_grad(x, g, W1.detach(), b1.detach(), W2.detach(), torch.zeros(W2.shape[0]), activation)
+    if not need_gx:
+        r.pop("grad_x")
+    return r
+
+
+def embedding_fwd(ids, W, dtype=torch.float32):
+    return O.embedding_forward(ids, W.detach()).to(dtype)
+
+
+def embedding_bwd(ids, g, vocab):
+    return torch.zeros(vocab, g.shape[-1], dtype=g.dtype).index_add_(0, ids.reshape(-1), g.reshape(-1, g.shape[-1]))
+
+
+def lm_head_ce_fwd(h, W, targets):
+    logits = h @ W.detach().t()
+    lse = torch.logsumexp(logits, -1)
+    return lse - logits[torch.arange(h.shape[0]), targets], lse
+
+
+def lm_head_ce_bwd(h, W, targets, lse, grad_scale, need_gh=True):
+    logits = h @ W.detach().t()
+    G = torch.exp(logits - lse[:, None])
+    G[torch.arange(h.shape[0]), targets] -= 1.0
+    G *= grad_scale
+    return G.t() @ h, (G @ W.detach() if need_gh else None)

@@ -1,0 +1,112 @@
+"""Sequence sharding of the PGF step across ranks: host logic on gloo CPU ranks against the oracle.
+
+Two (and three) CPU processes each hold a contiguous segment of the same sequences; the segment
+summaries are all-gathered and composed, gradients all-reduced.  The result must equal the
+single-process oracle step on the whole sequences.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import pgf_oracle as O
+from tests.conftest import ROOT
+
+V, D_MODEL, D_FF, N_LAYERS, B, L = 64, 16, 32, 2, 2, 48
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _model():
+    from icml_b200.lm import PGFLanguageModel
+    torch.manual_seed(3)
+    m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 16, "cpu")
+    with torch.no_grad():
+        m.emb_weight.normal_(0, 0.5)
+        m.lm_head_weight.normal_(0, 0.3)
+    return m
+
+
+def _data():
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, V, (B, L), generator=g)
+    return ids, torch.randint(0, V, (B, L), generator=g)
+
+
+def _worker(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+        sys.path.insert(0, ROOT)
+        from icml_b200 import seqpar
+        from tests import cpu_ops
+        m = _model()
+        ids, tg = _data()
+        seg = L // world
+        sl = slice(rank * seg, (rank + 1) * seg)
+        sp = seqpar.SeqGroup.from_default()
+        loss, grads = seqpar.lm_forward_backward(m, ids[:, sl].contiguous(), tg[:, sl].contiguous(), sp,
+                                                 ops=cpu_ops)
+        if rank == 0:
+            torch.save({"loss": loss, "grads": grads}, out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def _reference():
+    m = _model()
+    ids, tg = _data()
+    blocks = [{k: v.detach() for k, v in layer.state_dict().items()} for layer in m.backbone.layers]
+    return O.lm_pgf_step(m.emb_weight.detach(), m.lm_head_weight.detach(), blocks, ids, tg, 16)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sequence_sharded_step_matches_single_process_oracle(world, tmp_path):
+    out = str(tmp_path / "r0.pt")
+    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
+    got = torch.load(out, weights_only=False)
+    rloss, rgrads = _reference()
+    assert abs(got["loss"].item() - rloss.item()) < 1e-5
+    for k, v in rgrads.items():
+        err = (got["grads"][k] - v).abs().max().item()
+        assert err <= 1e-5 + 1e-4 * v.abs().max().item(), (k, err)
+
+
+def test_compose_functions_equal_sequential_scan():
+    """compose_forward_state / compose_backward_carry against one long oracle scan."""
+    from icml_b200.seqpar import compose_backward_carry, compose_forward_state
+    from tests import cpu_ops
+    g = torch.Generator().manual_seed(8)
+    d, N, Lt, P = 12, 16, 60, 4
+    p = O.ssm_init(d, N, g, dtype=torch.float64)
+    W = torch.cat([p["dt_w"], p["B_w"], p["C_w"]]).double()
+    bb = torch.cat([p["dt_b"], p["B_b"], p["C_b"]]).double()
+    u = torch.randn(1, Lt, d, generator=g, dtype=torch.float64)
+    gy = torch.randn(1, Lt, d, generator=g, dtype=torch.float64)
+    A = -torch.exp(p["A_log"])
+    segs = [slice(i * Lt // P, (i + 1) * Lt // P) for i in range(P)]
+    sums = [cpu_ops.ssm_summary(u[:, s], W, bb, p["A_log"]) for s in segs]
+    h_locs = torch.stack([s[0] for s in sums])
+    sdts = torch.stack([s[1] for s in sums])
+    _, h0s, _ = O.ssm_forward(p, u, Lt // P)
+    for r in range(P):
+        assert torch.allclose(compose_forward_state(h_locs, sdts, A, r), h0s[r], atol=1e-10)
+    # backward carries: the whole-sequence block chain of the oracle is the truth
+    bs = [cpu_ops.ssm_bwd_summary(u[:, s], gy[:, s], W, bb, p["A_log"], p["scale"]) for s in segs]
+    d_locs, dA0s, sdx = (torch.stack([b[i] for b in bs]) for i in range(3))
+    dh = torch.zeros(1, d, N, dtype=torch.float64)
+    dA = torch.ones(1, d, N, dtype=torch.float64)
+    for r in reversed(range(P)):
+        G, aE = compose_backward_carry(d_locs, dA0s, sdx, A, r)
+        assert torch.allclose(G, dh, atol=1e-10) and torch.allclose(aE, dA, atol=1e-12)
+        res = O.ssm_block_grad(p, u[:, segs[r]], gy[:, segs[r]], h0s[r], dh, dA)
+        dh, dA = res["delta_h0"], res["dA0"]
