@@ -3,8 +3,10 @@
 Workload (default): the 8-layer PGF Mamba language model of the reference's training scripts at
 d_model 256 / d_state 16 / d_ff 1024 / vocab 50257 (reference SSM variant, untied embedding and
 LM head as in train_wikitext_rebuttal.py:58-77), one sequence of L tokens per GPU, synthetic
-Zipf(1.1) token ids, bf16 activations, fp32 weights and AdamW.  N GPUs run N replicas with an NCCL
-gradient all-reduce (data parallel, per-GPU work fixed: weak scaling).
+Zipf(1.1) token ids, bf16 activations, fp32 weights and AdamW.  On N GPUs (one process each) the
+default shards ONE sequence of N x L tokens across the GPUs (segment state hand-off through small
+all-gathers, one gradient all-reduce); --parallel dp runs N independent sequences instead.  Either
+way the per-GPU work is fixed (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--seq-len L] [--impl b200|reference]
 
@@ -47,6 +49,9 @@ def parse():
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--cpu-sample-len", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parallel", default="sp", choices=["sp", "dp"],
+                    help="N>1: sp = one sequence of N x seq-len tokens sharded across the GPUs "
+                         "(state hand-off between segments), dp = N independent sequences")
     return ap.parse_args()
 
 
@@ -55,8 +60,9 @@ def config_of(a, world):
         "workload": f"8-layer PGF Mamba LM, d_model {a.d_model}, d_state 16, d_ff {a.d_ff}, vocab {a.vocab}, "
                     f"B={a.batch} x L={a.seq_len} tokens per GPU, bf16 activations / fp32 weights + AdamW",
         "layers": a.layers, "d_model": a.d_model, "d_state": 16, "d_ff": a.d_ff, "vocab": a.vocab,
-        "global_batch": a.batch * world, "seq_len": a.seq_len, "pgf_block_size": a.block_size,
-        "parallelism": f"dp{world}", "ssm_variant": "reference (d_inner = d_model, shared A)",
+        "global_batch": a.batch * (world if a.parallel == "dp" else 1),
+        "seq_len": a.seq_len * (world if a.parallel == "sp" else 1), "pgf_block_size": a.block_size,
+        "parallelism": f"{a.parallel}{world}", "ssm_variant": "reference (d_inner = d_model, shared A)",
         "l2": "per-step working set (weights, optimizer state, activations) > 126 MB L2; no explicit flush",
     }
 
@@ -225,7 +231,12 @@ def run_gpu(a, rank, world, local_rank):
         if pg is not None:
             torch.distributed.broadcast(p.data, 0)
 
-    ids_host = zipf_ids(a.batch * (a.seq_len + 1), a.vocab, seed=100 + rank).reshape(a.batch, a.seq_len + 1)
+    if world > 1 and a.parallel == "sp":
+        # one sequence of world x seq_len tokens; this rank holds the segment [rank*L, (rank+1)*L)
+        full = zipf_ids(a.batch * (a.seq_len * world + 1), a.vocab, seed=100).reshape(a.batch, -1)
+        ids_host = full[:, rank * a.seq_len: (rank + 1) * a.seq_len + 1]
+    else:
+        ids_host = zipf_ids(a.batch * (a.seq_len + 1), a.vocab, seed=100 + rank).reshape(a.batch, a.seq_len + 1)
     inp_host = ids_host[:, :-1].contiguous().pin_memory()
     tgt_host = ids_host[:, 1:].contiguous().pin_memory()
     inp = inp_host.to(dev)
@@ -244,11 +255,18 @@ def run_gpu(a, rank, world, local_rank):
             g.copy_(flat[o:o + n].view_as(g))
             o += n
 
+    from icml_b200 import seqpar
+    sp = seqpar.SeqGroup.from_default() if (world > 1 and a.parallel == "sp") else None
+
     def step(x, y):
         model.optimizer.zero_grad(set_to_none=True)
-        loss, grads = model.forward_backward(x, y)
-        model._assign(grads)
-        allreduce_grads()
+        if sp is not None:
+            loss, grads = seqpar.lm_forward_backward(model, x, y, sp)  # gradients already summed
+            model._assign(grads)
+        else:
+            loss, grads = model.forward_backward(x, y)
+            model._assign(grads)
+            allreduce_grads()
         model.optimizer.step()
         return loss
 

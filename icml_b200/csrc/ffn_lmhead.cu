@@ -348,7 +348,8 @@ static int ce_carve(Workspace& W, CeWs& c, int64_t T, int64_t V, int64_t d, int 
 constexpr int CE_NG = 16;                 // 128-column tiles per forward work unit (2048 vocab ids)
 constexpr int64_t CE_BWD_ROWS = 16384;    // rows of G (bf16, rows x vocab) materialised at a time
 
-static int64_t ce_ngroups(int64_t V) { return ((V + 127) / 128 + CE_NG - 1) / CE_NG; }
+// partial (max, sum) pairs per row: two column halves per group of CE_NG tiles
+static int64_t ce_ngroups(int64_t V) { return 2 * (((V + 127) / 128 + CE_NG - 1) / CE_NG); }
 static int64_t ce_ldv(int64_t V) { return (V + 63) / 64 * 64; }
 
 static size_t ce_tc_ws_bytes(int64_t T, int64_t V, int64_t d) {

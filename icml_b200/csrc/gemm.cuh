@@ -46,23 +46,39 @@ int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out
 // dst[i] = bf16(src[i]) (weights to the tensor-core operand type)
 int to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s);
 
-// Epilogue applied to one accumulator element.
-__device__ __forceinline__ void epi_store(const pgf_epilogue& e, void* D, int d_bf16, int64_t ldd,
-                                          int64_t m, int64_t n, float acc) {
-  float v = e.alpha * acc;
-  if (e.bias) v += e.bias[n];
+// GELU / GELU' with the hardware tanh approximation (tanh.approx.f32, relative error ~2^-11): used
+// only where the result is rounded to bf16 (8-bit mantissa) anyway.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float gelu_bf(float x) {
+  return 0.5f * x * (1.0f + tanh_approx(PGF_GELU_C * (x + PGF_GELU_A * x * x * x)));
+}
+__device__ __forceinline__ float gelu_prime_bf(float x) {
+  const float t = tanh_approx(PGF_GELU_C * (x + PGF_GELU_A * x * x * x));
+  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * (PGF_GELU_C * (1.0f + 3.0f * PGF_GELU_A * x * x));
+}
+
+// Epilogue applied to one accumulator element, the column's bias already loaded.
+__device__ __forceinline__ void epi_store_biased(const pgf_epilogue& e, void* D, int d_bf16, int64_t ldd,
+                                                 int64_t m, int64_t n, float acc, float bias_n) {
+  float v = fmaf(e.alpha, acc, bias_n);
   switch (e.kind) {
     case PGF_EPI_GELU:
       if (e.aux_out) stv(e.aux_out, e.aux_out_dtype, m * e.ld_aux_out + n, v);
-      v = gelu_f(v);
+      v = d_bf16 ? gelu_bf(v) : gelu_f(v);
       break;
     case PGF_EPI_RELU:
       if (e.aux_out) stv(e.aux_out, e.aux_out_dtype, m * e.ld_aux_out + n, v);
       v = v > 0.f ? v : 0.f;
       break;
-    case PGF_EPI_DGELU:
-      v *= gelu_prime_f(ldv(e.aux, e.aux_dtype, m * e.ld_aux + n));
+    case PGF_EPI_DGELU: {
+      const float zz = ldv(e.aux, e.aux_dtype, m * e.ld_aux + n);
+      v *= d_bf16 ? gelu_prime_bf(zz) : gelu_prime_f(zz);
       break;
+    }
     case PGF_EPI_DRELU:
       v *= ldv(e.aux, e.aux_dtype, m * e.ld_aux + n) > 0.f ? 1.f : 0.f;
       break;
@@ -73,6 +89,12 @@ __device__ __forceinline__ void epi_store(const pgf_epilogue& e, void* D, int d_
   const int64_t o = m * ldd + n;
   if (e.accumulate) v += reinterpret_cast<float*>(D)[o];
   stv(D, d_bf16, o, v);
+}
+
+// Epilogue applied to one accumulator element.
+__device__ __forceinline__ void epi_store(const pgf_epilogue& e, void* D, int d_bf16, int64_t ldd,
+                                          int64_t m, int64_t n, float acc) {
+  epi_store_biased(e, D, d_bf16, ldd, m, n, acc, e.bias ? e.bias[n] : 0.f);
 }
 
 }  // namespace pgf

@@ -1,6 +1,6 @@
 // tcgen05 / TMEM dense product for bf16 operands on sm_100a.
 //
-// Persistent, warp-specialised kernel, one CTA per SM, 192 threads:
+// Persistent, warp-specialised kernel, one CTA per SM, 320 threads:
 //   * warp 0 (one lane): TMA producer.  Operand tiles arrive 128B-swizzled through a TC_STAGES-deep
 //     mbarrier ring.  A K-major operand is one box {64 k, 128 rows}; an MN-major operand (stored
 //     transposed) is two boxes {64 rows, 64 k} side by side, so no operand is ever transposed in
@@ -8,8 +8,8 @@
 //   * warp 1 (one lane): issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32, M=128, N=128, K=16)
 //     into one of two TMEM accumulators (2 x 128 columns), frees smem stages with tcgen05.commit
 //     on their "empty" barriers and hands finished accumulators to the epilogue.
-//   * warps 2..5: epilogue.  Warp w reads TMEM lanes 32*(w%4).. (tile rows) with tcgen05.ld while
-//     the MMA warp already fills the other accumulator.  Modes:
+//   * warps 2..9: epilogue.  Warp w reads TMEM lanes 32*(w%4).. (tile rows) of one 64-column half
+//     with tcgen05.ld while the MMA warp already fills the other accumulator.  Modes:
 //       GENERIC  - 32x32 transposes through shared memory, then the shared epilogue (bias, GELU /
 //                  GELU', addend, accumulate) with coalesced row stores;
 //       CE_FWD   - online log-sum-exp of each row over the CTA's vocabulary range plus the target
@@ -30,11 +30,11 @@ namespace pgf {
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64;
 constexpr int TC_STAGES = 4;
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 320;  // TMA warp, MMA warp, 8 epilogue warps
 constexpr int TILE_A_BYTES = TC_BM * TC_BK * 2;
 constexpr int TILE_B_BYTES = TC_BN * TC_BK * 2;
 constexpr int STAGE_BYTES = TILE_A_BYTES + TILE_B_BYTES;
-constexpr int EPI_BYTES = 4 * 32 * 33 * 4;  // one 32x33 float transpose buffer per epilogue warp
+constexpr int EPI_BYTES = 8 * 32 * 33 * 4;  // one 32x33 float transpose buffer per epilogue warp
 constexpr uint32_t TMEM_COLS = 256;        // two 128-column fp32 accumulators
 constexpr size_t TC_SMEM = size_t(TC_STAGES) * STAGE_BYTES + EPI_BYTES + 256 /* barriers */ + 1024 /* align */;
 constexpr long long WAIT_CYCLES = 4000000000ll;  // about 2 s at the B200 clock
@@ -166,7 +166,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], 8);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
@@ -255,8 +255,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
   } else {
-    // ---- epilogue warps 2..5; TMEM lane quarter q = warp % 4
+    // ---- epilogue warps 2..9: TMEM lane quarter q = warp % 4 (rows 32q..32q+31), column half
+    //      hf = (warp - 2) / 4 (columns 64hf..64hf+63 of the 128-column tile)
     const int q = warp & 3;
+    const int hf = (warp - 2) >> 2;
     float* tb = epi_buf + (warp - 2) * 32 * 33;
     uint32_t tt = 0;
     bool ok = true;
@@ -278,22 +280,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int64_t n0 = int64_t(nt) * TC_BN;
 #pragma unroll 1
-        for (int c = 0; c < TC_BN / 32; ++c) {
+        for (int c = 2 * hf; c < 2 * hf + 2; ++c) {
           uint32_t r[32];
           tmem_ld32(tmem + buf * TC_BN + (uint32_t(q * 32) << 16) + uint32_t(c * 32), r);
           const int64_t nc = n0 + c * 32;
           if (p.mode == TC_CE_FWD) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (nc + j < p.N) mx = fmaxf(mx, __uint_as_float(r[j]));
-            if (mx > -INFINITY) {
-              const float m1 = fmaxf(run_m, mx);
-              float s = 0.f;
+            // online log-sum-exp in base 2: exp(v - m) = exp2(v log2e - m log2e)
+            constexpr float L2E = 1.4426950408889634f;
+            if (nc + 32 > p.N) {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (nc + j < p.N) s += expf(__uint_as_float(r[j]) - m1);
-              run_s = run_s * expf(run_m - m1) + s;
+                if (nc + j >= p.N) r[j] = __float_as_uint(-INFINITY);
+            }
+            float mx = __uint_as_float(r[0]);
+#pragma unroll
+            for (int j = 1; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
+            if (mx > -INFINITY) {
+              const float m1 = fmaxf(run_m, mx);
+              const float ml = m1 * L2E;
+              float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) {
+                s0 += exp2f(fmaf(__uint_as_float(r[j]), L2E, -ml));
+                s1 += exp2f(fmaf(__uint_as_float(r[j + 1]), L2E, -ml));
+              }
+              run_s = run_s * exp2f((run_m - m1) * L2E) + (s0 + s1);
               run_m = m1;
             }
             if (tgt >= nc && tgt < nc + 32) {
@@ -306,9 +317,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             continue;
           }
           if (p.mode == TC_CE_BWD) {
+            constexpr float L2E = 1.4426950408889634f;
+            const float ll = row_lse * L2E;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              float g = expf(__uint_as_float(r[j]) - row_lse);
+              float g = exp2f(fmaf(__uint_as_float(r[j]), L2E, -ll));
               if (tgt == nc + j) g -= 1.0f;
               r[j] = __float_as_uint(g * p.scale);
             }
@@ -318,13 +331,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           for (int j = 0; j < 32; ++j) tb[lane * 33 + j] = __uint_as_float(r[j]);
           __syncwarp();
           const int64_t n = nc + lane;
-#pragma unroll 4
-          for (int rr = 0; rr < 32; ++rr) {
-            const int64_t m = int64_t(mb) * TC_BM + q * 32 + rr;
-            if (m < p.M && n < p.N) {
-              const float v = tb[rr * 33 + lane];
-              if (p.mode == TC_GENERIC) epi_store(p.epi, p.D, p.d_bf16, p.ldd, m, n, v);
-              else reinterpret_cast<__nv_bfloat16*>(p.D)[m * p.ldd + n] = __float2bfloat16_rn(v);
+          const bool n_ok = n < p.N;
+          const int64_t mbase = int64_t(mb) * TC_BM + q * 32;
+          if (p.mode == TC_GENERIC) {
+            const float bias_n = (p.epi.bias && n_ok) ? p.epi.bias[n] : 0.f;
+#pragma unroll 8
+            for (int rr = 0; rr < 32; ++rr) {
+              const int64_t m = mbase + rr;
+              if (m < p.M && n_ok) epi_store_biased(p.epi, p.D, p.d_bf16, p.ldd, m, n, tb[rr * 33 + lane], bias_n);
+            }
+          } else {
+            __nv_bfloat16* G = reinterpret_cast<__nv_bfloat16*>(p.D);
+#pragma unroll 8
+            for (int rr = 0; rr < 32; ++rr) {
+              const int64_t m = mbase + rr;
+              if (m < p.M && n_ok) G[m * p.ldd + n] = __float2bfloat16_rn(tb[rr * 33 + lane]);
             }
           }
           __syncwarp();
@@ -334,8 +355,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (lane == 0) mbar_arrive(&tempty[buf]);
       }
       if (p.mode == TC_CE_FWD && row_ok && ok) {
-        p.part_m[row * p.n_groups + ng] = run_m;
-        p.part_s[row * p.n_groups + ng] = run_s;
+        p.part_m[row * (2 * p.n_groups) + 2 * ng + hf] = run_m;
+        p.part_s[row * (2 * p.n_groups) + 2 * ng + hf] = run_s;
       }
     }
   }
@@ -458,7 +479,7 @@ int tc_ce_fwd(const Gemm& g, int ng, const int64_t* targets, float* part_m, floa
   p.targets = targets;
   p.part_m = part_m; p.part_s = part_s; p.tgt_logit = tgt_logit;
   const int64_t n_tiles = (g.N + TC_BN - 1) / TC_BN;
-  *n_groups_out = int((n_tiles + ng - 1) / ng);
+  *n_groups_out = 2 * int((n_tiles + ng - 1) / ng);  // two column halves per unit
   return launch_tc(g, p, s, PROF_CE);
 }
 

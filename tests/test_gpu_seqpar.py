@@ -1,0 +1,81 @@
+"""Sequence sharding over NCCL on 2 GPUs against the single-GPU step on the whole sequence.
+
+Runs only where two GPUs are visible (skipped otherwise).  The ranks are child processes with a
+short process-group timeout; NVLS is off.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tests.conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+V, D_MODEL, D_FF, N_LAYERS, B, L = 512, 64, 128, 2, 1, 4096
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _model(dev):
+    from icml_b200.lm import PGFLanguageModel
+    torch.manual_seed(5)
+    m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 256, "cpu")
+    with torch.no_grad():
+        m.emb_weight.normal_(0, 0.5)
+        m.lm_head_weight.normal_(0, 0.3)
+    m.emb_weight.data = m.emb_weight.data.to(dev)
+    m.lm_head_weight.data = m.lm_head_weight.data.to(dev)
+    m.backbone.to(dev)
+    return m
+
+
+def _data():
+    g = torch.Generator().manual_seed(6)
+    return torch.randint(0, V, (B, L), generator=g), torch.randint(0, V, (B, L), generator=g)
+
+
+def _worker(rank, world, port, out_path):
+    import datetime
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from icml_b200 import seqpar
+        dev = torch.device("cuda", rank)
+        m = _model(dev)
+        ids, tg = _data()
+        seg = L // world
+        sl = slice(rank * seg, (rank + 1) * seg)
+        loss, grads = seqpar.lm_forward_backward(m, ids[:, sl].contiguous().to(dev), tg[:, sl].contiguous().to(dev),
+                                                 seqpar.SeqGroup.from_default())
+        torch.cuda.synchronize()
+        if rank == 0:
+            torch.save({"loss": loss.cpu(), "grads": {k: v.cpu() for k, v in grads.items()}}, out_path)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_sequence_sharding_matches_one_gpu(tmp_path):
+    out = str(tmp_path / "r0.pt")
+    mp.start_processes(_worker, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    got = torch.load(out, weights_only=False)
+    m = _model(torch.device("cuda", 0))
+    ids, tg = _data()
+    loss, ref = m.forward_backward(ids.cuda(), tg.cuda())
+    assert abs(got["loss"].item() - loss.item()) < 1e-5
+    for k, v in ref.items():
+        v = v.cpu()
+        err = (got["grads"][k] - v).abs().max().item()
+        assert err <= 1e-5 + 1e-4 * v.abs().max().item(), (k, err)
