@@ -66,6 +66,10 @@ SIGNATURES = {
                             c_size_t, P]),
     "pgf_ssm_bwd": (c_int, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, I64, I64,
                             I64, I64, c_int, c_int, P, c_size_t, P]),
+    "pgf_ssm_saved_size": (c_size_t, [I64, I64, I64, I64]),
+    "pgf_ssm_fwd_save": (c_int, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P, c_size_t, P]),
+    "pgf_ssm_bwd_saved": (c_int, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, I64, I64,
+                                  I64, I64, c_int, c_int, P, c_size_t, P]),
     "pgf_ssm_summary": (c_int, [P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, P, c_size_t, P]),
     "pgf_ssm_bwd_summary": (c_int, [P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P,
                                     c_size_t, P]),

@@ -52,6 +52,9 @@ struct SsmArgs {
   float* gstack; float* gu_scan; float* dbc_part;
   __nv_bfloat16* gstack_bf;  // bf16 copy of gstack (bf16 runs), operand of the tensor-core GEMMs
   float* partA; float* partD; float* partS;
+  // states at the start of every ST-token sub-chunk, (Bsz, nC, Tc/ST, D, N): written by the output
+  // pass when ckpt_write, read by the main backward kernel instead of its own forward pass
+  float* ckpt_g; int ckpt_write;
 };
 
 // One staged sub-chunk: ST tokens x DC channels (+ the token's B and C rows).
@@ -244,16 +247,17 @@ __global__ void ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_fi
   const int64_t cs = a.D, hs = a.D * NST;
   float H = a.h_init ? a.h_init[(b * a.D + d) * NST + n] : 0.f;
   hC[0] = H;
+  constexpr int PF = 16;  // chunks whose inputs are loaded ahead of the dependent chain
   int64_t c = 0;
-  for (; c + 4 <= a.nC; c += 4) {
-    float sd[4], hl[4];
+  for (; c + PF <= a.nC; c += PF) {
+    float sd[PF], hl[PF];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < PF; ++q) {
       sd[q] = sdt[(c + q) * cs];
       hl[q] = hloc[(c + q) * hs];
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < PF; ++q) {
       H = exp2f(A2 * sd[q]) * H + hl[q];
       hC[(c + q + 1) * hs] = H;
     }
@@ -286,8 +290,14 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
   pref_load(a, l, l.s, false, r);
   pref_store(r, l, false, stg[0]);
   __syncthreads();
+  const int KS = int((a.Tc + ST - 1) / ST);
   for (int k = 0; k < nsub; ++k) {
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    if (a.ckpt_write && l.ch) {
+      float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.D + l.d) * NST + l.nq * NS;
+#pragma unroll
+      for (int j = 0; j < NS; ++j) cp[j] = h[j];
+    }
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
@@ -389,17 +399,18 @@ __global__ void ssm_compose_bwd_kernel(const SsmArgs a, const float* __restrict_
   const int64_t cs = a.D, hs = a.D * NST;
   float G = dh_end ? dh_end[o] : 0.f;
   float aE = dA_end ? dA_end[o] : 1.f;
+  constexpr int PF = 16;
   int64_t c = a.nC - 1;
-  for (; c >= 3; c -= 4) {
-    float s2[4], d0[4], dl[4];
+  for (; c >= PF - 1; c -= PF) {
+    float s2[PF], d0[PF], dl[PF];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < PF; ++q) {
       s2[q] = sdt2[(c - q) * cs];
       d0[q] = dt0[(c - q) * cs];
       dl[q] = dloc[(c - q) * hs];
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < PF; ++q) {
       const float x = aE * G;
       X[(c - q) * hs] = x;
       G = exp2f(A2 * s2[q]) * x + dl[q];
@@ -429,8 +440,9 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const int KS = int((a.Tc + ST - 1) / ST);
+  const bool saved = a.ckpt_g != nullptr;  // checkpoints come from the forward output pass
   float* ckpt = sm;
-  float* red = ckpt + size_t(KS) * SSM_THREADS * NS;
+  float* red = ckpt + (saved ? size_t(0) : size_t(KS) * SSM_THREADS * NS);
   float* gbuf = red + ST * SSM_WARPS * 32;  // [2][ST][DC]
   const int lane = l.tid & 31, warp = l.tid >> 5;
   const AConst K = load_A(a, l.nq);
@@ -446,10 +458,12 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
   }
   // ---- pass 1: forward through the chunk, checkpoint at the start of every sub-chunk
   Pref r;
+  if (!saved) {
   pref_load(a, l, l.s, false, r);
   pref_store(r, l, false, stg[0]);
   __syncthreads();
-  for (int k = 0; k < nsub; ++k) {
+  }
+  for (int k = 0; k < (saved ? 0 : nsub); ++k) {
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
 #pragma unroll
     for (int j = 0; j < NS; ++j) ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j] = h[j];
@@ -474,8 +488,14 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
     float* gb = gbuf + (k & 1) * (2 * ST * DC);
     // re-run the sub-chunk into registers: tr[i] = state before token i, ex[i] = exp(dt_i A)
     float tr[ST + 1][NS], ex[ST][NS];
+    if (saved) {
+      const float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.D + l.d) * NST + l.nq * NS;
 #pragma unroll
-    for (int j = 0; j < NS; ++j) tr[0][j] = ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j];
+      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? cp[j] : 0.f;
+    } else {
+#pragma unroll
+      for (int j = 0; j < NS; ++j) tr[0][j] = ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j];
+    }
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
 #pragma unroll
@@ -708,15 +728,23 @@ static size_t ssm_ws(const SsmPlan& p, int dtype, int backward, int act) {
   return b + 4096;
 }
 
+// Floats of the saved-state buffer: boundary states, then the sub-chunk checkpoints.
+static size_t saved_hc_floats(const SsmPlan& p) { return size_t(p.Bsz) * (p.nC + 1) * p.D * NST; }
+static size_t saved_floats(const SsmPlan& p) {
+  const size_t KS = size_t((p.Tc + ST - 1) / ST);
+  return saved_hc_floats(p) + size_t(p.Bsz) * p.nC * KS * p.D * NST;
+}
+
 static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u, int dtype,
-                      const float* W_cat, const float* b_cat, const void** wcat_op, cudaStream_t s) {
+                      const float* W_cat, const float* b_cat, const void** wcat_op, cudaStream_t s,
+                      float* hC_ext = nullptr) {
   const size_t BL = size_t(p.Bsz) * p.L;
   a.Bsz = p.Bsz; a.L = p.L; a.D = p.D; a.P = p.P; a.Tc = p.Tc; a.nC = p.nC; a.G = p.G;
   a.u = u; a.u_bf16 = dtype;
   float* proj = W.take<float>(BL * p.P);
   a.hloc = W.take<float>(size_t(p.Bsz) * p.nC * p.D * NST);
   a.sdt = W.take<float>(size_t(p.Bsz) * p.nC * p.D);
-  a.hC = W.take<float>(size_t(p.Bsz) * (p.nC + 1) * p.D * NST);
+  a.hC = hC_ext ? hC_ext : W.take<float>(size_t(p.Bsz) * (p.nC + 1) * p.D * NST);
   __nv_bfloat16* wb = dtype ? W.take<__nv_bfloat16>(size_t(p.P) * p.D) : nullptr;
   if (!proj || !a.hloc || !a.sdt || !a.hC || (dtype && !wb)) {
     set_error("ssm: workspace too small (%zu)", W.cap);
@@ -749,7 +777,7 @@ static int ssm_forward_states(const SsmArgs& a, const SsmPlan& p, float* h_final
   PGF_LAUNCH_CHECK();
   const int64_t nth = p.Bsz * p.D * NST;
   prof_begin(PROF_SSM_COMPOSE, s);
-  ssm_compose_fwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, h_final, sum_dt);
+  ssm_compose_fwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a, h_final, sum_dt);
   prof_end(PROF_SSM_COMPOSE, s, bytes_compose(a));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
@@ -775,11 +803,11 @@ extern "C" size_t pgf_ssm_workspace(int64_t Bsz, int64_t L, int64_t D, int64_t N
   return ssm_ws(p, dtype, backward, PGF_ACT_TANH);
 }
 
-extern "C" int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat,
-                           const float* A_log, const float* Dp, const float* scale,
-                           const float* h_init, void* y, float* h_final, int64_t Bsz, int64_t L,
-                           int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
-                           pgf_stream_t stream) {
+namespace pgf {
+static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                        const float* Dp, const float* scale, const float* h_init, void* y,
+                        float* h_final, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act,
+                        int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream, float* saved) {
   PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
   PGF_CHECK_ARG(u && W_cat && b_cat && A_log && Dp && scale && y, "ssm_fwd: null pointer");
   cudaStream_t s = as_stream(stream);
@@ -795,10 +823,14 @@ extern "C" int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat
   SsmArgs a = {};
   a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act; a.h_init = h_init;
   const void* wop;
-  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved));
   PGF_TRY(ssm_forward_states(a, p, h_final, s));
   a.y = y;
   a.y_bf16 = dtype;
+  if (saved) {
+    a.ckpt_g = saved + saved_hc_floats(p);
+    a.ckpt_write = 1;
+  }
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
   prof_begin(PROF_SSM_OUT_FWD, s);
   ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
@@ -806,14 +838,42 @@ extern "C" int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
+}  // namespace pgf
 
-extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, const float* b_cat,
+extern "C" int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat,
                            const float* A_log, const float* Dp, const float* scale,
-                           const float* h_init, const float* dh_end, const float* dA_end,
-                           float* gW_cat, float* gb_cat, float* gA_log, float* gDp, float* gscale,
-                           void* gu, float* dh_start, float* dA_start, int accumulate, int64_t Bsz,
-                           int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
-                           size_t ws_bytes, pgf_stream_t stream) {
+                           const float* h_init, void* y, float* h_final, int64_t Bsz, int64_t L,
+                           int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                           pgf_stream_t stream) {
+  return ssm_fwd_impl(u, W_cat, b_cat, A_log, Dp, scale, h_init, y, h_final, Bsz, L, D, N, act, dtype,
+                      ws, ws_bytes, stream, nullptr);
+}
+
+extern "C" size_t pgf_ssm_saved_size(int64_t Bsz, int64_t L, int64_t D, int64_t N) {
+  (void)N;
+  SsmPlan p = plan_of(Bsz < 1 ? 1 : Bsz, L < 1 ? 1 : L, D < 1 ? 1 : D);
+  return saved_floats(p) * sizeof(float);
+}
+
+extern "C" int pgf_ssm_fwd_save(const void* u, const float* W_cat, const float* b_cat,
+                                const float* A_log, const float* Dp, const float* scale,
+                                const float* h_init, void* y, float* saved, int64_t Bsz, int64_t L,
+                                int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                                pgf_stream_t stream) {
+  PGF_CHECK_ARG(saved, "ssm_fwd_save: null saved-state buffer");
+  PGF_CHECK_ARG(L > 0, "ssm_fwd_save: empty sequence");
+  return ssm_fwd_impl(u, W_cat, b_cat, A_log, Dp, scale, h_init, y, nullptr, Bsz, L, D, N, act, dtype,
+                      ws, ws_bytes, stream, saved);
+}
+
+namespace pgf {
+static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                        const float* A_log, const float* Dp, const float* scale, const float* h_init,
+                        const float* dh_end, const float* dA_end, float* gW_cat, float* gb_cat,
+                        float* gA_log, float* gDp, float* gscale, void* gu, float* dh_start,
+                        float* dA_start, int accumulate, int64_t Bsz, int64_t L, int64_t D, int64_t N,
+                        int act, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream,
+                        const float* saved) {
   PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
   PGF_CHECK_ARG(u && g && W_cat && b_cat && A_log && Dp && scale && gW_cat && gb_cat && gA_log &&
                     gDp && gscale && gu,
@@ -826,7 +886,7 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act; a.h_init = h_init;
   a.g = g; a.g_bf16 = dtype;
   const void* wop;
-  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, const_cast<float*>(saved)));
   const size_t BL = size_t(Bsz) * L;
   a.gstack = W.take<float>(BL * p.P);
   a.gstack_bf = dtype ? W.take<__nv_bfloat16>(BL * p.P) : nullptr;
@@ -847,23 +907,25 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
     set_error("ssm_bwd: workspace too small (%zu)", ws_bytes);
     return PGF_ERR_WORKSPACE;
   }
-  PGF_TRY(ssm_forward_states(a, p, nullptr, s));
+  if (!saved) PGF_TRY(ssm_forward_states(a, p, nullptr, s));
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
   if (act != PGF_ACT_NONE) {
     a.y = nullptr;
     ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);  // act'(C h) per token and channel
     PGF_LAUNCH_CHECK();
   }
+  if (saved) a.ckpt_g = const_cast<float*>(saved) + saved_hc_floats(p);
   prof_begin(PROF_SSM_CHUNK_BWD, s);
   ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
   prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   const int64_t nth = Bsz * D * NST;
-  ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start,
+  ssm_compose_bwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start,
                                                             nullptr);
   PGF_LAUNCH_CHECK();
   const int KS = int((p.Tc + ST - 1) / ST);
-  const size_t smem = (size_t(KS) * SSM_THREADS * NS + size_t(ST) * SSM_WARPS * 32 + 2 * 2 * ST * DC) * 4;
+  const size_t smem = ((saved ? size_t(0) : size_t(KS) * SSM_THREADS * NS) + size_t(ST) * SSM_WARPS * 32 +
+                       2 * 2 * ST * DC) * 4;
   PGF_CUDA(cudaFuncSetAttribute(ssm_main_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(smem)));
   prof_begin(PROF_SSM_MAIN_BWD, s);
@@ -898,6 +960,32 @@ extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, con
   gx.epi.ld_addend = D;
   PGF_TRY(run_gemm(gx, s));
   return PGF_OK;
+}
+}  // namespace pgf
+
+extern "C" int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                           const float* A_log, const float* Dp, const float* scale,
+                           const float* h_init, const float* dh_end, const float* dA_end,
+                           float* gW_cat, float* gb_cat, float* gA_log, float* gDp, float* gscale,
+                           void* gu, float* dh_start, float* dA_start, int accumulate, int64_t Bsz,
+                           int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                           size_t ws_bytes, pgf_stream_t stream) {
+  return ssm_bwd_impl(u, g, W_cat, b_cat, A_log, Dp, scale, h_init, dh_end, dA_end, gW_cat, gb_cat, gA_log,
+                      gDp, gscale, gu, dh_start, dA_start, accumulate, Bsz, L, D, N, act, dtype, ws, ws_bytes,
+                      stream, nullptr);
+}
+
+extern "C" int pgf_ssm_bwd_saved(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                                 const float* A_log, const float* Dp, const float* scale,
+                                 const float* saved, const float* dh_end, const float* dA_end,
+                                 float* gW_cat, float* gb_cat, float* gA_log, float* gDp, float* gscale,
+                                 void* gu, float* dh_start, float* dA_start, int accumulate, int64_t Bsz,
+                                 int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                                 size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(saved, "ssm_bwd_saved: null saved-state buffer");
+  return ssm_bwd_impl(u, g, W_cat, b_cat, A_log, Dp, scale, nullptr, dh_end, dA_end, gW_cat, gb_cat, gA_log,
+                      gDp, gscale, gu, dh_start, dA_start, accumulate, Bsz, L, D, N, act, dtype, ws, ws_bytes,
+                      stream, saved);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -957,7 +1045,7 @@ extern "C" int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_
   ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
   const int64_t nth = Bsz * D * NST;
-  ssm_compose_bwd_kernel<<<ceil_div(nth, 128), 128, 0, s>>>(a, nullptr, nullptr, dh_start, dA_start,
+  ssm_compose_bwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a, nullptr, nullptr, dh_start, dA_start,
                                                             sum_dt_excl);
   PGF_LAUNCH_CHECK();
   return PGF_OK;

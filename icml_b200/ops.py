@@ -270,9 +270,28 @@ def ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, want_h_fin
     return y, hf
 
 
+def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None):
+    """ssm_fwd that also returns the saved scan states (boundary states + 8-token checkpoints)
+    for ssm_bwd(..., saved=...) on the same inputs."""
+    _cuda(u, W_cat)
+    u = _c(u)
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    y = torch.empty_like(u)
+    Lb = lib()
+    saved = torch.empty(Lb.pgf_ssm_saved_size(Bsz, L_, D, N) // 4, dtype=torch.float32, device=u.device)
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 0), u.device)
+    W_cat, b_cat, A_log, Dp, scale, h_init = (_f32(t) for t in (W_cat, b_cat, A_log, Dp, scale, h_init))
+    check(Lb.pgf_ssm_fwd_save(_p(u), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp), _p(scale), _p(h_init),
+                              _p(y), _p(saved), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(),
+                              _stream()), "ssm_fwd_save")
+    return y, saved
+
+
 def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_end=None, act=None,
-            want_carry=False):
-    """All gradients of the SSM layer over [0, L) plus the carries (delta_h[0], dA[0])."""
+            want_carry=False, saved=None):
+    """All gradients of the SSM layer over [0, L) plus the carries (delta_h[0], dA[0]).  With
+    `saved` (from ssm_fwd_save on the same inputs) the forward passes are not recomputed."""
     _cuda(u, g, W_cat)
     u, g = _c(u), _c(g.to(u.dtype))
     Bsz, L_, D = u.shape
@@ -290,8 +309,9 @@ def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_e
     Lb = lib()
     ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 1), dev)
     A_log, Dp, scale, h_init, dh_end, dA_end = (_f32(t) for t in (A_log, Dp, scale, h_init, dh_end, dA_end))
-    check(Lb.pgf_ssm_bwd(_p(u), _p(g), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp),
-                         _p(scale), _p(h_init), _p(dh_end), _p(dA_end),
+    fn = Lb.pgf_ssm_bwd if saved is None else Lb.pgf_ssm_bwd_saved
+    check(fn(_p(u), _p(g), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp),
+                         _p(scale), _p(h_init if saved is None else saved), _p(dh_end), _p(dA_end),
                          _p(gW), _p(gb), _p(gA), _p(gD), _p(gS), _p(gu), _p(dh0), _p(dA0), 0,
                          Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(), _stream()), "ssm_bwd")
     return {"W_cat": gW, "b_cat": gb, "A_log": gA, "D": gD, "scale": gS, "grad_u": gu,

@@ -81,7 +81,10 @@ class PGFMambaBlock(nn.Module):
         B, L, D = x.shape
         g_out = g_out.to(x.dtype)
         xn1 = self.norm1.pgf_forward(x, block_size=self.block_size)              # :157
-        y, _ = self.mamba.ssm_forward(xn1)                                       # :163-178
+        W, b = _cat_weights(self.mamba)
+        m = self.mamba
+        # :163-178; the states it passes through are kept for the scan backward below
+        y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
         m_out = y + x
         xn2 = self.norm2.pgf_forward(m_out, block_size=self.block_size)          # :179
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
@@ -89,9 +92,9 @@ class PGFMambaBlock(nn.Module):
                           compute_input_grads=True)                              # :183-192
         n2 = self.norm2.pgf_grad(m_out, fr["grad_x"].reshape(B, L, D), compute_input_grads=True)  # :196
         g_m = n2["grad_x"] + g_out                                               # :202
-        W, b = _cat_weights(self.mamba)
-        m = self.mamba
-        r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, act=m.output_activation)  # :206-234
+        r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, act=m.output_activation,
+                        saved=saved)                                             # :206-234
+        del saved
         n1 = self.norm1.pgf_grad(x, r["grad_u"], compute_input_grads=True)       # :237-242
         d, N = self.d_model, self.d_state
         gscale = r["scale"].sum().expand(d).clone() if m.reference_scale_grad else r["scale"]

@@ -112,7 +112,7 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
     A = -torch.exp(m.A_log.detach().float())
     g_out = g_out.to(x.dtype)
     xn1 = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
-    y, _ = ops.ssm_fwd(xn1, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
+    y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
     m_out = y + x
     xn2 = ops.rmsnorm_fwd(m_out, block.norm2.weight, block.norm2.eps)
     fr = ops.ffn_bwd(xn2.reshape(-1, D), g_out.reshape(-1, D), block.W1, block.b1, block.W2,
@@ -126,7 +126,8 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
         dh_end, dA_end = compose_backward_carry(sp.all_gather(d_loc), sp.all_gather(dA0), sp.all_gather(sdx),
                                                 A, sp.rank)
     r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, h_init=h_in, dh_end=dh_end, dA_end=dA_end,
-                    act=m.output_activation)
+                    act=m.output_activation, saved=saved)
+    del saved
     gn1w, gn1x = ops.rmsnorm_bwd(x, r["grad_u"], block.norm1.weight, block.norm1.eps)
     d, N = m.d_model, m.d_state
     gscale = r["scale"].sum().expand(d).clone() if m.reference_scale_grad else r["scale"]

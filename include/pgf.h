@@ -225,6 +225,25 @@ int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, const float* b
                 int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
                 pgf_stream_t stream);
 
+/* Saved scan states: pgf_ssm_fwd_save is pgf_ssm_fwd that also writes into `saved`
+ * (pgf_ssm_saved_size bytes) the boundary state of every chunk and the state at the start of every
+ * 8-token sub-chunk; pgf_ssm_bwd_saved is pgf_ssm_bwd for the same (u, parameters, h_init) that
+ * reads them instead of recomputing its forward passes.  This is the reference's pgf_backward
+ * recompute (pgf_mamba_block.py:157-178) feeding its block loop (:211-234) without a second scan.
+ * The buffer holds (L/8 + L/Tc) * Bsz * D * N floats: O(L/8) states, not the (L, D, N) trajectory. */
+size_t pgf_ssm_saved_size(int64_t Bsz, int64_t L, int64_t D, int64_t N);
+int pgf_ssm_fwd_save(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                     const float* Dp, const float* scale, const float* h_init, void* y, float* saved,
+                     int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                     size_t ws_bytes, pgf_stream_t stream);
+int pgf_ssm_bwd_saved(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                      const float* A_log, const float* Dp, const float* scale, const float* saved,
+                      const float* dh_end, const float* dA_end, float* grad_W_cat, float* grad_b_cat,
+                      float* grad_A_log, float* grad_Dp, float* grad_scale, void* grad_u,
+                      float* dh_start, float* dA_start, int accumulate, int64_t Bsz, int64_t L,
+                      int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                      pgf_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Segment summaries for a sequence sharded across GPUs.  No single-function counterpart in the
  * reference: they are the block hand-off of pgf_mamba_block.py:86-112 (forward, `curr_h`) and

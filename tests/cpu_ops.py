@@ -45,6 +45,11 @@ def ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, want_h_fin
     return y, (h if want_h_final else None)
 
 
+def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None):
+    y, _ = ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=h_init, act=act)
+    return y, None
+
+
 def ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=None, act=None):
     p = _params(W_cat, b_cat, A_log, None, scale)
     B, L, d = u.shape
@@ -56,7 +61,7 @@ def ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=None, act=None):
 
 
 def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_end=None, act=None,
-            want_carry=False):
+            want_carry=False, saved=None):
     p = _params(W_cat, b_cat, A_log, Dp, scale)
     B, L, d = u.shape
     N = A_log.shape[0]

@@ -301,3 +301,19 @@ def test_ssm_bf16_activations(ops):
     assert rel_err(r["grad_u"], rr["grad_u"]) < BF16_RTOL
     W_ref = torch.cat([rr["dt_w"], rr["B_w"], rr["C_w"]], 0)
     assert rel_err(r["W_cat"], W_ref) < BF16_RTOL
+
+
+@pytest.mark.parametrize("Bsz,L,D,act", [(1, 4100, 256, None), (2, 333, 100, "tanh"), (1, 1, 32, None)])
+def test_ssm_saved_states_equal_recompute(ops, Bsz, L, D, act):
+    """ssm_fwd_save + ssm_bwd(saved=...) gives the same gradients as the recomputing backward."""
+    p, u, gy, h0, dh, dA = _ssm_case(Bsz, L, D, seed=50 + L)
+    W, b = _wcat(p)
+    dv = lambda t: t.to(DEV)  # noqa: E731
+    args = (dv(W), dv(b), dv(p["A_log"]), dv(p["D"]), dv(p["scale"]))
+    y1, _ = ops.ssm_fwd(dv(u), *args, h_init=dv(h0), act=act)
+    y2, saved = ops.ssm_fwd_save(dv(u), *args, h_init=dv(h0), act=act)
+    assert torch.equal(y1, y2)
+    r1 = ops.ssm_bwd(dv(u), dv(gy), *args, h_init=dv(h0), dh_end=dv(dh), dA_end=dv(dA), act=act, want_carry=True)
+    r2 = ops.ssm_bwd(dv(u), dv(gy), *args, dh_end=dv(dh), dA_end=dv(dA), act=act, want_carry=True, saved=saved)
+    for k in ("W_cat", "b_cat", "A_log", "D", "scale", "grad_u", "delta_h0", "dA0"):
+        assert_close(r2[k], r1[k].double(), name=k)
