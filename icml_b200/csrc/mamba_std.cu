@@ -1,0 +1,908 @@
+// Mamba-standard mixer (the variant of the benchmark configurations; the reference has no code for
+// it): in_proj -> causal depthwise conv1d + SiLU -> x_proj -> low-rank dt_proj -> selective scan
+// with per-channel A and input delta*B*u -> gate y*SiLU(z) -> out_proj, and its PGF backward.
+//
+// The scan kernels follow the same design as the reference-variant ones in ssm.cu (chunk
+// summaries, sequential compose, output pass; reverse summaries, compose, main backward that
+// re-runs 8-token sub-chunks into registers), with the per-token differences of this variant:
+// exp(delta A_{e,n}) with A per channel, delta*B*u instead of phi_1(dt A)*B*u, and the gate fused
+// into the output pass (forward) and into the adjoint's source term and the gate gradient
+// (backward).  Channels are the E = expand*d_model inner channels.
+#include "gemm.cuh"
+
+namespace pgf {
+namespace mstd {
+
+constexpr int NST = 16;
+constexpr int NQ = 4;
+constexpr int NS = NST / NQ;
+constexpr int DC = 64;
+constexpr int THREADS = DC * NQ;
+constexpr int WARPS = THREADS / 32;
+constexpr int ST = 8;
+constexpr int TC_MAX = 128;
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct Args {
+  int64_t Bsz, L, E, Tc, nC, G;
+  int abf;                         // activation dtype (u, z, y, g, grad z)
+  const void* u;                   // (Bsz, L, E) SiLU(conv) output
+  const float* dt; int64_t ld_dt;  // dt_raw rows (dt_proj output incl. bias), float32
+  const float* bc; int64_t ld_bc;  // [B | C] rows, float32
+  const void* zg; int64_t ld_z;    // gate z rows
+  const float* A_log;              // (E, N)
+  const float* Dp;                 // (E,)
+  float* hloc; float* sdt; float* hC;
+  float* dloc; float* sdt2; float* dt0; float* X;
+  void* y;                         // gated output (Bsz, L, E)
+  const void* g;                   // gradient of the gated output
+  float* gdt; int64_t ld_gdt;      // grad of dt_raw
+  float* gbc; int64_t ld_gbc;      // grad of [B | C]
+  void* gz; int64_t ld_gz;         // grad of z
+  float* gu;                       // grad of u, scan part (Bsz, L, E)
+  float* dbc_part;                 // (G, Bsz, L, 32)
+  float* partA;                    // (nC, Bsz, E, N)
+  float* partD;                    // (nC, Bsz, E)
+  float* ckpt_g; int ckpt_write;   // sub-chunk start states (Bsz, nC, Tc/ST, E, N)
+};
+
+struct Stage {
+  float dt[ST][DC];   // delta = softplus(dt_raw)
+  float u[ST][DC];
+  float zs[ST][DC];   // forward: SiLU(z); backward: dy = g * SiLU(z)
+  float gs[ST][DC];   // backward: g * SiLU'(z)
+  float sig[ST][DC];  // backward: sigmoid(dt_raw)
+  float4 B[ST][NQ];
+  float4 C[ST][NQ];
+};
+
+struct Pref {
+  float dtr[2], u[2], z[2], g[2];
+  float bc;
+};
+
+struct Lane {
+  int tid, dl, nq, grp;
+  int64_t c, b, d, s, e;
+  bool ch;
+};
+
+__device__ __forceinline__ Lane lane_of(const Args& a) {
+  Lane l;
+  l.tid = threadIdx.x;
+  l.dl = l.tid / NQ;
+  l.nq = l.tid % NQ;
+  l.c = blockIdx.x;
+  l.b = blockIdx.y;
+  l.grp = blockIdx.z;
+  l.d = int64_t(l.grp) * DC + l.dl;
+  l.ch = l.d < a.E;
+  l.s = l.c * a.Tc;
+  l.e = l.s + a.Tc < a.L ? l.s + a.Tc : a.L;
+  return l;
+}
+
+struct AConst {
+  float A[NS], A2[NS];
+};
+__device__ __forceinline__ AConst load_A(const Args& a, const Lane& l) {
+  AConst c;
+  const int64_t d = l.ch ? l.d : 0;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    c.A[j] = -expf(a.A_log[d * NST + l.nq * NS + j]);
+    c.A2[j] = c.A[j] * LOG2E;
+  }
+  return c;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_prime_f(float x) {
+  const float s = 1.0f / (1.0f + expf(-x));
+  return s * (1.0f + x * (1.0f - s));
+}
+
+__device__ __forceinline__ void pref_load(const Args& a, const Lane& l, int64_t s0, bool bwd, Pref& r) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    const int64_t tok = s0 + t;
+    const int64_t d = int64_t(l.grp) * DC + dl;
+    const bool v = tok < l.e && d < a.E;
+    const int64_t row = l.b * a.L + tok;
+    r.dtr[q] = v ? a.dt[row * a.ld_dt + d] : 0.f;
+    r.u[q] = v ? ldv(a.u, a.abf, row * a.E + d) : 0.f;
+    r.z[q] = v ? ldv(a.zg, a.abf, row * a.ld_z + d) : 0.f;
+    if (bwd) r.g[q] = v ? ldv(a.g, a.abf, row * a.E + d) : 0.f;
+  }
+  const int t = l.tid >> 5, j = l.tid & 31;
+  const int64_t tok = s0 + t;
+  r.bc = (t < ST && tok < l.e) ? a.bc[(l.b * a.L + tok) * a.ld_bc + j] : 0.f;
+}
+
+__device__ __forceinline__ void pref_store(const Pref& r, const Lane& l, bool bwd, Stage& st) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    st.dt[t][dl] = softplus_f(r.dtr[q]);
+    st.u[t][dl] = r.u[q];
+    if (bwd) {
+      st.zs[t][dl] = r.g[q] * silu_f(r.z[q]);
+      st.gs[t][dl] = r.g[q] * silu_prime_f(r.z[q]);
+      st.sig[t][dl] = sigmoid_f(r.dtr[q]);
+    } else {
+      st.zs[t][dl] = silu_f(r.z[q]);
+    }
+  }
+  const int t = l.tid >> 5, j = l.tid & 31;
+  if (t < ST) {
+    float* dst = j < NST ? reinterpret_cast<float*>(&st.B[t][0]) + j : reinterpret_cast<float*>(&st.C[t][0]) + (j - NST);
+    *dst = r.bc;
+  }
+}
+
+__device__ __forceinline__ void step_fwd(const Stage& st, int i, int dl, int nq, const AConst& K, float h[NS],
+                                         float e_out[NS]) {
+  const float dt = st.dt[i][dl], uu = st.u[i][dl];
+  const float4 Bq = st.B[i][nq];
+  const float Bv[NS] = {Bq.x, Bq.y, Bq.z, Bq.w};
+  const float du = dt * uu;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const float ez = exp2f(dt * K.A2[j]);
+    h[j] = ez * h[j] + du * Bv[j];
+    e_out[j] = ez;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(THREADS) chunk_fwd_kernel(const Args a) {
+  __shared__ Stage stg[2];
+  const Lane l = lane_of(a);
+  const AConst K = load_A(a, l);
+  float h[NS] = {0.f, 0.f, 0.f, 0.f}, e[NS];
+  float sdt = 0.f;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s, false, r);
+  pref_store(r, l, false, stg[0]);
+  __syncthreads();
+  for (int k = 0; k < nsub; ++k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    const Stage& S = stg[k & 1];
+#pragma unroll
+    for (int i = 0; i < ST; ++i)
+      if (l.s + int64_t(k) * ST + i < l.e) {
+        step_fwd(S, i, l.dl, l.nq, K, h, e);
+        sdt += S.dt[i][l.dl];
+      }
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
+  }
+  if (!l.ch) return;
+  const int64_t cb = l.b * a.nC + l.c;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) a.hloc[(cb * a.E + l.d) * NST + l.nq * NS + j] = h[j];
+  if (l.nq == 0) a.sdt[cb * a.E + l.d] = sdt;
+}
+
+__global__ void compose_fwd_kernel(const Args a) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= a.Bsz * a.E * NST) return;
+  const int n = int(idx % NST);
+  const int64_t d = (idx / NST) % a.E;
+  const int64_t b = idx / (NST * a.E);
+  const float A2 = -expf(a.A_log[d * NST + n]) * LOG2E;
+  const float* __restrict__ sdt = a.sdt + b * a.nC * a.E + d;
+  const float* __restrict__ hloc = a.hloc + (b * a.nC * a.E + d) * NST + n;
+  float* __restrict__ hC = a.hC + (b * (a.nC + 1) * a.E + d) * NST + n;
+  const int64_t cs = a.E, hs = a.E * NST;
+  float H = 0.f;
+  hC[0] = H;
+  constexpr int PF = 16;
+  int64_t c = 0;
+  for (; c + PF <= a.nC; c += PF) {
+    float sd[PF], hl[PF];
+#pragma unroll
+    for (int q = 0; q < PF; ++q) {
+      sd[q] = sdt[(c + q) * cs];
+      hl[q] = hloc[(c + q) * hs];
+    }
+#pragma unroll
+    for (int q = 0; q < PF; ++q) {
+      H = exp2f(A2 * sd[q]) * H + hl[q];
+      hC[(c + q + 1) * hs] = H;
+    }
+  }
+  for (; c < a.nC; ++c) {
+    H = exp2f(A2 * sdt[c * cs]) * H + hloc[c * hs];
+    hC[(c + 1) * hs] = H;
+  }
+}
+
+__global__ void __launch_bounds__(THREADS) out_fwd_kernel(const Args a) {
+  __shared__ Stage stg[2];
+  __shared__ float ybuf[2][ST][DC];
+  const Lane l = lane_of(a);
+  const AConst K = load_A(a, l);
+  float h[NS], e[NS];
+#pragma unroll
+  for (int j = 0; j < NS; ++j)
+    h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.E + l.d) * NST + l.nq * NS + j] : 0.f;
+  const float Dd = l.ch ? a.Dp[l.d] : 0.f;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  const int KS = int((a.Tc + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s, false, r);
+  pref_store(r, l, false, stg[0]);
+  __syncthreads();
+  for (int k = 0; k < nsub; ++k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    if (a.ckpt_write && l.ch) {
+      float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS;
+#pragma unroll
+      for (int j = 0; j < NS; ++j) cp[j] = h[j];
+    }
+    const Stage& S = stg[k & 1];
+#pragma unroll
+    for (int i = 0; i < ST; ++i) {
+      if (l.s + int64_t(k) * ST + i < l.e) {
+        step_fwd(S, i, l.dl, l.nq, K, h, e);
+        const float4 Cq = S.C[i][l.nq];
+        float yc = Cq.x * h[0];
+        yc = fmaf(Cq.y, h[1], yc);
+        yc = fmaf(Cq.z, h[2], yc);
+        yc = fmaf(Cq.w, h[3], yc);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 1);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 2);
+        if (l.nq == 0) ybuf[k & 1][i][l.dl] = (yc + Dd * S.u[i][l.dl]) * S.zs[i][l.dl];
+      }
+    }
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int idx = l.tid + q * THREADS;
+      const int t = idx / DC, dl = idx % DC;
+      const int64_t tok = l.s + int64_t(k) * ST + t;
+      const int64_t d = int64_t(l.grp) * DC + dl;
+      if (tok < l.e && d < a.E) stv(a.y, a.abf, (l.b * a.L + tok) * a.E + d, ybuf[k & 1][t][dl]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
+  __shared__ Stage stg[2];
+  const Lane l = lane_of(a);
+  const AConst K = load_A(a, l);
+  float dlt[NS] = {0.f, 0.f, 0.f, 0.f};
+  float anext[NS] = {1.f, 1.f, 1.f, 1.f};
+  float sdt2 = 0.f, dt_first = 0.f;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+  pref_store(r, l, true, stg[(nsub - 1) & 1]);
+  __syncthreads();
+  for (int k = nsub - 1; k >= 0; --k) {
+    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    const Stage& S = stg[k & 1];
+#pragma unroll
+    for (int i = ST - 1; i >= 0; --i) {
+      const int64_t t = l.s + int64_t(k) * ST + i;
+      if (t < l.e) {
+        const float dt = S.dt[i][l.dl];
+        const float dy = S.zs[i][l.dl];
+        const float4 Cq = S.C[i][l.nq];
+        const float Cv[NS] = {Cq.x, Cq.y, Cq.z, Cq.w};
+#pragma unroll
+        for (int j = 0; j < NS; ++j) {
+          dlt[j] = anext[j] * dlt[j] + dy * Cv[j];
+          anext[j] = exp2f(dt * K.A2[j]);
+        }
+        if (t > l.s) sdt2 += dt;
+        dt_first = dt;
+      }
+    }
+    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
+    __syncthreads();
+  }
+  if (!l.ch) return;
+  const int64_t cb = l.b * a.nC + l.c;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) a.dloc[(cb * a.E + l.d) * NST + l.nq * NS + j] = dlt[j];
+  if (l.nq == 0) {
+    a.sdt2[cb * a.E + l.d] = sdt2;
+    a.dt0[cb * a.E + l.d] = dt_first;
+  }
+}
+
+__global__ void compose_bwd_kernel(const Args a) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= a.Bsz * a.E * NST) return;
+  const int n = int(idx % NST);
+  const int64_t d = (idx / NST) % a.E;
+  const int64_t b = idx / (NST * a.E);
+  const float A2 = -expf(a.A_log[d * NST + n]) * LOG2E;
+  const float* __restrict__ sdt2 = a.sdt2 + b * a.nC * a.E + d;
+  const float* __restrict__ dt0 = a.dt0 + b * a.nC * a.E + d;
+  const float* __restrict__ dloc = a.dloc + (b * a.nC * a.E + d) * NST + n;
+  float* __restrict__ X = a.X + (b * a.nC * a.E + d) * NST + n;
+  const int64_t cs = a.E, hs = a.E * NST;
+  float G = 0.f, aE = 1.f;
+  for (int64_t c = a.nC - 1; c >= 0; --c) {
+    const float x = aE * G;
+    X[c * hs] = x;
+    G = exp2f(A2 * sdt2[c * cs]) * x + dloc[c * hs];
+    aE = exp2f(dt0[c * cs] * A2);
+  }
+}
+
+// Main backward: checkpoints from the forward output pass (ckpt_g) are required.
+// Dynamic shared memory: red [ST][WARPS][32], gbuf [2][3][ST][DC].
+__global__ void __launch_bounds__(THREADS) main_bwd_kernel(const Args a) {
+  extern __shared__ float sm[];
+  __shared__ Stage stg[2];
+  const Lane l = lane_of(a);
+  const int KS = int((a.Tc + ST - 1) / ST);
+  float* red = sm;
+  float* gbuf = red + ST * WARPS * 32;
+  const int lane = l.tid & 31, warp = l.tid >> 5;
+  const AConst K = load_A(a, l);
+  const float Dd = l.ch ? a.Dp[l.d] : 0.f;
+  const int64_t cb = l.b * a.nC + l.c;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  float carry[NS];
+#pragma unroll
+  for (int j = 0; j < NS; ++j) carry[j] = l.ch ? a.X[(cb * a.E + l.d) * NST + l.nq * NS + j] : 0.f;
+  float accA[NS] = {0.f, 0.f, 0.f, 0.f};
+  float accD = 0.f;
+  const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+  Pref r;
+  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+  pref_store(r, l, true, stg[(nsub - 1) & 1]);
+  __syncthreads();
+  for (int k = nsub - 1; k >= 0; --k) {
+    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    const Stage& S = stg[k & 1];
+    float* gb = gbuf + (k & 1) * (3 * ST * DC);
+    float tr[ST + 1][NS], ex[ST][NS];
+    {
+      const float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS;
+#pragma unroll
+      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? cp[j] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < ST; ++i) {
+#pragma unroll
+      for (int j = 0; j < NS; ++j) tr[i + 1][j] = tr[i][j];
+      if (l.s + int64_t(k) * ST + i < l.e) step_fwd(S, i, l.dl, l.nq, K, tr[i + 1], ex[i]);
+      else {
+#pragma unroll
+        for (int j = 0; j < NS; ++j) ex[i][j] = 1.f;
+      }
+    }
+#pragma unroll
+    for (int i = ST - 1; i >= 0; --i) {
+      const bool valid = l.s + int64_t(k) * ST + i < l.e;
+      float v8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float gdt = 0.f, gur = 0.f, hc = 0.f;
+      const float dt = S.dt[i][l.dl], uu = S.u[i][l.dl], dy = S.zs[i][l.dl];
+      if (valid) {
+        const float4 Bq = S.B[i][l.nq], Cq = S.C[i][l.nq];
+        const float Bv[NS] = {Bq.x, Bq.y, Bq.z, Bq.w};
+        const float Cv[NS] = {Cq.x, Cq.y, Cq.z, Cq.w};
+        const float du = dt * uu;
+#pragma unroll
+        for (int j = 0; j < NS; ++j) {
+          hc = fmaf(Cv[j], tr[i + 1][j], hc);
+          const float dlt = carry[j] + dy * Cv[j];
+          const float ez = ex[i][j];
+          const float eh = ez * tr[i][j];
+          // dh_t/d delta = A e h_{t-1} + B u ;  dh_t/dA = delta e h_{t-1}
+          gdt = fmaf(dlt, fmaf(K.A[j], eh, Bv[j] * uu), gdt);
+          accA[j] = fmaf(dlt * dt, eh, accA[j]);
+          gur = fmaf(dlt * dt, Bv[j], gur);
+          v8[j] = dlt * du;
+          v8[NS + j] = dy * tr[i + 1][j];
+          carry[j] = ez * dlt;
+        }
+      }
+      gdt += __shfl_xor_sync(0xffffffffu, gdt, 1);
+      gdt += __shfl_xor_sync(0xffffffffu, gdt, 2);
+      gur += __shfl_xor_sync(0xffffffffu, gur, 1);
+      gur += __shfl_xor_sync(0xffffffffu, gur, 2);
+      hc += __shfl_xor_sync(0xffffffffu, hc, 1);
+      hc += __shfl_xor_sync(0xffffffffu, hc, 2);
+      if (valid && l.nq == 0) {
+        gb[i * DC + l.dl] = gdt * S.sig[i][l.dl];                            // grad dt_raw
+        gb[ST * DC + i * DC + l.dl] = dy * Dd + gur;                          // grad u (scan part)
+        gb[2 * ST * DC + i * DC + l.dl] = S.gs[i][l.dl] * (hc + Dd * uu);    // grad z
+        accD = fmaf(dy, uu, accD);
+      }
+      float w4[4], w2[2];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float keep = b4 ? v8[4 + q] : v8[q];
+        const float send = b4 ? v8[q] : v8[4 + q];
+        w4[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float keep = b3 ? w4[2 + q] : w4[q];
+        const float send = b3 ? w4[q] : w4[2 + q];
+        w2[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      const float keep = b2 ? w2[1] : w2[0];
+      const float send = b2 ? w2[0] : w2[1];
+      red[(i * WARPS + warp) * 32 + lane] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
+    __syncthreads();
+    {
+      const int i = l.tid >> 5, ln = l.tid & 31;
+      const int64_t t = l.s + int64_t(k) * ST + i;
+      if (i < ST && t < l.e) {
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) sum += red[(i * WARPS + w) * 32 + ln];
+        const int vi = (ln >> 2) & 7, nqq = ln & 3;
+        const int n = nqq * NS + (vi & 3);
+        const int which = vi >> 2;
+        a.dbc_part[((int64_t(l.grp) * a.Bsz + l.b) * a.L + t) * 32 + which * NST + n] = sum;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int idx = l.tid + q * THREADS;
+      const int t = idx / DC, dl = idx % DC;
+      const int64_t tok = l.s + int64_t(k) * ST + t;
+      const int64_t d = int64_t(l.grp) * DC + dl;
+      if (tok < l.e && d < a.E) {
+        const int64_t row = l.b * a.L + tok;
+        a.gdt[row * a.ld_gdt + d] = gb[t * DC + dl];
+        a.gu[row * a.E + d] = gb[ST * DC + t * DC + dl];
+        stv(a.gz, a.abf, row * a.ld_gz + d, gb[2 * ST * DC + t * DC + dl]);
+      }
+    }
+    __syncthreads();
+  }
+  if (l.ch) {
+#pragma unroll
+    for (int j = 0; j < NS; ++j)
+      a.partA[((l.c * a.Bsz + l.b) * a.E + l.d) * NST + l.nq * NS + j] = accA[j] * K.A[j];  // d/dA_log
+    if (l.nq == 0) a.partD[(l.c * a.Bsz + l.b) * a.E + l.d] = accD;
+  }
+}
+
+__global__ void bc_reduce_kernel(const Args a) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t rows = a.Bsz * a.L;
+  if (idx >= rows * 32) return;
+  const int64_t row = idx / 32;
+  const int m = int(idx % 32);
+  float s = 0.f;
+  for (int64_t gi = 0; gi < a.G; ++gi) s += a.dbc_part[(gi * rows + row) * 32 + m];
+  a.gbc[row * a.ld_gbc + m] = s;
+}
+
+__global__ void param_reduce_kernel(const Args a, float* __restrict__ gA, float* __restrict__ gD, int accumulate) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // over E*N (+ E for D)
+  const int64_t cnt = a.nC * a.Bsz;
+  if (i < a.E * NST) {
+    float s = 0.f;
+    for (int64_t c = 0; c < cnt; ++c) s += a.partA[c * a.E * NST + i];
+    gA[i] = accumulate ? gA[i] + s : s;
+  } else if (i < a.E * NST + a.E) {
+    const int64_t d = i - a.E * NST;
+    float s = 0.f;
+    for (int64_t c = 0; c < cnt; ++c) s += a.partD[c * a.E + d];
+    gD[d] = accumulate ? gD[d] + s : s;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// causal depthwise conv1d + SiLU
+// ---------------------------------------------------------------------------------------------
+constexpr int CONV_T = 64;  // tokens per thread block row
+constexpr int KMAX = 8;
+
+// u[t, e] = SiLU(b[e] + sum_k w[e, k] xi[t - (K-1) + k, e]); xi rows have pitch ld_x.
+__global__ void conv_fwd_kernel(const void* __restrict__ xi, int64_t ld_x, const float* __restrict__ w,
+                                const float* __restrict__ bias, void* __restrict__ u, int64_t Bsz, int64_t L,
+                                int64_t E, int K, int abf) {
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t b = blockIdx.z;
+  const int64_t t0 = int64_t(blockIdx.y) * CONV_T;
+  if (e >= E) return;
+  float wk[KMAX];
+  for (int k = 0; k < K; ++k) wk[k] = w[e * K + k];
+  const float be = bias[e];
+  float win[KMAX];  // win[k] = xi[t - (K-1) + k]
+  for (int k = 0; k < K - 1; ++k) {
+    const int64_t tt = t0 - (K - 1) + k;
+    win[k] = tt >= 0 ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f;
+  }
+  const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
+  for (int64_t t = t0; t < t1; ++t) {
+    win[K - 1] = ldv(xi, abf, (b * L + t) * ld_x + e);
+    float acc = be;
+    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], win[k], acc);
+    stv(u, abf, (b * L + t) * E + e, silu_f(acc));
+    for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
+  }
+}
+
+// Backward of conv + SiLU: du (float32) -> dxc = du * SiLU'(xc); dxi[t] = sum_k w[k] dxc[t + K-1-k]
+// (written with pitch ld_dx), and per-(token block, channel) partials of grad w and grad b.
+__global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const float* __restrict__ w,
+                                const float* __restrict__ bias, const float* __restrict__ du,
+                                void* __restrict__ dxi, int64_t ld_dx, float* __restrict__ part,
+                                int64_t Bsz, int64_t L, int64_t E, int K, int abf) {
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t b = blockIdx.z;
+  const int64_t tb = blockIdx.y;
+  const int64_t t0 = tb * CONV_T;
+  if (e >= E) return;
+  float wk[KMAX];
+  for (int k = 0; k < K; ++k) wk[k] = w[e * K + k];
+  const float be = bias[e];
+  const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
+  auto xin = [&](int64_t tt) { return (tt >= 0 && tt < L) ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f; };
+  auto dxc_at = [&](int64_t tt) -> float {
+    if (tt >= L) return 0.f;
+    float acc = be;
+    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], xin(tt - (K - 1) + k), acc);
+    return du[(b * L + tt) * E + e] * silu_prime_f(acc);
+  };
+  float gw[KMAX];
+  for (int k = 0; k < K; ++k) gw[k] = 0.f;
+  float gb = 0.f;
+  float fwin[KMAX];  // fwin[j] = dxc[t + j]
+  for (int j = 0; j < K - 1; ++j) fwin[j] = dxc_at(t0 + j);
+  for (int64_t t = t0; t < t1; ++t) {
+    fwin[K - 1] = dxc_at(t + K - 1);
+    float acc = 0.f;
+    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], fwin[K - 1 - k], acc);
+    stv(dxi, abf, (b * L + t) * ld_dx + e, acc);
+    const float g0 = fwin[0];
+    gb += g0;
+    for (int k = 0; k < K; ++k) gw[k] = fmaf(g0, xin(t - (K - 1) + k), gw[k]);
+    for (int j = 0; j < K - 1; ++j) fwin[j] = fwin[j + 1];
+  }
+  const int64_t nb = (L + CONV_T - 1) / CONV_T;
+  float* pp = part + ((b * nb + tb) * E + e) * (K + 1);
+  for (int k = 0; k < K; ++k) pp[k] = gw[k];
+  pp[K] = gb;
+}
+
+__global__ void conv_param_reduce_kernel(const float* __restrict__ part, int64_t cnt, int64_t E, int K,
+                                         float* __restrict__ gw, float* __restrict__ gb, int accumulate) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // over E*(K+1)
+  if (i >= E * (K + 1)) return;
+  float s = 0.f;
+  for (int64_t c = 0; c < cnt; ++c) s += part[c * E * (K + 1) + i];
+  const int64_t e = i / (K + 1);
+  const int k = int(i % (K + 1));
+  if (k < K) gw[e * K + k] = accumulate ? gw[e * K + k] + s : s;
+  else gb[e] = accumulate ? gb[e] + s : s;
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+struct Plan {
+  int64_t Bsz, L, d, E, R, N, K, Tc, nC, G, XD, T;
+};
+
+static Plan plan_of(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K) {
+  Plan p;
+  p.Bsz = Bsz; p.L = L; p.d = d; p.E = E; p.R = R; p.N = N; p.K = K;
+  p.G = (E + DC - 1) / DC;
+  int64_t tc = TC_MAX;
+  while (tc > 32 && ((L + tc - 1) / tc) * Bsz * p.G < 4 * 148) tc /= 2;
+  p.Tc = tc;
+  p.nC = (L + tc - 1) / tc;
+  p.XD = R + 2 * N;
+  p.T = Bsz * L;
+  return p;
+}
+
+struct Bufs {
+  void *xz, *u, *y, *gy, *dxz;
+  float *xdbl, *dtr, *dxdbl, *ddtr, *gu, *gu_tot;
+  float *hloc, *sdt, *hC, *ckpt, *dloc, *sdt2, *dt0, *X, *dbc, *partA, *partD, *cpart;
+  __nv_bfloat16 *in_wb, *out_wb;
+  void* cs;
+  size_t cs_bytes;
+};
+
+static size_t bufs_bytes(const Plan& p, int dtype, int bwd) {
+  const size_t es = dtype ? 2 : 4, T = size_t(p.T), E = size_t(p.E);
+  const size_t KS = size_t((p.Tc + ST - 1) / ST);
+  size_t b = 0;
+  auto add = [&](size_t n) { b += Workspace::round(n); };
+  add(T * 2 * E * es);            // xz
+  add(T * E * es);                // u
+  add(T * E * es);                // y
+  add(T * p.XD * 4);              // xdbl
+  add(T * E * 4);                 // dtr
+  add(size_t(p.Bsz) * p.nC * E * NST * 4);         // hloc
+  add(size_t(p.Bsz) * p.nC * E * 4);               // sdt
+  add(size_t(p.Bsz) * (p.nC + 1) * E * NST * 4);   // hC
+  add(size_t(p.Bsz) * p.nC * KS * E * NST * 4);    // ckpt
+  if (dtype) { add(size_t(2 * E) * p.d * 2); add(size_t(p.d) * E * 2); }
+  if (bwd) {
+    add(T * E * es);              // gy
+    add(T * 2 * E * es);          // dxz
+    add(T * p.XD * 4);            // dxdbl
+    add(T * E * 4);               // ddtr
+    add(T * E * 4);               // gu
+    add(T * E * 4);               // gu_tot
+    add(size_t(p.Bsz) * p.nC * E * NST * 4 * 2);   // dloc, X
+    add(size_t(p.Bsz) * p.nC * E * 4 * 2);         // sdt2, dt0
+    add(size_t(p.G) * T * 32 * 4);                 // dbc
+    add(size_t(p.nC) * p.Bsz * E * NST * 4);       // partA
+    add(size_t(p.nC) * p.Bsz * E * 4);             // partD
+    add(size_t(p.Bsz) * ((p.L + CONV_T - 1) / CONV_T) * E * (p.K + 1) * 4);  // conv partials
+    size_t c1 = colsum_ws(int64_t(T), E);
+    add(c1);
+  }
+  return b + 8192;
+}
+
+static int carve(Workspace& W, Bufs& B, const Plan& p, int dtype, int bwd) {
+  const size_t es = dtype ? 2 : 4, T = size_t(p.T), E = size_t(p.E);
+  const size_t KS = size_t((p.Tc + ST - 1) / ST);
+  B = Bufs{};
+  B.xz = W.take<char>(T * 2 * E * es);
+  B.u = W.take<char>(T * E * es);
+  B.y = W.take<char>(T * E * es);
+  B.xdbl = W.take<float>(T * p.XD);
+  B.dtr = W.take<float>(T * E);
+  B.hloc = W.take<float>(size_t(p.Bsz) * p.nC * E * NST);
+  B.sdt = W.take<float>(size_t(p.Bsz) * p.nC * E);
+  B.hC = W.take<float>(size_t(p.Bsz) * (p.nC + 1) * E * NST);
+  B.ckpt = W.take<float>(size_t(p.Bsz) * p.nC * KS * E * NST);
+  bool ok = B.xz && B.u && B.y && B.xdbl && B.dtr && B.hloc && B.sdt && B.hC && B.ckpt;
+  if (dtype) {
+    B.in_wb = W.take<__nv_bfloat16>(size_t(2 * E) * p.d);
+    B.out_wb = W.take<__nv_bfloat16>(size_t(p.d) * E);
+    ok = ok && B.in_wb && B.out_wb;
+  }
+  if (bwd) {
+    B.gy = W.take<char>(T * E * es);
+    B.dxz = W.take<char>(T * 2 * E * es);
+    B.dxdbl = W.take<float>(T * p.XD);
+    B.ddtr = W.take<float>(T * E);
+    B.gu = W.take<float>(T * E);
+    B.gu_tot = W.take<float>(T * E);
+    B.dloc = W.take<float>(size_t(p.Bsz) * p.nC * E * NST);
+    B.X = W.take<float>(size_t(p.Bsz) * p.nC * E * NST);
+    B.sdt2 = W.take<float>(size_t(p.Bsz) * p.nC * E);
+    B.dt0 = W.take<float>(size_t(p.Bsz) * p.nC * E);
+    B.dbc = W.take<float>(size_t(p.G) * T * 32);
+    B.partA = W.take<float>(size_t(p.nC) * p.Bsz * E * NST);
+    B.partD = W.take<float>(size_t(p.nC) * p.Bsz * E);
+    B.cpart = W.take<float>(size_t(p.Bsz) * ((p.L + CONV_T - 1) / CONV_T) * E * (p.K + 1));
+    B.cs_bytes = colsum_ws(int64_t(T), E);
+    B.cs = W.take<char>(B.cs_bytes);
+    ok = ok && B.gy && B.dxz && B.dxdbl && B.ddtr && B.gu && B.gu_tot && B.dloc && B.X && B.sdt2 && B.dt0 &&
+         B.dbc && B.partA && B.partD && B.cpart && B.cs;
+  }
+  if (!ok) {
+    set_error("mamba mixer: workspace too small (%zu)", W.cap);
+    return PGF_ERR_WORKSPACE;
+  }
+  return PGF_OK;
+}
+
+static Gemm G_(int64_t M, int64_t N, int64_t K, const void* A, int abf, int64_t lda, int at, const void* Bm,
+               int bbf, int64_t ldb, int bt, void* D, int dbf, int64_t ldd) {
+  Gemm g;
+  g.M = M; g.N = N; g.K = K;
+  g.A = A; g.a_bf16 = abf; g.lda = lda; g.a_trans = at;
+  g.B = Bm; g.b_bf16 = bbf; g.ldb = ldb; g.b_trans = bt;
+  g.D = D; g.d_bf16 = dbf; g.ldd = ldd;
+  g.epi = epi_default();
+  return g;
+}
+
+struct Params {
+  const float *in_w, *conv_w, *conv_b, *x_w, *dt_w, *dt_b, *A_log, *Dp, *out_w;
+};
+
+// forward up to the gated scan output y (B.y); optionally saves the states for the backward
+static int forward_to_y(const void* x, const Params& P, const Plan& p, Bufs& B, int dtype, bool save,
+                        Args& a, cudaStream_t s) {
+  const int64_t T = p.T, E = p.E;
+  const void* in_w = P.in_w;
+  if (dtype) {
+    PGF_TRY(to_bf16(P.in_w, B.in_wb, 2 * E * p.d, s));
+    in_w = B.in_wb;
+  }
+  // xz = x W_in^T
+  PGF_TRY(run_gemm(G_(T, 2 * E, p.d, x, dtype, p.d, 0, in_w, dtype, p.d, 0, B.xz, dtype, 2 * E), s));
+  // u = SiLU(conv(xi))
+  {
+    dim3 grid(ceil_div(E, 128), ceil_div(p.L, CONV_T), unsigned(p.Bsz));
+    conv_fwd_kernel<<<grid, 128, 0, s>>>(B.xz, 2 * E, P.conv_w, P.conv_b, B.u, p.Bsz, p.L, E, int(p.K), dtype);
+    PGF_LAUNCH_CHECK();
+  }
+  // x_dbl = u W_x^T (float32), dt_raw = x_dbl[:, :R] W_dt^T + b_dt
+  PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, dtype, E, 0, P.x_w, 0, E, 0, B.xdbl, 0, p.XD), s));
+  {
+    Gemm g = G_(T, E, p.R, B.xdbl, 0, p.XD, 0, P.dt_w, 0, p.R, 0, B.dtr, 0, E);
+    g.epi.bias = P.dt_b;
+    PGF_TRY(run_gemm(g, s));
+  }
+  a = Args{};
+  a.Bsz = p.Bsz; a.L = p.L; a.E = E; a.Tc = p.Tc; a.nC = p.nC; a.G = p.G; a.abf = dtype;
+  a.u = B.u;
+  a.dt = B.dtr; a.ld_dt = E;
+  a.bc = B.xdbl + p.R; a.ld_bc = p.XD;
+  a.zg = static_cast<const char*>(B.xz) + E * (dtype ? 2 : 4); a.ld_z = 2 * E;
+  a.A_log = P.A_log; a.Dp = P.Dp;
+  a.hloc = B.hloc; a.sdt = B.sdt; a.hC = B.hC;
+  a.y = B.y;
+  a.ckpt_g = B.ckpt; a.ckpt_write = save ? 1 : 0;
+  dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  prof_begin(PROF_SSM_CHUNK_FWD, s);
+  chunk_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_CHUNK_FWD, s, double(T) * (dtype ? 2 : 4) * (2.0 * E + NST));
+  PGF_LAUNCH_CHECK();
+  const int64_t nth = p.Bsz * E * NST;
+  compose_fwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  prof_begin(PROF_SSM_OUT_FWD, s);
+  out_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_OUT_FWD, s, double(T) * (dtype ? 2 : 4) * (4.0 * E + 2 * NST));
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+static int check_dims(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype) {
+  PGF_CHECK_ARG(N == NST, "mamba mixer: d_state must be %d", NST);
+  PGF_CHECK_ARG(Bsz > 0 && Bsz <= 65535 && L > 0 && d > 0 && E > 0 && R > 0, "mamba mixer: bad shape");
+  PGF_CHECK_ARG(K >= 1 && K <= KMAX, "mamba mixer: d_conv must be in [1, %d]", KMAX);
+  PGF_CHECK_ARG(dtype == 0 || dtype == 1, "mamba mixer: bad dtype");
+  return PGF_OK;
+}
+
+}  // namespace mstd
+}  // namespace pgf
+
+using namespace pgf;
+
+extern "C" size_t pgf_mamba_mixer_workspace(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                                            int64_t K, int dtype, int backward) {
+  mstd::Plan p = mstd::plan_of(Bsz < 1 ? 1 : Bsz, L < 1 ? 1 : L, d, E, R, N, K);
+  return mstd::bufs_bytes(p, dtype, backward);
+}
+
+extern "C" int pgf_mamba_mixer_fwd(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                                   const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                                   const float* Dp, const float* out_w, void* out, int64_t Bsz, int64_t L,
+                                   int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws,
+                                   size_t ws_bytes, pgf_stream_t stream) {
+  PGF_TRY(mstd::check_dims(Bsz, L, d, E, R, N, K, dtype));
+  PGF_CHECK_ARG(x && in_w && conv_w && conv_b && x_w && dt_w && dt_b && A_log && Dp && out_w && out,
+                "mamba_mixer_fwd: null pointer");
+  cudaStream_t s = as_stream(stream);
+  mstd::Plan p = mstd::plan_of(Bsz, L, d, E, R, N, K);
+  Workspace W(ws, ws_bytes);
+  mstd::Bufs B;
+  PGF_TRY(mstd::carve(W, B, p, dtype, 0));
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Args a;
+  PGF_TRY(mstd::forward_to_y(x, P, p, B, dtype, false, a, s));
+  const void* ow = out_w;
+  if (dtype) {
+    PGF_TRY(to_bf16(out_w, B.out_wb, d * E, s));
+    ow = B.out_wb;
+  }
+  return run_gemm(mstd::G_(p.T, d, E, B.y, dtype, E, 0, ow, dtype, E, 0, out, dtype, d), s);
+}
+
+extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                                   const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
+                                   const float* A_log, const float* Dp, const float* out_w, float* g_in_w,
+                                   float* g_conv_w, float* g_conv_b, float* g_x_w, float* g_dt_w, float* g_dt_b,
+                                   float* g_A_log, float* g_Dp, float* g_out_w, void* g_x, int accumulate,
+                                   int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K,
+                                   int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_TRY(mstd::check_dims(Bsz, L, d, E, R, N, K, dtype));
+  PGF_CHECK_ARG(x && g_out && in_w && conv_w && conv_b && x_w && dt_w && dt_b && A_log && Dp && out_w && g_in_w &&
+                    g_conv_w && g_conv_b && g_x_w && g_dt_w && g_dt_b && g_A_log && g_Dp && g_out_w && g_x,
+                "mamba_mixer_bwd: null pointer");
+  cudaStream_t s = as_stream(stream);
+  mstd::Plan p = mstd::plan_of(Bsz, L, d, E, R, N, K);
+  Workspace W(ws, ws_bytes);
+  mstd::Bufs B;
+  PGF_TRY(mstd::carve(W, B, p, dtype, 1));
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Args a;
+  PGF_TRY(mstd::forward_to_y(x, P, p, B, dtype, true, a, s));
+  const int64_t T = p.T;
+  const size_t es = dtype ? 2 : 4;
+  const void* ow = out_w;
+  if (dtype) {
+    PGF_TRY(to_bf16(out_w, B.out_wb, d * E, s));
+    ow = B.out_wb;
+  }
+  // out_proj: grad W_out (+)= g^T y ; gy = g W_out
+  {
+    Gemm g = mstd::G_(d, E, T, g_out, dtype, d, 1, B.y, dtype, E, 1, g_out_w, 0, E);
+    g.epi.accumulate = accumulate;
+    PGF_TRY(run_gemm(g, s));
+    PGF_TRY(run_gemm(mstd::G_(T, E, d, g_out, dtype, d, 0, ow, dtype, E, 1, B.gy, dtype, E), s));
+  }
+  // scan backward
+  a.g = B.gy;
+  a.gdt = B.ddtr; a.ld_gdt = E;
+  a.gbc = B.dxdbl + R; a.ld_gbc = p.XD;
+  a.gz = static_cast<char*>(B.dxz) + E * es; a.ld_gz = 2 * E;
+  a.gu = B.gu;
+  a.dbc_part = B.dbc;
+  a.partA = B.partA; a.partD = B.partD;
+  a.dloc = B.dloc; a.sdt2 = B.sdt2; a.dt0 = B.dt0; a.X = B.X;
+  a.ckpt_write = 0;
+  dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  mstd::chunk_bwd_kernel<<<grid, mstd::THREADS, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  const int64_t nth = p.Bsz * E * mstd::NST;
+  mstd::compose_bwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  const size_t smem = size_t(mstd::ST * mstd::WARPS * 32 + 2 * 3 * mstd::ST * mstd::DC) * 4;
+  prof_begin(PROF_SSM_MAIN_BWD, s);
+  mstd::main_bwd_kernel<<<grid, mstd::THREADS, smem, s>>>(a);
+  prof_end(PROF_SSM_MAIN_BWD, s, double(T) * es * (7.0 * E + 2 * mstd::NST) + double(T) * 8 * mstd::NST);
+  PGF_LAUNCH_CHECK();
+  mstd::bc_reduce_kernel<<<ceil_div(T * 32, 256), 256, 0, s>>>(a);
+  PGF_LAUNCH_CHECK();
+  mstd::param_reduce_kernel<<<ceil_div(E * mstd::NST + E, 256), 256, 0, s>>>(a, g_A_log, g_Dp, accumulate);
+  PGF_LAUNCH_CHECK();
+  // dt_proj: grad b_dt = colsum(ddtr); grad W_dt (+)= ddtr^T x_dbl[:, :R]; dxdbl[:, :R] = ddtr W_dt
+  PGF_TRY(colsum(B.ddtr, 0, T, E, E, g_dt_b, accumulate, B.cs, B.cs_bytes, s));
+  {
+    Gemm g = mstd::G_(E, R, T, B.ddtr, 0, E, 1, B.xdbl, 0, p.XD, 1, g_dt_w, 0, R);
+    g.epi.accumulate = accumulate;
+    PGF_TRY(run_gemm(g, s));
+    PGF_TRY(run_gemm(mstd::G_(T, R, E, B.ddtr, 0, E, 0, dt_w, 0, R, 1, B.dxdbl, 0, p.XD), s));
+  }
+  // x_proj: grad W_x (+)= dxdbl^T u ; du_total = dxdbl W_x + gu
+  {
+    Gemm g = mstd::G_(p.XD, E, T, B.dxdbl, 0, p.XD, 1, B.u, dtype, E, 1, g_x_w, 0, E);
+    g.epi.accumulate = accumulate;
+    PGF_TRY(run_gemm(g, s));
+    Gemm g2 = mstd::G_(T, E, p.XD, B.dxdbl, 0, p.XD, 0, x_w, 0, E, 1, B.gu_tot, 0, E);
+    g2.epi.addend = B.gu; g2.epi.addend_dtype = 0; g2.epi.ld_addend = E;
+    PGF_TRY(run_gemm(g2, s));
+  }
+  // conv + SiLU backward -> dxz[:, :E]
+  {
+    dim3 cg(ceil_div(E, 128), ceil_div(p.L, mstd::CONV_T), unsigned(p.Bsz));
+    mstd::conv_bwd_kernel<<<cg, 128, 0, s>>>(B.xz, 2 * E, conv_w, conv_b, B.gu_tot, B.dxz, 2 * E, B.cpart,
+                                             p.Bsz, p.L, E, int(K), dtype);
+    PGF_LAUNCH_CHECK();
+    const int64_t cnt = p.Bsz * ((p.L + mstd::CONV_T - 1) / mstd::CONV_T);
+    mstd::conv_param_reduce_kernel<<<ceil_div(E * (K + 1), 256), 256, 0, s>>>(B.cpart, cnt, E, int(K), g_conv_w,
+                                                                             g_conv_b, accumulate);
+    PGF_LAUNCH_CHECK();
+  }
+  // in_proj: grad W_in (+)= dxz^T x ; grad x = dxz W_in
+  {
+    Gemm g = mstd::G_(2 * E, d, T, B.dxz, dtype, 2 * E, 1, x, dtype, d, 1, g_in_w, 0, d);
+    g.epi.accumulate = accumulate;
+    PGF_TRY(run_gemm(g, s));
+    const void* iw = dtype ? (const void*)B.in_wb : (const void*)in_w;
+    PGF_TRY(run_gemm(mstd::G_(T, d, 2 * E, B.dxz, dtype, 2 * E, 0, iw, dtype, d, 1, g_x, dtype, d), s));
+  }
+  return PGF_OK;
+}

@@ -17,12 +17,17 @@ import torch.nn as nn
 
 from . import ops
 from .pgf_mamba_block import PGFMambaBlock, PGFMambaSequential
+from .pgf_rmsnorm import RMSNorm
 
 
 class PGFLanguageModel:
     def __init__(self, vocab_size: int, d_model: int, d_state: int, d_ff: int, n_layers: int,
                  block_size: int, device, act_dtype=torch.float32, lr: float = 1e-3,
-                 weight_decay: float = 0.01, tie_embeddings: bool = False, init_std: float = 0.02):
+                 weight_decay: float = 0.01, tie_embeddings: bool = False, init_std: float = 0.02,
+                 variant: str = "reference", final_norm: bool = False, expand: int = 2, d_conv: int = 4,
+                 dt_rank: Optional[int] = None):
+        """variant "reference": the reference's PGFMambaBlock; "std": the Mamba-standard block
+        (pgf_mamba_std.PGFMambaStdBlock).  final_norm adds an RMSNorm before the LM head."""
         self.vocab_size = vocab_size
         self.d_model = d_model
         self.block_size = block_size
@@ -33,10 +38,19 @@ class PGFLanguageModel:
         self.tied = tie_embeddings
         self.lm_head_weight = (self.emb_weight if tie_embeddings else
                                nn.Parameter(torch.randn(vocab_size, d_model, device=device) * init_std))
-        blocks = [PGFMambaBlock(d_model, d_state, d_ff, block_size) for _ in range(n_layers)]
+        if variant == "reference":
+            blocks = [PGFMambaBlock(d_model, d_state, d_ff, block_size) for _ in range(n_layers)]
+        elif variant == "std":
+            from .pgf_mamba_std import PGFMambaStdBlock
+            blocks = [PGFMambaStdBlock(d_model, d_state, d_ff, block_size, expand, d_conv, dt_rank)
+                      for _ in range(n_layers)]
+        else:
+            raise ValueError(variant)
+        self.variant = variant
         self.backbone = PGFMambaSequential(blocks).to(device)
+        self.final_norm = RMSNorm(d_model).to(device) if final_norm else None
         self.params = [self.emb_weight] + ([] if tie_embeddings else [self.lm_head_weight]) + \
-            list(self.backbone.parameters())
+            list(self.backbone.parameters()) + (list(self.final_norm.parameters()) if final_norm else [])
         self.optimizer = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay,
                                            fused=self.device.type == "cuda")
 
@@ -58,14 +72,18 @@ class PGFLanguageModel:
         for layer in self.backbone.layers:
             stash.append(x)
             x = layer.pgf_forward(x)
-        h = x.reshape(-1, d)
+        xf = ops.rmsnorm_fwd(x, self.final_norm.weight, self.final_norm.eps) if self.final_norm is not None else x
+        h = xf.reshape(-1, d)
         tg = targets.reshape(-1)
         loss_rows, lse = ops.lm_head_ce_fwd(h, self.lm_head_weight, tg)
         loss = loss_rows.mean()
         gW, gh = ops.lm_head_ce_bwd(h, self.lm_head_weight, tg, lse, 1.0 / h.shape[0])
         grads = {"lm_head": gW}
         g = gh.reshape(B, L, d)
-        del x, h, gh
+        if self.final_norm is not None:
+            gfw, g = ops.rmsnorm_bwd(x, g, self.final_norm.weight, self.final_norm.eps)
+            grads["final_norm"] = gfw
+        del x, xf, h, gh
         for i in reversed(range(self.n_layers)):
             res = self.backbone.layers[i].pgf_backward(stash.pop(), g)
             for k, v in res["grads"].items():
@@ -81,6 +99,8 @@ class PGFLanguageModel:
         self.emb_weight.grad = grads["emb"]
         if not self.tied:
             self.lm_head_weight.grad = grads["lm_head"]
+        if self.final_norm is not None:
+            self.final_norm.weight.grad = grads["final_norm"]
         for i, layer in enumerate(self.backbone.layers):
             for name, p in layer.named_parameters():
                 p.grad = grads[f"layers.{i}.{name}"]

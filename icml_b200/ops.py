@@ -351,3 +351,45 @@ def ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=None, act=None):
                                  _p(dh0), _p(dA0), _p(sdx), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws),
                                  ws.numel(), _stream()), "ssm_bwd_summary")
     return dh0, dA0, sdx
+
+
+# --------------------------------------------------------------------------- Mamba-standard mixer
+MIXER_KEYS = ("in_w", "conv_w", "conv_b", "x_w", "dt_w", "dt_b", "A_log", "D", "out_w")
+
+
+def _mixer_dims(x, p):
+    Bsz, L_, d = x.shape
+    E, N = p["A_log"].shape
+    R = p["dt_w"].shape[1]
+    K = p["conv_w"].shape[1]
+    return Bsz, L_, d, E, R, N, K
+
+
+def mamba_mixer_fwd(x, p):
+    """Standard Mamba mixer forward; p: dict of MIXER_KEYS float32 tensors."""
+    _cuda(x, p["in_w"])
+    x = _c(x)
+    Bsz, L_, d, E, R, N, K = _mixer_dims(x, p)
+    q = {k: _f32(p[k]) for k in MIXER_KEYS}
+    out = torch.empty_like(x)
+    Lb = lib()
+    ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 0), x.device)
+    check(Lb.pgf_mamba_mixer_fwd(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(out), Bsz, L_, d, E, R, N, K,
+                                 _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_fwd")
+    return out
+
+
+def mamba_mixer_bwd(x, g, p):
+    """(grads dict over MIXER_KEYS, grad_x) of the standard Mamba mixer."""
+    _cuda(x, g, p["in_w"])
+    x, g = _c(x), _c(g.to(x.dtype))
+    Bsz, L_, d, E, R, N, K = _mixer_dims(x, p)
+    q = {k: _f32(p[k]) for k in MIXER_KEYS}
+    grads = {k: torch.empty_like(q[k]) for k in MIXER_KEYS}
+    gx = torch.empty_like(x)
+    Lb = lib()
+    ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 1), x.device)
+    check(Lb.pgf_mamba_mixer_bwd(_p(x), _p(g), *[_p(q[k]) for k in MIXER_KEYS],
+                                 *[_p(grads[k]) for k in MIXER_KEYS], _p(gx), 0, Bsz, L_, d, E, R, N, K,
+                                 _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_bwd")
+    return grads, gx

@@ -267,6 +267,33 @@ int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_cat, const 
                         int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
                         pgf_stream_t stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Mamba-standard mixer: the variant the benchmark configurations describe; the reference has no
+ * code for it (its SSM, train_singlemamba_optimized.py:88-124, has no in/out projection, conv or
+ * gate).  x (Bsz, L, d) -> out (Bsz, L, d):
+ *   xz = x in_w^T (in_w: 2E x d); xi, z = xz[:, :E], xz[:, E:]
+ *   u = SiLU(causal depthwise conv1d(xi; conv_w (E, K), conv_b (E)))
+ *   [dt_low | B | C] = u x_w^T (x_w: R+2N x E); delta = softplus(dt_low dt_w^T + dt_b) (dt_w: E x R)
+ *   h_t = exp(delta_t A) h_{t-1} + delta_t B_t u_t, A = -exp(A_log) (E x N)
+ *   y = (C_t . h_t + Dp u_t) * SiLU(z);  out = y out_w^T (out_w: d x E)
+ * The backward re-runs the forward (keeping 8-token scan checkpoints) and returns every
+ * parameter gradient and grad x.  N must be 16, K <= 8.  Zero initial state and conv history.
+ * ------------------------------------------------------------------------------------------ */
+size_t pgf_mamba_mixer_workspace(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                                 int64_t K, int dtype, int backward);
+int pgf_mamba_mixer_fwd(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                        const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                        const float* Dp, const float* out_w, void* out, int64_t Bsz, int64_t L,
+                        int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws,
+                        size_t ws_bytes, pgf_stream_t stream);
+int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                        const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
+                        const float* A_log, const float* Dp, const float* out_w, float* g_in_w,
+                        float* g_conv_w, float* g_conv_b, float* g_x_w, float* g_dt_w, float* g_dt_b,
+                        float* g_A_log, float* g_Dp, float* g_out_w, void* g_x, int accumulate,
+                        int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K,
+                        int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

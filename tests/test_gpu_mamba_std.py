@@ -1,0 +1,118 @@
+"""Mamba-standard variant (BASELINE config 1 shapes) on the GPU against autograd of the float64 oracle.
+
+The reference has no code for this variant, so the truth is autograd of the CPU restatement in
+oracle/mamba_std.py (the comparison config 1 asks for: "every parameter/input gradient of the PGF
+path against plain autograd").
+"""
+import pytest
+import torch
+
+from oracle import mamba_std as MS
+from tests.parity import BF16_RTOL, assert_close, rel_err
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+NAMES = {"in_w": "mixer.in_proj.weight", "conv_w": "mixer.conv1d.weight", "conv_b": "mixer.conv1d.bias",
+         "x_w": "mixer.x_proj.weight", "dt_w": "mixer.dt_proj.weight", "dt_b": "mixer.dt_proj.bias",
+         "A_log": "mixer.A_log", "D": "mixer.D", "out_w": "mixer.out_proj.weight"}
+
+
+def _block_module(bp, d, d_ff, expand, K, R):
+    from icml_b200.pgf_mamba_std import PGFMambaStdBlock
+    blk = PGFMambaStdBlock(d, 16, d_ff, 128, expand, K, R)
+    sd = {}
+    for k, v in bp.items():
+        if k.startswith("mixer."):
+            name = NAMES[k[6:]]
+            sd[name] = v.float().reshape(blk.state_dict()[name].shape)
+        else:
+            sd[k] = v.float()
+    blk.load_state_dict(sd)
+    return blk.to(DEV)
+
+
+def _case(seed, B, L, d, E, R, K=4, d_ff=None):
+    g = torch.Generator().manual_seed(seed)
+    bp = MS.block_init(d, 16, d_ff or 2 * d, E // d, K, R, g)
+    bp["norm1.weight"] = 1 + 0.05 * torch.randn(d, generator=g, dtype=torch.float64)
+    bp["mixer.D"] = 1 + 0.2 * torch.randn(E, generator=g, dtype=torch.float64)
+    x = torch.randn(B, L, d, generator=g, dtype=torch.float64)
+    gy = torch.randn(B, L, d, generator=g, dtype=torch.float64)
+    return bp, x, gy
+
+
+@pytest.mark.parametrize("B,L,d,E,R", [(2, 512, 128, 256, 8), (1, 100, 64, 128, 4), (3, 37, 32, 64, 2)])
+def test_std_block_pgf_backward_matches_autograd(B, L, d, E, R):
+    bp, x, gy = _case(60 + L, B, L, d, E, R)
+    blk = _block_module(bp, d, 2 * d, E // d, 4, R)
+    y_ref, g_ref, gx_ref = MS.block_grads(bp, x, gy)
+    y = blk.pgf_forward(x.float().to(DEV))
+    assert_close(y, y_ref, name="pgf_forward")
+    r = blk.pgf_backward(x.float().to(DEV), gy.float().to(DEV))
+    assert_close(r["grad_input"], gx_ref, name="grad_input")
+    for k, v in g_ref.items():
+        name = NAMES[k[6:]] if k.startswith("mixer.") else k
+        got = r["grads"][name].reshape(v.shape)
+        assert_close(got, v, name=name)
+
+
+def test_std_block_autograd_forward():
+    bp, x, gy = _case(70, 2, 64, 32, 64, 2)
+    blk = _block_module(bp, 32, 64, 2, 4, 2)
+    xx = x.float().to(DEV).requires_grad_(True)
+    y = blk(xx)
+    y.backward(gy.float().to(DEV))
+    y_ref, g_ref, gx_ref = MS.block_grads(bp, x, gy)
+    assert_close(y, y_ref)
+    assert_close(xx.grad, gx_ref)
+    named = dict(blk.named_parameters())
+    for k, v in g_ref.items():
+        name = NAMES[k[6:]] if k.startswith("mixer.") else k
+        assert_close(named[name].grad.reshape(v.shape), v, name=name)
+
+
+def test_std_block_bf16_activations():
+    bp, x, gy = _case(71, 1, 2048, 256, 512, 16)
+    blk = _block_module(bp, 256, 1024, 2, 4, 16)
+    xb, gb = x.bfloat16(), gy.bfloat16()
+    r = blk.pgf_backward(xb.to(DEV), gb.to(DEV))
+    _, g_ref, gx_ref = MS.block_grads(bp, xb.double(), gb.double())
+    assert rel_err(r["grad_input"], gx_ref) < BF16_RTOL
+    for k in ("mixer.in_w", "mixer.x_w", "mixer.A_log", "mixer.conv_w", "W1"):
+        name = NAMES[k[6:]] if k.startswith("mixer.") else k
+        assert rel_err(r["grads"][name].reshape(g_ref[k].shape), g_ref[k]) < BF16_RTOL, name
+
+
+def test_std_lm_step_matches_autograd():
+    """8-layer shape family at small size: tied embedding / LM head and a final RMSNorm (config 3 layout)."""
+    from icml_b200.lm import PGFLanguageModel
+    g = torch.Generator().manual_seed(72)
+    V, d, E, R, nl, B, L = 97, 32, 64, 2, 2, 2, 40
+    blocks = [MS.block_init(d, 16, 4 * d, 2, 4, R, g) for _ in range(nl)]
+    emb = 0.5 * torch.randn(V, d, generator=g, dtype=torch.float64)
+    fnw = 1 + 0.1 * torch.randn(d, generator=g, dtype=torch.float64)
+    ids = torch.randint(0, V, (B, L), generator=g)
+    tg = torch.randint(0, V, (B, L), generator=g)
+    lm = PGFLanguageModel(V, d, 16, 4 * d, nl, 16, DEV, variant="std", tie_embeddings=True, final_norm=True,
+                          expand=2, d_conv=4, dt_rank=R)
+    with torch.no_grad():
+        lm.emb_weight.copy_(emb.float())
+        lm.final_norm.weight.copy_(fnw.float())
+        for i, layer in enumerate(lm.backbone.layers):
+            sd = {}
+            for k, v in blocks[i].items():
+                name = NAMES[k[6:]] if k.startswith("mixer.") else k
+                sd[name] = v.float().reshape(layer.state_dict()[name].shape)
+            layer.load_state_dict(sd)
+    loss, grads = lm.forward_backward(ids.to(DEV), tg.to(DEV))
+    rloss, rgrads = MS.lm_grads(emb, None, fnw, blocks, ids, tg)
+    assert abs(loss.item() - rloss.item()) < 1e-5
+    assert_close(grads["emb"], rgrads["emb"], name="emb (tied)")
+    assert_close(grads["final_norm"], rgrads["final_norm"], name="final_norm")
+    for i in range(nl):
+        for k, v in rgrads.items():
+            if not k.startswith(f"layers.{i}."):
+                continue
+            kk = k.split(".", 2)[2]
+            name = NAMES[kk[6:]] if kk.startswith("mixer.") else kk
+            assert_close(grads[f"layers.{i}.{name}"].reshape(v.shape), v, name=f"{i}.{name}")
