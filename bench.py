@@ -49,6 +49,13 @@ def parse():
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--cpu-sample-len", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--variant", default="reference", choices=["reference", "std"],
+                    help="reference: the reference's SSM block (d_inner = d_model); std: the Mamba-standard "
+                         "block of the benchmark configurations (expand 2, d_conv 4, dt_rank 16, final "
+                         "RMSNorm, tied LM head)")
+    ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "all"],
+                    help="component microbenchmarks instead of the LM step (RMSNorm [8,4096,1024]; FFN "
+                         "1024-4096-1024 on 32768 tokens; LM head + CE d=1024, vocab 50257, 32768 tokens)")
     ap.add_argument("--parallel", default="sp", choices=["sp", "dp"],
                     help="N>1: sp = one sequence of N x seq-len tokens sharded across the GPUs "
                          "(state hand-off between segments), dp = N independent sequences")
@@ -56,13 +63,18 @@ def parse():
 
 
 def config_of(a, world):
+    var = ("reference SSM variant" if a.variant == "reference" else
+           "Mamba-standard variant (d_inner 512, d_conv 4, dt_rank 16, final RMSNorm, tied head)")
     return {
-        "workload": f"8-layer PGF Mamba LM, d_model {a.d_model}, d_state 16, d_ff {a.d_ff}, vocab {a.vocab}, "
-                    f"B={a.batch} x L={a.seq_len} tokens per GPU, bf16 activations / fp32 weights + AdamW",
+        "workload": f"8-layer PGF Mamba LM ({var}), d_model {a.d_model}, d_state 16, d_ff {a.d_ff}, "
+                    f"vocab {a.vocab}, B={a.batch} x L={a.seq_len} tokens per GPU, {a.dtype} activations / "
+                    f"fp32 weights + AdamW",
         "layers": a.layers, "d_model": a.d_model, "d_state": 16, "d_ff": a.d_ff, "vocab": a.vocab,
         "global_batch": a.batch * (world if a.parallel == "dp" else 1),
         "seq_len": a.seq_len * (world if a.parallel == "sp" else 1), "pgf_block_size": a.block_size,
-        "parallelism": f"{a.parallel}{world}", "ssm_variant": "reference (d_inner = d_model, shared A)",
+        "parallelism": f"{a.parallel}{world}",
+        "ssm_variant": ("reference (d_inner = d_model, shared A)" if a.variant == "reference" else
+                        "mamba-standard (d_inner 2 d_model, conv1d, gate, per-channel A)"),
         "l2": "per-step working set (weights, optimizer state, activations) > 126 MB L2; no explicit flush",
     }
 
@@ -194,7 +206,76 @@ def main():
     if a.impl == "reference":
         run_reference(a, rank, world)
         return
+    if a.component:
+        run_components(a)
+        return
     run_gpu(a, rank, world, local_rank)
+
+
+def _time(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_components(a):
+    """Component microbenchmarks: one JSON line each (rates against MEASURED_PEAKS.json)."""
+    from icml_b200 import ops
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm, tf = peaks.get("hbm_gbs", 6650.0), peaks.get("bf16_tflops", 1590.0)
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cpu").manual_seed(0)
+    which = ["rmsnorm", "ffn", "lmhead"] if a.component == "all" else [a.component]
+    for dt_name, dt in (("bf16", torch.bfloat16), ("fp32", torch.float32)):
+        if "rmsnorm" in which:
+            x = torch.randn(8, 4096, 1024, generator=g).to(dev, dt)
+            gy = torch.randn(8, 4096, 1024, generator=g).to(dev, dt)
+            w = (1 + 0.02 * torch.randn(1024, generator=g)).to(dev)
+            ms = _time(lambda: (ops.rmsnorm_fwd(x, w, 1e-5), ops.rmsnorm_bwd(x, gy, w, 1e-5)), a.steps, a.warmup)
+            by = 8 * 4096 * 1024 * x.element_size() * 5  # read x twice, g; write y, dx
+            print(json.dumps({"metric": "RMSNorm fwd+bwd [8,4096,1024] eps 1e-5", "value": by / ms / 1e6,
+                              "unit": "GB/s", "dtype": dt_name, "ms": ms,
+                              "roofline": {"bound": "hbm", "achieved": by / ms / 1e6, "peak": hbm,
+                                           "frac": by / ms / 1e6 / hbm}}), flush=True)
+        if "ffn" in which:
+            T, d, dh = 32768, 1024, 4096
+            x = torch.randn(T, d, generator=g).to(dev, dt)
+            gy = torch.randn(T, d, generator=g).to(dev, dt)
+            W1 = (0.02 * torch.randn(dh, d, generator=g)).to(dev)
+            W2 = (0.02 * torch.randn(d, dh, generator=g)).to(dev)
+            b1, b2 = torch.zeros(dh, device=dev), torch.zeros(d, device=dev)
+            ms = _time(lambda: (ops.ffn_fwd(x, W1, b1, W2, b2), ops.ffn_bwd(x, gy, W1, b1, W2)), a.steps, a.warmup)
+            fl = 8 * 2.0 * T * d * dh  # fwd 2 + backward 6 (incl. the recomputed forward)
+            print(json.dumps({"metric": "FFN 1024-4096-1024 fwd+bwd, 32768 tokens", "value": fl / ms / 1e9,
+                              "unit": "TFLOP/s", "dtype": dt_name, "ms": ms,
+                              "roofline": {"bound": "tensor", "achieved": fl / ms / 1e9, "peak": tf,
+                                           "frac": fl / ms / 1e9 / tf}}), flush=True)
+        if "lmhead" in which:
+            T, d, V = 32768, 1024, 50257
+            h = torch.randn(T, d, generator=g).to(dev, dt)
+            W = (0.02 * torch.randn(V, d, generator=g)).to(dev)
+            tg = torch.randint(0, V, (T,), generator=g).to(dev)
+
+            def step():
+                _, lse = ops.lm_head_ce_fwd(h, W, tg)
+                ops.lm_head_ce_bwd(h, W, tg, lse, 1.0 / T)
+            ms = _time(step, max(1, a.steps // 3), max(1, a.warmup // 2))
+            fl = 4 * 2.0 * T * V * d  # forward, recomputed logits, dW, dh
+            print(json.dumps({"metric": "LM head + CE fwd+bwd, d 1024, vocab 50257, 32768 tokens",
+                              "value": fl / ms / 1e9, "unit": "TFLOP/s", "dtype": dt_name, "ms": ms,
+                              "roofline": {"bound": "tensor", "achieved": fl / ms / 1e9, "peak": tf,
+                                           "frac": fl / ms / 1e9 / tf}}), flush=True)
 
 
 def zipf_ids(n, vocab, seed, s=1.1):
@@ -226,7 +307,12 @@ def run_gpu(a, rank, world, local_rank):
     L = _lib.lib()
     act = torch.bfloat16 if a.dtype == "bf16" else torch.float32
     torch.manual_seed(1234)
-    model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act)
+    if a.variant == "std":
+        model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act,
+                                 variant="std", tie_embeddings=True, final_norm=True, expand=2, d_conv=4,
+                                 dt_rank=16)
+    else:
+        model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act)
     for p in model.params:  # identical replicas
         if pg is not None:
             torch.distributed.broadcast(p.data, 0)

@@ -72,7 +72,7 @@ def test_std_block_autograd_forward():
 
 
 def test_std_block_bf16_activations():
-    bp, x, gy = _case(71, 1, 2048, 256, 512, 16)
+    bp, x, gy = _case(71, 1, 2048, 256, 512, 16, d_ff=1024)
     blk = _block_module(bp, 256, 1024, 2, 4, 16)
     xb, gb = x.bfloat16(), gy.bfloat16()
     r = blk.pgf_backward(xb.to(DEV), gb.to(DEV))
