@@ -48,6 +48,9 @@ SIGNATURES = {
     "pgf_embedding_bwd": (c_int, [P, P, P, c_int, I64, I64, I64, c_int, P, c_size_t, P]),
     "pgf_gemm": (c_int, [I64, I64, I64, P, c_int, I64, c_int, P, c_int, I64, c_int, P, c_int, I64,
                          ctypes.POINTER(Epilogue), P]),
+    "pgf_gemm_workspace": (c_size_t, [I64, I64, I64]),
+    "pgf_gemm_ex": (c_int, [I64, I64, I64, P, c_int, I64, c_int, P, c_int, I64, c_int, P, c_int, I64,
+                            ctypes.POINTER(Epilogue), P, c_size_t, P]),
     "pgf_colsum_workspace": (c_size_t, [I64, I64]),
     "pgf_colsum": (c_int, [P, c_int, I64, I64, I64, P, c_int, P, c_size_t, P]),
     "pgf_ffn_workspace": (c_size_t, [I64, I64, I64, I64, c_int, c_int]),

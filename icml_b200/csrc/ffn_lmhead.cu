@@ -27,7 +27,14 @@ struct FfnWs {
   __nv_bfloat16 *W1b, *W2b;  // bf16 operand copies
   void* cs;     // colsum scratch
   size_t cs_bytes;
+  void* split;  // split-K partials of the weight gradients
+  size_t split_bytes;
 };
+
+static size_t ffn_split_bytes(int64_t tr, int64_t d_in, int64_t d_h, int64_t d_out) {
+  const size_t a = gemm_split_ws(d_out, d_h, tr), b = gemm_split_ws(d_h, d_in, tr);
+  return a > b ? a : b;
+}
 
 static size_t ffn_ws_bytes(int64_t rows, int64_t d_in, int64_t d_h, int64_t d_out, int dtype, int backward) {
   int64_t tr = ffn_tile_rows(rows < 1 ? 1 : rows, d_h, backward);
@@ -38,6 +45,7 @@ static size_t ffn_ws_bytes(int64_t rows, int64_t d_in, int64_t d_h, int64_t d_ou
   if (backward) {
     size_t c1 = colsum_ws(tr, d_h), c2 = colsum_ws(tr, d_out);
     b += Workspace::round(c1 > c2 ? c1 : c2);
+    b += Workspace::round(ffn_split_bytes(tr, d_in, d_h, d_out));
   }
   return b + 1024;
 }
@@ -54,11 +62,15 @@ static int ffn_carve(Workspace& W, FfnWs& f, int64_t rows, int64_t d_in, int64_t
     size_t c1 = colsum_ws(tr, d_h), c2 = colsum_ws(tr, d_out);
     f.cs_bytes = c1 > c2 ? c1 : c2;
     f.cs = W.take<char>(f.cs_bytes);
+    f.split_bytes = ffn_split_bytes(tr, d_in, d_h, d_out);
+    f.split = f.split_bytes ? W.take<char>(f.split_bytes) : nullptr;
   } else {
     f.cs = nullptr;
     f.cs_bytes = 0;
+    f.split = nullptr;
+    f.split_bytes = 0;
   }
-  if (!f.h || (backward && (!f.z || !f.cs)) || (dtype && (!f.W1b || !f.W2b))) {
+  if (!f.h || (backward && (!f.z || !f.cs || (f.split_bytes && !f.split))) || (dtype && (!f.W1b || !f.W2b))) {
     set_error("ffn: workspace too small (%zu)", W.cap);
     return PGF_ERR_WORKSPACE;
   }
@@ -72,13 +84,7 @@ static int act_epi(int activation, int backward) {
 
 static Gemm mk(int64_t M, int64_t N, int64_t K, const void* A, int abf, int64_t lda, int at,
                const void* B, int bbf, int64_t ldb, int bt, void* D, int dbf, int64_t ldd) {
-  Gemm g;
-  g.M = M; g.N = N; g.K = K;
-  g.A = A; g.a_bf16 = abf; g.lda = lda; g.a_trans = at;
-  g.B = B; g.b_bf16 = bbf; g.ldb = ldb; g.b_trans = bt;
-  g.D = D; g.d_bf16 = dbf; g.ldd = ldd;
-  g.epi = epi_default();
-  return g;
+  return gemm_make(M, N, K, A, abf, lda, at, B, bbf, ldb, bt, D, dbf, ldd);
 }
 
 }  // namespace pgf
@@ -176,6 +182,7 @@ extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const 
     // grad_W2 (+)= g^T h   (d_out x d_h, K = rows)
     Gemm g2 = mk(d_out, d_h, m, gt, dtype, d_out, 1, f.h, dtype, d_h, 1, gW2, 0, d_h);
     g2.epi.accumulate = acc;
+    g2.ws = f.split; g2.ws_bytes = f.split_bytes;
     PGF_TRY(run_gemm(g2, s));
     PGF_TRY(colsum(gt, dtype, m, d_out, d_out, gb2, acc, f.cs, f.cs_bytes, s));
     // grad_z = (g W2) * act'(z), written over h (no longer needed)
@@ -188,6 +195,7 @@ extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const 
     // grad_W1 (+)= grad_z^T x   (d_h x d_in, K = rows)
     Gemm g4 = mk(d_h, d_in, m, f.h, dtype, d_h, 1, xt, dtype, d_in, 1, gW1, 0, d_in);
     g4.epi.accumulate = acc;
+    g4.ws = f.split; g4.ws_bytes = f.split_bytes;
     PGF_TRY(run_gemm(g4, s));
     PGF_TRY(colsum(f.h, dtype, m, d_h, d_h, gb1, acc, f.cs, f.cs_bytes, s));
     if (gx) {

@@ -10,6 +10,10 @@ struct Gemm {
   const void* B; int b_bf16; int64_t ldb; int b_trans;
   void* D; int d_bf16; int64_t ldd;
   pgf_epilogue epi;
+  // Optional scratch for split-K (>= gemm_split_ws(M, N, K) bytes).  When the output has too few
+  // tiles to fill the GPU, K is cut into slices whose float32 partial products land here and are
+  // summed in slice order (deterministic) by the epilogue pass; without it the product is not split.
+  void* ws; size_t ws_bytes;
 };
 
 static inline pgf_epilogue epi_default() {
@@ -22,8 +26,29 @@ static inline pgf_epilogue epi_default() {
   return e;
 }
 
+static inline Gemm gemm_make(int64_t M, int64_t N, int64_t K, const void* A, int abf, int64_t lda, int at,
+                             const void* B, int bbf, int64_t ldb, int bt, void* D, int dbf, int64_t ldd) {
+  Gemm g;
+  g.M = M; g.N = N; g.K = K;
+  g.A = A; g.a_bf16 = abf; g.lda = lda; g.a_trans = at;
+  g.B = B; g.b_bf16 = bbf; g.ldb = ldb; g.b_trans = bt;
+  g.D = D; g.d_bf16 = dbf; g.ldd = ldd;
+  g.epi = epi_default();
+  g.ws = nullptr; g.ws_bytes = 0;
+  return g;
+}
+
 // D = epi(opA * opB^T); picks the tensor-core path when the operands allow it.
 int run_gemm(const Gemm& g, cudaStream_t s);
+// Split-K scratch bytes run_gemm may use for an (M x N, depth K) product on either engine.
+size_t gemm_split_ws(int64_t M, int64_t N, int64_t K);
+// Number of K slices each engine uses for the product (1 = no split).
+int split_slices_tc(int64_t M, int64_t N, int64_t K);
+int sm_count();  // streaming multiprocessors of the current device (cached)
+int split_slices_simt(int64_t M, int64_t N, int64_t K);
+// Engine entry points for one split: slice z covers k-range [z*kchunk, (z+1)*kchunk) and writes its
+// float32 partial to part + z*M*N (row pitch N).  They return the number of slices launched.
+int run_gemm_tc_split(const Gemm& g, int slices, float* part, int* launched, cudaStream_t s);
 // SIMT path (any dtype mix, any layout): the float32 reference-precision engine.
 int run_gemm_simt(const Gemm& g, cudaStream_t s);
 // tcgen05 path; returns PGF_ERR_UNSUPPORTED when the call does not fit it.

@@ -10,7 +10,9 @@ namespace pgf {
 
 constexpr int SG_BM = 64, SG_BN = 64, SG_BK = 16, SG_THREADS = 256;
 
-__global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g) {
+// blockIdx.z = K slice: k in [z*kchunk, min(K, (z+1)*kchunk)); slice z > 0 writes at D + z*split_stride
+// (float32 partials; only used with the plain epilogue).
+__global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g, int64_t kchunk, int64_t split_stride) {
   __shared__ __align__(16) float As[SG_BK][SG_BM + 4];
   __shared__ __align__(16) float Bs[SG_BK][SG_BN + 4];
   const int tid = threadIdx.x;
@@ -22,7 +24,9 @@ __global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
-  for (int64_t k0 = 0; k0 < g.K; k0 += SG_BK) {
+  const int64_t kbeg = int64_t(blockIdx.z) * kchunk;
+  const int64_t kend = kbeg + kchunk < g.K ? kbeg + kchunk : g.K;
+  for (int64_t k0 = kbeg; k0 < kend; k0 += SG_BK) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int li = tid + i * SG_THREADS;
@@ -30,7 +34,7 @@ __global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g) {
       if (!g.a_trans) { kk = li % SG_BK; mm = li / SG_BK; } else { mm = li % SG_BM; kk = li / SG_BM; }
       const int64_t gm = m0 + mm, gk = k0 + kk;
       float v = 0.f;
-      if (gm < g.M && gk < g.K)
+      if (gm < g.M && gk < kend)
         v = ldv(g.A, g.a_bf16, g.a_trans ? gk * g.lda + gm : gm * g.lda + gk);
       As[kk][mm] = v;
     }
@@ -41,7 +45,7 @@ __global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g) {
       if (!g.b_trans) { kk = li % SG_BK; nn = li / SG_BK; } else { nn = li % SG_BN; kk = li / SG_BN; }
       const int64_t gn = n0 + nn, gk = k0 + kk;
       float v = 0.f;
-      if (gn < g.N && gk < g.K)
+      if (gn < g.N && gk < kend)
         v = ldv(g.B, g.b_bf16, g.b_trans ? gk * g.ldb + gn : gn * g.ldb + gk);
       Bs[kk][nn] = v;
     }
@@ -59,6 +63,7 @@ __global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g) {
     }
     __syncthreads();
   }
+  void* D = blockIdx.z ? static_cast<void*>(static_cast<float*>(g.D) + blockIdx.z * split_stride) : g.D;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t m = m0 + ty * 4 + i;
@@ -66,7 +71,7 @@ __global__ void __launch_bounds__(SG_THREADS) gemm_simt_kernel(const Gemm g) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t n = n0 + tx * 4 + j;
-      if (n < g.N) epi_store(g.epi, g.D, g.d_bf16, g.ldd, m, n, acc[i][j]);
+      if (n < g.N) epi_store(g.epi, D, g.d_bf16, g.ldd, m, n, acc[i][j]);
     }
   }
 }
@@ -91,16 +96,84 @@ int run_gemm_simt(const Gemm& g, cudaStream_t s) {
     return PGF_OK;
   }
   prof_begin(PROF_GEMM_SIMT, s);
-  gemm_simt_kernel<<<grid, SG_THREADS, 0, s>>>(g);
+  gemm_simt_kernel<<<grid, SG_THREADS, 0, s>>>(g, g.K, 0);
   prof_end(PROF_GEMM_SIMT, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
 
+int split_slices_simt(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ceil_div(M, SG_BM) * ceil_div(N, SG_BN);
+  const int64_t target = int64_t(sm_count()) * 4;  // resident 256-thread CTAs to aim for
+  if (tiles * 2 > target) return 1;
+  int64_t S = ceil_div(target, tiles);
+  if (S > K / 256) S = K / 256;  // at least 256 deep per slice
+  if (S > 64) S = 64;
+  return S < 1 ? 1 : int(S);
+}
+
+size_t gemm_split_ws(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int a = split_slices_tc(M, N, K), b = split_slices_simt(M, N, K);
+  const int S = a > b ? a : b;
+  return S > 1 ? size_t(S) * size_t(M) * size_t(N) * 4 : 0;
+}
+
+static int run_gemm_simt_split(const Gemm& g, int slices, float* part, int* launched, cudaStream_t s) {
+  int64_t kchunk = ceil_div(ceil_div(g.K, slices), SG_BK) * SG_BK;
+  const int used = int(ceil_div(g.K, kchunk));
+  Gemm h = g;
+  h.D = part; h.d_bf16 = 0; h.ldd = g.N;
+  h.epi = epi_default();
+  dim3 grid(ceil_div(g.N, SG_BN), ceil_div(g.M, SG_BM), unsigned(used));
+  prof_begin(PROF_GEMM_SIMT, s);
+  gemm_simt_kernel<<<grid, SG_THREADS, 0, s>>>(h, kchunk, g.M * g.N);
+  prof_end(PROF_GEMM_SIMT, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
+  PGF_LAUNCH_CHECK();
+  *launched = used;
+  return PGF_OK;
+}
+
+// D = epi(sum over slices of the partial products), slices added in index order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int slices, int64_t M, int64_t N,
+                                     const pgf_epilogue e, void* D, int d_bf16, int64_t ldd) {
+  const int64_t MN = M * N;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < MN; i += int64_t(gridDim.x) * blockDim.x) {
+    float v = 0.f;
+    for (int z = 0; z < slices; ++z) v += part[z * MN + i];
+    const int64_t m = i / N, n = i - m * N;
+    epi_store(e, D, d_bf16, ldd, m, n, v);
+  }
+}
+
+static int splitk_finish(const Gemm& g, const float* part, int used, cudaStream_t s) {
+  int64_t blocks = ceil_div(g.M * g.N, 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  splitk_reduce_kernel<<<unsigned(blocks), 256, 0, s>>>(part, used, g.M, g.N, g.epi, g.D, g.d_bf16, g.ldd);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
 int run_gemm(const Gemm& g, cudaStream_t s) {
-  int rc = run_gemm_tc(g, s);
-  if (rc != PGF_ERR_UNSUPPORTED) return rc;
-  clear_error();
+  const size_t per = size_t(g.M > 0 ? g.M : 0) * size_t(g.N > 0 ? g.N : 0) * 4;
+  const size_t fit_sz = (g.ws && per) ? g.ws_bytes / per : 0;
+  const int fit = fit_sz > 64 ? 64 : int(fit_sz);  // slices the scratch can hold
+  float* part = static_cast<float*>(g.ws);
+  int used = 0;
+  if (tc_usable(g)) {
+    int S = split_slices_tc(g.M, g.N, g.K);
+    if (S > fit) S = fit;
+    const int rc = S > 1 ? run_gemm_tc_split(g, S, part, &used, s) : run_gemm_tc(g, s);
+    if (rc == PGF_OK) return S > 1 ? splitk_finish(g, part, used, s) : PGF_OK;
+    if (rc != PGF_ERR_UNSUPPORTED) return rc;
+    clear_error();
+  }
+  int S = split_slices_simt(g.M, g.N, g.K);
+  if (S > fit) S = fit;
+  if (S > 1) {
+    PGF_TRY(run_gemm_simt_split(g, S, part, &used, s));
+    return splitk_finish(g, part, used, s);
+  }
   return run_gemm_simt(g, s);
 }
 
@@ -173,21 +246,29 @@ using namespace pgf;
 extern "C" int pgf_gemm(int64_t M, int64_t N, int64_t K, const void* A, int a_dtype, int64_t lda,
                         int a_trans, const void* B, int b_dtype, int64_t ldb, int b_trans, void* D,
                         int d_dtype, int64_t ldd, const pgf_epilogue* epi, pgf_stream_t stream) {
+  return pgf_gemm_ex(M, N, K, A, a_dtype, lda, a_trans, B, b_dtype, ldb, b_trans, D, d_dtype, ldd, epi, nullptr, 0,
+                     stream);
+}
+
+extern "C" size_t pgf_gemm_workspace(int64_t M, int64_t N, int64_t K) { return gemm_split_ws(M, N, K); }
+
+extern "C" int pgf_gemm_ex(int64_t M, int64_t N, int64_t K, const void* A, int a_dtype, int64_t lda, int a_trans,
+                           const void* B, int b_dtype, int64_t ldb, int b_trans, void* D, int d_dtype, int64_t ldd,
+                           const pgf_epilogue* epi, void* ws, size_t ws_bytes, pgf_stream_t stream) {
   PGF_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "gemm: negative size");
   PGF_CHECK_ARG((M == 0 || N == 0 || K == 0) || (A && B), "gemm: null operand");
   PGF_CHECK_ARG(D || M == 0 || N == 0, "gemm: null output");
   PGF_CHECK_ARG((a_dtype == 0 || a_dtype == 1) && (b_dtype == 0 || b_dtype == 1) &&
                     (d_dtype == 0 || d_dtype == 1),
                 "gemm: bad dtype");
-  Gemm g;
-  g.M = M; g.N = N; g.K = K;
-  g.A = A; g.a_bf16 = a_dtype; g.lda = lda; g.a_trans = a_trans;
-  g.B = B; g.b_bf16 = b_dtype; g.ldb = ldb; g.b_trans = b_trans;
-  g.D = D; g.d_bf16 = d_dtype; g.ldd = ldd;
-  g.epi = epi ? *epi : epi_default();
+  Gemm g = gemm_make(M, N, K, A, a_dtype, lda, a_trans, B, b_dtype, ldb, b_trans, D, d_dtype, ldd);
+  if (epi) g.epi = *epi;
   PGF_CHECK_ARG(!g.epi.accumulate || d_dtype == PGF_DTYPE_F32, "gemm: accumulate needs float32 D");
   PGF_CHECK_ARG(!(g.epi.kind == PGF_EPI_DGELU || g.epi.kind == PGF_EPI_DRELU) || g.epi.aux,
                 "gemm: DGELU/DRELU need aux");
+  PGF_CHECK_ARG(!ws || (reinterpret_cast<uintptr_t>(ws) & 15) == 0, "gemm: workspace must be 16-byte aligned");
+  g.ws = ws;
+  g.ws_bytes = ws ? ws_bytes : 0;
   return run_gemm(g, as_stream(stream));
 }
 

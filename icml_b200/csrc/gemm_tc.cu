@@ -10,8 +10,10 @@
 //     on their "empty" barriers and hands finished accumulators to the epilogue.
 //   * warps 2..9: epilogue.  Warp w reads TMEM lanes 32*(w%4).. (tile rows) of one 64-column half
 //     with tcgen05.ld while the MMA warp already fills the other accumulator.  Modes:
-//       GENERIC  - 32x32 transposes through shared memory, then the shared epilogue (bias, GELU /
-//                  GELU', addend, accumulate) with coalesced row stores;
+//       GENERIC  - row-per-thread epilogue in registers (bias, GELU / GELU', addend, accumulate),
+//                  rows staged 128B-swizzled in shared memory and written by TMA bulk-tensor
+//                  stores (D and the pre-activation aux_out); outputs whose pitch or base does not
+//                  suit TMA take a 32x32 shared-memory transpose and coalesced row stores instead;
 //       CE_FWD   - online log-sum-exp of each row over the CTA's vocabulary range plus the target
 //                  logit; the logits never leave TMEM;
 //       CE_BWD   - g = (softmax - onehot) * scale from the recomputed logits and the saved lse,
@@ -25,6 +27,7 @@
 #include <math.h>
 
 #include <mutex>
+#include <string.h>
 
 namespace pgf {
 
@@ -34,7 +37,8 @@ constexpr int TC_THREADS = 320;  // TMA warp, MMA warp, 8 epilogue warps
 constexpr int TILE_A_BYTES = TC_BM * TC_BK * 2;
 constexpr int TILE_B_BYTES = TC_BN * TC_BK * 2;
 constexpr int STAGE_BYTES = TILE_A_BYTES + TILE_B_BYTES;
-constexpr int EPI_BYTES = 8 * 32 * 33 * 4;  // one 32x33 float transpose buffer per epilogue warp
+constexpr int EPI_WARP_BYTES = 8192;        // per epilogue warp: two 4 KB staging rows-of-128B buffers
+constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;  // (the transpose path uses the first 32x33 floats)
 constexpr uint32_t TMEM_COLS = 256;        // two 128-column fp32 accumulators
 constexpr size_t TC_SMEM = size_t(TC_STAGES) * STAGE_BYTES + EPI_BYTES + 256 /* barriers */ + 1024 /* align */;
 constexpr long long WAIT_CYCLES = 4000000000ll;  // about 2 s at the B200 clock
@@ -49,7 +53,13 @@ struct TcParams {
   int mode;
   int ng;              // 128-column tiles per work unit
   int n_groups;        // work units per row block
-  int64_t units;
+  int64_t tiles;       // work units per K slice (row blocks x column groups)
+  int64_t units;       // tiles x ksplit
+  int ksplit;          // K slices (1 = whole K per unit)
+  int kper;            // 64-deep k-blocks per slice
+  int64_t split_stride;  // floats between the partial products of consecutive slices
+  int fast;            // 1: row-per-thread epilogue with TMA stores (maps tmD / tmZ valid)
+  int z_bf16;          // aux_out element type on the fast path
   void* D;
   int d_bf16;
   int64_t ldd;
@@ -142,9 +152,81 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---- epilogue staging: 32 rows x 128 B, 128B-swizzled (16-byte chunk j of row r at j ^ (r % 8)),
+//      written by the warp and stored to global memory by one TMA bulk-tensor store.
+__device__ __forceinline__ uint8_t* stage_acquire(uint8_t* stg, uint32_t& sq, int lane) {
+  uint8_t* b = stg + (sq & 1u) * 4096u;
+  // the store issued from this buffer two stagings ago must have finished reading it
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  __syncwarp();
+  ++sq;
+  return b;
+}
+
+__device__ __forceinline__ void stage_row(uint8_t* b, int lane, const uint32_t (&w)[32]) {
+  const uint32_t row = smem_u32(b) + uint32_t(lane) * 128u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t a = row + ((uint32_t(j) ^ uint32_t(lane & 7)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[4 * j]), "r"(w[4 * j + 1]),
+                 "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                 : "memory");
+  }
+}
+
+// 3-D output map {columns, rows, K slice}: a box of 32 rows x 128 B at (col, row, slice).
+__device__ __forceinline__ void stage_store(uint8_t* b, const CUtensorMap* map, int64_t col, int64_t row, int slice,
+                                            int lane) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(int(col)), "r"(int(row)), "r"(slice),
+                 "r"(smem_u32(b))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 32 consecutive elements of row m from column nb (zeros outside M x N); vector loads when the whole
+// segment is in range and 16-byte aligned.
+__device__ __forceinline__ void load_seg(const void* base, int bf16, int64_t ld, int64_t m, int64_t nb, int64_t M,
+                                         int64_t N, float (&o)[32]) {
+  const int64_t off = m * ld + nb;
+  const bool full = m < M && nb + 32 <= N;
+  if (full && !bf16 && ((reinterpret_cast<uintptr_t>(static_cast<const float*>(base) + off) & 15) == 0)) {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 t = __ldg(q + j);
+      o[4 * j] = t.x; o[4 * j + 1] = t.y; o[4 * j + 2] = t.z; o[4 * j + 3] = t.w;
+    }
+  } else if (full && bf16 && ((reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16*>(base) + off) & 15) == 0)) {
+    const uint4* q = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(base) + off);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 t = __ldg(q + j);
+      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o[8 * j + 2 * k] = __uint_as_float(w[k] << 16);
+        o[8 * j + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) o[j] = (m < M && nb + j < N) ? ldv(base, bf16, off + j) : 0.f;
+  }
+}
+
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const TcParams p) {
+               const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmZ, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
@@ -188,12 +270,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t it = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const int mb = int(u / p.n_groups), ng = int(u % p.n_groups);
+        const int ks = int(u / p.tiles), ut = int(u % p.tiles);
+        const int mb = ut / p.n_groups, ng = ut % p.n_groups;
         const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
         const int m0 = mb * TC_BM;
+        const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
         for (int nt = nt0; nt < nt1 && ok; ++nt) {
           const int n0 = nt * TC_BN;
-          for (int kb = 0; kb < nk; ++kb, ++it) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = int(it % TC_STAGES), r = int(it / TC_STAGES);
             if (r > 0 && !mbar_wait(&empty[s], uint32_t((r - 1) & 1))) { ok = false; break; }
             mbar_expect_tx(&full[s], STAGE_BYTES);
@@ -225,14 +309,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t it = 0, tt = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const int ng = int(u % p.n_groups);
+        const int ks = int(u / p.tiles), ng = int(u % p.tiles) % p.n_groups;
         const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
+        const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
         for (int nt = nt0; nt < nt1 && ok; ++nt, ++tt) {
           const uint32_t buf = tt & 1, use = tt >> 1;
           if (use > 0 && !mbar_wait(&tempty[buf], (use - 1) & 1)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t dcol = tmem + buf * TC_BN;
-          for (int kb = 0; kb < nk; ++kb, ++it) {
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = int(it % TC_STAGES), r = int(it / TC_STAGES);
             if (!mbar_wait(&full[s], uint32_t(r & 1))) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -246,7 +331,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                          : sdesc(a_base + kk * 32, 16, 1024);
               const uint64_t bd = p.b_mn ? sdesc(b_base + kk * 2048, TILE_B_BYTES / 2, 1024)
                                          : sdesc(b_base + kk * 32, 16, 1024);
-              umma_bf16(dcol, ad, bd, idesc, (kb | kk) != 0);
+              umma_bf16(dcol, ad, bd, idesc, (kb != kb0) || (kk != 0));
             }
             umma_commit(&empty[s]);
           }
@@ -259,12 +344,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     //      hf = (warp - 2) / 4 (columns 64hf..64hf+63 of the 128-column tile)
     const int q = warp & 3;
     const int hf = (warp - 2) >> 2;
-    float* tb = epi_buf + (warp - 2) * 32 * 33;
+    uint8_t* stg = reinterpret_cast<uint8_t*>(epi_buf) + (warp - 2) * EPI_WARP_BYTES;
+    float* tb = reinterpret_cast<float*>(stg);
+    uint32_t sq = 0;  // staging buffers taken by this warp
     uint32_t tt = 0;
     bool ok = true;
     for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-      const int mb = int(u / p.n_groups), ng = int(u % p.n_groups);
+      const int ks = int(u / p.tiles), ut = int(u % p.tiles);
+      const int mb = ut / p.n_groups, ng = ut % p.n_groups;
       const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
+      // a K slice stores its plain float32 partial product; the reduction applies the epilogue
+      void* Dst = p.ksplit > 1 ? static_cast<void*>(static_cast<float*>(p.D) + ks * p.split_stride) : p.D;
       const int64_t row = int64_t(mb) * TC_BM + q * 32 + lane;  // this thread's row (CE modes)
       const bool row_ok = row < p.M;
       float run_m = -INFINITY, run_s = 0.f;
@@ -279,6 +369,134 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (!mbar_wait(&tfull[buf], use & 1)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int64_t n0 = int64_t(nt) * TC_BN;
+        if (p.fast) {
+          // ---- row-per-thread epilogue: this thread owns row `row`, columns nh .. nh+63
+          const int64_t nh = n0 + hf * 64;
+          const int64_t row0 = int64_t(mb) * TC_BM + q * 32;
+          const bool box_live = row0 < p.M;  // rows of this quarter exist (TMA clips the rest)
+          uint32_t dpk[32], zpk[32];          // bf16 pairs of D / aux_out for the 64 columns
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem + buf * TC_BN + (uint32_t(q * 32) << 16) + uint32_t(hf * 64 + c * 32), r);
+            if (c == 1) {
+              // both chunks are in registers: hand the accumulator back to the MMA warp
+              asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&tempty[buf]);
+            }
+            const int64_t nb = nh + c * 32;
+            float v[32];
+            if (p.mode == TC_CE_BWD) {
+              constexpr float L2E = 1.4426950408889634f;
+              const float ll = row_lse * L2E;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float g = exp2f(fmaf(__uint_as_float(r[j]), L2E, -ll));
+                if (tgt == nb + j) g -= 1.0f;
+                v[j] = g * p.scale;
+              }
+            } else {
+              const pgf_epilogue& e = p.epi;
+              if (e.bias) {
+                if (nb + 32 <= p.N && ((reinterpret_cast<uintptr_t>(e.bias + nb) & 15) == 0)) {
+                  const float4* bq = reinterpret_cast<const float4*>(e.bias + nb);
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) {
+                    const float4 b4 = __ldg(bq + j);
+                    v[4 * j] = fmaf(e.alpha, __uint_as_float(r[4 * j]), b4.x);
+                    v[4 * j + 1] = fmaf(e.alpha, __uint_as_float(r[4 * j + 1]), b4.y);
+                    v[4 * j + 2] = fmaf(e.alpha, __uint_as_float(r[4 * j + 2]), b4.z);
+                    v[4 * j + 3] = fmaf(e.alpha, __uint_as_float(r[4 * j + 3]), b4.w);
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    v[j] = fmaf(e.alpha, __uint_as_float(r[j]), nb + j < p.N ? __ldg(e.bias + nb + j) : 0.f);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = e.alpha * __uint_as_float(r[j]);
+              }
+              if (e.kind == PGF_EPI_GELU || e.kind == PGF_EPI_RELU) {
+                if (e.aux_out) {
+                  if (p.z_bf16) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) zpk[c * 16 + j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+                  } else if (box_live && nb < p.N) {
+                    uint32_t w[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
+                    uint8_t* b = stage_acquire(stg, sq, lane);
+                    stage_row(b, lane, w);
+                    stage_store(b, &tmZ, nb, row0, 0, lane);
+                  }
+                }
+                if (e.kind == PGF_EPI_GELU) {
+                  if (p.d_bf16) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = gelu_bf(v[j]);
+                  } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = gelu_f(v[j]);
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+                }
+              } else if (e.kind == PGF_EPI_DGELU || e.kind == PGF_EPI_DRELU) {
+                float a[32];
+                load_seg(e.aux, e.aux_dtype, e.ld_aux, row, nb, p.M, p.N, a);
+                if (e.kind == PGF_EPI_DRELU) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] = a[j] > 0.f ? v[j] : 0.f;
+                } else if (p.d_bf16) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] *= gelu_prime_bf(a[j]);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] *= gelu_prime_f(a[j]);
+                }
+              }
+              if (e.addend) {
+                float a[32];
+                load_seg(e.addend, e.addend_dtype, e.ld_addend, row, nb, p.M, p.N, a);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += a[j];
+              }
+              if (e.accumulate) {
+                float a[32];
+                load_seg(p.D, 0, p.ldd, row, nb, p.M, p.N, a);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += a[j];
+              }
+            }
+            if (p.d_bf16) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) dpk[c * 16 + j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+            } else if (box_live && nb < p.N) {
+              uint32_t w[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
+              uint8_t* b = stage_acquire(stg, sq, lane);
+              stage_row(b, lane, w);
+              stage_store(b, &tmD, nb, row0, ks, lane);
+            }
+          }
+          // boxes start inside the output (the TMA clips their far edges)
+          if (box_live && nh < p.N && p.d_bf16) {
+            uint8_t* b = stage_acquire(stg, sq, lane);
+            stage_row(b, lane, dpk);
+            stage_store(b, &tmD, nh, row0, ks, lane);
+          }
+          if (box_live && nh < p.N && p.mode == TC_GENERIC && p.epi.aux_out && p.z_bf16 &&
+              (p.epi.kind == PGF_EPI_GELU || p.epi.kind == PGF_EPI_RELU)) {
+            uint8_t* b = stage_acquire(stg, sq, lane);
+            stage_row(b, lane, zpk);
+            stage_store(b, &tmZ, nh, row0, 0, lane);
+          }
+          continue;
+        }
 #pragma unroll 1
         for (int c = 2 * hf; c < 2 * hf + 2; ++c) {
           uint32_t r[32];
@@ -338,7 +556,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll 8
             for (int rr = 0; rr < 32; ++rr) {
               const int64_t m = mbase + rr;
-              if (m < p.M && n_ok) epi_store_biased(p.epi, p.D, p.d_bf16, p.ldd, m, n, tb[rr * 33 + lane], bias_n);
+              if (m < p.M && n_ok) epi_store_biased(p.epi, Dst, p.d_bf16, p.ldd, m, n, tb[rr * 33 + lane], bias_n);
             }
           } else {
             __nv_bfloat16* G = reinterpret_cast<__nv_bfloat16*>(p.D);
@@ -359,6 +577,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         p.part_s[row * (2 * p.n_groups) + 2 * ng + hf] = run_s;
       }
     }
+    // all TMA stores of this warp complete before the CTA leaves
+    if (p.fast && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -402,6 +622,31 @@ static bool make_map(CUtensorMap* m, const void* ptr, int64_t inner, int64_t out
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D output map {cols, rows, slices} (float32 or bf16) with a 128-byte x 32-row box, 128B swizzle:
+// the store side of the row-per-thread epilogue.  slice_stride in elements (slices > 1: split-K).
+static bool make_out_map(CUtensorMap* m, void* ptr, int bf16, int64_t cols, int64_t rows, int64_t ld,
+                         int64_t slices, int64_t slice_stride) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const int64_t es = bf16 ? 2 : 4;
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(slices)};
+  cuuint64_t strides[2] = {cuuint64_t(ld * es), cuuint64_t((slices > 1 ? slice_stride : ld * rows) * es)};
+  cuuint32_t box[3] = {cuuint32_t(128 / es), 32, 1};
+  cuuint32_t est[3] = {1, 1, 1};
+  return fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box,
+            est, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool fast_epilogue_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PGF_TC_TRANSPOSE_EPILOGUE");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 static bool tc_disabled() {
   static int v = -1;
   if (v < 0) {
@@ -411,7 +656,7 @@ static bool tc_disabled() {
   return v == 1;
 }
 
-static int sm_count() {
+int sm_count() {
   static int n = 0;
   if (!n) {
     int dev = 0;
@@ -449,11 +694,36 @@ static int launch_tc(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
   p.a_mn = g.a_trans; p.b_mn = g.b_trans;
   const int64_t n_tiles = (g.N + TC_BN - 1) / TC_BN;
   const int64_t m_blocks = (g.M + TC_BM - 1) / TC_BM;
+  const int nk = int((g.K + TC_BK - 1) / TC_BK);
   p.n_groups = int((n_tiles + p.ng - 1) / p.ng);
-  p.units = m_blocks * p.n_groups;
+  p.tiles = m_blocks * p.n_groups;
+  if (p.ksplit < 1) {
+    p.ksplit = 1;
+    p.kper = nk;
+  }
+  p.units = p.tiles * p.ksplit;
+  // output maps of the row-per-thread epilogue (GENERIC / CE_BWD)
+  CUtensorMap md, mz;
+  memset(&md, 0, sizeof md);
+  memset(&mz, 0, sizeof mz);
+  p.fast = 0;
+  if ((p.mode == TC_GENERIC || p.mode == TC_CE_BWD) && !fast_epilogue_disabled()) {
+    const int64_t es = p.d_bf16 ? 2 : 4;
+    bool ok = aligned(p.D, 16) && (p.ldd * es) % 16 == 0 && (p.ksplit == 1 || (p.split_stride * es) % 16 == 0) &&
+              make_out_map(&md, p.D, p.d_bf16, g.N, g.M, p.ldd, p.ksplit, p.split_stride);
+    const bool want_z = p.mode == TC_GENERIC && p.epi.aux_out &&
+                        (p.epi.kind == PGF_EPI_GELU || p.epi.kind == PGF_EPI_RELU);
+    if (ok && want_z) {
+      const int64_t ez = p.epi.aux_out_dtype ? 2 : 4;
+      p.z_bf16 = p.epi.aux_out_dtype ? 1 : 0;
+      ok = aligned(p.epi.aux_out, 16) && (p.epi.ld_aux_out * ez) % 16 == 0 &&
+           make_out_map(&mz, p.epi.aux_out, p.z_bf16, g.N, g.M, p.epi.ld_aux_out, 1, 0);
+    }
+    p.fast = ok ? 1 : 0;
+  }
   const int64_t grid = p.units < sm_count() ? p.units : sm_count();
   prof_begin(prof_id, s);
-  gemm_tc_kernel<<<unsigned(grid), TC_THREADS, TC_SMEM, s>>>(ma, mb, p);
+  gemm_tc_kernel<<<unsigned(grid), TC_THREADS, TC_SMEM, s>>>(ma, mb, md, mz, p);
   prof_end(prof_id, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
@@ -467,6 +737,32 @@ int run_gemm_tc(const Gemm& g, cudaStream_t s) {
   p.ng = 1;
   p.D = g.D; p.d_bf16 = g.d_bf16; p.ldd = g.ldd;
   p.epi = g.epi;
+  return launch_tc(g, p, s, PROF_GEMM_TC);
+}
+
+int split_slices_tc(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+  const int64_t nk = (K + TC_BK - 1) / TC_BK;
+  const int64_t sm = sm_count();
+  if (tiles * 2 > sm) return 1;
+  int64_t S = sm / tiles;
+  if (S > nk / 4) S = nk / 4;  // at least four k-blocks (256 deep) per slice
+  if (S > 32) S = 32;
+  return S < 1 ? 1 : int(S);
+}
+
+int run_gemm_tc_split(const Gemm& g, int slices, float* part, int* launched, cudaStream_t s) {
+  if (!tc_usable(g)) return PGF_ERR_UNSUPPORTED;
+  const int nk = int((g.K + TC_BK - 1) / TC_BK);
+  TcParams p = {};
+  p.mode = TC_GENERIC;
+  p.ng = 1;
+  p.kper = (nk + slices - 1) / slices;
+  p.ksplit = (nk + p.kper - 1) / p.kper;
+  p.split_stride = g.M * g.N;
+  p.D = part; p.d_bf16 = 0; p.ldd = g.N;
+  p.epi = epi_default();
+  *launched = p.ksplit;
   return launch_tc(g, p, s, PROF_GEMM_TC);
 }
 

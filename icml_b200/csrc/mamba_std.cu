@@ -36,8 +36,9 @@ struct Args {
   float* dloc; float* sdt2; float* dt0; float* X;
   void* y;                         // gated output (Bsz, L, E)
   const void* g;                   // gradient of the gated output
-  float* gdt; int64_t ld_gdt;      // grad of dt_raw
-  float* gbc; int64_t ld_gbc;      // grad of [B | C]
+  void* gdt; int64_t ld_gdt;       // grad of dt_raw (gbf: bf16 else float32)
+  void* gbc; int64_t ld_gbc;       // grad of [B | C] (gbf: bf16 else float32)
+  int gbf;
   void* gz; int64_t ld_gz;         // grad of z
   float* gu;                       // grad of u, scan part (Bsz, L, E)
   float* dbc_part;                 // (G, Bsz, L, 32)
@@ -466,7 +467,7 @@ __global__ void __launch_bounds__(THREADS) main_bwd_kernel(const Args a) {
       const int64_t d = int64_t(l.grp) * DC + dl;
       if (tok < l.e && d < a.E) {
         const int64_t row = l.b * a.L + tok;
-        a.gdt[row * a.ld_gdt + d] = gb[t * DC + dl];
+        stv(a.gdt, a.gbf, row * a.ld_gdt + d, gb[t * DC + dl]);
         a.gu[row * a.E + d] = gb[ST * DC + t * DC + dl];
         stv(a.gz, a.abf, row * a.ld_gz + d, gb[2 * ST * DC + t * DC + dl]);
       }
@@ -489,7 +490,7 @@ __global__ void bc_reduce_kernel(const Args a) {
   const int m = int(idx % 32);
   float s = 0.f;
   for (int64_t gi = 0; gi < a.G; ++gi) s += a.dbc_part[(gi * rows + row) * 32 + m];
-  a.gbc[row * a.ld_gbc + m] = s;
+  stv(a.gbc, a.gbf, row * a.ld_gbc + m, s);
 }
 
 __global__ void param_reduce_kernel(const Args a, float* __restrict__ gA, float* __restrict__ gD, int accumulate) {
@@ -618,10 +619,20 @@ struct Bufs {
   void *xz, *u, *y, *gy, *dxz;
   float *xdbl, *dtr, *dxdbl, *ddtr, *gu, *gu_tot;
   float *hloc, *sdt, *hC, *ckpt, *dloc, *sdt2, *dt0, *X, *dbc, *partA, *partD, *cpart;
-  __nv_bfloat16 *in_wb, *out_wb;
+  __nv_bfloat16 *in_wb, *out_wb, *x_wb, *dt_wb, *xdbl_bf;
   void* cs;
   size_t cs_bytes;
+  void* split;  // split-K partials of the weight gradients
+  size_t split_bytes;
 };
+
+static size_t split_bytes_of(const Plan& p) {
+  const size_t c[4] = {gemm_split_ws(p.d, p.E, p.T), gemm_split_ws(p.E, p.R, p.T), gemm_split_ws(p.XD, p.E, p.T),
+                       gemm_split_ws(2 * p.E, p.d, p.T)};
+  size_t m = 0;
+  for (size_t v : c) m = v > m ? v : m;
+  return m;
+}
 
 static size_t bufs_bytes(const Plan& p, int dtype, int bwd) {
   const size_t es = dtype ? 2 : 4, T = size_t(p.T), E = size_t(p.E);
@@ -637,7 +648,10 @@ static size_t bufs_bytes(const Plan& p, int dtype, int bwd) {
   add(size_t(p.Bsz) * p.nC * E * 4);               // sdt
   add(size_t(p.Bsz) * (p.nC + 1) * E * NST * 4);   // hC
   add(size_t(p.Bsz) * p.nC * KS * E * NST * 4);    // ckpt
-  if (dtype) { add(size_t(2 * E) * p.d * 2); add(size_t(p.d) * E * 2); }
+  if (dtype) {
+    add(size_t(2 * E) * p.d * 2); add(size_t(p.d) * E * 2);                       // in_w, out_w
+    add(size_t(p.XD) * E * 2); add(size_t(E) * p.R * 2); add(T * p.XD * 2);        // x_w, dt_w, x_dbl
+  }
   if (bwd) {
     add(T * E * es);              // gy
     add(T * 2 * E * es);          // dxz
@@ -653,6 +667,7 @@ static size_t bufs_bytes(const Plan& p, int dtype, int bwd) {
     add(size_t(p.Bsz) * ((p.L + CONV_T - 1) / CONV_T) * E * (p.K + 1) * 4);  // conv partials
     size_t c1 = colsum_ws(int64_t(T), E);
     add(c1);
+    add(split_bytes_of(p));
   }
   return b + 8192;
 }
@@ -674,7 +689,10 @@ static int carve(Workspace& W, Bufs& B, const Plan& p, int dtype, int bwd) {
   if (dtype) {
     B.in_wb = W.take<__nv_bfloat16>(size_t(2 * E) * p.d);
     B.out_wb = W.take<__nv_bfloat16>(size_t(p.d) * E);
-    ok = ok && B.in_wb && B.out_wb;
+    B.x_wb = W.take<__nv_bfloat16>(size_t(p.XD) * E);
+    B.dt_wb = W.take<__nv_bfloat16>(size_t(E) * p.R);
+    B.xdbl_bf = W.take<__nv_bfloat16>(T * p.XD);
+    ok = ok && B.in_wb && B.out_wb && B.x_wb && B.dt_wb && B.xdbl_bf;
   }
   if (bwd) {
     B.gy = W.take<char>(T * E * es);
@@ -693,7 +711,9 @@ static int carve(Workspace& W, Bufs& B, const Plan& p, int dtype, int bwd) {
     B.cpart = W.take<float>(size_t(p.Bsz) * ((p.L + CONV_T - 1) / CONV_T) * E * (p.K + 1));
     B.cs_bytes = colsum_ws(int64_t(T), E);
     B.cs = W.take<char>(B.cs_bytes);
-    ok = ok && B.gy && B.dxz && B.dxdbl && B.ddtr && B.gu && B.gu_tot && B.dloc && B.X && B.sdt2 && B.dt0 &&
+    B.split_bytes = split_bytes_of(p);
+    B.split = B.split_bytes ? W.take<char>(B.split_bytes) : nullptr;
+    ok = ok && (!B.split_bytes || B.split) && B.gy && B.dxz && B.dxdbl && B.ddtr && B.gu && B.gu_tot && B.dloc && B.X && B.sdt2 && B.dt0 &&
          B.dbc && B.partA && B.partD && B.cpart && B.cs;
   }
   if (!ok) {
@@ -705,13 +725,7 @@ static int carve(Workspace& W, Bufs& B, const Plan& p, int dtype, int bwd) {
 
 static Gemm G_(int64_t M, int64_t N, int64_t K, const void* A, int abf, int64_t lda, int at, const void* Bm,
                int bbf, int64_t ldb, int bt, void* D, int dbf, int64_t ldd) {
-  Gemm g;
-  g.M = M; g.N = N; g.K = K;
-  g.A = A; g.a_bf16 = abf; g.lda = lda; g.a_trans = at;
-  g.B = Bm; g.b_bf16 = bbf; g.ldb = ldb; g.b_trans = bt;
-  g.D = D; g.d_bf16 = dbf; g.ldd = ldd;
-  g.epi = epi_default();
-  return g;
+  return gemm_make(M, N, K, A, abf, lda, at, Bm, bbf, ldb, bt, D, dbf, ldd);
 }
 
 struct Params {
@@ -735,9 +749,18 @@ static int forward_to_y(const void* x, const Params& P, const Plan& p, Bufs& B, 
     conv_fwd_kernel<<<grid, 128, 0, s>>>(B.xz, 2 * E, P.conv_w, P.conv_b, B.u, p.Bsz, p.L, E, int(p.K), dtype);
     PGF_LAUNCH_CHECK();
   }
-  // x_dbl = u W_x^T (float32), dt_raw = x_dbl[:, :R] W_dt^T + b_dt
-  PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, dtype, E, 0, P.x_w, 0, E, 0, B.xdbl, 0, p.XD), s));
-  {
+  // x_dbl = u W_x^T (float32), dt_raw = x_dbl[:, :R] W_dt^T + b_dt.  bf16 mode: bf16 operands
+  // (weights and x_dbl copies) so both products run on the tensor cores.
+  if (dtype) {
+    PGF_TRY(to_bf16(P.x_w, B.x_wb, p.XD * E, s));
+    PGF_TRY(to_bf16(P.dt_w, B.dt_wb, E * p.R, s));
+    PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, 1, E, 0, B.x_wb, 1, E, 0, B.xdbl, 0, p.XD), s));
+    PGF_TRY(to_bf16(B.xdbl, B.xdbl_bf, T * p.XD, s));
+    Gemm g = G_(T, E, p.R, B.xdbl_bf, 1, p.XD, 0, B.dt_wb, 1, p.R, 0, B.dtr, 0, E);
+    g.epi.bias = P.dt_b;
+    PGF_TRY(run_gemm(g, s));
+  } else {
+    PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, 0, E, 0, P.x_w, 0, E, 0, B.xdbl, 0, p.XD), s));
     Gemm g = G_(T, E, p.R, B.xdbl, 0, p.XD, 0, P.dt_w, 0, p.R, 0, B.dtr, 0, E);
     g.epi.bias = P.dt_b;
     PGF_TRY(run_gemm(g, s));
@@ -840,13 +863,16 @@ extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float
   {
     Gemm g = mstd::G_(d, E, T, g_out, dtype, d, 1, B.y, dtype, E, 1, g_out_w, 0, E);
     g.epi.accumulate = accumulate;
+    g.ws = B.split; g.ws_bytes = B.split_bytes;
     PGF_TRY(run_gemm(g, s));
     PGF_TRY(run_gemm(mstd::G_(T, E, d, g_out, dtype, d, 0, ow, dtype, E, 1, B.gy, dtype, E), s));
   }
   // scan backward
   a.g = B.gy;
+  // bf16 mode: grad dt_raw and grad x_dbl are bf16 (tensor-core operands of the products below)
+  a.gbf = dtype;
   a.gdt = B.ddtr; a.ld_gdt = E;
-  a.gbc = B.dxdbl + R; a.ld_gbc = p.XD;
+  a.gbc = static_cast<char*>(static_cast<void*>(B.dxdbl)) + R * (dtype ? 2 : 4); a.ld_gbc = p.XD;
   a.gz = static_cast<char*>(B.dxz) + E * es; a.ld_gz = 2 * E;
   a.gu = B.gu;
   a.dbc_part = B.dbc;
@@ -869,19 +895,24 @@ extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float
   mstd::param_reduce_kernel<<<ceil_div(E * mstd::NST + E, 256), 256, 0, s>>>(a, g_A_log, g_Dp, accumulate);
   PGF_LAUNCH_CHECK();
   // dt_proj: grad b_dt = colsum(ddtr); grad W_dt (+)= ddtr^T x_dbl[:, :R]; dxdbl[:, :R] = ddtr W_dt
-  PGF_TRY(colsum(B.ddtr, 0, T, E, E, g_dt_b, accumulate, B.cs, B.cs_bytes, s));
+  PGF_TRY(colsum(B.ddtr, dtype, T, E, E, g_dt_b, accumulate, B.cs, B.cs_bytes, s));
+  const void* xd = dtype ? static_cast<const void*>(B.xdbl_bf) : static_cast<const void*>(B.xdbl);
   {
-    Gemm g = mstd::G_(E, R, T, B.ddtr, 0, E, 1, B.xdbl, 0, p.XD, 1, g_dt_w, 0, R);
+    Gemm g = mstd::G_(E, R, T, B.ddtr, dtype, E, 1, xd, dtype, p.XD, 1, g_dt_w, 0, R);
     g.epi.accumulate = accumulate;
+    g.ws = B.split; g.ws_bytes = B.split_bytes;
     PGF_TRY(run_gemm(g, s));
-    PGF_TRY(run_gemm(mstd::G_(T, R, E, B.ddtr, 0, E, 0, dt_w, 0, R, 1, B.dxdbl, 0, p.XD), s));
+    const void* dw = dtype ? static_cast<const void*>(B.dt_wb) : static_cast<const void*>(dt_w);
+    PGF_TRY(run_gemm(mstd::G_(T, R, E, B.ddtr, dtype, E, 0, dw, dtype, R, 1, B.dxdbl, dtype, p.XD), s));
   }
   // x_proj: grad W_x (+)= dxdbl^T u ; du_total = dxdbl W_x + gu
   {
-    Gemm g = mstd::G_(p.XD, E, T, B.dxdbl, 0, p.XD, 1, B.u, dtype, E, 1, g_x_w, 0, E);
+    Gemm g = mstd::G_(p.XD, E, T, B.dxdbl, dtype, p.XD, 1, B.u, dtype, E, 1, g_x_w, 0, E);
     g.epi.accumulate = accumulate;
+    g.ws = B.split; g.ws_bytes = B.split_bytes;
     PGF_TRY(run_gemm(g, s));
-    Gemm g2 = mstd::G_(T, E, p.XD, B.dxdbl, 0, p.XD, 0, x_w, 0, E, 1, B.gu_tot, 0, E);
+    const void* xw = dtype ? static_cast<const void*>(B.x_wb) : static_cast<const void*>(x_w);
+    Gemm g2 = mstd::G_(T, E, p.XD, B.dxdbl, dtype, p.XD, 0, xw, dtype, E, 1, B.gu_tot, 0, E);
     g2.epi.addend = B.gu; g2.epi.addend_dtype = 0; g2.epi.ld_addend = E;
     PGF_TRY(run_gemm(g2, s));
   }
@@ -900,6 +931,7 @@ extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float
   {
     Gemm g = mstd::G_(2 * E, d, T, B.dxz, dtype, 2 * E, 1, x, dtype, d, 1, g_in_w, 0, d);
     g.epi.accumulate = accumulate;
+    g.ws = B.split; g.ws_bytes = B.split_bytes;
     PGF_TRY(run_gemm(g, s));
     const void* iw = dtype ? (const void*)B.in_wb : (const void*)in_w;
     PGF_TRY(run_gemm(mstd::G_(T, d, 2 * E, B.dxz, dtype, 2 * E, 0, iw, dtype, d, 1, g_x, dtype, d), s));

@@ -724,6 +724,7 @@ static size_t ssm_ws(const SsmPlan& p, int dtype, int backward, int act) {
     b += Workspace::round(size_t(p.nC) * p.Bsz * p.G * NST * 4);        // partA
     b += Workspace::round(size_t(p.nC) * p.Bsz * p.D * 4) * 2;          // partD, partS
     b += colsum_ws(int64_t(BL), p.P);
+    b += Workspace::round(gemm_split_ws(p.P, p.D, int64_t(BL)));        // split-K partials of grad W_cat
   }
   return b + 4096;
 }
@@ -758,12 +759,7 @@ static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u,
   }
   *wcat_op = w;
   // proj = u W_cat^T + b_cat   (train_singlemamba_optimized.py:116-124)
-  Gemm g;
-  g.M = int64_t(BL); g.N = p.P; g.K = p.D;
-  g.A = u; g.a_bf16 = dtype; g.lda = p.D; g.a_trans = 0;
-  g.B = w; g.b_bf16 = dtype; g.ldb = p.D; g.b_trans = 0;
-  g.D = proj; g.d_bf16 = 0; g.ldd = p.P;
-  g.epi = epi_default();
+  Gemm g = gemm_make(int64_t(BL), p.P, p.D, u, dtype, p.D, 0, w, dtype, p.D, 0, proj, 0, p.P);
   g.epi.bias = b_cat;
   return run_gemm(g, s);
 }
@@ -902,7 +898,9 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
   a.partS = W.take<float>(size_t(p.nC) * Bsz * D);
   const size_t csb = colsum_ws(int64_t(BL), p.P);
   void* cs = W.take<char>(csb);
-  if (!a.gstack || (dtype && !a.gstack_bf) || !a.gu_scan || !a.dbc_part || (act != PGF_ACT_NONE && !a.actp) || !a.dloc ||
+  const size_t split_ws_bytes = gemm_split_ws(p.P, D, int64_t(BL));
+  void* split_ws = split_ws_bytes ? W.take<char>(split_ws_bytes) : nullptr;
+  if ((split_ws_bytes && !split_ws) || !a.gstack || (dtype && !a.gstack_bf) || !a.gu_scan || !a.dbc_part || (act != PGF_ACT_NONE && !a.actp) || !a.dloc ||
       !a.X || !a.sdt2 || !a.dt0 || !a.partA || !a.partD || !a.partS || !cs) {
     set_error("ssm_bwd: workspace too small (%zu)", ws_bytes);
     return PGF_ERR_WORKSPACE;
@@ -937,24 +935,15 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
   ssm_param_reduce_kernel<<<NST + ceil_div(D, 256), 256, 0, s>>>(a, gA_log, gDp, gscale, accumulate);
   PGF_LAUNCH_CHECK();
   // grad W_cat (+)= gstack^T u ;  grad b_cat (+)= colsum(gstack)   (:438-451)
-  Gemm gw;
-  gw.M = p.P; gw.N = D; gw.K = int64_t(BL);
-  gw.A = dtype ? (const void*)a.gstack_bf : (const void*)a.gstack; gw.a_bf16 = dtype;
-  gw.lda = p.P; gw.a_trans = 1;
-  gw.B = u; gw.b_bf16 = dtype; gw.ldb = D; gw.b_trans = 1;
-  gw.D = gW_cat; gw.d_bf16 = 0; gw.ldd = D;
-  gw.epi = epi_default();
+  Gemm gw = gemm_make(p.P, D, int64_t(BL), dtype ? (const void*)a.gstack_bf : (const void*)a.gstack, dtype, p.P,
+                      1, u, dtype, D, 1, gW_cat, 0, D);
   gw.epi.accumulate = accumulate;
+  gw.ws = split_ws; gw.ws_bytes = split_ws_bytes;
   PGF_TRY(run_gemm(gw, s));
   PGF_TRY(colsum(a.gstack, 0, int64_t(BL), p.P, p.P, gb_cat, accumulate, cs, csb, s));
   // grad_u = gstack W_cat + (delta_in*D + sum_n delta_h phi_1 B)   (:453-463)
-  Gemm gx;
-  gx.M = int64_t(BL); gx.N = D; gx.K = p.P;
-  gx.A = dtype ? (const void*)a.gstack_bf : (const void*)a.gstack; gx.a_bf16 = dtype;
-  gx.lda = p.P; gx.a_trans = 0;
-  gx.B = wop; gx.b_bf16 = dtype; gx.ldb = D; gx.b_trans = 1;
-  gx.D = gu; gx.d_bf16 = dtype; gx.ldd = D;
-  gx.epi = epi_default();
+  Gemm gx = gemm_make(int64_t(BL), D, p.P, dtype ? (const void*)a.gstack_bf : (const void*)a.gstack, dtype, p.P,
+                      0, wop, dtype, D, 1, gu, dtype, D);
   gx.epi.addend = a.gu_scan;
   gx.epi.addend_dtype = 0;
   gx.epi.ld_addend = D;

@@ -110,8 +110,9 @@ def embedding_bwd(ids: torch.Tensor, g: torch.Tensor, vocab: int) -> torch.Tenso
 # --------------------------------------------------------------------------- dense products
 def gemm(A: torch.Tensor, B: torch.Tensor, *, a_trans=False, b_trans=False, out_dtype=torch.float32,
          bias=None, epilogue="none", aux=None, aux_out=None, addend=None, alpha=1.0,
-         out: Optional[torch.Tensor] = None, accumulate=False) -> torch.Tensor:
-    """D = epi(alpha * opA @ opB^T): opA = A (M,K) or A^T when a_trans; opB = B (N,K) or B^T."""
+         out: Optional[torch.Tensor] = None, accumulate=False, split_k=True) -> torch.Tensor:
+    """D = epi(alpha * opA @ opB^T): opA = A (M,K) or A^T when a_trans; opB = B (N,K) or B^T.
+    split_k: give the product split-K scratch (used only when the output has few tiles)."""
     _cuda(A, B)
     A, B = _c(A), _c(B)
     M, K = (A.shape[1], A.shape[0]) if a_trans else A.shape
@@ -133,8 +134,12 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, a_trans=False, b_trans=False, out_
     if addend is not None:
         e.addend, e.addend_dtype, e.ld_addend = addend.data_ptr(), _dt(addend), addend.shape[-1]
     e.accumulate = int(accumulate)
-    check(lib().pgf_gemm(M, N, K, _p(A), _dt(A), A.shape[1], int(a_trans), _p(B), _dt(B), B.shape[1],
-                         int(b_trans), _p(out), _dt(out), out.shape[1], e, _stream()), "gemm")
+    L = lib()
+    nws = L.pgf_gemm_workspace(M, N, K) if split_k else 0
+    ws = _ws(nws, A.device) if nws else None
+    check(L.pgf_gemm_ex(M, N, K, _p(A), _dt(A), A.shape[1], int(a_trans), _p(B), _dt(B), B.shape[1],
+                        int(b_trans), _p(out), _dt(out), out.shape[1], e, _p(ws) if ws is not None else None,
+                        ws.numel() if ws is not None else 0, _stream()), "gemm")
     return out
 
 

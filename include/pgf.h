@@ -148,6 +148,16 @@ int pgf_gemm(int64_t M, int64_t N, int64_t K, const void* A, int a_dtype, int64_
              const void* B, int b_dtype, int64_t ldb, int b_trans, void* D, int d_dtype,
              int64_t ldd, const pgf_epilogue* epi, pgf_stream_t stream);
 
+/* pgf_gemm with split-K scratch.  When the (M x N) output has too few tiles to occupy every SM
+   (weight gradients, whose depth K is the token count), K is cut into slices that run in
+   parallel; their float32 partial products go to `ws` and are summed in slice order
+   (deterministic) before the epilogue.  ws_bytes >= pgf_gemm_workspace(M, N, K); a smaller
+   scratch (or none) runs the product unsplit. */
+size_t pgf_gemm_workspace(int64_t M, int64_t N, int64_t K);
+int pgf_gemm_ex(int64_t M, int64_t N, int64_t K, const void* A, int a_dtype, int64_t lda, int a_trans,
+                const void* B, int b_dtype, int64_t ldb, int b_trans, void* D, int d_dtype,
+                int64_t ldd, const pgf_epilogue* epi, void* ws, size_t ws_bytes, pgf_stream_t stream);
+
 /* Column sums: out[n] (+)= sum_m X[m*ld + n]; deterministic (fixed-order two-level sum).
    The bias gradients of pgf_ffn.py:95,109 and train_singlemamba_optimized.py:443. */
 size_t pgf_colsum_workspace(int64_t M, int64_t N);
