@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "all"],
                     help="component microbenchmarks instead of the LM step (RMSNorm [8,4096,1024]; FFN "
                          "1024-4096-1024 on 32768 tokens; LM head + CE d=1024, vocab 50257, 32768 tokens)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time eager launches instead of the CUDA-graph captured step (1 GPU)")
     ap.add_argument("--parallel", default="sp", choices=["sp", "dp"],
                     help="N>1: sp = one sequence of N x seq-len tokens sharded across the GPUs "
                          "(state hand-off between segments), dp = N independent sequences")
@@ -76,6 +78,8 @@ def config_of(a, world):
         "ssm_variant": ("reference (d_inner = d_model, shared A)" if a.variant == "reference" else
                         "mamba-standard (d_inner 2 d_model, conv1d, gate, per-channel A)"),
         "l2": "per-step working set (weights, optimizer state, activations) > 126 MB L2; no explicit flush",
+        "launch": ("whole step captured once as a CUDA graph, replayed each step" if world == 1 and not a.no_graph
+                   else "eager launches"),
     }
 
 
@@ -364,27 +368,20 @@ def run_gpu(a, rank, world, local_rank):
         if pg is not None:
             torch.distributed.barrier()
 
-    # ---------------- device-timed region: inputs resident in HBM
-    torch.cuda.reset_peak_memory_stats(dev)
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
+    # ---------------- per-kernel breakdown: eager steps with libpgf's CUDA-event timers
+    n_prof = min(a.steps, 3)
     barrier()
     torch.cuda.synchronize()
+    # peak HBM of a step: measured on these eager steps (a graph replay reuses the memory pool its
+    # capture allocated, so the allocator sees no new peak during replays)
+    torch.cuda.reset_peak_memory_stats(dev)
     n0 = L.pgf_launch_count()
     L.pgf_profile(1)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(a.steps):
-        loss = step(inp, tgt)
-    ev1.record()
+    for _ in range(n_prof):
+        step(inp, tgt)
     torch.cuda.synchronize()
-    barrier()
     L.pgf_profile(0)
-    launches = (L.pgf_launch_count() - n0) // a.steps
-    clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
+    launches_eager = (L.pgf_launch_count() - n0) // n_prof
     peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     prof_ms, prof_n, prof_w = {}, {}, {}
     for i, nm in PROF_NAMES.items():
@@ -393,9 +390,37 @@ def run_gpu(a, rank, world, local_rank):
         w = ctypes.c_double(0.0)
         L.pgf_profile_read(i, ctypes.byref(c), ctypes.byref(t), ctypes.byref(w))
         if c.value:
-            prof_n[nm] = c.value
-            prof_ms[nm] = t.value
-            prof_w[nm] = w.value
+            prof_n[nm] = c.value / n_prof
+            prof_ms[nm] = t.value / n_prof
+            prof_w[nm] = w.value / n_prof
+
+    # ---------------- the step as one CUDA graph (1 GPU; N > 1 launches eagerly)
+    graphed = None
+    if world == 1 and not a.no_graph:
+        from icml_b200.lm import GraphedStep
+        graphed = GraphedStep(model, inp, tgt, warmup=1)
+        run_step = lambda x, y: graphed.run(x, y)  # noqa: E731
+        launches = graphed.launches
+    else:
+        run_step = step
+        launches = launches_eager
+
+    # ---------------- device-timed region: inputs resident in HBM
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        loss = run_step(inp, tgt) if graphed is None else graphed.run()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
     t_all = torch.tensor([ms], device=dev)
     if pg is not None:
         torch.distributed.all_reduce(t_all, op=torch.distributed.ReduceOp.MAX)
@@ -411,9 +436,12 @@ def run_gpu(a, rank, world, local_rank):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.steps):
-        x = inp_host.to(dev, non_blocking=True)
-        y = tgt_host.to(dev, non_blocking=True)
-        loss = step(x, y)
+        if graphed is None:
+            x = inp_host.to(dev, non_blocking=True)
+            y = tgt_host.to(dev, non_blocking=True)
+            loss = step(x, y)
+        else:
+            loss = graphed.run(inp_host, tgt_host)  # copies from pinned host memory into the graph's inputs
         loss_val = loss.item()
     e1.record()
     torch.cuda.synchronize()
@@ -425,8 +453,9 @@ def run_gpu(a, rank, world, local_rank):
 
     if rank == 0:
         dom = max(prof_ms, key=prof_ms.get) if prof_ms else None
-        kernels = {k: {"launches_per_step": prof_n[k] / a.steps, "ms_per_step": prof_ms[k] / a.steps,
-                       "share_of_step": prof_ms[k] / a.steps / ms_step if ms_step else None,
+        # per-kernel figures come from the eager profiled steps (graph replays carry no timers)
+        kernels = {k: {"launches_per_step": prof_n[k], "ms_per_step": prof_ms[k],
+                       "share_of_step": prof_ms[k] / ms_step if ms_step else None,
                        "roofline": roofline_entry(k, prof_ms[k], prof_n[k], prof_w[k])}
                    for k in prof_ms}
         line = {
@@ -438,6 +467,7 @@ def run_gpu(a, rank, world, local_rank):
             "e2e": {"value": e2e, "unit": UNIT,
                     "h2d_bytes_per_step": inp_host.numel() * 8 * 2, "d2h_bytes_per_step": 4},
             "gpu_launches": int(launches),
+            "cuda_graph": graphed is not None,
             "kernels": kernels, "dominant_kernel": dom,
             "roofline": kernels[dom]["roofline"] if dom else None,
         }

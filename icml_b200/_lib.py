@@ -76,6 +76,9 @@ SIGNATURES = {
     "pgf_mamba_mixer_workspace": (c_size_t, [I64, I64, I64, I64, I64, I64, I64, c_int, c_int]),
     "pgf_mamba_mixer_fwd": (c_int, [P] * 11 + [I64] * 7 + [c_int, P, c_size_t, P]),
     "pgf_mamba_mixer_bwd": (c_int, [P] * 21 + [c_int] + [I64] * 7 + [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_saved_size": (c_size_t, [I64] * 7 + [c_int]),
+    "pgf_mamba_mixer_fwd_save": (c_int, [P] * 12 + [c_size_t] + [I64] * 7 + [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_bwd_saved": (c_int, [P] * 21 + [c_int, P, c_size_t] + [I64] * 7 + [c_int, P, c_size_t, P]),
     "pgf_ssm_summary": (c_int, [P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, P, c_size_t, P]),
     "pgf_ssm_bwd_summary": (c_int, [P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P,
                                     c_size_t, P]),

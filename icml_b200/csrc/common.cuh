@@ -68,6 +68,18 @@ static inline cudaStream_t as_stream(pgf_stream_t s) { return reinterpret_cast<c
 
 static inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` the first time a launch needs more than
+// the limit already set through `limit` (one per kernel, per process; the default limit is 48 KB
+// minus the kernel's static shared memory, so any size is set once).  Calls that need no more
+// touch nothing, so launches inside a CUDA-graph capture make no runtime calls beyond the launch.
+template <class Kernel>
+static inline cudaError_t ensure_dynamic_smem(Kernel kernel, size_t bytes, int& limit) {
+  if (int(bytes) <= limit) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+  if (e == cudaSuccess) limit = int(bytes);
+  return e;
+}
+
 // Bump allocator over a caller-provided workspace.  Keeps every sub-buffer 256-byte aligned.
 struct Workspace {
   char* base;

@@ -10,10 +10,10 @@
 
 namespace pgf {
 
-static const int64_t kTileBytes = int64_t(64) << 20;  // scratch budget for one row tile
+static const int64_t kTileBytes = int64_t(128) << 20;  // scratch budget for one row tile
 
 static int64_t ffn_tile_rows(int64_t rows, int64_t d_hidden, int backward) {
-  // hidden activations (and the pre-activation in backward) of one tile, in float32
+  // hidden activations (and the pre-activation in backward) of one tile, budgeted as float32
   int64_t per_row = d_hidden * 4 * (backward ? 2 : 1);
   int64_t t = kTileBytes / (per_row > 0 ? per_row : 1);
   t = (t / 128) * 128;
@@ -23,7 +23,7 @@ static int64_t ffn_tile_rows(int64_t rows, int64_t d_hidden, int backward) {
 
 struct FfnWs {
   void* h;      // tile hidden activations (dtype)
-  float* z;     // tile pre-activation (backward)
+  void* z;      // tile pre-activation (backward): bf16 in bf16 runs (act' is evaluated at bf16 precision)
   __nv_bfloat16 *W1b, *W2b;  // bf16 operand copies
   void* cs;     // colsum scratch
   size_t cs_bytes;
@@ -55,7 +55,7 @@ static int ffn_carve(Workspace& W, FfnWs& f, int64_t rows, int64_t d_in, int64_t
   int64_t tr = ffn_tile_rows(rows, d_h, backward);
   size_t es = dtype ? 2 : 4;
   f.h = W.take<char>(size_t(tr) * d_h * es);
-  f.z = backward ? W.take<float>(size_t(tr) * d_h) : nullptr;
+  f.z = backward ? W.take<char>(size_t(tr) * d_h * es) : nullptr;
   f.W1b = dtype ? W.take<__nv_bfloat16>(size_t(d_h) * d_in) : nullptr;
   f.W2b = dtype ? W.take<__nv_bfloat16>(size_t(d_out) * d_h) : nullptr;
   if (backward) {
@@ -176,7 +176,7 @@ extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const 
     g1.epi.bias = b1;
     g1.epi.kind = act_epi(activation, 0);
     g1.epi.aux_out = f.z;
-    g1.epi.aux_out_dtype = 0;
+    g1.epi.aux_out_dtype = dtype;
     g1.epi.ld_aux_out = d_h;
     PGF_TRY(run_gemm(g1, s));
     // grad_W2 (+)= g^T h   (d_out x d_h, K = rows)
@@ -189,7 +189,7 @@ extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const 
     Gemm g3 = mk(m, d_h, d_out, gt, dtype, d_out, 0, w2, wbf, d_h, 1, f.h, dtype, d_h);
     g3.epi.kind = act_epi(activation, 1);
     g3.epi.aux = f.z;
-    g3.epi.aux_dtype = 0;
+    g3.epi.aux_dtype = dtype;
     g3.epi.ld_aux = d_h;
     PGF_TRY(run_gemm(g3, s));
     // grad_W1 (+)= grad_z^T x   (d_h x d_in, K = rows)

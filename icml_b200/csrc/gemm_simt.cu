@@ -206,6 +206,55 @@ size_t colsum_ws(int64_t M, int64_t N) {
   return Workspace::round(size_t(ceil_div(M < 1 ? 1 : M, CS_ROWS)) * size_t(N) * 4);
 }
 
+// Vector form: a CTA sums CS_ROWS rows of 256 columns; a thread owns 8 adjacent columns (one
+// 16-byte load per row in bf16, two in float32), warp w takes rows w, w+8, ... of the slab in order,
+// and the 8 warp partials are added in warp order.  Needs N % 8 == 0 and 16-byte aligned rows.
+constexpr int CSV_WARPS = 8;
+__global__ void __launch_bounds__(CSV_WARPS * 32)
+colsum_part_vec_kernel(const void* __restrict__ X, int bf16, int64_t M, int64_t N, int64_t ld,
+                       float* __restrict__ part) {
+  __shared__ float sm[CSV_WARPS][256 + 4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c0 = int64_t(blockIdx.x) * 256 + lane * 8;
+  const int64_t r0 = int64_t(blockIdx.y) * CS_ROWS;
+  const int64_t r1 = r0 + CS_ROWS < M ? r0 + CS_ROWS : M;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < N) {
+    if (bf16) {
+      const __nv_bfloat16* Xb = static_cast<const __nv_bfloat16*>(X);
+#pragma unroll 4
+      for (int64_t r = r0 + warp; r < r1; r += CSV_WARPS) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(Xb + r * ld + c0));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[2 * k] += __uint_as_float(w[k] << 16);
+          acc[2 * k + 1] += __uint_as_float(w[k] & 0xFFFF0000u);
+        }
+      }
+    } else {
+      const float* Xf = static_cast<const float*>(X);
+#pragma unroll 4
+      for (int64_t r = r0 + warp; r < r1; r += CSV_WARPS) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(Xf + r * ld + c0));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(Xf + r * ld + c0 + 4));
+        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+        acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) sm[warp][lane * 8 + k] = acc[k];
+  __syncthreads();
+  const int64_t c = int64_t(blockIdx.x) * 256 + threadIdx.x;
+  if (c < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < CSV_WARPS; ++w) t += sm[w][threadIdx.x];
+    part[int64_t(blockIdx.y) * N + c] = t;
+  }
+}
+
 int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out, int accumulate,
            void* ws, size_t ws_bytes, cudaStream_t s) {
   if (N == 0) return PGF_OK;
@@ -217,7 +266,12 @@ int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out
   if (size_t(np) * N * 4 > ws_bytes) { set_error("colsum: workspace too small"); return PGF_ERR_WORKSPACE; }
   if (np > 65535) { set_error("colsum: too many rows"); return PGF_ERR_UNSUPPORTED; }
   float* part = static_cast<float*>(ws);
-  colsum_part_kernel<<<dim3(ceil_div(N, 128), unsigned(np)), 128, 0, s>>>(X, bf16, M, N, ld, part);
+  const int64_t es = bf16 ? 2 : 4;
+  if (N % 8 == 0 && aligned(X, 16) && (ld * es) % 16 == 0) {
+    colsum_part_vec_kernel<<<dim3(ceil_div(N, 256), unsigned(np)), CSV_WARPS * 32, 0, s>>>(X, bf16, M, N, ld, part);
+  } else {
+    colsum_part_kernel<<<dim3(ceil_div(N, 128), unsigned(np)), 128, 0, s>>>(X, bf16, M, N, ld, part);
+  }
   PGF_LAUNCH_CHECK();
   colsum_final_kernel<<<ceil_div(N, 128), 128, 0, s>>>(part, np, N, out, accumulate);
   PGF_LAUNCH_CHECK();

@@ -9,6 +9,7 @@
 // into the output pass (forward) and into the adjoint's source term and the gate gradient
 // (backward).  Channels are the E = expand*d_model inner channels.
 #include "gemm.cuh"
+#include "scan_compose.cuh"
 
 namespace pgf {
 namespace mstd {
@@ -191,38 +192,17 @@ __global__ void __launch_bounds__(THREADS) chunk_fwd_kernel(const Args a) {
   if (l.nq == 0) a.sdt[cb * a.E + l.d] = sdt;
 }
 
-__global__ void compose_fwd_kernel(const Args a) {
-  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= a.Bsz * a.E * NST) return;
-  const int n = int(idx % NST);
-  const int64_t d = (idx / NST) % a.E;
-  const int64_t b = idx / (NST * a.E);
+// Chunk start states hC (zero initial state), segmented over the block's warps (scan_compose.cuh).
+__global__ void __launch_bounds__(32 * CSEG) compose_fwd_kernel(const Args a) {
+  const int64_t idx = int64_t(blockIdx.x) * 32 + (threadIdx.x & 31);
+  const bool valid = idx < a.Bsz * a.E * NST;
+  const int64_t ii = valid ? idx : 0;
+  const int n = int(ii % NST);
+  const int64_t d = (ii / NST) % a.E;
+  const int64_t b = ii / (NST * a.E);
   const float A2 = -expf(a.A_log[d * NST + n]) * LOG2E;
-  const float* __restrict__ sdt = a.sdt + b * a.nC * a.E + d;
-  const float* __restrict__ hloc = a.hloc + (b * a.nC * a.E + d) * NST + n;
-  float* __restrict__ hC = a.hC + (b * (a.nC + 1) * a.E + d) * NST + n;
-  const int64_t cs = a.E, hs = a.E * NST;
-  float H = 0.f;
-  hC[0] = H;
-  constexpr int PF = 16;
-  int64_t c = 0;
-  for (; c + PF <= a.nC; c += PF) {
-    float sd[PF], hl[PF];
-#pragma unroll
-    for (int q = 0; q < PF; ++q) {
-      sd[q] = sdt[(c + q) * cs];
-      hl[q] = hloc[(c + q) * hs];
-    }
-#pragma unroll
-    for (int q = 0; q < PF; ++q) {
-      H = exp2f(A2 * sd[q]) * H + hl[q];
-      hC[(c + q + 1) * hs] = H;
-    }
-  }
-  for (; c < a.nC; ++c) {
-    H = exp2f(A2 * sdt[c * cs]) * H + hloc[c * hs];
-    hC[(c + 1) * hs] = H;
-  }
+  compose_fwd_segmented(valid, a.sdt + b * a.nC * a.E + d, a.E, a.hloc + (b * a.nC * a.E + d) * NST + n, a.E * NST,
+                        a.hC + (b * (a.nC + 1) * a.E + d) * NST + n, A2, 0.f, a.nC, nullptr);
 }
 
 __global__ void __launch_bounds__(THREADS) out_fwd_kernel(const Args a) {
@@ -324,25 +304,18 @@ __global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
   }
 }
 
-__global__ void compose_bwd_kernel(const Args a) {
-  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= a.Bsz * a.E * NST) return;
-  const int n = int(idx % NST);
-  const int64_t d = (idx / NST) % a.E;
-  const int64_t b = idx / (NST * a.E);
+// Adjoint carries X entering each chunk from the right (zero final carry), segmented over warps.
+__global__ void __launch_bounds__(32 * CSEG) compose_bwd_kernel(const Args a) {
+  const int64_t idx = int64_t(blockIdx.x) * 32 + (threadIdx.x & 31);
+  const bool valid = idx < a.Bsz * a.E * NST;
+  const int64_t ii = valid ? idx : 0;
+  const int n = int(ii % NST);
+  const int64_t d = (ii / NST) % a.E;
+  const int64_t b = ii / (NST * a.E);
   const float A2 = -expf(a.A_log[d * NST + n]) * LOG2E;
-  const float* __restrict__ sdt2 = a.sdt2 + b * a.nC * a.E + d;
-  const float* __restrict__ dt0 = a.dt0 + b * a.nC * a.E + d;
-  const float* __restrict__ dloc = a.dloc + (b * a.nC * a.E + d) * NST + n;
-  float* __restrict__ X = a.X + (b * a.nC * a.E + d) * NST + n;
-  const int64_t cs = a.E, hs = a.E * NST;
-  float G = 0.f, aE = 1.f;
-  for (int64_t c = a.nC - 1; c >= 0; --c) {
-    const float x = aE * G;
-    X[c * hs] = x;
-    G = exp2f(A2 * sdt2[c * cs]) * x + dloc[c * hs];
-    aE = exp2f(dt0[c * cs] * A2);
-  }
+  compose_bwd_segmented(valid, a.sdt2 + b * a.nC * a.E + d, a.dt0 + b * a.nC * a.E + d, a.E,
+                        a.dloc + (b * a.nC * a.E + d) * NST + n, a.E * NST, a.X + (b * a.nC * a.E + d) * NST + n, A2,
+                        0.f, 1.f, a.nC, nullptr);
 }
 
 // Main backward: checkpoints from the forward output pass (ckpt_g) are required.
@@ -515,84 +488,150 @@ constexpr int CONV_T = 64;  // tokens per thread block row
 constexpr int KMAX = 8;
 
 // u[t, e] = SiLU(b[e] + sum_k w[e, k] xi[t - (K-1) + k, e]); xi rows have pitch ld_x.
+// Causal depthwise conv + SiLU, one thread per (channel, CONV_T-token slab), K a template
+// parameter so the sliding window lives in registers.
+template <int K>
 __global__ void conv_fwd_kernel(const void* __restrict__ xi, int64_t ld_x, const float* __restrict__ w,
                                 const float* __restrict__ bias, void* __restrict__ u, int64_t Bsz, int64_t L,
-                                int64_t E, int K, int abf) {
+                                int64_t E, int abf) {
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t b = blockIdx.z;
   const int64_t t0 = int64_t(blockIdx.y) * CONV_T;
   if (e >= E) return;
-  float wk[KMAX];
+  float wk[K];
+#pragma unroll
   for (int k = 0; k < K; ++k) wk[k] = w[e * K + k];
   const float be = bias[e];
-  float win[KMAX];  // win[k] = xi[t - (K-1) + k]
+  float win[K];  // win[k] = xi[t - (K-1) + k]
+#pragma unroll
   for (int k = 0; k < K - 1; ++k) {
     const int64_t tt = t0 - (K - 1) + k;
     win[k] = tt >= 0 ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f;
   }
   const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
+#pragma unroll 4
   for (int64_t t = t0; t < t1; ++t) {
     win[K - 1] = ldv(xi, abf, (b * L + t) * ld_x + e);
     float acc = be;
+#pragma unroll
     for (int k = 0; k < K; ++k) acc = fmaf(wk[k], win[k], acc);
     stv(u, abf, (b * L + t) * E + e, silu_f(acc));
+#pragma unroll
     for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
   }
 }
 
 // Backward of conv + SiLU: du (float32) -> dxc = du * SiLU'(xc); dxi[t] = sum_k w[k] dxc[t + K-1-k]
-// (written with pitch ld_dx), and per-(token block, channel) partials of grad w and grad b.
+// (written with pitch ld_dx), and per-(token slab, channel) partials of grad w and grad b in rows of
+// E*K + E floats: [grad w as (E, K) | grad b (E)], one row per (batch, slab).
+template <int K>
 __global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const float* __restrict__ w,
                                 const float* __restrict__ bias, const float* __restrict__ du,
                                 void* __restrict__ dxi, int64_t ld_dx, float* __restrict__ part,
-                                int64_t Bsz, int64_t L, int64_t E, int K, int abf) {
+                                int64_t Bsz, int64_t L, int64_t E, int abf) {
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t b = blockIdx.z;
   const int64_t tb = blockIdx.y;
   const int64_t t0 = tb * CONV_T;
   if (e >= E) return;
-  float wk[KMAX];
+  float wk[K];
+#pragma unroll
   for (int k = 0; k < K; ++k) wk[k] = w[e * K + k];
   const float be = bias[e];
   const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
   auto xin = [&](int64_t tt) { return (tt >= 0 && tt < L) ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f; };
-  auto dxc_at = [&](int64_t tt) -> float {
-    if (tt >= L) return 0.f;
+  // xs[j] = x[t - (K-1) + j], j = 0 .. 2K-2 (the inputs of dxc[t .. t+K-1] and of grad w at t)
+  float xs[2 * K - 1];
+#pragma unroll
+  for (int j = 0; j < 2 * K - 2; ++j) xs[j] = xin(t0 - (K - 1) + j);
+  // fwin[j] = dxc[t + j], j = 0 .. K-1
+  float fwin[K];
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) {
+    const int64_t tt = t0 + j;
     float acc = be;
-    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], xin(tt - (K - 1) + k), acc);
-    return du[(b * L + tt) * E + e] * silu_prime_f(acc);
-  };
-  float gw[KMAX];
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], xs[j + k], acc);
+    fwin[j] = tt < L ? du[(b * L + tt) * E + e] * silu_prime_f(acc) : 0.f;
+  }
+  float gw[K];
+#pragma unroll
   for (int k = 0; k < K; ++k) gw[k] = 0.f;
   float gb = 0.f;
-  float fwin[KMAX];  // fwin[j] = dxc[t + j]
-  for (int j = 0; j < K - 1; ++j) fwin[j] = dxc_at(t0 + j);
   for (int64_t t = t0; t < t1; ++t) {
-    fwin[K - 1] = dxc_at(t + K - 1);
+    xs[2 * K - 2] = xin(t + K - 1);
+    {
+      const int64_t tt = t + K - 1;
+      float acc = be;
+#pragma unroll
+      for (int k = 0; k < K; ++k) acc = fmaf(wk[k], xs[K - 1 + k], acc);
+      fwin[K - 1] = tt < L ? du[(b * L + tt) * E + e] * silu_prime_f(acc) : 0.f;
+    }
     float acc = 0.f;
+#pragma unroll
     for (int k = 0; k < K; ++k) acc = fmaf(wk[k], fwin[K - 1 - k], acc);
     stv(dxi, abf, (b * L + t) * ld_dx + e, acc);
     const float g0 = fwin[0];
     gb += g0;
-    for (int k = 0; k < K; ++k) gw[k] = fmaf(g0, xin(t - (K - 1) + k), gw[k]);
+#pragma unroll
+    for (int k = 0; k < K; ++k) gw[k] = fmaf(g0, xs[k], gw[k]);
+#pragma unroll
     for (int j = 0; j < K - 1; ++j) fwin[j] = fwin[j + 1];
+#pragma unroll
+    for (int j = 0; j < 2 * K - 2; ++j) xs[j] = xs[j + 1];
   }
   const int64_t nb = (L + CONV_T - 1) / CONV_T;
-  float* pp = part + ((b * nb + tb) * E + e) * (K + 1);
-  for (int k = 0; k < K; ++k) pp[k] = gw[k];
-  pp[K] = gb;
+  float* row = part + (b * nb + tb) * (E * (K + 1));
+#pragma unroll
+  for (int k = 0; k < K; ++k) row[e * K + k] = gw[k];
+  row[E * K + e] = gb;
 }
 
-__global__ void conv_param_reduce_kernel(const float* __restrict__ part, int64_t cnt, int64_t E, int K,
-                                         float* __restrict__ gw, float* __restrict__ gb, int accumulate) {
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // over E*(K+1)
-  if (i >= E * (K + 1)) return;
-  float s = 0.f;
-  for (int64_t c = 0; c < cnt; ++c) s += part[c * E * (K + 1) + i];
-  const int64_t e = i / (K + 1);
-  const int k = int(i % (K + 1));
-  if (k < K) gw[e * K + k] = accumulate ? gw[e * K + k] + s : s;
-  else gb[e] = accumulate ? gb[e] + s : s;
+template <int K>
+static void launch_conv_fwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w,
+                            const float* bias, void* u, int64_t Bsz, int64_t L, int64_t E, int abf) {
+  conv_fwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, w, bias, u, Bsz, L, E, abf);
+}
+template <int K>
+static void launch_conv_bwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w,
+                            const float* bias, const float* du, void* dxi, int64_t ld_dx, float* part, int64_t Bsz,
+                            int64_t L, int64_t E, int abf) {
+  conv_bwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf);
+}
+
+static int conv_fwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w, const float* bias,
+                    void* u, int64_t Bsz, int64_t L, int64_t E, int abf) {
+  switch (K) {
+    case 1: launch_conv_fwd<1>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    case 2: launch_conv_fwd<2>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    case 3: launch_conv_fwd<3>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    case 4: launch_conv_fwd<4>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    case 5: launch_conv_fwd<5>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    case 6: launch_conv_fwd<6>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    case 7: launch_conv_fwd<7>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    case 8: launch_conv_fwd<8>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+    default: set_error("mamba mixer: d_conv %d unsupported", K); return PGF_ERR_UNSUPPORTED;
+  }
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+static int conv_bwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w, const float* bias,
+                    const float* du, void* dxi, int64_t ld_dx, float* part, int64_t Bsz, int64_t L, int64_t E,
+                    int abf) {
+  switch (K) {
+    case 1: launch_conv_bwd<1>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    case 2: launch_conv_bwd<2>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    case 3: launch_conv_bwd<3>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    case 4: launch_conv_bwd<4>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    case 5: launch_conv_bwd<5>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    case 6: launch_conv_bwd<6>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    case 7: launch_conv_bwd<7>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    case 8: launch_conv_bwd<8>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+    default: set_error("mamba mixer: d_conv %d unsupported", K); return PGF_ERR_UNSUPPORTED;
+  }
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -626,6 +665,13 @@ struct Bufs {
   size_t split_bytes;
 };
 
+// column-sum scratch: grad dt_b over tokens and the conv parameter partials over slabs
+static size_t cs_bytes_of(const Plan& p) {
+  const int64_t cnt = p.Bsz * ((p.L + CONV_T - 1) / CONV_T);
+  const size_t a = colsum_ws(p.T, p.E), b = colsum_ws(cnt, p.E * p.K);
+  return a > b ? a : b;
+}
+
 static size_t split_bytes_of(const Plan& p) {
   const size_t c[4] = {gemm_split_ws(p.d, p.E, p.T), gemm_split_ws(p.E, p.R, p.T), gemm_split_ws(p.XD, p.E, p.T),
                        gemm_split_ws(2 * p.E, p.d, p.T)};
@@ -634,7 +680,10 @@ static size_t split_bytes_of(const Plan& p) {
   return m;
 }
 
-static size_t bufs_bytes(const Plan& p, int dtype, int bwd) {
+// Forward intermediates the backward reads (xz, u, y, x_dbl, dt_raw, chunk states, 8-token scan
+// checkpoints): carved from the caller's `saved` buffer when the forward is kept between calls,
+// else from the workspace.
+static size_t saved_part_bytes(const Plan& p, int dtype) {
   const size_t es = dtype ? 2 : 4, T = size_t(p.T), E = size_t(p.E);
   const size_t KS = size_t((p.Tc + ST - 1) / ST);
   size_t b = 0;
@@ -648,9 +697,17 @@ static size_t bufs_bytes(const Plan& p, int dtype, int bwd) {
   add(size_t(p.Bsz) * p.nC * E * 4);               // sdt
   add(size_t(p.Bsz) * (p.nC + 1) * E * NST * 4);   // hC
   add(size_t(p.Bsz) * p.nC * KS * E * NST * 4);    // ckpt
+  if (dtype) add(T * p.XD * 2);                    // xdbl bf16
+  return b + 1024;
+}
+
+static size_t bufs_bytes(const Plan& p, int dtype, int bwd, bool saved_external = false) {
+  const size_t es = dtype ? 2 : 4, T = size_t(p.T), E = size_t(p.E);
+  size_t b = saved_external ? 0 : saved_part_bytes(p, dtype);
+  auto add = [&](size_t n) { b += Workspace::round(n); };
   if (dtype) {
     add(size_t(2 * E) * p.d * 2); add(size_t(p.d) * E * 2);                       // in_w, out_w
-    add(size_t(p.XD) * E * 2); add(size_t(E) * p.R * 2); add(T * p.XD * 2);        // x_w, dt_w, x_dbl
+    add(size_t(p.XD) * E * 2); add(size_t(E) * p.R * 2);                           // x_w, dt_w
   }
   if (bwd) {
     add(T * E * es);              // gy
@@ -665,33 +722,33 @@ static size_t bufs_bytes(const Plan& p, int dtype, int bwd) {
     add(size_t(p.nC) * p.Bsz * E * NST * 4);       // partA
     add(size_t(p.nC) * p.Bsz * E * 4);             // partD
     add(size_t(p.Bsz) * ((p.L + CONV_T - 1) / CONV_T) * E * (p.K + 1) * 4);  // conv partials
-    size_t c1 = colsum_ws(int64_t(T), E);
-    add(c1);
+    add(cs_bytes_of(p));
     add(split_bytes_of(p));
   }
   return b + 8192;
 }
 
-static int carve(Workspace& W, Bufs& B, const Plan& p, int dtype, int bwd) {
+static int carve(Workspace& W, Workspace* Wsaved, Bufs& B, const Plan& p, int dtype, int bwd) {
   const size_t es = dtype ? 2 : 4, T = size_t(p.T), E = size_t(p.E);
   const size_t KS = size_t((p.Tc + ST - 1) / ST);
   B = Bufs{};
-  B.xz = W.take<char>(T * 2 * E * es);
-  B.u = W.take<char>(T * E * es);
-  B.y = W.take<char>(T * E * es);
-  B.xdbl = W.take<float>(T * p.XD);
-  B.dtr = W.take<float>(T * E);
-  B.hloc = W.take<float>(size_t(p.Bsz) * p.nC * E * NST);
-  B.sdt = W.take<float>(size_t(p.Bsz) * p.nC * E);
-  B.hC = W.take<float>(size_t(p.Bsz) * (p.nC + 1) * E * NST);
-  B.ckpt = W.take<float>(size_t(p.Bsz) * p.nC * KS * E * NST);
+  Workspace& F = Wsaved ? *Wsaved : W;
+  B.xz = F.take<char>(T * 2 * E * es);
+  B.u = F.take<char>(T * E * es);
+  B.y = F.take<char>(T * E * es);
+  B.xdbl = F.take<float>(T * p.XD);
+  B.dtr = F.take<float>(T * E);
+  B.hloc = F.take<float>(size_t(p.Bsz) * p.nC * E * NST);
+  B.sdt = F.take<float>(size_t(p.Bsz) * p.nC * E);
+  B.hC = F.take<float>(size_t(p.Bsz) * (p.nC + 1) * E * NST);
+  B.ckpt = F.take<float>(size_t(p.Bsz) * p.nC * KS * E * NST);
   bool ok = B.xz && B.u && B.y && B.xdbl && B.dtr && B.hloc && B.sdt && B.hC && B.ckpt;
   if (dtype) {
+    B.xdbl_bf = F.take<__nv_bfloat16>(T * p.XD);
     B.in_wb = W.take<__nv_bfloat16>(size_t(2 * E) * p.d);
     B.out_wb = W.take<__nv_bfloat16>(size_t(p.d) * E);
     B.x_wb = W.take<__nv_bfloat16>(size_t(p.XD) * E);
     B.dt_wb = W.take<__nv_bfloat16>(size_t(E) * p.R);
-    B.xdbl_bf = W.take<__nv_bfloat16>(T * p.XD);
     ok = ok && B.in_wb && B.out_wb && B.x_wb && B.dt_wb && B.xdbl_bf;
   }
   if (bwd) {
@@ -709,15 +766,15 @@ static int carve(Workspace& W, Bufs& B, const Plan& p, int dtype, int bwd) {
     B.partA = W.take<float>(size_t(p.nC) * p.Bsz * E * NST);
     B.partD = W.take<float>(size_t(p.nC) * p.Bsz * E);
     B.cpart = W.take<float>(size_t(p.Bsz) * ((p.L + CONV_T - 1) / CONV_T) * E * (p.K + 1));
-    B.cs_bytes = colsum_ws(int64_t(T), E);
+    B.cs_bytes = cs_bytes_of(p);
     B.cs = W.take<char>(B.cs_bytes);
     B.split_bytes = split_bytes_of(p);
     B.split = B.split_bytes ? W.take<char>(B.split_bytes) : nullptr;
-    ok = ok && (!B.split_bytes || B.split) && B.gy && B.dxz && B.dxdbl && B.ddtr && B.gu && B.gu_tot && B.dloc && B.X && B.sdt2 && B.dt0 &&
-         B.dbc && B.partA && B.partD && B.cpart && B.cs;
+    ok = ok && (!B.split_bytes || B.split) && B.gy && B.dxz && B.dxdbl && B.ddtr && B.gu && B.gu_tot && B.dloc &&
+         B.X && B.sdt2 && B.dt0 && B.dbc && B.partA && B.partD && B.cpart && B.cs;
   }
   if (!ok) {
-    set_error("mamba mixer: workspace too small (%zu)", W.cap);
+    set_error("mamba mixer: workspace or saved buffer too small (%zu, %zu)", W.cap, Wsaved ? Wsaved->cap : 0);
     return PGF_ERR_WORKSPACE;
   }
   return PGF_OK;
@@ -732,28 +789,47 @@ struct Params {
   const float *in_w, *conv_w, *conv_b, *x_w, *dt_w, *dt_b, *A_log, *Dp, *out_w;
 };
 
-// forward up to the gated scan output y (B.y); optionally saves the states for the backward
+// bf16 operand copies of the float32 weights (bf16 mode)
+static int convert_weights(const Params& P, const Plan& p, Bufs& B, int dtype, cudaStream_t s) {
+  if (!dtype) return PGF_OK;
+  const int64_t E = p.E;
+  PGF_TRY(to_bf16(P.in_w, B.in_wb, 2 * E * p.d, s));
+  PGF_TRY(to_bf16(P.x_w, B.x_wb, p.XD * E, s));
+  PGF_TRY(to_bf16(P.dt_w, B.dt_wb, E * p.R, s));
+  return to_bf16(P.out_w, B.out_wb, p.d * E, s);
+}
+
+// scan arguments over the forward buffers
+static Args args_of(const Params& P, const Plan& p, const Bufs& B, int dtype, bool save) {
+  Args a = Args{};
+  a.Bsz = p.Bsz; a.L = p.L; a.E = p.E; a.Tc = p.Tc; a.nC = p.nC; a.G = p.G; a.abf = dtype;
+  a.u = B.u;
+  a.dt = B.dtr; a.ld_dt = p.E;
+  a.bc = B.xdbl + p.R; a.ld_bc = p.XD;
+  a.zg = static_cast<const char*>(B.xz) + p.E * (dtype ? 2 : 4); a.ld_z = 2 * p.E;
+  a.A_log = P.A_log; a.Dp = P.Dp;
+  a.hloc = B.hloc; a.sdt = B.sdt; a.hC = B.hC;
+  a.y = B.y;
+  a.ckpt_g = B.ckpt; a.ckpt_write = save ? 1 : 0;
+  return a;
+}
+
+// forward up to the gated scan output y (B.y); optionally saves the 8-token scan checkpoints for
+// the backward.  The weights must already be converted (convert_weights).
 static int forward_to_y(const void* x, const Params& P, const Plan& p, Bufs& B, int dtype, bool save,
                         Args& a, cudaStream_t s) {
   const int64_t T = p.T, E = p.E;
-  const void* in_w = P.in_w;
-  if (dtype) {
-    PGF_TRY(to_bf16(P.in_w, B.in_wb, 2 * E * p.d, s));
-    in_w = B.in_wb;
-  }
+  const void* in_w = dtype ? static_cast<const void*>(B.in_wb) : static_cast<const void*>(P.in_w);
   // xz = x W_in^T
   PGF_TRY(run_gemm(G_(T, 2 * E, p.d, x, dtype, p.d, 0, in_w, dtype, p.d, 0, B.xz, dtype, 2 * E), s));
   // u = SiLU(conv(xi))
   {
     dim3 grid(ceil_div(E, 128), ceil_div(p.L, CONV_T), unsigned(p.Bsz));
-    conv_fwd_kernel<<<grid, 128, 0, s>>>(B.xz, 2 * E, P.conv_w, P.conv_b, B.u, p.Bsz, p.L, E, int(p.K), dtype);
-    PGF_LAUNCH_CHECK();
+    PGF_TRY(conv_fwd(int(p.K), grid, s, B.xz, 2 * E, P.conv_w, P.conv_b, B.u, p.Bsz, p.L, E, dtype));
   }
   // x_dbl = u W_x^T (float32), dt_raw = x_dbl[:, :R] W_dt^T + b_dt.  bf16 mode: bf16 operands
   // (weights and x_dbl copies) so both products run on the tensor cores.
   if (dtype) {
-    PGF_TRY(to_bf16(P.x_w, B.x_wb, p.XD * E, s));
-    PGF_TRY(to_bf16(P.dt_w, B.dt_wb, E * p.R, s));
     PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, 1, E, 0, B.x_wb, 1, E, 0, B.xdbl, 0, p.XD), s));
     PGF_TRY(to_bf16(B.xdbl, B.xdbl_bf, T * p.XD, s));
     Gemm g = G_(T, E, p.R, B.xdbl_bf, 1, p.XD, 0, B.dt_wb, 1, p.R, 0, B.dtr, 0, E);
@@ -765,23 +841,14 @@ static int forward_to_y(const void* x, const Params& P, const Plan& p, Bufs& B, 
     g.epi.bias = P.dt_b;
     PGF_TRY(run_gemm(g, s));
   }
-  a = Args{};
-  a.Bsz = p.Bsz; a.L = p.L; a.E = E; a.Tc = p.Tc; a.nC = p.nC; a.G = p.G; a.abf = dtype;
-  a.u = B.u;
-  a.dt = B.dtr; a.ld_dt = E;
-  a.bc = B.xdbl + p.R; a.ld_bc = p.XD;
-  a.zg = static_cast<const char*>(B.xz) + E * (dtype ? 2 : 4); a.ld_z = 2 * E;
-  a.A_log = P.A_log; a.Dp = P.Dp;
-  a.hloc = B.hloc; a.sdt = B.sdt; a.hC = B.hC;
-  a.y = B.y;
-  a.ckpt_g = B.ckpt; a.ckpt_write = save ? 1 : 0;
+  a = args_of(P, p, B, dtype, save);
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
   prof_begin(PROF_SSM_CHUNK_FWD, s);
   chunk_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
   prof_end(PROF_SSM_CHUNK_FWD, s, double(T) * (dtype ? 2 : 4) * (2.0 * E + NST));
   PGF_LAUNCH_CHECK();
   const int64_t nth = p.Bsz * E * NST;
-  compose_fwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a);
+  compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
   prof_begin(PROF_SSM_OUT_FWD, s);
   out_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
@@ -803,10 +870,40 @@ static int check_dims(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, i
 
 using namespace pgf;
 
+namespace pgf {
+namespace mstd {
+
+static int mixer_fwd_impl(const void* x, const Params& P, void* out, void* saved, size_t saved_bytes, int64_t Bsz,
+                          int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws,
+                          size_t ws_bytes, cudaStream_t s) {
+  PGF_TRY(check_dims(Bsz, L, d, E, R, N, K, dtype));
+  PGF_CHECK_ARG(x && P.in_w && P.conv_w && P.conv_b && P.x_w && P.dt_w && P.dt_b && P.A_log && P.Dp && P.out_w && out,
+                "mamba_mixer_fwd: null pointer");
+  Plan p = plan_of(Bsz, L, d, E, R, N, K);
+  Workspace W(ws, ws_bytes);
+  Workspace Ws(saved, saved_bytes);
+  Bufs B;
+  PGF_TRY(carve(W, saved ? &Ws : nullptr, B, p, dtype, 0));
+  PGF_TRY(convert_weights(P, p, B, dtype, s));
+  Args a;
+  PGF_TRY(forward_to_y(x, P, p, B, dtype, saved != nullptr, a, s));
+  const void* ow = dtype ? static_cast<const void*>(B.out_wb) : static_cast<const void*>(P.out_w);
+  return run_gemm(G_(p.T, d, E, B.y, dtype, E, 0, ow, dtype, E, 0, out, dtype, d), s);
+}
+
+}  // namespace mstd
+}  // namespace pgf
+
 extern "C" size_t pgf_mamba_mixer_workspace(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
                                             int64_t K, int dtype, int backward) {
   mstd::Plan p = mstd::plan_of(Bsz < 1 ? 1 : Bsz, L < 1 ? 1 : L, d, E, R, N, K);
   return mstd::bufs_bytes(p, dtype, backward);
+}
+
+extern "C" size_t pgf_mamba_mixer_saved_size(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                                             int64_t K, int dtype) {
+  mstd::Plan p = mstd::plan_of(Bsz < 1 ? 1 : Bsz, L < 1 ? 1 : L, d, E, R, N, K);
+  return mstd::saved_part_bytes(p, dtype);
 }
 
 extern "C" int pgf_mamba_mixer_fwd(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
@@ -814,51 +911,51 @@ extern "C" int pgf_mamba_mixer_fwd(const void* x, const float* in_w, const float
                                    const float* Dp, const float* out_w, void* out, int64_t Bsz, int64_t L,
                                    int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws,
                                    size_t ws_bytes, pgf_stream_t stream) {
-  PGF_TRY(mstd::check_dims(Bsz, L, d, E, R, N, K, dtype));
-  PGF_CHECK_ARG(x && in_w && conv_w && conv_b && x_w && dt_w && dt_b && A_log && Dp && out_w && out,
-                "mamba_mixer_fwd: null pointer");
-  cudaStream_t s = as_stream(stream);
-  mstd::Plan p = mstd::plan_of(Bsz, L, d, E, R, N, K);
-  Workspace W(ws, ws_bytes);
-  mstd::Bufs B;
-  PGF_TRY(mstd::carve(W, B, p, dtype, 0));
   mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
-  mstd::Args a;
-  PGF_TRY(mstd::forward_to_y(x, P, p, B, dtype, false, a, s));
-  const void* ow = out_w;
-  if (dtype) {
-    PGF_TRY(to_bf16(out_w, B.out_wb, d * E, s));
-    ow = B.out_wb;
-  }
-  return run_gemm(mstd::G_(p.T, d, E, B.y, dtype, E, 0, ow, dtype, E, 0, out, dtype, d), s);
+  return mstd::mixer_fwd_impl(x, P, out, nullptr, 0, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes, as_stream(stream));
 }
 
-extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float* in_w, const float* conv_w,
-                                   const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
-                                   const float* A_log, const float* Dp, const float* out_w, float* g_in_w,
-                                   float* g_conv_w, float* g_conv_b, float* g_x_w, float* g_dt_w, float* g_dt_b,
-                                   float* g_A_log, float* g_Dp, float* g_out_w, void* g_x, int accumulate,
-                                   int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K,
-                                   int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
-  PGF_TRY(mstd::check_dims(Bsz, L, d, E, R, N, K, dtype));
-  PGF_CHECK_ARG(x && g_out && in_w && conv_w && conv_b && x_w && dt_w && dt_b && A_log && Dp && out_w && g_in_w &&
-                    g_conv_w && g_conv_b && g_x_w && g_dt_w && g_dt_b && g_A_log && g_Dp && g_out_w && g_x,
-                "mamba_mixer_bwd: null pointer");
-  cudaStream_t s = as_stream(stream);
-  mstd::Plan p = mstd::plan_of(Bsz, L, d, E, R, N, K);
-  Workspace W(ws, ws_bytes);
-  mstd::Bufs B;
-  PGF_TRY(mstd::carve(W, B, p, dtype, 1));
+extern "C" int pgf_mamba_mixer_fwd_save(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                                        const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                                        const float* Dp, const float* out_w, void* out, void* saved,
+                                        size_t saved_bytes, int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R,
+                                        int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes,
+                                        pgf_stream_t stream) {
+  PGF_CHECK_ARG(saved, "mamba_mixer_fwd_save: null saved buffer");
   mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
-  mstd::Args a;
-  PGF_TRY(mstd::forward_to_y(x, P, p, B, dtype, true, a, s));
+  return mstd::mixer_fwd_impl(x, P, out, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream));
+}
+
+namespace pgf {
+namespace mstd {
+static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, float* g_in_w, float* g_conv_w,
+                          float* g_conv_b, float* g_x_w, float* g_dt_w, float* g_dt_b, float* g_A_log, float* g_Dp,
+                          float* g_out_w, void* g_x, int accumulate, const void* saved, size_t saved_bytes,
+                          int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype,
+                          void* ws, size_t ws_bytes, cudaStream_t s) {
+  PGF_TRY(check_dims(Bsz, L, d, E, R, N, K, dtype));
+  PGF_CHECK_ARG(x && g_out && P.in_w && P.conv_w && P.conv_b && P.x_w && P.dt_w && P.dt_b && P.A_log && P.Dp &&
+                    P.out_w && g_in_w && g_conv_w && g_conv_b && g_x_w && g_dt_w && g_dt_b && g_A_log && g_Dp &&
+                    g_out_w && g_x,
+                "mamba_mixer_bwd: null pointer");
+  const float *in_w = P.in_w, *conv_w = P.conv_w, *conv_b = P.conv_b, *x_w = P.x_w, *dt_w = P.dt_w;
+  (void)conv_b;
+  Plan p = plan_of(Bsz, L, d, E, R, N, K);
+  Workspace W(ws, ws_bytes);
+  Workspace Ws(const_cast<void*>(saved), saved_bytes);
+  Bufs B;
+  PGF_TRY(carve(W, saved ? &Ws : nullptr, B, p, dtype, 1));
+  PGF_TRY(convert_weights(P, p, B, dtype, s));
+  Args a;
+  if (saved) {
+    a = args_of(P, p, B, dtype, false);  // the forward of fwd_save is in `saved`
+  } else {
+    PGF_TRY(forward_to_y(x, P, p, B, dtype, true, a, s));
+  }
   const int64_t T = p.T;
   const size_t es = dtype ? 2 : 4;
-  const void* ow = out_w;
-  if (dtype) {
-    PGF_TRY(to_bf16(out_w, B.out_wb, d * E, s));
-    ow = B.out_wb;
-  }
+  const void* ow = dtype ? static_cast<const void*>(B.out_wb) : static_cast<const void*>(P.out_w);
   // out_proj: grad W_out (+)= g^T y ; gy = g W_out
   {
     Gemm g = mstd::G_(d, E, T, g_out, dtype, d, 1, B.y, dtype, E, 1, g_out_w, 0, E);
@@ -883,7 +980,7 @@ extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float
   mstd::chunk_bwd_kernel<<<grid, mstd::THREADS, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
   const int64_t nth = p.Bsz * E * mstd::NST;
-  mstd::compose_bwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a);
+  mstd::compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
   const size_t smem = size_t(mstd::ST * mstd::WARPS * 32 + 2 * 3 * mstd::ST * mstd::DC) * 4;
   prof_begin(PROF_SSM_MAIN_BWD, s);
@@ -919,13 +1016,12 @@ extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float
   // conv + SiLU backward -> dxz[:, :E]
   {
     dim3 cg(ceil_div(E, 128), ceil_div(p.L, mstd::CONV_T), unsigned(p.Bsz));
-    mstd::conv_bwd_kernel<<<cg, 128, 0, s>>>(B.xz, 2 * E, conv_w, conv_b, B.gu_tot, B.dxz, 2 * E, B.cpart,
-                                             p.Bsz, p.L, E, int(K), dtype);
-    PGF_LAUNCH_CHECK();
+    PGF_TRY(mstd::conv_bwd(int(K), cg, s, B.xz, 2 * E, conv_w, conv_b, B.gu_tot, B.dxz, 2 * E, B.cpart, p.Bsz, p.L,
+                           E, dtype));
+    // grad w, grad b: fixed-order column sums of the (batch, slab) partial rows
     const int64_t cnt = p.Bsz * ((p.L + mstd::CONV_T - 1) / mstd::CONV_T);
-    mstd::conv_param_reduce_kernel<<<ceil_div(E * (K + 1), 256), 256, 0, s>>>(B.cpart, cnt, E, int(K), g_conv_w,
-                                                                             g_conv_b, accumulate);
-    PGF_LAUNCH_CHECK();
+    PGF_TRY(colsum(B.cpart, 0, cnt, E * K, E * (K + 1), g_conv_w, accumulate, B.cs, B.cs_bytes, s));
+    PGF_TRY(colsum(B.cpart + E * K, 0, cnt, E, E * (K + 1), g_conv_b, accumulate, B.cs, B.cs_bytes, s));
   }
   // in_proj: grad W_in (+)= dxz^T x ; grad x = dxz W_in
   {
@@ -937,4 +1033,34 @@ extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float
     PGF_TRY(run_gemm(mstd::G_(T, d, 2 * E, B.dxz, dtype, 2 * E, 0, iw, dtype, d, 1, g_x, dtype, d), s));
   }
   return PGF_OK;
+}
+}  // namespace mstd
+}  // namespace pgf
+
+extern "C" int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                                   const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
+                                   const float* A_log, const float* Dp, const float* out_w, float* g_in_w,
+                                   float* g_conv_w, float* g_conv_b, float* g_x_w, float* g_dt_w, float* g_dt_b,
+                                   float* g_A_log, float* g_Dp, float* g_out_w, void* g_x, int accumulate,
+                                   int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K,
+                                   int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  return mstd::mixer_bwd_impl(x, g_out, P, g_in_w, g_conv_w, g_conv_b, g_x_w, g_dt_w, g_dt_b, g_A_log, g_Dp, g_out_w,
+                              g_x, accumulate, nullptr, 0, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream));
+}
+
+extern "C" int pgf_mamba_mixer_bwd_saved(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                                         const float* conv_b, const float* x_w, const float* dt_w,
+                                         const float* dt_b, const float* A_log, const float* Dp, const float* out_w,
+                                         float* g_in_w, float* g_conv_w, float* g_conv_b, float* g_x_w,
+                                         float* g_dt_w, float* g_dt_b, float* g_A_log, float* g_Dp, float* g_out_w,
+                                         void* g_x, int accumulate, const void* saved, size_t saved_bytes,
+                                         int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                                         int64_t K, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(saved, "mamba_mixer_bwd_saved: null saved buffer");
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  return mstd::mixer_bwd_impl(x, g_out, P, g_in_w, g_conv_w, g_conv_b, g_x_w, g_dt_w, g_dt_b, g_A_log, g_Dp, g_out_w,
+                              g_x, accumulate, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream));
 }

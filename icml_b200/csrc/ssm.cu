@@ -24,6 +24,7 @@
 // Sums over channels (grad B, grad C) and over tokens (grad A_log, D, scale) go through
 // fixed-order partial buffers: results are bitwise reproducible.
 #include "gemm.cuh"
+#include "scan_compose.cuh"
 
 namespace pgf {
 
@@ -86,14 +87,25 @@ __device__ __forceinline__ float act_deriv(int act, float x) {
   return 1.f;
 }
 
-// phi_1(z) and phi_1'(z) given e = e^z and rz = 1/z (series near 0, see common.cuh).
+// phi_1(z) = (e^z - 1)/z and phi_1'(z) = (e^z - phi_1(z))/z given e = e^z (exp2f) and rz = 1/z.
+// |z| < 1/8: Taylor series to z^4 (truncation < 5e-8); elsewhere the closed forms.  With e accurate
+// to 2 ulp the worst relative error is ~1.1e-6 for phi_1 and ~5.4e-6 for phi_1' (at the switch);
+// both branches are a few FMAs, so the select costs less than a divergent branch.
 __device__ __forceinline__ float phi1r(float z, float e, float rz) {
-  if (fabsf(z) < 0.25f) return phi1_from_exp(z, e);
-  return (e - 1.0f) * rz;
+  float p = fmaf(z, 1.0f / 120.0f, 1.0f / 24.0f);
+  p = fmaf(p, z, 1.0f / 6.0f);
+  p = fmaf(p, z, 0.5f);
+  p = fmaf(p, z, 1.0f);
+  const float c = (e - 1.0f) * rz;
+  return fabsf(z) < 0.125f ? p : c;
 }
-__device__ __forceinline__ float phi1pr(float z, float e, float rz) {
-  if (fabsf(z) < 0.5f) return phi1p_from_exp(z, e);
-  return fmaf(z - 1.0f, e, 1.0f) * (rz * rz);
+__device__ __forceinline__ float phi1pr(float z, float e, float p1, float rz) {
+  float p = fmaf(z, 5.0f / 720.0f, 4.0f / 120.0f);
+  p = fmaf(p, z, 3.0f / 24.0f);
+  p = fmaf(p, z, 2.0f / 6.0f);
+  p = fmaf(p, z, 0.5f);
+  const float c = (e - p1) * rz;
+  return fabsf(z) < 0.125f ? p : c;
 }
 
 struct Lane {
@@ -232,45 +244,25 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
   if (l.nq == 0) a.sdt[cb * a.D + l.d] = sdt;
 }
 
-// H_{c+1} = exp(A_n * sum_dt_c) H_c + hloc_c, sequential over chunks; loads run 4 chunks ahead.
-__global__ void ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_final,
-                                       float* __restrict__ sum_dt) {
-  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= a.Bsz * a.D * NST) return;
-  const int n = int(idx % NST);
-  const int64_t d = (idx / NST) % a.D;
-  const int64_t b = idx / (NST * a.D);
+// Chunk start states: H_{c+1} = exp(A_n * sum_dt_c) H_c + hloc_c from h_init (or zero), segmented
+// over the block's warps (scan_compose.cuh); optionally the end state and the total sum of dt.
+__global__ void __launch_bounds__(32 * CSEG) ssm_compose_fwd_kernel(const SsmArgs a, float* __restrict__ h_final,
+                                                                    float* __restrict__ sum_dt) {
+  const int64_t idx = int64_t(blockIdx.x) * 32 + (threadIdx.x & 31);
+  const bool valid = idx < a.Bsz * a.D * NST;
+  const int64_t ii = valid ? idx : 0;
+  const int n = int(ii % NST);
+  const int64_t d = (ii / NST) % a.D;
+  const int64_t b = ii / (NST * a.D);
   const float A2 = -expf(a.A_log[n]) * LOG2E;
-  const float* __restrict__ sdt = a.sdt + b * a.nC * a.D + d;
-  const float* __restrict__ hloc = a.hloc + (b * a.nC * a.D + d) * NST + n;
-  float* __restrict__ hC = a.hC + (b * (a.nC + 1) * a.D + d) * NST + n;
-  const int64_t cs = a.D, hs = a.D * NST;
-  float H = a.h_init ? a.h_init[(b * a.D + d) * NST + n] : 0.f;
-  hC[0] = H;
-  constexpr int PF = 16;  // chunks whose inputs are loaded ahead of the dependent chain
-  int64_t c = 0;
-  for (; c + PF <= a.nC; c += PF) {
-    float sd[PF], hl[PF];
-#pragma unroll
-    for (int q = 0; q < PF; ++q) {
-      sd[q] = sdt[(c + q) * cs];
-      hl[q] = hloc[(c + q) * hs];
-    }
-#pragma unroll
-    for (int q = 0; q < PF; ++q) {
-      H = exp2f(A2 * sd[q]) * H + hl[q];
-      hC[(c + q + 1) * hs] = H;
-    }
-  }
-  for (; c < a.nC; ++c) {
-    H = exp2f(A2 * sdt[c * cs]) * H + hloc[c * hs];
-    hC[(c + 1) * hs] = H;
-  }
-  if (h_final) h_final[(b * a.D + d) * NST + n] = H;
-  if (sum_dt && n == 0) {
-    float t = 0.f;
-    for (int64_t k = 0; k < a.nC; ++k) t += sdt[k * cs];
-    sum_dt[b * a.D + d] = t;
+  const float H0 = (valid && a.h_init) ? a.h_init[(b * a.D + d) * NST + n] : 0.f;
+  float tot = 0.f;
+  const float Hend = compose_fwd_segmented(valid, a.sdt + b * a.nC * a.D + d, a.D,
+                                           a.hloc + (b * a.nC * a.D + d) * NST + n, a.D * NST,
+                                           a.hC + (b * (a.nC + 1) * a.D + d) * NST + n, A2, H0, a.nC, &tot);
+  if (valid && threadIdx.x < 32) {
+    if (h_final) h_final[(b * a.D + d) * NST + n] = Hend;
+    if (sum_dt && n == 0) sum_dt[b * a.D + d] = tot;
   }
 }
 
@@ -382,54 +374,51 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArg
   }
 }
 
-__global__ void ssm_compose_bwd_kernel(const SsmArgs a, const float* __restrict__ dh_end,
-                                       const float* __restrict__ dA_end, float* __restrict__ dh_start,
-                                       float* __restrict__ dA_start, float* __restrict__ sum_dt_excl) {
-  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= a.Bsz * a.D * NST) return;
-  const int n = int(idx % NST);
-  const int64_t d = (idx / NST) % a.D;
-  const int64_t b = idx / (NST * a.D);
+// Adjoint carries X entering each chunk from the right, from (dh_end, dA_end) or (0, 1), segmented
+// over the block's warps (scan_compose.cuh); optionally the carry and decay at the first token
+// (dh_start, dA_start) and the sum of dt over every token but the first.
+__global__ void __launch_bounds__(32 * CSEG) ssm_compose_bwd_kernel(const SsmArgs a, const float* __restrict__ dh_end,
+                                                                    const float* __restrict__ dA_end,
+                                                                    float* __restrict__ dh_start,
+                                                                    float* __restrict__ dA_start,
+                                                                    float* __restrict__ sum_dt_excl) {
+  __shared__ float sSum[CSEG][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t idx = int64_t(blockIdx.x) * 32 + lane;
+  const bool valid = idx < a.Bsz * a.D * NST;
+  const int64_t ii = valid ? idx : 0;
+  const int n = int(ii % NST);
+  const int64_t d = (ii / NST) % a.D;
+  const int64_t b = ii / (NST * a.D);
   const float A2 = -expf(a.A_log[n]) * LOG2E;
   const int64_t o = (b * a.D + d) * NST + n;
-  const float* __restrict__ sdt2 = a.sdt2 + b * a.nC * a.D + d;
-  const float* __restrict__ dt0 = a.dt0 + b * a.nC * a.D + d;
-  const float* __restrict__ dloc = a.dloc + (b * a.nC * a.D + d) * NST + n;
-  float* __restrict__ X = a.X + (b * a.nC * a.D + d) * NST + n;
-  const int64_t cs = a.D, hs = a.D * NST;
-  float G = dh_end ? dh_end[o] : 0.f;
-  float aE = dA_end ? dA_end[o] : 1.f;
-  constexpr int PF = 16;
-  int64_t c = a.nC - 1;
-  for (; c >= PF - 1; c -= PF) {
-    float s2[PF], d0[PF], dl[PF];
-#pragma unroll
-    for (int q = 0; q < PF; ++q) {
-      s2[q] = sdt2[(c - q) * cs];
-      d0[q] = dt0[(c - q) * cs];
-      dl[q] = dloc[(c - q) * hs];
-    }
-#pragma unroll
-    for (int q = 0; q < PF; ++q) {
-      const float x = aE * G;
-      X[(c - q) * hs] = x;
-      G = exp2f(A2 * s2[q]) * x + dl[q];
-      aE = exp2f(d0[q] * A2);
-    }
+  const float* sdt2 = a.sdt2 + b * a.nC * a.D + d;
+  const float* dt0 = a.dt0 + b * a.nC * a.D + d;
+  const float G_end = (valid && dh_end) ? dh_end[o] : 0.f;
+  const float aE_end = (valid && dA_end) ? dA_end[o] : 1.f;
+  float aE0 = 1.f;
+  const float G0 = compose_bwd_segmented(valid, sdt2, dt0, a.D, a.dloc + (b * a.nC * a.D + d) * NST + n, a.D * NST,
+                                         a.X + (b * a.nC * a.D + d) * NST + n, A2, G_end, aE_end, a.nC, &aE0);
+  if (valid && w == 0) {
+    if (dh_start) dh_start[o] = G0;
+    if (dA_start) dA_start[o] = aE0;
   }
-  for (; c >= 0; --c) {
-    const float x = aE * G;
-    X[c * hs] = x;
-    G = exp2f(A2 * sdt2[c * cs]) * x + dloc[c * hs];
-    aE = exp2f(dt0[c * cs] * A2);
-  }
-  if (dh_start) dh_start[o] = G;
-  if (dA_start) dA_start[o] = aE;
-  if (sum_dt_excl && n == 0) {
-    // sum of dt over every token but the first: within-chunk sums plus the later chunks' first dt
+  if (sum_dt_excl) {
+    // sum of dt over every token but the first: the within-chunk sums plus the later chunks' first dt,
+    // per run of chunks, then the runs in order
+    const int64_t run = (a.nC + CSEG - 1) / CSEG;
+    const int64_t c0 = w * run < a.nC ? w * run : a.nC;
+    const int64_t c1 = c0 + run < a.nC ? c0 + run : a.nC;
     float t = 0.f;
-    for (int64_t k = 0; k < a.nC; ++k) t += sdt2[k * cs] + (k > 0 ? dt0[k * cs] : 0.f);
-    sum_dt_excl[b * a.D + d] = t;
+    if (valid && n == 0)
+      for (int64_t k = c0; k < c1; ++k) t += sdt2[k * a.D] + (k > 0 ? dt0[k * a.D] : 0.f);
+    sSum[w][lane] = t;
+    __syncthreads();
+    if (valid && w == 0 && n == 0) {
+      float tot = 0.f;
+      for (int v = 0; v < CSEG; ++v) tot += sSum[v][lane];
+      sum_dt_excl[b * a.D + d] = tot;
+    }
   }
 }
 
@@ -525,7 +514,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
           const float ez = ex[i][j];
           const float rz = rdt * K.rA[j];
           const float p1 = phi1r(z, ez, rz);
-          const float p1p = phi1pr(z, ez, rz);
+          const float p1p = phi1pr(z, ez, p1, rz);
           const float q = ez * tr[i][j] + p1p * (Bv[j] * uu);
           const float dq = dlt * q;
           accA[j] = fmaf(dq, z, accA[j]);
@@ -773,7 +762,7 @@ static int ssm_forward_states(const SsmArgs& a, const SsmPlan& p, float* h_final
   PGF_LAUNCH_CHECK();
   const int64_t nth = p.Bsz * p.D * NST;
   prof_begin(PROF_SSM_COMPOSE, s);
-  ssm_compose_fwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a, h_final, sum_dt);
+  ssm_compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, h_final, sum_dt);
   prof_end(PROF_SSM_COMPOSE, s, bytes_compose(a));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
@@ -918,14 +907,14 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
   prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   const int64_t nth = Bsz * D * NST;
-  ssm_compose_bwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start,
+  ssm_compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start,
                                                             nullptr);
   PGF_LAUNCH_CHECK();
   const int KS = int((p.Tc + ST - 1) / ST);
   const size_t smem = ((saved ? size_t(0) : size_t(KS) * SSM_THREADS * NS) + size_t(ST) * SSM_WARPS * 32 +
                        2 * 2 * ST * DC) * 4;
-  PGF_CUDA(cudaFuncSetAttribute(ssm_main_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(smem)));
+  static int smem_limit = 0;
+  PGF_CUDA(ensure_dynamic_smem(ssm_main_bwd_kernel, smem, smem_limit));
   prof_begin(PROF_SSM_MAIN_BWD, s);
   ssm_main_bwd_kernel<<<grid, SSM_THREADS, smem, s>>>(a);
   prof_end(PROF_SSM_MAIN_BWD, s, bytes_main_bwd(a, a.u_bf16 ? 2 : 4));
@@ -1034,7 +1023,7 @@ extern "C" int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_
   ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
   const int64_t nth = Bsz * D * NST;
-  ssm_compose_bwd_kernel<<<ceil_div(nth, 64), 64, 0, s>>>(a, nullptr, nullptr, dh_start, dA_start,
+  ssm_compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, nullptr, nullptr, dh_start, dA_start,
                                                             sum_dt_excl);
   PGF_LAUNCH_CHECK();
   return PGF_OK;

@@ -51,8 +51,11 @@ class PGFLanguageModel:
         self.final_norm = RMSNorm(d_model).to(device) if final_norm else None
         self.params = [self.emb_weight] + ([] if tie_embeddings else [self.lm_head_weight]) + \
             list(self.backbone.parameters()) + (list(self.final_norm.parameters()) if final_norm else [])
-        self.optimizer = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay,
-                                           fused=self.device.type == "cuda")
+        on_gpu = self.device.type == "cuda"
+        # capturable: the optimizer keeps its step count on the device, so the step can be captured
+        # in a CUDA graph (GraphedStep)
+        self.optimizer = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay, fused=on_gpu,
+                                           capturable=on_gpu)
 
     @torch.no_grad()
     def load_(self, emb: torch.Tensor, lm_head: torch.Tensor, backbone_state: Dict[str, torch.Tensor]):
@@ -118,4 +121,47 @@ class PGFLanguageModel:
         return self.step(input_ids, targets).item()
 
 
-__all__ = ["PGFLanguageModel"]
+class GraphedStep:
+    """One whole training step (embedding, PGF forward/backward of every layer, LM head + CE, AdamW)
+    captured once as a CUDA graph and replayed.
+
+    The step launches about a thousand kernels; replaying them as one graph removes the host's
+    per-launch work (Python, ctypes, the launch API), which otherwise sets the pace whenever the
+    host must wait for a step's loss.  Inputs live in static device buffers: ``run(x, y)`` copies
+    the step's ids and targets into them (from pinned host memory or the device), replays the
+    graph and returns the loss tensor, whose storage is reused by the next replay.  Construction
+    runs ``warmup`` eager steps (real training steps) on a side stream first, as capture requires
+    the optimizer state and every workspace size to be settled.
+    """
+
+    def __init__(self, model: PGFLanguageModel, input_ids: torch.Tensor, targets: torch.Tensor, warmup: int = 2):
+        from ._lib import lib
+        dev = model.device
+        self.model = model
+        self.x = torch.empty_like(input_ids, device=dev)
+        self.y = torch.empty_like(targets, device=dev)
+        self.x.copy_(input_ids)
+        self.y.copy_(targets)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                model.step(self.x, self.y)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = lib().pgf_launch_count()
+        with torch.cuda.graph(self.graph):
+            self.loss = model.step(self.x, self.y)
+        self.launches = int(lib().pgf_launch_count() - n0)  # libpgf kernels per replay
+
+    def run(self, input_ids: Optional[torch.Tensor] = None, targets: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if input_ids is not None:
+            self.x.copy_(input_ids, non_blocking=True)
+        if targets is not None:
+            self.y.copy_(targets, non_blocking=True)
+        self.graph.replay()
+        return self.loss
+
+
+__all__ = ["PGFLanguageModel", "GraphedStep"]

@@ -384,8 +384,25 @@ def mamba_mixer_fwd(x, p):
     return out
 
 
-def mamba_mixer_bwd(x, g, p):
-    """(grads dict over MIXER_KEYS, grad_x) of the standard Mamba mixer."""
+def mamba_mixer_fwd_save(x, p):
+    """Mixer forward that keeps its intermediates: (out, saved) for mamba_mixer_bwd(saved=...)."""
+    _cuda(x, p["in_w"])
+    x = _c(x)
+    Bsz, L_, d, E, R, N, K = _mixer_dims(x, p)
+    q = {k: _f32(p[k]) for k in MIXER_KEYS}
+    out = torch.empty_like(x)
+    Lb = lib()
+    saved = _ws(Lb.pgf_mamba_mixer_saved_size(Bsz, L_, d, E, R, N, K, _dt(x)), x.device)
+    ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 0), x.device)
+    check(Lb.pgf_mamba_mixer_fwd_save(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(out), _p(saved), saved.numel(),
+                                      Bsz, L_, d, E, R, N, K, _dt(x), _p(ws), ws.numel(), _stream()),
+          "mamba_mixer_fwd_save")
+    return out, saved
+
+
+def mamba_mixer_bwd(x, g, p, saved: Optional[torch.Tensor] = None):
+    """(grads dict over MIXER_KEYS, grad_x) of the standard Mamba mixer; `saved` from
+    mamba_mixer_fwd_save on the same x and weights skips the forward re-run."""
     _cuda(x, g, p["in_w"])
     x, g = _c(x), _c(g.to(x.dtype))
     Bsz, L_, d, E, R, N, K = _mixer_dims(x, p)
@@ -394,7 +411,13 @@ def mamba_mixer_bwd(x, g, p):
     gx = torch.empty_like(x)
     Lb = lib()
     ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 1), x.device)
-    check(Lb.pgf_mamba_mixer_bwd(_p(x), _p(g), *[_p(q[k]) for k in MIXER_KEYS],
-                                 *[_p(grads[k]) for k in MIXER_KEYS], _p(gx), 0, Bsz, L_, d, E, R, N, K,
-                                 _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_bwd")
+    if saved is None:
+        check(Lb.pgf_mamba_mixer_bwd(_p(x), _p(g), *[_p(q[k]) for k in MIXER_KEYS],
+                                     *[_p(grads[k]) for k in MIXER_KEYS], _p(gx), 0, Bsz, L_, d, E, R, N, K,
+                                     _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_bwd")
+    else:
+        check(Lb.pgf_mamba_mixer_bwd_saved(_p(x), _p(g), *[_p(q[k]) for k in MIXER_KEYS],
+                                           *[_p(grads[k]) for k in MIXER_KEYS], _p(gx), 0, _p(saved),
+                                           saved.numel(), Bsz, L_, d, E, R, N, K, _dt(x), _p(ws), ws.numel(),
+                                           _stream()), "mamba_mixer_bwd_saved")
     return grads, gx

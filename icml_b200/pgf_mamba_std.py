@@ -117,13 +117,16 @@ class PGFMambaStdBlock(nn.Module):
         g_out = g_out.to(x.dtype)
         p = self.mixer.params()
         xn1 = self.norm1.pgf_forward(x)
-        m_out = ops.mamba_mixer_fwd(xn1, p) + x
+        m_raw, saved = ops.mamba_mixer_fwd_save(xn1, p)
+        m_out = m_raw + x
+        del m_raw
         xn2 = self.norm2.pgf_forward(m_out)
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                           activation=self.ffn_activation, compute_input_grads=True)
         n2 = self.norm2.pgf_grad(m_out, fr["grad_x"].reshape(B, L, D), compute_input_grads=True)
         g_m = n2["grad_x"] + g_out
-        mg, gxn1 = ops.mamba_mixer_bwd(xn1, g_m, p)
+        mg, gxn1 = ops.mamba_mixer_bwd(xn1, g_m, p, saved=saved)
+        del saved
         n1 = self.norm1.pgf_grad(x, gxn1, compute_input_grads=True)
         grads = {"W1": fr["grad_W1"], "b1": fr["grad_b1"], "W2": fr["grad_W2"], "b2": fr["grad_b2"],
                  "norm1.weight": n1["grad_weight"], "norm2.weight": n2["grad_weight"]}

@@ -304,6 +304,27 @@ int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float* in_w, con
                         int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K,
                         int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
 
+/* The mixer forward kept for its backward (the PGF block backward runs the mixer forward once,
+   for the output the later operators need, and then its backward): fwd_save writes the forward
+   intermediates (xz, u, y, x_dbl, dt, chunk states, 8-token scan checkpoints) into `saved`
+   (>= pgf_mamba_mixer_saved_size bytes); bwd_saved reads them instead of re-running the forward.
+   Same inputs and weights in both calls; `saved` is not modified by bwd_saved. */
+size_t pgf_mamba_mixer_saved_size(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                                  int64_t K, int dtype);
+int pgf_mamba_mixer_fwd_save(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                             const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                             const float* Dp, const float* out_w, void* out, void* saved, size_t saved_bytes,
+                             int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K,
+                             int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_mamba_mixer_bwd_saved(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                              const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
+                              const float* A_log, const float* Dp, const float* out_w, float* g_in_w,
+                              float* g_conv_w, float* g_conv_b, float* g_x_w, float* g_dt_w, float* g_dt_b,
+                              float* g_A_log, float* g_Dp, float* g_out_w, void* g_x, int accumulate,
+                              const void* saved, size_t saved_bytes, int64_t Bsz, int64_t L, int64_t d,
+                              int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes,
+                              pgf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,41 @@
+"""The CUDA-graph captured training step replays exactly the eager step."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _pair(variant):
+    from icml_b200.lm import PGFLanguageModel
+    kw = dict(act_dtype=torch.bfloat16, variant=variant)
+    if variant == "std":
+        kw.update(tie_embeddings=True, final_norm=True, expand=2, d_conv=4, dt_rank=4)
+    torch.manual_seed(5)
+    m1 = PGFLanguageModel(301, 64, 16, 128, 2, 64, DEV, **kw)
+    m2 = PGFLanguageModel(301, 64, 16, 128, 2, 64, DEV, **kw)
+    with torch.no_grad():
+        for p1, p2 in zip(m1.params, m2.params):
+            p2.copy_(p1)
+    return m1, m2
+
+
+@pytest.mark.parametrize("variant", ["reference", "std"])
+def test_graphed_step_equals_eager(variant):
+    from icml_b200.lm import GraphedStep
+    m1, m2 = _pair(variant)
+    g = torch.Generator().manual_seed(9)
+    batches = [(torch.randint(0, 301, (2, 200), generator=g), torch.randint(0, 301, (2, 200), generator=g))
+               for _ in range(3)]
+    x0, y0 = batches[0][0].to(DEV), batches[0][1].to(DEV)
+    # eager: one step on batch 0 (the graph's warm-up step), then batches 1, 2
+    m1.step(x0, y0)
+    eager_losses = [m1.step(x.to(DEV), y.to(DEV)).item() for x, y in batches[1:]]
+    gs = GraphedStep(m2, x0, y0, warmup=1)
+    assert gs.launches > 0
+    graph_losses = []
+    for x, y in batches[1:]:
+        graph_losses.append(gs.run(x.pin_memory(), y.pin_memory()).item())
+    assert graph_losses == eager_losses
+    for p1, p2 in zip(m1.params, m2.params):
+        assert torch.equal(p1, p2)

@@ -116,3 +116,21 @@ def test_std_lm_step_matches_autograd():
             kk = k.split(".", 2)[2]
             name = NAMES[kk[6:]] if kk.startswith("mixer.") else kk
             assert_close(grads[f"layers.{i}.{name}"].reshape(v.shape), v, name=f"{i}.{name}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mixer_saved_forward_equals_recompute(dtype):
+    """bwd_saved over fwd_save's intermediates gives bitwise the gradients of the re-running bwd."""
+    from icml_b200 import ops
+    g = torch.Generator().manual_seed(80)
+    p = {k: v.float().to(DEV) for k, v in MS.std_init(64, 16, 2, 4, 4, g).items()}
+    x = torch.randn(2, 300, 64, generator=g).to(DEV, dtype)
+    gy = torch.randn(2, 300, 64, generator=g).to(DEV, dtype)
+    out_s, saved = ops.mamba_mixer_fwd_save(x, p)
+    out = ops.mamba_mixer_fwd(x, p)
+    assert torch.equal(out_s, out)
+    g1, gx1 = ops.mamba_mixer_bwd(x, gy, p)
+    g2, gx2 = ops.mamba_mixer_bwd(x, gy, p, saved=saved)
+    assert torch.equal(gx1, gx2)
+    for k in ops.MIXER_KEYS:
+        assert torch.equal(g1[k], g2[k]), k

@@ -129,9 +129,13 @@ def test_gemm_epilogues(ops):
     assert_close(out, acc.double() + 0.5 * (A.double() @ B.double().t()))
 
 
-def test_colsum(ops):
-    X = torch.randn(1000, 77, generator=_gen(7))
-    assert_close(ops.colsum(X.to(DEV)), X.double().sum(0))
+@pytest.mark.parametrize("M,N,dtype", [(1000, 77, torch.float32), (8192, 1024, torch.bfloat16),
+                                       (65536, 288, torch.float32), (300, 264, torch.bfloat16), (1, 8, torch.float32)])
+def test_colsum(ops, M, N, dtype):
+    X = torch.randn(M, N, generator=_gen(7 + N)).to(dtype)
+    got = ops.colsum(X.to(DEV))
+    assert_close(got, X.double().sum(0), atol=1e-5 * max(1.0, M ** 0.5), rtol=1e-5)
+    assert torch.equal(got, ops.colsum(X.to(DEV))), "column sums must be deterministic"
 
 
 # ----------------------------------------------------------------------------- FFN
