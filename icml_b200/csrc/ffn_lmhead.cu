@@ -7,6 +7,7 @@
 #include "gemm.cuh"
 
 #include <math.h>
+#include <stdlib.h>
 
 namespace pgf {
 
@@ -354,14 +355,23 @@ static int ce_carve(Workspace& W, CeWs& c, int64_t T, int64_t V, int64_t d, int 
 
 // ---- tensor-core path (bf16): fused online-LSE forward, bf16 G written by the logits epilogue
 constexpr int CE_NG = 16;                 // 128-column tiles per forward work unit (2048 vocab ids)
-constexpr int64_t CE_BWD_ROWS = 16384;    // rows of G (bf16, rows x vocab) materialised at a time
+// Rows of G (bf16, rows x vocab) materialised at a time; PGF_CE_BWD_ROWS (a multiple of 128) tunes it.
+static int64_t ce_bwd_rows() {
+  static int64_t r = 0;
+  if (!r) {
+    const char* e = getenv("PGF_CE_BWD_ROWS");
+    long long v = e ? atoll(e) : 0;
+    r = (v >= 128) ? (v / 128) * 128 : 16384;
+  }
+  return r;
+}
 
 // partial (max, sum) pairs per row: two column halves per group of CE_NG tiles
 static int64_t ce_ngroups(int64_t V) { return 2 * (((V + 127) / 128 + CE_NG - 1) / CE_NG); }
 static int64_t ce_ldv(int64_t V) { return (V + 63) / 64 * 64; }
 
 static size_t ce_tc_ws_bytes(int64_t T, int64_t V, int64_t d) {
-  const int64_t R = T < CE_BWD_ROWS ? T : CE_BWD_ROWS;
+  const int64_t R = T < ce_bwd_rows() ? T : ce_bwd_rows();
   size_t b = Workspace::round(size_t(V) * d * 2);                  // W bf16
   b += 2 * Workspace::round(size_t(T) * ce_ngroups(V) * 4);        // part_m, part_s
   b += Workspace::round(size_t(T) * 4);                            // target logits
@@ -417,6 +427,15 @@ static int ce_fwd_tc(const void* h, const float* W, const int64_t* targets, floa
   return PGF_OK;
 }
 
+static bool fused_ce_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PGF_CE_UNFUSED");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 static int ce_bwd_tc(const void* h, const float* W, const int64_t* targets, const float* lse, float scale,
                      float* grad_W, void* grad_h, int accumulate, int64_t T, int64_t V, int64_t d,
                      void* ws, size_t ws_bytes, cudaStream_t s) {
@@ -426,25 +445,32 @@ static int ce_bwd_tc(const void* h, const float* W, const int64_t* targets, cons
   Wk.take<float>(size_t(T) * ng);  // keep the forward layout: the same workspace serves both
   Wk.take<float>(size_t(T) * ng);
   Wk.take<float>(size_t(T));
-  const int64_t R = T < CE_BWD_ROWS ? T : CE_BWD_ROWS;
+  const int64_t R = T < ce_bwd_rows() ? T : ce_bwd_rows();
   const int64_t ldv = ce_ldv(V);
   __nv_bfloat16* G = Wk.take<__nv_bfloat16>(size_t(R) * ldv);
   if (!Wb || !G) { set_error("lm_head_ce_bwd: workspace too small"); return PGF_ERR_WORKSPACE; }
   Gemm probe = mk(R, V, d, h, 1, d, 0, Wb, 1, d, 0, G, 1, ldv);
   if (!tc_usable(probe)) return PGF_ERR_UNSUPPORTED;
   PGF_TRY(to_bf16(W, Wb, V * d, s));
+  // grad_h through the fused kernel (G written once, dh accumulated in TMEM) when it applies
+  const bool fused = grad_h && !fused_ce_disabled() && ce_bwd_dh_usable(h, Wb, G, ldv, grad_h, d);
   for (int64_t r = 0; r < T; r += R) {
     const int64_t m = T - r < R ? T - r : R;
     const __nv_bfloat16* ht = static_cast<const __nv_bfloat16*>(h) + r * d;
-    Gemm g = mk(m, V, d, ht, 1, d, 0, Wb, 1, d, 0, G, 1, ldv);
-    PGF_TRY(tc_ce_bwd(g, targets + r, lse + r, scale, G, ldv, s));
+    __nv_bfloat16* ght = grad_h ? static_cast<__nv_bfloat16*>(grad_h) + r * d : nullptr;
+    if (fused) {
+      PGF_TRY(ce_bwd_dh(ht, Wb, targets + r, lse + r, scale, G, ldv, ght, m, V, d, s));
+    } else {
+      Gemm g = mk(m, V, d, ht, 1, d, 0, Wb, 1, d, 0, G, 1, ldv);
+      PGF_TRY(tc_ce_bwd(g, targets + r, lse + r, scale, G, ldv, s));
+    }
     // grad_W (+)= G^T h_rows
     Gemm gw = mk(V, d, m, G, 1, ldv, 1, ht, 1, d, 1, grad_W, 0, d);
     gw.epi.accumulate = (r > 0) || accumulate;
     PGF_TRY(run_gemm(gw, s));
-    if (grad_h) {
+    if (ght && !fused) {
       // grad_h_rows = G W
-      Gemm gh = mk(m, d, V, G, 1, ldv, 0, Wb, 1, d, 1, static_cast<__nv_bfloat16*>(grad_h) + r * d, 1, d);
+      Gemm gh = mk(m, d, V, G, 1, ldv, 0, Wb, 1, d, 1, ght, 1, d);
       PGF_TRY(run_gemm(gh, s));
     }
   }

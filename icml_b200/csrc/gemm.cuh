@@ -63,10 +63,22 @@ int tc_ce_fwd(const Gemm& g, int ng, const int64_t* targets, float* part_m, floa
 int tc_ce_bwd(const Gemm& g, const int64_t* targets, const float* lse, float scale, __nv_bfloat16* G,
               int64_t ldg, cudaStream_t s);
 
+// Fault flag of the fused LM-head kernels (lmhead_tc.cu): read and cleared; -1 on a CUDA error.
+int lmhead_tc_fault();
+// Fused CE backward over M rows (lmhead_tc.cu): G = (softmax(h W^T) - onehot) * scale as bf16 (rows x
+// ldg, for grad W) and dh = G W (bf16, M x d) in one pass, G never re-read for dh.  d % 64 == 0,
+// d <= 256, 16-byte aligned operands; PGF_ERR_UNSUPPORTED otherwise.
+bool ce_bwd_dh_usable(const void* h, const void* Wb, const void* G, int64_t ldg, const void* dh, int64_t d);
+int ce_bwd_dh(const __nv_bfloat16* h, const __nv_bfloat16* Wb, const int64_t* targets, const float* lse, float scale,
+              __nv_bfloat16* G, int64_t ldg, __nv_bfloat16* dh, int64_t M, int64_t V, int64_t d, cudaStream_t s);
+
 // out[n] (+)= sum_m X[m*ld+n] with `ws` >= colsum_ws(M, N) bytes.
 size_t colsum_ws(int64_t M, int64_t N);
 int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out, int accumulate,
            void* ws, size_t ws_bytes, cudaStream_t s);
+
+// out[n] (+)= sum_p part[p*N + n] for p = 0 .. nparts-1, deterministic (fixed assignment and order).
+int column_reduce(const float* part, int64_t nparts, int64_t N, float* out, int accumulate, cudaStream_t s);
 
 // dst[i] = bf16(src[i]) (weights to the tensor-core operand type)
 int to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s);

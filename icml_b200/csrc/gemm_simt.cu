@@ -193,13 +193,40 @@ __global__ void colsum_part_kernel(const void* __restrict__ X, int bf16, int64_t
   part[int64_t(blockIdx.y) * N + n] = s;
 }
 
-__global__ void colsum_final_kernel(const float* __restrict__ part, int64_t nparts, int64_t N,
-                                    float* __restrict__ out, int accumulate) {
-  const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (n >= N) return;
+// out[c] (+)= sum_p part[p*N + c].  A CTA owns 32 columns; warp w sums parts w, w+32, w+64, ... in
+// order (coalesced 128 B rows), then the 32 warp sums are added in warp order: deterministic.
+constexpr int CR_WARPS = 32;
+__global__ void __launch_bounds__(CR_WARPS * 32)
+column_reduce_kernel(const float* __restrict__ part, int64_t nparts, int64_t N, float* __restrict__ out,
+                     int accumulate) {
+  __shared__ float sm[CR_WARPS][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c = int64_t(blockIdx.x) * 32 + lane;
   float s = 0.f;
-  for (int64_t p = 0; p < nparts; ++p) s += part[p * N + n];
-  out[n] = accumulate ? out[n] + s : s;
+  if (c < N) {
+    int64_t p = warp;
+    for (; p + 3 * CR_WARPS < nparts; p += 4 * CR_WARPS) {
+      const float a0 = part[p * N + c], a1 = part[(p + CR_WARPS) * N + c];
+      const float a2 = part[(p + 2 * CR_WARPS) * N + c], a3 = part[(p + 3 * CR_WARPS) * N + c];
+      s += a0; s += a1; s += a2; s += a3;
+    }
+    for (; p < nparts; p += CR_WARPS) s += part[p * N + c];
+  }
+  sm[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && c < N) {
+    float t = 0.f;
+#pragma unroll 8
+    for (int w = 0; w < CR_WARPS; ++w) t += sm[w][lane];
+    out[c] = accumulate ? out[c] + t : t;
+  }
+}
+
+int column_reduce(const float* part, int64_t nparts, int64_t N, float* out, int accumulate, cudaStream_t s) {
+  if (N <= 0) return PGF_OK;
+  column_reduce_kernel<<<unsigned(ceil_div(N, 32)), CR_WARPS * 32, 0, s>>>(part, nparts, N, out, accumulate);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
 }
 
 size_t colsum_ws(int64_t M, int64_t N) {
@@ -273,9 +300,7 @@ int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out
     colsum_part_kernel<<<dim3(ceil_div(N, 128), unsigned(np)), 128, 0, s>>>(X, bf16, M, N, ld, part);
   }
   PGF_LAUNCH_CHECK();
-  colsum_final_kernel<<<ceil_div(N, 128), 128, 0, s>>>(part, np, N, out, accumulate);
-  PGF_LAUNCH_CHECK();
-  return PGF_OK;
+  return column_reduce(part, np, N, out, accumulate, s);
 }
 
 __global__ void to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n) {

@@ -466,21 +466,6 @@ __global__ void bc_reduce_kernel(const Args a) {
   stv(a.gbc, a.gbf, row * a.ld_gbc + m, s);
 }
 
-__global__ void param_reduce_kernel(const Args a, float* __restrict__ gA, float* __restrict__ gD, int accumulate) {
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // over E*N (+ E for D)
-  const int64_t cnt = a.nC * a.Bsz;
-  if (i < a.E * NST) {
-    float s = 0.f;
-    for (int64_t c = 0; c < cnt; ++c) s += a.partA[c * a.E * NST + i];
-    gA[i] = accumulate ? gA[i] + s : s;
-  } else if (i < a.E * NST + a.E) {
-    const int64_t d = i - a.E * NST;
-    float s = 0.f;
-    for (int64_t c = 0; c < cnt; ++c) s += a.partD[c * a.E + d];
-    gD[d] = accumulate ? gD[d] + s : s;
-  }
-}
-
 // ---------------------------------------------------------------------------------------------
 // causal depthwise conv1d + SiLU
 // ---------------------------------------------------------------------------------------------
@@ -989,8 +974,9 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
   PGF_LAUNCH_CHECK();
   mstd::bc_reduce_kernel<<<ceil_div(T * 32, 256), 256, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
-  mstd::param_reduce_kernel<<<ceil_div(E * mstd::NST + E, 256), 256, 0, s>>>(a, g_A_log, g_Dp, accumulate);
-  PGF_LAUNCH_CHECK();
+  // grad A_log, grad D: fixed-order column sums of the per-(chunk, batch) partials
+  PGF_TRY(column_reduce(a.partA, p.nC * p.Bsz, E * mstd::NST, g_A_log, accumulate, s));
+  PGF_TRY(column_reduce(a.partD, p.nC * p.Bsz, E, g_Dp, accumulate, s));
   // dt_proj: grad b_dt = colsum(ddtr); grad W_dt (+)= ddtr^T x_dbl[:, :R]; dxdbl[:, :R] = ddtr W_dt
   PGF_TRY(colsum(B.ddtr, dtype, T, E, E, g_dt_b, accumulate, B.cs, B.cs_bytes, s));
   const void* xd = dtype ? static_cast<const void*>(B.xdbl_bf) : static_cast<const void*>(B.xdbl);

@@ -4,7 +4,7 @@
 // and g are read once.  grad_weight is reduced deterministically: each CTA sums its warps'
 // register partials through shared memory in warp order and writes one partial row; a second
 // kernel adds the CTA partials in CTA order.
-#include "common.cuh"
+#include "gemm.cuh"
 
 namespace pgf {
 
@@ -99,35 +99,6 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g, const float
   }
 }
 
-// out[c] (+)= sum_p part[p*dim + c].  A CTA owns 32 columns; warp w sums parts w, w+32, w+64, ...
-// in order (coalesced 128 B rows), then the 32 warp sums are added in warp order: deterministic.
-constexpr int RP_WARPS = 32;
-__global__ void __launch_bounds__(RP_WARPS * 32)
-reduce_partials_kernel(const float* __restrict__ part, int64_t nparts, int dim, float* __restrict__ out,
-                       int accumulate) {
-  __shared__ float sm[RP_WARPS][33];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int c = blockIdx.x * 32 + lane;
-  float s = 0.f;
-  if (c < dim) {
-    int64_t p = warp;
-    for (; p + 3 * RP_WARPS < nparts; p += 4 * RP_WARPS) {
-      const float a0 = part[p * dim + c], a1 = part[(p + RP_WARPS) * dim + c];
-      const float a2 = part[(p + 2 * RP_WARPS) * dim + c], a3 = part[(p + 3 * RP_WARPS) * dim + c];
-      s += a0; s += a1; s += a2; s += a3;
-    }
-    for (; p < nparts; p += RP_WARPS) s += part[p * dim + c];
-  }
-  sm[warp][lane] = s;
-  __syncthreads();
-  if (warp == 0 && c < dim) {
-    float t = 0.f;
-#pragma unroll 8
-    for (int w = 0; w < RP_WARPS; ++w) t += sm[w][lane];
-    out[c] = accumulate ? out[c] + t : t;
-  }
-}
-
 template <class T>
 static int rms_fwd_dispatch(const T* x, const float* w, T* y, int64_t rows, int dim, float eps,
                             cudaStream_t s) {
@@ -181,8 +152,7 @@ static int rms_bwd_dispatch(const T* x, const T* g, const float* w, T* gx, float
   else { set_error("rmsnorm: dim %d > 4096 unsupported", dim); return PGF_ERR_UNSUPPORTED; }
 #undef PGF_RMS_B
   PGF_LAUNCH_CHECK();
-  reduce_partials_kernel<<<ceil_div(dim, 32), RP_WARPS * 32, 0, s>>>(part, nct, dim, gw, acc);
-  PGF_LAUNCH_CHECK();
+  PGF_TRY(column_reduce(part, nct, dim, gw, acc, s));
   return PGF_OK;
 }
 

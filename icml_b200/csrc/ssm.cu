@@ -621,34 +621,21 @@ __global__ void ssm_bc_reduce_kernel(const SsmArgs a) {
 }
 
 // grad A_log / D / scale from the per-CTA partials, in a fixed order.
-__global__ void ssm_param_reduce_kernel(const SsmArgs a, float* __restrict__ gA,
-                                        float* __restrict__ gD, float* __restrict__ gS,
-                                        int accumulate) {
+// grad A_log from the per-CTA partials (A is shared by the channels: one block per state n, the
+// partials summed in a fixed order).  grad D and grad scale are column reductions (column_reduce).
+__global__ void ssm_param_reduce_kernel(const SsmArgs a, float* __restrict__ gA, int accumulate) {
   __shared__ float red[256];
-  if (blockIdx.x < NST) {
-    const int n = blockIdx.x;
-    const int64_t cnt = a.nC * a.Bsz * a.G;
-    float s = 0.f;
-    for (int64_t i = threadIdx.x; i < cnt; i += blockDim.x) s += a.partA[i * NST + n];
-    red[threadIdx.x] = s;
+  const int n = blockIdx.x;
+  const int64_t cnt = a.nC * a.Bsz * a.G;
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < cnt; i += blockDim.x) s += a.partA[i * NST + n];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (int(threadIdx.x) < o) red[threadIdx.x] += red[threadIdx.x + o];
     __syncthreads();
-    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-      if (int(threadIdx.x) < o) red[threadIdx.x] += red[threadIdx.x + o];
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) gA[n] = accumulate ? gA[n] + red[0] : red[0];
-    return;
   }
-  const int64_t d = int64_t(blockIdx.x - NST) * blockDim.x + threadIdx.x;
-  if (d >= a.D) return;
-  const int64_t cnt = a.nC * a.Bsz;
-  float sD = 0.f, sS = 0.f;
-  for (int64_t i = 0; i < cnt; ++i) {
-    sD += a.partD[i * a.D + d];
-    sS += a.partS[i * a.D + d];
-  }
-  gD[d] = accumulate ? gD[d] + sD : sD;
-  gS[d] = accumulate ? gS[d] + sS : sS;
+  if (threadIdx.x == 0) gA[n] = accumulate ? gA[n] + red[0] : red[0];
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -921,8 +908,10 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
   PGF_LAUNCH_CHECK();
   ssm_bc_reduce_kernel<<<ceil_div(int64_t(BL) * 32, 256), 256, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
-  ssm_param_reduce_kernel<<<NST + ceil_div(D, 256), 256, 0, s>>>(a, gA_log, gDp, gscale, accumulate);
+  ssm_param_reduce_kernel<<<NST, 256, 0, s>>>(a, gA_log, accumulate);
   PGF_LAUNCH_CHECK();
+  PGF_TRY(column_reduce(a.partD, p.nC * Bsz, D, gDp, accumulate, s));
+  PGF_TRY(column_reduce(a.partS, p.nC * Bsz, D, gscale, accumulate, s));
   // grad W_cat (+)= gstack^T u ;  grad b_cat (+)= colsum(gstack)   (:438-451)
   Gemm gw = gemm_make(p.P, D, int64_t(BL), dtype ? (const void*)a.gstack_bf : (const void*)a.gstack, dtype, p.P,
                       1, u, dtype, D, 1, gW_cat, 0, D);

@@ -197,6 +197,31 @@ def test_lm_head_ce_f32(ops, T, V, d):
     assert_close(gh, rgh, name="grad_h")
 
 
+@pytest.mark.parametrize("T,V,d", [(300, 1000, 64), (1000, 2051, 128), (2048, 50257, 256), (129, 130, 192)])
+def test_lm_head_ce_bf16_fused(ops, T, V, d):
+    """bf16 LM head + CE backward (the fused G / dh kernel for d <= 256) against float64 on the
+    same bf16-rounded inputs."""
+    g = _gen(19 + d)
+    h = torch.randn(T, d, generator=g).bfloat16()
+    W = 0.3 * torch.randn(V, d, generator=g)
+    tg = torch.randint(0, V, (T,), generator=g)
+    tg[:4] = torch.tensor([0, V - 1, min(127, V - 1), min(128, V - 1)])  # tile edges
+    loss_rows, lse = ops.lm_head_ce_fwd(h.to(DEV), W.to(DEV), tg.to(DEV))
+    Wb = W.bfloat16().double()
+    logits = h.double() @ Wb.t()
+    assert_close(lse, torch.logsumexp(logits, -1), atol=1e-3, rtol=1e-4, name="lse")
+    loss, gl = O.ce_loss_and_grad(logits, tg)
+    gW, gh = ops.lm_head_ce_bwd(h.to(DEV), W.to(DEV), tg.to(DEV), lse, 1.0 / T)
+    rgW, rgh = O.lm_head_grad(h.double(), gl, Wb)
+    assert gh.dtype == torch.bfloat16
+    assert rel_err(gW, rgW) < 1e-2, rel_err(gW, rgW)
+    assert rel_err(gh, rgh) < 1e-2, rel_err(gh, rgh)
+    gW2, gh2 = ops.lm_head_ce_bwd(h.to(DEV), W.to(DEV), tg.to(DEV), lse, 1.0 / T)
+    assert torch.equal(gW, gW2) and torch.equal(gh, gh2), "deterministic"
+    from icml_b200._lib import lib
+    assert lib().pgf_tc_fault() == 0
+
+
 # ----------------------------------------------------------------------------- selective scan
 def _ssm_case(Bsz, L, D, seed, carries=True):
     g = _gen(seed)
