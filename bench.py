@@ -78,8 +78,6 @@ def config_of(a, world):
         "ssm_variant": ("reference (d_inner = d_model, shared A)" if a.variant == "reference" else
                         "mamba-standard (d_inner 2 d_model, conv1d, gate, per-channel A)"),
         "l2": "per-step working set (weights, optimizer state, activations) > 126 MB L2; no explicit flush",
-        "launch": ("whole step captured once as a CUDA graph, replayed each step" if world == 1 and not a.no_graph
-                   else "eager launches"),
     }
 
 
@@ -394,11 +392,28 @@ def run_gpu(a, rank, world, local_rank):
             prof_ms[nm] = t.value / n_prof
             prof_w[nm] = w.value / n_prof
 
-    # ---------------- the step as one CUDA graph (1 GPU; N > 1 launches eagerly)
+    # ---------------- the step (with its collectives on N GPUs) as one CUDA graph
     graphed = None
-    if world == 1 and not a.no_graph:
+    if not a.no_graph:
         from icml_b200.lm import GraphedStep
-        graphed = GraphedStep(model, inp, tgt, warmup=1)
+        barrier()
+        err = None
+        try:
+            graphed = GraphedStep(step, inp, tgt, warmup=1)
+        except Exception as e:  # capture refused: every rank falls back to eager launches together
+            err = e
+            graphed = None
+        ok = torch.tensor([0 if err else 1], device=dev, dtype=torch.int32)
+        if pg is not None:
+            torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            if graphed is not None:
+                graphed.release()
+                graphed = None
+            if rank == 0:
+                print(f"[bench] CUDA-graph capture unavailable ({err}); timing eager launches", file=sys.stderr)
+        barrier()
+    if graphed is not None:
         run_step = lambda x, y: graphed.run(x, y)  # noqa: E731
         launches = graphed.launches
     else:
@@ -462,7 +477,9 @@ def run_gpu(a, rank, world, local_rank):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": a.dtype, "data": "synthetic (Zipf 1.1 token ids, random init)",
-            "config": config_of(a, world), "impl": "b200",
+            "config": dict(config_of(a, world), launch=(
+                "whole step (with its collectives) captured once as a CUDA graph, replayed each step"
+                if graphed is not None else "eager launches")), "impl": "b200",
             "peak_hbm_gb": peak_gb, "loss": loss_val, "clocks": clocks,
             "e2e": {"value": e2e, "unit": UNIT,
                     "h2d_bytes_per_step": inp_host.numel() * 8 * 2, "d2h_bytes_per_step": 4},
@@ -474,6 +491,10 @@ def run_gpu(a, rank, world, local_rank):
         if world == 1 and not a.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(a)
         print(json.dumps(line), flush=True)
+    if graphed is not None:
+        torch.cuda.synchronize()
+        graphed.release()  # the graph holds NCCL work on N GPUs: release it before the process group
+        del graphed
     if pg is not None:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -32,16 +32,23 @@
 
 namespace pgf {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64;
-constexpr int TC_STAGES = 4;
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64;  // TC_BN: the CE modes' (and narrow outputs') tile width
 constexpr int TC_THREADS = 320;  // TMA warp, MMA warp, 8 epilogue warps
 constexpr int TILE_A_BYTES = TC_BM * TC_BK * 2;
-constexpr int TILE_B_BYTES = TC_BN * TC_BK * 2;
-constexpr int STAGE_BYTES = TILE_A_BYTES + TILE_B_BYTES;
 constexpr int EPI_WARP_BYTES = 8192;        // per epilogue warp: two 4 KB staging rows-of-128B buffers
 constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;  // (the transpose path uses the first 32x33 floats)
-constexpr uint32_t TMEM_COLS = 256;        // two 128-column fp32 accumulators
-constexpr size_t TC_SMEM = size_t(TC_STAGES) * STAGE_BYTES + EPI_BYTES + 256 /* barriers */ + 1024 /* align */;
+
+// Tile width BN = 128 or 256 output columns.  At N = 256 a K = 16 MMA reads 12 KB of operands for
+// 1 MFLOP (8 KB for 0.5 MFLOP at N = 128), which keeps the tensor pipe ahead of the operand reads;
+// the price is three stages instead of four and all 512 TMEM columns (two accumulators).
+template <int BN>
+struct TcCfg {
+  static constexpr int TILE_B = BN * TC_BK * 2;
+  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr int STAGE = TILE_A_BYTES + TILE_B;
+  static constexpr uint32_t TMEM = 2 * BN;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE + EPI_BYTES + 256 /* barriers */ + 1024 /* align */;
+};
 
 enum { TC_GENERIC = 0, TC_CE_FWD = 1, TC_CE_BWD = 2 };
 
@@ -72,25 +79,27 @@ struct TcParams {
   float* tgt_logit;        // (M,)  CE_FWD
 };
 
+template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmZ, const TcParams p) {
+  using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  float* epi_buf = reinterpret_cast<float*>(tiles + TC_STAGES * STAGE_BYTES);
+  float* epi_buf = reinterpret_cast<float*>(tiles + C::STAGES * C::STAGE);
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi_buf) + EPI_BYTES);
-  uint64_t* empty = full + TC_STAGES;
-  uint64_t* tfull = empty + TC_STAGES;
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = int((p.K + TC_BK - 1) / TC_BK);
-  const int n_tiles = int((p.N + TC_BN - 1) / TC_BN);
+  const int n_tiles = int((p.N + BN - 1) / BN);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -104,7 +113,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(tslot)), "r"(TMEM_COLS));
+                 ::"r"(smem_u32(tslot)), "r"(C::TMEM));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -124,12 +133,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int m0 = mb * TC_BM;
         const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
         for (int nt = nt0; nt < nt1 && ok; ++nt) {
-          const int n0 = nt * TC_BN;
+          const int n0 = nt * BN;
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
-            const int s = int(it % TC_STAGES), r = int(it / TC_STAGES);
+            const int s = int(it % C::STAGES), r = int(it / C::STAGES);
             if (r > 0 && !mbar_wait(&empty[s], uint32_t((r - 1) & 1))) { ok = false; break; }
-            mbar_expect_tx(&full[s], STAGE_BYTES);
-            uint8_t* sa = tiles + s * STAGE_BYTES;
+            mbar_expect_tx(&full[s], C::STAGE);
+            uint8_t* sa = tiles + s * C::STAGE;
             uint8_t* sb = sa + TILE_A_BYTES;
             const int k0 = kb * TC_BK;
             if (!p.a_mn) {
@@ -141,8 +150,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (!p.b_mn) {
               tma_load_2d(sb, &tmB, &full[s], k0, n0);
             } else {
-              tma_load_2d(sb, &tmB, &full[s], n0, k0);
-              tma_load_2d(sb + TILE_B_BYTES / 2, &tmB, &full[s], n0 + 64, k0);
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i) tma_load_2d(sb + i * 8192, &tmB, &full[s], n0 + 64 * i, k0);
             }
           }
         }
@@ -152,7 +161,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       // ---- MMA issuer
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(p.a_mn) << 15) |
-                             (uint32_t(p.b_mn) << 16) | (uint32_t(TC_BN >> 3) << 17) |
+                             (uint32_t(p.b_mn) << 16) | (uint32_t(BN >> 3) << 17) |
                              (uint32_t(TC_BM >> 4) << 24);
       uint32_t it = 0, tt = 0;
       bool ok = true;
@@ -164,12 +173,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t buf = tt & 1, use = tt >> 1;
           if (use > 0 && !mbar_wait(&tempty[buf], (use - 1) & 1)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t dcol = tmem + buf * TC_BN;
+          const uint32_t dcol = tmem + buf * BN;
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
-            const int s = int(it % TC_STAGES), r = int(it / TC_STAGES);
+            const int s = int(it % C::STAGES), r = int(it / C::STAGES);
             if (!mbar_wait(&full[s], uint32_t(r & 1))) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_base = smem_u32(tiles + s * STAGE_BYTES);
+            const uint32_t a_base = smem_u32(tiles + s * C::STAGE);
             const uint32_t b_base = a_base + TILE_A_BYTES;
 #pragma unroll
             for (int kk = 0; kk < TC_BK / 16; ++kk) {
@@ -177,7 +186,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               // MN-major: advance 16 k-rows (2 KB), two 8-row atoms apart by SBO = 1 KB.
               const uint64_t ad = p.a_mn ? sdesc(a_base + kk * 2048, TILE_A_BYTES / 2, 1024)
                                          : sdesc(a_base + kk * 32, 16, 1024);
-              const uint64_t bd = p.b_mn ? sdesc(b_base + kk * 2048, TILE_B_BYTES / 2, 1024)
+              const uint64_t bd = p.b_mn ? sdesc(b_base + kk * 2048, 8192, 1024)
                                          : sdesc(b_base + kk * 32, 16, 1024);
               umma_bf16(dcol, ad, bd, idesc, (kb != kb0) || (kk != 0));
             }
@@ -214,20 +223,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       for (int nt = nt0; nt < nt1; ++nt, ++tt) {
         const uint32_t buf = tt & 1, use = tt >> 1;
-        if (!mbar_wait(&tfull[buf], use & 1)) { ok = false; break; }
+        if (!mbar_wait_warp(&tfull[buf], use & 1)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int64_t n0 = int64_t(nt) * TC_BN;
+        const int64_t n0 = int64_t(nt) * BN;
         if (p.fast) {
-          // ---- row-per-thread epilogue: this thread owns row `row`, columns nh .. nh+63
-          const int64_t nh = n0 + hf * 64;
+          // ---- row-per-thread epilogue: this thread owns row `row` and the warp's BN/2 columns,
+          //      taken 64 at a time (nh .. nh+63)
           const int64_t row0 = int64_t(mb) * TC_BM + q * 32;
           const bool box_live = row0 < p.M;  // rows of this quarter exist (TMA clips the rest)
+#pragma unroll 1
+          for (int g64 = 0; g64 < BN / 128; ++g64) {
+          const int64_t nh = n0 + hf * (BN / 2) + g64 * 64;
+          const uint32_t tcol = uint32_t(hf * (BN / 2) + g64 * 64);
           uint32_t dpk[32], zpk[32];          // bf16 pairs of D / aux_out for the 64 columns
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t r[32];
-            tmem_ld32(tmem + buf * TC_BN + (uint32_t(q * 32) << 16) + uint32_t(hf * 64 + c * 32), r);
-            if (c == 1) {
+            tmem_ld32(tmem + buf * BN + (uint32_t(q * 32) << 16) + tcol + uint32_t(c * 32), r);
+            if (c == 1 && g64 == BN / 128 - 1) {
               // both chunks are in registers: hand the accumulator back to the MMA warp
               asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
               __syncwarp();
@@ -343,12 +356,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             stage_row(b, lane, zpk);
             stage_store(b, &tmZ, nh, row0, 0, lane);
           }
+          }  // g64
           continue;
         }
 #pragma unroll 1
-        for (int c = 2 * hf; c < 2 * hf + 2; ++c) {
+        for (int c = hf * (BN / 64); c < (hf + 1) * (BN / 64); ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + buf * TC_BN + (uint32_t(q * 32) << 16) + uint32_t(c * 32), r);
+          tmem_ld32(tmem + buf * BN + (uint32_t(q * 32) << 16) + uint32_t(c * 32), r);
           const int64_t nc = n0 + c * 32;
           if (p.mode == TC_CE_FWD) {
             // online log-sum-exp in base 2: exp(v - m) = exp2(v log2e - m log2e)
@@ -431,7 +445,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM));
   }
 }
 
@@ -474,25 +488,35 @@ bool tc_usable(const Gemm& g) {
 }
 
 // Launch over the whole (M x N) output with the given mode; `ng` = column tiles per work unit.
-static int launch_tc(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
+// Tile width of a launch: 256 columns for generic products whose width pads no further at 256
+// than at 128 (N mod 256 = 0 or > 128; PGF_TC_BN128=1 keeps 128), else 128; the cross-entropy
+// modes always use 128.
+static int tile_bn(int mode, int64_t N) {
+  static int force128 = -1;
+  if (force128 < 0) {
+    const char* e = getenv("PGF_TC_BN128");
+    force128 = (e && e[0] == '1') ? 1 : 0;
+  }
+  if (force128 || N <= 128) return 128;
+  if (mode == TC_CE_FWD) return 256;  // no stored output: the wider tile only saves operand reads
+  const bool wide = ((N + 255) / 256) * 256 <= ((N + 127) / 128) * 128;
+  return (mode == TC_GENERIC && wide) ? 256 : 128;
+}
+
+template <int BN>
+static int launch_tc_bn(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
+  using C = TcCfg<BN>;
   CUtensorMap ma, mb;
   const bool oka = g.a_trans ? make_map(&ma, g.A, g.M, g.K, g.lda, 64, 64)
                              : make_map(&ma, g.A, g.K, g.M, g.lda, 64, TC_BM);
   const bool okb = g.b_trans ? make_map(&mb, g.B, g.N, g.K, g.ldb, 64, 64)
-                             : make_map(&mb, g.B, g.K, g.N, g.ldb, 64, TC_BN);
+                             : make_map(&mb, g.B, g.K, g.N, g.ldb, 64, BN);
   if (!oka || !okb) return PGF_ERR_UNSUPPORTED;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TC_SMEM));
-  });
-  if (attr_err != cudaSuccess) {
-    set_error("gemm_tc: smem attribute: %s", cudaGetErrorString(attr_err));
-    return PGF_ERR_CUDA;
-  }
+  static int smem_limit = 0;
+  PGF_CUDA(ensure_dynamic_smem(gemm_tc_kernel<BN>, C::SMEM, smem_limit));
   p.M = g.M; p.N = g.N; p.K = g.K;
   p.a_mn = g.a_trans; p.b_mn = g.b_trans;
-  const int64_t n_tiles = (g.N + TC_BN - 1) / TC_BN;
+  const int64_t n_tiles = (g.N + BN - 1) / BN;
   const int64_t m_blocks = (g.M + TC_BM - 1) / TC_BM;
   const int nk = int((g.K + TC_BK - 1) / TC_BK);
   p.n_groups = int((n_tiles + p.ng - 1) / p.ng);
@@ -521,12 +545,25 @@ static int launch_tc(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
     }
     p.fast = ok ? 1 : 0;
   }
+  // 256-wide tiles: generic products through the TMA-store epilogue, and the CE forward (no stored
+  // output); the transpose epilogue is only used at 128
+  if (BN == 256 && ((p.mode == TC_GENERIC && !p.fast) || p.mode == TC_CE_BWD)) return PGF_ERR_UNSUPPORTED;
   const int64_t grid = p.units < sm_count() ? p.units : sm_count();
   prof_begin(prof_id, s);
-  gemm_tc_kernel<<<unsigned(grid), TC_THREADS, TC_SMEM, s>>>(ma, mb, md, mz, p);
+  gemm_tc_kernel<BN><<<unsigned(grid), TC_THREADS, C::SMEM, s>>>(ma, mb, md, mz, p);
   prof_end(prof_id, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
+}
+
+static int launch_tc(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
+  if (tile_bn(p.mode, g.N) == 256) {
+    TcParams q = p;
+    const int rc = launch_tc_bn<256>(g, q, s, prof_id);
+    if (rc != PGF_ERR_UNSUPPORTED) return rc;
+    clear_error();
+  }
+  return launch_tc_bn<128>(g, p, s, prof_id);
 }
 
 int run_gemm_tc(const Gemm& g, cudaStream_t s) {
@@ -541,7 +578,8 @@ int run_gemm_tc(const Gemm& g, cudaStream_t s) {
 }
 
 int split_slices_tc(int64_t M, int64_t N, int64_t K) {
-  const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+  const int bn = tile_bn(TC_GENERIC, N);
+  const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn);
   const int64_t nk = (K + TC_BK - 1) / TC_BK;
   const int64_t sm = sm_count();
   if (tiles * 2 > sm) return 1;
@@ -574,9 +612,20 @@ int tc_ce_fwd(const Gemm& g, int ng, const int64_t* targets, float* part_m, floa
   p.ng = ng;
   p.targets = targets;
   p.part_m = part_m; p.part_s = part_s; p.tgt_logit = tgt_logit;
+  // `ng` counts 128-wide tiles; a 256-wide launch covers the same columns per unit with ng / 2
+  const int bn = tile_bn(TC_CE_FWD, g.N);
+  if (bn == 256) {
+    TcParams q = p;
+    q.ng = ng / 2 > 0 ? ng / 2 : 1;
+    const int64_t n_tiles = (g.N + 255) / 256;
+    *n_groups_out = 2 * int((n_tiles + q.ng - 1) / q.ng);  // two column halves per unit
+    const int rc = launch_tc_bn<256>(g, q, s, PROF_CE);
+    if (rc != PGF_ERR_UNSUPPORTED) return rc;
+    clear_error();
+  }
   const int64_t n_tiles = (g.N + TC_BN - 1) / TC_BN;
   *n_groups_out = 2 * int((n_tiles + ng - 1) / ng);  // two column halves per unit
-  return launch_tc(g, p, s, PROF_CE);
+  return launch_tc_bn<128>(g, p, s, PROF_CE);
 }
 
 int tc_ce_bwd(const Gemm& g, const int64_t* targets, const float* lse, float scale, __nv_bfloat16* G,

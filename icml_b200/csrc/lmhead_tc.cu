@@ -182,7 +182,7 @@ ce_bwd_dh_kernel(const __grid_constant__ CUtensorMap tmH, const __grid_constant_
       const float ll = row_ok ? p.lse[row] * L2E : 0.f;
       for (int j = 0; j < p.n_tiles; ++j, ++tt) {
         const uint32_t buf = tt & 1, use = tt >> 1;
-        if (!mbar_wait(&tfull[buf], use & 1)) { ok = false; break; }
+        if (!mbar_wait_warp(&tfull[buf], use & 1)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         uint32_t r0[32], r1[32];
         const uint32_t ta = tmem + buf * BV + (uint32_t(q * 32) << 16) + uint32_t(hf * 64);
@@ -211,7 +211,7 @@ ce_bwd_dh_kernel(const __grid_constant__ CUtensorMap tmH, const __grid_constant_
         }
         // the G tile is free once the dh product of the previous tile is done and the previous
         // TMA store has read it
-        if (tt > 0 && !mbar_wait(gfree, (tt - 1) & 1)) { ok = false; break; }
+        if (tt > 0 && !mbar_wait_warp(gfree, (tt - 1) & 1)) { ok = false; break; }
         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         __syncwarp();
         uint8_t* gb = sG + hf * 16384 + q * 4096;
@@ -231,7 +231,7 @@ ce_bwd_dh_kernel(const __grid_constant__ CUtensorMap tmH, const __grid_constant_
       }
       if (!ok) break;
       // the unit's dh: TMEM lanes of this warp, columns hf * d/2 .. (bf16, 16-byte stores)
-      if (!mbar_wait(dhdone, uu & 1)) { ok = false; break; }
+      if (!mbar_wait_warp(dhdone, uu & 1)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int half = p.d / 2;
       for (int c = 0; c < half; c += 32) {

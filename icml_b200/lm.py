@@ -122,8 +122,8 @@ class PGFLanguageModel:
 
 
 class GraphedStep:
-    """One whole training step (embedding, PGF forward/backward of every layer, LM head + CE, AdamW)
-    captured once as a CUDA graph and replayed.
+    """One whole training step (embedding, PGF forward/backward of every layer, LM head + CE, AdamW,
+    and, on several GPUs, the step's NCCL collectives) captured once as a CUDA graph and replayed.
 
     The step launches about a thousand kernels; replaying them as one graph removes the host's
     per-launch work (Python, ctypes, the launch API), which otherwise sets the pace whenever the
@@ -131,13 +131,17 @@ class GraphedStep:
     the step's ids and targets into them (from pinned host memory or the device), replays the
     graph and returns the loss tensor, whose storage is reused by the next replay.  Construction
     runs ``warmup`` eager steps (real training steps) on a side stream first, as capture requires
-    the optimizer state and every workspace size to be settled.
+    the optimizer state, the collectives' communicators and every workspace size to be settled.
+
+    ``step`` is ``model`` (its ``step(x, y)``) or any callable ``(x, y) -> loss`` (e.g. a sequence-
+    sharded or data-parallel step; every rank must capture the same collectives in the same order).
+    Delete the object (``release()``) before destroying a process group whose collectives it holds.
     """
 
-    def __init__(self, model: PGFLanguageModel, input_ids: torch.Tensor, targets: torch.Tensor, warmup: int = 2):
+    def __init__(self, step, input_ids: torch.Tensor, targets: torch.Tensor, warmup: int = 2):
         from ._lib import lib
-        dev = model.device
-        self.model = model
+        fn = step.step if isinstance(step, PGFLanguageModel) else step
+        dev = input_ids.device if input_ids.is_cuda else torch.device("cuda", torch.cuda.current_device())
         self.x = torch.empty_like(input_ids, device=dev)
         self.y = torch.empty_like(targets, device=dev)
         self.x.copy_(input_ids)
@@ -146,13 +150,13 @@ class GraphedStep:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(warmup):
-                model.step(self.x, self.y)
+                fn(self.x, self.y)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         n0 = lib().pgf_launch_count()
         with torch.cuda.graph(self.graph):
-            self.loss = model.step(self.x, self.y)
+            self.loss = fn(self.x, self.y)
         self.launches = int(lib().pgf_launch_count() - n0)  # libpgf kernels per replay
 
     def run(self, input_ids: Optional[torch.Tensor] = None, targets: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -162,6 +166,10 @@ class GraphedStep:
             self.y.copy_(targets, non_blocking=True)
         self.graph.replay()
         return self.loss
+
+    def release(self) -> None:
+        self.graph.reset()
+        self.loss = None
 
 
 __all__ = ["PGFLanguageModel", "GraphedStep"]
