@@ -29,7 +29,8 @@ if ROOT not in sys.path:
 
 import torch  # noqa: E402
 
-METRIC = "fwd+bwd tokens/s (8-layer PGF Mamba LM)"
+def metric_of(a) -> str:
+    return f"fwd+bwd tokens/s ({a.layers}-layer PGF Mamba LM)"
 UNIT = "tokens/s"
 
 
@@ -44,6 +45,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--d-model", type=int, default=256)
     ap.add_argument("--d-ff", type=int, default=1024)
+    ap.add_argument("--dt-rank", type=int, default=16, help="Mamba-standard variant: dt_proj rank")
     ap.add_argument("--vocab", type=int, default=50257)
     ap.add_argument("--block-size", type=int, default=4096)
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
@@ -66,9 +68,10 @@ def parse():
 
 def config_of(a, world):
     var = ("reference SSM variant" if a.variant == "reference" else
-           "Mamba-standard variant (d_inner 512, d_conv 4, dt_rank 16, final RMSNorm, tied head)")
+           f"Mamba-standard variant (d_inner {2 * a.d_model}, d_conv 4, dt_rank {a.dt_rank}, final RMSNorm, "
+           f"tied head)")
     return {
-        "workload": f"8-layer PGF Mamba LM ({var}), d_model {a.d_model}, d_state 16, d_ff {a.d_ff}, "
+        "workload": f"{a.layers}-layer PGF Mamba LM ({var}), d_model {a.d_model}, d_state 16, d_ff {a.d_ff}, "
                     f"vocab {a.vocab}, B={a.batch} x L={a.seq_len} tokens per GPU, {a.dtype} activations / "
                     f"fp32 weights + AdamW",
         "layers": a.layers, "d_model": a.d_model, "d_state": 16, "d_ff": a.d_ff, "vocab": a.vocab,
@@ -166,7 +169,7 @@ def run_reference(a, rank, world):
     if rank != 0:
         return
     cb = cpu_baseline(a)
-    line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world, "steps": a.steps,
+    line = {"metric": metric_of(a), "value": cb["value"], "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": 1000.0 * a.cpu_sample_len / cb["value"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference", "config": config_of(a, world),
@@ -312,7 +315,7 @@ def run_gpu(a, rank, world, local_rank):
     if a.variant == "std":
         model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act,
                                  variant="std", tie_embeddings=True, final_norm=True, expand=2, d_conv=4,
-                                 dt_rank=16)
+                                 dt_rank=a.dt_rank)
     else:
         model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act)
     for p in model.params:  # identical replicas
@@ -474,7 +477,7 @@ def run_gpu(a, rank, world, local_rank):
                        "roofline": roofline_entry(k, prof_ms[k], prof_n[k], prof_w[k])}
                    for k in prof_ms}
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "metric": metric_of(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": a.dtype, "data": "synthetic (Zipf 1.1 token ids, random init)",
             "config": dict(config_of(a, world), launch=(

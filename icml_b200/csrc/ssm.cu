@@ -56,6 +56,11 @@ struct SsmArgs {
   // states at the start of every ST-token sub-chunk, (Bsz, nC, Tc/ST, D, N): written by the output
   // pass when ckpt_write, read by the main backward kernel instead of its own forward pass
   float* ckpt_g; int ckpt_write;
+  // zero-start forward (chunk_y0 / out_corr): y0 = C h0 per (token, channel), float32 (Bsz, L, D);
+  // ckpt_s = sum of dt inside the chunk before each ST-token sub-chunk, (Bsz, nC, Tc/ST, D).  With
+  // them the saved checkpoints hold zero-start states h0, and a state is h0 + exp(A S) H_chunk.
+  float* y0;
+  float* ckpt_s;
 };
 
 // One staged sub-chunk: ST tokens x DC channels (+ the token's B and C rows).
@@ -266,6 +271,120 @@ __global__ void __launch_bounds__(32 * CSEG) ssm_compose_fwd_kernel(const SsmArg
   }
 }
 
+// Forward in two light passes instead of summary + full re-run.  The recurrence is linear in the
+// state: from the chunk's true start state H, h_t = h0_t + exp(A S_t) H with h0 the trajectory
+// from a zero state and S_t the sum of dt over the chunk's tokens up to t.  Pass 1 (this kernel)
+// runs the chunk from zero: its end state and sum of dt (the compose inputs), y0 = C h0 for every
+// token and, when checkpoints are kept, h0 and S at every sub-chunk start.  Pass 2
+// (ssm_out_corr_kernel) adds C_t (exp(A S_t) H) -- an exp2 and two FMAs per state instead of the
+// whole step -- and forms the output.
+__global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_y0_kernel(const SsmArgs a) {
+  __shared__ Stage stg[2];
+  __shared__ float ybuf[2][ST][DC];
+  const Lane l = lane_of(a);
+  const AConst K = load_A(a, l.nq);
+  float h[NS] = {0.f, 0.f, 0.f, 0.f}, e[NS];
+  float sdt = 0.f;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  const int KS = int((a.Tc + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s, false, r);
+  pref_store(r, l, false, stg[0]);
+  __syncthreads();
+  for (int k = 0; k < nsub; ++k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    if (a.ckpt_write && l.ch) {
+      const int64_t ck = (l.b * a.nC + l.c) * KS + k;
+      float* cp = a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS;
+#pragma unroll
+      for (int j = 0; j < NS; ++j) cp[j] = h[j];
+      if (l.nq == 0) a.ckpt_s[ck * a.D + l.d] = sdt;
+    }
+    const Stage& S = stg[k & 1];
+#pragma unroll
+    for (int i = 0; i < ST; ++i) {
+      if (l.s + int64_t(k) * ST + i < l.e) {
+        step_fwd(S, i, l.dl, l.nq, K, h, e);
+        sdt += S.dt[i][l.dl];
+        const float4 Cq = S.C[i][l.nq];
+        float yc = Cq.x * h[0];
+        yc = fmaf(Cq.y, h[1], yc);
+        yc = fmaf(Cq.z, h[2], yc);
+        yc = fmaf(Cq.w, h[3], yc);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 1);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 2);
+        if (l.nq == 0) ybuf[k & 1][i][l.dl] = yc;
+      }
+    }
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int idx = l.tid + q * SSM_THREADS;
+      const int t = idx / DC, dl = idx % DC;
+      const int64_t tok = l.s + int64_t(k) * ST + t;
+      const int64_t d = int64_t(l.grp) * DC + dl;
+      if (tok < l.e && d < a.D) a.y0[(l.b * a.L + tok) * a.D + d] = ybuf[k & 1][t][dl];
+    }
+  }
+  if (!l.ch) return;
+  const int64_t cb = l.b * a.nC + l.c;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) a.hloc[(cb * a.D + l.d) * NST + l.nq * NS + j] = h[j];
+  if (l.nq == 0) a.sdt[cb * a.D + l.d] = sdt;
+}
+
+// Pass 2 of the forward: y = (act(y0 + C_t (exp(A S_t) H)) + D u) scale, H the chunk's start state.
+__global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs a) {
+  __shared__ Stage stg[2];
+  __shared__ float ybuf[2][ST][DC];
+  const Lane l = lane_of(a);
+  const AConst K = load_A(a, l.nq);
+  float H[NS];
+#pragma unroll
+  for (int j = 0; j < NS; ++j)
+    H[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
+  float S_run = 0.f;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  Pref r;
+  pref_load(a, l, l.s, false, r);
+  pref_store(r, l, false, stg[0]);
+  __syncthreads();
+  for (int k = 0; k < nsub; ++k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    const Stage& S = stg[k & 1];
+#pragma unroll
+    for (int i = 0; i < ST; ++i) {
+      if (l.s + int64_t(k) * ST + i < l.e) {
+        S_run += S.dt[i][l.dl];
+        const float4 Cq = S.C[i][l.nq];
+        float yc = Cq.x * (exp2f(K.A2[0] * S_run) * H[0]);
+        yc = fmaf(Cq.y, exp2f(K.A2[1] * S_run) * H[1], yc);
+        yc = fmaf(Cq.z, exp2f(K.A2[2] * S_run) * H[2], yc);
+        yc = fmaf(Cq.w, exp2f(K.A2[3] * S_run) * H[3], yc);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 1);
+        yc += __shfl_xor_sync(0xffffffffu, yc, 2);
+        if (l.nq == 0) ybuf[k & 1][i][l.dl] = yc;
+      }
+    }
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int idx = l.tid + q * SSM_THREADS;
+      const int t = idx / DC, dl = idx % DC;
+      const int64_t tok = l.s + int64_t(k) * ST + t;
+      const int64_t d = int64_t(l.grp) * DC + dl;
+      if (tok < l.e && d < a.D) {
+        const int64_t o = (l.b * a.L + tok) * a.D + d;
+        // u from global memory: the stage of this sub-chunk may already be refilled by faster threads
+        const float yc = a.y0[o] + ybuf[k & 1][t][dl];
+        stv(a.y, a.y_bf16, o, (act_apply(a.act, yc) + a.Dp[d] * ldv(a.u, a.u_bf16, o)) * a.scale[d]);
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs a) {
   __shared__ Stage stg[2];
   __shared__ float ybuf[2][ST][DC];
@@ -424,7 +543,7 @@ __global__ void __launch_bounds__(32 * CSEG) ssm_compose_bwd_kernel(const SsmArg
 
 // Main backward kernel.  Shared memory (dynamic): ckpt [Tc/ST][SSM_THREADS][NS] floats, then
 // red [ST][SSM_WARPS][32], then gbuf [2][ST][DC] (grad_dt_in, grad_u_scan of the sub-chunk).
-__global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs a) {
+__global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmArgs a) {
   extern __shared__ float sm[];
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
@@ -478,9 +597,13 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_main_bwd_kernel(const SsmArgs
     // re-run the sub-chunk into registers: tr[i] = state before token i, ex[i] = exp(dt_i A)
     float tr[ST + 1][NS], ex[ST][NS];
     if (saved) {
-      const float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.D + l.d) * NST + l.nq * NS;
+      // zero-start checkpoint h0 of the forward, moved onto the chunk's start state h (= hC):
+      // state = h0 + exp(A S) h, S = sum of dt in the chunk before this sub-chunk
+      const int64_t ck = (l.b * a.nC + l.c) * KS + k;
+      const float* cp = a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS;
+      const float Sk = l.ch ? a.ckpt_s[ck * a.D + l.d] : 0.f;
 #pragma unroll
-      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? cp[j] : 0.f;
+      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? fmaf(exp2f(K.A2[j] * Sk), h[j], cp[j]) : 0.f;
     } else {
 #pragma unroll
       for (int j = 0; j < NS; ++j) tr[0][j] = ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j];
@@ -685,6 +808,7 @@ static size_t ssm_ws(const SsmPlan& p, int dtype, int backward, int act) {
   const size_t BL = size_t(p.Bsz) * p.L;
   size_t b = 0;
   b += Workspace::round(BL * p.P * 4);                                  // proj
+  b += Workspace::round(BL * p.D * 4);                                  // y0 (forward)
   b += Workspace::round(size_t(p.Bsz) * p.nC * p.D * NST * 4);          // hloc
   b += Workspace::round(size_t(p.Bsz) * p.nC * p.D * 4);                // sdt
   b += Workspace::round(size_t(p.Bsz) * (p.nC + 1) * p.D * NST * 4);    // hC
@@ -707,10 +831,11 @@ static size_t ssm_ws(const SsmPlan& p, int dtype, int backward, int act) {
 
 // Floats of the saved-state buffer: boundary states, then the sub-chunk checkpoints.
 static size_t saved_hc_floats(const SsmPlan& p) { return size_t(p.Bsz) * (p.nC + 1) * p.D * NST; }
-static size_t saved_floats(const SsmPlan& p) {
-  const size_t KS = size_t((p.Tc + ST - 1) / ST);
-  return saved_hc_floats(p) + size_t(p.Bsz) * p.nC * KS * p.D * NST;
+static size_t saved_ckpt_floats(const SsmPlan& p) {
+  return size_t(p.Bsz) * p.nC * size_t((p.Tc + ST - 1) / ST) * p.D * NST;
 }
+static size_t saved_s_floats(const SsmPlan& p) { return size_t(p.Bsz) * p.nC * size_t((p.Tc + ST - 1) / ST) * p.D; }
+static size_t saved_floats(const SsmPlan& p) { return saved_hc_floats(p) + saved_ckpt_floats(p) + saved_s_floats(p); }
 
 static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u, int dtype,
                       const float* W_cat, const float* b_cat, const void** wcat_op, cudaStream_t s,
@@ -796,17 +921,29 @@ static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, c
   a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act; a.h_init = h_init;
   const void* wop;
   PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved));
-  PGF_TRY(ssm_forward_states(a, p, h_final, s));
+  a.y0 = W.take<float>(size_t(Bsz) * L * D);
+  if (!a.y0) { set_error("ssm_fwd: workspace too small (%zu)", ws_bytes); return PGF_ERR_WORKSPACE; }
   a.y = y;
   a.y_bf16 = dtype;
   if (saved) {
     a.ckpt_g = saved + saved_hc_floats(p);
+    a.ckpt_s = a.ckpt_g + saved_ckpt_floats(p);
     a.ckpt_write = 1;
   }
+  // zero-start pass (y0, summaries, checkpoints), chunk start states, then the output correction
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  prof_begin(PROF_SSM_CHUNK_FWD, s);
+  ssm_chunk_y0_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_CHUNK_FWD, s, bytes_chunk_fwd(a, a.u_bf16 ? 2 : 4) + double(Bsz) * L * D * 4.0);
+  PGF_LAUNCH_CHECK();
+  const int64_t nth = p.Bsz * p.D * NST;
+  prof_begin(PROF_SSM_COMPOSE, s);
+  ssm_compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, h_final, nullptr);
+  prof_end(PROF_SSM_COMPOSE, s, bytes_compose(a));
+  PGF_LAUNCH_CHECK();
   prof_begin(PROF_SSM_OUT_FWD, s);
-  ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
-  prof_end(PROF_SSM_OUT_FWD, s, bytes_out_fwd(a, a.u_bf16 ? 2 : 4));
+  ssm_out_corr_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_OUT_FWD, s, bytes_out_fwd(a, a.u_bf16 ? 2 : 4) + double(Bsz) * L * D * 4.0);
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
@@ -888,7 +1025,10 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
     ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);  // act'(C h) per token and channel
     PGF_LAUNCH_CHECK();
   }
-  if (saved) a.ckpt_g = const_cast<float*>(saved) + saved_hc_floats(p);
+  if (saved) {
+    a.ckpt_g = const_cast<float*>(saved) + saved_hc_floats(p);
+    a.ckpt_s = a.ckpt_g + saved_ckpt_floats(p);
+  }
   prof_begin(PROF_SSM_CHUNK_BWD, s);
   ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
   prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
