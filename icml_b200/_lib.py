@@ -73,6 +73,10 @@ SIGNATURES = {
     "pgf_ssm_fwd_save": (c_int, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P, c_size_t, P]),
     "pgf_ssm_bwd_saved": (c_int, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, I64, I64,
                                   I64, I64, c_int, c_int, P, c_size_t, P]),
+    "pgf_ssm_fwd_begin": (c_int, [P] * 6 + [I64] * 4 + [c_int, P, c_size_t, P]),
+    "pgf_ssm_fwd_finish": (c_int, [P] * 9 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
+    "pgf_ssm_bwd_begin": (c_int, [P] * 11 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
+    "pgf_ssm_bwd_finish": (c_int, [P] * 19 + [c_int] + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
     "pgf_mamba_mixer_workspace": (c_size_t, [I64, I64, I64, I64, I64, I64, I64, c_int, c_int]),
     "pgf_mamba_mixer_fwd": (c_int, [P] * 11 + [I64] * 7 + [c_int, P, c_size_t, P]),
     "pgf_mamba_mixer_bwd": (c_int, [P] * 21 + [c_int] + [I64] * 7 + [c_int, P, c_size_t, P]),

@@ -837,9 +837,12 @@ static size_t saved_ckpt_floats(const SsmPlan& p) {
 static size_t saved_s_floats(const SsmPlan& p) { return size_t(p.Bsz) * p.nC * size_t((p.Tc + ST - 1) / ST) * p.D; }
 static size_t saved_floats(const SsmPlan& p) { return saved_hc_floats(p) + saved_ckpt_floats(p) + saved_s_floats(p); }
 
+// Carves the buffers every pass shares (projection, chunk summaries, start states, bf16 W_cat) in a
+// fixed order, and -- when `fill` -- computes the projection and the bf16 weights.  A staged call
+// (begin / finish on one workspace) carves the same layout again with fill = false.
 static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u, int dtype,
                       const float* W_cat, const float* b_cat, const void** wcat_op, cudaStream_t s,
-                      float* hC_ext = nullptr) {
+                      float* hC_ext = nullptr, bool fill = true) {
   const size_t BL = size_t(p.Bsz) * p.L;
   a.Bsz = p.Bsz; a.L = p.L; a.D = p.D; a.P = p.P; a.Tc = p.Tc; a.nC = p.nC; a.G = p.G;
   a.u = u; a.u_bf16 = dtype;
@@ -855,10 +858,11 @@ static int ssm_common(SsmArgs& a, const SsmPlan& p, Workspace& W, const void* u,
   a.proj = proj;
   const void* w = W_cat;
   if (dtype) {
-    PGF_TRY(to_bf16(W_cat, wb, p.P * p.D, s));
+    if (fill) PGF_TRY(to_bf16(W_cat, wb, p.P * p.D, s));
     w = wb;
   }
   *wcat_op = w;
+  if (!fill) return PGF_OK;
   // proj = u W_cat^T + b_cat   (train_singlemamba_optimized.py:116-124)
   Gemm g = gemm_make(int64_t(BL), p.P, p.D, u, dtype, p.D, 0, w, dtype, p.D, 0, proj, 0, p.P);
   g.epi.bias = b_cat;
@@ -901,26 +905,35 @@ extern "C" size_t pgf_ssm_workspace(int64_t Bsz, int64_t L, int64_t D, int64_t N
 }
 
 namespace pgf {
+// Forward stages: ALL (one call), BEGIN (projection, zero-start pass, summary of the segment from a
+// zero start into h_out / sum_dt), FINISH (on BEGIN's workspace: start states from h_init, output).
+enum { STAGE_ALL = 0, STAGE_BEGIN = 1, STAGE_FINISH = 2 };
+
 static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
                         const float* Dp, const float* scale, const float* h_init, void* y,
                         float* h_final, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act,
-                        int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream, float* saved) {
+                        int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream, float* saved,
+                        int stage = STAGE_ALL, float* sum_dt = nullptr) {
   PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
-  PGF_CHECK_ARG(u && W_cat && b_cat && A_log && Dp && scale && y, "ssm_fwd: null pointer");
+  PGF_CHECK_ARG(u && W_cat && b_cat && A_log, "ssm_fwd: null pointer");
+  PGF_CHECK_ARG(stage == STAGE_BEGIN || (Dp && scale && y), "ssm_fwd: null pointer");
   cudaStream_t s = as_stream(stream);
   if (L == 0) {
     if (h_final) {
-      if (h_init) PGF_CUDA(cudaMemcpyAsync(h_final, h_init, Bsz * D * NST * 4, cudaMemcpyDeviceToDevice, s));
+      if (h_init && stage != STAGE_BEGIN)
+        PGF_CUDA(cudaMemcpyAsync(h_final, h_init, Bsz * D * NST * 4, cudaMemcpyDeviceToDevice, s));
       else PGF_CUDA(cudaMemsetAsync(h_final, 0, Bsz * D * NST * 4, s));
     }
+    if (sum_dt) PGF_CUDA(cudaMemsetAsync(sum_dt, 0, Bsz * D * 4, s));
     return PGF_OK;
   }
   SsmPlan p = plan_of(Bsz, L, D);
   Workspace W(ws, ws_bytes);
   SsmArgs a = {};
-  a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act; a.h_init = h_init;
+  a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act;
+  a.h_init = stage == STAGE_BEGIN ? nullptr : h_init;
   const void* wop;
-  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved));
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved, stage != STAGE_FINISH));
   a.y0 = W.take<float>(size_t(Bsz) * L * D);
   if (!a.y0) { set_error("ssm_fwd: workspace too small (%zu)", ws_bytes); return PGF_ERR_WORKSPACE; }
   a.y = y;
@@ -930,17 +943,21 @@ static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, c
     a.ckpt_s = a.ckpt_g + saved_ckpt_floats(p);
     a.ckpt_write = 1;
   }
-  // zero-start pass (y0, summaries, checkpoints), chunk start states, then the output correction
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
-  prof_begin(PROF_SSM_CHUNK_FWD, s);
-  ssm_chunk_y0_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
-  prof_end(PROF_SSM_CHUNK_FWD, s, bytes_chunk_fwd(a, a.u_bf16 ? 2 : 4) + double(Bsz) * L * D * 4.0);
-  PGF_LAUNCH_CHECK();
+  if (stage != STAGE_FINISH) {
+    // zero-start pass (y0, summaries, checkpoints): independent of the start state
+    prof_begin(PROF_SSM_CHUNK_FWD, s);
+    ssm_chunk_y0_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+    prof_end(PROF_SSM_CHUNK_FWD, s, bytes_chunk_fwd(a, a.u_bf16 ? 2 : 4) + double(Bsz) * L * D * 4.0);
+    PGF_LAUNCH_CHECK();
+  }
+  // chunk start states (from h_init; from zero in BEGIN, whose end state and sum of dt are the summary)
   const int64_t nth = p.Bsz * p.D * NST;
   prof_begin(PROF_SSM_COMPOSE, s);
-  ssm_compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, h_final, nullptr);
+  ssm_compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, h_final, stage == STAGE_BEGIN ? sum_dt : nullptr);
   prof_end(PROF_SSM_COMPOSE, s, bytes_compose(a));
   PGF_LAUNCH_CHECK();
+  if (stage == STAGE_BEGIN) return PGF_OK;
   prof_begin(PROF_SSM_OUT_FWD, s);
   ssm_out_corr_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
   prof_end(PROF_SSM_OUT_FWD, s, bytes_out_fwd(a, a.u_bf16 ? 2 : 4) + double(Bsz) * L * D * 4.0);
@@ -982,11 +999,12 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
                         float* gA_log, float* gDp, float* gscale, void* gu, float* dh_start,
                         float* dA_start, int accumulate, int64_t Bsz, int64_t L, int64_t D, int64_t N,
                         int act, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream,
-                        const float* saved) {
+                        const float* saved, int stage = STAGE_ALL, float* sum_dt_excl = nullptr) {
   PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
-  PGF_CHECK_ARG(u && g && W_cat && b_cat && A_log && Dp && scale && gW_cat && gb_cat && gA_log &&
-                    gDp && gscale && gu,
+  PGF_CHECK_ARG(u && g && W_cat && b_cat && A_log && scale, "ssm_bwd: null pointer");
+  PGF_CHECK_ARG(stage == STAGE_BEGIN || (Dp && gW_cat && gb_cat && gA_log && gDp && gscale && gu),
                 "ssm_bwd: null pointer");
+  PGF_CHECK_ARG(stage == STAGE_ALL || saved, "ssm_bwd: a staged backward needs the saved forward states");
   PGF_CHECK_ARG(L > 0, "ssm_bwd: empty sequence");
   cudaStream_t s = as_stream(stream);
   SsmPlan p = plan_of(Bsz, L, D);
@@ -995,7 +1013,7 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
   a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act; a.h_init = h_init;
   a.g = g; a.g_bf16 = dtype;
   const void* wop;
-  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, const_cast<float*>(saved)));
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, const_cast<float*>(saved), stage != STAGE_FINISH));
   const size_t BL = size_t(Bsz) * L;
   a.gstack = W.take<float>(BL * p.P);
   a.gstack_bf = dtype ? W.take<__nv_bfloat16>(BL * p.P) : nullptr;
@@ -1018,22 +1036,34 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
     set_error("ssm_bwd: workspace too small (%zu)", ws_bytes);
     return PGF_ERR_WORKSPACE;
   }
-  if (!saved) PGF_TRY(ssm_forward_states(a, p, nullptr, s));
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
-  if (act != PGF_ACT_NONE) {
-    a.y = nullptr;
-    ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);  // act'(C h) per token and channel
-    PGF_LAUNCH_CHECK();
+  if (stage != STAGE_FINISH) {
+    if (!saved) PGF_TRY(ssm_forward_states(a, p, nullptr, s));
+    if (act != PGF_ACT_NONE) {
+      a.y = nullptr;
+      ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);  // act'(C h) per token and channel
+      PGF_LAUNCH_CHECK();
+    }
   }
   if (saved) {
     a.ckpt_g = const_cast<float*>(saved) + saved_hc_floats(p);
     a.ckpt_s = a.ckpt_g + saved_ckpt_floats(p);
   }
-  prof_begin(PROF_SSM_CHUNK_BWD, s);
-  ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
-  prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
-  PGF_LAUNCH_CHECK();
+  if (stage != STAGE_FINISH) {
+    // reverse chunk summaries from a zero carry: independent of the carry entering from the right
+    prof_begin(PROF_SSM_CHUNK_BWD, s);
+    ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+    prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
+    PGF_LAUNCH_CHECK();
+  }
   const int64_t nth = Bsz * D * NST;
+  if (stage == STAGE_BEGIN) {
+    // the segment's adjoint summary from a zero end carry
+    ssm_compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, nullptr, nullptr, dh_start, dA_start,
+                                                              sum_dt_excl);
+    PGF_LAUNCH_CHECK();
+    return PGF_OK;
+  }
   ssm_compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, dh_end, dA_end, dh_start, dA_start,
                                                             nullptr);
   PGF_LAUNCH_CHECK();
@@ -1113,6 +1143,45 @@ extern "C" int pgf_ssm_summary(const void* u, const float* W_cat, const float* b
   const void* wop;
   PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s));
   return ssm_forward_states(a, p, h_final, s, sum_dt);
+}
+
+extern "C" int pgf_ssm_fwd_begin(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                                 float* h_seg, float* sum_dt, int64_t Bsz, int64_t L, int64_t D, int64_t N,
+                                 int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(h_seg && sum_dt, "ssm_fwd_begin: null pointer");
+  return ssm_fwd_impl(u, W_cat, b_cat, A_log, nullptr, nullptr, nullptr, nullptr, h_seg, Bsz, L, D, N, PGF_ACT_NONE,
+                      dtype, ws, ws_bytes, stream, nullptr, STAGE_BEGIN, sum_dt);
+}
+
+extern "C" int pgf_ssm_fwd_finish(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                                  const float* Dp, const float* scale, const float* h_init, void* y,
+                                  float* h_final, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype,
+                                  void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  return ssm_fwd_impl(u, W_cat, b_cat, A_log, Dp, scale, h_init, y, h_final, Bsz, L, D, N, act, dtype, ws,
+                      ws_bytes, stream, nullptr, STAGE_FINISH);
+}
+
+extern "C" int pgf_ssm_bwd_begin(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                                 const float* A_log, const float* scale, const float* h_init, const float* saved,
+                                 float* dh_start, float* dA_start, float* sum_dt_excl, int64_t Bsz, int64_t L,
+                                 int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                                 pgf_stream_t stream) {
+  PGF_CHECK_ARG(dh_start && dA_start && sum_dt_excl, "ssm_bwd_begin: null pointer");
+  return ssm_bwd_impl(u, g, W_cat, b_cat, A_log, nullptr, scale, h_init, nullptr, nullptr, nullptr, nullptr,
+                      nullptr, nullptr, nullptr, nullptr, dh_start, dA_start, 0, Bsz, L, D, N, act, dtype, ws,
+                      ws_bytes, stream, saved, STAGE_BEGIN, sum_dt_excl);
+}
+
+extern "C" int pgf_ssm_bwd_finish(const void* u, const void* g, const float* W_cat, const float* b_cat,
+                                  const float* A_log, const float* Dp, const float* scale, const float* h_init,
+                                  const float* saved, const float* dh_end, const float* dA_end, float* gW_cat,
+                                  float* gb_cat, float* gA_log, float* gDp, float* gscale, void* gu,
+                                  float* dh_start, float* dA_start, int accumulate, int64_t Bsz, int64_t L,
+                                  int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
+                                  pgf_stream_t stream) {
+  return ssm_bwd_impl(u, g, W_cat, b_cat, A_log, Dp, scale, h_init, dh_end, dA_end, gW_cat, gb_cat, gA_log, gDp,
+                      gscale, gu, dh_start, dA_start, accumulate, Bsz, L, D, N, act, dtype, ws, ws_bytes, stream,
+                      saved, STAGE_FINISH);
 }
 
 extern "C" int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_cat, const float* b_cat,

@@ -358,6 +358,80 @@ def ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=None, act=None):
     return dh0, dA0, sdx
 
 
+def ssm_fwd_begin(u, W_cat, b_cat, A_log):
+    """Sequence sharding, forward part 1: (h_seg, sum_dt, state) -- this segment's end state and sum
+    of dt from a zero start (what the ranks exchange) and the state ssm_fwd_finish continues from."""
+    _cuda(u, W_cat)
+    u = _c(u)
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    hseg = torch.empty(Bsz, D, N, dtype=torch.float32, device=u.device)
+    sdt = torch.empty(Bsz, D, dtype=torch.float32, device=u.device)
+    Lb = lib()
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 0), u.device)
+    W_cat, b_cat, A_log = (_f32(t) for t in (W_cat, b_cat, A_log))
+    check(Lb.pgf_ssm_fwd_begin(_p(u), _p(W_cat), _p(b_cat), _p(A_log), _p(hseg), _p(sdt), Bsz, L_, D, N, _dt(u),
+                               _p(ws), ws.numel(), _stream()), "ssm_fwd_begin")
+    return hseg, sdt, {"u": u, "W_cat": W_cat, "b_cat": b_cat, "A_log": A_log, "ws": ws}
+
+
+def ssm_fwd_finish(state, Dp, scale, h_init=None, act=None):
+    """Sequence sharding, forward part 2: y from the state entering the segment."""
+    u = state["u"]
+    Bsz, L_, D = u.shape
+    N = state["A_log"].shape[0]
+    y = torch.empty_like(u)
+    Dp, scale, h_init = (_f32(t) for t in (Dp, scale, h_init))
+    ws = state["ws"]
+    check(lib().pgf_ssm_fwd_finish(_p(u), _p(state["W_cat"]), _p(state["b_cat"]), _p(state["A_log"]), _p(Dp),
+                                   _p(scale), _p(h_init), _p(y), None, Bsz, L_, D, N, ACT[act], _dt(u), _p(ws),
+                                   ws.numel(), _stream()), "ssm_fwd_finish")
+    return y
+
+
+def ssm_bwd_begin(u, g, W_cat, b_cat, A_log, scale, saved, h_init=None, act=None):
+    """Sequence sharding, backward part 1 (after ssm_fwd_save with the segment's h_init): (adjoint at
+    the first token for a zero end carry, its decay, sum of dt but the first, state)."""
+    _cuda(u, g, W_cat)
+    u, g = _c(u), _c(g.to(u.dtype))
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    dev = u.device
+    dh0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev)
+    dA0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev)
+    sdx = torch.empty(Bsz, D, dtype=torch.float32, device=dev)
+    Lb = lib()
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 1), dev)
+    W_cat, b_cat, A_log, scale, h_init = (_f32(t) for t in (W_cat, b_cat, A_log, scale, h_init))
+    check(Lb.pgf_ssm_bwd_begin(_p(u), _p(g), _p(W_cat), _p(b_cat), _p(A_log), _p(scale), _p(h_init), _p(saved),
+                               _p(dh0), _p(dA0), _p(sdx), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(),
+                               _stream()), "ssm_bwd_begin")
+    return dh0, dA0, sdx, {"u": u, "g": g, "W_cat": W_cat, "b_cat": b_cat, "A_log": A_log, "scale": scale,
+                           "h_init": h_init, "saved": saved, "act": act, "ws": ws}
+
+
+def ssm_bwd_finish(state, Dp, dh_end=None, dA_end=None):
+    """Sequence sharding, backward part 2: every gradient for the carry entering from the right."""
+    u, g = state["u"], state["g"]
+    Bsz, L_, D = u.shape
+    N = state["A_log"].shape[0]
+    dev = u.device
+    gW = torch.empty_like(state["W_cat"])
+    gb = torch.empty_like(state["b_cat"])
+    gA = torch.empty(N, dtype=torch.float32, device=dev)
+    gD = torch.empty(D, dtype=torch.float32, device=dev)
+    gS = torch.empty(D, dtype=torch.float32, device=dev)
+    gu = torch.empty_like(u)
+    Dp, dh_end, dA_end = (_f32(t) for t in (Dp, dh_end, dA_end))
+    ws = state["ws"]
+    check(lib().pgf_ssm_bwd_finish(_p(u), _p(g), _p(state["W_cat"]), _p(state["b_cat"]), _p(state["A_log"]),
+                                   _p(Dp), _p(state["scale"]), _p(state["h_init"]), _p(state["saved"]),
+                                   _p(dh_end), _p(dA_end), _p(gW), _p(gb), _p(gA), _p(gD), _p(gS), _p(gu), None,
+                                   None, 0, Bsz, L_, D, N, ACT[state["act"]], _dt(u), _p(ws), ws.numel(),
+                                   _stream()), "ssm_bwd_finish")
+    return {"W_cat": gW, "b_cat": gb, "A_log": gA, "D": gD, "scale": gS, "grad_u": gu}
+
+
 # --------------------------------------------------------------------------- Mamba-standard mixer
 MIXER_KEYS = ("in_w", "conv_w", "conv_b", "x_w", "dt_w", "dt_b", "A_log", "D", "out_w")
 

@@ -91,11 +91,14 @@ def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
     A = -torch.exp(m.A_log.detach().float())
     xn = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
     if sp.world > 1:
-        h_loc, sdt = ops.ssm_summary(xn, W, b, m.A_log)
+        # the zero-start pass gives the segment summary; the output pass continues from it
+        h_loc, sdt, st = ops.ssm_fwd_begin(xn, W, b, m.A_log)
         h_in = compose_forward_state(sp.all_gather(h_loc), sp.all_gather(sdt), A, sp.rank)
+        y = ops.ssm_fwd_finish(st, m.D, m.scale, h_init=h_in, act=m.output_activation)
+        del st
     else:
         h_in = None
-    y, _ = ops.ssm_fwd(xn, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
+        y, _ = ops.ssm_fwd(xn, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
     x1 = y + x
     xn2 = ops.rmsnorm_fwd(x1, block.norm2.weight, block.norm2.eps)
     f = ops.ffn_fwd(xn2.reshape(-1, D), block.W1, block.b1, block.W2, block.b2, block.ffn_activation)
@@ -119,14 +122,16 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
                      block.ffn_activation, need_gx=True)
     gn2w, gn2x = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), block.norm2.weight, block.norm2.eps)
     g_m = gn2x + g_out
-    dh_end = dA_end = None
     if sp.world > 1:
-        d_loc, dA0, sdx = ops.ssm_bwd_summary(xn1, g_m, W, b, m.A_log, m.scale, h_init=h_in,
-                                              act=m.output_activation)
+        # the reverse chunk pass gives the segment's adjoint summary; the gradients continue from it
+        d_loc, dA0, sdx, st = ops.ssm_bwd_begin(xn1, g_m, W, b, m.A_log, m.scale, saved, h_init=h_in,
+                                                act=m.output_activation)
         dh_end, dA_end = compose_backward_carry(sp.all_gather(d_loc), sp.all_gather(dA0), sp.all_gather(sdx),
                                                 A, sp.rank)
-    r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, h_init=h_in, dh_end=dh_end, dA_end=dA_end,
-                    act=m.output_activation, saved=saved)
+        r = ops.ssm_bwd_finish(st, m.D, dh_end=dh_end, dA_end=dA_end)
+        del st
+    else:
+        r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation, saved=saved)
     del saved
     gn1w, gn1x = ops.rmsnorm_bwd(x, r["grad_u"], block.norm1.weight, block.norm1.eps)
     d, N = m.d_model, m.d_state

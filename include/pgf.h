@@ -277,6 +277,31 @@ int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_cat, const 
                         int64_t N, int act, int dtype, void* ws, size_t ws_bytes,
                         pgf_stream_t stream);
 
+/* Staged scan for sequence sharding: one caller workspace (pgf_ssm_workspace(.., backward)) is
+   carried from begin to finish.  fwd_begin: projection and the zero-start chunk pass; writes the
+   segment's summary from a zero start (h_seg: state after the segment, sum_dt) -- what the ranks
+   exchange.  fwd_finish: the output from the state entering the segment (h_init).  Together they
+   equal pgf_ssm_fwd without a second projection or chunk pass.  bwd_begin (after pgf_ssm_fwd_save
+   with the segment's h_init): the reverse chunk pass and the segment's adjoint summary for a zero
+   end carry (as pgf_ssm_bwd_summary); bwd_finish: every gradient for the given end carry
+   (as pgf_ssm_bwd_saved).  The same u, g, weights and `saved` in both calls. */
+int pgf_ssm_fwd_begin(const void* u, const float* W_cat, const float* b_cat, const float* A_log, float* h_seg,
+                      float* sum_dt, int64_t Bsz, int64_t L, int64_t D, int64_t N, int dtype, void* ws,
+                      size_t ws_bytes, pgf_stream_t stream);
+int pgf_ssm_fwd_finish(const void* u, const float* W_cat, const float* b_cat, const float* A_log, const float* Dp,
+                       const float* scale, const float* h_init, void* y, float* h_final, int64_t Bsz, int64_t L,
+                       int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_ssm_bwd_begin(const void* u, const void* g, const float* W_cat, const float* b_cat, const float* A_log,
+                      const float* scale, const float* h_init, const float* saved, float* dh_start,
+                      float* dA_start, float* sum_dt_excl, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act,
+                      int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_ssm_bwd_finish(const void* u, const void* g, const float* W_cat, const float* b_cat, const float* A_log,
+                       const float* Dp, const float* scale, const float* h_init, const float* saved,
+                       const float* dh_end, const float* dA_end, float* gW_cat, float* gb_cat, float* gA_log,
+                       float* gDp, float* gscale, void* gu, float* dh_start, float* dA_start, int accumulate,
+                       int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                       size_t ws_bytes, pgf_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Mamba-standard mixer: the variant the benchmark configurations describe; the reference has no
  * code for it (its SSM, train_singlemamba_optimized.py:88-124, has no in/out projection, conv or

@@ -60,6 +60,27 @@ def ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=None, act=None):
     return r["delta_h0"], r["dA0"], _dt(u, W_cat, b_cat)[:, 1:].sum(1)
 
 
+def ssm_fwd_begin(u, W_cat, b_cat, A_log):
+    h, sdt = ssm_summary(u, W_cat, b_cat, A_log)
+    return h, sdt, {"u": u, "W_cat": W_cat, "b_cat": b_cat, "A_log": A_log}
+
+
+def ssm_fwd_finish(state, Dp, scale, h_init=None, act=None):
+    y, _ = ssm_fwd(state["u"], state["W_cat"], state["b_cat"], state["A_log"], Dp, scale, h_init=h_init, act=act)
+    return y
+
+
+def ssm_bwd_begin(u, g, W_cat, b_cat, A_log, scale, saved, h_init=None, act=None):
+    dh0, dA0, sdx = ssm_bwd_summary(u, g, W_cat, b_cat, A_log, scale, h_init=h_init, act=act)
+    return dh0, dA0, sdx, {"u": u, "g": g, "W_cat": W_cat, "b_cat": b_cat, "A_log": A_log, "scale": scale,
+                           "h_init": h_init, "saved": saved, "act": act}
+
+
+def ssm_bwd_finish(state, Dp, dh_end=None, dA_end=None):
+    return ssm_bwd(state["u"], state["g"], state["W_cat"], state["b_cat"], state["A_log"], Dp, state["scale"],
+                   h_init=state["h_init"], dh_end=dh_end, dA_end=dA_end, act=state["act"], saved=state["saved"])
+
+
 def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_end=None, act=None,
             want_carry=False, saved=None):
     p = _params(W_cat, b_cat, A_log, Dp, scale)

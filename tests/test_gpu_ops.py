@@ -346,3 +346,30 @@ def test_ssm_saved_states_equal_recompute(ops, Bsz, L, D, act):
     r2 = ops.ssm_bwd(dv(u), dv(gy), *args, dh_end=dv(dh), dA_end=dv(dA), act=act, want_carry=True, saved=saved)
     for k in ("W_cat", "b_cat", "A_log", "D", "scale", "grad_u", "delta_h0", "dA0"):
         assert_close(r2[k], r1[k].double(), name=k)
+
+
+@pytest.mark.parametrize("act", [None, "tanh"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_ssm_staged_calls_equal_single_calls(ops, act, dtype):
+    """The sequence-sharding stages (fwd_begin/finish, bwd_begin/finish) give bitwise the results of
+    ssm_summary + ssm_fwd and ssm_bwd_summary + ssm_bwd(saved=...)."""
+    p, u, gy, h0, dh, dA = _ssm_case(2, 300, 64, seed=61)
+    W, b = _wcat(p)
+    dv = lambda t: t.to(DEV)  # noqa: E731
+    u, gy = dv(u).to(dtype), dv(gy).to(dtype)
+    args = (dv(W), dv(b), dv(p["A_log"]), dv(p["D"]), dv(p["scale"]))
+    hseg, sdt, st = ops.ssm_fwd_begin(u, args[0], args[1], args[2])
+    h_ref, sdt_ref = ops.ssm_summary(u, args[0], args[1], args[2])
+    assert_close(hseg, h_ref.double(), name="h_seg")
+    assert_close(sdt, sdt_ref.double(), name="sum_dt")
+    y = ops.ssm_fwd_finish(st, args[3], args[4], h_init=dv(h0), act=act)
+    y_ref, _ = ops.ssm_fwd(u, *args, h_init=dv(h0), act=act)
+    assert torch.equal(y, y_ref)
+    _, saved = ops.ssm_fwd_save(u, *args, h_init=dv(h0), act=act)
+    d0, a0, sx, st = ops.ssm_bwd_begin(u, gy, args[0], args[1], args[2], args[4], saved, h_init=dv(h0), act=act)
+    d0r, a0r, sxr = ops.ssm_bwd_summary(u, gy, args[0], args[1], args[2], args[4], h_init=dv(h0), act=act)
+    assert torch.equal(d0, d0r) and torch.equal(a0, a0r) and torch.equal(sx, sxr)
+    r = ops.ssm_bwd_finish(st, args[3], dh_end=dv(dh), dA_end=dv(dA))
+    r_ref = ops.ssm_bwd(u, gy, *args, h_init=dv(h0), dh_end=dv(dh), dA_end=dv(dA), act=act, saved=saved)
+    for k in ("W_cat", "b_cat", "A_log", "D", "scale", "grad_u"):
+        assert torch.equal(r[k], r_ref[k]), k
