@@ -394,8 +394,9 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
 #pragma unroll
   for (int j = 0; j < NS; ++j)
     h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
-  const float Dd = l.ch ? a.Dp[l.d] : 0.f;
-  const float sc = l.ch ? a.scale[l.d] : 0.f;
+  // D and scale only enter the output (a.y); the act'(C h) mode (a.y == nullptr) may run without them
+  const float Dd = (l.ch && a.y) ? a.Dp[l.d] : 0.f;
+  const float sc = (l.ch && a.y) ? a.scale[l.d] : 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   Pref r;
   pref_load(a, l, l.s, false, r);
