@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(32 * CSEG) compose_bwd_kernel(const Args a) {
 
 // Main backward: checkpoints from the forward output pass (ckpt_g) are required.
 // Dynamic shared memory: red [ST][WARPS][32], gbuf [2][3][ST][DC].
-__global__ void __launch_bounds__(THREADS) main_bwd_kernel(const Args a) {
+__global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
   extern __shared__ float sm[];
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
@@ -342,16 +342,23 @@ __global__ void __launch_bounds__(THREADS) main_bwd_kernel(const Args a) {
   pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
   pref_store(r, l, true, stg[(nsub - 1) & 1]);
   __syncthreads();
+  // sub-chunk start states, loaded one sub-chunk ahead so the re-run never waits on memory
+  auto ckpt_at = [&](int k, float (&dst)[NS]) {
+    const float4 v = l.ch ? *reinterpret_cast<const float4*>(
+                                a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+  };
+  float ck_next[NS];
+  ckpt_at(nsub - 1, ck_next);
   for (int k = nsub - 1; k >= 0; --k) {
     if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
     const Stage& S = stg[k & 1];
     float* gb = gbuf + (k & 1) * (3 * ST * DC);
     float tr[ST + 1][NS], ex[ST][NS];
-    {
-      const float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS;
 #pragma unroll
-      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? cp[j] : 0.f;
-    }
+    for (int j = 0; j < NS; ++j) tr[0][j] = ck_next[j];
+    if (k > 0) ckpt_at(k - 1, ck_next);
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
 #pragma unroll

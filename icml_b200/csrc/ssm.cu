@@ -585,6 +585,16 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
   }
 
   // ---- pass 2: sub-chunks in reverse
+  // saved checkpoints (h0 and S), loaded one sub-chunk ahead so the re-run never waits on memory
+  float ck_h[NS] = {0.f, 0.f, 0.f, 0.f}, ck_s = 0.f;
+  auto ckpt_at = [&](int kk) {
+    if (!l.ch) return;
+    const int64_t ck = (l.b * a.nC + l.c) * KS + kk;
+    const float4 v = *reinterpret_cast<const float4*>(a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS);
+    ck_h[0] = v.x; ck_h[1] = v.y; ck_h[2] = v.z; ck_h[3] = v.w;
+    ck_s = a.ckpt_s[ck * a.D + l.d];
+  };
+  if (saved) ckpt_at(nsub - 1);
   float accA[NS] = {0.f, 0.f, 0.f, 0.f};
   float accD = 0.f, accS = 0.f;
   const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
@@ -598,13 +608,11 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
     // re-run the sub-chunk into registers: tr[i] = state before token i, ex[i] = exp(dt_i A)
     float tr[ST + 1][NS], ex[ST][NS];
     if (saved) {
-      // zero-start checkpoint h0 of the forward, moved onto the chunk's start state h (= hC):
-      // state = h0 + exp(A S) h, S = sum of dt in the chunk before this sub-chunk
-      const int64_t ck = (l.b * a.nC + l.c) * KS + k;
-      const float* cp = a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS;
-      const float Sk = l.ch ? a.ckpt_s[ck * a.D + l.d] : 0.f;
+      // zero-start checkpoint h0 of the forward (prefetched one sub-chunk ahead), moved onto the
+      // chunk's start state h (= hC): state = h0 + exp(A S) h, S = sum of dt before this sub-chunk
 #pragma unroll
-      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? fmaf(exp2f(K.A2[j] * Sk), h[j], cp[j]) : 0.f;
+      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? fmaf(exp2f(K.A2[j] * ck_s), h[j], ck_h[j]) : 0.f;
+      if (k > 0) ckpt_at(k - 1);
     } else {
 #pragma unroll
       for (int j = 0; j < NS; ++j) tr[0][j] = ckpt[(size_t(k) * SSM_THREADS + l.tid) * NS + j];
