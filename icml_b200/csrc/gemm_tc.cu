@@ -52,6 +52,12 @@ struct TcCfg {
 
 enum { TC_GENERIC = 0, TC_CE_FWD = 1, TC_CE_BWD = 2 };
 
+// Epilogue families, one kernel instantiation each (a kernel carries only its own epilogue code:
+// the single all-modes kernel spent a measurable share of its issue slots on instruction-cache misses):
+//   PLAIN: generic, no activation (bias / addend / accumulate);  ACT: GELU or ReLU (+ pre-activation);
+//   DACT: GELU' or ReLU' with the saved pre-activation;  CE_FWD / CE_BWD: the cross-entropy modes.
+enum { EK_PLAIN = 0, EK_ACT = 1, EK_DACT = 2, EK_CE_FWD = 3, EK_CE_BWD = 4, EK_COUNT = 5 };
+
 
 struct TcParams {
   int64_t M, N, K;
@@ -79,11 +85,12 @@ struct TcParams {
   float* tgt_logit;        // (M,)  CE_FWD
 };
 
-template <int BN>
+template <int BN, int EK>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmZ, const TcParams p) {
   using C = TcCfg<BN>;
+  constexpr int MODE = EK == EK_CE_FWD ? TC_CE_FWD : (EK == EK_CE_BWD ? TC_CE_BWD : TC_GENERIC);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
@@ -217,16 +224,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       float run_m = -INFINITY, run_s = 0.f;
       int64_t tgt = -1;
       float row_lse = 0.f;
-      if (p.mode != TC_GENERIC && row_ok) {
+      if (MODE != TC_GENERIC && row_ok) {
         tgt = p.targets[row];
-        if (p.mode == TC_CE_BWD) row_lse = p.lse[row];
+        if (MODE == TC_CE_BWD) row_lse = p.lse[row];
       }
       for (int nt = nt0; nt < nt1; ++nt, ++tt) {
         const uint32_t buf = tt & 1, use = tt >> 1;
         if (!mbar_wait_warp(&tfull[buf], use & 1)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int64_t n0 = int64_t(nt) * BN;
-        if (p.fast) {
+        if (EK != EK_CE_FWD && p.fast) {
           // ---- row-per-thread epilogue: this thread owns row `row` and the warp's BN/2 columns,
           //      taken 64 at a time (nh .. nh+63)
           const int64_t row0 = int64_t(mb) * TC_BM + q * 32;
@@ -248,7 +255,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             const int64_t nb = nh + c * 32;
             float v[32];
-            if (p.mode == TC_CE_BWD) {
+            if (MODE == TC_CE_BWD) {
               constexpr float L2E = 1.4426950408889634f;
               const float ll = row_lse * L2E;
 #pragma unroll
@@ -279,7 +286,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = e.alpha * __uint_as_float(r[j]);
               }
-              if (e.kind == PGF_EPI_GELU || e.kind == PGF_EPI_RELU) {
+              if (EK == EK_ACT) {
                 if (e.aux_out) {
                   if (p.z_bf16) {
 #pragma unroll
@@ -305,7 +312,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                   for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
                 }
-              } else if (e.kind == PGF_EPI_DGELU || e.kind == PGF_EPI_DRELU) {
+              } else if (EK == EK_DACT) {
                 float a[32];
                 load_seg(e.aux, e.aux_dtype, e.ld_aux, row, nb, p.M, p.N, a);
                 if (e.kind == PGF_EPI_DRELU) {
@@ -350,8 +357,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             stage_row(b, lane, dpk);
             stage_store(b, &tmD, nh, row0, ks, lane);
           }
-          if (box_live && nh < p.N && p.mode == TC_GENERIC && p.epi.aux_out && p.z_bf16 &&
-              (p.epi.kind == PGF_EPI_GELU || p.epi.kind == PGF_EPI_RELU)) {
+          if (box_live && nh < p.N && MODE == TC_GENERIC && p.epi.aux_out && p.z_bf16 &&
+              (EK == EK_ACT)) {
             uint8_t* b = stage_acquire(stg, sq, lane);
             stage_row(b, lane, zpk);
             stage_store(b, &tmZ, nh, row0, 0, lane);
@@ -359,12 +366,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }  // g64
           continue;
         }
+        // column-chunk path: the CE forward at either width, the transposed store only in 128-wide
+        // tiles (the host sends 256-wide generic and CE-backward tiles to the row-per-thread path)
 #pragma unroll 1
-        for (int c = hf * (BN / 64); c < (hf + 1) * (BN / 64); ++c) {
+        for (int c = hf * (BN / 64); c < (BN == 128 || EK == EK_CE_FWD ? (hf + 1) * (BN / 64) : 0); ++c) {
           uint32_t r[32];
           tmem_ld32(tmem + buf * BN + (uint32_t(q * 32) << 16) + uint32_t(c * 32), r);
           const int64_t nc = n0 + c * 32;
-          if (p.mode == TC_CE_FWD) {
+          if (MODE == TC_CE_FWD) {
             // online log-sum-exp in base 2: exp(v - m) = exp2(v log2e - m log2e)
             constexpr float L2E = 1.4426950408889634f;
             if (nc + 32 > p.N) {
@@ -396,7 +405,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             continue;
           }
-          if (p.mode == TC_CE_BWD) {
+          if (MODE == TC_CE_BWD) {
             constexpr float L2E = 1.4426950408889634f;
             const float ll = row_lse * L2E;
 #pragma unroll
@@ -413,7 +422,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const int64_t n = nc + lane;
           const bool n_ok = n < p.N;
           const int64_t mbase = int64_t(mb) * TC_BM + q * 32;
-          if (p.mode == TC_GENERIC) {
+          if (MODE == TC_GENERIC) {
             const float bias_n = (p.epi.bias && n_ok) ? p.epi.bias[n] : 0.f;
 #pragma unroll 8
             for (int rr = 0; rr < 32; ++rr) {
@@ -434,7 +443,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
       }
-      if (p.mode == TC_CE_FWD && row_ok && ok) {
+      if (MODE == TC_CE_FWD && row_ok && ok) {
         p.part_m[row * (2 * p.n_groups) + 2 * ng + hf] = run_m;
         p.part_s[row * (2 * p.n_groups) + 2 * ng + hf] = run_s;
       }
@@ -503,17 +512,36 @@ static int tile_bn(int mode, int64_t N) {
   return (mode == TC_GENERIC && wide) ? 256 : 128;
 }
 
+static int ek_of(const TcParams& p) {
+  if (p.mode == TC_CE_FWD) return EK_CE_FWD;
+  if (p.mode == TC_CE_BWD) return EK_CE_BWD;
+  switch (p.epi.kind) {
+    case PGF_EPI_GELU: case PGF_EPI_RELU: return EK_ACT;
+    case PGF_EPI_DGELU: case PGF_EPI_DRELU: return EK_DACT;
+    default: return EK_PLAIN;
+  }
+}
+
+template <int BN, int EK>
+static int launch_tc_kernel(unsigned grid, cudaStream_t s, const CUtensorMap& ma, const CUtensorMap& mb,
+                            const CUtensorMap& md, const CUtensorMap& mz, const TcParams& p) {
+  using C = TcCfg<BN>;
+  static int smem_limit = 0;
+  PGF_CUDA(ensure_dynamic_smem(gemm_tc_kernel<BN, EK>, C::SMEM, smem_limit));
+  gemm_tc_kernel<BN, EK><<<grid, TC_THREADS, C::SMEM, s>>>(ma, mb, md, mz, p);
+  return PGF_OK;
+}
+
 template <int BN>
 static int launch_tc_bn(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
   using C = TcCfg<BN>;
+  (void)sizeof(C);
   CUtensorMap ma, mb;
   const bool oka = g.a_trans ? make_map(&ma, g.A, g.M, g.K, g.lda, 64, 64)
                              : make_map(&ma, g.A, g.K, g.M, g.lda, 64, TC_BM);
   const bool okb = g.b_trans ? make_map(&mb, g.B, g.N, g.K, g.ldb, 64, 64)
                              : make_map(&mb, g.B, g.K, g.N, g.ldb, 64, BN);
   if (!oka || !okb) return PGF_ERR_UNSUPPORTED;
-  static int smem_limit = 0;
-  PGF_CUDA(ensure_dynamic_smem(gemm_tc_kernel<BN>, C::SMEM, smem_limit));
   p.M = g.M; p.N = g.N; p.K = g.K;
   p.a_mn = g.a_trans; p.b_mn = g.b_trans;
   const int64_t n_tiles = (g.N + BN - 1) / BN;
@@ -548,9 +576,17 @@ static int launch_tc_bn(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id)
   // 256-wide tiles: generic products through the TMA-store epilogue, and the CE forward (no stored
   // output); the transpose epilogue is only used at 128
   if (BN == 256 && ((p.mode == TC_GENERIC && !p.fast) || p.mode == TC_CE_BWD)) return PGF_ERR_UNSUPPORTED;
-  const int64_t grid = p.units < sm_count() ? p.units : sm_count();
+  const unsigned grid = unsigned(p.units < sm_count() ? p.units : sm_count());
   prof_begin(prof_id, s);
-  gemm_tc_kernel<BN><<<unsigned(grid), TC_THREADS, C::SMEM, s>>>(ma, mb, md, mz, p);
+  int rc = PGF_OK;
+  switch (ek_of(p)) {
+    case EK_PLAIN: rc = launch_tc_kernel<BN, EK_PLAIN>(grid, s, ma, mb, md, mz, p); break;
+    case EK_ACT: rc = launch_tc_kernel<BN, EK_ACT>(grid, s, ma, mb, md, mz, p); break;
+    case EK_DACT: rc = launch_tc_kernel<BN, EK_DACT>(grid, s, ma, mb, md, mz, p); break;
+    case EK_CE_FWD: rc = launch_tc_kernel<BN, EK_CE_FWD>(grid, s, ma, mb, md, mz, p); break;
+    default: rc = launch_tc_kernel<BN, EK_CE_BWD>(grid, s, ma, mb, md, mz, p); break;
+  }
+  PGF_TRY(rc);
   prof_end(prof_id, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
   PGF_LAUNCH_CHECK();
   return PGF_OK;
