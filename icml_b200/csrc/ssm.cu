@@ -25,12 +25,14 @@
 // fixed-order partial buffers: results are bitwise reproducible.
 #include "gemm.cuh"
 #include "scan_compose.cuh"
+#include "f32x2.cuh"
 
 namespace pgf {
 
 constexpr int NST = 16;              // d_state
 constexpr int NQ = 4;                // threads per channel
 constexpr int NS = NST / NQ;         // states per thread
+constexpr int NP = NS / 2;           // state pairs per thread (packed f32x2 arithmetic)
 constexpr int DC = 64;               // channels per CTA
 constexpr int SSM_THREADS = DC * NQ; // 256
 constexpr int SSM_WARPS = SSM_THREADS / 32;
@@ -92,27 +94,6 @@ __device__ __forceinline__ float act_deriv(int act, float x) {
   return 1.f;
 }
 
-// phi_1(z) = (e^z - 1)/z and phi_1'(z) = (e^z - phi_1(z))/z given e = e^z (exp2f) and rz = 1/z.
-// |z| < 1/8: Taylor series to z^4 (truncation < 5e-8); elsewhere the closed forms.  With e accurate
-// to 2 ulp the worst relative error is ~1.1e-6 for phi_1 and ~5.4e-6 for phi_1' (at the switch);
-// both branches are a few FMAs, so the select costs less than a divergent branch.
-__device__ __forceinline__ float phi1r(float z, float e, float rz) {
-  float p = fmaf(z, 1.0f / 120.0f, 1.0f / 24.0f);
-  p = fmaf(p, z, 1.0f / 6.0f);
-  p = fmaf(p, z, 0.5f);
-  p = fmaf(p, z, 1.0f);
-  const float c = (e - 1.0f) * rz;
-  return fabsf(z) < 0.125f ? p : c;
-}
-__device__ __forceinline__ float phi1pr(float z, float e, float p1, float rz) {
-  float p = fmaf(z, 5.0f / 720.0f, 4.0f / 120.0f);
-  p = fmaf(p, z, 3.0f / 24.0f);
-  p = fmaf(p, z, 2.0f / 6.0f);
-  p = fmaf(p, z, 0.5f);
-  const float c = (e - p1) * rz;
-  return fabsf(z) < 0.125f ? p : c;
-}
-
 struct Lane {
   int tid, dl, nq;
   int64_t c, b, d, s, e;
@@ -135,19 +116,36 @@ __device__ __forceinline__ Lane lane_of(const SsmArgs& a) {
   return l;
 }
 
-// per-thread state constants: A_n, A_n log2(e), 1/A_n
+// Tokens of sub-chunk k that lie inside the chunk (ST except in a ragged last sub-chunk).
+__device__ __forceinline__ int sub_len(const Lane& l, int k) {
+  const int64_t r = l.e - (l.s + int64_t(k) * ST);
+  return r < ST ? int(r) : ST;
+}
+
+// per-thread state constants, as pairs of states: A_n, A_n log2(e), 1/A_n
 struct AConst {
-  float A[NS], A2[NS], rA[NS];
+  float2 A[NP], A2[NP], rA[NP];
 };
 __device__ __forceinline__ AConst load_A(const SsmArgs& a, int nq) {
   AConst c;
 #pragma unroll
-  for (int j = 0; j < NS; ++j) {
-    c.A[j] = -expf(a.A_log[nq * NS + j]);
-    c.A2[j] = c.A[j] * LOG2E;
-    c.rA[j] = 1.0f / c.A[j];
+  for (int p = 0; p < NP; ++p) {
+    const float a0 = -expf(a.A_log[nq * NS + 2 * p]), a1 = -expf(a.A_log[nq * NS + 2 * p + 1]);
+    c.A[p] = f2(a0, a1);
+    c.A2[p] = f2(a0 * LOG2E, a1 * LOG2E);
+    c.rA[p] = f2(1.0f / a0, 1.0f / a1);
   }
   return c;
+}
+
+// The thread's NS states of row `o` (o = first state) as pairs; stores likewise.
+__device__ __forceinline__ void ld_states(const float* __restrict__ src, float2 v[NP]) {
+  const float4 q = *reinterpret_cast<const float4*>(src);
+  v[0] = lo2(q);
+  v[1] = hi2(q);
+}
+__device__ __forceinline__ void st_states(float* __restrict__ dst, const float2 v[NP]) {
+  *reinterpret_cast<float4*>(dst) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
 }
 
 __device__ __forceinline__ void pref_load(const SsmArgs& a, const Lane& l, int64_t s0, bool bwd, Pref& r) {
@@ -199,20 +197,27 @@ __device__ __forceinline__ void pref_store(const Pref& r, const Lane& l, bool bw
   }
 }
 
-// One forward step of the thread's NS states on staged token i; returns e = exp(dt A) per state.
+// One forward step of the thread's NS states (as pairs) on staged token i:
+// h = exp(dt A) h + phi_1(dt A) B u; returns phi_1(dt A) per state.
+template <bool OUT_E = false>
 __device__ __forceinline__ void step_fwd(const Stage& st, int i, int dl, int nq, const AConst& K,
-                                         float h[NS], float e_out[NS]) {
-  const float dt = st.dt[i][dl], rdt = st.rdt[i][dl], uu = st.u[i][dl];
+                                         float2 h[NP], float2 p1_out[NP]) {
+  const float2 dt = f2(st.dt[i][dl]), rdt = f2(st.rdt[i][dl]), uu = f2(st.u[i][dl]);
   const float4 Bq = st.B[i][nq];
-  const float Bv[NS] = {Bq.x, Bq.y, Bq.z, Bq.w};
+  const float2 Bv[NP] = {lo2(Bq), hi2(Bq)};
 #pragma unroll
-  for (int j = 0; j < NS; ++j) {
-    const float z = dt * K.A[j];
-    const float ez = exp2f(dt * K.A2[j]);
-    const float p1 = phi1r(z, ez, rdt * K.rA[j]);
-    h[j] = ez * h[j] + (p1 * Bv[j]) * uu;
-    e_out[j] = ez;
+  for (int p = 0; p < NP; ++p) {
+    const float2 z = mul2(dt, K.A[p]);
+    const float2 ez = ex2_2(mul2(dt, K.A2[p]));
+    const float2 p1 = phi1_2(z, ez, mul2(rdt, K.rA[p]));
+    h[p] = fma2(ez, h[p], mul2(mul2(p1, Bv[p]), uu));
+    p1_out[p] = OUT_E ? ez : p1;
   }
+}
+
+// C . h over the thread's states (the pair sums, then the two lanes).
+__device__ __forceinline__ float dot_c(const float4 Cq, const float2 h[NP]) {
+  return hsum2(fma2(hi2(Cq), h[1], mul2(lo2(Cq), h[0])));
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -222,7 +227,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l.nq);
-  float h[NS] = {0.f, 0.f, 0.f, 0.f}, e[NS];
+  float2 h[NP] = {f2(0.f), f2(0.f)}, e[NP];
   float sdt = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   Pref r;
@@ -230,11 +235,12 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
   pref_store(r, l, false, stg[0]);
   __syncthreads();
   for (int k = 0; k < nsub; ++k) {
+    const int nt = sub_len(l, k);
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
-      if (l.s + int64_t(k) * ST + i < l.e) {
+      if (i < nt) {
         step_fwd(S, i, l.dl, l.nq, K, h, e);
         sdt += S.dt[i][l.dl];
       }
@@ -244,8 +250,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
-#pragma unroll
-  for (int j = 0; j < NS; ++j) a.hloc[(cb * a.D + l.d) * NST + l.nq * NS + j] = h[j];
+  st_states(a.hloc + (cb * a.D + l.d) * NST + l.nq * NS, h);
   if (l.nq == 0) a.sdt[cb * a.D + l.d] = sdt;
 }
 
@@ -283,7 +288,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_y0_kernel(const SsmArgs
   __shared__ float ybuf[2][ST][DC];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l.nq);
-  float h[NS] = {0.f, 0.f, 0.f, 0.f}, e[NS];
+  float2 h[NP] = {f2(0.f), f2(0.f)}, e[NP];
   float sdt = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   const int KS = int((a.Tc + ST - 1) / ST);
@@ -292,25 +297,20 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_y0_kernel(const SsmArgs
   pref_store(r, l, false, stg[0]);
   __syncthreads();
   for (int k = 0; k < nsub; ++k) {
+    const int nt = sub_len(l, k);
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
     if (a.ckpt_write && l.ch) {
       const int64_t ck = (l.b * a.nC + l.c) * KS + k;
-      float* cp = a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS;
-#pragma unroll
-      for (int j = 0; j < NS; ++j) cp[j] = h[j];
+      st_states(a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS, h);
       if (l.nq == 0) a.ckpt_s[ck * a.D + l.d] = sdt;
     }
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
-      if (l.s + int64_t(k) * ST + i < l.e) {
+      if (i < nt) {
         step_fwd(S, i, l.dl, l.nq, K, h, e);
         sdt += S.dt[i][l.dl];
-        const float4 Cq = S.C[i][l.nq];
-        float yc = Cq.x * h[0];
-        yc = fmaf(Cq.y, h[1], yc);
-        yc = fmaf(Cq.z, h[2], yc);
-        yc = fmaf(Cq.w, h[3], yc);
+        float yc = dot_c(S.C[i][l.nq], h);
         yc += __shfl_xor_sync(0xffffffffu, yc, 1);
         yc += __shfl_xor_sync(0xffffffffu, yc, 2);
         if (l.nq == 0) ybuf[k & 1][i][l.dl] = yc;
@@ -329,8 +329,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_y0_kernel(const SsmArgs
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
-#pragma unroll
-  for (int j = 0; j < NS; ++j) a.hloc[(cb * a.D + l.d) * NST + l.nq * NS + j] = h[j];
+  st_states(a.hloc + (cb * a.D + l.d) * NST + l.nq * NS, h);
   if (l.nq == 0) a.sdt[cb * a.D + l.d] = sdt;
 }
 
@@ -340,10 +339,8 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs
   __shared__ float ybuf[2][ST][DC];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l.nq);
-  float H[NS];
-#pragma unroll
-  for (int j = 0; j < NS; ++j)
-    H[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
+  float2 H[NP] = {f2(0.f), f2(0.f)};
+  if (l.ch) ld_states(a.hC + ((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS, H);
   float S_run = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   Pref r;
@@ -351,17 +348,16 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs
   pref_store(r, l, false, stg[0]);
   __syncthreads();
   for (int k = 0; k < nsub; ++k) {
+    const int nt = sub_len(l, k);
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
-      if (l.s + int64_t(k) * ST + i < l.e) {
+      if (i < nt) {
         S_run += S.dt[i][l.dl];
-        const float4 Cq = S.C[i][l.nq];
-        float yc = Cq.x * (exp2f(K.A2[0] * S_run) * H[0]);
-        yc = fmaf(Cq.y, exp2f(K.A2[1] * S_run) * H[1], yc);
-        yc = fmaf(Cq.z, exp2f(K.A2[2] * S_run) * H[2], yc);
-        yc = fmaf(Cq.w, exp2f(K.A2[3] * S_run) * H[3], yc);
+        const float2 s2 = f2(S_run);
+        const float2 hs[NP] = {mul2(ex2_2(mul2(K.A2[0], s2)), H[0]), mul2(ex2_2(mul2(K.A2[1], s2)), H[1])};
+        float yc = dot_c(S.C[i][l.nq], hs);
         yc += __shfl_xor_sync(0xffffffffu, yc, 1);
         yc += __shfl_xor_sync(0xffffffffu, yc, 2);
         if (l.nq == 0) ybuf[k & 1][i][l.dl] = yc;
@@ -390,10 +386,8 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
   __shared__ float ybuf[2][ST][DC];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l.nq);
-  float h[NS], e[NS];
-#pragma unroll
-  for (int j = 0; j < NS; ++j)
-    h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS + j] : 0.f;
+  float2 h[NP] = {f2(0.f), f2(0.f)}, e[NP];
+  if (l.ch) ld_states(a.hC + ((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS, h);
   // D and scale only enter the output (a.y); the act'(C h) mode (a.y == nullptr) may run without them
   const float Dd = (l.ch && a.y) ? a.Dp[l.d] : 0.f;
   const float sc = (l.ch && a.y) ? a.scale[l.d] : 0.f;
@@ -404,22 +398,17 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
   __syncthreads();
   const int KS = int((a.Tc + ST - 1) / ST);
   for (int k = 0; k < nsub; ++k) {
+    const int nt = sub_len(l, k);
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
     if (a.ckpt_write && l.ch) {
-      float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.D + l.d) * NST + l.nq * NS;
-#pragma unroll
-      for (int j = 0; j < NS; ++j) cp[j] = h[j];
+      st_states(a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.D + l.d) * NST + l.nq * NS, h);
     }
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
-      if (l.s + int64_t(k) * ST + i < l.e) {
+      if (i < nt) {
         step_fwd(S, i, l.dl, l.nq, K, h, e);
-        const float4 Cq = S.C[i][l.nq];
-        float yc = Cq.x * h[0];
-        yc = fmaf(Cq.y, h[1], yc);
-        yc = fmaf(Cq.z, h[2], yc);
-        yc = fmaf(Cq.w, h[3], yc);
+        float yc = dot_c(S.C[i][l.nq], h);
         yc += __shfl_xor_sync(0xffffffffu, yc, 1);
         yc += __shfl_xor_sync(0xffffffffu, yc, 2);
         if (l.nq == 0) {
@@ -453,8 +442,8 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArg
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l.nq);
-  float dlt[NS] = {0.f, 0.f, 0.f, 0.f};
-  float anext[NS] = {1.f, 1.f, 1.f, 1.f};
+  float2 dlt[NP] = {f2(0.f), f2(0.f)};
+  float2 anext[NP] = {f2(1.f), f2(1.f)};
   float sdt2 = 0.f, dt_first = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   Pref r;
@@ -469,13 +458,13 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArg
       const int64_t t = l.s + int64_t(k) * ST + i;
       if (t < l.e) {
         const float dt = S.dt[i][l.dl];
-        const float dh = S.dh[i][l.dl];
+        const float2 dh = f2(S.dh[i][l.dl]);
         const float4 Cq = S.C[i][l.nq];
-        const float Cv[NS] = {Cq.x, Cq.y, Cq.z, Cq.w};
+        const float2 Cv[NP] = {lo2(Cq), hi2(Cq)};
 #pragma unroll
-        for (int j = 0; j < NS; ++j) {
-          dlt[j] = anext[j] * dlt[j] + dh * Cv[j];
-          anext[j] = exp2f(dt * K.A2[j]);
+        for (int p = 0; p < NP; ++p) {
+          dlt[p] = fma2(anext[p], dlt[p], mul2(dh, Cv[p]));
+          anext[p] = ex2_2(mul2(f2(dt), K.A2[p]));
         }
         if (t > l.s) sdt2 += dt;
         dt_first = dt;
@@ -486,8 +475,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArg
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
-#pragma unroll
-  for (int j = 0; j < NS; ++j) a.dloc[(cb * a.D + l.d) * NST + l.nq * NS + j] = dlt[j];
+  st_states(a.dloc + (cb * a.D + l.d) * NST + l.nq * NS, dlt);
   if (l.nq == 0) {
     a.sdt2[cb * a.D + l.d] = sdt2;
     a.dt0[cb * a.D + l.d] = dt_first;
@@ -545,7 +533,7 @@ __global__ void __launch_bounds__(32 * CSEG) ssm_compose_bwd_kernel(const SsmArg
 // Main backward kernel.  Shared memory (dynamic): ckpt [Tc/ST][SSM_THREADS][NS] floats, then
 // red [ST][SSM_WARPS][32], then gbuf [2][ST][DC] (grad_dt_in, grad_u_scan of the sub-chunk).
 __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmArgs a) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const int KS = int((a.Tc + ST - 1) / ST);
@@ -554,7 +542,30 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
   float* red = ckpt + (saved ? size_t(0) : size_t(KS) * SSM_THREADS * NS);
   float* gbuf = red + ST * SSM_WARPS * 32;  // [2][ST][DC]
   const int lane = l.tid & 31, warp = l.tid >> 5;
-  const AConst K = load_A(a, l.nq);
+  const AConst KP = load_A(a, l.nq);
+  // scalar state constants (this kernel steps its states one at a time: the packed step needs more
+  // live registers than two CTAs per SM leave)
+  struct { float A[NS], A2[NS], rA[NS]; } K;
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    K.A[2 * p] = KP.A[p].x; K.A[2 * p + 1] = KP.A[p].y;
+    K.A2[2 * p] = KP.A2[p].x; K.A2[2 * p + 1] = KP.A2[p].y;
+    K.rA[2 * p] = KP.rA[p].x; K.rA[2 * p + 1] = KP.rA[p].y;
+  }
+  // one forward step of the thread's states on staged token i; e = exp(dt A) per state
+  auto step = [&](const Stage& st, int i, float hh[NS], float eo[NS]) {
+    const float dt = st.dt[i][l.dl], rdt = st.rdt[i][l.dl], uu = st.u[i][l.dl];
+    const float4 Bq = st.B[i][l.nq];
+    const float Bv[NS] = {Bq.x, Bq.y, Bq.z, Bq.w};
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      const float z = dt * K.A[j];
+      const float ez = ex2f(dt * K.A2[j]);
+      const float p1 = phi1(z, ez, rdt * K.rA[j]);
+      hh[j] = ez * hh[j] + (p1 * Bv[j]) * uu;
+      eo[j] = ez;
+    }
+  };
   const float Dd = l.ch ? a.Dp[l.d] : 0.f;
   const int64_t cb = l.b * a.nC + l.c;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
@@ -579,7 +590,7 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i)
-      if (l.s + int64_t(k) * ST + i < l.e) step_fwd(S, i, l.dl, l.nq, K, h, e);
+      if (l.s + int64_t(k) * ST + i < l.e) step(S, i, h, e);
     if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
     __syncthreads();
   }
@@ -611,7 +622,7 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
       // zero-start checkpoint h0 of the forward (prefetched one sub-chunk ahead), moved onto the
       // chunk's start state h (= hC): state = h0 + exp(A S) h, S = sum of dt before this sub-chunk
 #pragma unroll
-      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? fmaf(exp2f(K.A2[j] * ck_s), h[j], ck_h[j]) : 0.f;
+      for (int j = 0; j < NS; ++j) tr[0][j] = l.ch ? fmaf(ex2f(K.A2[j] * ck_s), h[j], ck_h[j]) : 0.f;
       if (k > 0) ckpt_at(k - 1);
     } else {
 #pragma unroll
@@ -621,7 +632,7 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
     for (int i = 0; i < ST; ++i) {
 #pragma unroll
       for (int j = 0; j < NS; ++j) tr[i + 1][j] = tr[i][j];
-      if (l.s + int64_t(k) * ST + i < l.e) step_fwd(S, i, l.dl, l.nq, K, tr[i + 1], ex[i]);
+      if (l.s + int64_t(k) * ST + i < l.e) step(S, i, tr[i + 1], ex[i]);
       else {
 #pragma unroll
         for (int j = 0; j < NS; ++j) ex[i][j] = 1.f;
@@ -645,8 +656,8 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
           const float z = dt * K.A[j];
           const float ez = ex[i][j];
           const float rz = rdt * K.rA[j];
-          const float p1 = phi1r(z, ez, rz);
-          const float p1p = phi1pr(z, ez, p1, rz);
+          const float p1 = phi1(z, ez, rz);
+          const float p1p = phi1p(z, ez, p1, rz);
           const float q = ez * tr[i][j] + p1p * (Bv[j] * uu);
           const float dq = dlt * q;
           accA[j] = fmaf(dq, z, accA[j]);
