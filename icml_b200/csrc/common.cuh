@@ -156,6 +156,52 @@ __device__ __forceinline__ float phi1p_from_exp(float z, float e) {
 
 // torch.nn.functional.softplus with beta=1, threshold=20.
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// 2^x by the hardware approximation (ex2.approx.ftz: ~2 ulp; results below 2^-126 flush to zero,
+// which for the decays exp(dt A) <= 1 of the scans changes nothing that is added to a state).
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 1/x by the hardware approximation (rcp.approx.ftz: <= 1 ulp; denormal inputs count as zero).
+__device__ __forceinline__ float rcpf(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// softplus(x) = max(x, 0) + log1p(y), y = exp(-|x|) in (0, 1], branch-free:
+//   y = 2^t (1 + r ln 2) with t = -|x| log2(e) rounded and r its rounding residual (two FMAs: the
+//   product's error and the tail of log2(e)), so the exponent's rounding does not grow with |x|;
+//   log1p(y) = 2 atanh(s), s = y / (2 + y) <= 1/3, by its odd series to s^13.
+// Relative error <= 2.8e-7 with an exact 2^t and <= 5.4e-7 with the 2-ulp hardware ex2, over
+// x in [-87, 100] (below -87.3 the result flushes to zero).  About 20 instructions, where
+// log1pf(expf(x)) takes several times that with branches.  The scans derive dt = softplus(dt_in)
+// with it for every (token, channel) they stage.
+__device__ __forceinline__ float exp_neg_abs(float x) {
+  constexpr float L2E = 1.4426950408889634f, L2E_LO = 1.925963033500011e-08f, LN2 = 0.6931471805599453f;
+  const float na = -fabsf(x);
+  const float t = na * L2E;
+  float r = fmaf(na, L2E, -t);
+  r = fmaf(na, L2E_LO, r);
+  const float y0 = ex2f(t);
+  return fmaf(y0, r * LN2, y0);
+}
+__device__ __forceinline__ float softplus_from(float x, float y) {
+  const float s = y * rcpf(2.0f + y);
+  const float s2 = s * s;
+  float p = fmaf(s2, 1.0f / 13.0f, 1.0f / 11.0f);
+  p = fmaf(p, s2, 1.0f / 9.0f);
+  p = fmaf(p, s2, 1.0f / 7.0f);
+  p = fmaf(p, s2, 1.0f / 5.0f);
+  p = fmaf(p, s2, 1.0f / 3.0f);
+  p = fmaf(p, s2, 1.0f);
+  return fmaxf(x, 0.0f) + 2.0f * s * p;
+}
+__device__ __forceinline__ float softplus_fast(float x) { return softplus_from(x, exp_neg_abs(x)); }
+// sigmoid(x) from the same y = exp(-|x|): 1/(1+y) for x >= 0, y/(1+y) otherwise (~3 ulp).
+__device__ __forceinline__ float sigmoid_from(float x, float y) { return (x >= 0.0f ? 1.0f : y) * rcpf(1.0f + y); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 // tanh-approximated GELU and its derivative, constants of pgf_ffn.py:16-26.

@@ -4,7 +4,7 @@
 // an ordinary round-to-nearest float32 operation, so a packed op gives the same bits as the two
 // scalar ones.
 #pragma once
-#include <cuda_runtime.h>
+#include "common.cuh"
 
 namespace pgf {
 
@@ -18,13 +18,6 @@ __device__ __forceinline__ float hsum2(float2 a) { return a.x + a.y; }
 __device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
 __device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
 
-// 2^x by the hardware approximation (ex2.approx.ftz: ~2 ulp; results below 2^-126 flush to zero,
-// which for the decays exp(dt A) <= 1 of the scans changes nothing that is added to a state).
-__device__ __forceinline__ float ex2f(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 __device__ __forceinline__ float2 ex2_2(float2 x) { return make_float2(ex2f(x.x), ex2f(x.y)); }
 // The same, never merged with an equal expression elsewhere: a kernel that re-derives a value instead
 // of keeping it live in registers uses this so that the compiler cannot reuse the earlier result.

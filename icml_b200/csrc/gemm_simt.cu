@@ -343,6 +343,8 @@ extern "C" int pgf_gemm_ex(int64_t M, int64_t N, int64_t K, const void* A, int a
   Gemm g = gemm_make(M, N, K, A, a_dtype, lda, a_trans, B, b_dtype, ldb, b_trans, D, d_dtype, ldd);
   if (epi) g.epi = *epi;
   PGF_CHECK_ARG(!g.epi.accumulate || d_dtype == PGF_DTYPE_F32, "gemm: accumulate needs float32 D");
+  PGF_CHECK_ARG(g.epi.kind >= PGF_EPI_NONE && g.epi.kind <= PGF_EPI_DRELU, "gemm: bad epilogue kind %d",
+                g.epi.kind);
   PGF_CHECK_ARG(!(g.epi.kind == PGF_EPI_DGELU || g.epi.kind == PGF_EPI_DRELU) || g.epi.aux,
                 "gemm: DGELU/DRELU need aux");
   PGF_CHECK_ARG(!ws || (reinterpret_cast<uintptr_t>(ws) & 15) == 0, "gemm: workspace must be 16-byte aligned");

@@ -56,7 +56,7 @@ enum { TC_GENERIC = 0, TC_CE_FWD = 1, TC_CE_BWD = 2 };
 // the single all-modes kernel spent a measurable share of its issue slots on instruction-cache misses):
 //   PLAIN: generic, no activation (bias / addend / accumulate);  ACT: GELU or ReLU (+ pre-activation);
 //   DACT: GELU' or ReLU' with the saved pre-activation;  CE_FWD / CE_BWD: the cross-entropy modes.
-enum { EK_PLAIN = 0, EK_ACT = 1, EK_DACT = 2, EK_CE_FWD = 3, EK_CE_BWD = 4, EK_COUNT = 5 };
+enum { EK_PLAIN = 0, EK_ACT = 1, EK_DACT = 2, EK_CE_FWD = 3, EK_CE_BWD = 4 };
 
 
 struct TcParams {

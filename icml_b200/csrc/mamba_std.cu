@@ -98,9 +98,10 @@ __device__ __forceinline__ AConst load_A(const Args& a, const Lane& l) {
   return c;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// SiLU and its derivative through sigmoid(x) from exp(-|x|) (common.cuh; ~3 ulp).
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_from(x, exp_neg_abs(x)); }
 __device__ __forceinline__ float silu_prime_f(float x) {
-  const float s = 1.0f / (1.0f + expf(-x));
+  const float s = sigmoid_from(x, exp_neg_abs(x));
   return s * (1.0f + x * (1.0f - s));
 }
 
@@ -128,12 +129,13 @@ __device__ __forceinline__ void pref_store(const Pref& r, const Lane& l, bool bw
   for (int q = 0; q < 2; ++q) {
     const int idx = l.tid + q * THREADS;
     const int t = idx / DC, dl = idx % DC;
-    st.dt[t][dl] = softplus_f(r.dtr[q]);
+    const float y = exp_neg_abs(r.dtr[q]);
+    st.dt[t][dl] = softplus_from(r.dtr[q], y);
     st.u[t][dl] = r.u[q];
     if (bwd) {
       st.zs[t][dl] = r.g[q] * silu_f(r.z[q]);
       st.gs[t][dl] = r.g[q] * silu_prime_f(r.z[q]);
-      st.sig[t][dl] = sigmoid_f(r.dtr[q]);
+      st.sig[t][dl] = sigmoid_from(r.dtr[q], y);
     } else {
       st.zs[t][dl] = silu_f(r.z[q]);
     }
@@ -153,7 +155,7 @@ __device__ __forceinline__ void step_fwd(const Stage& st, int i, int dl, int nq,
   const float du = dt * uu;
 #pragma unroll
   for (int j = 0; j < NS; ++j) {
-    const float ez = exp2f(dt * K.A2[j]);
+    const float ez = ex2f(dt * K.A2[j]);
     h[j] = ez * h[j] + du * Bv[j];
     e_out[j] = ez;
   }
@@ -285,7 +287,7 @@ __global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
 #pragma unroll
         for (int j = 0; j < NS; ++j) {
           dlt[j] = anext[j] * dlt[j] + dy * Cv[j];
-          anext[j] = exp2f(dt * K.A2[j]);
+          anext[j] = ex2f(dt * K.A2[j]);
         }
         if (t > l.s) sdt2 += dt;
         dt_first = dt;

@@ -177,14 +177,15 @@ __device__ __forceinline__ void pref_store(const Pref& r, const Lane& l, bool bw
   for (int q = 0; q < 2; ++q) {
     const int idx = l.tid + q * SSM_THREADS;
     const int t = idx / DC, dl = idx % DC;
-    const float dt = softplus_f(r.dtin[q]);
+    const float y = exp_neg_abs(r.dtin[q]);
+    const float dt = softplus_from(r.dtin[q], y);
     st.dt[t][dl] = dt;
-    st.rdt[t][dl] = 1.0f / dt;
+    st.rdt[t][dl] = rcpf(dt);
     st.u[t][dl] = r.u[q];
     if (bwd) {
       st.gg[t][dl] = r.g[q];
       st.dh[t][dl] = r.g[q] * r.sc[q] * r.ap[q];
-      st.sig[t][dl] = sigmoid_f(r.dtin[q]);
+      st.sig[t][dl] = sigmoid_from(r.dtin[q], y);
     }
   }
   {
