@@ -344,13 +344,31 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs
   if (l.ch) ld_states(a.hC + ((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS, H);
   float S_run = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
+  // write-out operands of this thread's two (token, channel) slots per sub-chunk -- the slots its
+  // staging loads cover -- held in registers: u from those loads, y0 loaded with them (a sub-chunk
+  // ahead), D and scale of its fixed channel
+  const int64_t d_out = int64_t(l.grp) * DC + l.tid % DC;
+  const float D_out = d_out < a.D ? a.Dp[d_out] : 0.f, sc_out = d_out < a.D ? a.scale[d_out] : 0.f;
+  auto load_y0 = [&](int64_t s0, float y0v[2]) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int64_t tok = s0 + (l.tid + q * SSM_THREADS) / DC;
+      y0v[q] = (tok < l.e && d_out < a.D) ? a.y0[(l.b * a.L + tok) * a.D + d_out] : 0.f;
+    }
+  };
   Pref r;
+  float y0c[2], y0n[2], uc[2];
   pref_load(a, l, l.s, false, r);
+  load_y0(l.s, y0c);
   pref_store(r, l, false, stg[0]);
+  uc[0] = r.u[0]; uc[1] = r.u[1];
   __syncthreads();
   for (int k = 0; k < nsub; ++k) {
     const int nt = sub_len(l, k);
-    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    if (k + 1 < nsub) {
+      pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+      load_y0(l.s + int64_t(k + 1) * ST, y0n);
+    }
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
@@ -371,13 +389,15 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs
       const int idx = l.tid + q * SSM_THREADS;
       const int t = idx / DC, dl = idx % DC;
       const int64_t tok = l.s + int64_t(k) * ST + t;
-      const int64_t d = int64_t(l.grp) * DC + dl;
-      if (tok < l.e && d < a.D) {
-        const int64_t o = (l.b * a.L + tok) * a.D + d;
-        // u from global memory: the stage of this sub-chunk may already be refilled by faster threads
-        const float yc = a.y0[o] + ybuf[k & 1][t][dl];
-        stv(a.y, a.y_bf16, o, (act_apply(a.act, yc) + a.Dp[d] * ldv(a.u, a.u_bf16, o)) * a.scale[d]);
+      if (tok < l.e && d_out < a.D) {
+        const int64_t o = (l.b * a.L + tok) * a.D + d_out;
+        const float yc = y0c[q] + ybuf[k & 1][t][dl];
+        stv(a.y, a.y_bf16, o, (act_apply(a.act, yc) + D_out * uc[q]) * sc_out);
       }
+    }
+    if (k + 1 < nsub) {
+      uc[0] = r.u[0]; uc[1] = r.u[1];
+      y0c[0] = y0n[0]; y0c[1] = y0n[1];
     }
   }
 }
@@ -568,6 +588,7 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
     }
   };
   const float Dd = l.ch ? a.Dp[l.d] : 0.f;
+  const float sc = l.ch ? a.scale[l.d] : 0.f;  // in a register: the loop's stores may alias a.scale
   const int64_t cb = l.b * a.nC + l.c;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
 
@@ -677,7 +698,7 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
       hc += __shfl_xor_sync(0xffffffffu, hc, 2);
       if (valid && l.nq == 0) {
         const float gg = S.gg[i][l.dl];
-        const float din = l.ch ? gg * a.scale[l.d] : 0.f;
+        const float din = gg * sc;
         gb[i * DC + l.dl] = gdt * S.sig[i][l.dl];
         gb[ST * DC + i * DC + l.dl] = din * Dd + gur;
         accD = fmaf(din, uu, accD);
