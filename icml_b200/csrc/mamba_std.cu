@@ -10,6 +10,7 @@
 // (backward).  Channels are the E = expand*d_model inner channels.
 #include "gemm.cuh"
 #include "scan_compose.cuh"
+#include "f32x2.cuh"
 
 namespace pgf {
 namespace mstd {
@@ -161,6 +162,28 @@ __device__ __forceinline__ void step_fwd(const Stage& st, int i, int dl, int nq,
   }
 }
 
+// The forward-direction kernels step the thread's NS states as two packed f32x2 pairs.
+constexpr int NP = NS / 2;
+__device__ __forceinline__ void a2_pairs(const AConst& K, float2 A2p[NP]) {
+  A2p[0] = f2(K.A2[0], K.A2[1]);
+  A2p[1] = f2(K.A2[2], K.A2[3]);
+}
+__device__ __forceinline__ void step_fwd2(const Stage& st, int i, int dl, int nq, const float2 A2p[NP], float2 h[NP]) {
+  const float dt = st.dt[i][dl];
+  const float2 dt2 = f2(dt), du = f2(dt * st.u[i][dl]);
+  const float4 Bq = st.B[i][nq];
+  h[0] = fma2(ex2_2(mul2(dt2, A2p[0])), h[0], mul2(du, lo2(Bq)));
+  h[1] = fma2(ex2_2(mul2(dt2, A2p[1])), h[1], mul2(du, hi2(Bq)));
+}
+__device__ __forceinline__ void ld_pairs(const float* __restrict__ src, float2 v[NP]) {
+  const float4 q = *reinterpret_cast<const float4*>(src);
+  v[0] = lo2(q);
+  v[1] = hi2(q);
+}
+__device__ __forceinline__ void st_pairs(float* __restrict__ dst, const float2 v[NP]) {
+  *reinterpret_cast<float4*>(dst) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+}
+
 // ---------------------------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------------------------
@@ -168,7 +191,8 @@ __global__ void __launch_bounds__(THREADS) chunk_fwd_kernel(const Args a) {
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l);
-  float h[NS] = {0.f, 0.f, 0.f, 0.f}, e[NS];
+  float2 A2p[NP], h[NP] = {f2(0.f), f2(0.f)};
+  a2_pairs(K, A2p);
   float sdt = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   Pref r;
@@ -176,12 +200,14 @@ __global__ void __launch_bounds__(THREADS) chunk_fwd_kernel(const Args a) {
   pref_store(r, l, false, stg[0]);
   __syncthreads();
   for (int k = 0; k < nsub; ++k) {
+    const int64_t rem = l.e - (l.s + int64_t(k) * ST);
+    const int nt = rem < ST ? int(rem) : ST;
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i)
-      if (l.s + int64_t(k) * ST + i < l.e) {
-        step_fwd(S, i, l.dl, l.nq, K, h, e);
+      if (i < nt) {
+        step_fwd2(S, i, l.dl, l.nq, A2p, h);
         sdt += S.dt[i][l.dl];
       }
     if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
@@ -189,8 +215,7 @@ __global__ void __launch_bounds__(THREADS) chunk_fwd_kernel(const Args a) {
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
-#pragma unroll
-  for (int j = 0; j < NS; ++j) a.hloc[(cb * a.E + l.d) * NST + l.nq * NS + j] = h[j];
+  st_pairs(a.hloc + (cb * a.E + l.d) * NST + l.nq * NS, h);
   if (l.nq == 0) a.sdt[cb * a.E + l.d] = sdt;
 }
 
@@ -212,10 +237,9 @@ __global__ void __launch_bounds__(THREADS) out_fwd_kernel(const Args a) {
   __shared__ float ybuf[2][ST][DC];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l);
-  float h[NS], e[NS];
-#pragma unroll
-  for (int j = 0; j < NS; ++j)
-    h[j] = l.ch ? a.hC[((l.b * (a.nC + 1) + l.c) * a.E + l.d) * NST + l.nq * NS + j] : 0.f;
+  float2 A2p[NP], h[NP] = {f2(0.f), f2(0.f)};
+  a2_pairs(K, A2p);
+  if (l.ch) ld_pairs(a.hC + ((l.b * (a.nC + 1) + l.c) * a.E + l.d) * NST + l.nq * NS, h);
   const float Dd = l.ch ? a.Dp[l.d] : 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   const int KS = int((a.Tc + ST - 1) / ST);
@@ -225,21 +249,16 @@ __global__ void __launch_bounds__(THREADS) out_fwd_kernel(const Args a) {
   __syncthreads();
   for (int k = 0; k < nsub; ++k) {
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
-    if (a.ckpt_write && l.ch) {
-      float* cp = a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS;
-#pragma unroll
-      for (int j = 0; j < NS; ++j) cp[j] = h[j];
-    }
+    if (a.ckpt_write && l.ch) st_pairs(a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS, h);
+    const int64_t rem = l.e - (l.s + int64_t(k) * ST);
+    const int nt = rem < ST ? int(rem) : ST;
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
-      if (l.s + int64_t(k) * ST + i < l.e) {
-        step_fwd(S, i, l.dl, l.nq, K, h, e);
+      if (i < nt) {
+        step_fwd2(S, i, l.dl, l.nq, A2p, h);
         const float4 Cq = S.C[i][l.nq];
-        float yc = Cq.x * h[0];
-        yc = fmaf(Cq.y, h[1], yc);
-        yc = fmaf(Cq.z, h[2], yc);
-        yc = fmaf(Cq.w, h[3], yc);
+        float yc = hsum2(fma2(hi2(Cq), h[1], mul2(lo2(Cq), h[0])));
         yc += __shfl_xor_sync(0xffffffffu, yc, 1);
         yc += __shfl_xor_sync(0xffffffffu, yc, 2);
         if (l.nq == 0) ybuf[k & 1][i][l.dl] = (yc + Dd * S.u[i][l.dl]) * S.zs[i][l.dl];
@@ -265,8 +284,8 @@ __global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l);
-  float dlt[NS] = {0.f, 0.f, 0.f, 0.f};
-  float anext[NS] = {1.f, 1.f, 1.f, 1.f};
+  float2 A2p[NP], dlt[NP] = {f2(0.f), f2(0.f)}, anext[NP] = {f2(1.f), f2(1.f)};
+  a2_pairs(K, A2p);
   float sdt2 = 0.f, dt_first = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   Pref r;
@@ -281,14 +300,12 @@ __global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
       const int64_t t = l.s + int64_t(k) * ST + i;
       if (t < l.e) {
         const float dt = S.dt[i][l.dl];
-        const float dy = S.zs[i][l.dl];
+        const float2 dy = f2(S.zs[i][l.dl]), dt2 = f2(dt);
         const float4 Cq = S.C[i][l.nq];
-        const float Cv[NS] = {Cq.x, Cq.y, Cq.z, Cq.w};
-#pragma unroll
-        for (int j = 0; j < NS; ++j) {
-          dlt[j] = anext[j] * dlt[j] + dy * Cv[j];
-          anext[j] = ex2f(dt * K.A2[j]);
-        }
+        dlt[0] = fma2(anext[0], dlt[0], mul2(dy, lo2(Cq)));
+        dlt[1] = fma2(anext[1], dlt[1], mul2(dy, hi2(Cq)));
+        anext[0] = ex2_2(mul2(dt2, A2p[0]));
+        anext[1] = ex2_2(mul2(dt2, A2p[1]));
         if (t > l.s) sdt2 += dt;
         dt_first = dt;
       }
@@ -298,8 +315,7 @@ __global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
-#pragma unroll
-  for (int j = 0; j < NS; ++j) a.dloc[(cb * a.E + l.d) * NST + l.nq * NS + j] = dlt[j];
+  st_pairs(a.dloc + (cb * a.E + l.d) * NST + l.nq * NS, dlt);
   if (l.nq == 0) {
     a.sdt2[cb * a.E + l.d] = sdt2;
     a.dt0[cb * a.E + l.d] = dt_first;
