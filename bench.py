@@ -293,7 +293,7 @@ def zipf_ids(n, vocab, seed, s=1.1):
 
 PROF_NAMES = {0: "ssm_chunk_fwd", 1: "ssm_compose", 2: "ssm_out_fwd", 3: "ssm_chunk_bwd",
               4: "ssm_main_bwd", 5: "gemm_tc", 6: "gemm_simt", 7: "rmsnorm_fwd", 8: "rmsnorm_bwd",
-              9: "embedding", 10: "ce"}
+              9: "embedding", 10: "ce", 11: "adamw"}
 
 
 def run_gpu(a, rank, world, local_rank):
@@ -333,9 +333,17 @@ def run_gpu(a, rank, world, local_rank):
     inp = inp_host.to(dev)
     tgt = tgt_host.to(dev)
 
+    flat_opt = getattr(model, "optimizer_kind", "torch") == "flat"
+
     def allreduce_grads():
         if pg is None:
-            return
+            return False
+        if flat_opt:
+            # one all-reduce over the optimizer's flat gradient buffer, then the step without regather
+            model.optimizer.gather()
+            torch.distributed.all_reduce(model.optimizer.grad)
+            model.optimizer.grad.div_(world)
+            return True
         grads = [p.grad for p in model.params]
         flat = torch.cat([g.reshape(-1) for g in grads])
         torch.distributed.all_reduce(flat)
@@ -345,6 +353,7 @@ def run_gpu(a, rank, world, local_rank):
             n = g.numel()
             g.copy_(flat[o:o + n].view_as(g))
             o += n
+        return False
 
     from icml_b200 import seqpar
     sp = seqpar.SeqGroup.from_default() if (world > 1 and a.parallel == "sp") else None
@@ -354,11 +363,15 @@ def run_gpu(a, rank, world, local_rank):
         if sp is not None:
             loss, grads = seqpar.lm_forward_backward(model, x, y, sp)  # gradients already summed
             model._assign(grads)
+            gathered = False
         else:
             loss, grads = model.forward_backward(x, y)
             model._assign(grads)
-            allreduce_grads()
-        model.optimizer.step()
+            gathered = allreduce_grads()
+        if gathered:
+            model.optimizer.step(gather=False)
+        else:
+            model.optimizer.step()
         return loss
 
     for _ in range(a.warmup):

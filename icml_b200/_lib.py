@@ -86,6 +86,12 @@ SIGNATURES = {
     "pgf_ssm_summary": (c_int, [P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, P, c_size_t, P]),
     "pgf_ssm_bwd_summary": (c_int, [P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P,
                                     c_size_t, P]),
+    "pgf_adamw_step": (c_int, [P, P, P, P, I64, c_float, c_float, c_float, c_float, c_float, P, P, P]),
+    "pgf_adamw_step_multi": (c_int, [P, P, P, I64, P, P, P, c_int, c_float, c_float, c_float, c_float, c_float,
+                                     P, P, P]),
+    "pgf_gather_multi": (c_int, [P, I64, P, P, P, c_int, P]),
+    "pgf_grad_norm_workspace": (c_size_t, [I64]),
+    "pgf_grad_norm": (c_int, [P, I64, P, c_float, P, P, c_size_t, P]),
 }
 
 

@@ -40,7 +40,8 @@ void clear_error();
 // Kernel-launch accounting and optional CUDA-event timing of selected kernels (abi.cu).
 enum ProfId {
   PROF_SSM_CHUNK_FWD = 0, PROF_SSM_COMPOSE, PROF_SSM_OUT_FWD, PROF_SSM_CHUNK_BWD, PROF_SSM_MAIN_BWD,
-  PROF_GEMM_TC, PROF_GEMM_SIMT, PROF_RMSNORM_FWD, PROF_RMSNORM_BWD, PROF_EMBEDDING, PROF_CE, PROF_COUNT
+  PROF_GEMM_TC, PROF_GEMM_SIMT, PROF_RMSNORM_FWD, PROF_RMSNORM_BWD, PROF_EMBEDDING, PROF_CE, PROF_OPTIM,
+  PROF_COUNT
 };
 void count_launch();
 void prof_begin(int id, cudaStream_t s);

@@ -25,9 +25,13 @@ class PGFLanguageModel:
                  block_size: int, device, act_dtype=torch.float32, lr: float = 1e-3,
                  weight_decay: float = 0.01, tie_embeddings: bool = False, init_std: float = 0.02,
                  variant: str = "reference", final_norm: bool = False, expand: int = 2, d_conv: int = 4,
-                 dt_rank: Optional[int] = None):
+                 dt_rank: Optional[int] = None, optimizer: Optional[str] = None,
+                 max_grad_norm: Optional[float] = None):
         """variant "reference": the reference's PGFMambaBlock; "std": the Mamba-standard block
-        (pgf_mamba_std.PGFMambaStdBlock).  final_norm adds an RMSNorm before the LM head."""
+        (pgf_mamba_std.PGFMambaStdBlock).  final_norm adds an RMSNorm before the LM head.
+        optimizer "flat" (default on a GPU): AdamW over one flat parameter buffer on libpgf's kernels
+        (icml_b200.optim.FlatAdamW); "torch": torch.optim.AdamW (fused on a GPU).  max_grad_norm
+        clips the global gradient norm first (flat optimizer only)."""
         self.vocab_size = vocab_size
         self.d_model = d_model
         self.block_size = block_size
@@ -52,10 +56,19 @@ class PGFLanguageModel:
         self.params = [self.emb_weight] + ([] if tie_embeddings else [self.lm_head_weight]) + \
             list(self.backbone.parameters()) + (list(self.final_norm.parameters()) if final_norm else [])
         on_gpu = self.device.type == "cuda"
-        # capturable: the optimizer keeps its step count on the device, so the step can be captured
-        # in a CUDA graph (GraphedStep)
-        self.optimizer = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay, fused=on_gpu,
-                                           capturable=on_gpu)
+        self.optimizer_kind = optimizer or ("flat" if on_gpu else "torch")
+        if self.optimizer_kind == "flat":
+            from .optim import FlatAdamW
+            self.optimizer = FlatAdamW(self.params, lr=lr, weight_decay=weight_decay, max_grad_norm=max_grad_norm)
+        elif self.optimizer_kind == "torch":
+            if max_grad_norm is not None:
+                raise ValueError("max_grad_norm needs optimizer='flat'")
+            # capturable: the optimizer keeps its step count on the device, so the step can be
+            # captured in a CUDA graph (GraphedStep)
+            self.optimizer = torch.optim.AdamW(self.params, lr=lr, weight_decay=weight_decay, fused=on_gpu,
+                                               capturable=on_gpu)
+        else:
+            raise ValueError(f"optimizer: {optimizer!r}")
 
     @torch.no_grad()
     def load_(self, emb: torch.Tensor, lm_head: torch.Tensor, backbone_state: Dict[str, torch.Tensor]):

@@ -69,6 +69,7 @@ int pgf_version(void);
 #define PGF_PROF_RMSNORM_BWD 8
 #define PGF_PROF_EMBEDDING 9
 #define PGF_PROF_CE 10 /* the fused LM-head + cross-entropy tensor-core passes */
+#define PGF_PROF_OPTIM 11 /* pgf_adamw_step */
 long long pgf_launch_count(void);
 /* Reads and clears the fault flag of the tensor-core engine: 1 if a bounded mbarrier wait expired
  * in a tcgen05 kernel since the last call (the kernel then skipped its epilogue and returned).
@@ -349,6 +350,36 @@ int pgf_mamba_mixer_bwd_saved(const void* x, const void* g_out, const float* in_
                               const void* saved, size_t saved_bytes, int64_t Bsz, int64_t L, int64_t d,
                               int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes,
                               pgf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * The optimizer step after the PGF backward: the reference calls torch.optim.AdamW(lr=1e-3,
+ * weight_decay=0.01, betas (0.9, 0.999), eps 1e-8) on all parameters (train_wikitext_rebuttal.py:
+ * 77,148).  Here over ONE flat float32 buffer of n parameters with its flat gradient and moments.
+ * pgf_adamw_step: that optimizer's update per element (decoupled weight decay, bias-corrected
+ * moments) with the step count t read from and incremented in *step (device float, so a captured
+ * step replays with the right t); grad_scale (device float or NULL) multiplies every gradient (the
+ * clip factor).  All buffers 16-byte aligned.
+ * pgf_grad_norm: the global L2 norm of the flat gradient (torch.nn.utils.clip_grad_norm_ over all
+ * parameters) into *norm, and, when clip is non-NULL, the factor min(1, max_norm / (norm + 1e-6))
+ * into *clip; deterministic (fixed block partition, partials summed in block order). */
+int pgf_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t n, float lr,
+                   float beta1, float beta2, float eps, float weight_decay, float* step, const float* grad_scale,
+                   pgf_stream_t stream);
+/* pgf_adamw_step_multi: the same update with the gradients left in their own tensors: tensor i
+ * (grads[i], NULL = zero gradient) covers the flat elements [offsets[i], offsets[i] + sizes[i]);
+ * offsets multiples of 4.  grads / offsets / sizes are host arrays, read during the call (the
+ * chunk table travels in the launch parameters, so a captured launch keeps it).
+ * pgf_gather_multi: copies those tensors into the flat buffer dst (for a flat gradient that is then
+ * all-reduced or clipped). */
+int pgf_adamw_step_multi(float* param, float* exp_avg, float* exp_avg_sq, int64_t n, const float* const* grads,
+                         const int64_t* offsets, const int64_t* sizes, int count, float lr, float beta1,
+                         float beta2, float eps, float weight_decay, float* step, const float* grad_scale,
+                         pgf_stream_t stream);
+int pgf_gather_multi(float* dst, int64_t n, const float* const* srcs, const int64_t* offsets, const int64_t* sizes,
+                     int count, pgf_stream_t stream);
+size_t pgf_grad_norm_workspace(int64_t n);
+int pgf_grad_norm(const float* grad, int64_t n, float* norm, float max_norm, float* clip, void* ws,
+                  size_t ws_bytes, pgf_stream_t stream);
 
 #ifdef __cplusplus
 }
