@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "all"],
                     help="component microbenchmarks instead of the LM step (RMSNorm [8,4096,1024]; FFN "
                          "1024-4096-1024 on 32768 tokens; LM head + CE d=1024, vocab 50257, 32768 tokens)")
+    ap.add_argument("--stash", default="device", choices=["device", "host"],
+                    help="where layer inputs wait for the backward: device memory or pinned host memory")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of the CUDA-graph captured step (1 GPU)")
     ap.add_argument("--parallel", default="sp", choices=["sp", "dp"],
@@ -81,6 +83,8 @@ def config_of(a, world):
         "ssm_variant": ("reference (d_inner = d_model, shared A)" if a.variant == "reference" else
                         "mamba-standard (d_inner 2 d_model, conv1d, gate, per-channel A)"),
         "l2": "per-step working set (weights, optimizer state, activations) > 126 MB L2; no explicit flush",
+        "stash": a.stash,
+        "optimizer": "AdamW (flat parameter buffer, libpgf kernels)",
     }
 
 
@@ -315,9 +319,10 @@ def run_gpu(a, rank, world, local_rank):
     if a.variant == "std":
         model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act,
                                  variant="std", tie_embeddings=True, final_norm=True, expand=2, d_conv=4,
-                                 dt_rank=a.dt_rank)
+                                 dt_rank=a.dt_rank, stash=a.stash)
     else:
-        model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act)
+        model = PGFLanguageModel(a.vocab, a.d_model, 16, a.d_ff, a.layers, a.block_size, dev, act_dtype=act,
+                                 stash=a.stash)
     for p in model.params:  # identical replicas
         if pg is not None:
             torch.distributed.broadcast(p.data, 0)

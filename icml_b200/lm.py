@@ -20,18 +20,92 @@ from .pgf_mamba_block import PGFMambaBlock, PGFMambaSequential
 from .pgf_rmsnorm import RMSNorm
 
 
+class LayerStash:
+    """Where the step keeps each layer's input between its forward and its backward (the
+    ``layer_inputs`` list of train_wikitext_rebuttal.py:105-108, popped at :133).
+
+    policy "device": on the GPU (what the reference does; bf16 when the activations are bf16).
+    policy "host": each input except the last layer's is copied to pinned host memory on a copy
+    stream as soon as it is produced (its device memory is released when the copy has run), and the
+    backward brings input i-1 back while layer i runs its backward, so at most two stashed inputs
+    occupy device memory instead of one per layer.  The copies are ordered against the compute
+    stream with stream waits only, so the step stays capturable in a CUDA graph (the pinned buffers
+    are allocated at the first step and reused).
+    """
+
+    def __init__(self, policy: str = "device"):
+        if policy not in ("device", "host"):
+            raise ValueError(f"stash policy: {policy!r}")
+        self.policy = policy
+        self._host: Dict[int, torch.Tensor] = {}
+        self._stream: Optional[torch.cuda.Stream] = None
+        self.items: List = []
+
+    def begin(self, n: int):
+        self.items = [None] * n
+        self._where = ["device"] * n
+
+    def _copy_stream(self, dev) -> torch.cuda.Stream:
+        if self._stream is None:
+            self._stream = torch.cuda.Stream(device=dev)
+        return self._stream
+
+    def put(self, i: int, x: torch.Tensor):
+        n = len(self.items)
+        if self.policy == "device" or i == n - 1 or not x.is_cuda:
+            self.items[i] = x
+            return
+        h = self._host.get(i)
+        if h is None or h.shape != x.shape or h.dtype != x.dtype:
+            h = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+            self._host[i] = h
+        cur = torch.cuda.current_stream(x.device)
+        cs = self._copy_stream(x.device)
+        cs.wait_stream(cur)
+        with torch.cuda.stream(cs):
+            h.copy_(x, non_blocking=True)
+        x.record_stream(cs)  # x's memory returns to the allocator once the copy has run
+        self.items[i] = h
+        self._where[i] = "host"
+
+    def prefetch(self, i: int, dev):
+        """Start bringing input i back (on the copy stream, after its own download)."""
+        if self._where[i] != "host":
+            return
+        h = self.items[i]
+        d = torch.empty(h.shape, dtype=h.dtype, device=dev)  # allocated on the compute stream
+        cs = self._copy_stream(dev)
+        cs.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(cs):
+            d.copy_(h, non_blocking=True)
+        d.record_stream(cs)
+        self.items[i] = d
+        self._where[i] = "inflight"
+
+    def take(self, i: int, dev) -> torch.Tensor:
+        if self._where[i] == "host":
+            self.prefetch(i, dev)
+        if self._where[i] == "inflight":
+            torch.cuda.current_stream(dev).wait_stream(self._copy_stream(dev))
+            self._where[i] = "device"
+        x = self.items[i]
+        self.items[i] = None
+        return x
+
+
 class PGFLanguageModel:
     def __init__(self, vocab_size: int, d_model: int, d_state: int, d_ff: int, n_layers: int,
                  block_size: int, device, act_dtype=torch.float32, lr: float = 1e-3,
                  weight_decay: float = 0.01, tie_embeddings: bool = False, init_std: float = 0.02,
                  variant: str = "reference", final_norm: bool = False, expand: int = 2, d_conv: int = 4,
                  dt_rank: Optional[int] = None, optimizer: Optional[str] = None,
-                 max_grad_norm: Optional[float] = None):
+                 max_grad_norm: Optional[float] = None, stash: str = "device"):
         """variant "reference": the reference's PGFMambaBlock; "std": the Mamba-standard block
         (pgf_mamba_std.PGFMambaStdBlock).  final_norm adds an RMSNorm before the LM head.
         optimizer "flat" (default on a GPU): AdamW over one flat parameter buffer on libpgf's kernels
         (icml_b200.optim.FlatAdamW); "torch": torch.optim.AdamW (fused on a GPU).  max_grad_norm
-        clips the global gradient norm first (flat optimizer only)."""
+        clips the global gradient norm first (flat optimizer only).  stash: where the layer inputs wait
+        for the backward, "device" or "host" (pinned host memory; LayerStash)."""
         self.vocab_size = vocab_size
         self.d_model = d_model
         self.block_size = block_size
@@ -53,6 +127,7 @@ class PGFLanguageModel:
         self.variant = variant
         self.backbone = PGFMambaSequential(blocks).to(device)
         self.final_norm = RMSNorm(d_model).to(device) if final_norm else None
+        self.stash = LayerStash(stash)
         self.params = [self.emb_weight] + ([] if tie_embeddings else [self.lm_head_weight]) + \
             list(self.backbone.parameters()) + (list(self.final_norm.parameters()) if final_norm else [])
         on_gpu = self.device.type == "cuda"
@@ -84,9 +159,10 @@ class PGFLanguageModel:
         B, L = input_ids.shape
         d = self.d_model
         x = ops.embedding_fwd(input_ids, self.emb_weight, dtype=self.act_dtype)
-        stash: List[torch.Tensor] = []
-        for layer in self.backbone.layers:
-            stash.append(x)
+        stash = self.stash
+        stash.begin(self.n_layers)
+        for i, layer in enumerate(self.backbone.layers):
+            stash.put(i, x)
             x = layer.pgf_forward(x)
         xf = ops.rmsnorm_fwd(x, self.final_norm.weight, self.final_norm.eps) if self.final_norm is not None else x
         h = xf.reshape(-1, d)
@@ -101,7 +177,11 @@ class PGFLanguageModel:
             grads["final_norm"] = gfw
         del x, xf, h, gh
         for i in reversed(range(self.n_layers)):
-            res = self.backbone.layers[i].pgf_backward(stash.pop(), g)
+            xi = stash.take(i, g.device)
+            if i > 0:
+                stash.prefetch(i - 1, g.device)  # overlaps this layer's backward
+            res = self.backbone.layers[i].pgf_backward(xi, g)
+            del xi
             for k, v in res["grads"].items():
                 grads[f"layers.{i}.{k}"] = v
             g = res["grad_input"]
@@ -185,4 +265,4 @@ class GraphedStep:
         self.loss = None
 
 
-__all__ = ["PGFLanguageModel", "GraphedStep"]
+__all__ = ["PGFLanguageModel", "GraphedStep", "LayerStash"]

@@ -6,9 +6,9 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def _pair(variant):
+def _pair(variant, stash="device"):
     from icml_b200.lm import PGFLanguageModel
-    kw = dict(act_dtype=torch.bfloat16, variant=variant)
+    kw = dict(act_dtype=torch.bfloat16, variant=variant, stash=stash)
     if variant == "std":
         kw.update(tie_embeddings=True, final_norm=True, expand=2, d_conv=4, dt_rank=4)
     torch.manual_seed(5)
@@ -20,10 +20,10 @@ def _pair(variant):
     return m1, m2
 
 
-@pytest.mark.parametrize("variant", ["reference", "std"])
-def test_graphed_step_equals_eager(variant):
+@pytest.mark.parametrize("variant,stash", [("reference", "device"), ("std", "device"), ("reference", "host")])
+def test_graphed_step_equals_eager(variant, stash):
     from icml_b200.lm import GraphedStep
-    m1, m2 = _pair(variant)
+    m1, m2 = _pair(variant, stash)
     g = torch.Generator().manual_seed(9)
     batches = [(torch.randint(0, 301, (2, 200), generator=g), torch.randint(0, 301, (2, 200), generator=g))
                for _ in range(3)]
@@ -39,3 +39,24 @@ def test_graphed_step_equals_eager(variant):
     assert graph_losses == eager_losses
     for p1, p2 in zip(m1.params, m2.params):
         assert torch.equal(p1, p2)
+
+
+def test_host_stash_equals_device_stash():
+    """Layer inputs parked in pinned host memory between the passes give bitwise the same step."""
+    from icml_b200.lm import PGFLanguageModel
+    torch.manual_seed(6)
+    kw = dict(act_dtype=torch.bfloat16)
+    m1 = PGFLanguageModel(301, 64, 16, 128, 3, 64, DEV, stash="device", **kw)
+    m2 = PGFLanguageModel(301, 64, 16, 128, 3, 64, DEV, stash="host", **kw)
+    with torch.no_grad():
+        for p1, p2 in zip(m1.params, m2.params):
+            p2.copy_(p1)
+    g = torch.Generator().manual_seed(10)
+    x = torch.randint(0, 301, (2, 300), generator=g).to(DEV)
+    y = torch.randint(0, 301, (2, 300), generator=g).to(DEV)
+    l1, g1 = m1.forward_backward(x, y)
+    l2, g2 = m2.forward_backward(x, y)
+    assert torch.equal(l1, l2)
+    for k in g1:
+        assert torch.equal(g1[k], g2[k]), k
+    assert len(m2.stash._host) == 2  # every layer input but the last went through host memory
