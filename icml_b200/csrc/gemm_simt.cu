@@ -135,21 +135,56 @@ static int run_gemm_simt_split(const Gemm& g, int slices, float* part, int* laun
 }
 
 // D = epi(sum over slices of the partial products), slices added in index order.
+// Sum of the K slices' partial products, in slice order, then the epilogue.  A thread owns VEC
+// adjacent outputs (float4 loads when N % 4 == 0) and keeps SK slices' loads in flight before it
+// adds them (the adds stay in slice order: the same sum as one slice at a time).
+template <int VEC>
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int slices, int64_t M, int64_t N,
                                      const pgf_epilogue e, void* D, int d_bf16, int64_t ldd) {
-  const int64_t MN = M * N;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < MN; i += int64_t(gridDim.x) * blockDim.x) {
-    float v = 0.f;
-    for (int z = 0; z < slices; ++z) v += part[z * MN + i];
-    const int64_t m = i / N, n = i - m * N;
-    epi_store(e, D, d_bf16, ldd, m, n, v);
+  constexpr int SK = 8;
+  const int64_t MN = M * N, nv = MN / VEC;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += int64_t(gridDim.x) * blockDim.x) {
+    float v[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = 0.f;
+    int z = 0;
+    for (; z + SK <= slices; z += SK) {
+      float a[SK][VEC];
+#pragma unroll
+      for (int q = 0; q < SK; ++q) {
+        if (VEC == 4) {
+          const float4 t = __ldg(reinterpret_cast<const float4*>(part + (z + q) * MN) + i);
+          a[q][0] = t.x; a[q][VEC > 1 ? 1 : 0] = t.y; a[q][VEC > 2 ? 2 : 0] = t.z; a[q][VEC > 3 ? 3 : 0] = t.w;
+        } else {
+          a[q][0] = __ldg(part + (z + q) * MN + i);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < SK; ++q)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) v[k] += a[q][k];
+    }
+    for (; z < slices; ++z)
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] += __ldg(part + z * MN + i * VEC + k);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      const int64_t j = i * VEC + k;
+      const int64_t m = j / N, n = j - m * N;
+      epi_store(e, D, d_bf16, ldd, m, n, v[k]);
+    }
   }
 }
 
 static int splitk_finish(const Gemm& g, const float* part, int used, cudaStream_t s) {
-  int64_t blocks = ceil_div(g.M * g.N, 256);
-  if (blocks > 148 * 8) blocks = 148 * 8;
-  splitk_reduce_kernel<<<unsigned(blocks), 256, 0, s>>>(part, used, g.M, g.N, g.epi, g.D, g.d_bf16, g.ldd);
+  const bool vec = g.N % 4 == 0 && aligned(part, 16);
+  int64_t blocks = ceil_div(g.M * g.N / (vec ? 4 : 1), 256);
+  if (blocks > int64_t(sm_count()) * 8) blocks = int64_t(sm_count()) * 8;
+  if (blocks < 1) blocks = 1;
+  if (vec)
+    splitk_reduce_kernel<4><<<unsigned(blocks), 256, 0, s>>>(part, used, g.M, g.N, g.epi, g.D, g.d_bf16, g.ldd);
+  else
+    splitk_reduce_kernel<1><<<unsigned(blocks), 256, 0, s>>>(part, used, g.M, g.N, g.epi, g.D, g.d_bf16, g.ldd);
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
@@ -183,11 +218,11 @@ int run_gemm(const Gemm& g, cudaStream_t s) {
 constexpr int CS_ROWS = 256;
 
 __global__ void colsum_part_kernel(const void* __restrict__ X, int bf16, int64_t M, int64_t N,
-                                   int64_t ld, float* __restrict__ part) {
+                                   int64_t ld, int64_t rows, float* __restrict__ part) {
   const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (n >= N) return;
-  const int64_t r0 = int64_t(blockIdx.y) * CS_ROWS;
-  const int64_t r1 = r0 + CS_ROWS < M ? r0 + CS_ROWS : M;
+  const int64_t r0 = int64_t(blockIdx.y) * rows;
+  const int64_t r1 = r0 + rows < M ? r0 + rows : M;
   float s = 0.f;
   for (int64_t r = r0; r < r1; ++r) s += ldv(X, bf16, r * ld + n);
   part[int64_t(blockIdx.y) * N + n] = s;
@@ -205,10 +240,12 @@ column_reduce_kernel(const float* __restrict__ part, int64_t nparts, int64_t N, 
   float s = 0.f;
   if (c < N) {
     int64_t p = warp;
-    for (; p + 3 * CR_WARPS < nparts; p += 4 * CR_WARPS) {
-      const float a0 = part[p * N + c], a1 = part[(p + CR_WARPS) * N + c];
-      const float a2 = part[(p + 2 * CR_WARPS) * N + c], a3 = part[(p + 3 * CR_WARPS) * N + c];
-      s += a0; s += a1; s += a2; s += a3;
+    for (; p + 7 * CR_WARPS < nparts; p += 8 * CR_WARPS) {
+      float a[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) a[q] = __ldg(part + (p + q * CR_WARPS) * N + c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) s += a[q];
     }
     for (; p < nparts; p += CR_WARPS) s += part[p * N + c];
   }
@@ -229,22 +266,31 @@ int column_reduce(const float* part, int64_t nparts, int64_t N, float* out, int 
   return PGF_OK;
 }
 
-size_t colsum_ws(int64_t M, int64_t N) {
-  return Workspace::round(size_t(ceil_div(M < 1 ? 1 : M, CS_ROWS)) * size_t(N) * 4);
+// Rows per slab (one partial row each): CS_ROWS, halved (down to 32) while the vector kernel's grid
+// would not give every SM four CTAs, so narrow outputs (a few hundred columns) still fill the GPU.
+static int64_t colsum_rows(int64_t M, int64_t N) {
+  int64_t rows = CS_ROWS;
+  const int64_t want = int64_t(sm_count()) * 4;
+  while (rows > 32 && ceil_div(N, 256) * ceil_div(M < 1 ? 1 : M, rows) < want) rows /= 2;
+  return rows;
 }
 
-// Vector form: a CTA sums CS_ROWS rows of 256 columns; a thread owns 8 adjacent columns (one
-// 16-byte load per row in bf16, two in float32), warp w takes rows w, w+8, ... of the slab in order,
-// and the 8 warp partials are added in warp order.  Needs N % 8 == 0 and 16-byte aligned rows.
+size_t colsum_ws(int64_t M, int64_t N) {
+  return Workspace::round(size_t(ceil_div(M < 1 ? 1 : M, colsum_rows(M, N))) * size_t(N) * 4);
+}
+
+// Vector form: a CTA sums a slab of `rows` rows of 256 columns; a thread owns 8 adjacent columns
+// (one 16-byte load per row in bf16, two in float32), warp w takes rows w, w+8, ... of the slab in
+// order, and the 8 warp partials are added in warp order.  Needs N % 8 == 0 and 16-byte aligned rows.
 constexpr int CSV_WARPS = 8;
 __global__ void __launch_bounds__(CSV_WARPS * 32)
-colsum_part_vec_kernel(const void* __restrict__ X, int bf16, int64_t M, int64_t N, int64_t ld,
+colsum_part_vec_kernel(const void* __restrict__ X, int bf16, int64_t M, int64_t N, int64_t ld, int64_t rows,
                        float* __restrict__ part) {
   __shared__ float sm[CSV_WARPS][256 + 4];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t c0 = int64_t(blockIdx.x) * 256 + lane * 8;
-  const int64_t r0 = int64_t(blockIdx.y) * CS_ROWS;
-  const int64_t r1 = r0 + CS_ROWS < M ? r0 + CS_ROWS : M;
+  const int64_t r0 = int64_t(blockIdx.y) * rows;
+  const int64_t r1 = r0 + rows < M ? r0 + rows : M;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (c0 < N) {
     if (bf16) {
@@ -289,15 +335,17 @@ int colsum(const void* X, int bf16, int64_t M, int64_t N, int64_t ld, float* out
     if (!accumulate) PGF_CUDA(cudaMemsetAsync(out, 0, N * 4, s));
     return PGF_OK;
   }
-  const int64_t np = ceil_div(M, CS_ROWS);
+  const int64_t rows = colsum_rows(M, N);
+  const int64_t np = ceil_div(M, rows);
   if (size_t(np) * N * 4 > ws_bytes) { set_error("colsum: workspace too small"); return PGF_ERR_WORKSPACE; }
   if (np > 65535) { set_error("colsum: too many rows"); return PGF_ERR_UNSUPPORTED; }
   float* part = static_cast<float*>(ws);
   const int64_t es = bf16 ? 2 : 4;
   if (N % 8 == 0 && aligned(X, 16) && (ld * es) % 16 == 0) {
-    colsum_part_vec_kernel<<<dim3(ceil_div(N, 256), unsigned(np)), CSV_WARPS * 32, 0, s>>>(X, bf16, M, N, ld, part);
+    colsum_part_vec_kernel<<<dim3(ceil_div(N, 256), unsigned(np)), CSV_WARPS * 32, 0, s>>>(X, bf16, M, N, ld, rows,
+                                                                                          part);
   } else {
-    colsum_part_kernel<<<dim3(ceil_div(N, 128), unsigned(np)), 128, 0, s>>>(X, bf16, M, N, ld, part);
+    colsum_part_kernel<<<dim3(ceil_div(N, 128), unsigned(np)), 128, 0, s>>>(X, bf16, M, N, ld, rows, part);
   }
   PGF_LAUNCH_CHECK();
   return column_reduce(part, np, N, out, accumulate, s);
