@@ -40,6 +40,8 @@ SIGNATURES = {
     "pgf_profile_read": (c_int, [c_int, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_double),
                                  ctypes.POINTER(ctypes.c_double)]),
     "pgf_rmsnorm_fwd": (c_int, [P, P, P, I64, I64, c_float, c_int, P]),
+    "pgf_rmsnorm_fwd_res": (c_int, [P, P, P, P, P, I64, I64, c_float, c_int, P]),
+    "pgf_rmsnorm_bwd_add": (c_int, [P, P, P, P, P, P, c_int, I64, I64, c_float, c_int, P, c_size_t, P]),
     "pgf_rmsnorm_bwd_workspace": (c_size_t, [I64, I64]),
     "pgf_rmsnorm_bwd": (c_int, [P, P, P, P, P, c_int, I64, I64, c_float, c_int, P, c_size_t, P]),
     "pgf_rmsnorm_bwd_noalloc": (c_int, [P, P, P, P, P, c_int, I64, I64, c_float, c_int, P]),

@@ -1,7 +1,10 @@
 // RMSNorm forward / backward (pgf_rmsnorm.py:10-51).
 //
 // One warp per row; the row lives in registers (VPL values per lane, columns lane + 32*j), so x
-// and g are read once.  grad_weight is reduced deterministically: each CTA sums its warps'
+// and g are read once.  The forward can take a residual (sum = x + res, written out in the
+// activation type and normalised: the block's `y + x` then norm2 in one pass); the backward can
+// add a gradient to grad_x (the block's `norm.grad_x + g` skip connections).  Both round where the
+// separate add would, so the fused forms give the same bits.  grad_weight is reduced deterministically: each CTA sums its warps'
 // register partials through shared memory in warp order and writes one partial row; a second
 // kernel adds the CTA partials in CTA order.
 #include "gemm.cuh"
@@ -13,8 +16,8 @@ constexpr int RMS_ROWS_PER_WARP = 4;  // rows handled by a warp in the backward 
 
 template <int VPL, class T>
 __global__ void __launch_bounds__(RMS_WARPS * 32)
-rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, T* __restrict__ y,
-                   int64_t rows, int dim, float eps) {
+rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ res, T* __restrict__ sum_out,
+                   const float* __restrict__ w, T* __restrict__ y, int64_t rows, int dim, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * RMS_WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -25,6 +28,11 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, T* __re
   for (int j = 0; j < VPL; ++j) {
     int c = j * 32 + lane;
     v[j] = c < dim ? ld(xr, c) : 0.f;
+    if (res && c < dim) {
+      // the sum rounded to T, as the separate add stores it, then normalised
+      v[j] = rounded<T>(v[j] + ld(res + row * dim, c));
+      st(sum_out + row * dim, c, v[j]);
+    }
     ss = fmaf(v[j], v[j], ss);
   }
   ss = warp_sum(ss);
@@ -40,7 +48,7 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, T* __re
 template <int VPL, class T>
 __global__ void __launch_bounds__(RMS_WARPS * 32)
 rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g, const float* __restrict__ w,
-                   T* __restrict__ gx, float* __restrict__ gw_part, int64_t rows, int dim,
+                   const T* __restrict__ gadd, T* __restrict__ gx, float* __restrict__ gw_part, int64_t rows, int dim,
                    float eps) {
   extern __shared__ float sm_gw[];  // [RMS_WARPS][dim]
   const int lane = threadIdx.x & 31;
@@ -60,13 +68,14 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g, const float
     if (row >= rows) break;
     const T* xr = x + row * dim;
     const T* gr = g + row * dim;
-    float xv[VPL], gv[VPL];
+    float xv[VPL], gv[VPL], av[VPL];
     float ss = 0.f, dot = 0.f;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       int c = j * 32 + lane;
       xv[j] = c < dim ? ld(xr, c) : 0.f;
       gv[j] = c < dim ? ld(gr, c) : 0.f;
+      av[j] = (gadd && c < dim) ? ld(gadd + row * dim, c) : 0.f;  // loaded with x and g
       ss = fmaf(xv[j], xv[j], ss);
       dot = fmaf(gv[j] * wv[j], xv[j], dot);
     }
@@ -80,7 +89,11 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g, const float
 #pragma unroll
       for (int j = 0; j < VPL; ++j) {
         int c = j * 32 + lane;
-        if (c < dim) st(gxr, c, (gv[j] * wv[j]) * rinv - (xv[j] * dot) * r3 / float(dim));
+        if (c < dim) {
+          const float v = (gv[j] * wv[j]) * rinv - (xv[j] * dot) * r3 / float(dim);
+          // with an addend: grad_x rounded to T as a separate operator would return it, then added
+          st(gxr, c, gadd ? rounded<T>(v) + av[j] : v);
+        }
       }
     }
 #pragma unroll
@@ -99,16 +112,216 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g, const float
   }
 }
 
+// ---- vector forms: a lane owns CPL 16-byte chunks of a row (chunk k = columns (32k + lane) VW ..
+// + VW, VW = 16 / sizeof(T)), so a row is CPL coalesced 512-byte loads per tensor; a warp takes
+// RPW rows and issues every load of them before any arithmetic.  Used when dim is a multiple of
+// 32 VW and every row starts on a 16-byte boundary.
+template <class T> struct Vec16;
+template <> struct Vec16<float> {
+  static constexpr int VW = 4;
+  __device__ static void unpack(const uint4 q, float* o) {
+    o[0] = __uint_as_float(q.x); o[1] = __uint_as_float(q.y); o[2] = __uint_as_float(q.z); o[3] = __uint_as_float(q.w);
+  }
+  __device__ static uint4 pack(const float* v) {
+    return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+  }
+};
+template <> struct Vec16<__nv_bfloat16> {
+  static constexpr int VW = 8;
+  __device__ static void unpack(const uint4 q, float* o) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      o[2 * k] = __uint_as_float(w[k] << 16);
+      o[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+    }
+  }
+  __device__ static uint32_t pk(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  __device__ static uint4 pack(const float* v) {
+    return make_uint4(pk(v[0], v[1]), pk(v[2], v[3]), pk(v[4], v[5]), pk(v[6], v[7]));
+  }
+};
+
+template <int CPL, int RPW, class T>
+__global__ void __launch_bounds__(RMS_WARPS * 32)
+rmsnorm_fwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ res, T* __restrict__ sum_out,
+                       const float* __restrict__ w, T* __restrict__ y, int64_t rows, int dim, float eps) {
+  using V = Vec16<T>;
+  constexpr int VW = V::VW;
+  const int lane = threadIdx.x & 31;
+  const int64_t row0 = (int64_t(blockIdx.x) * RMS_WARPS + (threadIdx.x >> 5)) * RPW;
+  if (row0 >= rows) return;
+  uint4 qx[RPW][CPL], qr[RPW][CPL];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      const int64_t off = (row0 + r) * dim + int64_t(k * 32 + lane) * VW;
+      const bool ok = row0 + r < rows;
+      qx[r][k] = ok ? __ldg(reinterpret_cast<const uint4*>(x + off)) : make_uint4(0, 0, 0, 0);
+      qr[r][k] = (ok && res) ? __ldg(reinterpret_cast<const uint4*>(res + off)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int64_t row = row0 + r;
+    if (row >= rows) break;
+    float v[CPL][VW];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      V::unpack(qx[r][k], v[k]);
+      if (res) {
+        float a[VW];
+        V::unpack(qr[r][k], a);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) v[k][e] = rounded<T>(v[k][e] + a[e]);
+        *reinterpret_cast<uint4*>(sum_out + row * dim + int64_t(k * 32 + lane) * VW) = V::pack(v[k]);
+      }
+#pragma unroll
+      for (int e = 0; e < VW; ++e) ss = fmaf(v[k][e], v[k][e], ss);
+    }
+    ss = warp_sum(ss);
+    const float rinv = 1.0f / sqrtf(ss / float(dim) + eps);  // one divide per row
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      const int c0 = (k * 32 + lane) * VW;
+      float o[VW];
+#pragma unroll
+      for (int e = 0; e < VW; ++e) o[e] = (v[k][e] * rinv) * __ldg(w + c0 + e);
+      *reinterpret_cast<uint4*>(y + row * dim + c0) = V::pack(o);
+    }
+  }
+}
+
+template <int CPL, class T>
+__global__ void __launch_bounds__(RMS_WARPS * 32)
+rmsnorm_bwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ g, const float* __restrict__ w,
+                       const T* __restrict__ gadd, T* __restrict__ gx, float* __restrict__ gw_part, int64_t rows,
+                       int dim, float eps) {
+  using V = Vec16<T>;
+  constexpr int VW = V::VW;
+  extern __shared__ float sm_gw[];  // [RMS_WARPS][dim]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  // rows whose loads are issued together: four 16-byte chunks of each tensor per lane in flight
+  constexpr int RB = CPL >= 4 ? 1 : 4 / CPL;
+  float acc[CPL][VW];
+#pragma unroll
+  for (int k = 0; k < CPL; ++k)
+#pragma unroll
+    for (int e = 0; e < VW; ++e) acc[k][e] = 0.f;
+  const int64_t row0 = (int64_t(blockIdx.x) * RMS_WARPS + warp) * RMS_ROWS_PER_WARP;
+#pragma unroll 1
+  for (int rb = 0; rb < RMS_ROWS_PER_WARP; rb += RB) {
+  uint4 qx[RB][CPL], qg[RB][CPL], qa[RB][CPL];
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      const int64_t off = (row0 + rb + r) * dim + int64_t(k * 32 + lane) * VW;
+      const bool ok = row0 + rb + r < rows;
+      qx[r][k] = ok ? __ldg(reinterpret_cast<const uint4*>(x + off)) : make_uint4(0, 0, 0, 0);
+      qg[r][k] = ok ? __ldg(reinterpret_cast<const uint4*>(g + off)) : make_uint4(0, 0, 0, 0);
+      qa[r][k] = (ok && gadd) ? __ldg(reinterpret_cast<const uint4*>(gadd + off)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    const int64_t row = row0 + rb + r;
+    if (row >= rows) break;
+    float wv[CPL][VW];  // the weight, from L1 (it is the same for every row)
+#pragma unroll
+    for (int k = 0; k < CPL; ++k)
+#pragma unroll
+      for (int e = 0; e < VW; ++e) wv[k][e] = __ldg(w + (k * 32 + lane) * VW + e);
+    float xv[CPL][VW], gv[CPL][VW];
+    float ss = 0.f, dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      V::unpack(qx[r][k], xv[k]);
+      V::unpack(qg[r][k], gv[k]);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        ss = fmaf(xv[k][e], xv[k][e], ss);
+        dot = fmaf(gv[k][e] * wv[k][e], xv[k][e], dot);
+      }
+    }
+    ss = warp_sum(ss);
+    dot = warp_sum(dot);
+    const float rinv = 1.0f / sqrtf(ss / float(dim) + eps);
+    const float kx = dot * (rinv * rinv * rinv) / float(dim);  // per row: no divide per element
+    if (gx) {
+#pragma unroll
+      for (int k = 0; k < CPL; ++k) {
+        float o[VW], a[VW];
+        V::unpack(qa[r][k], a);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) {
+          const float v = fmaf(gv[k][e] * wv[k][e], rinv, -xv[k][e] * kx);
+          o[e] = gadd ? rounded<T>(v) + a[e] : v;
+        }
+        *reinterpret_cast<uint4*>(gx + row * dim + int64_t(k * 32 + lane) * VW) = V::pack(o);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < CPL; ++k)
+#pragma unroll
+      for (int e = 0; e < VW; ++e) acc[k][e] = fmaf(gv[k][e], xv[k][e] * rinv, acc[k][e]);
+  }
+  }  // row groups
+#pragma unroll
+  for (int k = 0; k < CPL; ++k)
+#pragma unroll
+    for (int e = 0; e < VW; ++e) sm_gw[warp * dim + (k * 32 + lane) * VW + e] = acc[k][e];
+  __syncthreads();
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+    float s = 0.f;
+    for (int q = 0; q < RMS_WARPS; ++q) s += sm_gw[q * dim + c];
+    gw_part[int64_t(blockIdx.x) * dim + c] = s;
+  }
+}
+
+// chunks per lane of the vector forms (0: use the scalar kernels)
 template <class T>
-static int rms_fwd_dispatch(const T* x, const float* w, T* y, int64_t rows, int dim, float eps,
-                            cudaStream_t s) {
+static int rms_vec_cpl(const void* a, const void* b, const void* c, const void* d, int64_t dim) {
+  constexpr int VW = 16 / int(sizeof(T));
+  if (dim % (32 * VW)) return 0;
+  const int cpl = int(dim / (32 * VW));
+  if (cpl != 1 && cpl != 2 && cpl != 4) return 0;
+  for (const void* p : {a, b, c, d})
+    if (p && !aligned(p, 16)) return 0;
+  return cpl;
+}
+
+template <class T>
+static int rms_fwd_dispatch(const T* x, const T* res, T* sum_out, const float* w, T* y, int64_t rows, int dim,
+                            float eps, cudaStream_t s) {
+  const int cpl = rms_vec_cpl<T>(x, res, sum_out, y, dim);
+  if (cpl) {
+    const double work = double(rows) * dim * (res ? 4.0 : 2.0) * sizeof(T) + dim * 4.0;
+#define PGF_RMS_FV(C, R)                                                                                   \
+  do {                                                                                                     \
+    prof_begin(PROF_RMSNORM_FWD, s);                                                                       \
+    rmsnorm_fwd_vec_kernel<C, R, T><<<unsigned(ceil_div(rows, RMS_WARPS * R)), RMS_WARPS * 32, 0, s>>>(     \
+        x, res, sum_out, w, y, rows, dim, eps);                                                            \
+    prof_end(PROF_RMSNORM_FWD, s, work);                                                                   \
+  } while (0)
+    if (cpl == 1) PGF_RMS_FV(1, 4);
+    else if (cpl == 2) PGF_RMS_FV(2, 2);
+    else PGF_RMS_FV(4, 1);
+#undef PGF_RMS_FV
+    PGF_LAUNCH_CHECK();
+    return PGF_OK;
+  }
   dim3 grid(ceil_div(rows, RMS_WARPS)), block(RMS_WARPS * 32);
   int vpl = ceil_div(dim, 32);
 #define PGF_RMS_F(V)                                                                  \
   do {                                                                                \
     prof_begin(PROF_RMSNORM_FWD, s);                                                  \
-    rmsnorm_fwd_kernel<V, T><<<grid, block, 0, s>>>(x, w, y, rows, dim, eps);         \
-    prof_end(PROF_RMSNORM_FWD, s, double(rows) * dim * 2.0 * sizeof(T) + dim * 4.0);    \
+    rmsnorm_fwd_kernel<V, T><<<grid, block, 0, s>>>(x, res, sum_out, w, y, rows, dim, eps); \
+    prof_end(PROF_RMSNORM_FWD, s, double(rows) * dim * (res ? 4.0 : 2.0) * sizeof(T) + dim * 4.0); \
   } while (0)
   if (vpl <= 1) PGF_RMS_F(1);
   else if (vpl <= 2) PGF_RMS_F(2);
@@ -127,19 +340,38 @@ static int rms_fwd_dispatch(const T* x, const float* w, T* y, int64_t rows, int 
 static int64_t rms_bwd_ctas(int64_t rows) { return ceil_div(rows, RMS_WARPS * RMS_ROWS_PER_WARP); }
 
 template <class T>
-static int rms_bwd_dispatch(const T* x, const T* g, const float* w, T* gx, float* gw, int acc,
+static int rms_bwd_dispatch(const T* x, const T* g, const float* w, const T* gadd, T* gx, float* gw, int acc,
                             int64_t rows, int dim, float eps, float* part, cudaStream_t s) {
   int64_t nct = rms_bwd_ctas(rows);
   dim3 grid((unsigned)nct), block(RMS_WARPS * 32);
   size_t smem = size_t(RMS_WARPS) * dim * sizeof(float);
+  const int cpl = rms_vec_cpl<T>(x, g, gadd, gx, dim);
+  if (cpl) {
+    const double work = double(rows) * dim * (gadd ? 4.0 : 3.0) * sizeof(T) + dim * 4.0;
+#define PGF_RMS_BV(C)                                                                                 \
+  do {                                                                                                \
+    static int smem_limit_v##C = 0;                                                                   \
+    PGF_CUDA(ensure_dynamic_smem(rmsnorm_bwd_vec_kernel<C, T>, smem, smem_limit_v##C));               \
+    prof_begin(PROF_RMSNORM_BWD, s);                                                                  \
+    rmsnorm_bwd_vec_kernel<C, T><<<grid, block, smem, s>>>(x, g, w, gadd, gx, part, rows, dim, eps);  \
+    prof_end(PROF_RMSNORM_BWD, s, work);                                                              \
+  } while (0)
+    if (cpl == 1) PGF_RMS_BV(1);
+    else if (cpl == 2) PGF_RMS_BV(2);
+    else PGF_RMS_BV(4);
+#undef PGF_RMS_BV
+    PGF_LAUNCH_CHECK();
+    PGF_TRY(column_reduce(part, nct, dim, gw, acc, s));
+    return PGF_OK;
+  }
   int vpl = ceil_div(dim, 32);
 #define PGF_RMS_B(V)                                                                           \
   do {                                                                                         \
     static int smem_limit_##V = 0;                                                             \
     PGF_CUDA(ensure_dynamic_smem(rmsnorm_bwd_kernel<V, T>, smem, smem_limit_##V));             \
     prof_begin(PROF_RMSNORM_BWD, s);                                                           \
-    rmsnorm_bwd_kernel<V, T><<<grid, block, smem, s>>>(x, g, w, gx, part, rows, dim, eps);     \
-    prof_end(PROF_RMSNORM_BWD, s, double(rows) * dim * 3.0 * sizeof(T) + dim * 4.0);           \
+    rmsnorm_bwd_kernel<V, T><<<grid, block, smem, s>>>(x, g, w, gadd, gx, part, rows, dim, eps); \
+    prof_end(PROF_RMSNORM_BWD, s, double(rows) * dim * (gadd ? 4.0 : 3.0) * sizeof(T) + dim * 4.0); \
   } while (0)
   if (vpl <= 1) PGF_RMS_B(1);
   else if (vpl <= 2) PGF_RMS_B(2);
@@ -168,11 +400,30 @@ extern "C" int pgf_rmsnorm_fwd(const void* x, const float* weight, void* y, int6
   PGF_CHECK_ARG(x && weight && y, "rmsnorm_fwd: null pointer");
   cudaStream_t s = as_stream(stream);
   if (dtype == PGF_DTYPE_F32)
-    return rms_fwd_dispatch((const float*)x, weight, (float*)y, rows, int(dim), eps, s);
+    return rms_fwd_dispatch((const float*)x, (const float*)nullptr, (float*)nullptr, weight, (float*)y, rows,
+                            int(dim), eps, s);
   if (dtype == PGF_DTYPE_BF16)
-    return rms_fwd_dispatch((const __nv_bfloat16*)x, weight, (__nv_bfloat16*)y, rows, int(dim),
-                            eps, s);
+    return rms_fwd_dispatch((const __nv_bfloat16*)x, (const __nv_bfloat16*)nullptr, (__nv_bfloat16*)nullptr,
+                            weight, (__nv_bfloat16*)y, rows, int(dim), eps, s);
   set_error("rmsnorm_fwd: bad dtype %d", dtype);
+  return PGF_ERR_INVALID;
+}
+
+extern "C" int pgf_rmsnorm_fwd_res(const void* x, const void* res, const float* weight, void* sum_out, void* y,
+                                   int64_t rows, int64_t dim, float eps, int dtype, pgf_stream_t stream) {
+  PGF_CHECK_ARG(rows >= 0 && dim > 0 && dim <= 4096, "rmsnorm_fwd_res: bad shape rows=%lld dim=%lld",
+                (long long)rows, (long long)dim);
+  if (rows == 0) return PGF_OK;
+  PGF_CHECK_ARG(x && res && weight && sum_out && y, "rmsnorm_fwd_res: null pointer");
+  PGF_CHECK_ARG(sum_out != x && sum_out != res, "rmsnorm_fwd_res: sum_out must not alias the inputs");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == PGF_DTYPE_F32)
+    return rms_fwd_dispatch((const float*)x, (const float*)res, (float*)sum_out, weight, (float*)y, rows, int(dim),
+                            eps, s);
+  if (dtype == PGF_DTYPE_BF16)
+    return rms_fwd_dispatch((const __nv_bfloat16*)x, (const __nv_bfloat16*)res, (__nv_bfloat16*)sum_out, weight,
+                            (__nv_bfloat16*)y, rows, int(dim), eps, s);
+  set_error("rmsnorm_fwd_res: bad dtype %d", dtype);
   return PGF_ERR_INVALID;
 }
 
@@ -180,11 +431,11 @@ extern "C" size_t pgf_rmsnorm_bwd_workspace(int64_t rows, int64_t dim) {
   return Workspace::round(size_t(rms_bwd_ctas(rows < 1 ? 1 : rows)) * size_t(dim) * sizeof(float));
 }
 
-extern "C" int pgf_rmsnorm_bwd(const void* x, const void* g, const float* weight, void* grad_x,
-                               float* grad_weight, int accumulate, int64_t rows, int64_t dim,
-                               float eps, int dtype, void* ws, size_t ws_bytes,
-                               pgf_stream_t stream) {
+static int rmsnorm_bwd_impl(const void* x, const void* g, const float* weight, const void* g_add, void* grad_x,
+                            float* grad_weight, int accumulate, int64_t rows, int64_t dim, float eps, int dtype,
+                            void* ws, size_t ws_bytes, pgf_stream_t stream) {
   PGF_CHECK_ARG(weight && grad_weight, "rmsnorm_bwd: null pointer");
+  PGF_CHECK_ARG(!g_add || grad_x, "rmsnorm_bwd: an addend needs grad_x");
   PGF_CHECK_ARG(rows >= 0 && dim > 0 && dim <= 4096, "rmsnorm_bwd: bad shape");
   cudaStream_t s = as_stream(stream);
   if (rows > 0) PGF_CHECK_ARG(x && g, "rmsnorm_bwd: null pointer");
@@ -196,14 +447,29 @@ extern "C" int pgf_rmsnorm_bwd(const void* x, const void* g, const float* weight
   float* part = W.take<float>(size_t(rms_bwd_ctas(rows)) * dim);
   if (!part) { set_error("rmsnorm_bwd: workspace too small (%zu)", ws_bytes); return PGF_ERR_WORKSPACE; }
   if (dtype == PGF_DTYPE_F32)
-    return rms_bwd_dispatch((const float*)x, (const float*)g, weight, (float*)grad_x, grad_weight,
-                            accumulate, rows, int(dim), eps, part, s);
+    return rms_bwd_dispatch((const float*)x, (const float*)g, weight, (const float*)g_add, (float*)grad_x,
+                            grad_weight, accumulate, rows, int(dim), eps, part, s);
   if (dtype == PGF_DTYPE_BF16)
     return rms_bwd_dispatch((const __nv_bfloat16*)x, (const __nv_bfloat16*)g, weight,
-                            (__nv_bfloat16*)grad_x, grad_weight, accumulate, rows, int(dim), eps,
-                            part, s);
+                            (const __nv_bfloat16*)g_add, (__nv_bfloat16*)grad_x, grad_weight, accumulate, rows,
+                            int(dim), eps, part, s);
   set_error("rmsnorm_bwd: bad dtype %d", dtype);
   return PGF_ERR_INVALID;
+}
+
+extern "C" int pgf_rmsnorm_bwd(const void* x, const void* g, const float* weight, void* grad_x, float* grad_weight,
+                               int accumulate, int64_t rows, int64_t dim, float eps, int dtype, void* ws,
+                               size_t ws_bytes, pgf_stream_t stream) {
+  return rmsnorm_bwd_impl(x, g, weight, nullptr, grad_x, grad_weight, accumulate, rows, dim, eps, dtype, ws,
+                          ws_bytes, stream);
+}
+
+extern "C" int pgf_rmsnorm_bwd_add(const void* x, const void* g, const float* weight, const void* g_add,
+                                   void* grad_x, float* grad_weight, int accumulate, int64_t rows, int64_t dim,
+                                   float eps, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(g_add && grad_x, "rmsnorm_bwd_add: null pointer");
+  return rmsnorm_bwd_impl(x, g, weight, g_add, grad_x, grad_weight, accumulate, rows, dim, eps, dtype, ws,
+                          ws_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -273,12 +539,12 @@ extern "C" int pgf_rmsnorm_bwd_noalloc(const void* x, const void* g, const float
   float* part = nullptr;
   PGF_TRY(noalloc_scratch(&part));
   if (dtype == PGF_DTYPE_F32)
-    return rms_bwd_dispatch((const float*)x, (const float*)g, weight, (float*)grad_x, grad_weight,
-                            accumulate, rows, int(dim), eps, part, s);
+    return rms_bwd_dispatch((const float*)x, (const float*)g, weight, (const float*)nullptr, (float*)grad_x,
+                            grad_weight, accumulate, rows, int(dim), eps, part, s);
   if (dtype == PGF_DTYPE_BF16)
     return rms_bwd_dispatch((const __nv_bfloat16*)x, (const __nv_bfloat16*)g, weight,
-                            (__nv_bfloat16*)grad_x, grad_weight, accumulate, rows, int(dim), eps,
-                            part, s);
+                            (const __nv_bfloat16*)nullptr, (__nv_bfloat16*)grad_x, grad_weight, accumulate, rows,
+                            int(dim), eps, part, s);
   set_error("rmsnorm_bwd_noalloc: bad dtype %d", dtype);
   return PGF_ERR_INVALID;
 }

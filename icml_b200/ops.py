@@ -64,20 +64,41 @@ def rmsnorm_fwd(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return y
 
 
+def rmsnorm_fwd_res(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float):
+    """(x + res, RMSNorm(x + res) * w) in one pass; bitwise the separate add and norm."""
+    _cuda(x, res, w)
+    x, res = _c(x), _c(res.to(x.dtype))
+    w = _f32(w)
+    dim = x.shape[-1]
+    rows = x.numel() // dim
+    sm = torch.empty_like(x)
+    y = torch.empty_like(x)
+    check(lib().pgf_rmsnorm_fwd_res(_p(x), _p(res), _p(w), _p(sm), _p(y), rows, dim, eps, _dt(x), _stream()),
+          "rmsnorm_fwd_res")
+    return sm, y
+
+
 def rmsnorm_bwd(x: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float,
-                need_gx: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+                need_gx: bool = True, g_add: Optional[torch.Tensor] = None
+                ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """(grad weight, grad x); with g_add, grad x + g_add (fused, bitwise the separate add)."""
     _cuda(x, g, w)
     x, g = _c(x), _c(g.to(x.dtype))
     w = _f32(w)
     dim = x.shape[-1]
     rows = x.numel() // dim
     gw = torch.empty(dim, dtype=torch.float32, device=x.device)
-    gx = torch.empty_like(x) if need_gx else None
+    gx = torch.empty_like(x) if (need_gx or g_add is not None) else None
     L = lib()
     nb = L.pgf_rmsnorm_bwd_workspace(rows, dim)
     ws = _ws(nb, x.device)
-    check(L.pgf_rmsnorm_bwd(_p(x), _p(g), _p(w), _p(gx), _p(gw), 0, rows, dim, eps, _dt(x),
-                            _p(ws), ws.numel(), _stream()), "rmsnorm_bwd")
+    if g_add is not None:
+        ga = _c(g_add.to(x.dtype))
+        check(L.pgf_rmsnorm_bwd_add(_p(x), _p(g), _p(w), _p(ga), _p(gx), _p(gw), 0, rows, dim, eps, _dt(x),
+                                    _p(ws), ws.numel(), _stream()), "rmsnorm_bwd_add")
+    else:
+        check(L.pgf_rmsnorm_bwd(_p(x), _p(g), _p(w), _p(gx), _p(gw), 0, rows, dim, eps, _dt(x),
+                                _p(ws), ws.numel(), _stream()), "rmsnorm_bwd")
     return gw, gx
 
 

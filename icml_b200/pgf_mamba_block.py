@@ -69,8 +69,8 @@ class PGFMambaBlock(nn.Module):
         B, L, D = x.shape
         xn = self.norm1.pgf_forward(x, block_size=self.block_size)
         y, _ = self.mamba.ssm_forward(xn)
-        x1 = y + x
-        xn2 = self.norm2.pgf_forward(x1, block_size=self.block_size)
+        # x1 = y + x and norm2(x1) in one pass (same bits as the separate add and norm)
+        x1, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)
         f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                             block_size=self.block_size, activation=self.ffn_activation)
         return f.reshape(B, L, D) + x1
@@ -85,17 +85,18 @@ class PGFMambaBlock(nn.Module):
         m = self.mamba
         # :163-178; the states it passes through are kept for the scan backward below
         y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
-        m_out = y + x
-        xn2 = self.norm2.pgf_forward(m_out, block_size=self.block_size)          # :179
+        m_out, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)  # y + x, :179
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                           block_size=self.block_size, activation=self.ffn_activation,
                           compute_input_grads=True)                              # :183-192
-        n2 = self.norm2.pgf_grad(m_out, fr["grad_x"].reshape(B, L, D), compute_input_grads=True)  # :196
-        g_m = n2["grad_x"] + g_out                                               # :202
+        # :196 and :202 (norm2's grad_x + g_out) in one pass
+        gw2, g_m = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), self.norm2.weight, self.norm2.eps,
+                                   g_add=g_out)
         r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, act=m.output_activation,
                         saved=saved)                                             # :206-234
         del saved
-        n1 = self.norm1.pgf_grad(x, r["grad_u"], compute_input_grads=True)       # :237-242
+        # :237-242 and :246-249 (norm1's grad_x + g_m) in one pass
+        gw1, grad_input = ops.rmsnorm_bwd(x, r["grad_u"], self.norm1.weight, self.norm1.eps, g_add=g_m)
         d, N = self.d_model, self.d_state
         gscale = r["scale"].sum().expand(d).clone() if m.reference_scale_grad else r["scale"]
         grads = {
@@ -104,9 +105,9 @@ class PGFMambaBlock(nn.Module):
             "mamba.dt_proj.weight": r["W_cat"][:d], "mamba.dt_proj.bias": r["b_cat"][:d],
             "mamba.B_proj.weight": r["W_cat"][d:d + N], "mamba.B_proj.bias": r["b_cat"][d:d + N],
             "mamba.C_proj.weight": r["W_cat"][d + N:], "mamba.C_proj.bias": r["b_cat"][d + N:],
-            "norm1.weight": n1["grad_weight"], "norm2.weight": n2["grad_weight"],
+            "norm1.weight": gw1, "norm2.weight": gw2,
         }
-        return {"grads": grads, "grad_input": n1["grad_x"] + g_m}               # :246-249
+        return {"grads": grads, "grad_input": grad_input}
 
     @torch.no_grad()
     def pgf_forward_mamba_only(self, x_norm: torch.Tensor) -> torch.Tensor:

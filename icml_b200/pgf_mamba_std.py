@@ -106,8 +106,10 @@ class PGFMambaStdBlock(nn.Module):
     @torch.no_grad()
     def pgf_forward(self, x: torch.Tensor) -> torch.Tensor:
         B, L, D = x.shape
-        x1 = ops.mamba_mixer_fwd(self.norm1.pgf_forward(x), self.mixer.params()) + x
-        f = pgf_ffn_forward(self.norm2.pgf_forward(x1).reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
+        # x1 = mixer + x and norm2(x1) in one pass (same bits as the separate add and norm)
+        x1, xn2 = ops.rmsnorm_fwd_res(ops.mamba_mixer_fwd(self.norm1.pgf_forward(x), self.mixer.params()), x,
+                                      self.norm2.weight, self.norm2.eps)
+        f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                             activation=self.ffn_activation)
         return f.reshape(B, L, D) + x1
 
@@ -118,20 +120,19 @@ class PGFMambaStdBlock(nn.Module):
         p = self.mixer.params()
         xn1 = self.norm1.pgf_forward(x)
         m_raw, saved = ops.mamba_mixer_fwd_save(xn1, p)
-        m_out = m_raw + x
+        m_out, xn2 = ops.rmsnorm_fwd_res(m_raw, x, self.norm2.weight, self.norm2.eps)
         del m_raw
-        xn2 = self.norm2.pgf_forward(m_out)
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                           activation=self.ffn_activation, compute_input_grads=True)
-        n2 = self.norm2.pgf_grad(m_out, fr["grad_x"].reshape(B, L, D), compute_input_grads=True)
-        g_m = n2["grad_x"] + g_out
+        gw2, g_m = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), self.norm2.weight, self.norm2.eps,
+                                   g_add=g_out)  # norm2's grad_x + g_out in one pass
         mg, gxn1 = ops.mamba_mixer_bwd(xn1, g_m, p, saved=saved)
         del saved
-        n1 = self.norm1.pgf_grad(x, gxn1, compute_input_grads=True)
+        gw1, grad_input = ops.rmsnorm_bwd(x, gxn1, self.norm1.weight, self.norm1.eps, g_add=g_m)
         grads = {"W1": fr["grad_W1"], "b1": fr["grad_b1"], "W2": fr["grad_W2"], "b2": fr["grad_b2"],
-                 "norm1.weight": n1["grad_weight"], "norm2.weight": n2["grad_weight"]}
+                 "norm1.weight": gw1, "norm2.weight": gw2}
         grads.update(self.mixer.grads_to_named(mg, "mixer."))
-        return {"grads": grads, "grad_input": n1["grad_x"] + g_m}
+        return {"grads": grads, "grad_input": grad_input}
 
 
 __all__ = ["MambaMixer", "PGFMambaStdBlock"]

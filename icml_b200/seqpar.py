@@ -99,8 +99,7 @@ def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
     else:
         h_in = None
         y, _ = ops.ssm_fwd(xn, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
-    x1 = y + x
-    xn2 = ops.rmsnorm_fwd(x1, block.norm2.weight, block.norm2.eps)
+    x1, xn2 = ops.rmsnorm_fwd_res(y, x, block.norm2.weight, block.norm2.eps)  # y + x, then norm2
     f = ops.ffn_fwd(xn2.reshape(-1, D), block.W1, block.b1, block.W2, block.b2, block.ffn_activation)
     return f.reshape(B, L, D) + x1, h_in
 
@@ -116,12 +115,11 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
     g_out = g_out.to(x.dtype)
     xn1 = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
     y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
-    m_out = y + x
-    xn2 = ops.rmsnorm_fwd(m_out, block.norm2.weight, block.norm2.eps)
+    m_out, xn2 = ops.rmsnorm_fwd_res(y, x, block.norm2.weight, block.norm2.eps)
     fr = ops.ffn_bwd(xn2.reshape(-1, D), g_out.reshape(-1, D), block.W1, block.b1, block.W2,
                      block.ffn_activation, need_gx=True)
-    gn2w, gn2x = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), block.norm2.weight, block.norm2.eps)
-    g_m = gn2x + g_out
+    gn2w, g_m = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), block.norm2.weight, block.norm2.eps,
+                                g_add=g_out)  # norm2's grad_x + g_out
     if sp.world > 1:
         # the reverse chunk pass gives the segment's adjoint summary; the gradients continue from it
         d_loc, dA0, sdx, st = ops.ssm_bwd_begin(xn1, g_m, W, b, m.A_log, m.scale, saved, h_init=h_in,
@@ -133,7 +131,7 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
     else:
         r = ops.ssm_bwd(xn1, g_m, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation, saved=saved)
     del saved
-    gn1w, gn1x = ops.rmsnorm_bwd(x, r["grad_u"], block.norm1.weight, block.norm1.eps)
+    gn1w, grad_input = ops.rmsnorm_bwd(x, r["grad_u"], block.norm1.weight, block.norm1.eps, g_add=g_m)
     d, N = m.d_model, m.d_state
     gscale = r["scale"].sum().expand(d).clone() if m.reference_scale_grad else r["scale"]
     grads = {
@@ -144,7 +142,7 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
         "mamba.C_proj.weight": r["W_cat"][d + N:], "mamba.C_proj.bias": r["b_cat"][d + N:],
         "norm1.weight": gn1w, "norm2.weight": gn2w,
     }
-    return {"grads": grads, "grad_input": gn1x + g_m}
+    return {"grads": grads, "grad_input": grad_input}
 
 
 @torch.no_grad()

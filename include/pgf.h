@@ -86,10 +86,21 @@ int pgf_profile_read(int id, long long* count, double* total_ms, double* total_w
  * ------------------------------------------------------------------------------------------ */
 int pgf_rmsnorm_fwd(const void* x, const float* weight, void* y, int64_t rows, int64_t dim,
                     float eps, int dtype, pgf_stream_t stream);
+/* The block's residual sum and its norm in one pass (pgf_mamba_block.py:109-112, `y + x` then
+ * norm2): sum_out = x + res (stored in dtype), y = RMSNorm(sum_out) * weight.  Same bits as the
+ * separate add followed by pgf_rmsnorm_fwd.  sum_out must not alias x or res. */
+int pgf_rmsnorm_fwd_res(const void* x, const void* res, const float* weight, void* sum_out, void* y,
+                        int64_t rows, int64_t dim, float eps, int dtype, pgf_stream_t stream);
 size_t pgf_rmsnorm_bwd_workspace(int64_t rows, int64_t dim);
 int pgf_rmsnorm_bwd(const void* x, const void* g, const float* weight, void* grad_x /* nullable */,
                     float* grad_weight, int accumulate, int64_t rows, int64_t dim, float eps,
                     int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+/* pgf_rmsnorm_bwd with the skip connection's gradient added to grad_x (pgf_mamba_block.py:202,
+ * :246-249, `norm.grad_x + g`): grad_x = RMSNorm'(x)^T g + g_add, with the first term rounded to
+ * dtype first, so the bits match the separate add. */
+int pgf_rmsnorm_bwd_add(const void* x, const void* g, const float* weight, const void* g_add, void* grad_x,
+                        float* grad_weight, int accumulate, int64_t rows, int64_t dim, float eps, int dtype,
+                        void* ws, size_t ws_bytes, pgf_stream_t stream);
 /* Same results as pgf_rmsnorm_bwd, for callers that cannot allocate device memory (an engine that
  * owns all device memory and forbids allocation from its operators, or a loop that must not enter
  * the allocator).  No counterpart in the reference, which has no native layer.  Scratch is a 4 MiB

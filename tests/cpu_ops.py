@@ -28,8 +28,15 @@ def rmsnorm_fwd(x, w, eps):
     return O.rmsnorm_forward(x, w.detach(), eps)
 
 
-def rmsnorm_bwd(x, g, w, eps, need_gx=True):
+def rmsnorm_fwd_res(x, res, w, eps):
+    s = x + res
+    return s, O.rmsnorm_forward(s, w.detach(), eps)
+
+
+def rmsnorm_bwd(x, g, w, eps, need_gx=True, g_add=None):
     gw, gx = O.rmsnorm_grad(x, g, w.detach(), eps)
+    if g_add is not None:
+        return gw, gx + g_add
     return gw, (gx if need_gx else None)
 
 

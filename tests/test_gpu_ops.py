@@ -23,7 +23,10 @@ def _gen(seed):
 
 
 # ----------------------------------------------------------------------------- RMSNorm
-@pytest.mark.parametrize("shape", [(3, 40, 48), (7, 1024), (5, 100), (1, 1, 4096), (0, 64)])
+# (33, 256), (9, 512), (70, 128): the 16-byte vector kernels (2, 4, 1 chunks per lane; row counts that
+# leave a warp's row group partly empty); the others the scalar kernels
+@pytest.mark.parametrize("shape", [(3, 40, 48), (7, 1024), (5, 100), (1, 1, 4096), (0, 64), (33, 256), (9, 512),
+                                   (70, 128)])
 @pytest.mark.parametrize("eps", [1e-6, 1e-5])
 def test_rmsnorm_f32(ops, shape, eps):
     g = _gen(1)
@@ -48,11 +51,12 @@ def test_rmsnorm_golden(ops):
         assert_close(gx, c["grad_x"])
 
 
-def test_rmsnorm_bf16(ops):
+@pytest.mark.parametrize("rows,dim", [(8 * 256, 1024), (333, 256), (17, 512), (40, 200)])
+def test_rmsnorm_bf16(ops, rows, dim):
     g = _gen(2)
-    x = torch.randn(8, 256, 1024, generator=g)
-    gy = torch.randn(8, 256, 1024, generator=g)
-    w = 1 + 0.02 * torch.randn(1024, generator=g)
+    x = torch.randn(rows, dim, generator=g)
+    gy = torch.randn(rows, dim, generator=g)
+    w = 1 + 0.02 * torch.randn(dim, generator=g)
     xb, gb = x.bfloat16(), gy.bfloat16()
     y = ops.rmsnorm_fwd(xb.to(DEV), w.to(DEV), 1e-5)
     assert y.dtype == torch.bfloat16
@@ -373,3 +377,23 @@ def test_ssm_staged_calls_equal_single_calls(ops, act, dtype):
     r_ref = ops.ssm_bwd(u, gy, *args, h_init=dv(h0), dh_end=dv(dh), dA_end=dv(dA), act=act, saved=saved)
     for k in ("W_cat", "b_cat", "A_log", "D", "scale", "grad_u"):
         assert torch.equal(r[k], r_ref[k]), k
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,dim", [(1000, 256), (37, 1024), (5, 100)])
+def test_rmsnorm_fused_residual_forms_equal_separate_ops(ops, dtype, rows, dim):
+    """rmsnorm_fwd_res = (x + r, norm(x + r)) and rmsnorm_bwd(g_add=) = grad_x + g_add, bit for bit."""
+    g = _gen(rows + dim)
+    x = torch.randn(rows, dim, generator=g).to(DEV, dtype)
+    r = torch.randn(rows, dim, generator=g).to(DEV, dtype)
+    w = (1 + 0.1 * torch.randn(dim, generator=g)).to(DEV)
+    gy = torch.randn(rows, dim, generator=g).to(DEV, dtype)
+    ga = torch.randn(rows, dim, generator=g).to(DEV, dtype)
+    s, y = ops.rmsnorm_fwd_res(x, r, w, 1e-6)
+    s_ref = x + r
+    assert torch.equal(s, s_ref)
+    assert torch.equal(y, ops.rmsnorm_fwd(s_ref, w, 1e-6))
+    gw, gx = ops.rmsnorm_bwd(s_ref, gy, w, 1e-6, g_add=ga)
+    gw_ref, gx_ref = ops.rmsnorm_bwd(s_ref, gy, w, 1e-6)
+    assert torch.equal(gw, gw_ref)
+    assert torch.equal(gx, gx_ref + ga)
