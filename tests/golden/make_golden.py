@@ -2,7 +2,8 @@
 
 Run in a container where the reference (zhry915/icml, pure Python) is mounted read-only:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py /root/reference          # every fixture
+    python tests/golden/make_golden.py /root/reference jvp      # jvp.pt only
 
 The reference is imported as-is with two adjustments, both applied from the outside:
 * ``TORCHDYNAMO_DISABLE=1`` so ``pgf_lm_head``'s ``torch.compile`` wrapper runs eagerly on the CPU;
@@ -34,6 +35,7 @@ def _import_reference(path):
     import pgf_lm_head  # noqa: F401
     import train_singlemamba_optimized as tso  # noqa: F401
     import pgf_mamba_block  # noqa: F401
+    import pgf_mamba  # noqa: F401
 
     def fixed_block_grad(x_block, g_out_block, W1, b1, W2, b2, activation="gelu", comp_dtype=None):
         if comp_dtype is not None:
@@ -57,7 +59,7 @@ def _import_reference(path):
     pgf_ffn._process_single_block_grad = fixed_block_grad
     return {
         "ffn": pgf_ffn, "rms": pgf_rmsnorm, "emb": pgf_embedding, "lm": pgf_lm_head,
-        "tso": tso, "blk": pgf_mamba_block,
+        "tso": tso, "blk": pgf_mamba_block, "mamba": pgf_mamba,
     }
 
 
@@ -229,9 +231,51 @@ def gen_init(R):
     return out
 
 
-def main(ref_path="/root/reference"):
+def gen_jvp(R):
+    """The forward-mode operators: RMSNorm.pgf_jvp (pgf_rmsnorm.py:119-155), pgf_ffn_jvp
+    (pgf_ffn.py:146-180) and FrechetMambaOperator.pgf_forward (pgf_mamba.py:69-139), blocked and
+    streamed as the reference runs them."""
+    out = {}
+    g = torch.Generator().manual_seed(31)
+    x = torch.randn(3, 40, 48, generator=g)
+    xd = torch.randn(3, 40, 48, generator=g)
+    wd = 0.1 * torch.randn(48, generator=g)
+    torch.manual_seed(32)
+    norm = R["rms"].RMSNorm(48)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.05 * torch.randn(48, generator=g))
+    y, yd = norm.pgf_jvp(x, xd, wd, block_size=16)
+    out["rmsnorm"] = {"x": x, "x_dot": xd, "w": norm.weight.detach().clone(), "w_dot": wd, "eps": norm.eps,
+                      "y": y, "y_dot": yd}
+    for act in ("gelu", "relu"):
+        t = {k: torch.randn(*s, generator=g) * sc for k, s, sc in (
+            ("x", (100, 24), 1.0), ("x_dot", (100, 24), 1.0), ("W1", (64, 24), 0.2), ("W1_dot", (64, 24), 0.05),
+            ("b1", (64,), 0.1), ("b1_dot", (64,), 0.05), ("W2", (24, 64), 0.2), ("W2_dot", (24, 64), 0.05),
+            ("b2", (24,), 0.1), ("b2_dot", (24,), 0.05))}
+        y, yd = R["ffn"].pgf_ffn_jvp(t["x"], t["x_dot"], t["W1"], t["W1_dot"], t["b1"], t["b1_dot"], t["W2"],
+                                     t["W2_dot"], t["b2"], t["b2_dot"], block_size=32, activation=act)
+        out[f"ffn_{act}"] = dict(t, y=y, y_dot=yd)
+    for name, L, D in (("frechet", 150, 32), ("frechet_short", 2, 16)):
+        torch.manual_seed(33)
+        m = R["mamba"].FrechetMambaOperator(d_model=D, d_state=16)
+        u = 0.5 * torch.randn(L, D, generator=g)
+        du = torch.randn(L, D, generator=g)
+        y, yd = m.pgf_forward(u, du, block_size=64)
+        blocks = []
+        m.pgf_forward(u, du, block_size=64, streaming=True,
+                      callback=lambda a, b, s, e: blocks.append((s, e, float(a.sum()), float(b.sum()))))
+        out[name] = {"params": _sd(m), "u": u, "du": du, "y": y, "y_dot": yd, "stream": blocks,
+                     "y_standard": m.forward(u).detach()}
+    return out
+
+
+def main(ref_path="/root/reference", only=None):
     R = _import_reference(ref_path)
     torch.set_num_threads(1)
+    if only == "jvp":
+        torch.save(gen_jvp(R), os.path.join(HERE, "jvp.pt"))
+        print("golden fixture jvp.pt written to", HERE)
+        return
     torch.save(gen_ssm_block(R), os.path.join(HERE, "ssm_block.pt"))
     torch.save({"none": gen_ssm_autograd(R, None), "tanh": gen_ssm_autograd(R, "tanh")},
                os.path.join(HERE, "ssm_autograd.pt"))
@@ -240,8 +284,9 @@ def main(ref_path="/root/reference"):
     torch.save(gen_lm(R), os.path.join(HERE, "lm.pt"))
     torch.save(gen_components(R), os.path.join(HERE, "components.pt"))
     torch.save(gen_init(R), os.path.join(HERE, "init.pt"))
+    torch.save(gen_jvp(R), os.path.join(HERE, "jvp.pt"))
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2] if len(sys.argv) > 2 else None)

@@ -117,3 +117,43 @@ def test_float64_oracle_agrees_with_float32_reference():
     r = O.block_pgf_backward(bp, G["x"].double(), G["g"].double(), G["block_size"], scale_grad="reference")
     for k, v in G["grads"].items():
         _close(r["grads"][k].float(), v, atol=2e-5, rtol=1e-4)
+
+
+# ----------------------------------------------------------------------------- forward-mode operators
+def frechet_params(sd):
+    """FrechetMambaOperator state dict (pgf_mamba.py:33-49) -> the oracle's parameter dict."""
+    return {"A_log": sd["A_log"], "dt_w": sd["dt_proj.weight"], "dt_b": sd["dt_proj.bias"],
+            "B_w": sd["B_proj.weight"], "B_b": sd["B_proj.bias"], "C_w": sd["C_proj.weight"],
+            "C_b": sd["C_proj.bias"], "D_w": sd["D"], "scale": sd["redshift_scale"],
+            "init_w": sd["init_estimator.weight"], "init_b": sd["init_estimator.bias"],
+            "init_window": torch.tensor(sd["init_estimator.weight"].shape[1] // sd["D"].shape[0])}
+
+
+def _jclose(a, b, name=""):
+    """float64 oracle vs the reference's float32 outputs: 1e-5 absolute + 1e-4 relative to max|ref|."""
+    _close(a.to(b.dtype) if a.dtype != b.dtype else a, b, atol=1e-5, rtol=1e-4)
+
+
+def test_jvp_oracle_matches_reference():
+    from oracle import jvp_oracle as J
+    G = golden("jvp.pt")
+    r = G["rmsnorm"]
+    y, yd = J.rmsnorm_jvp(r["x"].double(), r["x_dot"].double(), r["w"].double(), r["w_dot"].double(), r["eps"])
+    _jclose(y, r["y"], name="rmsnorm y")
+    _jclose(yd, r["y_dot"], name="rmsnorm y_dot")
+    for act in ("gelu", "relu"):
+        f = {k: v.double() if torch.is_tensor(v) else v for k, v in G[f"ffn_{act}"].items()}
+        y, yd = J.ffn_jvp(f["x"], f["x_dot"], f["W1"], f["W1_dot"], f["b1"], f["b1_dot"], f["W2"], f["W2_dot"],
+                          f["b2"], f["b2_dot"], act)
+        _jclose(y, G[f"ffn_{act}"]["y"], name=f"ffn {act} y")
+        _jclose(yd, G[f"ffn_{act}"]["y_dot"], name=f"ffn {act} y_dot")
+    for name in ("frechet", "frechet_short"):
+        c = G[name]
+        p = {k: v.double() for k, v in frechet_params(c["params"]).items()}
+        y, yd, _, _ = J.frechet_jvp(p, c["u"].double(), c["du"].double())
+        _jclose(y, c["y"], name=f"{name} y")
+        _jclose(yd, c["y_dot"], name=f"{name} y_dot")
+        _jclose(y, c["y_standard"], name=f"{name} y vs forward()")
+        for s, e, ys, yds in c["stream"]:   # the streamed blocks carry the same values
+            assert abs(float(y[s:e].sum()) - ys) <= 1e-5 * max(1.0, abs(ys))
+            assert abs(float(yd[s:e].sum()) - yds) <= 1e-4 * max(1.0, abs(yds))
