@@ -93,6 +93,11 @@ SIGNATURES = {
                                      P, P, P]),
     "pgf_gather_multi": (c_int, [P, I64, P, P, P, c_int, P]),
     "pgf_grad_norm_workspace": (c_size_t, [I64]),
+    "pgf_rmsnorm_jvp": (c_int, [P, P, P, P, P, P, I64, I64, c_float, c_int, P]),
+    "pgf_ffn_jvp_workspace": (c_size_t, [I64, I64, I64, I64, c_int]),
+    "pgf_ffn_jvp": (c_int, [P] * 12 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
+    "pgf_frechet_jvp_workspace": (c_size_t, [I64, I64, I64]),
+    "pgf_frechet_jvp": (c_int, [P] * 13 + [I64] * 3 + [P, c_size_t, P]),
     "pgf_grad_norm": (c_int, [P, I64, P, c_float, P, P, c_size_t, P]),
 }
 

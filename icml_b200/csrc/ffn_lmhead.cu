@@ -134,6 +134,125 @@ extern "C" int pgf_ffn_fwd(const void* x, const float* W1, const float* b1, cons
   return PGF_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Forward-mode derivative (pgf_ffn_jvp, pgf_ffn.py:120-180), per row tile of m rows:
+//   [h_dot | h] (m x 2H): h = act(x W1^T + b1) (GELU epilogue, z kept as aux), and
+//   h_dot = ([x_dot | x] [W1 | W1_dot]^T + b1_dot) act'(z) (act' epilogue at z): the two terms of
+//   z_dot as one product over the concatenated depth;
+//   y = h W2^T + b2;  y_dot = [h_dot | h] [W2 | W2_dot]^T + b2_dot.
+// Four dense products; only x (into [x_dot | x]) and the weights are copied, both with strided
+// 2-D copies.
+// ---------------------------------------------------------------------------------------------
+namespace pgf {
+static int64_t ffn_jvp_tile_rows(int64_t rows, int64_t d_in, int64_t d_h) {
+  const int64_t per_row = (2 * d_in + 3 * d_h) * 4;
+  int64_t t = kTileBytes / (per_row > 0 ? per_row : 1);
+  t = (t / 128) * 128;
+  if (t < 128) t = 128;
+  return rows < t ? rows : t;
+}
+static size_t ffn_jvp_ws_bytes(int64_t rows, int64_t d_in, int64_t d_h, int64_t d_out, int dtype) {
+  const int64_t tr = ffn_jvp_tile_rows(rows < 1 ? 1 : rows, d_in, d_h);
+  const size_t es = dtype ? 2 : 4;
+  size_t b = Workspace::round(size_t(d_h) * 2 * d_in * es) + Workspace::round(size_t(d_out) * 2 * d_h * es);
+  if (dtype) {
+    const size_t t1 = size_t(d_h) * d_in, t2 = size_t(d_out) * d_h;
+    b += Workspace::round((t1 > t2 ? t1 : t2) * 2);
+  }
+  b += Workspace::round(size_t(tr) * 2 * d_in * es) + Workspace::round(size_t(tr) * d_h * es) +
+       Workspace::round(size_t(tr) * 2 * d_h * es);
+  return b + 1024;
+}
+// dst[:, off : off + cols] (pitch dpitch elements) = src (rows x cols float32), in dtype
+static int copy_cols(void* dst, int64_t dpitch, int64_t off, const float* src, int64_t rows, int64_t cols, int dtype,
+                     __nv_bfloat16* tmp, cudaStream_t s) {
+  const size_t es = dtype ? 2 : 4;
+  const void* from = src;
+  if (dtype) {
+    PGF_TRY(to_bf16(src, tmp, rows * cols, s));
+    from = tmp;
+  }
+  PGF_CUDA(cudaMemcpy2DAsync(static_cast<char*>(dst) + off * es, dpitch * es, from, cols * es, cols * es, rows,
+                             cudaMemcpyDeviceToDevice, s));
+  return PGF_OK;
+}
+}  // namespace pgf
+
+extern "C" size_t pgf_ffn_jvp_workspace(int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out, int dtype) {
+  return ffn_jvp_ws_bytes(rows, d_in, d_hidden, d_out, dtype);
+}
+
+extern "C" int pgf_ffn_jvp(const void* x, const void* x_dot, const float* W1, const float* W1_dot, const float* b1,
+                           const float* b1_dot, const float* W2, const float* W2_dot, const float* b2,
+                           const float* b2_dot, void* y, void* y_dot, int64_t rows, int64_t d_in, int64_t d_h,
+                           int64_t d_out, int activation, int dtype, void* ws, size_t ws_bytes,
+                           pgf_stream_t stream) {
+  PGF_CHECK_ARG(x && x_dot && W1 && W1_dot && b1 && b1_dot && W2 && W2_dot && b2 && b2_dot && y && y_dot,
+                "ffn_jvp: null pointer");
+  PGF_CHECK_ARG(activation == PGF_ACT_GELU || activation == PGF_ACT_RELU, "ffn_jvp: bad activation");
+  PGF_CHECK_ARG(dtype == 0 || dtype == 1, "ffn_jvp: bad dtype");
+  PGF_CHECK_ARG(rows >= 0 && d_in > 0 && d_h > 0 && d_out > 0, "ffn_jvp: bad shape");
+  if (rows == 0) return PGF_OK;
+  cudaStream_t s = as_stream(stream);
+  const size_t es = dtype ? 2 : 4;
+  const int64_t tr = ffn_jvp_tile_rows(rows, d_in, d_h);
+  Workspace W(ws, ws_bytes);
+  char* B1 = W.take<char>(size_t(d_h) * 2 * d_in * es);   // [W1 | W1_dot]
+  char* B2 = W.take<char>(size_t(d_out) * 2 * d_h * es);  // [W2 | W2_dot]
+  __nv_bfloat16* tmp = nullptr;
+  if (dtype) {
+    const size_t t1 = size_t(d_h) * d_in, t2 = size_t(d_out) * d_h;
+    tmp = W.take<__nv_bfloat16>(t1 > t2 ? t1 : t2);
+  }
+  char* A1 = W.take<char>(size_t(tr) * 2 * d_in * es);    // [x_dot | x] of a tile
+  char* Z = W.take<char>(size_t(tr) * d_h * es);          // pre-activation of a tile
+  char* HH = W.take<char>(size_t(tr) * 2 * d_h * es);     // [h_dot | h] of a tile
+  if (!B1 || !B2 || (dtype && !tmp) || !A1 || !Z || !HH) {
+    set_error("ffn_jvp: workspace too small (%zu)", ws_bytes);
+    return PGF_ERR_WORKSPACE;
+  }
+  PGF_TRY(copy_cols(B1, 2 * d_in, 0, W1, d_h, d_in, dtype, tmp, s));
+  PGF_TRY(copy_cols(B1, 2 * d_in, d_in, W1_dot, d_h, d_in, dtype, tmp, s));
+  PGF_TRY(copy_cols(B2, 2 * d_h, 0, W2, d_out, d_h, dtype, tmp, s));
+  PGF_TRY(copy_cols(B2, 2 * d_h, d_h, W2_dot, d_out, d_h, dtype, tmp, s));
+  for (int64_t r = 0; r < rows; r += tr) {
+    const int64_t m = rows - r < tr ? rows - r : tr;
+    const char* xt = static_cast<const char*>(x) + r * d_in * es;
+    const char* xdt = static_cast<const char*>(x_dot) + r * d_in * es;
+    PGF_CUDA(cudaMemcpy2DAsync(A1, 2 * d_in * es, xdt, d_in * es, d_in * es, m, cudaMemcpyDeviceToDevice, s));
+    PGF_CUDA(cudaMemcpy2DAsync(A1 + d_in * es, 2 * d_in * es, xt, d_in * es, d_in * es, m, cudaMemcpyDeviceToDevice,
+                               s));
+    // h = act(x W1^T + b1) into the right half of HH, z kept
+    Gemm g1 = mk(m, d_h, d_in, A1 + d_in * es, dtype, 2 * d_in, 0, B1, dtype, 2 * d_in, 0, HH + d_h * es, dtype,
+                 2 * d_h);
+    g1.epi.bias = b1;
+    g1.epi.kind = act_epi(activation, 0);
+    g1.epi.aux_out = Z;
+    g1.epi.aux_out_dtype = dtype;
+    g1.epi.ld_aux_out = d_h;
+    PGF_TRY(run_gemm(g1, s));
+    // h_dot = ([x_dot | x] [W1 | W1_dot]^T + b1_dot) act'(z) into the left half
+    Gemm g2 = mk(m, d_h, 2 * d_in, A1, dtype, 2 * d_in, 0, B1, dtype, 2 * d_in, 0, HH, dtype, 2 * d_h);
+    g2.epi.bias = b1_dot;
+    g2.epi.kind = act_epi(activation, 1);
+    g2.epi.aux = Z;
+    g2.epi.aux_dtype = dtype;
+    g2.epi.ld_aux = d_h;
+    PGF_TRY(run_gemm(g2, s));
+    // y = h W2^T + b2
+    Gemm g3 = mk(m, d_out, d_h, HH + d_h * es, dtype, 2 * d_h, 0, B2, dtype, 2 * d_h, 0,
+                 static_cast<char*>(y) + r * d_out * es, dtype, d_out);
+    g3.epi.bias = b2;
+    PGF_TRY(run_gemm(g3, s));
+    // y_dot = [h_dot | h] [W2 | W2_dot]^T + b2_dot
+    Gemm g4 = mk(m, d_out, 2 * d_h, HH, dtype, 2 * d_h, 0, B2, dtype, 2 * d_h, 0,
+                 static_cast<char*>(y_dot) + r * d_out * es, dtype, d_out);
+    g4.epi.bias = b2_dot;
+    PGF_TRY(run_gemm(g4, s));
+  }
+  return PGF_OK;
+}
+
 extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const float* b1,
                            const float* W2, float* gW1, float* gb1, float* gW2, float* gb2,
                            void* gx, int accumulate, int64_t rows, int64_t d_in, int64_t d_h,

@@ -283,6 +283,62 @@ rmsnorm_bwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ g, const f
   }
 }
 
+// Forward-mode derivative (RMSNorm.pgf_jvp, pgf_rmsnorm.py:54-72): along (x_dot, w_dot),
+//   y = x w / rms,  rms' = mean(x x_dot) / rms,
+//   y_dot = (x_dot / rms - x rms' / rms^2) w + x w_dot / rms.
+template <int VPL, class T>
+__global__ void __launch_bounds__(RMS_WARPS * 32)
+rmsnorm_jvp_kernel(const T* __restrict__ x, const T* __restrict__ xd, const float* __restrict__ w,
+                   const float* __restrict__ wd, T* __restrict__ y, T* __restrict__ yd, int64_t rows, int dim,
+                   float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * RMS_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float v[VPL], t[VPL];
+  float ss = 0.f, sd = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int c = j * 32 + lane;
+    v[j] = c < dim ? ld(x + row * dim, c) : 0.f;
+    t[j] = c < dim ? ld(xd + row * dim, c) : 0.f;
+    ss = fmaf(v[j], v[j], ss);
+    sd = fmaf(v[j], t[j], sd);
+  }
+  ss = warp_sum(ss);
+  sd = warp_sum(sd);
+  const float rinv = 1.0f / sqrtf(ss / float(dim) + eps);
+  const float rdot = (sd / float(dim)) * rinv;  // rms'
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int c = j * 32 + lane;
+    if (c < dim) {
+      const float wc = w[c];
+      st(y + row * dim, c, (v[j] * rinv) * wc);
+      st(yd + row * dim, c, fmaf(t[j], rinv, -v[j] * rdot * rinv * rinv) * wc + (v[j] * rinv) * wd[c]);
+    }
+  }
+}
+
+template <class T>
+static int rms_jvp_dispatch(const T* x, const T* xd, const float* w, const float* wd, T* y, T* yd, int64_t rows,
+                            int dim, float eps, cudaStream_t s) {
+  dim3 grid(ceil_div(rows, RMS_WARPS)), block(RMS_WARPS * 32);
+  const int vpl = ceil_div(dim, 32);
+#define PGF_RMS_J(V) rmsnorm_jvp_kernel<V, T><<<grid, block, 0, s>>>(x, xd, w, wd, y, yd, rows, dim, eps)
+  if (vpl <= 1) PGF_RMS_J(1);
+  else if (vpl <= 2) PGF_RMS_J(2);
+  else if (vpl <= 4) PGF_RMS_J(4);
+  else if (vpl <= 8) PGF_RMS_J(8);
+  else if (vpl <= 16) PGF_RMS_J(16);
+  else if (vpl <= 32) PGF_RMS_J(32);
+  else if (vpl <= 64) PGF_RMS_J(64);
+  else if (vpl <= 128) PGF_RMS_J(128);
+  else { set_error("rmsnorm_jvp: dim %d > 4096 unsupported", dim); return PGF_ERR_UNSUPPORTED; }
+#undef PGF_RMS_J
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
 // chunks per lane of the vector forms (0: use the scalar kernels)
 template <class T>
 static int rms_vec_cpl(const void* a, const void* b, const void* c, const void* d, int64_t dim) {
@@ -406,6 +462,24 @@ extern "C" int pgf_rmsnorm_fwd(const void* x, const float* weight, void* y, int6
     return rms_fwd_dispatch((const __nv_bfloat16*)x, (const __nv_bfloat16*)nullptr, (__nv_bfloat16*)nullptr,
                             weight, (__nv_bfloat16*)y, rows, int(dim), eps, s);
   set_error("rmsnorm_fwd: bad dtype %d", dtype);
+  return PGF_ERR_INVALID;
+}
+
+extern "C" int pgf_rmsnorm_jvp(const void* x, const void* x_dot, const float* weight, const float* weight_dot,
+                               void* y, void* y_dot, int64_t rows, int64_t dim, float eps, int dtype,
+                               pgf_stream_t stream) {
+  PGF_CHECK_ARG(rows >= 0 && dim > 0 && dim <= 4096, "rmsnorm_jvp: bad shape rows=%lld dim=%lld", (long long)rows,
+                (long long)dim);
+  if (rows == 0) return PGF_OK;
+  PGF_CHECK_ARG(x && x_dot && weight && weight_dot && y && y_dot, "rmsnorm_jvp: null pointer");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == PGF_DTYPE_F32)
+    return rms_jvp_dispatch((const float*)x, (const float*)x_dot, weight, weight_dot, (float*)y, (float*)y_dot, rows,
+                            int(dim), eps, s);
+  if (dtype == PGF_DTYPE_BF16)
+    return rms_jvp_dispatch((const __nv_bfloat16*)x, (const __nv_bfloat16*)x_dot, weight, weight_dot,
+                            (__nv_bfloat16*)y, (__nv_bfloat16*)y_dot, rows, int(dim), eps, s);
+  set_error("rmsnorm_jvp: bad dtype %d", dtype);
   return PGF_ERR_INVALID;
 }
 

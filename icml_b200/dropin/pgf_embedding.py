@@ -1,6 +1,6 @@
 """Drop-in module name of the reference's pgf_embedding.py: re-exports icml_b200.pgf_embedding.
 
-Put this directory first on PYTHONPATH (see INTEGRATION.md) and the reference's training
+Put this directory first on PYTHONPATH and the reference's training
 scripts import the CUDA implementation under their own module names.
 """
 import os as _os

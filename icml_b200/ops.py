@@ -190,6 +190,59 @@ def ffn_fwd(x, W1, b1, W2, b2, activation="gelu") -> torch.Tensor:
     return y
 
 
+def ffn_jvp(x, x_dot, W1, W1_dot, b1, b1_dot, W2, W2_dot, b2, b2_dot, activation="gelu"):
+    """(y, y_dot) of the FFN along every input's tangent (pgf_ffn.py:120-180)."""
+    _cuda(x, x_dot, W1)
+    x, x_dot = _c(x), _c(x_dot.to(x.dtype))
+    W1, W1_dot, b1, b1_dot = _f32(W1), _f32(W1_dot), _f32(b1), _f32(b1_dot)
+    W2, W2_dot, b2, b2_dot = _f32(W2), _f32(W2_dot), _f32(b2), _f32(b2_dot)
+    rows, d_in = x.shape
+    d_h, d_out = W1.shape[0], W2.shape[0]
+    y = torch.empty(rows, d_out, dtype=x.dtype, device=x.device)
+    y_dot = torch.empty_like(y)
+    L = lib()
+    ws = _ws(L.pgf_ffn_jvp_workspace(rows, d_in, d_h, d_out, _dt(x)), x.device)
+    check(L.pgf_ffn_jvp(_p(x), _p(x_dot), _p(W1), _p(W1_dot), _p(b1), _p(b1_dot), _p(W2), _p(W2_dot), _p(b2),
+                        _p(b2_dot), _p(y), _p(y_dot), rows, d_in, d_h, d_out, ACT[activation], _dt(x), _p(ws),
+                        ws.numel(), _stream()), "ffn_jvp")
+    return y, y_dot
+
+
+def rmsnorm_jvp(x, x_dot, w, w_dot, eps: float):
+    """(y, y_dot) of RMSNorm along (x_dot, w_dot) (pgf_rmsnorm.py:54-72)."""
+    _cuda(x, x_dot, w)
+    x, x_dot = _c(x), _c(x_dot.to(x.dtype))
+    w, w_dot = _f32(w), _f32(w_dot)
+    dim = x.shape[-1]
+    rows = x.numel() // dim
+    y, y_dot = torch.empty_like(x), torch.empty_like(x)
+    check(lib().pgf_rmsnorm_jvp(_p(x), _p(x_dot), _p(w), _p(w_dot), _p(y), _p(y_dot), rows, dim, eps, _dt(x),
+                                _stream()), "rmsnorm_jvp")
+    return y, y_dot
+
+
+def frechet_jvp(u, u_dot, W_cat, b_cat, A_log, Dp, scale, h0=None, h0_dot=None, want_state=False):
+    """(y, y_dot[, h_end, h_end_dot]) of the Frechet operator's scan over one (L, D) float32
+    sequence along (h0_dot, u_dot) (pgf_mamba.py:69-139)."""
+    _cuda(u, u_dot, W_cat)
+    if u.dtype != torch.float32:
+        raise TypeError("frechet_jvp: float32 sequences only")
+    u, u_dot = _c(u), _c(u_dot.to(u.dtype))
+    W_cat, b_cat, A_log, Dp = _f32(W_cat), _f32(b_cat), _f32(A_log), _f32(Dp)
+    scale = _f32(scale.reshape(1))
+    L_, D = u.shape
+    N = A_log.shape[0]
+    y, y_dot = torch.empty_like(u), torch.empty_like(u)
+    he = torch.empty(D, N, device=u.device) if want_state else None
+    hde = torch.empty(D, N, device=u.device) if want_state else None
+    lb = lib()
+    ws = _ws(lb.pgf_frechet_jvp_workspace(L_, D, N), u.device)
+    check(lb.pgf_frechet_jvp(_p(u), _p(u_dot), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp), _p(scale), _p(_f32(h0)),
+                             _p(_f32(h0_dot)), _p(y), _p(y_dot), _p(he), _p(hde), L_, D, N, _p(ws), ws.numel(),
+                             _stream()), "frechet_jvp")
+    return (y, y_dot, he, hde) if want_state else (y, y_dot)
+
+
 def ffn_bwd(x, g, W1, b1, W2, activation="gelu", need_gx=True) -> Dict[str, torch.Tensor]:
     _cuda(x, g, W1)
     x, g = _c(x), _c(g.to(x.dtype))

@@ -54,4 +54,13 @@ class FFNFunction(torch.autograd.Function):
         return (r.get("grad_x"), r["grad_W1"], r["grad_b1"], r["grad_W2"], r["grad_b2"], None)
 
 
-__all__ = ["pgf_ffn_grad", "pgf_ffn_forward", "FFNFunction"]
+@torch.no_grad()
+def pgf_ffn_jvp(x: torch.Tensor, x_dot: torch.Tensor, W1: torch.Tensor, W1_dot: torch.Tensor, b1: torch.Tensor,
+                b1_dot: torch.Tensor, W2: torch.Tensor, W2_dot: torch.Tensor, b2: torch.Tensor, b2_dot: torch.Tensor,
+                block_size: int = 512, activation: str = "gelu"):
+    """pgf_ffn.py:146-180: (y, y_dot) of the FFN along every input's tangent; rows in workspace-bounded
+    tiles (block_size is accepted for signature compatibility)."""
+    return ops.ffn_jvp(x.detach(), x_dot.detach(), W1, W1_dot, b1, b1_dot, W2, W2_dot, b2, b2_dot, activation)
+
+
+__all__ = ["pgf_ffn_grad", "pgf_ffn_forward", "pgf_ffn_jvp", "FFNFunction"]

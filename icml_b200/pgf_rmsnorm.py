@@ -43,6 +43,12 @@ class RMSNorm(nn.Module):
         return ops.rmsnorm_fwd(x, self.weight, self.eps)
 
     @torch.no_grad()
+    def pgf_jvp(self, x: torch.Tensor, x_dot: torch.Tensor, weight_dot: torch.Tensor,
+                block_size: int = 512):
+        """pgf_rmsnorm.py:119-155: (y, y_dot) along (x_dot, weight_dot), one pass over all rows."""
+        return ops.rmsnorm_jvp(x.detach(), x_dot.detach(), self.weight, weight_dot, self.eps)
+
+    @torch.no_grad()
     def pgf_grad(self, x: torch.Tensor, g_out: torch.Tensor, block_size: int = 512,
                  fp32_accum: bool = True, compute_input_grads: bool = False) -> dict:
         """pgf_rmsnorm.py:157-214: {"grad_weight"[, "grad_x"]}."""

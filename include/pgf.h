@@ -392,6 +392,33 @@ size_t pgf_grad_norm_workspace(int64_t n);
 int pgf_grad_norm(const float* grad, int64_t n, float* norm, float max_norm, float* clip, void* ws,
                   size_t ws_bytes, pgf_stream_t stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Forward-mode (JVP) operators: directional derivatives computed alongside the forward, the
+ * reference's forward-mode PGF path.
+ * pgf_rmsnorm_jvp replaces RMSNorm.pgf_jvp (pgf_rmsnorm.py:54-72, 119-155): y and its derivative
+ *   along (x_dot, weight_dot).
+ * pgf_ffn_jvp replaces pgf_ffn_jvp (pgf_ffn.py:120-180): y = act(x W1^T + b1) W2^T + b2 and its
+ *   derivative along every input's tangent (x_dot, W1_dot, b1_dot, W2_dot, b2_dot); rows are
+ *   processed in tiles bounded by the workspace.
+ * pgf_frechet_jvp replaces the scan of FrechetMambaOperator.pgf_forward (pgf_mamba.py:69-139) over
+ *   a whole (L, D) sequence: W_cat = [dt_proj.weight; B_proj.weight; C_proj.weight] (D+2N, D),
+ *   b_cat likewise, scale = redshift_scale (device scalar), h0 / h0_dot (D, N) the initial state
+ *   and its tangent (NULL = zero; the operator's init_estimator produces them), outputs y, y_dot
+ *   (L, D) and, when non-NULL, the end state and its tangent.  float32; N must be 16.
+ * ------------------------------------------------------------------------------------------ */
+int pgf_rmsnorm_jvp(const void* x, const void* x_dot, const float* weight, const float* weight_dot, void* y,
+                    void* y_dot, int64_t rows, int64_t dim, float eps, int dtype, pgf_stream_t stream);
+size_t pgf_ffn_jvp_workspace(int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out, int dtype);
+int pgf_ffn_jvp(const void* x, const void* x_dot, const float* W1, const float* W1_dot, const float* b1,
+                const float* b1_dot, const float* W2, const float* W2_dot, const float* b2, const float* b2_dot,
+                void* y, void* y_dot, int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out, int activation,
+                int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+size_t pgf_frechet_jvp_workspace(int64_t L, int64_t D, int64_t N);
+int pgf_frechet_jvp(const float* u, const float* u_dot, const float* W_cat, const float* b_cat, const float* A_log,
+                    const float* Dp, const float* scale, const float* h0, const float* h0_dot, float* y,
+                    float* y_dot, float* h_end, float* h_end_dot, int64_t L, int64_t D, int64_t N, void* ws,
+                    size_t ws_bytes, pgf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

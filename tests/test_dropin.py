@@ -10,8 +10,9 @@ from tests.conftest import ROOT, golden
 
 
 def test_dropin_modules_import_under_reference_names():
-    code = ("import pgf_mamba_block, pgf_rmsnorm, pgf_ffn, pgf_embedding, pgf_lm_head, "
+    code = ("import pgf_mamba_block, pgf_rmsnorm, pgf_ffn, pgf_embedding, pgf_lm_head, pgf_mamba, "
             "train_singlemamba_optimized as t;"
+            "assert hasattr(pgf_mamba, 'FrechetMambaOperator');"
             "assert hasattr(pgf_mamba_block, 'PGFMambaSequential');"
             "assert hasattr(t, 'SingleLayerMambaPGF');"
             "print(pgf_mamba_block.PGFMambaBlock.__module__)")
@@ -44,6 +45,14 @@ def test_signatures_match_reference():
                                               "output_activation", "ffn_activation"]
     assert params(SingleLayerMambaPGF._pass2_block_direct_grad) == [
         "self", "u_block", "g_out_block", "h0_block", "delta_h_next", "dA_next", "fp32_accum"]
+    # forward-mode operators (pgf_ffn.py:146-158, pgf_rmsnorm.py:120-126, pgf_mamba.py:36,69)
+    from icml_b200.pgf_mamba import FrechetMambaOperator
+    assert params(pgf_ffn.pgf_ffn_jvp) == ["x", "x_dot", "W1", "W1_dot", "b1", "b1_dot", "W2", "W2_dot", "b2",
+                                            "b2_dot", "block_size", "activation"]
+    assert params(RMSNorm.pgf_jvp) == ["self", "x", "x_dot", "weight_dot", "block_size"]
+    assert params(FrechetMambaOperator.__init__) == ["self", "d_model", "d_state", "init_window"]
+    assert params(FrechetMambaOperator.pgf_forward) == ["self", "u_seq", "du_seq", "block_size", "streaming",
+                                                        "callback"]
 
 
 def test_seeded_init_matches_reference():
@@ -59,3 +68,16 @@ def test_seeded_init_matches_reference():
     sd = SingleLayerMambaPGF(24, 16).state_dict()
     for k, v in G["ssm"].items():
         assert torch.equal(sd[k], v), k
+
+
+def test_frechet_operator_seeded_init_matches_reference():
+    """FrechetMambaOperator keeps the reference's parameter names and construction order
+    (pgf_mamba.py:33-49): a seeded construction gives the reference's initial weights."""
+    from icml_b200.pgf_mamba import FrechetMambaOperator
+    G = golden("jvp.pt")
+    for name, D in (("frechet", 32), ("frechet_short", 16)):
+        torch.manual_seed(33)
+        sd = FrechetMambaOperator(d_model=D, d_state=16).state_dict()
+        assert set(sd) == set(G[name]["params"])
+        for k, v in G[name]["params"].items():
+            assert torch.equal(sd[k], v), k
