@@ -55,7 +55,7 @@ def parse():
                     help="reference: the reference's SSM block (d_inner = d_model); std: the Mamba-standard "
                          "block of the benchmark configurations (expand 2, d_conv 4, dt_rank 16, final "
                          "RMSNorm, tied LM head)")
-    ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "all"],
+    ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "jvp", "all"],
                     help="component microbenchmarks instead of the LM step (RMSNorm [8,4096,1024]; FFN "
                          "1024-4096-1024 on 32768 tokens; LM head + CE d=1024, vocab 50257, 32768 tokens)")
     ap.add_argument("--stash", default="device", choices=["device", "host"],
@@ -245,7 +245,10 @@ def run_components(a):
     hbm, tf = peaks.get("hbm_gbs", 6650.0), peaks.get("bf16_tflops", 1590.0)
     dev = torch.device("cuda")
     g = torch.Generator(device="cpu").manual_seed(0)
-    which = ["rmsnorm", "ffn", "lmhead"] if a.component == "all" else [a.component]
+    which = ["rmsnorm", "ffn", "lmhead", "jvp"] if a.component == "all" else [a.component]
+    if "jvp" in which:
+        run_jvp_components(a, hbm, tf, g, dev)
+        which = [w for w in which if w != "jvp"]
     for dt_name, dt in (("bf16", torch.bfloat16), ("fp32", torch.float32)):
         if "rmsnorm" in which:
             x = torch.randn(8, 4096, 1024, generator=g).to(dev, dt)
@@ -285,6 +288,61 @@ def run_components(a):
                               "value": fl / ms / 1e9, "unit": "TFLOP/s", "dtype": dt_name, "ms": ms,
                               "roofline": {"bound": "tensor", "achieved": fl / ms / 1e9, "peak": tf,
                                            "frac": fl / ms / 1e9 / tf}}), flush=True)
+
+
+def run_jvp_components(a, hbm, tf, g, dev):
+    """Forward-mode operators: the Frechet operator's JVP at the reference scaling benchmark's model
+    (d_model 256, d_state 16; bench_scaling.py:29-32), the FFN JVP and the RMSNorm JVP."""
+    from icml_b200 import ops
+    from icml_b200.pgf_mamba import FrechetMambaOperator
+    L, D = a.seq_len, 256
+    torch.manual_seed(0)
+    m = FrechetMambaOperator(d_model=D, d_state=16).to(dev)
+    u = (0.1 * torch.randn(L, D, generator=g)).to(dev)
+    du = torch.randn(L, D, generator=g)
+    du = (du / du.norm()).to(dev)
+    ms = _time(lambda: m.pgf_forward(u, du), a.steps, a.warmup)
+    by = L * D * 4 * 4  # read u, u_dot; write y, y_dot (float32)
+    line = {"metric": "Frechet operator JVP tokens/s (d_model 256, d_state 16, y and y_dot)", "value": L / ms * 1e3,
+            "unit": "tokens/s", "dtype": "fp32", "ms": ms, "config": {"workload": f"L={L} x d_model {D}"},
+            "roofline": {"bound": "hbm", "achieved": by / ms / 1e6, "peak": hbm, "frac": by / ms / 1e6 / hbm,
+                         "note": "the (state, tangent) scan is instruction-bound; bytes are its inputs/outputs"}}
+    if not a.no_cpu_baseline:
+        import time
+        from oracle import jvp_oracle as J
+        from tests.test_oracle_golden import frechet_params
+        torch.set_num_threads(os.cpu_count() or 1)
+        n = 512
+        p = {k: v.detach().cpu().double() for k, v in
+             frechet_params({k: v.detach().cpu() for k, v in m.state_dict().items()}).items()}
+        uc, duc = u[:n].cpu().double(), du[:n].cpu().double()
+        t0 = time.perf_counter()
+        J.frechet_jvp(p, uc, duc)
+        dt_ = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": n / dt_, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                                "sample": f"the oracle's token-by-token JVP (float64) over the first {n} tokens"}
+    print(json.dumps(line), flush=True)
+    T, d, dh = 32768, 1024, 4096
+    for dt_name, dt in (("bf16", torch.bfloat16), ("fp32", torch.float32)):
+        x = torch.randn(T, d, generator=g).to(dev, dt)
+        xd = torch.randn(T, d, generator=g).to(dev, dt)
+        ws = [(0.02 * torch.randn(*s_, generator=g)).to(dev) for s_ in ((dh, d), (dh, d), (dh,), (dh,), (d, dh),
+                                                                       (d, dh), (d,), (d,))]
+        ms = _time(lambda: ops.ffn_jvp(x, xd, *ws), a.steps, a.warmup)
+        fl = 6 * 2.0 * T * d * dh  # z (1), z_dot over 2d (2), y (1), y_dot over 2 dh (2)
+        print(json.dumps({"metric": "FFN JVP 1024-4096-1024, 32768 tokens", "value": fl / ms / 1e9, "unit": "TFLOP/s",
+                          "dtype": dt_name, "ms": ms,
+                          "roofline": {"bound": "tensor", "achieved": fl / ms / 1e9, "peak": tf,
+                                       "frac": fl / ms / 1e9 / tf}}), flush=True)
+        x3 = torch.randn(8, 4096, 1024, generator=g).to(dev, dt)
+        xd3 = torch.randn(8, 4096, 1024, generator=g).to(dev, dt)
+        w, wd = (1 + 0.02 * torch.randn(1024, generator=g)).to(dev), (0.02 * torch.randn(1024, generator=g)).to(dev)
+        ms = _time(lambda: ops.rmsnorm_jvp(x3, xd3, w, wd, 1e-5), a.steps, a.warmup)
+        by = 8 * 4096 * 1024 * x3.element_size() * 4  # read x, x_dot; write y, y_dot
+        print(json.dumps({"metric": "RMSNorm JVP [8,4096,1024]", "value": by / ms / 1e6, "unit": "GB/s",
+                          "dtype": dt_name, "ms": ms,
+                          "roofline": {"bound": "hbm", "achieved": by / ms / 1e6, "peak": hbm,
+                                       "frac": by / ms / 1e6 / hbm}}), flush=True)
 
 
 def zipf_ids(n, vocab, seed, s=1.1):
