@@ -184,6 +184,44 @@ def _act_prime(act, x):
     raise ValueError(act)
 
 
+def _act_double_prime(act, x):
+    """train_singlemamba_optimized.py:103-114."""
+    if act == "tanh":
+        t = torch.tanh(x)
+        return -2.0 * t * (1.0 - t * t)
+    return torch.zeros_like(x)
+
+
+def ssm_state_hvp(p: Dict[str, Tensor], u: Tensor, target: Tensor, v_h: Tensor,
+                  act: Optional[str] = None) -> Tensor:
+    """State HVP trajectory (L, B, d, N) of SingleLayerMambaPGF.compute_state_hvp
+    (train_singlemamba_optimized.py:563-685 with _pass2_block's HVP branch :249-275), over the
+    whole sequence instead of blocks (the block hand-offs are the same recurrences):
+      xi_t = dA_t xi_{t-1}, xi_{-1} = v_h;
+      S_t = hf_t (C_t . xi_t) C_t,  hf = l'' (no activation) or l'' act'(C.h)^2 + grad_y act''(C.h),
+      l'' = 2 scale_const, grad_y = scale_const (y_pred - target), scale_const = 2 / (L d B);
+      zeta_t = dA_{t+1} zeta_{t+1} + S_t with dA_L = 1, zeta_L = 0 (the output).
+    h is the forward trajectory from a zero state (:580-596)."""
+    Bsz, L, d = u.shape
+    dt_in, Bv, Cv = ssm_project(p, u)
+    _, _, dA, b = _discretise(p, u, dt_in, Bv)                     # (L, B, d, N)
+    Ct = Cv.transpose(0, 1)                                          # (L, B, N)
+    scale_const = 2.0 / (L * d * Bsz)
+    l2 = 2.0 * scale_const
+    if act is None:
+        hf = torch.full((L, Bsz, d), l2, dtype=u.dtype)
+    else:
+        traj = scan_linear(dA, b, torch.zeros(Bsz, d, dA.shape[-1], dtype=u.dtype))
+        hc = (Ct.unsqueeze(2) * traj).sum(-1)                        # (L, B, d)
+        y_pred = (_act(act, hc) + p["D"] * u.transpose(0, 1)) * p["scale"]
+        grad_y = scale_const * (y_pred - target.transpose(0, 1))
+        hf = l2 * _act_prime(act, hc) ** 2 + grad_y * _act_double_prime(act, hc)
+    xi = scan_linear(dA, torch.zeros_like(dA), v_h)
+    S = (hf * (Ct.unsqueeze(2) * xi).sum(-1)).unsqueeze(-1) * Ct.unsqueeze(2)
+    a_fwd = torch.cat([dA[1:], torch.ones_like(dA[:1])], 0)
+    return scan_linear_reverse(a_fwd, S, torch.zeros_like(v_h))
+
+
 def ssm_block_grad(p: Dict[str, Tensor], u_block: Tensor, g_block: Tensor, h0: Tensor,
                    delta_h_next: Tensor, dA_next: Tensor, act: Optional[str] = None) -> Dict[str, Tensor]:
     """One block of the PGF backward: recompute from h0, reverse adjoint scan, all grads.

@@ -4,6 +4,7 @@ Run in a container where the reference (zhry915/icml, pure Python) is mounted re
 
     python tests/golden/make_golden.py /root/reference          # every fixture
     python tests/golden/make_golden.py /root/reference jvp      # jvp.pt only
+    python tests/golden/make_golden.py /root/reference hvp      # hvp.pt only
 
 The reference is imported as-is with two adjustments, both applied from the outside:
 * ``TORCHDYNAMO_DISABLE=1`` so ``pgf_lm_head``'s ``torch.compile`` wrapper runs eagerly on the CPU;
@@ -269,12 +270,36 @@ def gen_jvp(R):
     return out
 
 
+def gen_hvp(R):
+    """SingleLayerMambaPGF.compute_state_hvp (train_singlemamba_optimized.py:563-685), blocked as the
+    reference runs it, with no output activation and with tanh and relu."""
+    out = {}
+    for act, seed in ((None, 41), ("tanh", 42), ("relu", 43)):
+        torch.manual_seed(seed)
+        B, L, d, N = 2, 100, 16, 16
+        m = R["tso"].SingleLayerMambaPGF(d, N, output_activation=act)
+        with torch.no_grad():
+            m.scale.mul_(torch.rand(d) + 0.5)
+            m.D.mul_(torch.rand(d) + 0.5)
+        u = torch.randn(B, L, d)
+        target = torch.randn(B, L, d)
+        v_h = torch.randn(B, d, N)
+        hvp = m.compute_state_hvp(u, target, v_h, block_size=32)
+        out[str(act)] = {"params": {k: v.detach().clone() for k, v in _sd(m).items()}, "u": u, "target": target,
+                         "v_h": v_h, "act": act, "block_size": 32, "hvp": hvp.detach().clone()}
+    return out
+
+
 def main(ref_path="/root/reference", only=None):
     R = _import_reference(ref_path)
     torch.set_num_threads(1)
     if only == "jvp":
         torch.save(gen_jvp(R), os.path.join(HERE, "jvp.pt"))
         print("golden fixture jvp.pt written to", HERE)
+        return
+    if only == "hvp":
+        torch.save(gen_hvp(R), os.path.join(HERE, "hvp.pt"))
+        print("golden fixture hvp.pt written to", HERE)
         return
     torch.save(gen_ssm_block(R), os.path.join(HERE, "ssm_block.pt"))
     torch.save({"none": gen_ssm_autograd(R, None), "tanh": gen_ssm_autograd(R, "tanh")},
@@ -285,6 +310,7 @@ def main(ref_path="/root/reference", only=None):
     torch.save(gen_components(R), os.path.join(HERE, "components.pt"))
     torch.save(gen_init(R), os.path.join(HERE, "init.pt"))
     torch.save(gen_jvp(R), os.path.join(HERE, "jvp.pt"))
+    torch.save(gen_hvp(R), os.path.join(HERE, "hvp.pt"))
     print("golden fixtures written to", HERE)
 
 

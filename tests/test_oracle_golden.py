@@ -157,3 +157,11 @@ def test_jvp_oracle_matches_reference():
         for s, e, ys, yds in c["stream"]:   # the streamed blocks carry the same values
             assert abs(float(y[s:e].sum()) - ys) <= 1e-5 * max(1.0, abs(ys))
             assert abs(float(yd[s:e].sum()) - yds) <= 1e-4 * max(1.0, abs(yds))
+
+
+def test_state_hvp_oracle_matches_reference():
+    G = golden("hvp.pt")
+    for act, c in G.items():
+        p = {k: v.double() for k, v in _ssm_params(c["params"]).items()}
+        z = O.ssm_state_hvp(p, c["u"].double(), c["target"].double(), c["v_h"].double(), c["act"])
+        _close(z.to(c["hvp"].dtype), c["hvp"], atol=1e-7, rtol=1e-4)
