@@ -322,6 +322,18 @@ def run_jvp_components(a, hbm, tf, g, dev):
         line["cpu_baseline"] = {"value": n / dt_, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                                 "sample": f"the oracle's token-by-token JVP (float64) over the first {n} tokens"}
     print(json.dumps(line), flush=True)
+    # state HVP trajectory of the reference SSM layer (train_singlemamba_optimized.py:563-685)
+    from icml_b200.train_singlemamba_optimized import SingleLayerMambaPGF
+    lay = SingleLayerMambaPGF(D, 16).to(dev)
+    uh = torch.randn(1, L, D, generator=g).to(dev)
+    th = torch.randn(1, L, D, generator=g).to(dev)
+    vh = torch.randn(1, D, 16, generator=g).to(dev)
+    ms = _time(lambda: lay.compute_state_hvp(uh, th, vh, 4096), a.steps, a.warmup)
+    by = L * D * 16 * 4 + 2 * L * D * 4  # the (L, B, D, N) trajectory written, u and target read
+    print(json.dumps({"metric": "SSM state-HVP trajectory tokens/s (d_model 256, d_state 16)", "value": L / ms * 1e3,
+                      "unit": "tokens/s", "dtype": "fp32", "ms": ms, "config": {"workload": f"B=1 x L={L} x d {D}"},
+                      "roofline": {"bound": "hbm", "achieved": by / ms / 1e6, "peak": hbm,
+                                   "frac": by / ms / 1e6 / hbm}}), flush=True)
     T, d, dh = 32768, 1024, 4096
     for dt_name, dt in (("bf16", torch.bfloat16), ("fp32", torch.float32)):
         x = torch.randn(T, d, generator=g).to(dev, dt)

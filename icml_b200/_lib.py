@@ -97,6 +97,8 @@ SIGNATURES = {
     "pgf_ffn_jvp_workspace": (c_size_t, [I64, I64, I64, I64, c_int]),
     "pgf_ffn_jvp": (c_int, [P] * 12 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
     "pgf_frechet_jvp_workspace": (c_size_t, [I64, I64, I64]),
+    "pgf_ssm_state_hvp_workspace": (c_size_t, [I64, I64, I64, I64, c_int]),
+    "pgf_ssm_state_hvp": (c_int, [P] * 9 + [I64] * 4 + [c_int, P, c_size_t, P]),
     "pgf_frechet_jvp": (c_int, [P] * 13 + [I64] * 3 + [P, c_size_t, P]),
     "pgf_grad_norm": (c_int, [P, I64, P, c_float, P, P, c_size_t, P]),
 }

@@ -243,6 +243,21 @@ def frechet_jvp(u, u_dot, W_cat, b_cat, A_log, Dp, scale, h0=None, h0_dot=None, 
     return (y, y_dot, he, hde) if want_state else (y, y_dot)
 
 
+def ssm_state_hvp(u, target, W_cat, b_cat, A_log, Dp, scale, v_h, act=None):
+    """(L, B, D, N) state-HVP trajectory of the MSE loss (train_singlemamba_optimized.py:563-685)."""
+    _cuda(u, target, W_cat)
+    u, target = _f32(u), _f32(target)
+    W_cat, b_cat, A_log, Dp, scale, v_h = (_f32(t) for t in (W_cat, b_cat, A_log, Dp, scale, v_h))
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    out = torch.empty(L_, Bsz, D, N, device=u.device)
+    lb = lib()
+    ws = _ws(lb.pgf_ssm_state_hvp_workspace(Bsz, L_, D, N, ACT[act]), u.device)
+    check(lb.pgf_ssm_state_hvp(_p(u), _p(target), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp), _p(scale), _p(v_h),
+                               _p(out), Bsz, L_, D, N, ACT[act], _p(ws), ws.numel(), _stream()), "ssm_state_hvp")
+    return out
+
+
 def ffn_bwd(x, g, W1, b1, W2, activation="gelu", need_gx=True) -> Dict[str, torch.Tensor]:
     _cuda(x, g, W1)
     x, g = _c(x), _c(g.to(x.dtype))

@@ -116,6 +116,17 @@ class SingleLayerMambaPGF(nn.Module):
         optimizer.step()
         return loss.item()
 
+    # --- (:563-685)
+    @torch.no_grad()
+    def compute_state_hvp(self, u, target_y, v_h, block_size):
+        """State HVP trajectory (L, B, D, N) of the MSE loss against target_y along v_h (B, D, N) on the
+        initial state, for the whole sequence at once (block_size is accepted for signature
+        compatibility; the kernels chunk the sequence themselves)."""
+        W, b = _cat_weights(self)
+        B_, L_, D = u.shape
+        v = v_h if v_h is not None else torch.zeros(B_, D, self.d_state, device=u.device)
+        return ops.ssm_state_hvp(u, target_y, W, b, self.A_log, self.D, self.scale, v, act=self.output_activation)
+
     # --- (:731-765)
     def forward_standard(self, u):
         return SSMFunction.apply(u, self.dt_proj.weight, self.dt_proj.bias, self.B_proj.weight,

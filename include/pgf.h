@@ -414,6 +414,15 @@ int pgf_ffn_jvp(const void* x, const void* x_dot, const float* W1, const float* 
                 void* y, void* y_dot, int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out, int activation,
                 int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
 size_t pgf_frechet_jvp_workspace(int64_t L, int64_t D, int64_t N);
+/* State Hessian-vector product: replaces SingleLayerMambaPGF.compute_state_hvp
+ * (train_singlemamba_optimized.py:563-685, HVP branch :249-275) for the MSE loss against target
+ * (B, L, D): out (L, B, D, N) = the trajectory of d^2 Loss / dh^2 . v_h with v_h (B, D, N) the
+ * direction on the initial state.  Same weights as pgf_ssm_fwd; float32; N must be 16. */
+size_t pgf_ssm_state_hvp_workspace(int64_t Bsz, int64_t L, int64_t D, int64_t N, int act);
+int pgf_ssm_state_hvp(const float* u, const float* target, const float* W_cat, const float* b_cat,
+                      const float* A_log, const float* Dp, const float* scale, const float* v_h, float* out,
+                      int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, void* ws, size_t ws_bytes,
+                      pgf_stream_t stream);
 int pgf_frechet_jvp(const float* u, const float* u_dot, const float* W_cat, const float* b_cat, const float* A_log,
                     const float* Dp, const float* scale, const float* h0, const float* h0_dot, float* y,
                     float* y_dot, float* h_end, float* h_end_dot, int64_t L, int64_t D, int64_t N, void* ws,

@@ -1,5 +1,6 @@
-"""Forward-mode operators on the GPU: RMSNorm.pgf_jvp, pgf_ffn_jvp and the Frechet operator's
-pgf_forward against the reference's own outputs (tests/golden/jvp.pt) and the float64 oracle."""
+"""Forward-mode operators and the state HVP on the GPU: RMSNorm.pgf_jvp, pgf_ffn_jvp, the Frechet
+operator's pgf_forward and SingleLayerMambaPGF.compute_state_hvp against the reference's own outputs
+(tests/golden/jvp.pt, hvp.pt) and the float64 oracle."""
 import pytest
 import torch
 
@@ -141,3 +142,44 @@ def test_frechet_jvp_end_state_and_linearity():
     _, yb = ops.frechet_jvp(u, d2, W, b, m.A_log, m.D, m.redshift_scale)
     _, yab = ops.frechet_jvp(u, 2 * d1 - 3 * d2, W, b, m.A_log, m.D, m.redshift_scale)
     assert_close(yab, 2 * ya - 3 * yb, atol=1e-4, name="linearity")
+
+
+# ----------------------------------------------------------------------------- state HVP
+def _ssm_layer(c):
+    from icml_b200.train_singlemamba_optimized import SingleLayerMambaPGF
+    d = c["params"]["D"].shape[0]
+    m = SingleLayerMambaPGF(d, 16, output_activation=c["act"])
+    m.load_state_dict(c["params"])
+    return m.to(DEV)
+
+
+@pytest.mark.parametrize("act", ["None", "tanh", "relu"])
+def test_state_hvp_golden(act):
+    c = golden("hvp.pt")[act]
+    m = _ssm_layer(c)
+    z = m.compute_state_hvp(c["u"].to(DEV), c["target"].to(DEV), c["v_h"].to(DEV), c["block_size"])
+    assert z.shape == c["hvp"].shape
+    assert_close(z, c["hvp"], atol=1e-7, name="hvp")
+
+
+@pytest.mark.parametrize("act", [None, "tanh"])
+@pytest.mark.parametrize("B,L,d", [(2, 1000, 64), (1, 4099, 32), (3, 7, 16)])
+def test_state_hvp_f64(act, B, L, d):
+    """Many chunks (prefix of dt over chunks, reverse compose) and ragged / single-chunk lengths."""
+    from oracle import pgf_oracle as O
+    from icml_b200.train_singlemamba_optimized import SingleLayerMambaPGF
+    torch.manual_seed(L + d)
+    m = SingleLayerMambaPGF(d, 16, output_activation=act)
+    g = _gen(L)
+    with torch.no_grad():
+        m.scale.mul_(0.5 + torch.rand(d, generator=g))
+    u = torch.randn(B, L, d, generator=g)
+    tg = torch.randn(B, L, d, generator=g)
+    v = torch.randn(B, d, 16, generator=g)
+    z = m.to(DEV).compute_state_hvp(u.to(DEV), tg.to(DEV), v.to(DEV), 64)
+    p = {k: getattr(m, k).detach().cpu().double() for k in ("A_log", "D", "scale")}
+    p.update({"dt_w": m.dt_proj.weight, "dt_b": m.dt_proj.bias, "B_w": m.B_proj.weight, "B_b": m.B_proj.bias,
+              "C_w": m.C_proj.weight, "C_b": m.C_proj.bias})
+    p = {k: v_.detach().cpu().double() for k, v_ in p.items()}
+    ref = O.ssm_state_hvp(p, u.double(), tg.double(), v.double(), act)
+    assert_close(z, ref, atol=1e-9, rtol=1e-4, name="hvp")
