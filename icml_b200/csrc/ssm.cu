@@ -409,6 +409,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
   const AConst K = load_A(a, l.nq);
   float2 h[NP] = {f2(0.f), f2(0.f)}, e[NP];
   if (l.ch) ld_states(a.hC + ((l.b * (a.nC + 1) + l.c) * a.D + l.d) * NST + l.nq * NS, h);
+  const float2 h_start[NP] = {h[0], h[1]};
   // D and scale only enter the output (a.y); the act'(C h) mode (a.y == nullptr) may run without them
   const float Dd = (l.ch && a.y) ? a.Dp[l.d] : 0.f;
   const float sc = (l.ch && a.y) ? a.scale[l.d] : 0.f;
@@ -422,7 +423,16 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
     const int nt = sub_len(l, k);
     if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
     if (a.ckpt_write && l.ch) {
-      st_states(a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.D + l.d) * NST + l.nq * NS, h);
+      const int64_t ck = (l.b * a.nC + l.c) * KS + k;
+      if (a.ckpt_write == 2) {
+        // the layout the main backward reads: a state is ckpt + exp(A S) H_chunk; with S = 0 the
+        // checkpoint is the state's offset from the chunk start state
+        const float2 off[NP] = {fma2(h_start[0], f2(-1.f), h[0]), fma2(h_start[1], f2(-1.f), h[1])};
+        st_states(a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS, off);
+        if (l.nq == 0) a.ckpt_s[ck * a.D + l.d] = 0.f;
+      } else {
+        st_states(a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS, h);
+      }
     }
     const Stage& S = stg[k & 1];
 #pragma unroll
@@ -955,7 +965,7 @@ static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, c
                         const float* Dp, const float* scale, const float* h_init, void* y,
                         float* h_final, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act,
                         int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream, float* saved,
-                        int stage = STAGE_ALL, float* sum_dt = nullptr) {
+                        int stage = STAGE_ALL, float* sum_dt = nullptr, float* states_out = nullptr) {
   PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
   PGF_CHECK_ARG(u && W_cat && b_cat && A_log, "ssm_fwd: null pointer");
   PGF_CHECK_ARG(stage == STAGE_BEGIN || (Dp && scale && y), "ssm_fwd: null pointer");
@@ -975,7 +985,7 @@ static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, c
   a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act;
   a.h_init = stage == STAGE_BEGIN ? nullptr : h_init;
   const void* wop;
-  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved, stage != STAGE_FINISH));
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved ? saved : states_out, stage != STAGE_FINISH));
   a.y0 = W.take<float>(size_t(Bsz) * L * D);
   if (!a.y0) { set_error("ssm_fwd: workspace too small (%zu)", ws_bytes); return PGF_ERR_WORKSPACE; }
   a.y = y;
@@ -1015,6 +1025,51 @@ extern "C" int pgf_ssm_fwd(const void* u, const float* W_cat, const float* b_cat
                            pgf_stream_t stream) {
   return ssm_fwd_impl(u, W_cat, b_cat, A_log, Dp, scale, h_init, y, h_final, Bsz, L, D, N, act, dtype,
                       ws, ws_bytes, stream, nullptr);
+}
+
+extern "C" size_t pgf_ssm_states_size(int64_t Bsz, int64_t L, int64_t D, int64_t N) {
+  (void)N;
+  SsmPlan p = plan_of(Bsz < 1 ? 1 : Bsz, L < 1 ? 1 : L, D < 1 ? 1 : D);
+  return saved_hc_floats(p) * sizeof(float);
+}
+
+extern "C" int pgf_ssm_fwd_states(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                                  const float* Dp, const float* scale, const float* h_init, void* y, float* states,
+                                  int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                                  size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(states, "ssm_fwd_states: null state buffer");
+  PGF_CHECK_ARG(L > 0, "ssm_fwd_states: empty sequence");
+  return ssm_fwd_impl(u, W_cat, b_cat, A_log, Dp, scale, h_init, y, nullptr, Bsz, L, D, N, act, dtype, ws, ws_bytes,
+                      stream, nullptr, STAGE_ALL, nullptr, states);
+}
+
+extern "C" int pgf_ssm_fwd_save_states(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                                       const float* Dp, const float* scale, const float* states, void* y,
+                                       float* saved, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act,
+                                       int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_TRY(check_common(Bsz, L, D, N, act, dtype));
+  PGF_CHECK_ARG(u && W_cat && b_cat && A_log && Dp && scale && states && y && saved, "ssm_fwd_save_states: null pointer");
+  PGF_CHECK_ARG(L > 0, "ssm_fwd_save_states: empty sequence");
+  cudaStream_t s = as_stream(stream);
+  SsmPlan p = plan_of(Bsz, L, D);
+  Workspace W(ws, ws_bytes);
+  SsmArgs a = {};
+  a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act;
+  const void* wop;
+  // projection; the boundary states come from the caller (copied where the backward reads them)
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved, true));
+  PGF_CUDA(cudaMemcpyAsync(saved, states, saved_hc_floats(p) * sizeof(float), cudaMemcpyDeviceToDevice, s));
+  a.y = y;
+  a.y_bf16 = dtype;
+  a.ckpt_g = saved + saved_hc_floats(p);
+  a.ckpt_s = a.ckpt_g + saved_ckpt_floats(p);
+  a.ckpt_write = 2;
+  dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
+  prof_begin(PROF_SSM_OUT_FWD, s);
+  ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+  prof_end(PROF_SSM_OUT_FWD, s, bytes_out_fwd(a, a.u_bf16 ? 2 : 4));
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
 }
 
 extern "C" size_t pgf_ssm_saved_size(int64_t Bsz, int64_t L, int64_t D, int64_t N) {

@@ -364,9 +364,27 @@ def ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, want_h_fin
     return y, hf
 
 
-def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None):
+def ssm_fwd_states(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None):
+    """ssm_fwd that also returns the boundary states of every chunk (for ssm_fwd_save(states=...))."""
+    _cuda(u, W_cat)
+    u = _c(u)
+    Bsz, L_, D = u.shape
+    N = A_log.shape[0]
+    y = torch.empty_like(u)
+    Lb = lib()
+    states = torch.empty(Lb.pgf_ssm_states_size(Bsz, L_, D, N) // 4, dtype=torch.float32, device=u.device)
+    ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 0), u.device)
+    W_cat, b_cat, A_log, Dp, scale, h_init = (_f32(t) for t in (W_cat, b_cat, A_log, Dp, scale, h_init))
+    check(Lb.pgf_ssm_fwd_states(_p(u), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp), _p(scale), _p(h_init), _p(y),
+                                _p(states), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(), _stream()),
+          "ssm_fwd_states")
+    return y, states
+
+
+def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, states=None):
     """ssm_fwd that also returns the saved scan states (boundary states + 8-token checkpoints)
-    for ssm_bwd(..., saved=...) on the same inputs."""
+    for ssm_bwd(..., saved=...) on the same inputs.  With `states` (from ssm_fwd_states on the
+    same inputs) the boundary states are not recomputed: one pass over the sequence."""
     _cuda(u, W_cat)
     u = _c(u)
     Bsz, L_, D = u.shape
@@ -376,6 +394,13 @@ def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None):
     saved = torch.empty(Lb.pgf_ssm_saved_size(Bsz, L_, D, N) // 4, dtype=torch.float32, device=u.device)
     ws = _ws(Lb.pgf_ssm_workspace(Bsz, L_, D, N, _dt(u), 0), u.device)
     W_cat, b_cat, A_log, Dp, scale, h_init = (_f32(t) for t in (W_cat, b_cat, A_log, Dp, scale, h_init))
+    if states is not None:
+        if h_init is not None:
+            raise ValueError("ssm_fwd_save: states already include the initial state")
+        check(Lb.pgf_ssm_fwd_save_states(_p(u), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp), _p(scale), _p(states),
+                                         _p(y), _p(saved), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(),
+                                         _stream()), "ssm_fwd_save_states")
+        return y, saved
     check(Lb.pgf_ssm_fwd_save(_p(u), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp), _p(scale), _p(h_init),
                               _p(y), _p(saved), Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(),
                               _stream()), "ssm_fwd_save")

@@ -64,27 +64,37 @@ class PGFMambaBlock(nn.Module):
         return f.reshape(B, L, D) + res
 
     @torch.no_grad()
-    def pgf_forward(self, x: torch.Tensor) -> torch.Tensor:
-        """pgf_mamba_block.py:70-126."""
+    def pgf_forward(self, x: torch.Tensor, return_ssm_states: bool = False):
+        """pgf_mamba_block.py:70-126.  With return_ssm_states, also the scan's boundary states (for
+        pgf_backward(..., ssm_states=...), which then need not recompute them)."""
         B, L, D = x.shape
         xn = self.norm1.pgf_forward(x, block_size=self.block_size)
-        y, _ = self.mamba.ssm_forward(xn)
+        st = None
+        if return_ssm_states:
+            W, b = _cat_weights(self.mamba)
+            m = self.mamba
+            y, st = ops.ssm_fwd_states(xn, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
+        else:
+            y, _ = self.mamba.ssm_forward(xn)
         # x1 = y + x and norm2(x1) in one pass (same bits as the separate add and norm)
         x1, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)
         f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                             block_size=self.block_size, activation=self.ffn_activation)
-        return f.reshape(B, L, D) + x1
+        out = f.reshape(B, L, D) + x1
+        return (out, st) if return_ssm_states else out
 
     @torch.no_grad()
-    def pgf_backward(self, x: torch.Tensor, g_out: torch.Tensor, fp32_accum: bool = True) -> Dict[str, Any]:
-        """pgf_mamba_block.py:128-249."""
+    def pgf_backward(self, x: torch.Tensor, g_out: torch.Tensor, fp32_accum: bool = True,
+                     ssm_states: Optional[torch.Tensor] = None) -> Dict[str, Any]:
+        """pgf_mamba_block.py:128-249.  ssm_states: the boundary states pgf_forward returned for the
+        same x (the recompute then runs one scan pass instead of rebuilding them, :157-175)."""
         B, L, D = x.shape
         g_out = g_out.to(x.dtype)
         xn1 = self.norm1.pgf_forward(x, block_size=self.block_size)              # :157
         W, b = _cat_weights(self.mamba)
         m = self.mamba
         # :163-178; the states it passes through are kept for the scan backward below
-        y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
+        y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, act=m.output_activation, states=ssm_states)
         m_out, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)  # y + x, :179
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                           block_size=self.block_size, activation=self.ffn_activation,

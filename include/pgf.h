@@ -254,6 +254,20 @@ int pgf_ssm_bwd(const void* u, const void* g, const float* W_cat, const float* b
  * recompute (pgf_mamba_block.py:157-178) feeding its block loop (:211-234) without a second scan.
  * The buffer holds (L/8 + L/Tc) * Bsz * D * N floats: O(L/8) states, not the (L, D, N) trajectory. */
 size_t pgf_ssm_saved_size(int64_t Bsz, int64_t L, int64_t D, int64_t N);
+/* The PGF boundary states alone, handed from the forward pass to the block's backward: fwd_states
+ * is pgf_ssm_fwd that also writes every chunk's start state (and the end state) into `states`
+ * (pgf_ssm_states_size bytes, the boundary states the reference recomputes at
+ * pgf_mamba_block.py:157-175); fwd_save_states, given those states, produces the same y and
+ * saved buffer as pgf_ssm_fwd_save in one pass over the sequence (no zero-start pass, compose or
+ * correction). */
+size_t pgf_ssm_states_size(int64_t Bsz, int64_t L, int64_t D, int64_t N);
+int pgf_ssm_fwd_states(const void* u, const float* W_cat, const float* b_cat, const float* A_log, const float* Dp,
+                       const float* scale, const float* h_init, void* y, float* states, int64_t Bsz, int64_t L,
+                       int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_ssm_fwd_save_states(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                            const float* Dp, const float* scale, const float* states, void* y, float* saved,
+                            int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                            size_t ws_bytes, pgf_stream_t stream);
 int pgf_ssm_fwd_save(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
                      const float* Dp, const float* scale, const float* h_init, void* y, float* saved,
                      int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,

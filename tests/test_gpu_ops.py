@@ -397,3 +397,30 @@ def test_rmsnorm_fused_residual_forms_equal_separate_ops(ops, dtype, rows, dim):
     gw_ref, gx_ref = ops.rmsnorm_bwd(s_ref, gy, w, 1e-6)
     assert torch.equal(gw, gw_ref)
     assert torch.equal(gx, gx_ref + ga)
+
+
+@pytest.mark.parametrize("act", [None, "tanh"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_ssm_save_from_boundary_states(ops, act, dtype):
+    """ssm_fwd_states' boundary states let ssm_fwd_save run one pass; the output and the backward
+    over its saved buffer match the ordinary save (fp32 tolerance; the states are the same)."""
+    g = _gen(91)
+    Bsz, L, D = 2, 1000, 64
+    p = O.ssm_init(D, 16, g)
+    u = torch.randn(Bsz, L, D, generator=g).to(DEV, dtype)
+    gy = torch.randn(Bsz, L, D, generator=g).to(DEV, dtype)
+    W = torch.cat([p["dt_w"], p["B_w"], p["C_w"]]).to(DEV)
+    b = torch.cat([p["dt_b"], p["B_b"], p["C_b"]]).to(DEV)
+    A, Dp, sc = p["A_log"].to(DEV), p["D"].to(DEV), p["scale"].to(DEV)
+    y1, st = ops.ssm_fwd_states(u, W, b, A, Dp, sc, act=act)
+    y0, _ = ops.ssm_fwd(u, W, b, A, Dp, sc, act=act)
+    assert torch.equal(y1, y0)                       # same forward, states written alongside
+    ya, sa = ops.ssm_fwd_save(u, W, b, A, Dp, sc, act=act)
+    yb, sb = ops.ssm_fwd_save(u, W, b, A, Dp, sc, act=act, states=st)
+    tol = dict(atol=1e-5, rtol=1e-4) if dtype == torch.float32 else dict(atol=2e-2, rtol=1e-2)
+    assert_close(yb.float(), ya.float(), **tol, name="y")
+    ra = ops.ssm_bwd(u, gy, W, b, A, Dp, sc, act=act, saved=sa)
+    rb = ops.ssm_bwd(u, gy, W, b, A, Dp, sc, act=act, saved=sb)
+    for k in ("grad_u", "A_log", "D", "scale", "W_cat", "b_cat"):
+        ref = ra[k].float()
+        assert (rb[k].float() - ref).abs().max().item() <= 1e-5 + 1e-4 * ref.abs().max().item(), k
