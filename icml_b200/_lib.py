@@ -95,6 +95,9 @@ SIGNATURES = {
     "pgf_grad_norm_workspace": (c_size_t, [I64]),
     "pgf_rmsnorm_jvp": (c_int, [P, P, P, P, P, P, I64, I64, c_float, c_int, P]),
     "pgf_ssm_states_size": (c_size_t, [I64] * 4),
+    "pgf_mamba_mixer_states_size": (c_size_t, [I64] * 7),
+    "pgf_mamba_mixer_fwd_states": (c_int, [P] * 12 + [I64] * 7 + [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_fwd_save_states": (c_int, [P] * 13 + [c_size_t] + [I64] * 7 + [c_int, P, c_size_t, P]),
     "pgf_ssm_fwd_states": (c_int, [P] * 9 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
     "pgf_ssm_fwd_save_states": (c_int, [P] * 9 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
     "pgf_ffn_jvp_workspace": (c_size_t, [I64, I64, I64, I64, c_int]),

@@ -827,7 +827,7 @@ static Args args_of(const Params& P, const Plan& p, const Bufs& B, int dtype, bo
 // forward up to the gated scan output y (B.y); optionally saves the 8-token scan checkpoints for
 // the backward.  The weights must already be converted (convert_weights).
 static int forward_to_y(const void* x, const Params& P, const Plan& p, Bufs& B, int dtype, bool save,
-                        Args& a, cudaStream_t s) {
+                        Args& a, cudaStream_t s, const float* states_in = nullptr, float* states_out = nullptr) {
   const int64_t T = p.T, E = p.E;
   const void* in_w = dtype ? static_cast<const void*>(B.in_wb) : static_cast<const void*>(P.in_w);
   // xz = x W_in^T
@@ -853,13 +853,20 @@ static int forward_to_y(const void* x, const Params& P, const Plan& p, Bufs& B, 
   }
   a = args_of(P, p, B, dtype, save);
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
-  prof_begin(PROF_SSM_CHUNK_FWD, s);
-  chunk_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
-  prof_end(PROF_SSM_CHUNK_FWD, s, double(T) * (dtype ? 2 : 4) * (2.0 * E + NST));
-  PGF_LAUNCH_CHECK();
-  const int64_t nth = p.Bsz * E * NST;
-  compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
-  PGF_LAUNCH_CHECK();
+  const size_t hc_bytes = size_t(p.Bsz) * (p.nC + 1) * E * NST * sizeof(float);
+  if (states_in) {
+    // the boundary states of an earlier forward on the same input: no chunk pass or compose
+    PGF_CUDA(cudaMemcpyAsync(B.hC, states_in, hc_bytes, cudaMemcpyDeviceToDevice, s));
+  } else {
+    prof_begin(PROF_SSM_CHUNK_FWD, s);
+    chunk_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
+    prof_end(PROF_SSM_CHUNK_FWD, s, double(T) * (dtype ? 2 : 4) * (2.0 * E + NST));
+    PGF_LAUNCH_CHECK();
+    const int64_t nth = p.Bsz * E * NST;
+    compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
+    PGF_LAUNCH_CHECK();
+    if (states_out) PGF_CUDA(cudaMemcpyAsync(states_out, B.hC, hc_bytes, cudaMemcpyDeviceToDevice, s));
+  }
   prof_begin(PROF_SSM_OUT_FWD, s);
   out_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
   prof_end(PROF_SSM_OUT_FWD, s, double(T) * (dtype ? 2 : 4) * (4.0 * E + 2 * NST));
@@ -885,7 +892,8 @@ namespace mstd {
 
 static int mixer_fwd_impl(const void* x, const Params& P, void* out, void* saved, size_t saved_bytes, int64_t Bsz,
                           int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws,
-                          size_t ws_bytes, cudaStream_t s) {
+                          size_t ws_bytes, cudaStream_t s, const float* states_in = nullptr,
+                          float* states_out = nullptr) {
   PGF_TRY(check_dims(Bsz, L, d, E, R, N, K, dtype));
   PGF_CHECK_ARG(x && P.in_w && P.conv_w && P.conv_b && P.x_w && P.dt_w && P.dt_b && P.A_log && P.Dp && P.out_w && out,
                 "mamba_mixer_fwd: null pointer");
@@ -896,7 +904,7 @@ static int mixer_fwd_impl(const void* x, const Params& P, void* out, void* saved
   PGF_TRY(carve(W, saved ? &Ws : nullptr, B, p, dtype, 0));
   PGF_TRY(convert_weights(P, p, B, dtype, s));
   Args a;
-  PGF_TRY(forward_to_y(x, P, p, B, dtype, saved != nullptr, a, s));
+  PGF_TRY(forward_to_y(x, P, p, B, dtype, saved != nullptr, a, s, states_in, states_out));
   const void* ow = dtype ? static_cast<const void*>(B.out_wb) : static_cast<const void*>(P.out_w);
   return run_gemm(G_(p.T, d, E, B.y, dtype, E, 0, ow, dtype, E, 0, out, dtype, d), s);
 }
@@ -935,6 +943,36 @@ extern "C" int pgf_mamba_mixer_fwd_save(const void* x, const float* in_w, const 
   mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
   return mstd::mixer_fwd_impl(x, P, out, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
                               as_stream(stream));
+}
+
+extern "C" size_t pgf_mamba_mixer_states_size(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                                              int64_t K) {
+  mstd::Plan p = mstd::plan_of(Bsz < 1 ? 1 : Bsz, L < 1 ? 1 : L, d, E, R, N, K);
+  return size_t(p.Bsz) * (p.nC + 1) * p.E * mstd::NST * sizeof(float);
+}
+
+extern "C" int pgf_mamba_mixer_fwd_states(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                                          const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                                          const float* Dp, const float* out_w, void* out, float* states, int64_t Bsz,
+                                          int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype,
+                                          void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(states, "mamba_mixer_fwd_states: null state buffer");
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  return mstd::mixer_fwd_impl(x, P, out, nullptr, 0, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes, as_stream(stream),
+                              nullptr, states);
+}
+
+extern "C" int pgf_mamba_mixer_fwd_save_states(const void* x, const float* in_w, const float* conv_w,
+                                               const float* conv_b, const float* x_w, const float* dt_w,
+                                               const float* dt_b, const float* A_log, const float* Dp,
+                                               const float* out_w, const float* states, void* out, void* saved,
+                                               size_t saved_bytes, int64_t Bsz, int64_t L, int64_t d, int64_t E,
+                                               int64_t R, int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes,
+                                               pgf_stream_t stream) {
+  PGF_CHECK_ARG(saved && states, "mamba_mixer_fwd_save_states: null pointer");
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  return mstd::mixer_fwd_impl(x, P, out, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream), states, nullptr);
 }
 
 namespace pgf {

@@ -161,14 +161,11 @@ class PGFLanguageModel:
         x = ops.embedding_fwd(input_ids, self.emb_weight, dtype=self.act_dtype)
         stash = self.stash
         stash.begin(self.n_layers)
-        # the reference-variant blocks hand their scan boundary states to their backward
+        # every block hands its scan's boundary states to its backward (PGF keeps them per block)
         ssm_states: List[Optional[torch.Tensor]] = [None] * self.n_layers
         for i, layer in enumerate(self.backbone.layers):
             stash.put(i, x)
-            if self.variant == "reference":
-                x, ssm_states[i] = layer.pgf_forward(x, return_ssm_states=True)
-            else:
-                x = layer.pgf_forward(x)
+            x, ssm_states[i] = layer.pgf_forward(x, return_ssm_states=True)
         xf = ops.rmsnorm_fwd(x, self.final_norm.weight, self.final_norm.eps) if self.final_norm is not None else x
         h = xf.reshape(-1, d)
         tg = targets.reshape(-1)
@@ -185,11 +182,8 @@ class PGFLanguageModel:
             xi = stash.take(i, g.device)
             if i > 0:
                 stash.prefetch(i - 1, g.device)  # overlaps this layer's backward
-            if self.variant == "reference":
-                res = self.backbone.layers[i].pgf_backward(xi, g, ssm_states=ssm_states[i])
-                ssm_states[i] = None
-            else:
-                res = self.backbone.layers[i].pgf_backward(xi, g)
+            res = self.backbone.layers[i].pgf_backward(xi, g, ssm_states=ssm_states[i])
+            ssm_states[i] = None
             del xi
             for k, v in res["grads"].items():
                 grads[f"layers.{i}.{k}"] = v

@@ -558,8 +558,9 @@ def _mixer_dims(x, p):
     return Bsz, L_, d, E, R, N, K
 
 
-def mamba_mixer_fwd(x, p):
-    """Standard Mamba mixer forward; p: dict of MIXER_KEYS float32 tensors."""
+def mamba_mixer_fwd(x, p, want_states: bool = False):
+    """Standard Mamba mixer forward; p: dict of MIXER_KEYS float32 tensors.  want_states: also the
+    scan's boundary states, for mamba_mixer_fwd_save(states=...)."""
     _cuda(x, p["in_w"])
     x = _c(x)
     Bsz, L_, d, E, R, N, K = _mixer_dims(x, p)
@@ -567,13 +568,20 @@ def mamba_mixer_fwd(x, p):
     out = torch.empty_like(x)
     Lb = lib()
     ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 0), x.device)
+    if want_states:
+        st = torch.empty(Lb.pgf_mamba_mixer_states_size(Bsz, L_, d, E, R, N, K) // 4, device=x.device)
+        check(Lb.pgf_mamba_mixer_fwd_states(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(out), _p(st), Bsz, L_, d, E,
+                                            R, N, K, _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_fwd_states")
+        return out, st
     check(Lb.pgf_mamba_mixer_fwd(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(out), Bsz, L_, d, E, R, N, K,
                                  _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_fwd")
     return out
 
 
-def mamba_mixer_fwd_save(x, p):
-    """Mixer forward that keeps its intermediates: (out, saved) for mamba_mixer_bwd(saved=...)."""
+def mamba_mixer_fwd_save(x, p, states: Optional[torch.Tensor] = None):
+    """Mixer forward that keeps its intermediates: (out, saved) for mamba_mixer_bwd(saved=...).
+    With `states` (from mamba_mixer_fwd(want_states=True) on the same x) the scan's boundary states
+    are not rebuilt."""
     _cuda(x, p["in_w"])
     x = _c(x)
     Bsz, L_, d, E, R, N, K = _mixer_dims(x, p)
@@ -582,6 +590,11 @@ def mamba_mixer_fwd_save(x, p):
     Lb = lib()
     saved = _ws(Lb.pgf_mamba_mixer_saved_size(Bsz, L_, d, E, R, N, K, _dt(x)), x.device)
     ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 0), x.device)
+    if states is not None:
+        check(Lb.pgf_mamba_mixer_fwd_save_states(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(states), _p(out),
+                                                 _p(saved), saved.numel(), Bsz, L_, d, E, R, N, K, _dt(x), _p(ws),
+                                                 ws.numel(), _stream()), "mamba_mixer_fwd_save_states")
+        return out, saved
     check(Lb.pgf_mamba_mixer_fwd_save(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(out), _p(saved), saved.numel(),
                                       Bsz, L_, d, E, R, N, K, _dt(x), _p(ws), ws.numel(), _stream()),
           "mamba_mixer_fwd_save")

@@ -104,22 +104,28 @@ class PGFMambaStdBlock(nn.Module):
         return f.reshape(B, L, D) + x1
 
     @torch.no_grad()
-    def pgf_forward(self, x: torch.Tensor) -> torch.Tensor:
+    def pgf_forward(self, x: torch.Tensor, return_ssm_states: bool = False):
         B, L, D = x.shape
+        st = None
+        if return_ssm_states:
+            m, st = ops.mamba_mixer_fwd(self.norm1.pgf_forward(x), self.mixer.params(), want_states=True)
+        else:
+            m = ops.mamba_mixer_fwd(self.norm1.pgf_forward(x), self.mixer.params())
         # x1 = mixer + x and norm2(x1) in one pass (same bits as the separate add and norm)
-        x1, xn2 = ops.rmsnorm_fwd_res(ops.mamba_mixer_fwd(self.norm1.pgf_forward(x), self.mixer.params()), x,
-                                      self.norm2.weight, self.norm2.eps)
+        x1, xn2 = ops.rmsnorm_fwd_res(m, x, self.norm2.weight, self.norm2.eps)
         f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                             activation=self.ffn_activation)
-        return f.reshape(B, L, D) + x1
+        out = f.reshape(B, L, D) + x1
+        return (out, st) if return_ssm_states else out
 
     @torch.no_grad()
-    def pgf_backward(self, x: torch.Tensor, g_out: torch.Tensor, fp32_accum: bool = True) -> Dict[str, Any]:
+    def pgf_backward(self, x: torch.Tensor, g_out: torch.Tensor, fp32_accum: bool = True,
+                     ssm_states: Optional[torch.Tensor] = None) -> Dict[str, Any]:
         B, L, D = x.shape
         g_out = g_out.to(x.dtype)
         p = self.mixer.params()
         xn1 = self.norm1.pgf_forward(x)
-        m_raw, saved = ops.mamba_mixer_fwd_save(xn1, p)
+        m_raw, saved = ops.mamba_mixer_fwd_save(xn1, p, states=ssm_states)
         m_out, xn2 = ops.rmsnorm_fwd_res(m_raw, x, self.norm2.weight, self.norm2.eps)
         del m_raw
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,

@@ -362,6 +362,21 @@ int pgf_mamba_mixer_bwd(const void* x, const void* g_out, const float* in_w, con
    Same inputs and weights in both calls; `saved` is not modified by bwd_saved. */
 size_t pgf_mamba_mixer_saved_size(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
                                   int64_t K, int dtype);
+/* The scan's boundary states handed from the block forward to its backward (as
+ * pgf_ssm_fwd_states / pgf_ssm_fwd_save_states): fwd_states is pgf_mamba_mixer_fwd that also writes
+ * them (pgf_mamba_mixer_states_size bytes); fwd_save_states is pgf_mamba_mixer_fwd_save given them,
+ * without the scan's chunk pass and compose. */
+size_t pgf_mamba_mixer_states_size(int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K);
+int pgf_mamba_mixer_fwd_states(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                               const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                               const float* Dp, const float* out_w, void* out, float* states, int64_t Bsz, int64_t L,
+                               int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws,
+                               size_t ws_bytes, pgf_stream_t stream);
+int pgf_mamba_mixer_fwd_save_states(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                                    const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                                    const float* Dp, const float* out_w, const float* states, void* out, void* saved,
+                                    size_t saved_bytes, int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R,
+                                    int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
 int pgf_mamba_mixer_fwd_save(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
                              const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
                              const float* Dp, const float* out_w, void* out, void* saved, size_t saved_bytes,

@@ -134,3 +134,25 @@ def test_mixer_saved_forward_equals_recompute(dtype):
     assert torch.equal(gx1, gx2)
     for k in ops.MIXER_KEYS:
         assert torch.equal(g1[k], g2[k]), k
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mixer_save_from_boundary_states_is_bitwise(dtype):
+    """fwd_save given the boundary states of fwd(want_states=True) skips the scan's chunk pass and
+    compose; the output and the backward over its saved buffer are the same bits (the buffer's
+    forward-only chunk summaries are left unwritten)."""
+    from icml_b200 import ops
+    g = torch.Generator().manual_seed(81)
+    p = {k: v.float().to(DEV) for k, v in MS.std_init(64, 16, 2, 4, 4, g).items()}
+    x = torch.randn(2, 700, 64, generator=g).to(DEV, dtype)
+    gy = torch.randn(2, 700, 64, generator=g).to(DEV, dtype)
+    out0, st = ops.mamba_mixer_fwd(x, p, want_states=True)
+    assert torch.equal(out0, ops.mamba_mixer_fwd(x, p))
+    o1, s1 = ops.mamba_mixer_fwd_save(x, p)
+    o2, s2 = ops.mamba_mixer_fwd_save(x, p, states=st)
+    assert torch.equal(o1, o2)
+    g1, gx1 = ops.mamba_mixer_bwd(x, gy, p, saved=s1)
+    g2, gx2 = ops.mamba_mixer_bwd(x, gy, p, saved=s2)
+    assert torch.equal(gx1, gx2)
+    for k in ops.MIXER_KEYS:
+        assert torch.equal(g1[k], g2[k]), k
