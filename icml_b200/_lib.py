@@ -77,6 +77,7 @@ SIGNATURES = {
                                   I64, I64, c_int, c_int, P, c_size_t, P]),
     "pgf_ssm_fwd_begin": (c_int, [P] * 6 + [I64] * 4 + [c_int, P, c_size_t, P]),
     "pgf_ssm_fwd_finish": (c_int, [P] * 9 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
+    "pgf_ssm_fwd_finish_states": (c_int, [P] * 9 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
     "pgf_ssm_bwd_begin": (c_int, [P] * 11 + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
     "pgf_ssm_bwd_finish": (c_int, [P] * 19 + [c_int] + [I64] * 4 + [c_int, c_int, P, c_size_t, P]),
     "pgf_mamba_mixer_workspace": (c_size_t, [I64, I64, I64, I64, I64, I64, I64, c_int, c_int]),

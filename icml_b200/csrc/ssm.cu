@@ -985,7 +985,9 @@ static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, c
   a.A_log = A_log; a.Dp = Dp; a.scale = scale; a.act = act;
   a.h_init = stage == STAGE_BEGIN ? nullptr : h_init;
   const void* wop;
-  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s, saved ? saved : states_out, stage != STAGE_FINISH));
+  // (a staged call keeps the start states in the workspace, whose layout BEGIN and FINISH share)
+  PGF_TRY(ssm_common(a, p, W, u, dtype, W_cat, b_cat, &wop, s,
+                     saved ? saved : (stage == STAGE_ALL ? states_out : nullptr), stage != STAGE_FINISH));
   a.y0 = W.take<float>(size_t(Bsz) * L * D);
   if (!a.y0) { set_error("ssm_fwd: workspace too small (%zu)", ws_bytes); return PGF_ERR_WORKSPACE; }
   a.y = y;
@@ -1010,6 +1012,8 @@ static int ssm_fwd_impl(const void* u, const float* W_cat, const float* b_cat, c
   prof_end(PROF_SSM_COMPOSE, s, bytes_compose(a));
   PGF_LAUNCH_CHECK();
   if (stage == STAGE_BEGIN) return PGF_OK;
+  if (states_out && states_out != a.hC)
+    PGF_CUDA(cudaMemcpyAsync(states_out, a.hC, saved_hc_floats(p) * sizeof(float), cudaMemcpyDeviceToDevice, s));
   prof_begin(PROF_SSM_OUT_FWD, s);
   ssm_out_corr_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
   prof_end(PROF_SSM_OUT_FWD, s, bytes_out_fwd(a, a.u_bf16 ? 2 : 4) + double(Bsz) * L * D * 4.0);
@@ -1256,6 +1260,16 @@ extern "C" int pgf_ssm_fwd_finish(const void* u, const float* W_cat, const float
                                   void* ws, size_t ws_bytes, pgf_stream_t stream) {
   return ssm_fwd_impl(u, W_cat, b_cat, A_log, Dp, scale, h_init, y, h_final, Bsz, L, D, N, act, dtype, ws,
                       ws_bytes, stream, nullptr, STAGE_FINISH);
+}
+
+extern "C" int pgf_ssm_fwd_finish_states(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                                         const float* Dp, const float* scale, const float* h_init, void* y,
+                                         float* states, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act,
+                                         int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(states, "ssm_fwd_finish_states: null state buffer");
+  PGF_CHECK_ARG(L > 0, "ssm_fwd_finish_states: empty sequence");
+  return ssm_fwd_impl(u, W_cat, b_cat, A_log, Dp, scale, h_init, y, nullptr, Bsz, L, D, N, act, dtype, ws,
+                      ws_bytes, stream, nullptr, STAGE_FINISH, nullptr, states);
 }
 
 extern "C" int pgf_ssm_bwd_begin(const void* u, const void* g, const float* W_cat, const float* b_cat,

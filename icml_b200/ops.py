@@ -489,17 +489,23 @@ def ssm_fwd_begin(u, W_cat, b_cat, A_log):
     return hseg, sdt, {"u": u, "W_cat": W_cat, "b_cat": b_cat, "A_log": A_log, "ws": ws}
 
 
-def ssm_fwd_finish(state, Dp, scale, h_init=None, act=None):
-    """Sequence sharding, forward part 2: y from the state entering the segment."""
+def ssm_fwd_finish(state, Dp, scale, h_init=None, act=None, want_states=False):
+    """Sequence sharding, forward part 2: y from the state entering the segment.  With want_states,
+    (y, states): the segment's boundary states for ssm_fwd_save(states=...) in the backward."""
     u = state["u"]
     Bsz, L_, D = u.shape
     N = state["A_log"].shape[0]
     y = torch.empty_like(u)
     Dp, scale, h_init = (_f32(t) for t in (Dp, scale, h_init))
     ws = state["ws"]
-    check(lib().pgf_ssm_fwd_finish(_p(u), _p(state["W_cat"]), _p(state["b_cat"]), _p(state["A_log"]), _p(Dp),
-                                   _p(scale), _p(h_init), _p(y), None, Bsz, L_, D, N, ACT[act], _dt(u), _p(ws),
-                                   ws.numel(), _stream()), "ssm_fwd_finish")
+    Lb = lib()
+    args = (_p(u), _p(state["W_cat"]), _p(state["b_cat"]), _p(state["A_log"]), _p(Dp), _p(scale), _p(h_init), _p(y))
+    tail = (Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(), _stream())
+    if want_states:
+        states = torch.empty(Lb.pgf_ssm_states_size(Bsz, L_, D, N) // 4, dtype=torch.float32, device=u.device)
+        check(Lb.pgf_ssm_fwd_finish_states(*args, _p(states), *tail), "ssm_fwd_finish_states")
+        return y, states
+    check(Lb.pgf_ssm_fwd_finish(*args, None, *tail), "ssm_fwd_finish")
     return y
 
 

@@ -84,7 +84,8 @@ def _wb(m):
 
 @torch.no_grad()
 def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
-    """PGFMambaBlock.pgf_forward on this rank's segment; returns (y, state entering the segment)."""
+    """PGFMambaBlock.pgf_forward on this rank's segment; returns (y, state entering the segment,
+    the scan's boundary states for block_backward)."""
     B, L, D = x.shape
     m = block.mamba
     W, b = _wb(m)
@@ -94,27 +95,31 @@ def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
         # the zero-start pass gives the segment summary; the output pass continues from it
         h_loc, sdt, st = ops.ssm_fwd_begin(xn, W, b, m.A_log)
         h_in = compose_forward_state(sp.all_gather(h_loc), sp.all_gather(sdt), A, sp.rank)
-        y = ops.ssm_fwd_finish(st, m.D, m.scale, h_init=h_in, act=m.output_activation)
+        y, states = ops.ssm_fwd_finish(st, m.D, m.scale, h_init=h_in, act=m.output_activation, want_states=True)
         del st
     else:
         h_in = None
-        y, _ = ops.ssm_fwd(xn, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
+        y, states = ops.ssm_fwd_states(xn, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
     x1, xn2 = ops.rmsnorm_fwd_res(y, x, block.norm2.weight, block.norm2.eps)  # y + x, then norm2
     f = ops.ffn_fwd(xn2.reshape(-1, D), block.W1, block.b1, block.W2, block.b2, block.ffn_activation)
-    return f.reshape(B, L, D) + x1, h_in
+    return f.reshape(B, L, D) + x1, h_in, states
 
 
 @torch.no_grad()
 def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[torch.Tensor], sp: SeqGroup,
-                   ops=cuda_ops) -> Dict[str, Any]:
-    """PGFMambaBlock.pgf_backward on this rank's segment (local partial parameter gradients)."""
+                   ops=cuda_ops, states=None) -> Dict[str, Any]:
+    """PGFMambaBlock.pgf_backward on this rank's segment (local partial parameter gradients).  With
+    `states` from block_forward on the same input, the scan's forward is one pass."""
     B, L, D = x.shape
     m = block.mamba
     W, b = _wb(m)
     A = -torch.exp(m.A_log.detach().float())
     g_out = g_out.to(x.dtype)
     xn1 = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
-    y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
+    if states is not None:
+        y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, act=m.output_activation, states=states)
+    else:
+        y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, h_init=h_in, act=m.output_activation)
     m_out, xn2 = ops.rmsnorm_fwd_res(y, x, block.norm2.weight, block.norm2.eps)
     fr = ops.ffn_bwd(xn2.reshape(-1, D), g_out.reshape(-1, D), block.W1, block.b1, block.W2,
                      block.ffn_activation, need_gx=True)
@@ -154,10 +159,10 @@ def lm_forward_backward(model, input_ids: torch.Tensor, targets: torch.Tensor, s
     d = model.d_model
     T_total = total_tokens if total_tokens is not None else B * L * sp.world
     x = ops.embedding_fwd(input_ids, model.emb_weight, dtype=model.act_dtype)
-    stash: List[Tuple[torch.Tensor, Optional[torch.Tensor]]] = []
+    stash: List[Tuple[torch.Tensor, Optional[torch.Tensor], Any]] = []
     for layer in model.backbone.layers:
-        y, h_in = block_forward(layer, x, sp, ops)
-        stash.append((x, h_in))
+        y, h_in, states = block_forward(layer, x, sp, ops)
+        stash.append((x, h_in, states))
         x = y
     h = x.reshape(-1, d)
     tg = targets.reshape(-1)
@@ -166,8 +171,8 @@ def lm_forward_backward(model, input_ids: torch.Tensor, targets: torch.Tensor, s
     grads = {"lm_head": gW}
     g = gh.reshape(B, L, d)
     for i in reversed(range(model.n_layers)):
-        xi, h_in = stash.pop()
-        res = block_backward(model.backbone.layers[i], xi, g, h_in, sp, ops)
+        xi, h_in, states = stash.pop()
+        res = block_backward(model.backbone.layers[i], xi, g, h_in, sp, ops, states=states)
         for k, v in res["grads"].items():
             grads[f"layers.{i}.{k}"] = v
         g = res["grad_input"]

@@ -317,6 +317,13 @@ int pgf_ssm_fwd_begin(const void* u, const float* W_cat, const float* b_cat, con
 int pgf_ssm_fwd_finish(const void* u, const float* W_cat, const float* b_cat, const float* A_log, const float* Dp,
                        const float* scale, const float* h_init, void* y, float* h_final, int64_t Bsz, int64_t L,
                        int64_t D, int64_t N, int act, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+/* pgf_ssm_fwd_finish that also writes the segment's boundary states (pgf_ssm_states_size bytes, the
+ * state entering the segment folded in) for pgf_ssm_fwd_save_states: a sequence-sharded backward
+ * (pgf_mamba_block.py:157-175 per segment) then skips the zero-start pass and compose. */
+int pgf_ssm_fwd_finish_states(const void* u, const float* W_cat, const float* b_cat, const float* A_log,
+                              const float* Dp, const float* scale, const float* h_init, void* y, float* states,
+                              int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
+                              size_t ws_bytes, pgf_stream_t stream);
 int pgf_ssm_bwd_begin(const void* u, const void* g, const float* W_cat, const float* b_cat, const float* A_log,
                       const float* scale, const float* h_init, const float* saved, float* dh_start,
                       float* dA_start, float* sum_dt_excl, int64_t Bsz, int64_t L, int64_t D, int64_t N, int act,

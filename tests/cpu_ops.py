@@ -52,7 +52,16 @@ def ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, want_h_fin
     return y, (h if want_h_final else None)
 
 
-def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None):
+def ssm_fwd_states(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None):
+    """The boundary-state buffer's stand-in is the state that entered the segment."""
+    y, _ = ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=h_init, act=act)
+    return y, {"h_init": h_init}
+
+
+def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, states=None):
+    if states is not None:
+        assert h_init is None
+        h_init = states["h_init"]
     y, _ = ssm_fwd(u, W_cat, b_cat, A_log, Dp, scale, h_init=h_init, act=act)
     return y, None
 
@@ -72,9 +81,9 @@ def ssm_fwd_begin(u, W_cat, b_cat, A_log):
     return h, sdt, {"u": u, "W_cat": W_cat, "b_cat": b_cat, "A_log": A_log}
 
 
-def ssm_fwd_finish(state, Dp, scale, h_init=None, act=None):
+def ssm_fwd_finish(state, Dp, scale, h_init=None, act=None, want_states=False):
     y, _ = ssm_fwd(state["u"], state["W_cat"], state["b_cat"], state["A_log"], Dp, scale, h_init=h_init, act=act)
-    return y
+    return (y, {"h_init": h_init}) if want_states else y
 
 
 def ssm_bwd_begin(u, g, W_cat, b_cat, A_log, scale, saved, h_init=None, act=None):

@@ -424,3 +424,38 @@ def test_ssm_save_from_boundary_states(ops, act, dtype):
     for k in ("grad_u", "A_log", "D", "scale", "W_cat", "b_cat"):
         ref = ra[k].float()
         assert (rb[k].float() - ref).abs().max().item() <= 1e-5 + 1e-4 * ref.abs().max().item(), k
+
+
+@pytest.mark.parametrize("act", [None, "relu"])
+def test_ssm_staged_finish_states(ops, act):
+    """Sequence-sharded form: ssm_fwd_finish's boundary states (the entering state folded in) let the
+    segment's backward save in one pass; its staged backward matches the one after an ordinary save."""
+    g = _gen(93)
+    Bsz, L, D = 2, 1500, 64
+    p = O.ssm_init(D, 16, g)
+    u = torch.randn(Bsz, L, D, generator=g).to(DEV)
+    gy = torch.randn(Bsz, L, D, generator=g).to(DEV)
+    h0 = (0.3 * torch.randn(Bsz, D, 16, generator=g)).to(DEV)
+    W = torch.cat([p["dt_w"], p["B_w"], p["C_w"]]).to(DEV)
+    b = torch.cat([p["dt_b"], p["B_b"], p["C_b"]]).to(DEV)
+    A, Dp, sc = p["A_log"].to(DEV), p["D"].to(DEV), p["scale"].to(DEV)
+    _, _, st = ops.ssm_fwd_begin(u, W, b, A)
+    y1, states = ops.ssm_fwd_finish(st, Dp, sc, h_init=h0, act=act, want_states=True)
+    y0, _ = ops.ssm_fwd(u, W, b, A, Dp, sc, h_init=h0, act=act)
+    assert torch.equal(y1, y0)
+    ya, sa = ops.ssm_fwd_save(u, W, b, A, Dp, sc, h_init=h0, act=act)
+    yb, sb = ops.ssm_fwd_save(u, W, b, A, Dp, sc, act=act, states=states)
+    assert_close(yb, ya, atol=1e-5, rtol=1e-4, name="y")
+    dh_end = (0.1 * torch.randn(Bsz, D, 16, generator=g)).to(DEV)
+    dA_end = (0.5 + torch.rand(Bsz, D, 16, generator=g)).to(DEV)
+    out = []
+    for saved in (sa, sb):
+        dh0, dA0, sdx, bs = ops.ssm_bwd_begin(u, gy, W, b, A, sc, saved, h_init=h0, act=act)
+        r = ops.ssm_bwd_finish(bs, Dp, dh_end=dh_end, dA_end=dA_end)
+        out.append((dh0, dA0, sdx, r))
+    (da, aa, xa, ra), (db, ab, xb, rb) = out
+    for name, x_, y_ in (("dh0", db, da), ("dA0", ab, aa), ("sdx", xb, xa)):
+        assert_close(x_, y_, atol=1e-5, rtol=1e-4, name=name)
+    for k in ("grad_u", "A_log", "D", "scale", "W_cat", "b_cat"):
+        ref = ra[k].float()
+        assert (rb[k].float() - ref).abs().max().item() <= 1e-5 + 1e-4 * ref.abs().max().item(), k
