@@ -12,11 +12,14 @@
 namespace pgf {
 
 static const int64_t kTileBytes = int64_t(128) << 20;  // scratch budget for one row tile
+// The FFN's budget is larger: each row tile of the backward pays a split-K reduction and two column
+// sums of its own, so a 65536-token sequence at d_hidden 1024 in bf16 runs as one tile.
+static const int64_t kFfnTileBytes = int64_t(256) << 20;
 
-static int64_t ffn_tile_rows(int64_t rows, int64_t d_hidden, int backward) {
-  // hidden activations (and the pre-activation in backward) of one tile, budgeted as float32
-  int64_t per_row = d_hidden * 4 * (backward ? 2 : 1);
-  int64_t t = kTileBytes / (per_row > 0 ? per_row : 1);
+static int64_t ffn_tile_rows(int64_t rows, int64_t d_hidden, int backward, int dtype) {
+  // hidden activations (and the pre-activation in backward) of one tile, in the activation dtype
+  int64_t per_row = d_hidden * (dtype ? 2 : 4) * (backward ? 2 : 1);
+  int64_t t = kFfnTileBytes / (per_row > 0 ? per_row : 1);
   t = (t / 128) * 128;
   if (t < 128) t = 128;
   return rows < t ? rows : t;
@@ -38,10 +41,10 @@ static size_t ffn_split_bytes(int64_t tr, int64_t d_in, int64_t d_h, int64_t d_o
 }
 
 static size_t ffn_ws_bytes(int64_t rows, int64_t d_in, int64_t d_h, int64_t d_out, int dtype, int backward) {
-  int64_t tr = ffn_tile_rows(rows < 1 ? 1 : rows, d_h, backward);
+  int64_t tr = ffn_tile_rows(rows < 1 ? 1 : rows, d_h, backward, dtype);
   size_t es = dtype ? 2 : 4;
   size_t b = Workspace::round(size_t(tr) * d_h * es);
-  if (backward) b += Workspace::round(size_t(tr) * d_h * 4);
+  if (backward) b += Workspace::round(size_t(tr) * d_h * es);
   if (dtype) b += Workspace::round(size_t(d_h) * d_in * 2) + Workspace::round(size_t(d_out) * d_h * 2);
   if (backward) {
     size_t c1 = colsum_ws(tr, d_h), c2 = colsum_ws(tr, d_out);
@@ -53,7 +56,7 @@ static size_t ffn_ws_bytes(int64_t rows, int64_t d_in, int64_t d_h, int64_t d_ou
 
 static int ffn_carve(Workspace& W, FfnWs& f, int64_t rows, int64_t d_in, int64_t d_h, int64_t d_out,
                      int dtype, int backward) {
-  int64_t tr = ffn_tile_rows(rows, d_h, backward);
+  int64_t tr = ffn_tile_rows(rows, d_h, backward, dtype);
   size_t es = dtype ? 2 : 4;
   f.h = W.take<char>(size_t(tr) * d_h * es);
   f.z = backward ? W.take<char>(size_t(tr) * d_h * es) : nullptr;
@@ -117,7 +120,7 @@ extern "C" int pgf_ffn_fwd(const void* x, const float* W1, const float* b1, cons
     w1 = f.W1b;
     w2 = f.W2b;
   }
-  const int64_t tr = ffn_tile_rows(rows, d_hidden, 0);
+  const int64_t tr = ffn_tile_rows(rows, d_hidden, 0, dtype);
   const size_t es = dtype ? 2 : 4;
   for (int64_t r = 0; r < rows; r += tr) {
     const int64_t m = rows - r < tr ? rows - r : tr;
@@ -284,14 +287,14 @@ extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const 
     w2 = f.W2b;
     wbf = 1;
   }
-  const int64_t tr = ffn_tile_rows(rows, d_h, 1);
+  const int64_t tr = ffn_tile_rows(rows, d_h, 1, dtype);
   const size_t es = dtype ? 2 : 4;
   for (int64_t r = 0; r < rows; r += tr) {
     const int64_t m = rows - r < tr ? rows - r : tr;
     const int acc = (r > 0) || accumulate;
     const char* xt = static_cast<const char*>(x) + r * d_in * es;
     const char* gt = static_cast<const char*>(g) + r * d_out * es;
-    // z = x W1^T + b1 (kept in float32 for act'), h = act(z) (activation dtype)
+    // z = x W1^T + b1 and h = act(z), both in the activation dtype
     Gemm g1 = mk(m, d_h, d_in, xt, dtype, d_in, 0, w1, wbf, d_in, 0, f.h, dtype, d_h);
     g1.epi.bias = b1;
     g1.epi.kind = act_epi(activation, 0);
