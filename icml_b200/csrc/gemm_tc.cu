@@ -21,6 +21,7 @@
 // Work unit = (128-row block, group of `ng` consecutive 128-column tiles); CTAs stride over units.
 // Every mbarrier wait is bounded by a clock budget; on expiry the kernel records a fault in
 // g_tc_fault and stops issuing work.
+#include "f32x2.cuh"
 #include "gemm.cuh"
 #include "tc_common.cuh"
 
@@ -57,6 +58,25 @@ enum { TC_GENERIC = 0, TC_CE_FWD = 1, TC_CE_BWD = 2 };
 //   PLAIN: generic, no activation (bias / addend / accumulate);  ACT: GELU or ReLU (+ pre-activation);
 //   DACT: GELU' or ReLU' with the saved pre-activation;  CE_FWD / CE_BWD: the cross-entropy modes.
 enum { EK_PLAIN = 0, EK_ACT = 1, EK_DACT = 2, EK_CE_FWD = 3, EK_CE_BWD = 4 };
+
+// The bf16-output GELU and GELU' (tanh form) on a pair of columns with packed float32 instructions:
+// GELU(x) = hx + hx tanh(u) with hx = x/2, u = C x (1 + A x^2);
+// GELU'(x) = (1 + tanh(u))/2 + hx (1 - tanh(u)^2) (C + 3AC x^2).
+__device__ __forceinline__ float2 gelu2_bf(float2 x) {
+  const float2 q = fma2(mul2(x, x), f2(PGF_GELU_A), f2(1.0f));
+  const float2 u = mul2(mul2(x, f2(PGF_GELU_C)), q);
+  const float2 t = f2(tanh_approx(u.x), tanh_approx(u.y));
+  const float2 hx = mul2(x, f2(0.5f));
+  return fma2(hx, t, hx);
+}
+__device__ __forceinline__ float2 gelu_prime2_bf(float2 x) {
+  const float2 x2 = mul2(x, x);
+  const float2 u = mul2(mul2(x, f2(PGF_GELU_C)), fma2(x2, f2(PGF_GELU_A), f2(1.0f)));
+  const float2 t = f2(tanh_approx(u.x), tanh_approx(u.y));
+  const float2 w = fma2(x2, f2(3.0f * PGF_GELU_A * PGF_GELU_C), f2(PGF_GELU_C));
+  const float2 hs = mul2(mul2(x, f2(0.5f)), fma2(t, f2(-t.x, -t.y), f2(1.0f)));
+  return fma2(hs, w, fma2(t, f2(0.5f), f2(0.5f)));
+}
 
 
 struct TcParams {
@@ -272,10 +292,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                   for (int j = 0; j < 8; ++j) {
                     const float4 b4 = __ldg(bq + j);
-                    v[4 * j] = fmaf(e.alpha, __uint_as_float(r[4 * j]), b4.x);
-                    v[4 * j + 1] = fmaf(e.alpha, __uint_as_float(r[4 * j + 1]), b4.y);
-                    v[4 * j + 2] = fmaf(e.alpha, __uint_as_float(r[4 * j + 2]), b4.z);
-                    v[4 * j + 3] = fmaf(e.alpha, __uint_as_float(r[4 * j + 3]), b4.w);
+                    const float2 lo = fma2(f2(e.alpha), f2(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1])),
+                                           lo2(b4));
+                    const float2 hi = fma2(f2(e.alpha), f2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
+                                           hi2(b4));
+                    v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
                   }
                 } else {
 #pragma unroll
@@ -303,7 +324,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (e.kind == PGF_EPI_GELU) {
                   if (p.d_bf16) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = gelu_bf(v[j]);
+                    for (int j = 0; j < 16; ++j) {
+                      const float2 g = gelu2_bf(f2(v[2 * j], v[2 * j + 1]));
+                      v[2 * j] = g.x; v[2 * j + 1] = g.y;
+                    }
                   } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = gelu_f(v[j]);
@@ -320,7 +344,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                   for (int j = 0; j < 32; ++j) v[j] = a[j] > 0.f ? v[j] : 0.f;
                 } else if (p.d_bf16) {
 #pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] *= gelu_prime_bf(a[j]);
+                  for (int j = 0; j < 16; ++j) {
+                    const float2 g = mul2(f2(v[2 * j], v[2 * j + 1]), gelu_prime2_bf(f2(a[2 * j], a[2 * j + 1])));
+                    v[2 * j] = g.x; v[2 * j + 1] = g.y;
+                  }
                 } else {
 #pragma unroll
                   for (int j = 0; j < 32; ++j) v[j] *= gelu_prime_f(a[j]);
