@@ -58,8 +58,9 @@ def parse():
     ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "jvp", "all"],
                     help="component microbenchmarks instead of the LM step (RMSNorm [8,4096,1024]; FFN "
                          "1024-4096-1024 on 32768 tokens; LM head + CE d=1024, vocab 50257, 32768 tokens)")
-    ap.add_argument("--stash", default="device", choices=["device", "host"],
-                    help="where layer inputs wait for the backward: device memory or pinned host memory")
+    ap.add_argument("--stash", default="device", choices=["device", "host", "scan"],
+                    help="where layer inputs wait for the backward: device memory, pinned host memory, or "
+                         "device memory together with each layer's scan states (no scan recompute)")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of the CUDA-graph captured step (1 GPU)")
     ap.add_argument("--parallel", default="sp", choices=["sp", "dp"],

@@ -64,20 +64,32 @@ class PGFMambaBlock(nn.Module):
         return f.reshape(B, L, D) + res
 
     @torch.no_grad()
-    def pgf_forward(self, x: torch.Tensor, return_ssm_states: bool = False):
+    def pgf_forward(self, x: torch.Tensor, return_ssm_states: bool = False, keep_scan: bool = False):
         """pgf_mamba_block.py:70-126.  With return_ssm_states, also the scan's boundary states (for
-        pgf_backward(..., ssm_states=...), which then need not recompute them)."""
+        pgf_backward(..., ssm_states=...), which then need not recompute them).  With keep_scan as
+        well, what is returned instead is everything the backward's recompute of the scan produces
+        (the scan's saved states and the residual sum y + x), so the backward runs no scan pass before
+        its scan backward.  That holds, per block until its backward, about 8.5 bytes per token and
+        channel of scan states (an 8-token checkpoint of the 16 states) and y + x in the activation
+        dtype."""
         B, L, D = x.shape
         xn = self.norm1.pgf_forward(x, block_size=self.block_size)
         st = None
-        if return_ssm_states:
+        if return_ssm_states and keep_scan:
+            W, b = _cat_weights(self.mamba)
+            m = self.mamba
+            y, saved = ops.ssm_fwd_save(xn, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
+            x1, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)
+            st = {"saved": saved, "m_out": x1}
+        elif return_ssm_states:
             W, b = _cat_weights(self.mamba)
             m = self.mamba
             y, st = ops.ssm_fwd_states(xn, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
         else:
             y, _ = self.mamba.ssm_forward(xn)
-        # x1 = y + x and norm2(x1) in one pass (same bits as the separate add and norm)
-        x1, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)
+        if not isinstance(st, dict):
+            # x1 = y + x and norm2(x1) in one pass (same bits as the separate add and norm)
+            x1, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)
         f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                             block_size=self.block_size, activation=self.ffn_activation)
         out = f.reshape(B, L, D) + x1
@@ -86,16 +98,22 @@ class PGFMambaBlock(nn.Module):
     @torch.no_grad()
     def pgf_backward(self, x: torch.Tensor, g_out: torch.Tensor, fp32_accum: bool = True,
                      ssm_states: Optional[torch.Tensor] = None) -> Dict[str, Any]:
-        """pgf_mamba_block.py:128-249.  ssm_states: the boundary states pgf_forward returned for the
-        same x (the recompute then runs one scan pass instead of rebuilding them, :157-175)."""
+        """pgf_mamba_block.py:128-249.  ssm_states: what pgf_forward returned for the same x -- the
+        boundary states (the recompute then runs one scan pass instead of rebuilding them, :157-175),
+        or, from pgf_forward(keep_scan=True), the scan's saved states and y + x (no scan recompute)."""
         B, L, D = x.shape
         g_out = g_out.to(x.dtype)
         xn1 = self.norm1.pgf_forward(x, block_size=self.block_size)              # :157
         W, b = _cat_weights(self.mamba)
         m = self.mamba
-        # :163-178; the states it passes through are kept for the scan backward below
-        y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, act=m.output_activation, states=ssm_states)
-        m_out, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)  # y + x, :179
+        if isinstance(ssm_states, dict):
+            saved, m_out = ssm_states["saved"], ssm_states["m_out"]
+            xn2 = ops.rmsnorm_fwd(m_out, self.norm2.weight, self.norm2.eps)        # :179
+        else:
+            # :163-178; the states it passes through are kept for the scan backward below
+            y, saved = ops.ssm_fwd_save(xn1, W, b, m.A_log, m.D, m.scale, act=m.output_activation,
+                                        states=ssm_states)
+            m_out, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)  # y + x, :179
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                           block_size=self.block_size, activation=self.ffn_activation,
                           compute_input_grads=True)                              # :183-192

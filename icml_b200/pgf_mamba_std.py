@@ -104,15 +104,22 @@ class PGFMambaStdBlock(nn.Module):
         return f.reshape(B, L, D) + x1
 
     @torch.no_grad()
-    def pgf_forward(self, x: torch.Tensor, return_ssm_states: bool = False):
+    def pgf_forward(self, x: torch.Tensor, return_ssm_states: bool = False, keep_scan: bool = False):
+        """With return_ssm_states, also the scan's boundary states for pgf_backward; with keep_scan as
+        well, the mixer's saved buffer and mixer + x instead (the backward then runs no mixer forward)."""
         B, L, D = x.shape
         st = None
-        if return_ssm_states:
+        if return_ssm_states and keep_scan:
+            m, saved = ops.mamba_mixer_fwd_save(self.norm1.pgf_forward(x), self.mixer.params())
+            st = {"saved": saved}
+        elif return_ssm_states:
             m, st = ops.mamba_mixer_fwd(self.norm1.pgf_forward(x), self.mixer.params(), want_states=True)
         else:
             m = ops.mamba_mixer_fwd(self.norm1.pgf_forward(x), self.mixer.params())
         # x1 = mixer + x and norm2(x1) in one pass (same bits as the separate add and norm)
         x1, xn2 = ops.rmsnorm_fwd_res(m, x, self.norm2.weight, self.norm2.eps)
+        if isinstance(st, dict):
+            st["m_out"] = x1
         f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                             activation=self.ffn_activation)
         out = f.reshape(B, L, D) + x1
@@ -125,9 +132,13 @@ class PGFMambaStdBlock(nn.Module):
         g_out = g_out.to(x.dtype)
         p = self.mixer.params()
         xn1 = self.norm1.pgf_forward(x)
-        m_raw, saved = ops.mamba_mixer_fwd_save(xn1, p, states=ssm_states)
-        m_out, xn2 = ops.rmsnorm_fwd_res(m_raw, x, self.norm2.weight, self.norm2.eps)
-        del m_raw
+        if isinstance(ssm_states, dict):  # from pgf_forward(keep_scan=True)
+            saved, m_out = ssm_states["saved"], ssm_states["m_out"]
+            xn2 = ops.rmsnorm_fwd(m_out, self.norm2.weight, self.norm2.eps)
+        else:
+            m_raw, saved = ops.mamba_mixer_fwd_save(xn1, p, states=ssm_states)
+            m_out, xn2 = ops.rmsnorm_fwd_res(m_raw, x, self.norm2.weight, self.norm2.eps)
+            del m_raw
         fr = pgf_ffn_grad(xn2.reshape(-1, D), g_out.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
                           activation=self.ffn_activation, compute_input_grads=True)
         gw2, g_m = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), self.norm2.weight, self.norm2.eps,
