@@ -263,9 +263,273 @@ ce_bwd_dh_kernel(const __grid_constant__ CUtensorMap tmH, const __grid_constant_
   }
 }
 
+// The same product with the h rows in tensor memory instead of shared memory.  With two W slots and
+// the dh product one tile behind the logits, the TMA load of tile j+2 can only start once dh(j) has
+// released its slot, which is the product just before logits(j+2): every tile waited for a W load.
+// Here the unit's h rows sit in TMEM (d/2 columns, the A operand of the logits product) and the
+// 64 KB they took in shared memory hold a third W slot, so W(j+2) loads while logits(j+1) and dh(j)
+// run.  TMEM: logits 128 columns (one buffer: the epilogue reads it out right after it completes,
+// while dh of the previous tile runs), dh d columns, h d/2 columns: 512 at d = 256.
+// The epilogue warps write the h rows into TMEM (tcgen05.st) at the start of each unit.
+constexpr int NSLOT3 = 3;
+
+struct Params3 {
+  int64_t M, V;
+  int d, n_tiles;
+  int64_t units;
+  const __nv_bfloat16* h;  // (M, d) bf16, row pitch d
+  const int64_t* targets;
+  const float* lse;
+  float scale;
+  __nv_bfloat16* dh;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+ce_bwd_dh3_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmG,
+                  const Params3 p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int dch = p.d / 64;
+  const uint32_t HB = uint32_t(dch) * 16384u;     // bytes of one W slot
+  uint8_t* sW = base;                             // slots 0..2
+  uint8_t* sG = base + NSLOT3 * HB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sG + G_BYTES);
+  uint64_t* wfull = bars + 0;    // [3]
+  uint64_t* wempty = bars + 3;   // [3]
+  uint64_t* tfull = bars + 6;
+  uint64_t* tempty = bars + 7;
+  uint64_t* hready = bars + 8;
+  uint64_t* hfree = bars + 9;
+  uint64_t* gready = bars + 10;
+  uint64_t* gfree = bars + 11;
+  uint64_t* dhdone = bars + 12;
+  uint64_t* dhfree = bars + 13;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSLOT3; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 8);
+    mbar_init(hready, 8);
+    mbar_init(hfree, 1);
+    mbar_init(gready, 8);
+    mbar_init(gfree, 1);
+    mbar_init(dhdone, 1);
+    mbar_init(dhfree, 8);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmG)) : "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(tslot)), "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tslot;
+  const uint32_t tmem_l = tmem;                    // logits, BV columns
+  const uint32_t tmem_dh = tmem + BV;              // dh, d columns
+  const uint32_t tmem_h = tmem + BV + 256;         // h rows, d/2 columns
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer: W tiles through the three slots
+      uint32_t jj = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        for (int j = 0; j < p.n_tiles; ++j, ++jj) {
+          const uint32_t s = jj % NSLOT3, r = jj / NSLOT3;
+          if (r > 0 && !mbar_wait(&wempty[s], (r - 1) & 1)) { ok = false; break; }
+          mbar_expect_tx(&wfull[s], HB);
+          for (int c = 0; c < dch; ++c) tma_load_2d(sW + s * HB + c * 16384, &tmW, &wfull[s], c * 64, j * BV);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer: logits of tile j (A = h rows in TMEM), then dh of tile j-1
+      const uint32_t idesc_l = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BV >> 3) << 17) |
+                               (uint32_t(BM >> 4) << 24);
+      const uint32_t idesc_d = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (uint32_t(p.d >> 3) << 17) |
+                               (uint32_t(BM >> 4) << 24);
+      uint32_t jj = 0, tt = 0, uu = 0;
+      bool ok = true;
+      auto issue_dh = [&](uint32_t t, uint32_t s, bool first) -> bool {
+        if (!mbar_wait(gready, t & 1)) return false;
+        if (first && uu > 0 && !mbar_wait(dhfree, (uu - 1) & 1)) return false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t g_base = smem_u32(sG), w_base = smem_u32(sW + s * HB);
+#pragma unroll
+        for (int kk = 0; kk < BV / 16; ++kk) {
+          const uint64_t ad = sdesc(g_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc(w_base + kk * 2048, 16384, 1024);
+          umma_bf16(tmem_dh, ad, bd, idesc_d, (!first || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&wempty[s]);
+        umma_commit(gfree);
+        return true;
+      };
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uu) {
+        if (!mbar_wait(hready, uu & 1)) { ok = false; break; }
+        uint32_t prev_t = 0, prev_s = 0;
+        for (int j = 0; j < p.n_tiles && ok; ++j, ++jj, ++tt) {
+          const uint32_t s = jj % NSLOT3, r = jj / NSLOT3;
+          if (!mbar_wait(&wfull[s], r & 1)) { ok = false; break; }
+          if (tt > 0 && !mbar_wait(tempty, (tt - 1) & 1)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t w_base = smem_u32(sW + s * HB);
+          for (int kk = 0; kk < 4 * dch; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_bf16_ta(tmem_l, tmem_h + uint32_t(8 * kk), sdesc(w_base + off, 16, 1024), idesc_l,
+                         kk > 0 ? 1u : 0u);
+          }
+          umma_commit(tfull);
+          if (j == p.n_tiles - 1) umma_commit(hfree);  // the unit's h rows are no longer read
+          if (j > 0 && !issue_dh(prev_t, prev_s, j == 1)) { ok = false; break; }
+          prev_t = tt;
+          prev_s = s;
+        }
+        if (!ok) break;
+        if (!issue_dh(prev_t, prev_s, p.n_tiles == 1)) { ok = false; break; }
+        umma_commit(dhdone);
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..9: TMEM lane quarter q, vocabulary half hf of each tile
+    const int q = warp & 3;
+    const int hf = (warp - 2) >> 2;
+    const int dq = p.d / 4;  // TMEM columns of h rows written by this warp
+    constexpr float L2E = 1.4426950408889634f;
+    uint32_t tt = 0, uu = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uu) {
+      const int64_t m0 = u * BM;
+      const int64_t row = m0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const int64_t tgt = row_ok ? p.targets[row] : -1;
+      const float ll = row_ok ? p.lse[row] * L2E : 0.f;
+      // the unit's h rows into TMEM: this thread's row, elements 2 hf dq .. 2 (hf + 1) dq (zero past M)
+      if (uu > 0 && !mbar_wait_warp(hfree, (uu - 1) & 1)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      for (int c = 0; c < dq; c += 16) {
+        uint32_t v[16];
+        if (row_ok) {
+          const uint4* src = reinterpret_cast<const uint4*>(p.h + row * p.d + 2 * (hf * dq + c));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 t = __ldg(src + i);
+            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0u;
+        }
+        tmem_st16(tmem_h + (uint32_t(q * 32) << 16) + uint32_t(hf * dq + c), v);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(hready);
+      for (int j = 0; j < p.n_tiles; ++j, ++tt) {
+        if (!mbar_wait_warp(tfull, tt & 1)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        uint32_t r0[32], r1[32];
+        const uint32_t ta = tmem_l + (uint32_t(q * 32) << 16) + uint32_t(hf * 64);
+        tmem_ld32(ta, r0);
+        tmem_ld32(ta + 32, r1);
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty);
+        const int64_t nb = int64_t(j) * BV + hf * 64;
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float g0 = exp2f(fmaf(__uint_as_float(r0[2 * i]), L2E, -ll));
+          float g1 = exp2f(fmaf(__uint_as_float(r0[2 * i + 1]), L2E, -ll));
+          if (tgt == nb + 2 * i) g0 -= 1.0f;
+          if (tgt == nb + 2 * i + 1) g1 -= 1.0f;
+          pk[i] = pack_bf16(g0 * p.scale, g1 * p.scale);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float g0 = exp2f(fmaf(__uint_as_float(r1[2 * i]), L2E, -ll));
+          float g1 = exp2f(fmaf(__uint_as_float(r1[2 * i + 1]), L2E, -ll));
+          if (tgt == nb + 32 + 2 * i) g0 -= 1.0f;
+          if (tgt == nb + 32 + 2 * i + 1) g1 -= 1.0f;
+          pk[16 + i] = pack_bf16(g0 * p.scale, g1 * p.scale);
+        }
+        if (tt > 0 && !mbar_wait_warp(gfree, (tt - 1) & 1)) { ok = false; break; }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
+        uint8_t* gb = sG + hf * 16384 + q * 4096;
+        stage_row(gb, lane, pk);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          if (m0 + q * 32 < p.M && nb < p.V) {
+            asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                         ::"l"(reinterpret_cast<uint64_t>(&tmG)), "r"(int(nb)), "r"(int(m0 + q * 32)), "r"(0),
+                         "r"(smem_u32(gb))
+                         : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          mbar_arrive(gready);
+        }
+      }
+      if (!ok) break;
+      if (!mbar_wait_warp(dhdone, uu & 1)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int half = p.d / 2;
+      for (int c = 0; c < half; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_dh + (uint32_t(q * 32) << 16) + uint32_t(hf * half + c), r);
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(p.dh + row * p.d + hf * half + c);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(r[8 * v]), __uint_as_float(r[8 * v + 1]));
+            w.y = pack_bf16(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+            w.z = pack_bf16(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+            w.w = pack_bf16(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+            dst[v] = w;
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dhfree);
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
 }  // namespace lmh
 
 static size_t ce_bwd_dh_smem(int d) { return size_t(3) * (d / 64) * 16384 + lmh::G_BYTES + 8 * lmh::NBARS + 64 + 1024; }
+static size_t ce_bwd_dh3_smem(int d) {
+  return size_t(lmh::NSLOT3) * (d / 64) * 16384 + lmh::G_BYTES + 8 * lmh::NBARS + 64 + 1024;
+}
+// PGF_CE_BWD_TWO_SLOTS=1 selects the kernel with the h rows in shared memory and two W slots.
+static bool ce_bwd_two_slots() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PGF_CE_BWD_TWO_SLOTS");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
 
 bool ce_bwd_dh_usable(const void* h, const void* Wb, const void* G, int64_t ldg, const void* dh, int64_t d) {
   if (d % 64 != 0 || d < 64 || d > 256) return false;
@@ -292,10 +556,23 @@ int ce_bwd_dh(const __nv_bfloat16* h, const __nv_bfloat16* Wb, const int64_t* ta
   p.lse = lse;
   p.scale = scale;
   p.dh = dh;
+  const int64_t grid = p.units < sm_count() ? p.units : sm_count();
+  if (!ce_bwd_two_slots()) {
+    lmh::Params3 p3;
+    p3.M = M; p3.V = V; p3.d = int(d); p3.n_tiles = p.n_tiles; p3.units = p.units;
+    p3.h = h; p3.targets = targets; p3.lse = lse; p3.scale = scale; p3.dh = dh;
+    const size_t smem3 = ce_bwd_dh3_smem(int(d));
+    static int smem_limit3 = 0;
+    PGF_CUDA(ensure_dynamic_smem(lmh::ce_bwd_dh3_kernel, smem3, smem_limit3));
+    prof_begin(PROF_CE, s);
+    lmh::ce_bwd_dh3_kernel<<<unsigned(grid), lmh::THREADS, smem3, s>>>(mw, mg, p3);
+    prof_end(PROF_CE, s, 4.0 * double(M) * double(V) * double(d));
+    PGF_LAUNCH_CHECK();
+    return PGF_OK;
+  }
   const size_t smem = ce_bwd_dh_smem(int(d));
   static int smem_limit = 0;
   PGF_CUDA(ensure_dynamic_smem(lmh::ce_bwd_dh_kernel, smem, smem_limit));
-  const int64_t grid = p.units < sm_count() ? p.units : sm_count();
   prof_begin(PROF_CE, s);
   lmh::ce_bwd_dh_kernel<<<unsigned(grid), lmh::THREADS, smem, s>>>(mh, mw, mg, p);
   prof_end(PROF_CE, s, 4.0 * double(M) * double(V) * double(d));

@@ -487,3 +487,33 @@ def test_ssm_staged_finish_states(ops, act):
     for k in ("grad_u", "A_log", "D", "scale", "W_cat", "b_cat"):
         ref = ra[k].float()
         assert (rb[k].float() - ref).abs().max().item() <= 1e-5 + 1e-4 * ref.abs().max().item(), k
+
+
+def test_lm_head_ce_bwd_two_slot_kernel(tmp_path):
+    """The fused CE backward with the h rows in shared memory and two W slots
+    (PGF_CE_BWD_TWO_SLOTS=1, read once per process) gives the gradients of the default kernel, whose
+    h rows sit in tensor memory."""
+    import os
+    import subprocess
+    import sys
+    from icml_b200 import ops
+    g = _gen(23)
+    T, V, d = 700, 5000, 256
+    h = torch.randn(T, d, generator=g).bfloat16()
+    W = 0.3 * torch.randn(V, d, generator=g)
+    tg = torch.randint(0, V, (T,), generator=g)
+    torch.save({"h": h, "W": W, "tg": tg}, tmp_path / "in.pt")
+    _, lse = ops.lm_head_ce_fwd(h.to(DEV), W.to(DEV), tg.to(DEV))
+    gW, gh = ops.lm_head_ce_bwd(h.to(DEV), W.to(DEV), tg.to(DEV), lse, 1.0 / T)
+    code = ("import torch, sys; from icml_b200 import ops; c = torch.load(sys.argv[1]);"
+            "h, W, tg = (c[k].cuda() for k in ('h', 'W', 'tg'));"
+            "_, lse = ops.lm_head_ce_fwd(h, W, tg);"
+            "gW, gh = ops.lm_head_ce_bwd(h, W, tg, lse, 1.0 / h.shape[0]);"
+            "torch.save({'gW': gW.cpu(), 'gh': gh.cpu()}, sys.argv[2])")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PGF_CE_BWD_TWO_SLOTS="1", PYTHONPATH=root)
+    subprocess.run([sys.executable, "-c", code, str(tmp_path / "in.pt"), str(tmp_path / "out.pt")],
+                   env=env, check=True, timeout=300)
+    r = torch.load(tmp_path / "out.pt")
+    assert rel_err(r["gW"], gW) < 1e-5, rel_err(r["gW"], gW)
+    assert rel_err(r["gh"], gh) < 1e-5, rel_err(r["gh"], gh)
