@@ -417,10 +417,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               float s0 = 0.f, s1 = 0.f;
 #pragma unroll
               for (int j = 0; j < 32; j += 2) {
-                s0 += exp2f(fmaf(__uint_as_float(r[j]), L2E, -ml));
-                s1 += exp2f(fmaf(__uint_as_float(r[j + 1]), L2E, -ml));
+                s0 += ex2f(fmaf(__uint_as_float(r[j]), L2E, -ml));
+                s1 += ex2f(fmaf(__uint_as_float(r[j + 1]), L2E, -ml));
               }
-              run_s = run_s * exp2f((run_m - m1) * L2E) + (s0 + s1);
+              run_s = run_s * ex2f((run_m - m1) * L2E) + (s0 + s1);
               run_m = m1;
             }
             if (tgt >= nc && tgt < nc + 32) {

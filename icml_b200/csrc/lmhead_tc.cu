@@ -281,6 +281,7 @@ struct Params3 {
   const int64_t* targets;
   const float* lse;
   float scale;
+  float log2_scale;        // log2(scale): the scale is folded into the exponent
   __nv_bfloat16* dh;
 };
 
@@ -413,7 +414,8 @@ ce_bwd_dh3_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       const int64_t row = m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
       const int64_t tgt = row_ok ? p.targets[row] : -1;
-      const float ll = row_ok ? p.lse[row] * L2E : 0.f;
+      // g = scale exp(l - lse) = exp2(l log2e - (lse log2e - log2 scale))
+      const float lls = row_ok ? fmaf(p.lse[row], L2E, -p.log2_scale) : 0.f;
       // the unit's h rows into TMEM: this thread's row, elements 2 hf dq .. 2 (hf + 1) dq (zero past M)
       if (uu > 0 && !mbar_wait_warp(hfree, (uu - 1) & 1)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -450,25 +452,43 @@ ce_bwd_dh3_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float g0 = exp2f(fmaf(__uint_as_float(r0[2 * i]), L2E, -ll));
-          float g1 = exp2f(fmaf(__uint_as_float(r0[2 * i + 1]), L2E, -ll));
-          if (tgt == nb + 2 * i) g0 -= 1.0f;
-          if (tgt == nb + 2 * i + 1) g1 -= 1.0f;
-          pk[i] = pack_bf16(g0 * p.scale, g1 * p.scale);
+          pk[i] = pack_bf16(ex2f(fmaf(__uint_as_float(r0[2 * i]), L2E, -lls)),
+                            ex2f(fmaf(__uint_as_float(r0[2 * i + 1]), L2E, -lls)));
+          pk[16 + i] = pack_bf16(ex2f(fmaf(__uint_as_float(r1[2 * i]), L2E, -lls)),
+                                 ex2f(fmaf(__uint_as_float(r1[2 * i + 1]), L2E, -lls)));
         }
+        // the one-hot term: a row meets its target in one tile of the vocabulary, so this branch is
+        // rare.  The target's value (with scale subtracted) is formed here and written over its
+        // element of the staged tile below: fix = column << 16 | bf16 bits, or ~0 for none.
+        const int64_t off = tgt - nb;
+        const bool hit = off >= 0 && off < 64;
+        uint32_t fix = 0xFFFFFFFFu;
+        if (__any_sync(0xffffffffu, hit)) {
+          if (hit) {
+            const int e = int(off);
+            float x = 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float g0 = exp2f(fmaf(__uint_as_float(r1[2 * i]), L2E, -ll));
-          float g1 = exp2f(fmaf(__uint_as_float(r1[2 * i + 1]), L2E, -ll));
-          if (tgt == nb + 32 + 2 * i) g0 -= 1.0f;
-          if (tgt == nb + 32 + 2 * i + 1) g1 -= 1.0f;
-          pk[16 + i] = pack_bf16(g0 * p.scale, g1 * p.scale);
+            for (int i = 0; i < 32; ++i) {
+              x = e == i ? __uint_as_float(r0[i]) : x;
+              x = e == 32 + i ? __uint_as_float(r1[i]) : x;
+            }
+            const float g = ex2f(fmaf(x, L2E, -lls)) - p.scale;
+            fix = (uint32_t(e) << 16) | uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(g)));
+          }
         }
         if (tt > 0 && !mbar_wait_warp(gfree, (tt - 1) & 1)) { ok = false; break; }
         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         __syncwarp();
         uint8_t* gb = sG + hf * 16384 + q * 4096;
         stage_row(gb, lane, pk);
+        if (fix != 0xFFFFFFFFu) {
+          // element e of this lane's row: 16-byte chunk e / 8 (swizzled by the row), bf16 e % 8
+          const uint32_t e = fix >> 16;
+          const uint32_t addr = smem_u32(gb) + uint32_t(lane) * 128u + (((e >> 3) ^ uint32_t(lane & 7)) << 4) +
+                                (e & 7u) * 2u;
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(static_cast<unsigned short>(fix & 0xFFFFu))
+                       : "memory");
+        }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
@@ -557,10 +577,12 @@ int ce_bwd_dh(const __nv_bfloat16* h, const __nv_bfloat16* Wb, const int64_t* ta
   p.scale = scale;
   p.dh = dh;
   const int64_t grid = p.units < sm_count() ? p.units : sm_count();
-  if (!ce_bwd_two_slots()) {
+  // (the scale is folded into the exponent, so a scale that is not positive takes the other kernel)
+  if (!ce_bwd_two_slots() && scale > 0.f) {
     lmh::Params3 p3;
     p3.M = M; p3.V = V; p3.d = int(d); p3.n_tiles = p.n_tiles; p3.units = p.units;
     p3.h = h; p3.targets = targets; p3.lse = lse; p3.scale = scale; p3.dh = dh;
+    p3.log2_scale = float(log2(double(scale)));
     const size_t smem3 = ce_bwd_dh3_smem(int(d));
     static int smem_limit3 = 0;
     PGF_CUDA(ensure_dynamic_smem(lmh::ce_bwd_dh3_kernel, smem3, smem_limit3));

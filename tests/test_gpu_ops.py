@@ -515,5 +515,7 @@ def test_lm_head_ce_bwd_two_slot_kernel(tmp_path):
     subprocess.run([sys.executable, "-c", code, str(tmp_path / "in.pt"), str(tmp_path / "out.pt")],
                    env=env, check=True, timeout=300)
     r = torch.load(tmp_path / "out.pt")
-    assert rel_err(r["gW"], gW) < 1e-5, rel_err(r["gW"], gW)
-    assert rel_err(r["gh"], gh) < 1e-5, rel_err(r["gh"], gh)
+    # the default kernel forms exp with the hardware exp2 and folds the scale into the exponent, so a
+    # few bf16 elements of G round the other way: agreement to bf16 rounding
+    assert rel_err(r["gW"], gW) < 1e-3, rel_err(r["gW"], gW)
+    assert rel_err(r["gh"], gh) < 1e-3, rel_err(r["gh"], gh)
