@@ -188,9 +188,9 @@ def run_reference(a, rank, world):
 # launches) from one ncu capture of the default workload (8-layer reference variant, d 256, d_ff
 # 1024, vocab 50257, B=1 x L=65536, bf16; `--steps 1 --warmup 1 --no-cpu-baseline --no-graph`).
 # Reported as `traffic` only for that workload.
-TRAFFIC_DEFAULT = {"gemm_tc": 70859515, "ssm_main_bwd": 491883560, "ce": 1318646746, "ssm_chunk_fwd": 217940236,
-                   "ssm_out_fwd": 208103736, "ssm_chunk_bwd": 146987688, "ssm_compose": 9116957,
-                   "rmsnorm_fwd": 58905892, "rmsnorm_bwd": 110434924, "adamw": 395506336}
+TRAFFIC_DEFAULT = {"gemm_tc": 194818014, "ssm_main_bwd": 491831096, "ce": 1316616857, "ssm_chunk_fwd": 150740000,
+                   "ssm_out_fwd": 230101748, "ssm_chunk_bwd": 147060344, "ssm_compose": 8940480,
+                   "rmsnorm_fwd": 58914490, "rmsnorm_bwd": 110329568, "adamw": 395415392}
 
 
 def default_workload(a, world):
