@@ -57,6 +57,7 @@ SIGNATURES = {
     "pgf_colsum": (c_int, [P, c_int, I64, I64, I64, P, c_int, P, c_size_t, P]),
     "pgf_ffn_workspace": (c_size_t, [I64, I64, I64, I64, c_int, c_int]),
     "pgf_ffn_fwd": (c_int, [P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P, c_size_t, P]),
+    "pgf_ffn_fwd_res": (c_int, [P, P, P, P, P, P, P, I64, I64, I64, I64, c_int, c_int, P, c_size_t, P]),
     "pgf_ffn_bwd": (c_int, [P, P, P, P, P, P, P, P, P, P, c_int, I64, I64, I64, I64, c_int, c_int,
                             P, c_size_t, P]),
     "pgf_lm_head_workspace": (c_size_t, [I64, I64, I64, c_int]),

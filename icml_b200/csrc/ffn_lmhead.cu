@@ -100,10 +100,33 @@ extern "C" size_t pgf_ffn_workspace(int64_t rows, int64_t d_in, int64_t d_hidden
   return ffn_ws_bytes(rows, d_in, d_hidden, d_out, dtype, backward);
 }
 
+namespace pgf {
+static int ffn_fwd_impl(const void* x, const float* W1, const float* b1, const float* W2, const float* b2,
+                        const void* res, void* y, int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out,
+                        int activation, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+}
+
 extern "C" int pgf_ffn_fwd(const void* x, const float* W1, const float* b1, const float* W2,
                            const float* b2, void* y, int64_t rows, int64_t d_in, int64_t d_hidden,
                            int64_t d_out, int activation, int dtype, void* ws, size_t ws_bytes,
                            pgf_stream_t stream) {
+  return ffn_fwd_impl(x, W1, b1, W2, b2, nullptr, y, rows, d_in, d_hidden, d_out, activation, dtype, ws, ws_bytes,
+                      stream);
+}
+
+extern "C" int pgf_ffn_fwd_res(const void* x, const float* W1, const float* b1, const float* W2,
+                               const float* b2, const void* res, void* y, int64_t rows, int64_t d_in,
+                               int64_t d_hidden, int64_t d_out, int activation, int dtype, void* ws,
+                               size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(res, "ffn_fwd_res: null residual");
+  return ffn_fwd_impl(x, W1, b1, W2, b2, res, y, rows, d_in, d_hidden, d_out, activation, dtype, ws, ws_bytes,
+                      stream);
+}
+
+namespace pgf {
+static int ffn_fwd_impl(const void* x, const float* W1, const float* b1, const float* W2, const float* b2,
+                        const void* res, void* y, int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out,
+                        int activation, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
   PGF_CHECK_ARG(x && W1 && b1 && W2 && b2 && y, "ffn_fwd: null pointer");
   PGF_CHECK_ARG(activation == PGF_ACT_GELU || activation == PGF_ACT_RELU, "ffn_fwd: bad activation");
   PGF_CHECK_ARG(dtype == 0 || dtype == 1, "ffn_fwd: bad dtype");
@@ -132,10 +155,17 @@ extern "C" int pgf_ffn_fwd(const void* x, const float* W1, const float* b1, cons
     PGF_TRY(run_gemm(g1, s));
     Gemm g2 = mk(m, d_out, d_hidden, f.h, dtype, d_hidden, 0, w2, dtype, d_hidden, 0, yt, dtype, d_out);
     g2.epi.bias = b2;
+    if (res) {
+      // y = h W2^T + b2 + res, rounded once (the block's FFN output plus its skip connection)
+      g2.epi.addend = static_cast<const char*>(res) + r * d_out * es;
+      g2.epi.addend_dtype = dtype;
+      g2.epi.ld_addend = d_out;
+    }
     PGF_TRY(run_gemm(g2, s));
   }
   return PGF_OK;
 }
+}  // namespace pgf
 
 // ---------------------------------------------------------------------------------------------
 // Forward-mode derivative (pgf_ffn_jvp, pgf_ffn.py:120-180), per row tile of m rows:

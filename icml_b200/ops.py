@@ -176,7 +176,8 @@ def colsum(X: torch.Tensor) -> torch.Tensor:
 
 
 # --------------------------------------------------------------------------- FFN
-def ffn_fwd(x, W1, b1, W2, b2, activation="gelu") -> torch.Tensor:
+def ffn_fwd(x, W1, b1, W2, b2, activation="gelu", residual=None) -> torch.Tensor:
+    """FFN(x); with `residual` (rows x d_out, x's dtype), FFN(x) + residual from the same kernel."""
     _cuda(x, W1)
     x = _c(x)
     W1, b1, W2, b2 = _f32(W1), _f32(b1), _f32(W2), _f32(b2)
@@ -185,6 +186,13 @@ def ffn_fwd(x, W1, b1, W2, b2, activation="gelu") -> torch.Tensor:
     y = torch.empty(rows, d_out, dtype=x.dtype, device=x.device)
     L = lib()
     ws = _ws(L.pgf_ffn_workspace(rows, d_in, d_h, d_out, _dt(x), 0), x.device)
+    if residual is not None:
+        res = _c(residual.to(x.dtype))
+        if res.shape != (rows, d_out):
+            raise ValueError(f"ffn_fwd: residual shape {tuple(res.shape)} != {(rows, d_out)}")
+        check(L.pgf_ffn_fwd_res(_p(x), _p(W1), _p(b1), _p(W2), _p(b2), _p(res), _p(y), rows, d_in, d_h, d_out,
+                                ACT[activation], _dt(x), _p(ws), ws.numel(), _stream()), "ffn_fwd_res")
+        return y
     check(L.pgf_ffn_fwd(_p(x), _p(W1), _p(b1), _p(W2), _p(b2), _p(y), rows, d_in, d_h, d_out,
                         ACT[activation], _dt(x), _p(ws), ws.numel(), _stream()), "ffn_fwd")
     return y

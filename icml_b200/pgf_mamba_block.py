@@ -16,7 +16,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
-from .pgf_ffn import FFNFunction, pgf_ffn_forward, pgf_ffn_grad
+from .pgf_ffn import FFNFunction, pgf_ffn_grad
 from .pgf_rmsnorm import RMSNorm
 from .train_singlemamba_optimized import SingleLayerMambaPGF, _cat_weights
 
@@ -90,9 +90,9 @@ class PGFMambaBlock(nn.Module):
         if not isinstance(st, dict):
             # x1 = y + x and norm2(x1) in one pass (same bits as the separate add and norm)
             x1, xn2 = ops.rmsnorm_fwd_res(y, x, self.norm2.weight, self.norm2.eps)
-        f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
-                            block_size=self.block_size, activation=self.ffn_activation)
-        out = f.reshape(B, L, D) + x1
+        # ffn(norm2(x1)) + x1 (:120-126), the skip connection added in the FFN's last epilogue
+        out = ops.ffn_fwd(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2, self.ffn_activation,
+                          residual=x1.reshape(-1, D)).reshape(B, L, D)
         return (out, st) if return_ssm_states else out
 
     @torch.no_grad()

@@ -16,7 +16,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from .pgf_ffn import FFNFunction, pgf_ffn_forward, pgf_ffn_grad
+from .pgf_ffn import FFNFunction, pgf_ffn_grad
 from .pgf_rmsnorm import RMSNorm
 
 _GRAD_NAMES = {"in_w": "in_proj.weight", "conv_w": "conv1d.weight", "conv_b": "conv1d.bias",
@@ -120,9 +120,8 @@ class PGFMambaStdBlock(nn.Module):
         x1, xn2 = ops.rmsnorm_fwd_res(m, x, self.norm2.weight, self.norm2.eps)
         if isinstance(st, dict):
             st["m_out"] = x1
-        f = pgf_ffn_forward(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2,
-                            activation=self.ffn_activation)
-        out = f.reshape(B, L, D) + x1
+        out = ops.ffn_fwd(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2, self.ffn_activation,
+                          residual=x1.reshape(-1, D)).reshape(B, L, D)  # ffn(norm2(x1)) + x1
         return (out, st) if return_ssm_states else out
 
     @torch.no_grad()

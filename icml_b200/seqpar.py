@@ -101,8 +101,9 @@ def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
         h_in = None
         y, states = ops.ssm_fwd_states(xn, W, b, m.A_log, m.D, m.scale, act=m.output_activation)
     x1, xn2 = ops.rmsnorm_fwd_res(y, x, block.norm2.weight, block.norm2.eps)  # y + x, then norm2
-    f = ops.ffn_fwd(xn2.reshape(-1, D), block.W1, block.b1, block.W2, block.b2, block.ffn_activation)
-    return f.reshape(B, L, D) + x1, h_in, states
+    f = ops.ffn_fwd(xn2.reshape(-1, D), block.W1, block.b1, block.W2, block.b2, block.ffn_activation,
+                    residual=x1.reshape(-1, D))  # ffn(norm2(x1)) + x1
+    return f.reshape(B, L, D), h_in, states
 
 
 @torch.no_grad()

@@ -187,6 +187,12 @@ size_t pgf_ffn_workspace(int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d
 int pgf_ffn_fwd(const void* x, const float* W1, const float* b1, const float* W2, const float* b2,
                 void* y, int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out,
                 int activation, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+/* pgf_ffn_fwd plus a residual in the activation dtype, added in the second product's epilogue and
+ * rounded once: y = FFN(x) + res, the block's `ffn(norm2(x1)) + x1` (pgf_mamba_block.py:120-126)
+ * without a separate add over the activations. */
+int pgf_ffn_fwd_res(const void* x, const float* W1, const float* b1, const float* W2, const float* b2,
+                    const void* res, void* y, int64_t rows, int64_t d_in, int64_t d_hidden, int64_t d_out,
+                    int activation, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
 int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const float* b1, const float* W2,
                 float* grad_W1, float* grad_b1, float* grad_W2, float* grad_b2,
                 void* grad_x /* nullable */, int accumulate, int64_t rows, int64_t d_in,

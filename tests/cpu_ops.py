@@ -111,8 +111,9 @@ def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_e
             "delta_h0": r["delta_h0"], "dA0": r["dA0"]}
 
 
-def ffn_fwd(x, W1, b1, W2, b2, activation="gelu"):
-    return O.ffn_forward(x, W1.detach(), b1.detach(), W2.detach(), b2.detach(), activation)
+def ffn_fwd(x, W1, b1, W2, b2, activation="gelu", residual=None):
+    y = O.ffn_forward(x, W1.detach(), b1.detach(), W2.detach(), b2.detach(), activation)
+    return y if residual is None else y + residual
 
 
 def ffn_bwd(x, g, W1, b1, W2, activation="gelu", need_gx=True):

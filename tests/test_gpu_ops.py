@@ -163,6 +163,25 @@ def test_ffn_f32(ops, act, rows, d, dh):
         assert_close(r[k], ref[k], name=k)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,d,dh", [(70, 24, 64), (5000, 256, 1024)])
+def test_ffn_fwd_residual(ops, dtype, rows, d, dh):
+    """FFN(x) + residual from the second product's epilogue equals the separate add (float32:
+    within float32 rounding; bf16: one rounding instead of two)."""
+    g = _gen(12)
+    x = torch.randn(rows, d, generator=g).to(dtype).to(DEV)
+    res = torch.randn(rows, d, generator=g).to(dtype).to(DEV)
+    W1, W2 = (0.1 * torch.randn(dh, d, generator=g)).to(DEV), (0.1 * torch.randn(d, dh, generator=g)).to(DEV)
+    b1, b2 = (0.1 * torch.randn(dh, generator=g)).to(DEV), (0.1 * torch.randn(d, generator=g)).to(DEV)
+    y = ops.ffn_fwd(x, W1, b1, W2, b2, "gelu", residual=res)
+    ref = ops.ffn_fwd(x, W1, b1, W2, b2, "gelu").double() + res.double()
+    assert y.dtype == dtype
+    if dtype == torch.float32:
+        assert_close(y, ref, name="y")
+    else:
+        assert (y.double() - ref).abs().max().item() <= 2 ** -7 * ref.abs().max().item()
+
+
 @pytest.mark.parametrize("act", ["gelu", "relu"])
 @pytest.mark.parametrize("rows,dtype", [(9000, torch.float32), (17000, torch.bfloat16)])
 def test_ffn_row_tiles(ops, act, rows, dtype):
