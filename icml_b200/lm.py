@@ -132,8 +132,10 @@ class PGFLanguageModel:
         self.backbone = PGFMambaSequential(blocks).to(device)
         self.final_norm = RMSNorm(d_model).to(device) if final_norm else None
         self.stash = LayerStash(stash)
+        from .train_singlemamba_optimized import flat_order
         self.params = [self.emb_weight] + ([] if tie_embeddings else [self.lm_head_weight]) + \
-            list(self.backbone.parameters()) + (list(self.final_norm.parameters()) if final_norm else [])
+            flat_order(self.backbone.parameters(), self.backbone) + \
+            (list(self.final_norm.parameters()) if final_norm else [])
         on_gpu = self.device.type == "cuda"
         self.optimizer_kind = optimizer or ("flat" if on_gpu else "torch")
         if self.optimizer_kind == "flat":

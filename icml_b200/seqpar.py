@@ -77,9 +77,8 @@ def compose_backward_carry(d_locs: torch.Tensor, dA_starts: torch.Tensor, sum_dt
 
 
 def _wb(m):
-    W = torch.cat([m.dt_proj.weight, m.B_proj.weight, m.C_proj.weight], 0)
-    b = torch.cat([m.dt_proj.bias, m.B_proj.bias, m.C_proj.bias], 0)
-    return W, b
+    from .train_singlemamba_optimized import _cat_weights
+    return _cat_weights(m)
 
 
 @torch.no_grad()

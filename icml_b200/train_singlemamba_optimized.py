@@ -19,10 +19,47 @@ from . import ops
 _ACTS = (None, "relu", "tanh")
 
 
+def _adjacent(ts):
+    """The tensors as one flat view when they lie back to back in one storage (as the flat optimizer
+    buffer lays out a layer's projections), else None."""
+    t0 = ts[0]
+    st = t0.untyped_storage().data_ptr()
+    off = t0.storage_offset()
+    for t in ts:
+        if not t.is_contiguous() or t.untyped_storage().data_ptr() != st or t.storage_offset() != off:
+            return None
+        off += t.numel()
+    n = off - t0.storage_offset()
+    return torch.empty(0, dtype=t0.dtype, device=t0.device).set_(t0.untyped_storage(), t0.storage_offset(), (n,))
+
+
+@torch.no_grad()
 def _cat_weights(m):
-    W = torch.cat([m.dt_proj.weight, m.B_proj.weight, m.C_proj.weight], dim=0)
-    b = torch.cat([m.dt_proj.bias, m.B_proj.bias, m.C_proj.bias], dim=0)
+    """W_cat = [dt_proj.weight; B_proj.weight; C_proj.weight] and b_cat likewise: views of the flat
+    parameter buffer when the optimizer keeps them adjacent, else concatenated copies."""
+    ws = [m.dt_proj.weight, m.B_proj.weight, m.C_proj.weight]
+    bs = [m.dt_proj.bias, m.B_proj.bias, m.C_proj.bias]
+    W, b = _adjacent(ws), _adjacent(bs)
+    W = W.view(-1, ws[0].shape[1]) if W is not None else torch.cat(ws, dim=0)
+    b = b if b is not None else torch.cat(bs, dim=0)
     return W, b
+
+
+def flat_order(params, module):
+    """`params` with each SingleLayerMambaPGF's projection weights, then its projection biases, moved
+    next to each other (at the first one's place), so a flat buffer in this order holds W_cat and
+    b_cat contiguously."""
+    params = list(params)
+    for m in module.modules():
+        if isinstance(m, SingleLayerMambaPGF):
+            group = [m.dt_proj.weight, m.B_proj.weight, m.C_proj.weight, m.dt_proj.bias, m.B_proj.bias,
+                     m.C_proj.bias]
+            ids = {id(p) for p in group}
+            at = min(i for i, p in enumerate(params) if id(p) in ids)
+            rest = [p for p in params if id(p) not in ids]
+            before = [p for p in params[:at] if id(p) not in ids]
+            params = before + group + rest[len(before):]
+    return params
 
 
 class SSMFunction(torch.autograd.Function):

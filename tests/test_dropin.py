@@ -81,3 +81,33 @@ def test_frechet_operator_seeded_init_matches_reference():
         assert set(sd) == set(G[name]["params"])
         for k, v in G[name]["params"].items():
             assert torch.equal(sd[k], v), k
+
+
+def test_projection_weights_adjacent_view():
+    """With a layer's projections laid out back to back in one flat buffer (the order flat_order
+    gives), _cat_weights returns views of that buffer equal to the concatenation; otherwise copies."""
+    from icml_b200.train_singlemamba_optimized import SingleLayerMambaPGF, _cat_weights, flat_order
+    torch.manual_seed(3)
+    m = SingleLayerMambaPGF(24, 16)
+    ref_W = torch.cat([m.dt_proj.weight, m.B_proj.weight, m.C_proj.weight]).detach().clone()
+    ref_b = torch.cat([m.dt_proj.bias, m.B_proj.bias, m.C_proj.bias]).detach().clone()
+    W, b = _cat_weights(m)                       # separate parameters: copies
+    assert torch.equal(W, ref_W) and torch.equal(b, ref_b)
+    order = flat_order(m.parameters(), m)
+    at = [id(p) for p in order].index(id(m.dt_proj.weight))
+    assert [id(p) for p in order[at:at + 6]] == [
+        id(p) for p in (m.dt_proj.weight, m.B_proj.weight, m.C_proj.weight, m.dt_proj.bias, m.B_proj.bias,
+                        m.C_proj.bias)]
+    assert sorted(map(id, order)) == sorted(map(id, m.parameters()))
+    flat = torch.zeros(sum(p.numel() for p in order))
+    o = 0
+    with torch.no_grad():
+        for p in order:
+            v = flat[o:o + p.numel()].view_as(p)
+            v.copy_(p)
+            p.data = v
+            o += p.numel()
+    W, b = _cat_weights(m)
+    assert torch.equal(W, ref_W) and torch.equal(b, ref_b)
+    assert W.untyped_storage().data_ptr() == flat.untyped_storage().data_ptr()
+    assert b.untyped_storage().data_ptr() == flat.untyped_storage().data_ptr()
