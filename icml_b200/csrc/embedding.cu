@@ -13,6 +13,7 @@ constexpr int RADIX_TILE = 2048;      // elements ranked by one warp, in order
 constexpr int RADIX_WARPS = 4;        // tiles per CTA
 constexpr int SEG_TILE = 256;         // sorted entries per segment-sum tile
 constexpr int SEG_THREADS = 256;
+constexpr int SEG_BATCH = 8;          // gradient rows loaded together per thread
 
 // Out-of-range ids give zero rows (the API does not synchronise to report them).
 template <class T>
@@ -134,22 +135,32 @@ seg_tile_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ 
   for (int c = threadIdx.x; c < dim; c += blockDim.x) {
     float s = 0.f;
     bool first = true;  // current segment is the tile's first
-    for (int64_t i = a; i < b; ++i) {
-      s += ld(g, int64_t(pos[i]) * dim + c);
-      const bool seg_end = (i + 1 == b) || keys[i + 1] != keys[i];
-      if (!seg_end) continue;
-      const uint32_t k = keys[i];
-      const bool last = (i + 1 == b);
-      if (first && head_cont) {
-        head[int64_t(tile) * dim + c] = s;          // piece of a segment owned by an earlier tile
-      } else if (last && tail_cont) {
-        tail[int64_t(tile) * dim + c] = s;          // this tile owns a segment that continues
-      } else if (k < vocab) {
-        float* dst = gw + int64_t(k) * dim + c;     // segment entirely inside the tile
-        *dst = accumulate ? *dst + s : s;
+    // entries are taken SEG_BATCH at a time: their gradient rows are loaded together (independent
+    // loads in flight), then summed in order, so the sums are those of the one-by-one loop
+    for (int64_t i0 = a; i0 < b; i0 += SEG_BATCH) {
+      float v[SEG_BATCH];
+#pragma unroll
+      for (int q = 0; q < SEG_BATCH; ++q) v[q] = i0 + q < b ? ld(g, int64_t(pos[i0 + q]) * dim + c) : 0.f;
+#pragma unroll
+      for (int q = 0; q < SEG_BATCH; ++q) {
+        const int64_t i = i0 + q;
+        if (i >= b) break;
+        s += v[q];
+        const bool seg_end = (i + 1 == b) || keys[i + 1] != keys[i];
+        if (!seg_end) continue;
+        const uint32_t k = keys[i];
+        const bool last = (i + 1 == b);
+        if (first && head_cont) {
+          head[int64_t(tile) * dim + c] = s;          // piece of a segment owned by an earlier tile
+        } else if (last && tail_cont) {
+          tail[int64_t(tile) * dim + c] = s;          // this tile owns a segment that continues
+        } else if (k < vocab) {
+          float* dst = gw + int64_t(k) * dim + c;     // segment entirely inside the tile
+          *dst = accumulate ? *dst + s : s;
+        }
+        s = 0.f;
+        first = false;
       }
-      s = 0.f;
-      first = false;
     }
   }
 }
