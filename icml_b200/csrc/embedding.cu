@@ -30,6 +30,30 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const floa
   for (int c = threadIdx.x; c < dim; c += blockDim.x) st(yr, c, wr[c]);
 }
 
+// The same with a warp per token and 16-byte rows pieces (dim a multiple of 4, aligned rows): eight
+// tokens per CTA instead of one CTA per token.
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+template <class T>
+__global__ void __launch_bounds__(256) embedding_fwd_vec_kernel(const int64_t* __restrict__ ids,
+                                                                 const float* __restrict__ W, T* __restrict__ y,
+                                                                 int64_t n, int64_t vocab, int dim) {
+  const int64_t t = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const int64_t id = ids[t];
+  const bool ok = id >= 0 && id < vocab;
+  const float4* wr = reinterpret_cast<const float4*>(W + (ok ? id : 0) * dim);
+  T* yr = y + t * dim;
+  for (int c4 = lane; c4 < dim / 4; c4 += 32) st4(yr + 4 * c4, ok ? __ldg(wr + c4) : make_float4(0.f, 0.f, 0.f, 0.f));
+}
+
 __global__ void make_keys_kernel(const int64_t* __restrict__ ids, uint32_t* __restrict__ keys,
                                  uint32_t* __restrict__ vals, int64_t n, int64_t vocab,
                                  int* __restrict__ bad) {
@@ -258,6 +282,18 @@ extern "C" int pgf_embedding_fwd(const int64_t* ids, const float* weight, void* 
                 "embedding_fwd: bad shape");
   if (n_tokens == 0) return PGF_OK;
   cudaStream_t s = as_stream(stream);
+  const size_t ya = dtype == PGF_DTYPE_F32 ? 16 : 8;
+  if (dim % 4 == 0 && reinterpret_cast<uintptr_t>(weight) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % ya == 0 &&
+      (dtype == PGF_DTYPE_F32 || dtype == PGF_DTYPE_BF16)) {
+    const unsigned grid = unsigned((n_tokens + 7) / 8);
+    if (dtype == PGF_DTYPE_F32)
+      embedding_fwd_vec_kernel<float><<<grid, 256, 0, s>>>(ids, weight, (float*)y, n_tokens, vocab, int(dim));
+    else
+      embedding_fwd_vec_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(ids, weight, (__nv_bfloat16*)y, n_tokens,
+                                                                   vocab, int(dim));
+    PGF_LAUNCH_CHECK();
+    return PGF_OK;
+  }
   int threads = dim >= 256 ? 256 : int((dim + 31) / 32 * 32);
   if (dtype == PGF_DTYPE_F32)
     embedding_fwd_kernel<float><<<unsigned(n_tokens), threads, 0, s>>>(ids, weight, (float*)y,

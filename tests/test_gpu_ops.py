@@ -84,6 +84,21 @@ def test_embedding(ops, n, V, d):
     assert torch.equal(gw, gw2), "embedding gradient must be bitwise reproducible"
 
 
+@pytest.mark.parametrize("d", [6, 256])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_embedding_fwd_rows(ops, d, dtype):
+    """Rows gathered (widths that take the 16-byte path and one that does not) in either dtype,
+    and zero rows for ids outside the vocabulary."""
+    g = _gen(4 + d)
+    V, n = 500, 3001
+    ids = torch.randint(0, V, (n,), generator=g)
+    ids[:3] = torch.tensor([-1, V, V + 7])
+    W = torch.randn(V, d, generator=g)
+    y = ops.embedding_fwd(ids.to(DEV), W.to(DEV), dtype=dtype).cpu()
+    ref = torch.cat([torch.zeros(3, d), W[ids[3:]]]).to(dtype)
+    assert y.dtype == dtype and torch.equal(y, ref)
+
+
 def test_embedding_golden(ops):
     c = golden("components.pt")["embedding"]
     y = ops.embedding_fwd(c["ids"].to(DEV), c["W"].to(DEV))
