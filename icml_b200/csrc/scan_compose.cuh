@@ -111,7 +111,24 @@ __device__ __forceinline__ float compose_bwd_segmented(bool valid, const float* 
   float M = 1.f, G = 0.f;
   if (valid) {
     float aE = aE_right;
-    for (int64_t c = c1 - 1; c >= c0; --c) {
+    int64_t c = c1 - 1;
+    for (; c - CSEG_PF + 1 >= c0; c -= CSEG_PF) {
+      float s2[CSEG_PF], d0[CSEG_PF], dl[CSEG_PF];
+#pragma unroll
+      for (int q = 0; q < CSEG_PF; ++q) {
+        s2[q] = sdt2[(c - q) * cs];
+        d0[q] = dt0[(c - q) * cs];
+        dl[q] = dloc[(c - q) * hs];
+      }
+#pragma unroll
+      for (int q = 0; q < CSEG_PF; ++q) {
+        const float m = exp2f(A2 * s2[q]) * aE;
+        G = m * G + dl[q];
+        M *= m;
+        aE = exp2f(A2 * d0[q]);
+      }
+    }
+    for (; c >= c0; --c) {
       const float m = exp2f(A2 * sdt2[c * cs]) * aE;
       G = m * G + dloc[c * hs];
       M *= m;
