@@ -124,11 +124,16 @@ __global__ void radix_scatter_kernel(const uint32_t* __restrict__ kin, const uin
   int64_t a = int64_t(tile) * RADIX_TILE;
   int64_t b = a + RADIX_TILE < n ? a + RADIX_TILE : n;
   const unsigned lt = (1u << lane) - 1u;
+  // the next 32 keys and values are loaded while the current ones are ranked and stored
+  uint32_t kn = a + lane < b ? kin[a + lane] : 0u, vn = a + lane < b ? vin[a + lane] : 0u;
   for (int64_t i0 = a; i0 < b; i0 += 32) {
     int64_t i = i0 + lane;
     bool valid = i < b;
-    uint32_t k = valid ? kin[i] : 0u;
-    uint32_t v = valid ? vin[i] : 0u;
+    const uint32_t k = kn, v = vn;
+    if (i + 32 < b) {
+      kn = kin[i + 32];
+      vn = vin[i + 32];
+    }
     int dgt = valid ? int((k >> shift) & 255u) : 256 + lane;  // invalid lanes match nobody
     unsigned peers = __match_any_sync(0xffffffffu, dgt);
     uint32_t pos = 0;
