@@ -164,33 +164,53 @@ rmsnorm_fwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ res, T* __
       qx[r][k] = ok ? __ldg(reinterpret_cast<const uint4*>(x + off)) : make_uint4(0, 0, 0, 0);
       qr[r][k] = (ok && res) ? __ldg(reinterpret_cast<const uint4*>(res + off)) : make_uint4(0, 0, 0, 0);
     }
+  // the weight slice of this lane, once for all of the warp's rows (one row per warp: read in place)
+  constexpr bool HOIST_W = RPW > 1;
+  float wv[HOIST_W ? CPL : 1][VW];
+  if (HOIST_W) {
+#pragma unroll
+    for (int k = 0; k < (HOIST_W ? CPL : 1); ++k)
+#pragma unroll
+      for (int e = 0; e < VW; ++e) wv[k][e] = __ldg(w + (k * 32 + lane) * VW + e);
+  }
+  // sums of squares of all the warp's rows first, then their warp reductions side by side (the
+  // same butterfly order per row), then the per-row divides: the rows' dependent chains overlap
+  float v[RPW][CPL][VW];
+  float ss[RPW];
 #pragma unroll
   for (int r = 0; r < RPW; ++r) {
     const int64_t row = row0 + r;
-    if (row >= rows) break;
-    float v[CPL][VW];
-    float ss = 0.f;
+    ss[r] = 0.f;
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
-      V::unpack(qx[r][k], v[k]);
+      V::unpack(qx[r][k], v[r][k]);
       if (res) {
         float a[VW];
         V::unpack(qr[r][k], a);
 #pragma unroll
-        for (int e = 0; e < VW; ++e) v[k][e] = rounded<T>(v[k][e] + a[e]);
-        *reinterpret_cast<uint4*>(sum_out + row * dim + int64_t(k * 32 + lane) * VW) = V::pack(v[k]);
+        for (int e = 0; e < VW; ++e) v[r][k][e] = rounded<T>(v[r][k][e] + a[e]);
+        if (row < rows)
+          *reinterpret_cast<uint4*>(sum_out + row * dim + int64_t(k * 32 + lane) * VW) = V::pack(v[r][k]);
       }
 #pragma unroll
-      for (int e = 0; e < VW; ++e) ss = fmaf(v[k][e], v[k][e], ss);
+      for (int e = 0; e < VW; ++e) ss[r] = fmaf(v[r][k][e], v[r][k][e], ss[r]);
     }
-    ss = warp_sum(ss);
-    const float rinv = 1.0f / sqrtf(ss / float(dim) + eps);  // one divide per row
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], o);
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int64_t row = row0 + r;
+    const float rinv = 1.0f / sqrtf(ss[r] / float(dim) + eps);  // one divide per row
+    if (row >= rows) continue;
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
       const int c0 = (k * 32 + lane) * VW;
       float o[VW];
 #pragma unroll
-      for (int e = 0; e < VW; ++e) o[e] = (v[k][e] * rinv) * __ldg(w + c0 + e);
+      for (int e = 0; e < VW; ++e) o[e] = (v[r][k][e] * rinv) * (HOIST_W ? wv[HOIST_W ? k : 0][e] : __ldg(w + c0 + e));
       *reinterpret_cast<uint4*>(y + row * dim + c0) = V::pack(o);
     }
   }
