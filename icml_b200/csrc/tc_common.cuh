@@ -16,7 +16,8 @@ namespace pgf {
 constexpr long long WAIT_CYCLES = 4000000000ll;  // about 2 s at the B200 clock
 
 // Set (never cleared by a kernel) when a bounded mbarrier wait expires.  One flag per translation
-// unit (device variables do not link across units in this build); take_tc_fault() reads and
+// unit (the library is compiled without relocatable device code, so device variables do not link
+// across units); take_tc_fault() reads and
 // clears this unit's flag, and pgf_tc_fault() combines the units.
 static __device__ int g_tc_fault;
 

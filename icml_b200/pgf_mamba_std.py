@@ -1,7 +1,7 @@
 """Mamba-standard variant of the PGF block, on libpgf.so.
 
 The reference's PGFMambaBlock (pgf_mamba_block.py:16-249) wraps its own simplified SSM.  The
-benchmark configurations of this build use the standard Mamba mixer instead (in_proj, causal
+8-layer d_inner-512 and 24-layer d_model-1024 LM configurations use the standard Mamba mixer (in_proj, causal
 depthwise conv1d + SiLU, x_proj, low-rank dt_proj, per-channel A, gate SiLU(z), out_proj); the
 reference has no code for it.  `PGFMambaStdBlock` keeps the reference block's structure and PGF
 API (pgf_forward / pgf_backward returning {"grads", "grad_input"}) around that mixer; parameter

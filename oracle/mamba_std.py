@@ -1,8 +1,8 @@
 """CPU oracle of the Mamba-standard variant of the PGF block.  TEST INFRASTRUCTURE ONLY.
 
 The reference (zhry915/icml) has no code for this variant: its SSM (train_singlemamba_optimized.py:
-88-124) has no in_proj/out_proj, no convolution, no gate and a shared A.  The benchmark
-configurations of this build nevertheless describe the standard Mamba mixer (Gu & Dao, "Mamba:
+88-124) has no in_proj/out_proj, no convolution, no gate and a shared A.  The 8-layer
+d_inner-512 and 24-layer d_model-1024 LM configurations describe the standard Mamba mixer (Gu & Dao, "Mamba:
 Linear-Time Sequence Modeling with Selective State Spaces", 2023, Algorithm 2 / Section 3.4):
 
     xz = x W_in^T                      (2E outputs, no bias); xi, z = xz[:E], xz[E:]
