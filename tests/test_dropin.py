@@ -111,3 +111,24 @@ def test_projection_weights_adjacent_view():
     assert torch.equal(W, ref_W) and torch.equal(b, ref_b)
     assert W.untyped_storage().data_ptr() == flat.untyped_storage().data_ptr()
     assert b.untyped_storage().data_ptr() == flat.untyped_storage().data_ptr()
+
+
+def test_layer_stash_policies():
+    """The stash policies the LM accepts; tensors that stay on their device come back as they were
+    put, and each slot is released when taken."""
+    import pytest
+    from icml_b200.lm import LayerStash
+    for bad in ("gpu", "", "Host"):
+        with pytest.raises(ValueError):
+            LayerStash(bad)
+    for policy in ("device", "host", "scan"):
+        st = LayerStash(policy)
+        st.begin(3)
+        xs = [torch.randn(2, 5) for _ in range(3)]  # CPU tensors never go through the copy stream
+        for i, x in enumerate(xs):
+            st.put(i, x)
+        for i in reversed(range(3)):
+            if i > 0:
+                st.prefetch(i - 1, "cpu")
+            assert st.take(i, "cpu") is xs[i]
+            assert st.items[i] is None
