@@ -2,15 +2,17 @@
 
 Workload (default): the 8-layer PGF Mamba language model of the reference's training scripts at
 d_model 256 / d_state 16 / d_ff 1024 / vocab 50257 (reference SSM variant, untied embedding and
-LM head as in train_wikitext_rebuttal.py:58-77), one sequence of L tokens per GPU, synthetic
-Zipf(1.1) token ids, bf16 activations, fp32 weights and AdamW.  On N GPUs (one process each) the
-default shards ONE sequence of N x L tokens across the GPUs (segment state hand-off through small
-all-gathers, one gradient all-reduce); --parallel dp runs N independent sequences instead.  Either
-way the per-GPU work is fixed (weak scaling).
+LM head as in train_wikitext_rebuttal.py:58-77), ONE sequence of L = 1,048,576 tokens with PGF
+block size 4096, synthetic Zipf(1.1) token ids, bf16 activations, fp32 weights and AdamW.  On N GPUs
+(one process each) the default shards that one sequence across the GPUs (contiguous segments,
+boundary-state hand-off between segments, one gradient all-reduce): the total work is fixed (strong
+scaling).  --parallel dp runs one such sequence per GPU instead (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--seq-len L] [--impl b200|reference]
 
-Prints one JSON line on rank 0.
+--impl reference times the reference's PGF step restated on the CPU (the oracle, float32, all host
+threads) on a bounded prefix of the same sequence (--cpu-sample-len tokens, same model and block
+size), K steps after W warm-ups.  Prints one JSON line on rank 0.
 """
 from __future__ import annotations
 
@@ -40,7 +42,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--seq-len", type=int, default=65536)
+    ap.add_argument("--seq-len", type=int, default=1048576,
+                    help="tokens of one sequence (sp: the one sequence sharded over the GPUs; dp: one per GPU)")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--d-model", type=int, default=256)
@@ -49,7 +52,8 @@ def parse():
     ap.add_argument("--vocab", type=int, default=50257)
     ap.add_argument("--block-size", type=int, default=4096)
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
-    ap.add_argument("--cpu-sample-len", type=int, default=1024)
+    ap.add_argument("--cpu-sample-len", type=int, default=2048,
+                    help="tokens of the sequence prefix one CPU step processes (reference arm, cpu_baseline)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--variant", default="reference", choices=["reference", "std"],
                     help="reference: the reference's SSM block (d_inner = d_model); std: the Mamba-standard "
@@ -64,22 +68,37 @@ def parse():
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of the CUDA-graph captured step (1 GPU)")
     ap.add_argument("--parallel", default="sp", choices=["sp", "dp"],
-                    help="N>1: sp = one sequence of N x seq-len tokens sharded across the GPUs "
-                         "(state hand-off between segments), dp = N independent sequences")
+                    help="N>1: sp = the one sequence of seq-len tokens sharded across the GPUs (state "
+                         "hand-off between segments; strong scaling), dp = one sequence per GPU (weak)")
     return ap.parse_args()
+
+
+def per_rank_len(a, world):
+    """Tokens of the sequence each rank holds: its segment (sp) or its own sequence (dp)."""
+    if world > 1 and a.parallel == "sp":
+        if a.seq_len % world:
+            raise SystemExit(f"--seq-len {a.seq_len} must split evenly over {world} GPUs")
+        return a.seq_len // world
+    return a.seq_len
+
+
+def scaling_of(a, world):
+    return "strong" if a.parallel == "sp" else "weak"
 
 
 def config_of(a, world):
     var = ("reference SSM variant" if a.variant == "reference" else
            f"Mamba-standard variant (d_inner {2 * a.d_model}, d_conv 4, dt_rank {a.dt_rank}, final RMSNorm, "
            f"tied head)")
+    seqs = a.batch * (world if a.parallel == "dp" else 1)
+    where = (f"one sequence per GPU" if a.parallel == "dp" else
+             (f"sharded over {world} GPUs ({a.seq_len // world} tokens each)" if world > 1 else "on one GPU"))
     return {
         "workload": f"{a.layers}-layer PGF Mamba LM ({var}), d_model {a.d_model}, d_state 16, d_ff {a.d_ff}, "
-                    f"vocab {a.vocab}, B={a.batch} x L={a.seq_len} tokens per GPU, {a.dtype} activations / "
-                    f"fp32 weights + AdamW",
+                    f"vocab {a.vocab}, B={a.batch} x L={a.seq_len} tokens {where}, PGF block {a.block_size}, "
+                    f"{a.dtype} activations / fp32 weights + AdamW",
         "layers": a.layers, "d_model": a.d_model, "d_state": 16, "d_ff": a.d_ff, "vocab": a.vocab,
-        "global_batch": a.batch * (world if a.parallel == "dp" else 1),
-        "seq_len": a.seq_len * (world if a.parallel == "sp" else 1), "pgf_block_size": a.block_size,
+        "global_batch": seqs, "seq_len": a.seq_len, "pgf_block_size": a.block_size,
         "parallelism": f"{a.parallel}{world}",
         "ssm_variant": ("reference (d_inner = d_model, shared A)" if a.variant == "reference" else
                         "mamba-standard (d_inner 2 d_model, conv1d, gate, per-channel A)"),
@@ -143,43 +162,67 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_baseline(a, kind="port"):
-    """The oracle (CPU restatement of the reference PGF step, float32, all host threads) on a
-    bounded sample of the workload: the same model at L = cpu_sample_len tokens."""
-    from oracle import pgf_oracle as O
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(0)
-    blocks = [O.block_init(a.d_model, 16, a.d_ff, g) for _ in range(a.layers)]
-    emb = torch.randn(a.vocab, a.d_model, generator=g) * 0.02
-    lmw = torch.randn(a.vocab, a.d_model, generator=g) * 0.02
-    L = a.cpu_sample_len
-    ids = O.zipf_tokens(L + 1, a.vocab, generator=g).reshape(1, L + 1)
-    bs = min(a.block_size, 128)
-    O.lm_pgf_step(emb, lmw, blocks, ids[:, :-1], ids[:, 1:], bs)  # warm-up
-    times = []
-    t_end = time.time() + 20.0
-    while len(times) < 3 and (not times or time.time() < t_end):
-        t0 = time.perf_counter()
-        O.lm_pgf_step(emb, lmw, blocks, ids[:, :-1], ids[:, 1:], bs)
-        times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
-    return {"value": L / med, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
-            "sample": f"oracle PGF step (fp32, no optimizer) of the same 8-layer model on B=1 x L={L} "
-                      f"tokens, pgf block {bs}, median of {len(times)} steps after 1 warm-up, "
-                      f"{threads} host threads"}
+class CpuStep:
+    """The oracle (CPU restatement of the reference's PGF LM step, float32, all host threads) on a
+    bounded prefix of the benchmark sequence: the same model, vocabulary and PGF block size, the
+    first cpu_sample_len tokens."""
+
+    def __init__(self, a):
+        from oracle import pgf_oracle as O
+        self.O = O
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        g = torch.Generator().manual_seed(0)
+        self.blocks = [O.block_init(a.d_model, 16, a.d_ff, g) for _ in range(a.layers)]
+        self.emb = torch.randn(a.vocab, a.d_model, generator=g) * 0.02
+        self.lmw = torch.randn(a.vocab, a.d_model, generator=g) * 0.02
+        self.L = a.cpu_sample_len
+        ids = zipf_ids(self.L + 1, a.vocab, seed=100).reshape(1, self.L + 1)
+        self.x, self.y = ids[:, :-1], ids[:, 1:]
+        self.bs = a.block_size
+
+    def __call__(self):
+        self.O.lm_pgf_step(self.emb, self.lmw, self.blocks, self.x, self.y, self.bs)
+
+    def sample(self, steps, warmup):
+        return (f"the oracle's PGF step (fp32, no optimizer) of the same {len(self.blocks)}-layer model on the first "
+                f"{self.L} tokens of the sequence (PGF block {self.bs}), {steps} timed steps after {warmup} warm-up, "
+                f"{self.threads} host threads")
+
+
+def cpu_baseline(a, kind="port", steps=3, warmup=1):
+    """Bounded CPU sample (about 10-30 s of host work) reported beside the GPU arm."""
+    st = CpuStep(a)
+    for _ in range(warmup):
+        st()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        st()
+    dt = time.perf_counter() - t0
+    return {"value": st.L * steps / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
+            "sample": st.sample(steps, warmup)}
 
 
 def run_reference(a, rank, world):
+    """The reference arm: K timed CPU steps (after W warm-ups) of the bounded sample, rank 0 only."""
     if rank != 0:
         return
-    cb = cpu_baseline(a)
-    line = {"metric": metric_of(a), "value": cb["value"], "unit": UNIT, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": 1000.0 * a.cpu_sample_len / cb["value"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference", "config": config_of(a, world),
+    st = CpuStep(a)
+    for _ in range(a.warmup):
+        st()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        st()
+    dt = time.perf_counter() - t0
+    value = st.L * a.steps / dt
+    cb = {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+          "sample": st.sample(a.steps, a.warmup)}
+    line = {"metric": metric_of(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": 1000.0 * dt / max(a.steps, 1),
+            "higher_is_better": True, "scaling": scaling_of(a, world), "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (Zipf 1.1 token ids, random init)", "impl": "reference", "config": config_of(a, world),
             "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -412,12 +455,13 @@ def run_gpu(a, rank, world, local_rank):
         if pg is not None:
             torch.distributed.broadcast(p.data, 0)
 
+    Lr = per_rank_len(a, world)
     if world > 1 and a.parallel == "sp":
-        # one sequence of world x seq_len tokens; this rank holds the segment [rank*L, (rank+1)*L)
-        full = zipf_ids(a.batch * (a.seq_len * world + 1), a.vocab, seed=100).reshape(a.batch, -1)
-        ids_host = full[:, rank * a.seq_len: (rank + 1) * a.seq_len + 1]
+        # the one sequence; this rank holds the segment [rank*Lr, (rank+1)*Lr)
+        full = zipf_ids(a.batch * (a.seq_len + 1), a.vocab, seed=100).reshape(a.batch, -1)
+        ids_host = full[:, rank * Lr: (rank + 1) * Lr + 1]
     else:
-        ids_host = zipf_ids(a.batch * (a.seq_len + 1), a.vocab, seed=100 + rank).reshape(a.batch, a.seq_len + 1)
+        ids_host = zipf_ids(a.batch * (Lr + 1), a.vocab, seed=100 + rank).reshape(a.batch, Lr + 1)
     inp_host = ids_host[:, :-1].contiguous().pin_memory()
     tgt_host = ids_host[:, 1:].contiguous().pin_memory()
     inp = inp_host.to(dev)
@@ -547,7 +591,7 @@ def run_gpu(a, rank, world, local_rank):
         torch.distributed.all_reduce(t_all, op=torch.distributed.ReduceOp.MAX)
     ms = t_all.item()
     ms_step = ms / a.steps
-    tokens = a.batch * a.seq_len * world * a.steps
+    tokens = a.batch * Lr * world * a.steps
     value = tokens / (ms / 1e3)
 
     # ---------------- end to end: host ids -> device each step, loss read back each step
@@ -582,7 +626,7 @@ def run_gpu(a, rank, world, local_rank):
                    for k in prof_ms}
         line = {
             "metric": metric_of(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling_of(a, world),
             "vs_baseline": None, "dtype": a.dtype, "data": "synthetic (Zipf 1.1 token ids, random init)",
             "config": dict(config_of(a, world), launch=(
                 "whole step (with its collectives) captured once as a CUDA graph, replayed each step"

@@ -571,7 +571,8 @@ static int ce_fwd_tc(const void* h, const float* W, const int64_t* targets, floa
   Gemm g = mk(T, V, d, h, 1, d, 0, Wb, 1, d, 0, nullptr, 0, 0);
   if (!tc_usable(g)) return PGF_ERR_UNSUPPORTED;
   PGF_TRY(to_bf16(W, Wb, V * d, s));
-  PGF_CUDA(cudaMemsetAsync(tg, 0, size_t(T) * 4, s));
+  // all-ones bytes = NaN: a row whose target lies outside [0, V) is never written and gets a NaN loss
+  PGF_CUDA(cudaMemsetAsync(tg, 0xFF, size_t(T) * 4, s));
   int ngo = 0;
   PGF_TRY(tc_ce_fwd(g, CE_NG, targets, pm, ps, tg, &ngo, s));
   ce_combine_kernel<<<ceil_div(T, 256), 256, 0, s>>>(pm, ps, tg, T, ngo, loss_rows, lse);
@@ -656,6 +657,7 @@ extern "C" int pgf_lm_head_ce_fwd(const void* h, const float* W, const int64_t* 
   for (int64_t r = 0; r < T; r += tr) {
     const int64_t m = T - r < tr ? T - r : tr;
     const char* ht = static_cast<const char*>(h) + r * d * es;
+    PGF_CUDA(cudaMemsetAsync(c.tgt, 0xFF, size_t(m) * 4, s));  // NaN loss for a target outside [0, V)
     for (int64_t v0 = 0; v0 < V; v0 += CE_VT) {
       const int64_t nv = V - v0 < CE_VT ? V - v0 : CE_VT;
       const int64_t ldt = (nv + 63) / 64 * 64;  // 128-byte aligned tile pitch (TMA operand rule)

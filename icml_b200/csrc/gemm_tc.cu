@@ -423,7 +423,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               run_s = run_s * ex2f((run_m - m1) * L2E) + (s0 + s1);
               run_m = m1;
             }
-            if (tgt >= nc && tgt < nc + 32) {
+            if (tgt >= nc && tgt < nc + 32 && tgt < p.N) {  // a target >= N stays unwritten (NaN loss)
               float v = 0.f;
 #pragma unroll
               for (int j = 0; j < 32; ++j)

@@ -573,42 +573,32 @@ extern "C" int pgf_rmsnorm_bwd_add(const void* x, const void* g, const float* we
 // device memory and forbids allocation from its operators, or a latency-critical loop that must
 // not enter the allocator.  The grad-weight partials live in the file-scope array below instead
 // of a workspace: NOALLOC_RMS_FLOATS floats (4 MiB), held by every GPU that loads this library
-// until the process exits.  A call needs ceil(rows / 32) * dim of them.
+// until the process exits.  A call needs ceil(rows / 32) * dim of them, and dim <= 4096.
 //
 // The host cannot pass the array's name to a kernel (in host code it is only a stand-in for the
-// device symbol): the first call on each device, with that device current, looks up the device
-// address with cudaGetSymbolAddress and caches it.  Make that first call before any stream
-// capture.  Every call overwrites all the partial slots it reads, so nothing needs clearing, but
-// the calls share the one array: calls that overlap on the GPU (other streams, other threads)
-// race on it and must be serialised by the caller.
+// device symbol): every call looks up the array's device address with cudaGetSymbolAddress in the
+// calling thread's current context, so the address always belongs to the context the kernel runs
+// in (a non-primary context, or a primary context re-created after cudaDeviceReset, included).  The
+// lookup is a table read once the library's module is loaded in that context; the first call in a
+// context may load it, so make that first call before any stream capture.  Every call overwrites
+// all the partial slots it reads, so nothing needs clearing, but the calls share the one array:
+// calls that overlap on the GPU (other streams, other threads) race on it and must be serialised
+// by the caller.
 // ---------------------------------------------------------------------------------------------
-#include <mutex>
-
 namespace pgf {
 
 constexpr size_t NOALLOC_RMS_FLOATS = size_t(1) << 20;
 static __device__ __align__(256) float g_rms_noalloc_scratch[NOALLOC_RMS_FLOATS];
 
-constexpr int NOALLOC_MAX_DEVICES = 64;
-static std::mutex g_noalloc_mu;
-static float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
-
-// Device address of the scratch array on the current device (looked up once per device).
+// Device address of the scratch array in the current context.
 static int noalloc_scratch(float** out) {
-  int dev = 0;
-  PGF_CUDA(cudaGetDevice(&dev));
-  PGF_CHECK_ARG(dev >= 0 && dev < NOALLOC_MAX_DEVICES, "rmsnorm_bwd_noalloc: device %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_rms_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      set_error("rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-      return PGF_ERR_CUDA;
-    }
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_rms_noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    set_error("rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    return PGF_ERR_CUDA;
   }
-  *out = g_noalloc_ptr[dev];
+  *out = static_cast<float*>(p);
   return PGF_OK;
 }
 

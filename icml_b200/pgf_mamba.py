@@ -3,9 +3,10 @@ PGF forward computes the sequence output and its directional derivative (JVP) on
 kernels (pgf_frechet_jvp: chunked scan of the (state, tangent) pair; float32).
 
 Same module, class, method and parameter names as the reference, constructed in the same order,
-so a seeded construction gives the reference's initial weights.  ``mamba_discretization``,
-``tiled_parallel_scan`` and ``mamba_atomic_step`` are kept for import compatibility as plain torch
-helpers; they are not on the operator's path.
+so a seeded construction gives the reference's initial weights.  The reference's two module-level
+torch helpers (its phi_1 discretisation and log-shifted cumsum scan, pgf_mamba.py:7-31) are not
+provided: nothing outside that file calls them, and here the scan kernels do that work.
+``mamba_atomic_step`` (one token) runs the same kernels as ``pgf_forward`` on a one-token sequence.
 """
 from __future__ import annotations
 
@@ -13,23 +14,8 @@ from typing import Callable, Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import ops
-
-
-def mamba_discretization(z: torch.Tensor) -> torch.Tensor:
-    """pgf_mamba.py:7-12: expm1(z) / (z + 1e-9)."""
-    return torch.expm1(z) / (z + 1e-9)
-
-
-def tiled_parallel_scan(dA: torch.Tensor, Bu: torch.Tensor, h0: torch.Tensor) -> torch.Tensor:
-    """pgf_mamba.py:15-31: h_t = dA_t h_{t-1} + Bu_t over the leading axis, log-shifted cumsum form."""
-    log_dA = torch.log(dA + 1e-12)
-    Lam = torch.cumsum(log_dA, dim=0)
-    m, _ = torch.max(Lam, dim=0, keepdim=True)
-    C_t = torch.cumsum(Bu * torch.exp(m - Lam), dim=0)
-    return h0.unsqueeze(0) * torch.exp(Lam) + torch.exp(Lam - m) * C_t
 
 
 class FrechetMambaOperator(nn.Module):
@@ -104,18 +90,17 @@ class FrechetMambaOperator(nn.Module):
         y, _ = self.pgf_forward(u_seq, torch.zeros_like(u_seq))
         return y
 
+    @torch.no_grad()
     def mamba_atomic_step(self, u_t, h_prev, params):
-        """pgf_mamba.py:151-163, one token in plain torch."""
-        dt = F.softplus(F.linear(u_t, params["dt_w"], params["dt_b"]))
-        B = F.linear(u_t, params["B_w"], params["B_b"])
-        C = F.linear(u_t, params["C_w"], params["C_b"])
-        A = -torch.exp(params["A_log"])
-        dtA = dt.unsqueeze(-1) * A.unsqueeze(0)
-        dA = torch.exp(dtA)
-        dB = mamba_discretization(dtA) * B.unsqueeze(0)
-        h_curr = dA * h_prev + dB * u_t.unsqueeze(-1)
-        y_raw = torch.einsum("n,dn->d", C, h_curr) + params["D_w"] * u_t
-        return F.softplus(y_raw) * torch.clamp(params["scale"], min=0.5), h_curr
+        """One token from state h_prev (pgf_mamba.py:151-163): (y_t, h_t), computed as a one-token
+        sequence by the scan kernels of pgf_forward (CUDA tensors)."""
+        W = torch.cat([params["dt_w"], params["B_w"], params["C_w"]], 0).detach()
+        b = torch.cat([params["dt_b"], params["B_b"], params["C_b"]], 0).detach()
+        u = u_t.detach().float().reshape(1, -1)
+        h0 = h_prev.detach().float()
+        y, _, h, _ = ops.frechet_jvp(u, torch.zeros_like(u), W, b, params["A_log"], params["D_w"], params["scale"],
+                                     h0, torch.zeros_like(h0), want_state=True)
+        return y[0], h
 
 
-__all__ = ["FrechetMambaOperator", "mamba_discretization", "tiled_parallel_scan"]
+__all__ = ["FrechetMambaOperator"]

@@ -105,8 +105,11 @@ int pgf_rmsnorm_bwd_add(const void* x, const void* g, const float* weight, const
  * owns all device memory and forbids allocation from its operators, or a loop that must not enter
  * the allocator).  No counterpart in the reference, which has no native layer.  Scratch is a 4 MiB
  * static device array inside libpgf.so instead of `ws`: the call is rejected (PGF_ERR_INVALID) when
- * ceil(rows/32)*dim > 1048576.  Its first call on a device looks the array up (make it before any
- * stream capture).  All calls share the array: calls that overlap on the GPU race; serialise them. */
+ * dim > 4096 or ceil(rows/32)*dim > 1048576.  Each call looks up the array's address in the calling
+ * thread's current CUDA context (the address belongs to that context); the first call in a context
+ * may load the library's device code, so make it before any stream capture.  rows = 0 sets
+ * grad_weight to zero (leaves it unchanged with accumulate).  All calls share the array: calls that
+ * overlap on the GPU race; serialise them. */
 int pgf_rmsnorm_bwd_noalloc(const void* x, const void* g, const float* weight,
                             void* grad_x /* nullable */, float* grad_weight, int accumulate,
                             int64_t rows, int64_t dim, float eps, int dtype, pgf_stream_t stream);
@@ -214,7 +217,9 @@ int pgf_lm_head_bwd(const void* h, const float* g_logits, const float* W, float*
  * train_wikitext_rebuttal.py:116-125, tiled over tokens and vocabulary: the (T x V) logits and
  * their gradient exist only one (token tile x vocab tile) at a time.
  *   fwd: loss_rows[t] = lse_t - logit[t, target_t], lse[t] = logsumexp_v logit[t, v].
- *   bwd: g = (softmax - onehot(target)) * grad_scale; grad_W (+)= g^T h; grad_h = g W. */
+ *   bwd: g = (softmax - onehot(target)) * grad_scale; grad_W (+)= g^T h; grad_h = g W.
+ * A target outside [0, V) gives that row a NaN loss (the reference's F.cross_entropy raises; these
+ * calls do not synchronise to report it). */
 size_t pgf_lm_head_ce_workspace(int64_t T, int64_t V, int64_t d, int dtype);
 int pgf_lm_head_ce_fwd(const void* h, const float* W, const int64_t* targets, float* loss_rows,
                        float* lse, int64_t T, int64_t V, int64_t d, int dtype, void* ws,

@@ -1,10 +1,11 @@
 """Generate the golden fixtures in this folder from the reference implementation itself.
 
-Run in a container where the reference (zhry915/icml, pure Python) is mounted read-only:
+Run where a checkout of the reference (zhry915/icml, pure Python) is readable; its directory is
+a required argument:
 
-    python tests/golden/make_golden.py /root/reference          # every fixture
-    python tests/golden/make_golden.py /root/reference jvp      # jvp.pt only
-    python tests/golden/make_golden.py /root/reference hvp      # hvp.pt only
+    python tests/golden/make_golden.py REF_DIR          # every fixture
+    python tests/golden/make_golden.py REF_DIR jvp      # jvp.pt only
+    python tests/golden/make_golden.py REF_DIR hvp      # hvp.pt only
 
 The reference is imported as-is with two adjustments, both applied from the outside:
 * ``TORCHDYNAMO_DISABLE=1`` so ``pgf_lm_head``'s ``torch.compile`` wrapper runs eagerly on the CPU;
@@ -290,7 +291,104 @@ def gen_hvp(R):
     return out
 
 
-def main(ref_path="/root/reference", only=None):
+def gen_multilayer(R, n_layers=2):
+    """test_multi_layer_grads.py:10-126 as the reference runs it (seed 1, B=2, L=512, d_model=64,
+    d_state=16, d_ff=128, block_size=128, vocab 1000), at its smallest layer count, on the CPU: the
+    weights, the PGF gradients of every parameter and the autograd gradients."""
+    torch.manual_seed(1)
+    B, L, d, N, dff, bs, V = 2, 512, 64, 16, 128, 128, 1000
+    ids = torch.randint(0, V, (B, L))
+    tg = torch.randint(0, V, (B, L))
+    emb = torch.randn(V, d)
+    lmw = torch.randn(V, d)
+    seq = R["blk"].PGFMambaSequential([R["blk"].PGFMambaBlock(d, N, dff, bs) for _ in range(n_layers)])
+    params = _sd(seq)
+    # PGF path (:89-126)
+    h = R["emb"].pgf_embedding_forward(ids, emb, bs)
+    inputs, cur = [], h
+    for layer in seq.layers:
+        inputs.append(cur.detach().clone())
+        cur = layer.pgf_forward(cur)
+    lf = R["lm"].pgf_lm_head_forward(cur.view(-1, d), lmw, bs).view(-1, V)
+    loss = F.cross_entropy(lf, tg.view(-1))
+    gl = F.softmax(lf, dim=-1).clone()
+    gl[torch.arange(gl.size(0)), tg.view(-1)] -= 1.0
+    gl /= lf.size(0)
+    lres = R["lm"].pgf_lm_head_grad(cur.view(-1, d), gl, lmw, bs, compute_input_grads=True)
+    g = lres["grad_hidden"].view(B, L, d)
+    grads = {"lm_head": lres["grad_W_lm_head"].clone()}
+    for i in reversed(range(n_layers)):
+        r = seq.layers[i].pgf_backward(inputs[i], g)
+        for k, v in r["grads"].items():
+            grads[f"layers.{i}.{k}"] = v.clone()
+        g = r["grad_input"]
+    grads["emb"] = R["emb"].pgf_embedding_grad(ids, g, emb, bs)["grad_weight"].clone()
+    # autograd path (:57-68)
+    emb_a = emb.clone().requires_grad_(True)
+    lm_a = lmw.clone().requires_grad_(True)
+    x = F.embedding(ids, emb_a)
+    for layer in seq.layers:
+        x = layer.forward(x)
+    la = F.cross_entropy((x @ lm_a.t()).view(-1, V), tg.view(-1))
+    la.backward()
+    ag = {"emb": emb_a.grad.clone(), "lm_head": lm_a.grad.clone()}
+    for k, p in seq.named_parameters():
+        ag[k] = p.grad.clone()
+    return {"ids": ids, "targets": tg, "emb": emb, "lm_head": lmw, "params": params, "n_layers": n_layers,
+            "d_ff": dff, "block_size": bs, "loss": loss.detach(), "grads": grads,
+            "autograd": {"loss": la.detach(), "grads": ag}}
+
+
+def gen_train_steps(R):
+    """SingleLayerMambaPGF.pgf_train_step (train_singlemamba_optimized.py:474-561: MSE target, two
+    block passes, writes .grad, steps the optimizer) and PGFMambaSequential.pgf_train_step
+    (pgf_mamba_block.py:290-322) with an MSE loss_fn, plus autograd of the same losses."""
+    out = {}
+    torch.manual_seed(51)
+    B, L, d, N, bs, lr = 2, 72, 24, 16, 32, 0.05
+    m = R["tso"].SingleLayerMambaPGF(d, N)
+    with torch.no_grad():
+        m.scale.mul_(torch.rand(d) + 0.5)
+        m.D.mul_(torch.rand(d) + 0.5)
+    u = torch.randn(B, L, d)
+    target = torch.randn(B, L, d)
+    p0 = _sd(m)
+    # autograd of the same MSE loss through forward_standard (the truth for the per-channel scale)
+    ua = u.clone()
+    ya = m.forward_standard(ua)
+    la = ((ya - target) ** 2).mean()
+    la.backward()
+    ag = {k: p.grad.detach().clone() for k, p in m.named_parameters()}
+    m.zero_grad(set_to_none=True)
+    opt = torch.optim.SGD(m.parameters(), lr=lr)
+    loss = m.pgf_train_step(u, target, opt, bs)
+    out["single"] = {"params": p0, "u": u, "target": target, "block_size": bs, "lr": lr, "loss": loss,
+                     "grads": {k: p.grad.detach().clone() for k, p in m.named_parameters()},
+                     "params_after": _sd(m), "autograd": {"loss": la.detach(), "grads": ag}}
+    torch.manual_seed(52)
+    B, L, d, N, dff, bs, nl = 2, 80, 32, 16, 64, 32, 3
+    seq = R["blk"].PGFMambaSequential([R["blk"].PGFMambaBlock(d, N, dff, bs) for _ in range(nl)])
+    x = torch.randn(B, L, d)
+    target = torch.randn(B, L, d)
+
+    def mse(o, tg):
+        diff = o - tg
+        return (diff * diff).mean(), 2.0 * diff / diff.numel()
+
+    p0 = _sd(seq)
+    r = seq.pgf_train_step(x, target, mse)
+    xa = x.clone().requires_grad_(True)
+    la = ((seq(xa) - target) ** 2).mean()
+    la.backward()
+    out["sequential"] = {"params": p0, "x": x, "target": target, "n_layers": nl, "d_ff": dff, "block_size": bs,
+                         "loss": r["loss"].detach().clone(),
+                         "grads": {k: v.detach().clone() for k, v in r["grads"].items()},
+                         "autograd": {"loss": la.detach(),
+                                      "grads": {k: p.grad.detach().clone() for k, p in seq.named_parameters()}}}
+    return out
+
+
+def main(ref_path, only=None):
     R = _import_reference(ref_path)
     torch.set_num_threads(1)
     if only == "jvp":
@@ -300,6 +398,11 @@ def main(ref_path="/root/reference", only=None):
     if only == "hvp":
         torch.save(gen_hvp(R), os.path.join(HERE, "hvp.pt"))
         print("golden fixture hvp.pt written to", HERE)
+        return
+    if only == "train_step":
+        torch.save(gen_train_steps(R), os.path.join(HERE, "train_step.pt"))
+        torch.save(gen_multilayer(R), os.path.join(HERE, "multilayer.pt"))
+        print("golden fixtures train_step.pt and multilayer.pt written to", HERE)
         return
     torch.save(gen_ssm_block(R), os.path.join(HERE, "ssm_block.pt"))
     torch.save({"none": gen_ssm_autograd(R, None), "tanh": gen_ssm_autograd(R, "tanh")},
@@ -311,8 +414,12 @@ def main(ref_path="/root/reference", only=None):
     torch.save(gen_init(R), os.path.join(HERE, "init.pt"))
     torch.save(gen_jvp(R), os.path.join(HERE, "jvp.pt"))
     torch.save(gen_hvp(R), os.path.join(HERE, "hvp.pt"))
+    torch.save(gen_train_steps(R), os.path.join(HERE, "train_step.pt"))
+    torch.save(gen_multilayer(R), os.path.join(HERE, "multilayer.pt"))
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2] if len(sys.argv) > 2 else None)
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py REF_DIR [jvp|hvp|train_step]")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

@@ -288,6 +288,24 @@ def test_lm_head_ce_bf16_fused(ops, T, V, d):
     assert lib().pgf_tc_fault() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_lm_head_ce_out_of_range_target_gives_nan_loss(ops, dtype):
+    """A target outside [0, V) leaves its row's target logit unset: that row's loss is NaN (the
+    reference's F.cross_entropy raises); every other row is unaffected."""
+    g = _gen(23)
+    T, V, d = 256, 50257, 64
+    h = torch.randn(T, d, generator=g).to(dtype)
+    W = 0.3 * torch.randn(V, d, generator=g)
+    tg = torch.randint(0, V, (T,), generator=g)
+    bad = tg.clone()
+    bad[3], bad[100], bad[200] = -1, V, V + 5
+    lr_ok, _ = ops.lm_head_ce_fwd(h.to(DEV), W.to(DEV), tg.to(DEV))
+    lr_bad, _ = ops.lm_head_ce_fwd(h.to(DEV), W.to(DEV), bad.to(DEV))
+    nan = torch.isnan(lr_bad.cpu())
+    assert nan.tolist() == [i in (3, 100, 200) for i in range(T)]
+    assert torch.equal(lr_bad.cpu()[~nan], lr_ok.cpu()[~nan])
+
+
 # ----------------------------------------------------------------------------- selective scan
 def _ssm_case(Bsz, L, D, seed, carries=True):
     g = _gen(seed)
