@@ -503,7 +503,10 @@ def test_ssm_save_from_boundary_states(ops, act, dtype):
     rb = ops.ssm_bwd(u, gy, W, b, A, Dp, sc, act=act, saved=sb)
     for k in ("grad_u", "A_log", "D", "scale", "W_cat", "b_cat"):
         ref = ra[k].float()
-        assert (rb[k].float() - ref).abs().max().item() <= 1e-5 + 1e-4 * ref.abs().max().item(), k
+        # grad_u is a bf16 tensor in bf16 runs: the two saved forms differ in float32 rounding, which
+        # may flip a bf16 rounding, so there the bound is one bf16 ulp at the tensor's largest value
+        rt = 2.0 ** -8 if (k == "grad_u" and dtype == torch.bfloat16) else 1e-4
+        assert (rb[k].float() - ref).abs().max().item() <= 1e-5 + rt * ref.abs().max().item(), k
 
 
 @pytest.mark.parametrize("act", [None, "relu"])
