@@ -199,6 +199,121 @@ __device__ __forceinline__ void pref_store(const Pref& r, const Lane& l, bool bw
   }
 }
 
+// Untransformed inputs of one backward sub-chunk, copied global -> shared by cp.async in 16-byte
+// pieces two sub-chunks ahead of their use, so that no thread holds them in registers or waits for
+// them: projection columns dt_in and [B | C], u and g (bf16 rows fill the first half of each row),
+// act'(C h) with an output activation, and the forward's checkpoint (h0, S) of the 64 channels.
+struct Raw {
+  float dtin[ST][DC];
+  float bc[ST][32];
+  float u[ST][DC];
+  float g[ST][DC];
+  float ap[ST][DC];
+  float ckh[DC * NST];
+  float cks[DC];
+};
+
+__device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Issue the copies of sub-chunk k into R (every thread takes every 256th 16-byte piece).  Pieces of
+// tokens past the chunk or channels past D are zero-filled (nothing is read for them).  Needs D a
+// multiple of 8 and 16-byte aligned rows (the host checks).
+__device__ __forceinline__ void raw_issue(const SsmArgs& a, const Lane& l, int k, Raw& R) {
+  const int es = a.u_bf16 ? 2 : 4;
+  const int pu = DC * es / 16;                      // pieces per token row of u (and of g)
+  const int n_dt = ST * 16, n_bc = ST * 8, n_u = ST * pu, n_ap = a.actp ? ST * 16 : 0;
+  const int n_ck = a.ckpt_g ? DC * NST / 4 + DC / 4 : 0;
+  const int total = n_dt + n_bc + 2 * n_u + n_ap + n_ck;
+  const int64_t t0 = l.s + int64_t(k) * ST, c0 = int64_t(l.grp) * DC;
+  const int KS = int((a.Tc + ST - 1) / ST);
+  const int64_t ck = (l.b * a.nC + l.c) * KS + k;
+  for (int pc = l.tid; pc < total; pc += SSM_THREADS) {
+    int q = pc;
+    if (q < n_dt) {
+      const int t = q >> 4, c = (q & 15) * 4;
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e && c0 + c < a.D;
+      cp16(&R.dtin[t][c], v ? a.proj + (l.b * a.L + tok) * a.P + c0 + c : a.proj, v);
+      continue;
+    }
+    q -= n_dt;
+    if (q < n_bc) {
+      const int t = q >> 3, c = (q & 7) * 4;
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e;
+      cp16(&R.bc[t][c], v ? a.proj + (l.b * a.L + tok) * a.P + a.D + c : a.proj, v);
+      continue;
+    }
+    q -= n_bc;
+    if (q < 2 * n_u) {
+      const bool isg = q >= n_u;
+      if (isg) q -= n_u;
+      const int t = q / pu, c = (q % pu) * (16 / es);
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e && c0 + c < a.D;
+      const char* base = static_cast<const char*>(isg ? a.g : a.u);
+      float* dst = isg ? &R.g[t][0] : &R.u[t][0];
+      cp16(reinterpret_cast<char*>(dst) + c * es, v ? base + ((l.b * a.L + tok) * a.D + c0 + c) * es : base, v);
+      continue;
+    }
+    q -= 2 * n_u;
+    if (q < n_ap) {
+      const int t = q >> 4, c = (q & 15) * 4;
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e && c0 + c < a.D;
+      cp16(&R.ap[t][c], v ? a.actp + (l.b * a.L + tok) * a.D + c0 + c : a.actp, v);
+      continue;
+    }
+    q -= n_ap;
+    if (q < DC * NST / 4) {
+      const int c = q >> 2;  // channel; four pieces of four states each
+      const bool v = c0 + c < a.D;
+      cp16(&R.ckh[q * 4], v ? a.ckpt_g + (ck * a.D + c0) * NST + q * 4 : a.ckpt_g, v);
+      continue;
+    }
+    q -= DC * NST / 4;
+    {
+      const int c = q * 4;
+      const bool v = c0 + c < a.D;
+      cp16(&R.cks[c], v ? a.ckpt_s + ck * a.D + c0 + c : a.ckpt_s, v);
+    }
+  }
+  cp_commit();
+}
+
+// The stage of a backward sub-chunk from its raw inputs (the transform of pref_store); sc_ch is the
+// scale of the thread's write-out channel (the same channel for both of its slots).
+__device__ __forceinline__ void raw_store(const SsmArgs& a, const Raw& R, const Lane& l, float sc_ch, Stage& st) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * SSM_THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    const float x = R.dtin[t][dl];
+    const float uu = a.u_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.u[t][0])[dl]) : R.u[t][dl];
+    const float gg = a.g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.g[t][0])[dl]) : R.g[t][dl];
+    const float ap = a.actp ? R.ap[t][dl] : 1.f;
+    const float y = exp_neg_abs(x);
+    const float dt = softplus_from(x, y);
+    st.dt[t][dl] = dt;
+    st.rdt[t][dl] = rcpf(dt);
+    st.u[t][dl] = uu;
+    st.gg[t][dl] = gg;
+    st.dh[t][dl] = gg * sc_ch * ap;
+    st.rs[t][dl] = dt > 0.f ? sigmoid_from(x, y) * rcpf(dt) : 1.f;
+  }
+  const int t = l.tid >> 5, j = l.tid & 31;
+  if (t < ST) {
+    float* dst = j < NST ? reinterpret_cast<float*>(&st.B[t][0]) + j
+                         : reinterpret_cast<float*>(&st.C[t][0]) + (j - NST);
+    *dst = R.bc[t][j];
+  }
+}
+
 // One forward step of the thread's NS states (as pairs) on staged token i:
 // h = exp(dt A) h + phi_1(dt A) B u; returns phi_1(dt A) per state.
 template <bool OUT_E = false>
@@ -574,15 +689,21 @@ __global__ void __launch_bounds__(32 * CSEG) ssm_compose_bwd_kernel(const SsmArg
 //   w = delta_h z dh_t/dz = delta_h (z e^z h_{t-1} + (e^z - phi_1) B u)     (z phi_1'(z) = e^z - phi_1)
 // as grad A_log_n = sum w (dz/dA_log = z) and grad dt = sum_n w / dt (dz/ddt = A = z/dt), so phi_1'
 // is never formed.  Both passes step the thread's states as packed f32x2 pairs.
+//
+// ASYNC (saved checkpoints, D a multiple of 8, aligned rows): the inputs of each sub-chunk arrive by
+// cp.async into two Raw buffers after gbuf (see Raw), issued two sub-chunks ahead; otherwise they
+// are prefetched through registers one sub-chunk ahead.
+template <bool ASYNC>
 __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmArgs a) {
   extern __shared__ __align__(16) float sm[];
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const int KS = int((a.Tc + ST - 1) / ST);
-  const bool saved = a.ckpt_g != nullptr;  // checkpoints come from the forward output pass
+  const bool saved = ASYNC || a.ckpt_g != nullptr;  // checkpoints come from the forward output pass
   float* ckpt = sm;
   float* red = ckpt + (saved ? size_t(0) : size_t(KS) * SSM_THREADS * NS);
   float* gbuf = red + ST * SSM_WARPS * 32;  // [2][ST][DC]
+  Raw* raw = reinterpret_cast<Raw*>(gbuf + 2 * 2 * ST * DC);  // [2], ASYNC only
   const int lane = l.tid & 31, warp = l.tid >> 5;
   const AConst K = load_A(a, l.nq);
   // one forward step of the thread's state pairs on staged token i; p1o = phi_1(dt A) per state
@@ -638,20 +759,44 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
     ld_states(a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS, ck_h);
     ck_s = a.ckpt_s[ck * a.D + l.d];
   };
-  if (saved) ckpt_at(nsub - 1);
+  // ASYNC: the start state of the next sub-chunk to run, formed from its raw checkpoint when its
+  // stage is filled (the raw buffer is refilled before that sub-chunk runs)
+  float2 tr0n[NP] = {f2(0.f), f2(0.f)};
+  const float sc_ch = (int64_t(l.grp) * DC + l.tid % DC) < a.D ? a.scale[int64_t(l.grp) * DC + l.tid % DC] : 0.f;
+  auto fill = [&](int kk) {  // stage kk from raw buffer kk & 1 (ASYNC)
+    const Raw& R = raw[kk & 1];
+    raw_store(a, R, l, sc_ch, stg[kk & 1]);
+    const float4 q = *reinterpret_cast<const float4*>(&R.ckh[l.dl * NST + l.nq * NS]);
+    const float2 s2 = f2(R.cks[l.dl]);
+    tr0n[0] = l.ch ? fma2(ex2_2(mul2(K.A2[0], s2)), h[0], lo2(q)) : f2(0.f);
+    tr0n[1] = l.ch ? fma2(ex2_2(mul2(K.A2[1], s2)), h[1], hi2(q)) : f2(0.f);
+  };
+  if (!ASYNC && saved) ckpt_at(nsub - 1);
   float2 accA[NP] = {f2(0.f), f2(0.f)};
   float accD = 0.f, accS = 0.f;
   const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
-  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
-  pref_store(r, l, true, stg[(nsub - 1) & 1]);
-  __syncthreads();
+  if (ASYNC) {
+    raw_issue(a, l, nsub - 1, raw[(nsub - 1) & 1]);
+    cp_wait_all();
+    __syncthreads();
+    fill(nsub - 1);
+    __syncthreads();
+    if (nsub > 1) raw_issue(a, l, nsub - 2, raw[(nsub - 2) & 1]);
+  } else {
+    pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+    pref_store(r, l, true, stg[(nsub - 1) & 1]);
+    __syncthreads();
+  }
   for (int k = nsub - 1; k >= 0; --k) {
-    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    if (!ASYNC && k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
     const Stage& S = stg[k & 1];
     float* gb = gbuf + (k & 1) * (2 * ST * DC);
     // re-run the sub-chunk into registers: tr[i] = state before token i, ph[i] = phi_1(dt_i A)
     float2 tr[ST + 1][NP], ph[ST][NP];
-    if (saved) {
+    if (ASYNC) {
+      tr[0][0] = tr0n[0];
+      tr[0][1] = tr0n[1];
+    } else if (saved) {
       // zero-start checkpoint h0 of the forward (prefetched one sub-chunk ahead), moved onto the
       // chunk's start state h (= hC): state = h0 + exp(A S) h, S = sum of dt before this sub-chunk
       const float2 s2 = f2(ck_s);
@@ -732,8 +877,14 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
       const float send = b2 ? w2[0] : w2[1];
       red[(i * SSM_WARPS + warp) * 32 + lane] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
     }
-    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
-    __syncthreads();
+    if (ASYNC) {
+      if (k > 0) cp_wait_all();  // sub-chunk k-1's raw inputs (issued a sub-chunk ago) have landed
+      __syncthreads();
+      if (k > 0) fill(k - 1);
+    } else {
+      if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
+      __syncthreads();
+    }
     // grad B / grad C of the sub-chunk: sum over the CTA's warps, one partial per channel group
     {
       const int i = l.tid >> 5, ln = l.tid & 31;
@@ -764,6 +915,8 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
       }
     }
     __syncthreads();
+    // raw buffer (k - 2) & 1 held sub-chunk k, whose stage was filled a sub-chunk ago
+    if (ASYNC && k > 1) raw_issue(a, l, k - 2, raw[k & 1]);
   }
   // per-CTA parameter partials
   float* sA = sm;  // [SSM_THREADS][NS]; checkpoints are no longer needed
@@ -1169,12 +1322,23 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
                                                             nullptr);
   PGF_LAUNCH_CHECK();
   const int KS = int((p.Tc + ST - 1) / ST);
+  // cp.async staging: saved checkpoints, whole 16-byte pieces per row (D a multiple of 8) and
+  // 16-byte aligned bases
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool async = saved && D % 8 == 0 && al16(u) && al16(g) && al16(a.proj) && al16(a.ckpt_g) &&
+                     al16(a.ckpt_s) && (!a.actp || al16(a.actp));
   const size_t smem = ((saved ? size_t(0) : size_t(KS) * SSM_THREADS * NS) + size_t(ST) * SSM_WARPS * 32 +
-                       2 * 2 * ST * DC) * 4;
-  static int smem_limit = 0;
-  PGF_CUDA(ensure_dynamic_smem(ssm_main_bwd_kernel, smem, smem_limit));
+                       2 * 2 * ST * DC) * 4 + (async ? 2 * sizeof(Raw) : 0);
   prof_begin(PROF_SSM_MAIN_BWD, s);
-  ssm_main_bwd_kernel<<<grid, SSM_THREADS, smem, s>>>(a);
+  if (async) {
+    static int smem_limit_async = 0;
+    PGF_CUDA(ensure_dynamic_smem(ssm_main_bwd_kernel<true>, smem, smem_limit_async));
+    ssm_main_bwd_kernel<true><<<grid, SSM_THREADS, smem, s>>>(a);
+  } else {
+    static int smem_limit = 0;
+    PGF_CUDA(ensure_dynamic_smem(ssm_main_bwd_kernel<false>, smem, smem_limit));
+    ssm_main_bwd_kernel<false><<<grid, SSM_THREADS, smem, s>>>(a);
+  }
   prof_end(PROF_SSM_MAIN_BWD, s, bytes_main_bwd(a, a.u_bf16 ? 2 : 4));
   PGF_LAUNCH_CHECK();
   ssm_bc_reduce_kernel<<<ceil_div(int64_t(BL) * 32, 256), 256, 0, s>>>(a);
