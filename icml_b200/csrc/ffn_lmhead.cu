@@ -522,11 +522,16 @@ static int64_t ce_bwd_rows() {
 static int64_t ce_ngroups(int64_t V) { return 2 * (((V + 127) / 128 + CE_NG - 1) / CE_NG); }
 static int64_t ce_ldv(int64_t V) { return (V + 63) / 64 * 64; }
 
+// Rows of the forward's partial (max, sum) pairs held at a time: the rows run in chunks of this many,
+// so the workspace does not grow with T beyond it.
+constexpr int64_t CE_FWD_ROWS = 65536;
+
 static size_t ce_tc_ws_bytes(int64_t T, int64_t V, int64_t d) {
   const int64_t R = T < ce_bwd_rows() ? T : ce_bwd_rows();
+  const int64_t Rf = T < CE_FWD_ROWS ? T : CE_FWD_ROWS;
   size_t b = Workspace::round(size_t(V) * d * 2);                  // W bf16
-  b += 2 * Workspace::round(size_t(T) * ce_ngroups(V) * 4);        // part_m, part_s
-  b += Workspace::round(size_t(T) * 4);                            // target logits
+  b += 2 * Workspace::round(size_t(Rf) * ce_ngroups(V) * 4);       // part_m, part_s
+  b += Workspace::round(size_t(Rf) * 4);                           // target logits
   b += Workspace::round(size_t(R < 1 ? 1 : R) * ce_ldv(V) * 2);    // G
   return b + 1024;
 }
@@ -564,19 +569,24 @@ static int ce_fwd_tc(const void* h, const float* W, const int64_t* targets, floa
   Workspace Wk(ws, ws_bytes);
   __nv_bfloat16* Wb = Wk.take<__nv_bfloat16>(size_t(V) * d);
   const int64_t ng = ce_ngroups(V);
-  float* pm = Wk.take<float>(size_t(T) * ng);
-  float* ps = Wk.take<float>(size_t(T) * ng);
-  float* tg = Wk.take<float>(size_t(T));
+  const int64_t Rf = T < CE_FWD_ROWS ? T : CE_FWD_ROWS;
+  float* pm = Wk.take<float>(size_t(Rf) * ng);
+  float* ps = Wk.take<float>(size_t(Rf) * ng);
+  float* tg = Wk.take<float>(size_t(Rf));
   if (!Wb || !pm || !ps || !tg) { set_error("lm_head_ce_fwd: workspace too small"); return PGF_ERR_WORKSPACE; }
-  Gemm g = mk(T, V, d, h, 1, d, 0, Wb, 1, d, 0, nullptr, 0, 0);
+  Gemm g = mk(Rf, V, d, h, 1, d, 0, Wb, 1, d, 0, nullptr, 0, 0);
   if (!tc_usable(g)) return PGF_ERR_UNSUPPORTED;
   PGF_TRY(to_bf16(W, Wb, V * d, s));
-  // all-ones bytes = NaN: a row whose target lies outside [0, V) is never written and gets a NaN loss
-  PGF_CUDA(cudaMemsetAsync(tg, 0xFF, size_t(T) * 4, s));
-  int ngo = 0;
-  PGF_TRY(tc_ce_fwd(g, CE_NG, targets, pm, ps, tg, &ngo, s));
-  ce_combine_kernel<<<ceil_div(T, 256), 256, 0, s>>>(pm, ps, tg, T, ngo, loss_rows, lse);
-  PGF_LAUNCH_CHECK();
+  for (int64_t r = 0; r < T; r += Rf) {
+    const int64_t m = T - r < Rf ? T - r : Rf;
+    Gemm gc = mk(m, V, d, static_cast<const __nv_bfloat16*>(h) + r * d, 1, d, 0, Wb, 1, d, 0, nullptr, 0, 0);
+    // all-ones bytes = NaN: a row whose target lies outside [0, V) is never written and gets a NaN loss
+    PGF_CUDA(cudaMemsetAsync(tg, 0xFF, size_t(m) * 4, s));
+    int ngo = 0;
+    PGF_TRY(tc_ce_fwd(gc, CE_NG, targets + r, pm, ps, tg, &ngo, s));
+    ce_combine_kernel<<<ceil_div(m, 256), 256, 0, s>>>(pm, ps, tg, m, ngo, loss_rows + r, lse + r);
+    PGF_LAUNCH_CHECK();
+  }
   return PGF_OK;
 }
 
@@ -595,9 +605,10 @@ static int ce_bwd_tc(const void* h, const float* W, const int64_t* targets, cons
   Workspace Wk(ws, ws_bytes);
   __nv_bfloat16* Wb = Wk.take<__nv_bfloat16>(size_t(V) * d);
   const int64_t ng = ce_ngroups(V);
-  Wk.take<float>(size_t(T) * ng);  // keep the forward layout: the same workspace serves both
-  Wk.take<float>(size_t(T) * ng);
-  Wk.take<float>(size_t(T));
+  const int64_t Rf = T < CE_FWD_ROWS ? T : CE_FWD_ROWS;
+  Wk.take<float>(size_t(Rf) * ng);  // keep the forward layout: the same workspace serves both
+  Wk.take<float>(size_t(Rf) * ng);
+  Wk.take<float>(size_t(Rf));
   const int64_t R = T < ce_bwd_rows() ? T : ce_bwd_rows();
   const int64_t ldv = ce_ldv(V);
   __nv_bfloat16* G = Wk.take<__nv_bfloat16>(size_t(R) * ldv);

@@ -78,26 +78,50 @@ def rmsnorm_fwd_res(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: fl
     return sm, y
 
 
+def _out_buf(out: Optional[torch.Tensor], shape, dtype, device, name: str) -> torch.Tensor:
+    """`out` (contiguous, of this shape and dtype, e.g. a view into a larger buffer) or a new tensor."""
+    if out is None:
+        return torch.empty(*shape, dtype=dtype, device=device)
+    if tuple(out.shape) != tuple(shape) or out.dtype != dtype or not out.is_contiguous() or out.device != device:
+        raise ValueError(f"{name}: out must be contiguous {tuple(shape)} {dtype} on {device}")
+    return out
+
+
+def _out_like(out: Optional[torch.Tensor], ref: torch.Tensor, name: str) -> torch.Tensor:
+    return _out_buf(out, ref.shape, ref.dtype, ref.device, name)
+
+
+def _acc_buffer(acc: Optional[torch.Tensor], shape, device, name: str):
+    """(buffer, accumulate flag): `acc` (float32, `shape`) to add into, or a new buffer to write."""
+    if acc is None:
+        return torch.empty(*shape, dtype=torch.float32, device=device), 0
+    if tuple(acc.shape) != tuple(shape) or acc.dtype != torch.float32 or not acc.is_contiguous():
+        raise ValueError(f"{name}: accumulator must be contiguous float32 {tuple(shape)}")
+    return acc, 1
+
+
 def rmsnorm_bwd(x: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float,
-                need_gx: bool = True, g_add: Optional[torch.Tensor] = None
+                need_gx: bool = True, g_add: Optional[torch.Tensor] = None,
+                gw_acc: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None
                 ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-    """(grad weight, grad x); with g_add, grad x + g_add (fused, bitwise the separate add)."""
+    """(grad weight, grad x); with g_add, grad x + g_add (fused, bitwise the separate add).  gw_acc:
+    add grad weight into this float32 buffer instead (it is returned); out: write grad x there."""
     _cuda(x, g, w)
     x, g = _c(x), _c(g.to(x.dtype))
     w = _f32(w)
     dim = x.shape[-1]
     rows = x.numel() // dim
-    gw = torch.empty(dim, dtype=torch.float32, device=x.device)
-    gx = torch.empty_like(x) if (need_gx or g_add is not None) else None
+    gw, accum = _acc_buffer(gw_acc, (dim,), x.device, "rmsnorm_bwd")
+    gx = _out_like(out, x, "rmsnorm_bwd") if (need_gx or g_add is not None) else None
     L = lib()
     nb = L.pgf_rmsnorm_bwd_workspace(rows, dim)
     ws = _ws(nb, x.device)
     if g_add is not None:
         ga = _c(g_add.to(x.dtype))
-        check(L.pgf_rmsnorm_bwd_add(_p(x), _p(g), _p(w), _p(ga), _p(gx), _p(gw), 0, rows, dim, eps, _dt(x),
+        check(L.pgf_rmsnorm_bwd_add(_p(x), _p(g), _p(w), _p(ga), _p(gx), _p(gw), accum, rows, dim, eps, _dt(x),
                                     _p(ws), ws.numel(), _stream()), "rmsnorm_bwd_add")
     else:
-        check(L.pgf_rmsnorm_bwd(_p(x), _p(g), _p(w), _p(gx), _p(gw), 0, rows, dim, eps, _dt(x),
+        check(L.pgf_rmsnorm_bwd(_p(x), _p(g), _p(w), _p(gx), _p(gw), accum, rows, dim, eps, _dt(x),
                                 _p(ws), ws.numel(), _stream()), "rmsnorm_bwd")
     return gw, gx
 
@@ -176,14 +200,15 @@ def colsum(X: torch.Tensor) -> torch.Tensor:
 
 
 # --------------------------------------------------------------------------- FFN
-def ffn_fwd(x, W1, b1, W2, b2, activation="gelu", residual=None) -> torch.Tensor:
-    """FFN(x); with `residual` (rows x d_out, x's dtype), FFN(x) + residual from the same kernel."""
+def ffn_fwd(x, W1, b1, W2, b2, activation="gelu", residual=None, out=None) -> torch.Tensor:
+    """FFN(x); with `residual` (rows x d_out, x's dtype), FFN(x) + residual from the same kernel.
+    out: write the result there (contiguous rows x d_out in x's dtype)."""
     _cuda(x, W1)
     x = _c(x)
     W1, b1, W2, b2 = _f32(W1), _f32(b1), _f32(W2), _f32(b2)
     rows, d_in = x.shape
     d_h, d_out = W1.shape[0], W2.shape[0]
-    y = torch.empty(rows, d_out, dtype=x.dtype, device=x.device)
+    y = _out_buf(out, (rows, d_out), x.dtype, x.device, "ffn_fwd")
     L = lib()
     ws = _ws(L.pgf_ffn_workspace(rows, d_in, d_h, d_out, _dt(x), 0), x.device)
     if residual is not None:
@@ -266,22 +291,27 @@ def ssm_state_hvp(u, target, W_cat, b_cat, A_log, Dp, scale, v_h, act=None):
     return out
 
 
-def ffn_bwd(x, g, W1, b1, W2, activation="gelu", need_gx=True) -> Dict[str, torch.Tensor]:
+def ffn_bwd(x, g, W1, b1, W2, activation="gelu", need_gx=True, acc=None) -> Dict[str, torch.Tensor]:
+    """Gradients of the FFN; acc: a dict of float32 grad_W1 / grad_b1 / grad_W2 / grad_b2 buffers to
+    add into (those buffers are returned)."""
     _cuda(x, g, W1)
     x, g = _c(x), _c(g.to(x.dtype))
     W1, b1, W2 = _f32(W1), _f32(b1), _f32(W2)
     rows, d_in = x.shape
     d_h, d_out = W1.shape[0], W2.shape[0]
     dev = x.device
-    gW1 = torch.empty(d_h, d_in, device=dev)
-    gb1 = torch.empty(d_h, device=dev)
-    gW2 = torch.empty(d_out, d_h, device=dev)
-    gb2 = torch.empty(d_out, device=dev)
+    acc = acc or {}
+    gW1, accum = _acc_buffer(acc.get("grad_W1"), (d_h, d_in), dev, "ffn_bwd")
+    gb1, a1 = _acc_buffer(acc.get("grad_b1"), (d_h,), dev, "ffn_bwd")
+    gW2, a2 = _acc_buffer(acc.get("grad_W2"), (d_out, d_h), dev, "ffn_bwd")
+    gb2, a3 = _acc_buffer(acc.get("grad_b2"), (d_out,), dev, "ffn_bwd")
+    if len({accum, a1, a2, a3}) != 1:
+        raise ValueError("ffn_bwd: give all four accumulators or none")
     gx = torch.empty_like(x) if need_gx else None
     L = lib()
     ws = _ws(L.pgf_ffn_workspace(rows, d_in, d_h, d_out, _dt(x), 1), dev)
     check(L.pgf_ffn_bwd(_p(x), _p(g), _p(W1), _p(b1), _p(W2), _p(gW1), _p(gb1), _p(gW2), _p(gb2),
-                        _p(gx), 0, rows, d_in, d_h, d_out, ACT[activation], _dt(x), _p(ws),
+                        _p(gx), accum, rows, d_in, d_h, d_out, ACT[activation], _dt(x), _p(ws),
                         ws.numel(), _stream()), "ffn_bwd")
     r = {"grad_W1": gW1, "grad_b1": gb1, "grad_W2": gW2, "grad_b2": gb2}
     if need_gx:
@@ -415,21 +445,33 @@ def ssm_fwd_save(u, W_cat, b_cat, A_log, Dp, scale, h_init=None, act=None, state
     return y, saved
 
 
+def ssm_end_state(states: torch.Tensor, Bsz: int, L_: int, D: int, N: int) -> torch.Tensor:
+    """The state after the last token, (Bsz, D, N), from the boundary states that ssm_fwd_states
+    returns or the saved buffer of ssm_fwd_save (both begin with the (Bsz, chunks + 1, D, N) chunk
+    start states, the last of which is the end state)."""
+    n1 = lib().pgf_ssm_states_size(Bsz, L_, D, N) // (4 * Bsz * D * N)
+    return states[:Bsz * n1 * D * N].view(Bsz, n1, D, N)[:, n1 - 1]
+
+
 def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_end=None, act=None,
-            want_carry=False, saved=None):
+            want_carry=False, saved=None, acc=None):
     """All gradients of the SSM layer over [0, L) plus the carries (delta_h[0], dA[0]).  With
-    `saved` (from ssm_fwd_save on the same inputs) the forward passes are not recomputed."""
+    `saved` (from ssm_fwd_save on the same inputs) the forward passes are not recomputed.  acc: a dict
+    of float32 W_cat / b_cat / A_log / D / scale buffers to add the parameter gradients into."""
     _cuda(u, g, W_cat)
     u, g = _c(u), _c(g.to(u.dtype))
     Bsz, L_, D = u.shape
     N = A_log.shape[0]
     dev = u.device
     W_cat, b_cat = _f32(W_cat), _f32(b_cat)
-    gW = torch.empty_like(W_cat)
-    gb = torch.empty_like(b_cat)
-    gA = torch.empty(N, dtype=torch.float32, device=dev)
-    gD = torch.empty(D, dtype=torch.float32, device=dev)
-    gS = torch.empty(D, dtype=torch.float32, device=dev)
+    acc = acc or {}
+    gW, accum = _acc_buffer(acc.get("W_cat"), tuple(W_cat.shape), dev, "ssm_bwd")
+    gb, a1 = _acc_buffer(acc.get("b_cat"), tuple(b_cat.shape), dev, "ssm_bwd")
+    gA, a2 = _acc_buffer(acc.get("A_log"), (N,), dev, "ssm_bwd")
+    gD, a3 = _acc_buffer(acc.get("D"), (D,), dev, "ssm_bwd")
+    gS, a4 = _acc_buffer(acc.get("scale"), (D,), dev, "ssm_bwd")
+    if len({accum, a1, a2, a3, a4}) != 1:
+        raise ValueError("ssm_bwd: give all five accumulators or none")
     gu = torch.empty_like(u)
     dh0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev) if want_carry else None
     dA0 = torch.empty(Bsz, D, N, dtype=torch.float32, device=dev) if want_carry else None
@@ -439,7 +481,7 @@ def ssm_bwd(u, g, W_cat, b_cat, A_log, Dp, scale, h_init=None, dh_end=None, dA_e
     fn = Lb.pgf_ssm_bwd if saved is None else Lb.pgf_ssm_bwd_saved
     check(fn(_p(u), _p(g), _p(W_cat), _p(b_cat), _p(A_log), _p(Dp),
                          _p(scale), _p(h_init if saved is None else saved), _p(dh_end), _p(dA_end),
-                         _p(gW), _p(gb), _p(gA), _p(gD), _p(gS), _p(gu), _p(dh0), _p(dA0), 0,
+                         _p(gW), _p(gb), _p(gA), _p(gD), _p(gS), _p(gu), _p(dh0), _p(dA0), accum,
                          Bsz, L_, D, N, ACT[act], _dt(u), _p(ws), ws.numel(), _stream()), "ssm_bwd")
     return {"W_cat": gW, "b_cat": gb, "A_log": gA, "D": gD, "scale": gS, "grad_u": gu,
             "delta_h0": dh0, "dA0": dA0}

@@ -127,3 +127,74 @@ def test_lm_training_step_updates_and_loss_decreases():
     tg = torch.roll(ids, -1, 1)
     losses = [lm.step(ids, tg).item() for _ in range(30)]
     assert losses[-1] < losses[0] - 0.5, losses
+
+
+@pytest.mark.parametrize("mode", ["recompute", "states", "scan"])
+@pytest.mark.parametrize("act", ["none", "tanh"])
+def test_block_segments_match_reference_golden(mode, act):
+    """A block whose sequence runs in several segments (state carried forward, adjoint and decay
+    carried backward, parameter gradients added up) matches the reference's block-wise PGF."""
+    G = golden("block.pt")[act]
+    d = G["x"].shape[-1]
+    blk = _block_from(G["params"], d, G["d_ff"], G["block_size"], G["act"])
+    blk.segment_tokens = 2 * G["block_size"]  # B=2: one PGF block per segment, three segments of L=80
+    B, L, _ = G["x"].shape
+    assert len(blk._segments(B, L)) == 3
+    x, g = G["x"].to(DEV), G["g"].to(DEV)
+    blk.reference_scale_grad = True
+    if mode == "recompute":
+        y = blk.pgf_forward(x)
+        r = blk.pgf_backward(x, g)
+    else:
+        y, st = blk.pgf_forward(x, return_ssm_states=True, keep_scan=mode == "scan")
+        assert isinstance(st, list) and len(st) == 3
+        r = blk.pgf_backward(x, g, ssm_states=st)
+    assert_close(y, G["y"], name="pgf_forward")
+    assert_close(r["grad_input"], G["grad_input"], name="grad_input")
+    for k, v in G["grads"].items():
+        assert_close(r["grads"][k], v, name=k)
+
+
+def test_lm_step_segmented_matches_reference_golden():
+    G = golden("lm.pt")
+    lm = _lm_from_golden(G)
+    for layer in lm.backbone.layers:
+        layer.reference_scale_grad = True
+        layer.segment_tokens = 2 * G["block_size"]
+    loss, grads = lm.forward_backward(G["ids"].to(DEV), G["targets"].to(DEV))
+    assert abs(loss.item() - G["loss"].item()) < 1e-5
+    for k, v in G["grads"].items():
+        assert_close(grads[k], v, atol=2e-5, name=k)
+
+
+def _step_peak(L, stash="device"):
+    from icml_b200.lm import PGFLanguageModel
+    torch.manual_seed(0)
+    lm = PGFLanguageModel(50257, 256, 16, 1024, 8, 4096, DEV, act_dtype=torch.bfloat16, stash=stash)
+    ids = torch.randint(0, 50257, (1, L + 1), device=DEV)
+    lm.step(ids[:, :-1], ids[:, 1:])  # settles the optimizer state
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    loss, grads = lm.forward_backward(ids[:, :-1], ids[:, 1:])
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated() - base
+    del loss, grads, lm
+    torch.cuda.empty_cache()
+    return peak
+
+
+@pytest.mark.parametrize("stash", ["device", "host"])
+def test_step_memory_grows_only_by_the_per_token_buffers(stash):
+    """Peak memory of the 8-layer step (d_model 256, bf16) at 262144 tokens minus that at 65536 stays
+    within what must grow with L: the stashed layer inputs (8 per token-channel, or 2 with the host
+    stash), the scan's boundary states (16 floats per channel per 128-token chunk and layer), the
+    step's activation, gradient and output buffers (6 per token-channel) and the per-token vectors of
+    the embedding and the cross entropy (64 bytes).  Scan, FFN and LM-head workspaces run in segments
+    and tiles of fixed size, so they do not grow."""
+    d, layers = 256, 8
+    L1, L2 = 65536, 262144
+    p1, p2 = _step_peak(L1, stash), _step_peak(L2, stash)
+    stashed = layers if stash == "device" else 2
+    per_token = (stashed + 6) * d * 2 + layers * d * 16 * 4 / 128 + 64
+    assert p2 - p1 <= (L2 - L1) * per_token, (p1 / 1e9, p2 / 1e9, (L2 - L1) * per_token / 1e9)
