@@ -472,12 +472,6 @@ def run_gpu(a, rank, world, local_rank):
     def allreduce_grads():
         if pg is None:
             return False
-        if flat_opt:
-            # one all-reduce over the optimizer's flat gradient buffer, then the step without regather
-            model.optimizer.gather()
-            torch.distributed.all_reduce(model.optimizer.grad)
-            model.optimizer.grad.div_(world)
-            return True
         grads = [p.grad for p in model.params]
         flat = torch.cat([g.reshape(-1) for g in grads])
         torch.distributed.all_reduce(flat)
@@ -491,21 +485,32 @@ def run_gpu(a, rank, world, local_rank):
 
     from icml_b200 import seqpar
     sp = seqpar.SeqGroup.from_default() if (world > 1 and a.parallel == "sp") else None
+    # N GPUs: each layer's gradients are all-reduced (in the flat optimizer buffer, on a side stream)
+    # as soon as its backward returns, overlapping the backward of the layers below
+    reducer = None
+    if pg is not None and flat_opt:
+        from icml_b200.optim import OverlappedGradReduce
+        RO = torch.distributed.ReduceOp
+        reducer = OverlappedGradReduce(model, RO.SUM if sp is not None else RO.AVG)
 
     def step(x, y):
         model.optimizer.zero_grad(set_to_none=True)
         if sp is not None:
-            loss, grads = seqpar.lm_forward_backward(model, x, y, sp)  # gradients already summed
-            model._assign(grads)
-            gathered = False
+            loss, grads = seqpar.lm_forward_backward(model, x, y, sp, reducer=reducer)
+            if reducer is not None:
+                model.optimizer.step(gather=False)
+                return loss
+            model._assign(grads)  # gradients already summed
+        elif reducer is not None:
+            loss, grads = model.forward_backward(x, y, on_layer_grads=reducer.layer)
+            reducer.finish(grads)
+            model.optimizer.step(gather=False)
+            return loss
         else:
             loss, grads = model.forward_backward(x, y)
             model._assign(grads)
-            gathered = allreduce_grads()
-        if gathered:
-            model.optimizer.step(gather=False)
-        else:
-            model.optimizer.step()
+            allreduce_grads()
+        model.optimizer.step()
         return loss
 
     for _ in range(a.warmup):

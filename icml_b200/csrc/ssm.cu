@@ -1501,3 +1501,74 @@ extern "C" int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
+
+// ---------------------------------------------------------------------------------------------
+// Composition of the ranks' segment summaries (sequence sharding): one thread per (b, d, n) folds
+// the P summaries gathered into one buffer, in rank order, instead of a host loop of small ops.
+// ---------------------------------------------------------------------------------------------
+namespace pgf {
+
+__global__ void compose_ranks_fwd_kernel(const float* __restrict__ gat, int64_t stride, int P, int rank,
+                                         const float* __restrict__ A_log, int a_pc, float* __restrict__ h_in,
+                                         int64_t Bsz, int64_t D, int64_t N) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nth = Bsz * D * N;
+  if (i >= nth) return;
+  const int64_t n = i % N, bd = i / N, d = bd % D;
+  const float A = -expf(A_log[a_pc ? d * N + n : n]);
+  float H = 0.f;
+  for (int j = 0; j < rank && j < P; ++j) {
+    const float* g = gat + int64_t(j) * stride;
+    H = fmaf(expf(A * g[nth + bd]), H, g[i]);
+  }
+  h_in[i] = H;
+}
+
+__global__ void compose_ranks_bwd_kernel(const float* __restrict__ gat, int64_t stride, int P, int rank,
+                                         const float* __restrict__ A_log, int a_pc, float* __restrict__ dh_end,
+                                         float* __restrict__ dA_end, int64_t Bsz, int64_t D, int64_t N) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nth = Bsz * D * N;
+  if (i >= nth) return;
+  const int64_t n = i % N, bd = i / N, d = bd % D;
+  const float A = -expf(A_log[a_pc ? d * N + n : n]);
+  float G = 0.f, aE = 1.f;
+  for (int j = P - 1; j > rank; --j) {
+    const float* g = gat + int64_t(j) * stride;
+    G = fmaf(expf(A * g[2 * nth + bd]), aE * G, g[i]);
+    aE = g[nth + i];
+  }
+  dh_end[i] = G;
+  dA_end[i] = aE;
+}
+
+}  // namespace pgf
+
+extern "C" int pgf_ssm_compose_ranks_fwd(const float* gathered, int64_t stride, int P, int rank, const float* A_log,
+                                         int a_per_channel, float* h_in, int64_t Bsz, int64_t D, int64_t N,
+                                         pgf_stream_t stream) {
+  PGF_CHECK_ARG(gathered && A_log && h_in, "ssm_compose_ranks_fwd: null pointer");
+  PGF_CHECK_ARG(P >= 1 && rank >= 0 && rank < P && Bsz > 0 && D > 0 && N > 0, "ssm_compose_ranks_fwd: bad shape");
+  PGF_CHECK_ARG(stride >= Bsz * D * (N + 1), "ssm_compose_ranks_fwd: stride %lld below one summary",
+                (long long)stride);
+  const int64_t nth = Bsz * D * N;
+  compose_ranks_fwd_kernel<<<ceil_div(nth, 256), 256, 0, as_stream(stream)>>>(gathered, stride, P, rank, A_log,
+                                                                              a_per_channel, h_in, Bsz, D, N);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
+extern "C" int pgf_ssm_compose_ranks_bwd(const float* gathered, int64_t stride, int P, int rank, const float* A_log,
+                                         int a_per_channel, float* dh_end, float* dA_end, int64_t Bsz, int64_t D,
+                                         int64_t N, pgf_stream_t stream) {
+  PGF_CHECK_ARG(gathered && A_log && dh_end && dA_end, "ssm_compose_ranks_bwd: null pointer");
+  PGF_CHECK_ARG(P >= 1 && rank >= 0 && rank < P && Bsz > 0 && D > 0 && N > 0, "ssm_compose_ranks_bwd: bad shape");
+  PGF_CHECK_ARG(stride >= Bsz * D * (2 * N + 1), "ssm_compose_ranks_bwd: stride %lld below one summary",
+                (long long)stride);
+  const int64_t nth = Bsz * D * N;
+  compose_ranks_bwd_kernel<<<ceil_div(nth, 256), 256, 0, as_stream(stream)>>>(gathered, stride, P, rank, A_log,
+                                                                              a_per_channel, dh_end, dA_end, Bsz, D,
+                                                                              N);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}

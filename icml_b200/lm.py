@@ -159,9 +159,10 @@ class PGFLanguageModel:
         self.backbone.load_state_dict(backbone_state)
 
     @torch.no_grad()
-    def forward_backward(self, input_ids: torch.Tensor, targets: torch.Tensor):
+    def forward_backward(self, input_ids: torch.Tensor, targets: torch.Tensor, on_layer_grads=None):
         """PGF pass 1 over all layers (stashing each layer's input), fused LM head + CE, pass 2 in
-        reverse.  Returns (loss tensor, {param name: grad})."""
+        reverse.  Returns (loss tensor, {param name: grad}).  on_layer_grads(i, {name: grad}) is
+        called as soon as layer i's gradients are final (e.g. to start their all-reduce)."""
         B, L = input_ids.shape
         d = self.d_model
         x = ops.embedding_fwd(input_ids, self.emb_weight, dtype=self.act_dtype)
@@ -194,6 +195,8 @@ class PGFLanguageModel:
             del xi
             for k, v in res["grads"].items():
                 grads[f"layers.{i}.{k}"] = v
+            if on_layer_grads is not None:
+                on_layer_grads(i, res["grads"])
             g = res["grad_input"]
             del res
         grads["emb"] = ops.embedding_bwd(input_ids, g, self.vocab_size)

@@ -602,6 +602,31 @@ def ssm_bwd_finish(state, Dp, dh_end=None, dA_end=None):
     return {"W_cat": gW, "b_cat": gb, "A_log": gA, "D": gD, "scale": gS, "grad_u": gu}
 
 
+def ssm_compose_ranks_fwd(gathered, rank: int, A_log, Bsz: int, D: int, N: int) -> torch.Tensor:
+    """State entering segment `rank` of a sharded sequence, from every rank's [h_seg | sum_dt]
+    summary gathered as rows of `gathered` (P, stride).  A_log (N,) or, per channel, (D, N)."""
+    _cuda(gathered, A_log)
+    g, A = _c(gathered.float()), _f32(A_log)
+    P, stride = g.shape
+    h = torch.empty(Bsz, D, N, dtype=torch.float32, device=g.device)
+    check(lib().pgf_ssm_compose_ranks_fwd(_p(g), stride, P, rank, _p(A), int(A.dim() == 2), _p(h), Bsz, D, N,
+                                          _stream()), "ssm_compose_ranks_fwd")
+    return h
+
+
+def ssm_compose_ranks_bwd(gathered, rank: int, A_log, Bsz: int, D: int, N: int):
+    """(dh_end, dA_end) entering segment `rank` from the right, from every rank's
+    [dh_start | dA_start | sum_dt_excl] summary gathered as rows of `gathered` (P, stride)."""
+    _cuda(gathered, A_log)
+    g, A = _c(gathered.float()), _f32(A_log)
+    P, stride = g.shape
+    dh = torch.empty(Bsz, D, N, dtype=torch.float32, device=g.device)
+    dA = torch.empty(Bsz, D, N, dtype=torch.float32, device=g.device)
+    check(lib().pgf_ssm_compose_ranks_bwd(_p(g), stride, P, rank, _p(A), int(A.dim() == 2), _p(dh), _p(dA), Bsz, D,
+                                          N, _stream()), "ssm_compose_ranks_bwd")
+    return dh, dA
+
+
 # --------------------------------------------------------------------------- Mamba-standard mixer
 MIXER_KEYS = ("in_w", "conv_w", "conv_b", "x_w", "dt_w", "dt_b", "A_log", "D", "out_w")
 

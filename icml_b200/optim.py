@@ -89,6 +89,33 @@ class FlatAdamW:
         self._keep = []
 
     @torch.no_grad()
+    def gather_subset(self, params: Sequence[torch.nn.Parameter], grads: Sequence[torch.Tensor]):
+        """Copy the gradients of some parameters into their slots of ``self.grad`` (one launch)."""
+        idx = {id(p): k for k, p in enumerate(self.params)}
+        ks = [idx[id(p)] for p in params]
+        keep = [g.contiguous() for g in grads]
+        for k, g in zip(ks, keep):
+            p = self.params[k]
+            if g.dtype != torch.float32 or g.shape != p.shape or g.device != p.device:
+                raise ValueError("FlatAdamW: gradients must match their parameters (float32, same shape)")
+        n = len(ks)
+        ptrs = (ctypes.c_void_p * n)(*[g.data_ptr() for g in keep])
+        offs = (ctypes.c_int64 * n)(*[self.offsets[k] for k in ks])
+        sizes = (ctypes.c_int64 * n)(*[self.params[k].numel() for k in ks])
+        check(lib().pgf_gather_multi(self.grad.data_ptr(), self.n, ptrs, offs, sizes, n, _stream()),
+              "pgf_gather_multi")
+
+    def slice_of(self, params: Sequence[torch.nn.Parameter]) -> torch.Tensor:
+        """The range of ``self.grad`` covering the slots of these parameters (adjacent in the buffer)."""
+        idx = {id(p): k for k, p in enumerate(self.params)}
+        ks = sorted(idx[id(p)] for p in params)
+        if ks != list(range(ks[0], ks[-1] + 1)):
+            raise ValueError("FlatAdamW.slice_of: the parameters are not adjacent in the flat buffer")
+        a = self.offsets[ks[0]]
+        b = self.offsets[ks[-1]] + (self.params[ks[-1]].numel() + 3) // 4 * 4
+        return self.grad[a:b]
+
+    @torch.no_grad()
     def step(self, grads: Optional[Sequence[Optional[torch.Tensor]]] = None, gather: bool = True):
         """One AdamW step.  Without clipping, the update reads each gradient where it lies (no flat
         copy); with clipping the gradients are gathered first.  gather=False uses the flat gradient
@@ -116,6 +143,56 @@ class FlatAdamW:
         check(L.pgf_adamw_step(self.flat.data_ptr(), self.grad.data_ptr(), self.exp_avg.data_ptr(),
                                self.exp_avg_sq.data_ptr(), self.n, *hyper, self.step_count.data_ptr(), clip_ptr, s),
               "pgf_adamw_step")
+
+
+class OverlappedGradReduce:
+    """All-reduce of the step's gradients across ranks, layer by layer while the backward goes on.
+
+    PGF's backward finishes the gradients of layer i as soon as that layer's pgf_backward returns
+    (pgf_mamba_block.py:238), so each layer's gradients are copied into their (adjacent) slots of the
+    flat optimizer's gradient buffer and all-reduced there on a side stream, overlapping the
+    backward of the layers below; ``finish`` reduces the rest (embedding, LM head, final norm) and
+    joins the side stream.  Works inside CUDA-graph capture (every rank issues the same collectives
+    in the same order).  op: ReduceOp.AVG for data parallelism (replicas), SUM for sequence sharding
+    (partial sums)."""
+
+    def __init__(self, model, op):
+        import torch.distributed as dist
+        self.dist = dist
+        self.model = model
+        self.opt = model.optimizer
+        self.op = op
+        self.stream = torch.cuda.Stream(device=self.opt.flat.device)
+
+    def _reduce(self, params, grads):
+        self.opt.gather_subset(params, grads)
+        sl = self.opt.slice_of(params)
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):
+            self.dist.all_reduce(sl, op=self.op)
+
+    def layer(self, i: int, grads) -> None:
+        named = list(self.model.backbone.layers[i].named_parameters())
+        self._reduce([p for _, p in named], [grads[n] for n, _ in named])
+
+    def finish(self, grads, extra: Optional[torch.Tensor] = None) -> None:
+        """Reduce the non-layer gradients (and `extra`, e.g. a loss sum, in place), then wait for all."""
+        m = self.model
+        ps, gs = [m.emb_weight], [grads["emb"]]
+        if not m.tied:
+            ps.append(m.lm_head_weight)
+            gs.append(grads["lm_head"])
+        if m.final_norm is not None:
+            ps.append(m.final_norm.weight)
+            gs.append(grads["final_norm"])
+        self.opt.gather_subset(ps, gs)
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):
+            for p in ps:
+                self.dist.all_reduce(self.opt.slice_of([p]), op=self.op)
+            if extra is not None:
+                self.dist.all_reduce(extra, op=self.op)
+        torch.cuda.current_stream().wait_stream(self.stream)
 
 
 def grad_norm(grad: torch.Tensor, max_norm: Optional[float] = None):

@@ -46,34 +46,20 @@ class SeqGroup:
         dist.all_gather(out, t, group=self.group)
         return torch.stack(out, 0)
 
+    def all_gather_flat(self, ts) -> torch.Tensor:
+        """(world, n): each rank's tensors, flattened to float32 and concatenated, in rank order --
+        one collective for the whole summary."""
+        flat = torch.cat([t.reshape(-1).float() for t in ts])
+        if self.world == 1:
+            return flat.unsqueeze(0)
+        out = torch.empty(self.world * flat.numel(), dtype=flat.dtype, device=flat.device)
+        dist.all_gather_into_tensor(out, flat, group=self.group)
+        return out.view(self.world, -1)
+
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
             dist.all_reduce(t, group=self.group)
         return t
-
-
-def compose_forward_state(h_locs: torch.Tensor, sum_dts: torch.Tensor, A: torch.Tensor, rank: int) -> torch.Tensor:
-    """State entering segment `rank`: fold H <- exp(A * sum_dt_j) H + h_loc_j over ranks j < rank.
-    h_locs (P, B, d, N), sum_dts (P, B, d), A (N,) = -exp(A_log)."""
-    H = torch.zeros_like(h_locs[0])
-    for j in range(rank):
-        H = torch.exp(A * sum_dts[j].unsqueeze(-1)) * H + h_locs[j]
-    return H
-
-
-def compose_backward_carry(d_locs: torch.Tensor, dA_starts: torch.Tensor, sum_dt_excls: torch.Tensor,
-                           A: torch.Tensor, rank: int) -> Tuple[torch.Tensor, torch.Tensor]:
-    """(dh_end, dA_end) for segment `rank`: the adjoint at the first token of the next segment and
-    that token's decay.  Folds from the last rank down to rank + 1:
-    X = a_E * G;  G <- exp(A * sum_dt_excl_j) X + d_loc_j;  a_E <- dA_start_j."""
-    P = d_locs.shape[0]
-    G = torch.zeros_like(d_locs[0])
-    aE = torch.ones_like(d_locs[0])
-    for j in range(P - 1, rank, -1):
-        X = aE * G
-        G = torch.exp(A * sum_dt_excls[j].unsqueeze(-1)) * X + d_locs[j]
-        aE = dA_starts[j]
-    return G, aE
 
 
 def _wb(m):
@@ -88,12 +74,11 @@ def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
     B, L, D = x.shape
     m = block.mamba
     W, b = _wb(m)
-    A = -torch.exp(m.A_log.detach().float())
     xn = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
     if sp.world > 1:
         # the zero-start pass gives the segment summary; the output pass continues from it
         h_loc, sdt, st = ops.ssm_fwd_begin(xn, W, b, m.A_log)
-        h_in = compose_forward_state(sp.all_gather(h_loc), sp.all_gather(sdt), A, sp.rank)
+        h_in = ops.ssm_compose_ranks_fwd(sp.all_gather_flat([h_loc, sdt]), sp.rank, m.A_log, B, D, m.d_state)
         y, states = ops.ssm_fwd_finish(st, m.D, m.scale, h_init=h_in, act=m.output_activation, want_states=True)
         del st
     else:
@@ -113,7 +98,6 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
     B, L, D = x.shape
     m = block.mamba
     W, b = _wb(m)
-    A = -torch.exp(m.A_log.detach().float())
     g_out = g_out.to(x.dtype)
     xn1 = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
     if states is not None:
@@ -129,8 +113,8 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
         # the reverse chunk pass gives the segment's adjoint summary; the gradients continue from it
         d_loc, dA0, sdx, st = ops.ssm_bwd_begin(xn1, g_m, W, b, m.A_log, m.scale, saved, h_init=h_in,
                                                 act=m.output_activation)
-        dh_end, dA_end = compose_backward_carry(sp.all_gather(d_loc), sp.all_gather(dA0), sp.all_gather(sdx),
-                                                A, sp.rank)
+        dh_end, dA_end = ops.ssm_compose_ranks_bwd(sp.all_gather_flat([d_loc, dA0, sdx]), sp.rank, m.A_log, B, D,
+                                                   m.d_state)
         r = ops.ssm_bwd_finish(st, m.D, dh_end=dh_end, dA_end=dA_end)
         del st
     else:
@@ -152,9 +136,11 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
 
 @torch.no_grad()
 def lm_forward_backward(model, input_ids: torch.Tensor, targets: torch.Tensor, sp: SeqGroup,
-                        ops=cuda_ops, total_tokens: Optional[int] = None):
+                        ops=cuda_ops, total_tokens: Optional[int] = None, reducer=None):
     """The PGF LM step on this rank's segment of every sequence.  Returns (global mean loss, grads):
-    gradients are summed over ranks (all-reduce), the loss is the mean over all ranks' tokens."""
+    gradients are summed over ranks (all-reduce), the loss is the mean over all ranks' tokens.  With
+    `reducer` (an optim.OverlappedGradReduce with SUM) the gradients are summed layer by layer into the
+    flat optimizer's gradient buffer while the backward goes on, and the returned ones stay local."""
     B, L = input_ids.shape
     d = model.d_model
     T_total = total_tokens if total_tokens is not None else B * L * sp.world
@@ -175,12 +161,16 @@ def lm_forward_backward(model, input_ids: torch.Tensor, targets: torch.Tensor, s
         res = block_backward(model.backbone.layers[i], xi, g, h_in, sp, ops, states=states)
         for k, v in res["grads"].items():
             grads[f"layers.{i}.{k}"] = v
+        if reducer is not None:
+            reducer.layer(i, res["grads"])
         g = res["grad_input"]
     grads["emb"] = ops.embedding_bwd(input_ids, g, model.vocab_size)
     if getattr(model, "tied", False):
         grads["emb"] = grads["emb"] + grads.pop("lm_head")
     loss_sum = loss_rows.sum().reshape(1).float()
-    if sp.world > 1:
+    if reducer is not None:
+        reducer.finish(grads, extra=loss_sum)
+    elif sp.world > 1:
         names = sorted(grads)
         flat = torch.cat([grads[k].reshape(-1).float() for k in names] + [loss_sum])
         sp.all_reduce_(flat)
@@ -193,5 +183,4 @@ def lm_forward_backward(model, input_ids: torch.Tensor, targets: torch.Tensor, s
     return loss_sum[0] / T_total, grads
 
 
-__all__ = ["SeqGroup", "compose_forward_state", "compose_backward_carry", "block_forward", "block_backward",
-           "lm_forward_backward"]
+__all__ = ["SeqGroup", "block_forward", "block_backward", "lm_forward_backward"]

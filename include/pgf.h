@@ -345,6 +345,20 @@ int pgf_ssm_bwd_finish(const void* u, const void* g, const float* W_cat, const f
                        float* gDp, float* gscale, void* gu, float* dh_start, float* dA_start, int accumulate,
                        int64_t Bsz, int64_t L, int64_t D, int64_t N, int act, int dtype, void* ws,
                        size_t ws_bytes, pgf_stream_t stream);
+/* The block hand-off of the reference (pgf_mamba_block.py:86-112 forward, :207-234 backward) across
+ * the P ranks of a sharded sequence, from the ranks' segment summaries gathered into one buffer
+ * (`stride` floats per rank, rank order).  A_log is (N,) (shared) or, with a_per_channel, (D, N).
+ *   fwd: rank j's entry is [h_seg (Bsz,D,N) | sum_dt (Bsz,D)] (pgf_ssm_fwd_begin); h_in = the fold
+ *        H <- exp(A sum_dt_j) H + h_seg_j over j < rank from H = 0: the state entering `rank`.
+ *   bwd: rank j's entry is [dh_start | dA_start (Bsz,D,N each) | sum_dt_excl (Bsz,D)]
+ *        (pgf_ssm_bwd_begin); from G = 0, aE = 1, for j = P-1 down to rank+1:
+ *        G <- exp(A sum_dt_excl_j) aE G + dh_start_j, aE <- dA_start_j; then dh_end = G, dA_end = aE. */
+int pgf_ssm_compose_ranks_fwd(const float* gathered, int64_t stride, int P, int rank, const float* A_log,
+                              int a_per_channel, float* h_in, int64_t Bsz, int64_t D, int64_t N,
+                              pgf_stream_t stream);
+int pgf_ssm_compose_ranks_bwd(const float* gathered, int64_t stride, int P, int rank, const float* A_log,
+                              int a_per_channel, float* dh_end, float* dA_end, int64_t Bsz, int64_t D, int64_t N,
+                              pgf_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * Mamba-standard mixer: the variant the benchmark configurations describe; the reference has no

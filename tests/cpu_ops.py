@@ -143,3 +143,34 @@ def lm_head_ce_bwd(h, W, targets, lse, grad_scale, need_gh=True):
     G[torch.arange(h.shape[0]), targets] -= 1.0
     G *= grad_scale
     return G.t() @ h, (G @ W.detach() if need_gh else None)
+
+
+def ssm_compose_ranks_fwd(gathered, rank, A_log, Bsz, D, N):
+    """State entering segment `rank`: fold H <- exp(A sum_dt_j) H + h_seg_j over ranks j < rank, from
+    rows [h_seg (Bsz,D,N) | sum_dt (Bsz,D)] of `gathered` (the host statement of the kernel's fold)."""
+    A = -torch.exp(A_log.detach().to(gathered.dtype))
+    A = A if A.dim() == 2 else A.expand(D, N)
+    n = Bsz * D * N
+    H = torch.zeros(Bsz, D, N, dtype=gathered.dtype)
+    for j in range(rank):
+        h_loc = gathered[j, :n].view(Bsz, D, N)
+        sdt = gathered[j, n:n + Bsz * D].view(Bsz, D, 1)
+        H = torch.exp(A * sdt) * H + h_loc
+    return H
+
+
+def ssm_compose_ranks_bwd(gathered, rank, A_log, Bsz, D, N):
+    """(dh_end, dA_end) for segment `rank` from rows [dh_start | dA_start | sum_dt_excl]: from the last
+    rank down to rank + 1, X = aE G; G <- exp(A sum_dt_excl_j) X + dh_start_j; aE <- dA_start_j."""
+    A = -torch.exp(A_log.detach().to(gathered.dtype))
+    A = A if A.dim() == 2 else A.expand(D, N)
+    n = Bsz * D * N
+    G = torch.zeros(Bsz, D, N, dtype=gathered.dtype)
+    aE = torch.ones(Bsz, D, N, dtype=gathered.dtype)
+    for j in range(gathered.shape[0] - 1, rank, -1):
+        d_loc = gathered[j, :n].view(Bsz, D, N)
+        dA0 = gathered[j, n:2 * n].view(Bsz, D, N)
+        sdx = gathered[j, 2 * n:2 * n + Bsz * D].view(Bsz, D, 1)
+        G = torch.exp(A * sdx) * (aE * G) + d_loc
+        aE = dA0
+    return G, aE

@@ -81,9 +81,12 @@ def test_sequence_sharded_step_matches_single_process_oracle(world, tmp_path):
         assert err <= 1e-5 + 1e-4 * v.abs().max().item(), (k, err)
 
 
+def _gathered(rows):
+    return torch.stack([torch.cat([t.reshape(-1) for t in r]) for r in rows])
+
+
 def test_compose_functions_equal_sequential_scan():
-    """compose_forward_state / compose_backward_carry against one long oracle scan."""
-    from icml_b200.seqpar import compose_backward_carry, compose_forward_state
+    """The rank composition (forward state, backward carry) against one long oracle scan."""
     from tests import cpu_ops
     g = torch.Generator().manual_seed(8)
     d, N, Lt, P = 12, 16, 60, 4
@@ -92,21 +95,17 @@ def test_compose_functions_equal_sequential_scan():
     bb = torch.cat([p["dt_b"], p["B_b"], p["C_b"]]).double()
     u = torch.randn(1, Lt, d, generator=g, dtype=torch.float64)
     gy = torch.randn(1, Lt, d, generator=g, dtype=torch.float64)
-    A = -torch.exp(p["A_log"])
     segs = [slice(i * Lt // P, (i + 1) * Lt // P) for i in range(P)]
-    sums = [cpu_ops.ssm_summary(u[:, s], W, bb, p["A_log"]) for s in segs]
-    h_locs = torch.stack([s[0] for s in sums])
-    sdts = torch.stack([s[1] for s in sums])
+    fwd = _gathered([cpu_ops.ssm_summary(u[:, s], W, bb, p["A_log"]) for s in segs])
     _, h0s, _ = O.ssm_forward(p, u, Lt // P)
     for r in range(P):
-        assert torch.allclose(compose_forward_state(h_locs, sdts, A, r), h0s[r], atol=1e-10)
+        assert torch.allclose(cpu_ops.ssm_compose_ranks_fwd(fwd, r, p["A_log"], 1, d, N), h0s[r], atol=1e-10)
     # backward carries: the whole-sequence block chain of the oracle is the truth
-    bs = [cpu_ops.ssm_bwd_summary(u[:, s], gy[:, s], W, bb, p["A_log"], p["scale"]) for s in segs]
-    d_locs, dA0s, sdx = (torch.stack([b[i] for b in bs]) for i in range(3))
+    bwd = _gathered([cpu_ops.ssm_bwd_summary(u[:, s], gy[:, s], W, bb, p["A_log"], p["scale"]) for s in segs])
     dh = torch.zeros(1, d, N, dtype=torch.float64)
     dA = torch.ones(1, d, N, dtype=torch.float64)
     for r in reversed(range(P)):
-        G, aE = compose_backward_carry(d_locs, dA0s, sdx, A, r)
+        G, aE = cpu_ops.ssm_compose_ranks_bwd(bwd, r, p["A_log"], 1, d, N)
         assert torch.allclose(G, dh, atol=1e-10) and torch.allclose(aE, dA, atol=1e-12)
         res = O.ssm_block_grad(p, u[:, segs[r]], gy[:, segs[r]], h0s[r], dh, dA)
         dh, dA = res["delta_h0"], res["dA0"]
