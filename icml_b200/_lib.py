@@ -109,6 +109,14 @@ SIGNATURES = {
     "pgf_ssm_state_hvp": (c_int, [P] * 9 + [I64] * 4 + [c_int, P, c_size_t, P]),
     "pgf_frechet_jvp": (c_int, [P] * 13 + [I64] * 3 + [P, c_size_t, P]),
     "pgf_grad_norm": (c_int, [P, I64, P, c_float, P, P, c_size_t, P]),
+    "pgf_mamba_mixer_fwd_seg": (c_int, [P] * 17 + [c_size_t] + [I64] * 7 + [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_fwd_begin": (c_int, [P] * 13 + [I64] * 7 + [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_fwd_finish": (c_int, [P] * 14 + [I64] * 7 + [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_bwd_seg": (c_int, [P] * 13 + [c_size_t] + [P] * 2 + [P] * 9 + [P] * 4 + [c_int] + [I64] * 7 +
+                                [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_bwd_begin": (c_int, [P] * 13 + [c_size_t] + [P] * 3 + [I64] * 7 + [c_int, P, c_size_t, P]),
+    "pgf_mamba_mixer_bwd_finish": (c_int, [P] * 13 + [c_size_t] + [P] * 2 + [P] * 9 + [P] * 2 + [c_int] +
+                                   [I64] * 7 + [c_int, P, c_size_t, P]),
     "pgf_ssm_compose_ranks_fwd": (c_int, [P, I64, c_int, c_int, P, c_int, P, I64, I64, I64, P]),
     "pgf_ssm_compose_ranks_bwd": (c_int, [P, I64, c_int, c_int, P, c_int, P, P, I64, I64, I64, P]),
 }

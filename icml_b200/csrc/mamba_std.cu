@@ -47,6 +47,12 @@ struct Args {
   float* partA;                    // (nC, Bsz, E, N)
   float* partD;                    // (nC, Bsz, E)
   float* ckpt_g; int ckpt_write;   // sub-chunk start states (Bsz, nC, Tc/ST, E, N)
+  // carries across segments of one sequence (all nullable): forward start state, end state and sum
+  // of dt; backward carry entering from the right, and the adjoint / decay / sum of dt over every
+  // token but the first at the segment's start
+  const float* h_init; float* h_final; float* sum_dt_out;
+  const float* dh_end; const float* dA_end;
+  float* dh_start; float* dA_start; float* sum_dt_excl;
 };
 
 struct Stage {
@@ -228,8 +234,16 @@ __global__ void __launch_bounds__(32 * CSEG) compose_fwd_kernel(const Args a) {
   const int64_t d = (ii / NST) % a.E;
   const int64_t b = ii / (NST * a.E);
   const float A2 = -expf(a.A_log[d * NST + n]) * LOG2E;
-  compose_fwd_segmented(valid, a.sdt + b * a.nC * a.E + d, a.E, a.hloc + (b * a.nC * a.E + d) * NST + n, a.E * NST,
-                        a.hC + (b * (a.nC + 1) * a.E + d) * NST + n, A2, 0.f, a.nC, nullptr);
+  const int64_t o = (b * a.E + d) * NST + n;
+  const float H0 = (valid && a.h_init) ? a.h_init[o] : 0.f;
+  float tot = 0.f;
+  const float Hend = compose_fwd_segmented(valid, a.sdt + b * a.nC * a.E + d, a.E,
+                                           a.hloc + (b * a.nC * a.E + d) * NST + n, a.E * NST,
+                                           a.hC + (b * (a.nC + 1) * a.E + d) * NST + n, A2, H0, a.nC, &tot);
+  if (valid && threadIdx.x < 32) {
+    if (a.h_final) a.h_final[o] = Hend;
+    if (a.sum_dt_out && n == 0) a.sum_dt_out[b * a.E + d] = tot;
+  }
 }
 
 __global__ void __launch_bounds__(THREADS) out_fwd_kernel(const Args a) {
@@ -324,16 +338,44 @@ __global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
 
 // Adjoint carries X entering each chunk from the right (zero final carry), segmented over warps.
 __global__ void __launch_bounds__(32 * CSEG) compose_bwd_kernel(const Args a) {
-  const int64_t idx = int64_t(blockIdx.x) * 32 + (threadIdx.x & 31);
+  __shared__ float sSum[CSEG][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t idx = int64_t(blockIdx.x) * 32 + lane;
   const bool valid = idx < a.Bsz * a.E * NST;
   const int64_t ii = valid ? idx : 0;
   const int n = int(ii % NST);
   const int64_t d = (ii / NST) % a.E;
   const int64_t b = ii / (NST * a.E);
   const float A2 = -expf(a.A_log[d * NST + n]) * LOG2E;
-  compose_bwd_segmented(valid, a.sdt2 + b * a.nC * a.E + d, a.dt0 + b * a.nC * a.E + d, a.E,
-                        a.dloc + (b * a.nC * a.E + d) * NST + n, a.E * NST, a.X + (b * a.nC * a.E + d) * NST + n, A2,
-                        0.f, 1.f, a.nC, nullptr);
+  const int64_t o = (b * a.E + d) * NST + n;
+  const float* sdt2 = a.sdt2 + b * a.nC * a.E + d;
+  const float* dt0 = a.dt0 + b * a.nC * a.E + d;
+  const float G_end = (valid && a.dh_end) ? a.dh_end[o] : 0.f;
+  const float aE_end = (valid && a.dA_end) ? a.dA_end[o] : 1.f;
+  float aE0 = 1.f;
+  const float G0 = compose_bwd_segmented(valid, sdt2, dt0, a.E, a.dloc + (b * a.nC * a.E + d) * NST + n, a.E * NST,
+                                         a.X + (b * a.nC * a.E + d) * NST + n, A2, G_end, aE_end, a.nC, &aE0);
+  if (valid && w == 0) {
+    if (a.dh_start) a.dh_start[o] = G0;
+    if (a.dA_start) a.dA_start[o] = aE0;
+  }
+  if (a.sum_dt_excl) {
+    // sum of dt over every token but the first: within-chunk sums plus the later chunks' first dt,
+    // per run of chunks, then the runs in order
+    const int64_t run = (a.nC + CSEG - 1) / CSEG;
+    const int64_t c0 = w * run < a.nC ? w * run : a.nC;
+    const int64_t c1 = c0 + run < a.nC ? c0 + run : a.nC;
+    float t = 0.f;
+    if (valid && n == 0)
+      for (int64_t k = c0; k < c1; ++k) t += sdt2[k * a.E] + (k > 0 ? dt0[k * a.E] : 0.f);
+    sSum[w][lane] = t;
+    __syncthreads();
+    if (valid && w == 0 && n == 0) {
+      float tot = 0.f;
+      for (int v = 0; v < CSEG; ++v) tot += sSum[v][lane];
+      a.sum_dt_excl[b * a.E + d] = tot;
+    }
+  }
 }
 
 // Main backward: checkpoints from the forward output pass (ckpt_g) are required.
@@ -500,10 +542,19 @@ constexpr int KMAX = 8;
 // u[t, e] = SiLU(b[e] + sum_k w[e, k] xi[t - (K-1) + k, e]); xi rows have pitch ld_x.
 // Causal depthwise conv + SiLU, one thread per (channel, CONV_T-token slab), K a template
 // parameter so the sliding window lives in registers.
+//
+// `halo` (nullable): the K-1 xi rows before token 0, (Bsz, K-1, E) in the activation dtype -- the tail
+// of the previous segment of the same sequence; without it they are the conv's zero padding.
+__device__ __forceinline__ float xi_at(const void* xi, int64_t ld_x, const void* halo, int abf, int64_t b, int64_t L,
+                                       int64_t E, int K, int64_t tt, int64_t e) {
+  if (tt >= 0) return tt < L ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f;
+  return halo ? ldv(halo, abf, (b * (K - 1) + (K - 1) + tt) * E + e) : 0.f;
+}
+
 template <int K>
-__global__ void conv_fwd_kernel(const void* __restrict__ xi, int64_t ld_x, const float* __restrict__ w,
-                                const float* __restrict__ bias, void* __restrict__ u, int64_t Bsz, int64_t L,
-                                int64_t E, int abf) {
+__global__ void conv_fwd_kernel(const void* __restrict__ xi, int64_t ld_x, const void* __restrict__ halo,
+                                const float* __restrict__ w, const float* __restrict__ bias, void* __restrict__ u,
+                                int64_t Bsz, int64_t L, int64_t E, int abf) {
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t b = blockIdx.z;
   const int64_t t0 = int64_t(blockIdx.y) * CONV_T;
@@ -514,10 +565,7 @@ __global__ void conv_fwd_kernel(const void* __restrict__ xi, int64_t ld_x, const
   const float be = bias[e];
   float win[K];  // win[k] = xi[t - (K-1) + k]
 #pragma unroll
-  for (int k = 0; k < K - 1; ++k) {
-    const int64_t tt = t0 - (K - 1) + k;
-    win[k] = tt >= 0 ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f;
-  }
+  for (int k = 0; k < K - 1; ++k) win[k] = xi_at(xi, ld_x, halo, abf, b, L, E, K, t0 - (K - 1) + k, e);
   const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
 #pragma unroll 4
   for (int64_t t = t0; t < t1; ++t) {
@@ -535,10 +583,10 @@ __global__ void conv_fwd_kernel(const void* __restrict__ xi, int64_t ld_x, const
 // (written with pitch ld_dx), and per-(token slab, channel) partials of grad w and grad b in rows of
 // E*K + E floats: [grad w as (E, K) | grad b (E)], one row per (batch, slab).
 template <int K>
-__global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const float* __restrict__ w,
-                                const float* __restrict__ bias, const float* __restrict__ du,
-                                void* __restrict__ dxi, int64_t ld_dx, float* __restrict__ part,
-                                int64_t Bsz, int64_t L, int64_t E, int abf) {
+__global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const void* __restrict__ halo,
+                                const float* __restrict__ w, const float* __restrict__ bias,
+                                const float* __restrict__ du, void* __restrict__ dxi, int64_t ld_dx,
+                                float* __restrict__ part, int64_t Bsz, int64_t L, int64_t E, int abf) {
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t b = blockIdx.z;
   const int64_t tb = blockIdx.y;
@@ -549,7 +597,7 @@ __global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const
   for (int k = 0; k < K; ++k) wk[k] = w[e * K + k];
   const float be = bias[e];
   const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
-  auto xin = [&](int64_t tt) { return (tt >= 0 && tt < L) ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f; };
+  auto xin = [&](int64_t tt) { return xi_at(xi, ld_x, halo, abf, b, L, E, K, tt, e); };
   // xs[j] = x[t - (K-1) + j], j = 0 .. 2K-2 (the inputs of dxc[t .. t+K-1] and of grad w at t)
   float xs[2 * K - 1];
 #pragma unroll
@@ -597,47 +645,78 @@ __global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const
   row[E * K + e] = gb;
 }
 
+// Gradient of the halo rows: dxi_halo[b, K-1+j, e] = sum_k w[e, k] dxc[j + K-1-k] over the tokens
+// 0 <= j + K-1-k < L that read halo row j (j = -(K-1) .. -1), float32 (Bsz, K-1, E).
 template <int K>
-static void launch_conv_fwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w,
-                            const float* bias, void* u, int64_t Bsz, int64_t L, int64_t E, int abf) {
-  conv_fwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, w, bias, u, Bsz, L, E, abf);
-}
-template <int K>
-static void launch_conv_bwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w,
-                            const float* bias, const float* du, void* dxi, int64_t ld_dx, float* part, int64_t Bsz,
-                            int64_t L, int64_t E, int abf) {
-  conv_bwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf);
+__global__ void conv_halo_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const void* __restrict__ halo,
+                                     const float* __restrict__ w, const float* __restrict__ bias,
+                                     const float* __restrict__ du, float* __restrict__ dhalo, int64_t Bsz,
+                                     int64_t L, int64_t E, int abf) {
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t b = blockIdx.y;
+  if (e >= E || K < 2) return;
+  float wk[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) wk[k] = w[e * K + k];
+  const float be = bias[e];
+  float dxc[K > 1 ? K - 1 : 1];  // dxc[t], t = 0 .. K-2
+#pragma unroll
+  for (int t = 0; t < K - 1; ++t) {
+    float acc = be;
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], xi_at(xi, ld_x, halo, abf, b, L, E, K, t - (K - 1) + k, e), acc);
+    dxc[t] = t < L ? du[(b * L + t) * E + e] * silu_prime_f(acc) : 0.f;
+  }
+#pragma unroll
+  for (int j = -(K - 1); j < 0; ++j) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int t = j + (K - 1) - k;
+      if (t >= 0) acc = fmaf(wk[k], dxc[t], acc);
+    }
+    dhalo[(b * (K - 1) + (K - 1) + j) * E + e] = acc;
+  }
 }
 
-static int conv_fwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w, const float* bias,
-                    void* u, int64_t Bsz, int64_t L, int64_t E, int abf) {
+template <int K>
+static void launch_conv_fwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo, const float* w,
+                            const float* bias, void* u, int64_t Bsz, int64_t L, int64_t E, int abf) {
+  conv_fwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, halo, w, bias, u, Bsz, L, E, abf);
+}
+template <int K>
+static void launch_conv_bwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo,
+                            const float* w, const float* bias, const float* du, void* dxi, int64_t ld_dx, float* part,
+                            int64_t Bsz, int64_t L, int64_t E, int abf, float* dhalo) {
+  conv_bwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf);
+  if (dhalo && K > 1)
+    conv_halo_bwd_kernel<K><<<dim3(grid.x, unsigned(Bsz)), 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dhalo, Bsz, L,
+                                                                         E, abf);
+}
+
+static int conv_fwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo, const float* w,
+                    const float* bias, void* u, int64_t Bsz, int64_t L, int64_t E, int abf) {
   switch (K) {
-    case 1: launch_conv_fwd<1>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
-    case 2: launch_conv_fwd<2>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
-    case 3: launch_conv_fwd<3>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
-    case 4: launch_conv_fwd<4>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
-    case 5: launch_conv_fwd<5>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
-    case 6: launch_conv_fwd<6>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
-    case 7: launch_conv_fwd<7>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
-    case 8: launch_conv_fwd<8>(grid, s, xi, ld_x, w, bias, u, Bsz, L, E, abf); break;
+#define PGF_CONV_FWD(k) \
+    case k: launch_conv_fwd<k>(grid, s, xi, ld_x, halo, w, bias, u, Bsz, L, E, abf); break;
+    PGF_CONV_FWD(1) PGF_CONV_FWD(2) PGF_CONV_FWD(3) PGF_CONV_FWD(4)
+    PGF_CONV_FWD(5) PGF_CONV_FWD(6) PGF_CONV_FWD(7) PGF_CONV_FWD(8)
+#undef PGF_CONV_FWD
     default: set_error("mamba mixer: d_conv %d unsupported", K); return PGF_ERR_UNSUPPORTED;
   }
   PGF_LAUNCH_CHECK();
   return PGF_OK;
 }
 
-static int conv_bwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const float* w, const float* bias,
-                    const float* du, void* dxi, int64_t ld_dx, float* part, int64_t Bsz, int64_t L, int64_t E,
-                    int abf) {
+static int conv_bwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo, const float* w,
+                    const float* bias, const float* du, void* dxi, int64_t ld_dx, float* part, int64_t Bsz, int64_t L,
+                    int64_t E, int abf, float* dhalo) {
   switch (K) {
-    case 1: launch_conv_bwd<1>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
-    case 2: launch_conv_bwd<2>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
-    case 3: launch_conv_bwd<3>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
-    case 4: launch_conv_bwd<4>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
-    case 5: launch_conv_bwd<5>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
-    case 6: launch_conv_bwd<6>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
-    case 7: launch_conv_bwd<7>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
-    case 8: launch_conv_bwd<8>(grid, s, xi, ld_x, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf); break;
+#define PGF_CONV_BWD(k) \
+    case k: launch_conv_bwd<k>(grid, s, xi, ld_x, halo, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf, dhalo); break;
+    PGF_CONV_BWD(1) PGF_CONV_BWD(2) PGF_CONV_BWD(3) PGF_CONV_BWD(4)
+    PGF_CONV_BWD(5) PGF_CONV_BWD(6) PGF_CONV_BWD(7) PGF_CONV_BWD(8)
+#undef PGF_CONV_BWD
     default: set_error("mamba mixer: d_conv %d unsupported", K); return PGF_ERR_UNSUPPORTED;
   }
   PGF_LAUNCH_CHECK();
@@ -673,6 +752,8 @@ struct Bufs {
   size_t cs_bytes;
   void* split;  // split-K partials of the weight gradients
   size_t split_bytes;
+  void* xi_halo;     // pre-conv projection of the halo rows (Bsz, K-1, E), activation dtype
+  float* dxi_halo;   // its gradient (Bsz, K-1, E)
 };
 
 // column-sum scratch: grad dt_b over tokens and the conv parameter partials over slabs
@@ -715,6 +796,8 @@ static size_t bufs_bytes(const Plan& p, int dtype, int bwd, bool saved_external 
   const size_t es = dtype ? 2 : 4, T = size_t(p.T), E = size_t(p.E);
   size_t b = saved_external ? 0 : saved_part_bytes(p, dtype);
   auto add = [&](size_t n) { b += Workspace::round(n); };
+  add(size_t(p.Bsz) * (p.K - 1) * E * es + 16);  // xi_halo
+  add(size_t(p.Bsz) * (p.K - 1) * E * 4 + 16);   // dxi_halo
   if (dtype) {
     add(size_t(2 * E) * p.d * 2); add(size_t(p.d) * E * 2);                       // in_w, out_w
     add(size_t(p.XD) * E * 2); add(size_t(E) * p.R * 2);                           // x_w, dt_w
@@ -752,7 +835,9 @@ static int carve(Workspace& W, Workspace* Wsaved, Bufs& B, const Plan& p, int dt
   B.sdt = F.take<float>(size_t(p.Bsz) * p.nC * E);
   B.hC = F.take<float>(size_t(p.Bsz) * (p.nC + 1) * E * NST);
   B.ckpt = F.take<float>(size_t(p.Bsz) * p.nC * KS * E * NST);
-  bool ok = B.xz && B.u && B.y && B.xdbl && B.dtr && B.hloc && B.sdt && B.hC && B.ckpt;
+  B.xi_halo = W.take<char>(size_t(p.Bsz) * (p.K - 1) * E * es + 16);
+  B.dxi_halo = W.take<float>(size_t(p.Bsz) * (p.K - 1) * E + 4);
+  bool ok = B.xz && B.u && B.y && B.xdbl && B.dtr && B.hloc && B.sdt && B.hC && B.ckpt && B.xi_halo && B.dxi_halo;
   if (dtype) {
     B.xdbl_bf = F.take<__nv_bfloat16>(T * p.XD);
     B.in_wb = W.take<__nv_bfloat16>(size_t(2 * E) * p.d);
@@ -824,47 +909,94 @@ static Args args_of(const Params& P, const Plan& p, const Bufs& B, int dtype, bo
   return a;
 }
 
+// Carries of a mixer call that covers one segment of a longer sequence (all nullable).
+struct Ctx {
+  const void* x_halo;    // (Bsz, K-1, d) mixer input rows before the segment: the conv's left context
+  const float* h_init;   // (Bsz, E, N) scan state entering the segment
+  float* h_final;        // (Bsz, E, N) scan state after the segment
+  float* sum_dt;         // (Bsz, E) fwd_begin: sum of delta over the segment
+  const float* dh_end;   // (Bsz, E, N) adjoint entering the segment's last token from the right
+  const float* dA_end;   // (Bsz, E, N) decay of the token after the segment
+  float* dh_start;       // (Bsz, E, N) adjoint at the segment's first token
+  float* dA_start;       // (Bsz, E, N) decay of the segment's first token
+  float* sum_dt_excl;    // (Bsz, E) sum of delta over every token but the first
+  void* g_x_halo;        // (Bsz, K-1, d) gradient of x_halo
+};
+enum { MSTAGE_ALL = 0, MSTAGE_BEGIN = 1, MSTAGE_FINISH = 2 };
+
 // forward up to the gated scan output y (B.y); optionally saves the 8-token scan checkpoints for
-// the backward.  The weights must already be converted (convert_weights).
+// the backward.  The weights must already be converted (convert_weights).  BEGIN stops after the
+// chunk summaries composed from a zero state (the segment summary into c.h_final / c.sum_dt);
+// FINISH continues on BEGIN's workspace from c.h_init.
 static int forward_to_y(const void* x, const Params& P, const Plan& p, Bufs& B, int dtype, bool save,
-                        Args& a, cudaStream_t s, const float* states_in = nullptr, float* states_out = nullptr) {
+                        Args& a, cudaStream_t s, const float* states_in = nullptr, float* states_out = nullptr,
+                        const Ctx* ctx = nullptr, int stage = MSTAGE_ALL) {
+  static const Ctx none = {};
+  const Ctx& c = ctx ? *ctx : none;
   const int64_t T = p.T, E = p.E;
   const void* in_w = dtype ? static_cast<const void*>(B.in_wb) : static_cast<const void*>(P.in_w);
-  // xz = x W_in^T
-  PGF_TRY(run_gemm(G_(T, 2 * E, p.d, x, dtype, p.d, 0, in_w, dtype, p.d, 0, B.xz, dtype, 2 * E), s));
-  // u = SiLU(conv(xi))
-  {
-    dim3 grid(ceil_div(E, 128), ceil_div(p.L, CONV_T), unsigned(p.Bsz));
-    PGF_TRY(conv_fwd(int(p.K), grid, s, B.xz, 2 * E, P.conv_w, P.conv_b, B.u, p.Bsz, p.L, E, dtype));
-  }
-  // x_dbl = u W_x^T (float32), dt_raw = x_dbl[:, :R] W_dt^T + b_dt.  bf16 mode: bf16 operands
-  // (weights and x_dbl copies) so both products run on the tensor cores.
-  if (dtype) {
-    PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, 1, E, 0, B.x_wb, 1, E, 0, B.xdbl, 0, p.XD), s));
-    PGF_TRY(to_bf16(B.xdbl, B.xdbl_bf, T * p.XD, s));
-    Gemm g = G_(T, E, p.R, B.xdbl_bf, 1, p.XD, 0, B.dt_wb, 1, p.R, 0, B.dtr, 0, E);
-    g.epi.bias = P.dt_b;
-    PGF_TRY(run_gemm(g, s));
-  } else {
-    PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, 0, E, 0, P.x_w, 0, E, 0, B.xdbl, 0, p.XD), s));
-    Gemm g = G_(T, E, p.R, B.xdbl, 0, p.XD, 0, P.dt_w, 0, p.R, 0, B.dtr, 0, E);
-    g.epi.bias = P.dt_b;
-    PGF_TRY(run_gemm(g, s));
+  const void* halo = (c.x_halo && p.K > 1) ? B.xi_halo : nullptr;
+  if (stage != MSTAGE_FINISH) {
+    // xz = x W_in^T
+    PGF_TRY(run_gemm(G_(T, 2 * E, p.d, x, dtype, p.d, 0, in_w, dtype, p.d, 0, B.xz, dtype, 2 * E), s));
+    // the halo rows' pre-conv projection xi = x_halo W_in[:E]^T
+    if (halo) PGF_TRY(run_gemm(G_(p.Bsz * (p.K - 1), E, p.d, c.x_halo, dtype, p.d, 0, in_w, dtype, p.d, 0, B.xi_halo,
+                                  dtype, E), s));
+    // u = SiLU(conv(xi))
+    {
+      dim3 grid(ceil_div(E, 128), ceil_div(p.L, CONV_T), unsigned(p.Bsz));
+      PGF_TRY(conv_fwd(int(p.K), grid, s, B.xz, 2 * E, halo, P.conv_w, P.conv_b, B.u, p.Bsz, p.L, E, dtype));
+    }
+    // x_dbl = u W_x^T (float32), dt_raw = x_dbl[:, :R] W_dt^T + b_dt.  bf16 mode: bf16 operands
+    // (weights and x_dbl copies) so both products run on the tensor cores.
+    if (dtype) {
+      PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, 1, E, 0, B.x_wb, 1, E, 0, B.xdbl, 0, p.XD), s));
+      PGF_TRY(to_bf16(B.xdbl, B.xdbl_bf, T * p.XD, s));
+      Gemm g = G_(T, E, p.R, B.xdbl_bf, 1, p.XD, 0, B.dt_wb, 1, p.R, 0, B.dtr, 0, E);
+      g.epi.bias = P.dt_b;
+      PGF_TRY(run_gemm(g, s));
+    } else {
+      PGF_TRY(run_gemm(G_(T, p.XD, E, B.u, 0, E, 0, P.x_w, 0, E, 0, B.xdbl, 0, p.XD), s));
+      Gemm g = G_(T, E, p.R, B.xdbl, 0, p.XD, 0, P.dt_w, 0, p.R, 0, B.dtr, 0, E);
+      g.epi.bias = P.dt_b;
+      PGF_TRY(run_gemm(g, s));
+    }
   }
   a = args_of(P, p, B, dtype, save);
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
   const size_t hc_bytes = size_t(p.Bsz) * (p.nC + 1) * E * NST * sizeof(float);
-  if (states_in) {
-    // the boundary states of an earlier forward on the same input: no chunk pass or compose
-    PGF_CUDA(cudaMemcpyAsync(B.hC, states_in, hc_bytes, cudaMemcpyDeviceToDevice, s));
-  } else {
+  const int64_t nth = p.Bsz * E * NST;
+  if (stage == MSTAGE_BEGIN) {
     prof_begin(PROF_SSM_CHUNK_FWD, s);
     chunk_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
     prof_end(PROF_SSM_CHUNK_FWD, s, double(T) * (dtype ? 2 : 4) * (2.0 * E + NST));
     PGF_LAUNCH_CHECK();
-    const int64_t nth = p.Bsz * E * NST;
+    a.h_final = c.h_final;
+    a.sum_dt_out = c.sum_dt;
     compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
     PGF_LAUNCH_CHECK();
+    return PGF_OK;
+  }
+  if (states_in) {
+    // the boundary states of an earlier forward on the same input: no chunk pass or compose
+    PGF_CUDA(cudaMemcpyAsync(B.hC, states_in, hc_bytes, cudaMemcpyDeviceToDevice, s));
+    if (c.h_final)
+      PGF_CUDA(cudaMemcpy2DAsync(c.h_final, size_t(E) * NST * sizeof(float), B.hC + p.nC * E * NST,
+                                 size_t(p.nC + 1) * E * NST * sizeof(float), size_t(E) * NST * sizeof(float),
+                                 size_t(p.Bsz), cudaMemcpyDeviceToDevice, s));
+  } else {
+    if (stage != MSTAGE_FINISH) {
+      prof_begin(PROF_SSM_CHUNK_FWD, s);
+      chunk_fwd_kernel<<<grid, THREADS, 0, s>>>(a);
+      prof_end(PROF_SSM_CHUNK_FWD, s, double(T) * (dtype ? 2 : 4) * (2.0 * E + NST));
+      PGF_LAUNCH_CHECK();
+    }
+    a.h_init = c.h_init;
+    a.h_final = c.h_final;
+    compose_fwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
+    PGF_LAUNCH_CHECK();
+    a.h_init = nullptr;
+    a.h_final = nullptr;
     if (states_out) PGF_CUDA(cudaMemcpyAsync(states_out, B.hC, hc_bytes, cudaMemcpyDeviceToDevice, s));
   }
   prof_begin(PROF_SSM_OUT_FWD, s);
@@ -893,9 +1025,10 @@ namespace mstd {
 static int mixer_fwd_impl(const void* x, const Params& P, void* out, void* saved, size_t saved_bytes, int64_t Bsz,
                           int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws,
                           size_t ws_bytes, cudaStream_t s, const float* states_in = nullptr,
-                          float* states_out = nullptr) {
+                          float* states_out = nullptr, const Ctx* ctx = nullptr, int stage = MSTAGE_ALL) {
   PGF_TRY(check_dims(Bsz, L, d, E, R, N, K, dtype));
-  PGF_CHECK_ARG(x && P.in_w && P.conv_w && P.conv_b && P.x_w && P.dt_w && P.dt_b && P.A_log && P.Dp && P.out_w && out,
+  PGF_CHECK_ARG(x && P.in_w && P.conv_w && P.conv_b && P.x_w && P.dt_w && P.dt_b && P.A_log && P.Dp && P.out_w &&
+                    (out || stage == MSTAGE_BEGIN),
                 "mamba_mixer_fwd: null pointer");
   Plan p = plan_of(Bsz, L, d, E, R, N, K);
   Workspace W(ws, ws_bytes);
@@ -904,7 +1037,8 @@ static int mixer_fwd_impl(const void* x, const Params& P, void* out, void* saved
   PGF_TRY(carve(W, saved ? &Ws : nullptr, B, p, dtype, 0));
   PGF_TRY(convert_weights(P, p, B, dtype, s));
   Args a;
-  PGF_TRY(forward_to_y(x, P, p, B, dtype, saved != nullptr, a, s, states_in, states_out));
+  PGF_TRY(forward_to_y(x, P, p, B, dtype, saved != nullptr, a, s, states_in, states_out, ctx, stage));
+  if (stage == MSTAGE_BEGIN) return PGF_OK;
   const void* ow = dtype ? static_cast<const void*>(B.out_wb) : static_cast<const void*>(P.out_w);
   return run_gemm(G_(p.T, d, E, B.y, dtype, E, 0, ow, dtype, E, 0, out, dtype, d), s);
 }
@@ -981,12 +1115,18 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
                           float* g_conv_b, float* g_x_w, float* g_dt_w, float* g_dt_b, float* g_A_log, float* g_Dp,
                           float* g_out_w, void* g_x, int accumulate, const void* saved, size_t saved_bytes,
                           int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype,
-                          void* ws, size_t ws_bytes, cudaStream_t s) {
+                          void* ws, size_t ws_bytes, cudaStream_t s, const Ctx* ctx = nullptr,
+                          int stage = MSTAGE_ALL) {
+  static const Ctx none = {};
+  const Ctx& c = ctx ? *ctx : none;
   PGF_TRY(check_dims(Bsz, L, d, E, R, N, K, dtype));
   PGF_CHECK_ARG(x && g_out && P.in_w && P.conv_w && P.conv_b && P.x_w && P.dt_w && P.dt_b && P.A_log && P.Dp &&
-                    P.out_w && g_in_w && g_conv_w && g_conv_b && g_x_w && g_dt_w && g_dt_b && g_A_log && g_Dp &&
-                    g_out_w && g_x,
+                    P.out_w,
                 "mamba_mixer_bwd: null pointer");
+  PGF_CHECK_ARG(stage == MSTAGE_BEGIN || (g_in_w && g_conv_w && g_conv_b && g_x_w && g_dt_w && g_dt_b && g_A_log &&
+                                          g_Dp && g_out_w && g_x),
+                "mamba_mixer_bwd: null pointer");
+  PGF_CHECK_ARG(stage == MSTAGE_ALL || saved, "mamba_mixer_bwd: a staged backward needs the saved forward");
   const float *in_w = P.in_w, *conv_w = P.conv_w, *conv_b = P.conv_b, *x_w = P.x_w, *dt_w = P.dt_w;
   (void)conv_b;
   Plan p = plan_of(Bsz, L, d, E, R, N, K);
@@ -999,19 +1139,29 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
   if (saved) {
     a = args_of(P, p, B, dtype, false);  // the forward of fwd_save is in `saved`
   } else {
-    PGF_TRY(forward_to_y(x, P, p, B, dtype, true, a, s));
+    Ctx fc = {};
+    fc.x_halo = c.x_halo;
+    fc.h_init = c.h_init;
+    PGF_TRY(forward_to_y(x, P, p, B, dtype, true, a, s, nullptr, nullptr, &fc));
   }
   const int64_t T = p.T;
   const size_t es = dtype ? 2 : 4;
   const void* ow = dtype ? static_cast<const void*>(B.out_wb) : static_cast<const void*>(P.out_w);
-  // out_proj: grad W_out (+)= g^T y ; gy = g W_out
-  {
+  const void* halo = (c.x_halo && p.K > 1) ? B.xi_halo : nullptr;
+  if (halo && saved && stage != MSTAGE_BEGIN) {
+    // the halo rows' pre-conv projection (a workspace buffer, not part of the saved forward)
+    const void* iw = dtype ? static_cast<const void*>(B.in_wb) : static_cast<const void*>(P.in_w);
+    PGF_TRY(run_gemm(mstd::G_(p.Bsz * (p.K - 1), E, d, c.x_halo, dtype, d, 0, iw, dtype, d, 0, B.xi_halo, dtype, E),
+                     s));
+  }
+  // out_proj: grad W_out (+)= g^T y ; gy = g W_out (BEGIN computes gy, FINISH the weight gradient)
+  if (stage != MSTAGE_BEGIN) {
     Gemm g = mstd::G_(d, E, T, g_out, dtype, d, 1, B.y, dtype, E, 1, g_out_w, 0, E);
     g.epi.accumulate = accumulate;
     g.ws = B.split; g.ws_bytes = B.split_bytes;
     PGF_TRY(run_gemm(g, s));
-    PGF_TRY(run_gemm(mstd::G_(T, E, d, g_out, dtype, d, 0, ow, dtype, E, 1, B.gy, dtype, E), s));
   }
+  if (stage != MSTAGE_FINISH) PGF_TRY(run_gemm(mstd::G_(T, E, d, g_out, dtype, d, 0, ow, dtype, E, 1, B.gy, dtype, E), s));
   // scan backward
   a.g = B.gy;
   // bf16 mode: grad dt_raw and grad x_dbl are bf16 (tensor-core operands of the products below)
@@ -1025,11 +1175,23 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
   a.dloc = B.dloc; a.sdt2 = B.sdt2; a.dt0 = B.dt0; a.X = B.X;
   a.ckpt_write = 0;
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
-  mstd::chunk_bwd_kernel<<<grid, mstd::THREADS, 0, s>>>(a);
-  PGF_LAUNCH_CHECK();
+  if (stage != MSTAGE_FINISH) {
+    mstd::chunk_bwd_kernel<<<grid, mstd::THREADS, 0, s>>>(a);
+    PGF_LAUNCH_CHECK();
+  }
   const int64_t nth = p.Bsz * E * mstd::NST;
+  if (stage == MSTAGE_BEGIN) {
+    // the segment's adjoint summary for a zero carry at its end
+    a.dh_start = c.dh_start; a.dA_start = c.dA_start; a.sum_dt_excl = c.sum_dt_excl;
+    mstd::compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
+    PGF_LAUNCH_CHECK();
+    return PGF_OK;
+  }
+  a.dh_end = c.dh_end; a.dA_end = c.dA_end; a.dh_start = c.dh_start; a.dA_start = c.dA_start;
   mstd::compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a);
   PGF_LAUNCH_CHECK();
+  a.dh_end = a.dA_end = nullptr;
+  a.dh_start = a.dA_start = nullptr;
   const size_t smem = size_t(mstd::ST * mstd::WARPS * 32 + 2 * 3 * mstd::ST * mstd::DC) * 4;
   prof_begin(PROF_SSM_MAIN_BWD, s);
   mstd::main_bwd_kernel<<<grid, mstd::THREADS, smem, s>>>(a);
@@ -1065,8 +1227,8 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
   // conv + SiLU backward -> dxz[:, :E]
   {
     dim3 cg(ceil_div(E, 128), ceil_div(p.L, mstd::CONV_T), unsigned(p.Bsz));
-    PGF_TRY(mstd::conv_bwd(int(K), cg, s, B.xz, 2 * E, conv_w, conv_b, B.gu_tot, B.dxz, 2 * E, B.cpart, p.Bsz, p.L,
-                           E, dtype));
+    PGF_TRY(mstd::conv_bwd(int(K), cg, s, B.xz, 2 * E, halo, conv_w, conv_b, B.gu_tot, B.dxz, 2 * E, B.cpart, p.Bsz,
+                           p.L, E, dtype, halo ? B.dxi_halo : nullptr));
     // grad w, grad b: fixed-order column sums of the (batch, slab) partial rows
     const int64_t cnt = p.Bsz * ((p.L + mstd::CONV_T - 1) / mstd::CONV_T);
     PGF_TRY(colsum(B.cpart, 0, cnt, E * K, E * (K + 1), g_conv_w, accumulate, B.cs, B.cs_bytes, s));
@@ -1080,6 +1242,15 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
     PGF_TRY(run_gemm(g, s));
     const void* iw = dtype ? (const void*)B.in_wb : (const void*)in_w;
     PGF_TRY(run_gemm(mstd::G_(T, d, 2 * E, B.dxz, dtype, 2 * E, 0, iw, dtype, d, 1, g_x, dtype, d), s));
+    if (halo) {
+      // the halo rows fed this segment's conv through W_in[:E]: grad W_in[:E] += dxi_halo^T x_halo,
+      // and their own gradient g_x_halo = dxi_halo W_in[:E] goes back to the segment they belong to
+      const int64_t Th = p.Bsz * (p.K - 1);
+      Gemm gh = mstd::G_(E, d, Th, B.dxi_halo, 0, E, 1, c.x_halo, dtype, d, 1, g_in_w, 0, d);
+      gh.epi.accumulate = 1;
+      PGF_TRY(run_gemm(gh, s));
+      if (c.g_x_halo) PGF_TRY(run_gemm(mstd::G_(Th, d, E, B.dxi_halo, 0, E, 0, in_w, 0, d, 1, c.g_x_halo, dtype, d), s));
+    }
   }
   return PGF_OK;
 }
@@ -1112,4 +1283,87 @@ extern "C" int pgf_mamba_mixer_bwd_saved(const void* x, const void* g_out, const
   return mstd::mixer_bwd_impl(x, g_out, P, g_in_w, g_conv_w, g_conv_b, g_x_w, g_dt_w, g_dt_b, g_A_log, g_Dp, g_out_w,
                               g_x, accumulate, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
                               as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------------------------
+// One segment of a longer sequence: the calls above with the carries of Ctx (conv halo, scan state
+// and adjoint across the segment boundary), one call each or staged for sequence sharding.
+// ---------------------------------------------------------------------------------------------
+#define PGF_MIXER_W const float *in_w, const float *conv_w, const float *conv_b, const float *x_w, \
+    const float *dt_w, const float *dt_b, const float *A_log, const float *Dp, const float *out_w
+#define PGF_MIXER_G float *g_in_w, float *g_conv_w, float *g_conv_b, float *g_x_w, float *g_dt_w, float *g_dt_b, \
+    float *g_A_log, float *g_Dp, float *g_out_w
+#define PGF_MIXER_DIMS int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K
+
+extern "C" int pgf_mamba_mixer_fwd_seg(const void* x, PGF_MIXER_W, const void* x_halo, const float* h_init,
+                                       const float* states_in, void* out, float* h_final, float* states_out,
+                                       void* saved, size_t saved_bytes, PGF_MIXER_DIMS, int dtype, void* ws,
+                                       size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(!(states_in && h_init), "mamba_mixer_fwd_seg: the states already include the initial state");
+  PGF_CHECK_ARG(!(states_in && states_out), "mamba_mixer_fwd_seg: states in and out");
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Ctx c = {};
+  c.x_halo = x_halo; c.h_init = h_init; c.h_final = h_final;
+  return mstd::mixer_fwd_impl(x, P, out, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream), states_in, states_out, &c);
+}
+
+extern "C" int pgf_mamba_mixer_fwd_begin(const void* x, PGF_MIXER_W, const void* x_halo, float* h_seg, float* sum_dt,
+                                         PGF_MIXER_DIMS, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  PGF_CHECK_ARG(h_seg && sum_dt, "mamba_mixer_fwd_begin: null pointer");
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Ctx c = {};
+  c.x_halo = x_halo; c.h_final = h_seg; c.sum_dt = sum_dt;
+  return mstd::mixer_fwd_impl(x, P, nullptr, nullptr, 0, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream), nullptr, nullptr, &c, mstd::MSTAGE_BEGIN);
+}
+
+extern "C" int pgf_mamba_mixer_fwd_finish(const void* x, PGF_MIXER_W, const void* x_halo, const float* h_init,
+                                          void* out, float* states_out, PGF_MIXER_DIMS, int dtype, void* ws,
+                                          size_t ws_bytes, pgf_stream_t stream) {
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Ctx c = {};
+  c.x_halo = x_halo; c.h_init = h_init;
+  return mstd::mixer_fwd_impl(x, P, out, nullptr, 0, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes, as_stream(stream),
+                              nullptr, states_out, &c, mstd::MSTAGE_FINISH);
+}
+
+extern "C" int pgf_mamba_mixer_bwd_seg(const void* x, const void* g_out, PGF_MIXER_W, const void* x_halo,
+                                       const void* saved, size_t saved_bytes, const float* dh_end, const float* dA_end,
+                                       PGF_MIXER_G, void* g_x, void* g_x_halo, float* dh_start, float* dA_start,
+                                       int accumulate, PGF_MIXER_DIMS, int dtype, void* ws, size_t ws_bytes,
+                                       pgf_stream_t stream) {
+  PGF_CHECK_ARG(saved, "mamba_mixer_bwd_seg: null saved buffer");
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Ctx c = {};
+  c.x_halo = x_halo; c.dh_end = dh_end; c.dA_end = dA_end; c.dh_start = dh_start; c.dA_start = dA_start;
+  c.g_x_halo = g_x_halo;
+  return mstd::mixer_bwd_impl(x, g_out, P, g_in_w, g_conv_w, g_conv_b, g_x_w, g_dt_w, g_dt_b, g_A_log, g_Dp, g_out_w,
+                              g_x, accumulate, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream), &c);
+}
+
+extern "C" int pgf_mamba_mixer_bwd_begin(const void* x, const void* g_out, PGF_MIXER_W, const void* x_halo,
+                                         const void* saved, size_t saved_bytes, float* dh_start, float* dA_start,
+                                         float* sum_dt_excl, PGF_MIXER_DIMS, int dtype, void* ws, size_t ws_bytes,
+                                         pgf_stream_t stream) {
+  PGF_CHECK_ARG(dh_start && dA_start && sum_dt_excl, "mamba_mixer_bwd_begin: null pointer");
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Ctx c = {};
+  c.x_halo = x_halo; c.dh_start = dh_start; c.dA_start = dA_start; c.sum_dt_excl = sum_dt_excl;
+  return mstd::mixer_bwd_impl(x, g_out, P, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                              nullptr, nullptr, 0, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream), &c, mstd::MSTAGE_BEGIN);
+}
+
+extern "C" int pgf_mamba_mixer_bwd_finish(const void* x, const void* g_out, PGF_MIXER_W, const void* x_halo,
+                                          const void* saved, size_t saved_bytes, const float* dh_end,
+                                          const float* dA_end, PGF_MIXER_G, void* g_x, void* g_x_halo, int accumulate,
+                                          PGF_MIXER_DIMS, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream) {
+  mstd::Params P{in_w, conv_w, conv_b, x_w, dt_w, dt_b, A_log, Dp, out_w};
+  mstd::Ctx c = {};
+  c.x_halo = x_halo; c.dh_end = dh_end; c.dA_end = dA_end; c.g_x_halo = g_x_halo;
+  return mstd::mixer_bwd_impl(x, g_out, P, g_in_w, g_conv_w, g_conv_b, g_x_w, g_dt_w, g_dt_b, g_A_log, g_Dp, g_out_w,
+                              g_x, accumulate, saved, saved_bytes, Bsz, L, d, E, R, N, K, dtype, ws, ws_bytes,
+                              as_stream(stream), &c, mstd::MSTAGE_FINISH);
 }

@@ -703,3 +703,129 @@ def mamba_mixer_bwd(x, g, p, saved: Optional[torch.Tensor] = None):
                                            saved.numel(), Bsz, L_, d, E, R, N, K, _dt(x), _p(ws), ws.numel(),
                                            _stream()), "mamba_mixer_bwd_saved")
     return grads, gx
+
+
+# --------------------------------------------------------------------------- mixer over segments
+def _mixer_prep(x, p):
+    _cuda(x, p["in_w"])
+    x = _c(x)
+    dims = _mixer_dims(x, p)
+    q = {k: _f32(p[k]) for k in MIXER_KEYS}
+    return x, dims, q
+
+
+def _halo(x_halo, x):
+    return None if x_halo is None else _c(x_halo.to(x.dtype))
+
+
+def mamba_mixer_fwd_seg(x, p, x_halo=None, h_init=None, states_in=None, want_h_final=False, want_states=False,
+                        save=False):
+    """The mixer over one segment of a longer sequence: x_halo (Bsz, K-1, d) the mixer inputs of the
+    K-1 tokens before it (conv context), h_init the scan state entering it, states_in the boundary
+    states of an earlier call with want_states on the same input.  Returns (out, h_final, states,
+    saved) (None where not asked)."""
+    x, (Bsz, L_, d, E, R, N, K), q = _mixer_prep(x, p)
+    Lb = lib()
+    out = torch.empty_like(x)
+    hf = torch.empty(Bsz, E, N, device=x.device) if want_h_final else None
+    st = torch.empty(Lb.pgf_mamba_mixer_states_size(Bsz, L_, d, E, R, N, K) // 4, device=x.device) if want_states \
+        else None
+    saved = _ws(Lb.pgf_mamba_mixer_saved_size(Bsz, L_, d, E, R, N, K, _dt(x)), x.device) if save else None
+    ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 0), x.device)
+    check(Lb.pgf_mamba_mixer_fwd_seg(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(_halo(x_halo, x)), _p(_f32(h_init)),
+                                     _p(states_in), _p(out), _p(hf), _p(st), _p(saved),
+                                     saved.numel() if saved is not None else 0, Bsz, L_, d, E, R, N, K, _dt(x), _p(ws),
+                                     ws.numel(), _stream()), "mamba_mixer_fwd_seg")
+    return out, hf, st, saved
+
+
+def mamba_mixer_end_state(states, Bsz, L_, d, E, R, N, K):
+    """The scan state after the segment, (Bsz, E, N), from the boundary states of mamba_mixer_fwd_seg."""
+    n1 = lib().pgf_mamba_mixer_states_size(Bsz, L_, d, E, R, N, K) // (4 * Bsz * E * N)
+    return states.view(Bsz, n1, E, N)[:, n1 - 1]
+
+
+def mamba_mixer_fwd_begin(x, p, x_halo=None):
+    """Sequence sharding, forward part 1: (h_seg, sum_dt, state) -- the segment's summary from a zero
+    start and the state mamba_mixer_fwd_finish continues from."""
+    x, (Bsz, L_, d, E, R, N, K), q = _mixer_prep(x, p)
+    Lb = lib()
+    hs = torch.empty(Bsz, E, N, device=x.device)
+    sdt = torch.empty(Bsz, E, device=x.device)
+    ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 0), x.device)
+    xh = _halo(x_halo, x)
+    check(Lb.pgf_mamba_mixer_fwd_begin(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(xh), _p(hs), _p(sdt), Bsz, L_, d, E,
+                                       R, N, K, _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_fwd_begin")
+    return hs, sdt, {"x": x, "q": q, "x_halo": xh, "ws": ws, "dims": (Bsz, L_, d, E, R, N, K)}
+
+
+def mamba_mixer_fwd_finish(state, h_init, want_states=False):
+    """Sequence sharding, forward part 2: the output from the state entering the segment (and, with
+    want_states, its boundary states for mamba_mixer_fwd_seg(states_in=...))."""
+    x, q, ws = state["x"], state["q"], state["ws"]
+    Bsz, L_, d, E, R, N, K = state["dims"]
+    out = torch.empty_like(x)
+    st = torch.empty(lib().pgf_mamba_mixer_states_size(Bsz, L_, d, E, R, N, K) // 4, device=x.device) \
+        if want_states else None
+    check(lib().pgf_mamba_mixer_fwd_finish(_p(x), *[_p(q[k]) for k in MIXER_KEYS], _p(state["x_halo"]),
+                                           _p(_f32(h_init)), _p(out), _p(st), Bsz, L_, d, E, R, N, K, _dt(x), _p(ws),
+                                           ws.numel(), _stream()), "mamba_mixer_fwd_finish")
+    return (out, st) if want_states else out
+
+
+def mamba_mixer_bwd_seg(x, g, p, saved, x_halo=None, dh_end=None, dA_end=None, want_carry=False, want_g_halo=False,
+                        acc=None):
+    """Gradients of the mixer over one segment (saved: from mamba_mixer_fwd_seg(save=True) on the same
+    input with the segment's h_init and x_halo).  Returns (grads, grad_x, grad_x_halo, dh_start,
+    dA_start); acc: a dict over MIXER_KEYS of float32 buffers to add the parameter gradients into."""
+    x, (Bsz, L_, d, E, R, N, K), q = _mixer_prep(x, p)
+    g = _c(g.to(x.dtype))
+    acc = acc or {}
+    bufs = [_acc_buffer(acc.get(k), tuple(q[k].shape), x.device, "mamba_mixer_bwd_seg") for k in MIXER_KEYS]
+    if len({a for _, a in bufs}) != 1:
+        raise ValueError("mamba_mixer_bwd_seg: give all accumulators or none")
+    grads = {k: b for k, (b, _) in zip(MIXER_KEYS, bufs)}
+    accum = bufs[0][1]
+    gx = torch.empty_like(x)
+    xh = _halo(x_halo, x)
+    gh = torch.empty_like(xh) if (want_g_halo and xh is not None) else None
+    dh0 = torch.empty(Bsz, E, N, device=x.device) if want_carry else None
+    dA0 = torch.empty(Bsz, E, N, device=x.device) if want_carry else None
+    Lb = lib()
+    ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 1), x.device)
+    check(Lb.pgf_mamba_mixer_bwd_seg(_p(x), _p(g), *[_p(q[k]) for k in MIXER_KEYS], _p(xh), _p(saved), saved.numel(),
+                                     _p(_f32(dh_end)), _p(_f32(dA_end)), *[_p(grads[k]) for k in MIXER_KEYS], _p(gx),
+                                     _p(gh), _p(dh0), _p(dA0), accum, Bsz, L_, d, E, R, N, K, _dt(x), _p(ws),
+                                     ws.numel(), _stream()), "mamba_mixer_bwd_seg")
+    return grads, gx, gh, dh0, dA0
+
+
+def mamba_mixer_bwd_begin(x, g, p, saved, x_halo=None):
+    """Sequence sharding, backward part 1: (dh_start, dA_start, sum_dt_excl, state) for a zero end carry."""
+    x, (Bsz, L_, d, E, R, N, K), q = _mixer_prep(x, p)
+    g = _c(g.to(x.dtype))
+    Lb = lib()
+    dh0 = torch.empty(Bsz, E, N, device=x.device)
+    dA0 = torch.empty(Bsz, E, N, device=x.device)
+    sdx = torch.empty(Bsz, E, device=x.device)
+    ws = _ws(Lb.pgf_mamba_mixer_workspace(Bsz, L_, d, E, R, N, K, _dt(x), 1), x.device)
+    xh = _halo(x_halo, x)
+    check(Lb.pgf_mamba_mixer_bwd_begin(_p(x), _p(g), *[_p(q[k]) for k in MIXER_KEYS], _p(xh), _p(saved),
+                                       saved.numel(), _p(dh0), _p(dA0), _p(sdx), Bsz, L_, d, E, R, N, K, _dt(x),
+                                       _p(ws), ws.numel(), _stream()), "mamba_mixer_bwd_begin")
+    return dh0, dA0, sdx, {"x": x, "g": g, "q": q, "x_halo": xh, "saved": saved, "ws": ws,
+                           "dims": (Bsz, L_, d, E, R, N, K)}
+
+
+def mamba_mixer_bwd_finish(state, dh_end=None, dA_end=None, want_g_halo=False):
+    """Sequence sharding, backward part 2: (grads, grad_x, grad_x_halo) for the carry from the right."""
+    x, g, q, ws, saved, xh = state["x"], state["g"], state["q"], state["ws"], state["saved"], state["x_halo"]
+    Bsz, L_, d, E, R, N, K = state["dims"]
+    grads = {k: torch.empty_like(q[k]) for k in MIXER_KEYS}
+    gx = torch.empty_like(x)
+    gh = torch.empty_like(xh) if (want_g_halo and xh is not None) else None
+    check(lib().pgf_mamba_mixer_bwd_finish(_p(x), _p(g), *[_p(q[k]) for k in MIXER_KEYS], _p(xh), _p(saved),
+                                           saved.numel(), _p(_f32(dh_end)), _p(_f32(dA_end)),
+                                           *[_p(grads[k]) for k in MIXER_KEYS], _p(gx), _p(gh), 0, Bsz, L_, d, E, R,
+                                           N, K, _dt(x), _p(ws), ws.numel(), _stream()), "mamba_mixer_bwd_finish")
+    return grads, gx, gh

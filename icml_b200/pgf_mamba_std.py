@@ -103,10 +103,54 @@ class PGFMambaStdBlock(nn.Module):
         f = FFNFunction.apply(self.norm2(x1).reshape(-1, D), self.W1, self.b1, self.W2, self.b2, self.ffn_activation)
         return f.reshape(B, L, D) + x1
 
+    #: tokens per batch row of one segment (whole PGF blocks); longer sequences run segment by segment
+    segment_tokens: int = 65536
+
+    def _segments(self, B: int, L: int):
+        bs = max(int(self.block_size), 1, self.mixer.d_conv - 1)
+        per_row = max(int(self.segment_tokens) // max(B, 1), bs)
+        seg = -(-per_row // bs) * bs
+        if L <= seg:
+            return [(0, L)]
+        return [(a, min(a + seg, L)) for a in range(0, L, seg)]
+
+    def _halo_rows(self, x, a):
+        """norm1 of the K-1 rows before token a (the conv context of the segment starting there)."""
+        K = self.mixer.d_conv
+        if a == 0 or K < 2:
+            return None
+        return self.norm1.pgf_forward(x[:, a - (K - 1):a].contiguous())
+
     @torch.no_grad()
     def pgf_forward(self, x: torch.Tensor, return_ssm_states: bool = False, keep_scan: bool = False):
         """With return_ssm_states, also the scan's boundary states for pgf_backward; with keep_scan as
-        well, the mixer's saved buffer and mixer + x instead (the backward then runs no mixer forward)."""
+        well, the mixer's saved buffer and mixer + x instead (the backward then runs no mixer forward).
+        A sequence longer than one segment runs segment by segment, carrying the scan state and the
+        conv's K-1-token context (the states are then a list, one entry per segment)."""
+        B, L, D = x.shape
+        segs = self._segments(B, L)
+        if len(segs) == 1:
+            return self._forward_single(x, return_ssm_states, keep_scan)
+        p = self.mixer.params()
+        out = torch.empty_like(x)
+        states, h = [], None
+        for a, e in segs:
+            xs = x[:, a:e] if B == 1 else x[:, a:e].contiguous()
+            xn = self.norm1.pgf_forward(xs)
+            m, h, st, saved = ops.mamba_mixer_fwd_seg(xn, p, x_halo=self._halo_rows(x, a), h_init=h, want_h_final=True,
+                                                      want_states=return_ssm_states and not keep_scan,
+                                                      save=return_ssm_states and keep_scan)
+            del xn
+            x1, xn2 = ops.rmsnorm_fwd_res(m, xs, self.norm2.weight, self.norm2.eps)
+            del m
+            o = ops.ffn_fwd(xn2.reshape(-1, D), self.W1, self.b1, self.W2, self.b2, self.ffn_activation,
+                            residual=x1.reshape(-1, D), out=out[:, a:e].view(-1, D) if B == 1 else None)
+            if B != 1:
+                out[:, a:e] = o.view(B, e - a, D)
+            states.append({"saved": saved, "m_out": x1} if saved is not None else st)
+        return (out, states) if return_ssm_states else out
+
+    def _forward_single(self, x, return_ssm_states, keep_scan):
         B, L, D = x.shape
         st = None
         if return_ssm_states and keep_scan:
@@ -126,7 +170,79 @@ class PGFMambaStdBlock(nn.Module):
 
     @torch.no_grad()
     def pgf_backward(self, x: torch.Tensor, g_out: torch.Tensor, fp32_accum: bool = True,
-                     ssm_states: Optional[torch.Tensor] = None) -> Dict[str, Any]:
+                     ssm_states: Optional[Any] = None) -> Dict[str, Any]:
+        B, L, D = x.shape
+        segs = self._segments(B, L)
+        if isinstance(ssm_states, list) and len(segs) == 1:
+            ssm_states = ssm_states[0]
+        if len(segs) == 1:
+            return self._backward_single(x, g_out, ssm_states)
+        g_out = g_out.to(x.dtype)
+        p = self.mixer.params()
+        n = len(segs)
+        hs = [None] * n
+        if ssm_states is None:
+            # the scan state entering each segment (:157-175 of the reference block, per segment)
+            states = [None] * n
+            h = None
+            for j, (a, e) in enumerate(segs[:-1]):
+                xs = x[:, a:e] if B == 1 else x[:, a:e].contiguous()
+                _, h, _, _ = ops.mamba_mixer_fwd_seg(self.norm1.pgf_forward(xs), p, x_halo=self._halo_rows(x, a),
+                                                     h_init=h, want_h_final=True)
+                hs[j + 1] = h
+        else:
+            states = list(ssm_states)
+        grad_input = torch.empty_like(x)
+        acc: Dict[str, Any] = {}
+        dh = dA = g_tail = None
+        K = self.mixer.d_conv
+        for j in reversed(range(n)):
+            a, e = segs[j]
+            xs = x[:, a:e] if B == 1 else x[:, a:e].contiguous()
+            gs = g_out[:, a:e] if B == 1 else g_out[:, a:e].contiguous()
+            Ls = e - a
+            xn1 = self.norm1.pgf_forward(xs)
+            halo = self._halo_rows(x, a)
+            st = states[j]
+            states[j] = None
+            if isinstance(st, dict):
+                saved, m_out = st["saved"], st["m_out"]
+                xn2 = ops.rmsnorm_fwd(m_out, self.norm2.weight, self.norm2.eps)
+            else:
+                m_raw, _, _, saved = ops.mamba_mixer_fwd_seg(xn1, p, x_halo=halo, h_init=hs[j] if st is None else None,
+                                                             states_in=st, save=True)
+                m_out, xn2 = ops.rmsnorm_fwd_res(m_raw, xs, self.norm2.weight, self.norm2.eps)
+                del m_raw
+            fr = ops.ffn_bwd(xn2.reshape(-1, D), gs.reshape(-1, D), self.W1, self.b1, self.W2, self.ffn_activation,
+                             need_gx=True, acc=acc.get("ffn"))
+            del xn2
+            acc["ffn"] = {k: fr[k] for k in ("grad_W1", "grad_b1", "grad_W2", "grad_b2")}
+            gw2, g_m = ops.rmsnorm_bwd(m_out, fr["grad_x"].view(B, Ls, D), self.norm2.weight, self.norm2.eps,
+                                       g_add=gs, gw_acc=acc.get("norm2"))
+            del fr, m_out
+            acc["norm2"] = gw2
+            mg, gxn1, g_halo, dh, dA = ops.mamba_mixer_bwd_seg(xn1, g_m, p, saved, x_halo=halo, dh_end=dh, dA_end=dA,
+                                                                want_carry=j > 0, want_g_halo=j > 0,
+                                                                acc=acc.get("mixer"))
+            del saved, xn1
+            acc["mixer"] = mg
+            if g_tail is not None:
+                # the next segment's conv read this segment's last K-1 mixer inputs
+                gxn1[:, Ls - (K - 1):] += g_tail
+            g_tail = g_halo
+            gw1, gin = ops.rmsnorm_bwd(xs, gxn1, self.norm1.weight, self.norm1.eps, g_add=g_m,
+                                       gw_acc=acc.get("norm1"), out=grad_input[:, a:e] if B == 1 else None)
+            acc["norm1"] = gw1
+            if B != 1:
+                grad_input[:, a:e] = gin
+            del gxn1, g_m, gin
+        f = acc["ffn"]
+        grads = {"W1": f["grad_W1"], "b1": f["grad_b1"], "W2": f["grad_W2"], "b2": f["grad_b2"],
+                 "norm1.weight": acc["norm1"], "norm2.weight": acc["norm2"]}
+        grads.update(self.mixer.grads_to_named(acc["mixer"], "mixer."))
+        return {"grads": grads, "grad_input": grad_input}
+
+    def _backward_single(self, x, g_out, ssm_states):
         B, L, D = x.shape
         g_out = g_out.to(x.dtype)
         p = self.mixer.params()

@@ -422,6 +422,64 @@ int pgf_mamba_mixer_bwd_saved(const void* x, const void* g_out, const float* in_
                               const void* saved, size_t saved_bytes, int64_t Bsz, int64_t L, int64_t d,
                               int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes,
                               pgf_stream_t stream);
+/* The mixer over one segment of a longer sequence: the reference's block hand-off
+ * (pgf_mamba_block.py:86-112 forward, :207-234 backward) for this variant, whose causal conv1d also
+ * reads the K-1 tokens before the segment.  Carries (all nullable; NULL = the sequence starts or
+ * ends here):
+ *   x_halo  (Bsz, K-1, d): the mixer inputs of the K-1 tokens before the segment (conv context);
+ *   h_init / h_final (Bsz, E, N): scan state entering / leaving the segment;
+ *   dh_end / dA_end (Bsz, E, N): adjoint at the token after the segment and that token's decay
+ *     exp(delta A); dh_start / dA_start: the same at the segment's first token, for the segment before;
+ *   g_x_halo (Bsz, K-1, d): gradient of x_halo, to be added to the previous segment's input gradient
+ *     (grad W_in already includes the halo rows' part).
+ * fwd_seg: one call; states_in (from an earlier fwd_seg's states_out on the same input) replaces
+ *   the chunk pass and compose, saved (pgf_mamba_mixer_saved_size bytes) keeps the forward for bwd_seg.
+ * Staged (sequence sharding, one workspace carried between the two calls of a pair):
+ *   fwd_begin: projections, conv, chunk pass; the segment's summary from a zero state (h_seg, sum_dt
+ *   (Bsz, E): sum of delta).  fwd_finish: output from h_init (states_out: its boundary states).
+ *   bwd_begin (saved from a fwd_seg with the segment's h_init): the adjoint summary for a zero end
+ *   carry (dh_start, dA_start, sum_dt_excl (Bsz, E): sum of delta over every token but the first).
+ *   bwd_finish: every gradient for the carry (dh_end, dA_end). */
+int pgf_mamba_mixer_fwd_seg(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                            const float* x_w, const float* dt_w, const float* dt_b, const float* A_log, const float* Dp,
+                            const float* out_w, const void* x_halo, const float* h_init, const float* states_in,
+                            void* out, float* h_final, float* states_out, void* saved, size_t saved_bytes,
+                            int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K, int dtype,
+                            void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_mamba_mixer_fwd_begin(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                              const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                              const float* Dp, const float* out_w, const void* x_halo, float* h_seg, float* sum_dt,
+                              int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N, int64_t K,
+                              int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_mamba_mixer_fwd_finish(const void* x, const float* in_w, const float* conv_w, const float* conv_b,
+                               const float* x_w, const float* dt_w, const float* dt_b, const float* A_log,
+                               const float* Dp, const float* out_w, const void* x_halo, const float* h_init, void* out,
+                               float* states_out, int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                               int64_t K, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_mamba_mixer_bwd_seg(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                            const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
+                            const float* A_log, const float* Dp, const float* out_w, const void* x_halo,
+                            const void* saved, size_t saved_bytes, const float* dh_end, const float* dA_end,
+                            float* g_in_w, float* g_conv_w, float* g_conv_b, float* g_x_w, float* g_dt_w,
+                            float* g_dt_b, float* g_A_log, float* g_Dp, float* g_out_w, void* g_x, void* g_x_halo,
+                            float* dh_start, float* dA_start, int accumulate, int64_t Bsz, int64_t L, int64_t d,
+                            int64_t E, int64_t R, int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes,
+                            pgf_stream_t stream);
+int pgf_mamba_mixer_bwd_begin(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                              const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
+                              const float* A_log, const float* Dp, const float* out_w, const void* x_halo,
+                              const void* saved, size_t saved_bytes, float* dh_start, float* dA_start,
+                              float* sum_dt_excl, int64_t Bsz, int64_t L, int64_t d, int64_t E, int64_t R, int64_t N,
+                              int64_t K, int dtype, void* ws, size_t ws_bytes, pgf_stream_t stream);
+int pgf_mamba_mixer_bwd_finish(const void* x, const void* g_out, const float* in_w, const float* conv_w,
+                               const float* conv_b, const float* x_w, const float* dt_w, const float* dt_b,
+                               const float* A_log, const float* Dp, const float* out_w, const void* x_halo,
+                               const void* saved, size_t saved_bytes, const float* dh_end, const float* dA_end,
+                               float* g_in_w, float* g_conv_w, float* g_conv_b, float* g_x_w, float* g_dt_w,
+                               float* g_dt_b, float* g_A_log, float* g_Dp, float* g_out_w, void* g_x,
+                               void* g_x_halo, int accumulate, int64_t Bsz, int64_t L, int64_t d, int64_t E,
+                               int64_t R, int64_t N, int64_t K, int dtype, void* ws, size_t ws_bytes,
+                               pgf_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * The optimizer step after the PGF backward: the reference calls torch.optim.AdamW(lr=1e-3,

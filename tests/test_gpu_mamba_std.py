@@ -156,3 +156,61 @@ def test_mixer_save_from_boundary_states_is_bitwise(dtype):
     assert torch.equal(gx1, gx2)
     for k in ops.MIXER_KEYS:
         assert torch.equal(g1[k], g2[k]), k
+
+
+@pytest.mark.parametrize("mode", ["recompute", "states", "scan"])
+@pytest.mark.parametrize("K", [4, 2])
+def test_std_block_segments_match_autograd(mode, K):
+    """The Mamba-standard block over several segments (scan state and the conv's K-1-token context
+    carried forward; adjoint, decay and the context rows' gradient carried backward; parameter
+    gradients added up) against autograd of the float64 oracle over the whole sequence."""
+    B, L, d, E, R = 2, 300, 32, 64, 2
+    bp, x, gy = _case(80 + K, B, L, d, E, R, K=K)
+    blk = _block_module(bp, d, 2 * d, E // d, K, R)
+    blk.block_size = 64
+    blk.segment_tokens = 2 * 64  # B=2: 64 tokens per segment, five segments of L=300
+    assert len(blk._segments(B, L)) == 5
+    y_ref, g_ref, gx_ref = MS.block_grads(bp, x, gy)
+    xd, gd = x.float().to(DEV), gy.float().to(DEV)
+    if mode == "recompute":
+        y = blk.pgf_forward(xd)
+        r = blk.pgf_backward(xd, gd)
+    else:
+        y, st = blk.pgf_forward(xd, return_ssm_states=True, keep_scan=mode == "scan")
+        assert isinstance(st, list) and len(st) == 5
+        r = blk.pgf_backward(xd, gd, ssm_states=st)
+    assert_close(y, y_ref, name="pgf_forward")
+    assert_close(r["grad_input"], gx_ref, name="grad_input")
+    for k, v in g_ref.items():
+        name = NAMES[k[6:]] if k.startswith("mixer.") else k
+        assert_close(r["grads"][name].reshape(v.shape), v, name=name)
+
+
+def test_std_mixer_staged_calls_equal_segment_call():
+    """fwd_begin + fwd_finish and bwd_begin + bwd_finish with the carries equal the one-call segment
+    forms (the pieces sequence sharding runs on each rank)."""
+    from icml_b200 import ops
+    B, L, d, E, R, K = 1, 200, 32, 64, 2, 4
+    bp, x, gy = _case(90, B, L, d, E, R, K=K)
+    blk = _block_module(bp, d, 2 * d, E // d, K, R)
+    p = blk.mixer.params()
+    g = torch.Generator().manual_seed(91)
+    xn = x.float().to(DEV)
+    halo = torch.randn(B, K - 1, d, generator=g).to(DEV)
+    h0 = (0.3 * torch.randn(B, E, 16, generator=g)).to(DEV)
+    dh = (0.3 * torch.randn(B, E, 16, generator=g)).to(DEV)
+    dA = (0.5 + 0.5 * torch.rand(B, E, 16, generator=g)).to(DEV)
+    out1, hf1, st1, saved = ops.mamba_mixer_fwd_seg(xn, p, x_halo=halo, h_init=h0, want_h_final=True,
+                                                    want_states=False, save=True)
+    hs, sdt, state = ops.mamba_mixer_fwd_begin(xn, p, x_halo=halo)
+    out2, st2 = ops.mamba_mixer_fwd_finish(state, h0, want_states=True)
+    assert_close(out2, out1, name="out")
+    assert_close(ops.mamba_mixer_end_state(st2, B, L, d, E, R, 16, K), hf1, name="h_final")
+    g1, gx1, gh1, dh0_1, dA0_1 = ops.mamba_mixer_bwd_seg(xn, gy.float().to(DEV), p, saved, x_halo=halo, dh_end=dh,
+                                                        dA_end=dA, want_carry=True, want_g_halo=True)
+    d0, a0, sx, bst = ops.mamba_mixer_bwd_begin(xn, gy.float().to(DEV), p, saved, x_halo=halo)
+    g2, gx2, gh2 = ops.mamba_mixer_bwd_finish(bst, dh_end=dh, dA_end=dA, want_g_halo=True)
+    assert_close(gx2, gx1, name="grad_x")
+    assert_close(gh2, gh1, name="grad_x_halo")
+    for k in g1:
+        assert_close(g2[k], g1[k], name=k)
