@@ -67,10 +67,87 @@ def _wb(m):
     return _cat_weights(m)
 
 
+def _is_std(block) -> bool:
+    return hasattr(block, "mixer")
+
+
+def _prev_rows(sp: SeqGroup, rows: torch.Tensor) -> Optional[torch.Tensor]:
+    """The previous rank's `rows` (same shape on every rank), or None on rank 0: the conv context a
+    Mamba-standard segment needs from the segment before it."""
+    g = sp.all_gather_flat([rows])
+    return g[sp.rank - 1].view_as(rows).to(rows.dtype) if sp.rank > 0 else None
+
+
+def _next_rows(sp: SeqGroup, rows: Optional[torch.Tensor], like: torch.Tensor) -> Optional[torch.Tensor]:
+    """The next rank's `rows` (zeros stand in where a rank has none), or None on the last rank."""
+    g = sp.all_gather_flat([rows if rows is not None else torch.zeros_like(like)])
+    return g[sp.rank + 1].view_as(like).to(like.dtype) if sp.rank + 1 < sp.world else None
+
+
+@torch.no_grad()
+def std_block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
+    """PGFMambaStdBlock.pgf_forward on this rank's segment: the conv's K-1 context rows come from the
+    previous rank, the scan state entering the segment from the composed summaries of all earlier
+    ranks (per-channel A).  Returns (y, (conv context rows, boundary states) for std_block_backward)."""
+    B, L, D = x.shape
+    m = block.mixer
+    p = m.params()
+    K = m.d_conv
+    xn = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
+    halo = _prev_rows(sp, xn[:, L - (K - 1):].contiguous()) if (sp.world > 1 and K > 1) else None
+    hs, sdt, st = ops.mamba_mixer_fwd_begin(xn, p, x_halo=halo)
+    h_in = ops.ssm_compose_ranks_fwd(sp.all_gather_flat([hs, sdt]), sp.rank, m.A_log, B, m.d_inner, m.d_state)
+    y, states = ops.mamba_mixer_fwd_finish(st, h_in, want_states=True)
+    del st
+    x1, xn2 = ops.rmsnorm_fwd_res(y, x, block.norm2.weight, block.norm2.eps)
+    f = ops.ffn_fwd(xn2.reshape(-1, D), block.W1, block.b1, block.W2, block.b2, block.ffn_activation,
+                    residual=x1.reshape(-1, D))
+    return f.reshape(B, L, D), (halo, states)
+
+
+@torch.no_grad()
+def std_block_backward(block, x: torch.Tensor, g_out: torch.Tensor, ctx, sp: SeqGroup, ops=cuda_ops):
+    """PGFMambaStdBlock.pgf_backward on this rank's segment (local partial parameter gradients): the
+    adjoint carry from the right comes from the composed summaries of the later ranks, and the
+    gradient of the next rank's conv context rows is added to this segment's last K-1 rows."""
+    B, L, D = x.shape
+    m = block.mixer
+    p = m.params()
+    K = m.d_conv
+    halo, states = ctx
+    g_out = g_out.to(x.dtype)
+    xn1 = ops.rmsnorm_fwd(x, block.norm1.weight, block.norm1.eps)
+    m_raw, _, _, saved = ops.mamba_mixer_fwd_seg(xn1, p, x_halo=halo, states_in=states, save=True)
+    m_out, xn2 = ops.rmsnorm_fwd_res(m_raw, x, block.norm2.weight, block.norm2.eps)
+    del m_raw
+    fr = ops.ffn_bwd(xn2.reshape(-1, D), g_out.reshape(-1, D), block.W1, block.b1, block.W2, block.ffn_activation,
+                     need_gx=True)
+    gn2w, g_m = ops.rmsnorm_bwd(m_out, fr["grad_x"].reshape(B, L, D), block.norm2.weight, block.norm2.eps,
+                                g_add=g_out)
+    d_loc, dA0, sdx, bst = ops.mamba_mixer_bwd_begin(xn1, g_m, p, saved, x_halo=halo)
+    dh_end, dA_end = ops.ssm_compose_ranks_bwd(sp.all_gather_flat([d_loc, dA0, sdx]), sp.rank, m.A_log, B, m.d_inner,
+                                               m.d_state)
+    mg, gxn1, g_halo = ops.mamba_mixer_bwd_finish(bst, dh_end=dh_end, dA_end=dA_end, want_g_halo=halo is not None)
+    del bst, saved
+    if sp.world > 1 and K > 1:
+        tail = gxn1[:, L - (K - 1):]
+        g_next = _next_rows(sp, g_halo, tail)
+        if g_next is not None:
+            gxn1[:, L - (K - 1):] = tail + g_next
+    gn1w, grad_input = ops.rmsnorm_bwd(x, gxn1, block.norm1.weight, block.norm1.eps, g_add=g_m)
+    grads = {"W1": fr["grad_W1"], "b1": fr["grad_b1"], "W2": fr["grad_W2"], "b2": fr["grad_b2"],
+             "norm1.weight": gn1w, "norm2.weight": gn2w}
+    grads.update(m.grads_to_named(mg, "mixer."))
+    return {"grads": grads, "grad_input": grad_input}
+
+
 @torch.no_grad()
 def block_forward(block, x: torch.Tensor, sp: SeqGroup, ops=cuda_ops):
     """PGFMambaBlock.pgf_forward on this rank's segment; returns (y, state entering the segment,
     the scan's boundary states for block_backward)."""
+    if _is_std(block):
+        y, ctx = std_block_forward(block, x, sp, ops)
+        return y, None, ctx
     B, L, D = x.shape
     m = block.mamba
     W, b = _wb(m)
@@ -95,6 +172,8 @@ def block_backward(block, x: torch.Tensor, g_out: torch.Tensor, h_in: Optional[t
                    ops=cuda_ops, states=None) -> Dict[str, Any]:
     """PGFMambaBlock.pgf_backward on this rank's segment (local partial parameter gradients).  With
     `states` from block_forward on the same input, the scan's forward is one pass."""
+    if _is_std(block):
+        return std_block_backward(block, x, g_out, states, sp, ops)
     B, L, D = x.shape
     m = block.mamba
     W, b = _wb(m)
@@ -150,12 +229,16 @@ def lm_forward_backward(model, input_ids: torch.Tensor, targets: torch.Tensor, s
         y, h_in, states = block_forward(layer, x, sp, ops)
         stash.append((x, h_in, states))
         x = y
-    h = x.reshape(-1, d)
+    xf = ops.rmsnorm_fwd(x, model.final_norm.weight, model.final_norm.eps) if model.final_norm is not None else x
+    h = xf.reshape(-1, d)
     tg = targets.reshape(-1)
     loss_rows, lse = ops.lm_head_ce_fwd(h, model.lm_head_weight, tg)
     gW, gh = ops.lm_head_ce_bwd(h, model.lm_head_weight, tg, lse, 1.0 / T_total)
     grads = {"lm_head": gW}
     g = gh.reshape(B, L, d)
+    if model.final_norm is not None:
+        grads["final_norm"], g = ops.rmsnorm_bwd(x, g, model.final_norm.weight, model.final_norm.eps)
+    del x, xf, h, gh
     for i in reversed(range(model.n_layers)):
         xi, h_in, states = stash.pop()
         res = block_backward(model.backbone.layers[i], xi, g, h_in, sp, ops, states=states)

@@ -174,3 +174,86 @@ def ssm_compose_ranks_bwd(gathered, rank, A_log, Bsz, D, N):
         G = torch.exp(A * sdx) * (aE * G) + d_loc
         aE = dA0
     return G, aE
+
+
+# --------------------------------------------------------------------------- Mamba-standard mixer
+def _std_params(p):
+    return {k: v.detach() for k, v in p.items()}
+
+
+def _std_run(p, x, halo=None, h0=None, first_leaf=False):
+    """The oracle's standard mixer (oracle/mamba_std.py) over one segment with the conv context rows
+    `halo` (mixer inputs of the K-1 tokens before it) and the entering state h0: (out, h_final,
+    delta, state after the first token)."""
+    from oracle import mamba_std as MS
+    E = p["D"].shape[0]
+    N = p["A_log"].shape[1]
+    R = p["dt_w"].shape[1]
+    xz = x @ p["in_w"].t()
+    xi, z = xz[..., :E], xz[..., E:]
+    pre = halo @ p["in_w"][:E].t() if halo is not None else None
+    u = F.silu(MS.causal_conv(xi, p["conv_w"], p["conv_b"], pre))
+    xd = u @ p["x_w"].t()
+    dt_low, Bm, Cm = xd[..., :R], xd[..., R:R + N], xd[..., R + N:]
+    delta = F.softplus(dt_low @ p["dt_w"].t() + p["dt_b"])
+    A = -torch.exp(p["A_log"])
+    Bsz, L, _ = x.shape
+    h = x.new_zeros(Bsz, E, N) if h0 is None else h0
+    ys, first = [], None
+    for t in range(L):
+        h = torch.exp(delta[:, t, :, None] * A) * h + delta[:, t, :, None] * Bm[:, t, None, :] * u[:, t, :, None]
+        if t == 0 and first_leaf:
+            h.retain_grad()
+            first = h
+        ys.append((h * Cm[:, t, None, :]).sum(-1) + p["D"] * u[:, t])
+    y = torch.stack(ys, 1) * F.silu(z)
+    return y @ p["out_w"].t(), h, delta, first
+
+
+def mamba_mixer_fwd_begin(x, p, x_halo=None):
+    q = _std_params(p)
+    with torch.no_grad():
+        _, hf, delta, _ = _std_run(q, x, x_halo)
+    return hf, delta.sum(1), {"x": x, "p": q, "x_halo": x_halo}
+
+
+def mamba_mixer_fwd_finish(state, h_init, want_states=False):
+    with torch.no_grad():
+        out, _, _, _ = _std_run(state["p"], state["x"], state["x_halo"], h_init)
+    return (out, {"h_init": h_init}) if want_states else out
+
+
+def mamba_mixer_fwd_seg(x, p, x_halo=None, h_init=None, states_in=None, want_h_final=False, want_states=False,
+                        save=False):
+    if states_in is not None:
+        h_init = states_in["h_init"]
+    with torch.no_grad():
+        out, hf, _, _ = _std_run(_std_params(p), x, x_halo, h_init)
+    return out, hf, {"h_init": h_init}, {"h_init": h_init}
+
+
+@torch.enable_grad()
+def _std_grads(x, g, p, saved, x_halo, dh_end=None, dA_end=None):
+    q = {k: v.detach().clone().requires_grad_(True) for k, v in p.items()}
+    xx = x.detach().clone().requires_grad_(True)
+    hh = x_halo.detach().clone().requires_grad_(True) if x_halo is not None else None
+    out, hf, delta, first = _std_run(q, xx, hh, saved["h_init"], first_leaf=True)
+    loss = (out * g).sum()
+    if dh_end is not None:
+        loss = loss + (hf * (dA_end * dh_end)).sum()
+    loss.backward()
+    A = -torch.exp(q["A_log"].detach())
+    return q, xx, hh, first, delta.detach(), A
+
+
+def mamba_mixer_bwd_begin(x, g, p, saved, x_halo=None):
+    q, xx, hh, first, delta, A = _std_grads(x, g, p, saved, x_halo)
+    dA0 = torch.exp(delta[:, 0, :, None] * A)
+    return first.grad.detach(), dA0, delta[:, 1:].sum(1), {"x": x, "g": g, "p": p, "saved": saved, "x_halo": x_halo}
+
+
+def mamba_mixer_bwd_finish(state, dh_end=None, dA_end=None, want_g_halo=False):
+    q, xx, hh, _, _, _ = _std_grads(state["x"], state["g"], state["p"], state["saved"], state["x_halo"], dh_end,
+                                    dA_end)
+    grads = {k: v.grad.detach() for k, v in q.items()}
+    return grads, xx.grad.detach(), (hh.grad.detach() if (want_g_halo and hh is not None) else None)

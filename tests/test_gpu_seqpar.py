@@ -81,10 +81,14 @@ def test_two_gpu_sequence_sharding_matches_one_gpu(tmp_path):
         assert err <= 1e-5 + 1e-4 * v.abs().max().item(), (k, err)
 
 
-def _flat_model(dev):
+def _flat_model(dev, variant="reference"):
     from icml_b200.lm import PGFLanguageModel
     torch.manual_seed(5)
-    m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 256, dev)  # flat AdamW on the GPU
+    if variant == "std":
+        m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 256, dev, variant="std", tie_embeddings=True,
+                             final_norm=True, expand=2, d_conv=4, dt_rank=4)
+    else:
+        m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 256, dev)  # flat AdamW on the GPU
     with torch.no_grad():
         m.emb_weight.normal_(0, 0.5)
         m.lm_head_weight.normal_(0, 0.3)
@@ -92,7 +96,11 @@ def _flat_model(dev):
 
 
 def _named_params(m):
-    out = {"emb": m.emb_weight, "lm_head": m.lm_head_weight}
+    out = {"emb": m.emb_weight}
+    if not m.tied:
+        out["lm_head"] = m.lm_head_weight
+    if m.final_norm is not None:
+        out["final_norm"] = m.final_norm.weight
     for i, layer in enumerate(m.backbone.layers):
         for n, p in layer.named_parameters():
             out[f"layers.{i}.{n}"] = p
@@ -111,9 +119,9 @@ def _reducer_worker(rank, world, port, out_path, mode):
         from icml_b200 import seqpar
         from icml_b200.optim import OverlappedGradReduce
         dev = torch.device("cuda", rank)
-        m = _flat_model(dev)
+        m = _flat_model(dev, "std" if mode == "sp_std" else "reference")
         ids, tg = _data()
-        if mode == "sp":
+        if mode in ("sp", "sp_std"):
             seg = L // world
             sl = slice(rank * seg, (rank + 1) * seg)
             red = OverlappedGradReduce(m, dist.ReduceOp.SUM)
@@ -137,14 +145,14 @@ def _reducer_worker(rank, world, port, out_path, mode):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["sp", "dp"])
+@pytest.mark.parametrize("mode", ["sp", "dp", "sp_std"])
 def test_two_gpu_overlapped_reduce_matches_one_gpu(tmp_path, mode):
     """Layer-by-layer gradient all-reduce into the flat optimizer buffer (side stream), for sequence
     sharding (sum of partial gradients) and data parallelism (average of replicas)."""
     out = str(tmp_path / "r0.pt")
     mp.start_processes(_reducer_worker, args=(2, _free_port(), out, mode), nprocs=2, start_method="spawn")
     got = torch.load(out, weights_only=False)
-    m = _flat_model(torch.device("cuda", 0))
+    m = _flat_model(torch.device("cuda", 0), "std" if mode == "sp_std" else "reference")
     ids, tg = _data()
     loss, ref = m.forward_backward(ids.cuda(), tg.cuda())
     assert abs(got["loss"].item() - loss.item()) < 1e-5

@@ -24,10 +24,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _model():
+def _model(variant="reference"):
     from icml_b200.lm import PGFLanguageModel
     torch.manual_seed(3)
-    m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 16, "cpu")
+    if variant == "std":
+        m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 16, "cpu", variant="std", tie_embeddings=True,
+                             final_norm=True, expand=2, d_conv=4, dt_rank=2)
+    else:
+        m = PGFLanguageModel(V, D_MODEL, 16, D_FF, N_LAYERS, 16, "cpu")
     with torch.no_grad():
         m.emb_weight.normal_(0, 0.5)
         m.lm_head_weight.normal_(0, 0.3)
@@ -40,7 +44,7 @@ def _data():
     return ids, torch.randint(0, V, (B, L), generator=g)
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, variant="reference"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -49,7 +53,7 @@ def _worker(rank, world, port, out_path):
         sys.path.insert(0, ROOT)
         from icml_b200 import seqpar
         from tests import cpu_ops
-        m = _model()
+        m = _model(variant)
         ids, tg = _data()
         seg = L // world
         sl = slice(rank * seg, (rank + 1) * seg)
@@ -67,6 +71,47 @@ def _reference():
     ids, tg = _data()
     blocks = [{k: v.detach() for k, v in layer.state_dict().items()} for layer in m.backbone.layers]
     return O.lm_pgf_step(m.emb_weight.detach(), m.lm_head_weight.detach(), blocks, ids, tg, 16)
+
+
+def _std_reference():
+    from oracle import mamba_std as MS
+    m = _model("std")
+    ids, tg = _data()
+    blocks = []
+    for layer in m.backbone.layers:
+        sd = {k: v.detach().double() for k, v in layer.state_dict().items()}
+        bp = {k: v for k, v in sd.items() if not k.startswith("mixer.")}
+        for k, name in (("in_w", "in_proj.weight"), ("conv_b", "conv1d.bias"), ("x_w", "x_proj.weight"),
+                        ("dt_w", "dt_proj.weight"), ("dt_b", "dt_proj.bias"), ("A_log", "A_log"), ("D", "D"),
+                        ("out_w", "out_proj.weight")):
+            bp["mixer." + k] = sd["mixer." + name]
+        bp["mixer.conv_w"] = sd["mixer.conv1d.weight"].reshape(sd["mixer.conv1d.weight"].shape[0], -1)
+        blocks.append(bp)
+    loss, g = MS.lm_grads(m.emb_weight.detach().double(), None, m.final_norm.weight.detach().double(), blocks, ids, tg)
+    names = {"in_w": "in_proj.weight", "conv_w": "conv1d.weight", "conv_b": "conv1d.bias", "x_w": "x_proj.weight",
+             "dt_w": "dt_proj.weight", "dt_b": "dt_proj.bias", "A_log": "A_log", "D": "D", "out_w": "out_proj.weight"}
+    out = {}
+    for k, v in g.items():
+        parts = k.split(".")
+        if len(parts) > 3 and parts[2] == "mixer":
+            k = ".".join(parts[:3] + [names[parts[3]]])
+        out[k] = v
+    return loss, out
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_std_sequence_sharded_step_matches_oracle_autograd(world, tmp_path):
+    """The Mamba-standard model (final RMSNorm, tied head) sharded over gloo ranks: conv context rows
+    from the previous rank, per-channel-A state and adjoint composition, context-row gradients back."""
+    out = str(tmp_path / "r0.pt")
+    mp.start_processes(_worker, args=(world, _free_port(), out, "std"), nprocs=world, start_method="spawn")
+    got = torch.load(out, weights_only=False)
+    rloss, rgrads = _std_reference()
+    assert abs(got["loss"].item() - rloss.item()) < 1e-5
+    for k, v in rgrads.items():
+        gv = got["grads"][k].reshape(v.shape).double()
+        err = (gv - v).abs().max().item()
+        assert err <= 1e-5 + 1e-4 * v.abs().max().item(), (k, err)
 
 
 @pytest.mark.parametrize("world", [2, 3])
