@@ -220,15 +220,20 @@ __device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// Issue the copies of sub-chunk k into R (every thread takes every 256th 16-byte piece).  Pieces of
-// tokens past the chunk or channels past D are zero-filled (nothing is read for them).  Needs D a
-// multiple of 8 and 16-byte aligned rows (the host checks).
-__device__ __forceinline__ void raw_issue(const SsmArgs& a, const Lane& l, int k, Raw& R) {
+// Issue the copies of sub-chunk k into R (every thread takes every 256th 16-byte piece): dt_in and
+// [B | C] always, u, g, act' and the checkpoint as `fl` asks (RAW_* bits; act' only when the
+// layer has an output activation).  Pieces of tokens past the chunk or channels past D are
+// zero-filled (nothing is read for them).  Needs D a multiple of 8 and 16-byte aligned rows (the
+// host checks).
+enum { RAW_U = 1, RAW_G = 2, RAW_AP = 4, RAW_CK = 8 };
+__device__ __forceinline__ void raw_issue(const SsmArgs& a, const Lane& l, int k, Raw& R, int fl) {
   const int es = a.u_bf16 ? 2 : 4;
   const int pu = DC * es / 16;                      // pieces per token row of u (and of g)
-  const int n_dt = ST * 16, n_bc = ST * 8, n_u = ST * pu, n_ap = a.actp ? ST * 16 : 0;
-  const int n_ck = a.ckpt_g ? DC * NST / 4 + DC / 4 : 0;
-  const int total = n_dt + n_bc + 2 * n_u + n_ap + n_ck;
+  const int n_dt = ST * 16, n_bc = ST * 8;
+  const int n_u = (fl & RAW_U) ? ST * pu : 0, n_g = (fl & RAW_G) ? ST * pu : 0;
+  const int n_ap = ((fl & RAW_AP) && a.actp) ? ST * 16 : 0;
+  const int n_ck = ((fl & RAW_CK) && a.ckpt_g) ? DC * NST / 4 + DC / 4 : 0;
+  const int total = n_dt + n_bc + n_u + n_g + n_ap + n_ck;
   const int64_t t0 = l.s + int64_t(k) * ST, c0 = int64_t(l.grp) * DC;
   const int KS = int((a.Tc + ST - 1) / ST);
   const int64_t ck = (l.b * a.nC + l.c) * KS + k;
@@ -250,7 +255,7 @@ __device__ __forceinline__ void raw_issue(const SsmArgs& a, const Lane& l, int k
       continue;
     }
     q -= n_bc;
-    if (q < 2 * n_u) {
+    if (q < n_u + n_g) {
       const bool isg = q >= n_u;
       if (isg) q -= n_u;
       const int t = q / pu, c = (q % pu) * (16 / es);
@@ -261,7 +266,7 @@ __device__ __forceinline__ void raw_issue(const SsmArgs& a, const Lane& l, int k
       cp16(reinterpret_cast<char*>(dst) + c * es, v ? base + ((l.b * a.L + tok) * a.D + c0 + c) * es : base, v);
       continue;
     }
-    q -= 2 * n_u;
+    q -= n_u + n_g;
     if (q < n_ap) {
       const int t = q >> 4, c = (q & 15) * 4;
       const int64_t tok = t0 + t;
@@ -314,6 +319,32 @@ __device__ __forceinline__ void raw_store(const SsmArgs& a, const Raw& R, const 
   }
 }
 
+// Forward-order staging of a chunk's sub-chunks into stg[k & 1]: the inputs come through registers
+// one sub-chunk ahead.  Per sub-chunk k: before(k), the compute on stg[k & 1], then after(k), which
+// ends with the sub-chunk's barrier (stg[(k + 1) & 1] is then ready).  (Staging these by cp.async,
+// as the backward kernels do, measured slower: they are issue-bound and rarely wait on loads.)
+struct FwdStager {
+  const SsmArgs& a;
+  const Lane& l;
+  Stage* stg;
+  int nsub;
+  Pref r;
+  __device__ FwdStager(const SsmArgs& a_, const Lane& l_, Stage* stg_, int nsub_)
+      : a(a_), l(l_), stg(stg_), nsub(nsub_) {}
+  __device__ void begin() {
+    pref_load(a, l, l.s, false, r);
+    pref_store(r, l, false, stg[0]);
+    __syncthreads();
+  }
+  __device__ void before(int k) {
+    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+  }
+  __device__ void after(int k) {
+    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
+    __syncthreads();
+  }
+};
+
 // One forward step of the thread's NS states (as pairs) on staged token i:
 // h = exp(dt A) h + phi_1(dt A) B u; returns phi_1(dt A) per state.
 template <bool OUT_E = false>
@@ -347,13 +378,11 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
   float2 h[NP] = {f2(0.f), f2(0.f)}, e[NP];
   float sdt = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
-  Pref r;
-  pref_load(a, l, l.s, false, r);
-  pref_store(r, l, false, stg[0]);
-  __syncthreads();
+  FwdStager fs(a, l, stg, nsub);
+  fs.begin();
   for (int k = 0; k < nsub; ++k) {
     const int nt = sub_len(l, k);
-    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    fs.before(k);
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
@@ -362,8 +391,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_fwd_kernel(const SsmArg
         sdt += S.dt[i][l.dl];
       }
     }
-    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
-    __syncthreads();
+    fs.after(k);
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
@@ -409,13 +437,11 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_y0_kernel(const SsmArgs
   float sdt = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
   const int KS = int((a.Tc + ST - 1) / ST);
-  Pref r;
-  pref_load(a, l, l.s, false, r);
-  pref_store(r, l, false, stg[0]);
-  __syncthreads();
+  FwdStager fs(a, l, stg, nsub);
+  fs.begin();
   for (int k = 0; k < nsub; ++k) {
     const int nt = sub_len(l, k);
-    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    fs.before(k);
     if (a.ckpt_write && l.ch) {
       const int64_t ck = (l.b * a.nC + l.c) * KS + k;
       st_states(a.ckpt_g + (ck * a.D + l.d) * NST + l.nq * NS, h);
@@ -433,8 +459,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_y0_kernel(const SsmArgs
         if (l.nq == 0) ybuf[k & 1][i][l.dl] = yc;
       }
     }
-    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
-    __syncthreads();
+    fs.after(k);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int idx = l.tid + q * SSM_THREADS;
@@ -472,20 +497,18 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs
       y0v[q] = (tok < l.e && d_out < a.D) ? a.y0[(l.b * a.L + tok) * a.D + d_out] : 0.f;
     }
   };
-  Pref r;
   float y0c[2], y0n[2], uc[2];
-  pref_load(a, l, l.s, false, r);
+  FwdStager fs(a, l, stg, nsub);
   load_y0(l.s, y0c);
-  pref_store(r, l, false, stg[0]);
-  uc[0] = r.u[0]; uc[1] = r.u[1];
-  __syncthreads();
+  fs.begin();
   for (int k = 0; k < nsub; ++k) {
     const int nt = sub_len(l, k);
-    if (k + 1 < nsub) {
-      pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
-      load_y0(l.s + int64_t(k + 1) * ST, y0n);
-    }
+    fs.before(k);
+    if (k + 1 < nsub) load_y0(l.s + int64_t(k + 1) * ST, y0n);
     const Stage& S = stg[k & 1];
+    // u of the thread's write-out slots, from the stage before the barrier lets it be refilled
+#pragma unroll
+    for (int q = 0; q < 2; ++q) uc[q] = S.u[(l.tid + q * SSM_THREADS) / DC][l.tid % DC];
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
       if (i < nt) {
@@ -498,8 +521,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs
         if (l.nq == 0) ybuf[k & 1][i][l.dl] = yc;
       }
     }
-    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
-    __syncthreads();
+    fs.after(k);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int idx = l.tid + q * SSM_THREADS;
@@ -512,7 +534,6 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_corr_kernel(const SsmArgs
       }
     }
     if (k + 1 < nsub) {
-      uc[0] = r.u[0]; uc[1] = r.u[1];
       y0c[0] = y0n[0]; y0c[1] = y0n[1];
     }
   }
@@ -530,14 +551,12 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
   const float Dd = (l.ch && a.y) ? a.Dp[l.d] : 0.f;
   const float sc = (l.ch && a.y) ? a.scale[l.d] : 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
-  Pref r;
-  pref_load(a, l, l.s, false, r);
-  pref_store(r, l, false, stg[0]);
-  __syncthreads();
+  FwdStager fs(a, l, stg, nsub);
+  fs.begin();
   const int KS = int((a.Tc + ST - 1) / ST);
   for (int k = 0; k < nsub; ++k) {
     const int nt = sub_len(l, k);
-    if (k + 1 < nsub) pref_load(a, l, l.s + int64_t(k + 1) * ST, false, r);
+    fs.before(k);
     if (a.ckpt_write && l.ch) {
       const int64_t ck = (l.b * a.nC + l.c) * KS + k;
       if (a.ckpt_write == 2) {
@@ -564,8 +583,7 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
         }
       }
     }
-    if (k + 1 < nsub) pref_store(r, l, false, stg[(k + 1) & 1]);
-    __syncthreads();
+    fs.after(k);
     // coalesced write-out of the sub-chunk (y, or act'(C h) for the backward)
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
@@ -585,20 +603,59 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_out_fwd_kernel(const SsmArgs 
 // ---------------------------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArgs a) {
+// Bytes of a Raw buffer the adjoint-only pass uses (its leading fields up to act'; u is not filled).
+constexpr size_t RAW_ADJ_BYTES = offsetof(Raw, ckh);
+__device__ __forceinline__ Raw& raw_at(float* smr, size_t stride, int k) {
+  return *reinterpret_cast<Raw*>(reinterpret_cast<char*>(smr) + (k & 1) * stride);
+}
+
+// The parts of a backward stage the adjoint-only pass reads (dt, delta_in_h, C) from raw inputs.
+__device__ __forceinline__ void raw_store_adj(const SsmArgs& a, const Raw& R, const Lane& l, float sc_ch, Stage& st) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * SSM_THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    const float gg = a.g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.g[t][0])[dl]) : R.g[t][dl];
+    const float ap = a.actp ? R.ap[t][dl] : 1.f;
+    st.dt[t][dl] = softplus_fast(R.dtin[t][dl]);
+    st.dh[t][dl] = gg * sc_ch * ap;
+  }
+  const int t = l.tid >> 5, j = l.tid & 31;
+  if (t < ST && j >= NST) reinterpret_cast<float*>(&st.C[t][0])[j - NST] = R.bc[t][j];
+}
+
+// Reverse chunk summaries of the adjoint from a zero carry.  ASYNC (D a multiple of 8, aligned rows):
+// inputs staged by cp.async into two Raw buffers in dynamic shared memory, three sub-chunks ahead
+// of their use, one barrier per sub-chunk.
+template <bool ASYNC>
+__global__ void __launch_bounds__(SSM_THREADS, 4) ssm_chunk_bwd_kernel(const SsmArgs a) {
+  extern __shared__ __align__(16) float smr[];
   __shared__ Stage stg[2];
+  auto raw = [&](int k) -> Raw& { return raw_at(smr, RAW_ADJ_BYTES, k); };
   const Lane l = lane_of(a);
   const AConst K = load_A(a, l.nq);
   float2 dlt[NP] = {f2(0.f), f2(0.f)};
   float2 anext[NP] = {f2(1.f), f2(1.f)};
   float sdt2 = 0.f, dt_first = 0.f;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
+  const int64_t c_out = int64_t(l.grp) * DC + l.tid % DC;
+  const float sc_ch = c_out < a.D ? a.scale[c_out] : 0.f;
   Pref r;
-  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
-  pref_store(r, l, true, stg[(nsub - 1) & 1]);
-  __syncthreads();
+  if (ASYNC) {
+    raw_issue(a, l, nsub - 1, raw(nsub - 1), RAW_G | RAW_AP);
+    if (nsub > 1) raw_issue(a, l, nsub - 2, raw(nsub - 2), RAW_G | RAW_AP);
+    cp_wait_all();
+    __syncthreads();
+    raw_store_adj(a, raw(nsub - 1), l, sc_ch, stg[(nsub - 1) & 1]);
+    __syncthreads();
+    if (nsub > 2) raw_issue(a, l, nsub - 3, raw(nsub - 3), RAW_G | RAW_AP);
+  } else {
+    pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+    pref_store(r, l, true, stg[(nsub - 1) & 1]);
+    __syncthreads();
+  }
   for (int k = nsub - 1; k >= 0; --k) {
-    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    if (!ASYNC && k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
     const Stage& S = stg[k & 1];
 #pragma unroll
     for (int i = ST - 1; i >= 0; --i) {
@@ -617,8 +674,16 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArg
         dt_first = dt;
       }
     }
-    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
-    __syncthreads();
+    if (ASYNC) {
+      // stage k-1 from its raw inputs (landed by the previous barrier); raw k-2 lands by this one
+      if (k > 0) raw_store_adj(a, raw(k - 1), l, sc_ch, stg[(k - 1) & 1]);
+      cp_wait_all();
+      __syncthreads();
+      if (k > 2) raw_issue(a, l, k - 3, raw(k - 3), RAW_G | RAW_AP);
+    } else {
+      if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
+      __syncthreads();
+    }
   }
   if (!l.ch) return;
   const int64_t cb = l.b * a.nC + l.c;
@@ -627,6 +692,21 @@ __global__ void __launch_bounds__(SSM_THREADS) ssm_chunk_bwd_kernel(const SsmArg
     a.sdt2[cb * a.D + l.d] = sdt2;
     a.dt0[cb * a.D + l.d] = dt_first;
   }
+}
+
+// Launch of the reverse chunk summaries: the cp.async form when the rows allow it.
+static int launch_chunk_bwd(const SsmArgs& a, dim3 grid, cudaStream_t s) {
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool async = a.D % 8 == 0 && al16(a.proj) && al16(a.g) && (!a.actp || al16(a.actp));
+  if (async) {
+    static int lim = 0;
+    PGF_CUDA(ensure_dynamic_smem(ssm_chunk_bwd_kernel<true>, 2 * RAW_ADJ_BYTES, lim));
+    ssm_chunk_bwd_kernel<true><<<grid, SSM_THREADS, 2 * RAW_ADJ_BYTES, s>>>(a);
+  } else {
+    ssm_chunk_bwd_kernel<false><<<grid, SSM_THREADS, 0, s>>>(a);
+  }
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
 }
 
 // Adjoint carries X entering each chunk from the right, from (dh_end, dA_end) or (0, 1), segmented
@@ -776,12 +856,12 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
   float accD = 0.f, accS = 0.f;
   const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
   if (ASYNC) {
-    raw_issue(a, l, nsub - 1, raw[(nsub - 1) & 1]);
+    raw_issue(a, l, nsub - 1, raw[(nsub - 1) & 1], RAW_U | RAW_G | RAW_AP | RAW_CK);
     cp_wait_all();
     __syncthreads();
     fill(nsub - 1);
     __syncthreads();
-    if (nsub > 1) raw_issue(a, l, nsub - 2, raw[(nsub - 2) & 1]);
+    if (nsub > 1) raw_issue(a, l, nsub - 2, raw[(nsub - 2) & 1], RAW_U | RAW_G | RAW_AP | RAW_CK);
   } else {
     pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
     pref_store(r, l, true, stg[(nsub - 1) & 1]);
@@ -916,7 +996,7 @@ __global__ void __launch_bounds__(SSM_THREADS, 2) ssm_main_bwd_kernel(const SsmA
     }
     __syncthreads();
     // raw buffer (k - 2) & 1 held sub-chunk k, whose stage was filled a sub-chunk ago
-    if (ASYNC && k > 1) raw_issue(a, l, k - 2, raw[k & 1]);
+    if (ASYNC && k > 1) raw_issue(a, l, k - 2, raw[k & 1], RAW_U | RAW_G | RAW_AP | RAW_CK);
   }
   // per-CTA parameter partials
   float* sA = sm;  // [SSM_THREADS][NS]; checkpoints are no longer needed
@@ -1306,9 +1386,8 @@ static int ssm_bwd_impl(const void* u, const void* g, const float* W_cat, const 
   if (stage != STAGE_FINISH) {
     // reverse chunk summaries from a zero carry: independent of the carry entering from the right
     prof_begin(PROF_SSM_CHUNK_BWD, s);
-    ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
+    PGF_TRY(launch_chunk_bwd(a, grid, s));
     prof_end(PROF_SSM_CHUNK_BWD, s, bytes_chunk_bwd(a, a.u_bf16 ? 2 : 4));
-    PGF_LAUNCH_CHECK();
   }
   const int64_t nth = Bsz * D * NST;
   if (stage == STAGE_BEGIN) {
@@ -1493,8 +1572,7 @@ extern "C" int pgf_ssm_bwd_summary(const void* u, const void* g, const float* W_
     ssm_out_fwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
     PGF_LAUNCH_CHECK();
   }
-  ssm_chunk_bwd_kernel<<<grid, SSM_THREADS, 0, s>>>(a);
-  PGF_LAUNCH_CHECK();
+  PGF_TRY(launch_chunk_bwd(a, grid, s));
   const int64_t nth = Bsz * D * NST;
   ssm_compose_bwd_kernel<<<ceil_div(nth, 32), 32 * CSEG, 0, s>>>(a, nullptr, nullptr, dh_start, dA_start,
                                                             sum_dt_excl);
