@@ -59,9 +59,10 @@ def parse():
                     help="reference: the reference's SSM block (d_inner = d_model); std: the Mamba-standard "
                          "block of the benchmark configurations (expand 2, d_conv 4, dt_rank 16, final "
                          "RMSNorm, tied LM head)")
-    ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "jvp", "all"],
+    ap.add_argument("--component", default=None, choices=["rmsnorm", "ffn", "lmhead", "jvp", "scan", "all"],
                     help="component microbenchmarks instead of the LM step (RMSNorm [8,4096,1024]; FFN "
-                         "1024-4096-1024 on 32768 tokens; LM head + CE d=1024, vocab 50257, 32768 tokens)")
+                         "1024-4096-1024 on 32768 tokens; LM head + CE d=1024, vocab 50257, 32768 tokens; "
+                         "scan: one reference-variant SSM layer's saved forward and backward on one segment)")
     ap.add_argument("--stash", default="device", choices=["device", "host", "scan"],
                     help="where layer inputs wait for the backward: device memory, pinned host memory, or "
                          "device memory together with each layer's scan states (no scan recompute)")
@@ -227,18 +228,35 @@ def run_reference(a, rank, world):
 
 
 # ----------------------------------------------------------------------------- GPU arm
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, mean over the group's
-# launches) from one ncu capture of the default workload (8-layer reference variant, d 256, d_ff
-# 1024, vocab 50257, B=1 x L=65536, bf16; `--steps 1 --warmup 1 --no-cpu-baseline --no-graph`).
-# Reported as `traffic` only for that workload.
-TRAFFIC_DEFAULT = {"gemm_tc": 194818014, "ssm_main_bwd": 491831096, "ce": 1316616857, "ssm_chunk_fwd": 150740000,
-                   "ssm_out_fwd": 230101748, "ssm_chunk_bwd": 147060344, "ssm_compose": 8940480,
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant kernels, from
+# ncu captures of one launch each on the 65536-token segment every launch of the default workload
+# covers (8-layer reference variant, d 256, d_ff 1024, vocab 50257, bf16; the scan kernels from
+# `bench.py --component scan`, the others from the 65536-token step).  Reported as `traffic` only
+# for that workload.
+TRAFFIC_DEFAULT = {"gemm_tc": 194818014, "ssm_main_bwd": 496966144, "ce": 1316616857, "ssm_chunk_fwd": 288500000,
+                   "ssm_out_fwd": 230101748, "ssm_chunk_bwd": 114800000, "ssm_compose": 8940480,
                    "rmsnorm_fwd": 58914490, "rmsnorm_bwd": 110329568, "adamw": 395415392}
+# Warp instructions per launch of the scan backward on that segment (smsp__inst_executed.sum, same
+# capture): the kernel is bound by instruction issue, so its compute roofline is issue rate.
+MAIN_BWD_WARP_INSTS = 517951488
+SMS, ISSUE_PER_SM_CLK = 148, 4
 
 
 def default_workload(a, world):
+    """The default LM workload, whose per-launch shapes the captures above measured (sequences of
+    65536 tokens or longer run in 65536-token segments)."""
+    per_rank = a.seq_len // world if (world > 1 and a.parallel == "sp") else a.seq_len
     return (a.variant == "reference" and a.layers == 8 and a.d_model == 256 and a.d_ff == 1024 and a.vocab == 50257
-            and a.batch == 1 and a.seq_len == 65536 and a.dtype == "bf16" and a.block_size == 4096)
+            and a.batch == 1 and per_rank % 65536 == 0 and a.dtype == "bf16" and a.block_size == 4096)
+
+
+def issue_roofline(ms_per_launch, sm_mhz):
+    """The scan backward against the SMs' instruction-issue peak (4 warp instructions per SM per clock)."""
+    ach = MAIN_BWD_WARP_INSTS / (ms_per_launch / 1e3) / 1e9
+    peak = SMS * ISSUE_PER_SM_CLK * sm_mhz / 1e3
+    return {"bound": "issue", "achieved": ach, "peak": peak, "unit": "G warp-instructions/s", "frac": ach / peak,
+            "kernel": "ssm_main_bwd", "warp_instructions_per_launch": MAIN_BWD_WARP_INSTS,
+            "peak_source": f"{SMS} SMs x {ISSUE_PER_SM_CLK} per clock at the sampled {sm_mhz:.0f} MHz"}
 
 
 def roofline_entry(name, ms_total, n, work_total, traffic=None):
@@ -303,10 +321,13 @@ def run_components(a):
     hbm, tf = peaks.get("hbm_gbs", 6650.0), peaks.get("bf16_tflops", 1590.0)
     dev = torch.device("cuda")
     g = torch.Generator(device="cpu").manual_seed(0)
-    which = ["rmsnorm", "ffn", "lmhead", "jvp"] if a.component == "all" else [a.component]
+    which = ["rmsnorm", "ffn", "lmhead", "jvp", "scan"] if a.component == "all" else [a.component]
     if "jvp" in which:
         run_jvp_components(a, hbm, tf, g, dev)
         which = [w for w in which if w != "jvp"]
+    if "scan" in which:
+        run_scan_component(a, g, dev)
+        which = [w for w in which if w != "scan"]
     for dt_name, dt in (("bf16", torch.bfloat16), ("fp32", torch.float32)):
         if "rmsnorm" in which:
             x = torch.randn(8, 4096, 1024, generator=g).to(dev, dt)
@@ -346,6 +367,44 @@ def run_components(a):
                               "value": fl / ms / 1e9, "unit": "TFLOP/s", "dtype": dt_name, "ms": ms,
                               "roofline": {"bound": "tensor", "achieved": fl / ms / 1e9, "peak": tf,
                                            "frac": fl / ms / 1e9 / tf}}), flush=True)
+
+
+def run_scan_component(a, g, dev):
+    """The selective-scan layer of the reference variant (d_model x 16 states) on one 65536-token
+    segment in bf16: the backward's saved forward (re-run, checkpoints) and the scan backward, the
+    kernels the LM step launches per layer and segment.  One JSON line with each kernel's time per
+    launch (libpgf's CUDA events) and its roofline against MEASURED_PEAKS.json."""
+    import ctypes
+    from icml_b200 import _lib, ops
+    from icml_b200.train_singlemamba_optimized import SingleLayerMambaPGF, _cat_weights
+    L = min(a.seq_len, 65536)
+    torch.manual_seed(0)
+    layer = SingleLayerMambaPGF(a.d_model, 16).to(dev)
+    u = torch.randn(1, L, a.d_model, generator=g).to(dev, torch.bfloat16)
+    gy = torch.randn(1, L, a.d_model, generator=g).to(dev, torch.bfloat16)
+    W, b = _cat_weights(layer)
+
+    def step():
+        y, saved = ops.ssm_fwd_save(u, W, b, layer.A_log, layer.D, layer.scale)
+        ops.ssm_bwd(u, gy, W, b, layer.A_log, layer.D, layer.scale, saved=saved)
+
+    for _ in range(max(a.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    Lb = _lib.lib()
+    Lb.pgf_profile(1)
+    for _ in range(a.steps):
+        step()
+    torch.cuda.synchronize()
+    Lb.pgf_profile(0)
+    kernels = {}
+    for i, nm in PROF_NAMES.items():
+        c, t, w = ctypes.c_longlong(0), ctypes.c_double(0.0), ctypes.c_double(0.0)
+        Lb.pgf_profile_read(i, ctypes.byref(c), ctypes.byref(t), ctypes.byref(w))
+        if c.value:
+            kernels[nm] = roofline_entry(nm, t.value, c.value, w.value)
+    print(json.dumps({"metric": f"scan layer saved forward + backward, B=1 x L={L}, d {a.d_model}, 16 states, bf16",
+                      "unit": "ms per launch", "steps": a.steps, "kernels": kernels}), flush=True)
 
 
 def run_jvp_components(a, hbm, tf, g, dev):
@@ -629,6 +688,10 @@ def run_gpu(a, rank, world, local_rank):
                        "share_of_step": prof_ms[k] / ms_step if ms_step else None,
                        "roofline": roofline_entry(k, prof_ms[k], prof_n[k], prof_w[k], traffic.get(k))}
                    for k in prof_ms}
+        compute_roofline = None
+        if "ssm_main_bwd" in kernels and default_workload(a, world):
+            mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
+            compute_roofline = issue_roofline(kernels["ssm_main_bwd"]["roofline"]["ms_per_launch"], mhz)
         line = {
             "metric": metric_of(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling_of(a, world),
@@ -643,6 +706,7 @@ def run_gpu(a, rank, world, local_rank):
             "cuda_graph": graphed is not None,
             "kernels": kernels, "dominant_kernel": dom,
             "roofline": kernels[dom]["roofline"] if dom else None,
+            "compute_roofline": compute_roofline,
         }
         if world == 1 and not a.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(a)
