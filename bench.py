@@ -339,8 +339,10 @@ def run_components(a):
                               "unit": "GB/s", "dtype": dt_name, "ms": ms,
                               "roofline": {"bound": "hbm", "achieved": by / ms / 1e6, "peak": hbm,
                                            "frac": by / ms / 1e6 / hbm}}), flush=True)
-        if "ffn" in which:
-            T, d, dh = 32768, 1024, 4096
+        # the wide FFN of the component configuration, and the LM's own FFN on one 65536-token segment
+        for T, d, dh in ((32768, 1024, 4096), (65536, 256, 1024)):
+            if "ffn" not in which or (dt_name == "fp32" and d == 256):
+                continue
             x = torch.randn(T, d, generator=g).to(dev, dt)
             gy = torch.randn(T, d, generator=g).to(dev, dt)
             W1 = (0.02 * torch.randn(dh, d, generator=g)).to(dev)
@@ -348,7 +350,7 @@ def run_components(a):
             b1, b2 = torch.zeros(dh, device=dev), torch.zeros(d, device=dev)
             ms = _time(lambda: (ops.ffn_fwd(x, W1, b1, W2, b2), ops.ffn_bwd(x, gy, W1, b1, W2)), a.steps, a.warmup)
             fl = 8 * 2.0 * T * d * dh  # fwd 2 + backward 6 (incl. the recomputed forward)
-            print(json.dumps({"metric": "FFN 1024-4096-1024 fwd+bwd, 32768 tokens", "value": fl / ms / 1e9,
+            print(json.dumps({"metric": f"FFN {d}-{dh}-{d} fwd+bwd, {T} tokens", "value": fl / ms / 1e9,
                               "unit": "TFLOP/s", "dtype": dt_name, "ms": ms,
                               "roofline": {"bound": "tensor", "achieved": fl / ms / 1e9, "peak": tf,
                                            "frac": fl / ms / 1e9 / tf}}), flush=True)

@@ -54,6 +54,23 @@ int run_gemm_simt(const Gemm& g, cudaStream_t s);
 // tcgen05 path; returns PGF_ERR_UNSUPPORTED when the call does not fit it.
 int run_gemm_tc(const Gemm& g, cudaStream_t s);
 bool tc_usable(const Gemm& g);
+// Two products into one (M x N) output tile, on the tcgen05 engine, for the FFN backward: with
+//   z = A1 B1^T + bias  (A1: M x K1, B1: N x K1, or K1 x N when b1_trans),
+//   d = A2 B2^T         (A2: M x K2, B2: N x K2, or K2 x N when b2_trans),
+// it writes H = act(z) and DZ = d * act'(z) (act = GELU (tanh form) or ReLU), all bf16; z itself is
+// never stored.  PGF_ERR_UNSUPPORTED when the operands do not suit the engine.
+struct DualGemm {
+  int64_t M, N, K1, K2;
+  const void* A1; int64_t lda1;
+  const void* B1; int64_t ldb1; int b1_trans;
+  const void* A2; int64_t lda2;
+  const void* B2; int64_t ldb2; int b2_trans;
+  const float* bias;  // (N,) or NULL
+  int kind;           // PGF_EPI_GELU or PGF_EPI_RELU
+  void* H; int64_t ldh;
+  void* DZ; int64_t lddz;
+};
+int run_gemm_tc_dual(const DualGemm& g, cudaStream_t s);
 // Fused LM-head + cross-entropy passes on the tcgen05 engine (g: logits = h W^T, N = vocab).
 // Forward: per row and per group of `ng` 128-column tiles, the running max / sum of exp of the
 // logits (part_m, part_s: (M, n_groups)) and the target logit; the logits are never stored.

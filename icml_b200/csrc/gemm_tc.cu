@@ -17,7 +17,11 @@
 //       CE_FWD   - online log-sum-exp of each row over the CTA's vocabulary range plus the target
 //                  logit; the logits never leave TMEM;
 //       CE_BWD   - g = (softmax - onehot) * scale from the recomputed logits and the saved lse,
-//                  stored as bf16 through the transpose.
+//                  stored as bf16 through the transpose;
+//       DUAL     - two products per output tile into two accumulators (z = A1 B1^T and
+//                  d = A2 B2^T, 128 columns each, four TMEM accumulators in all), stored as
+//                  act(z + bias) and d * act'(z + bias): the FFN backward's recomputed hidden
+//                  activation and its pre-activation gradient, z never leaving TMEM.
 // Work unit = (128-row block, group of `ng` consecutive 128-column tiles); CTAs stride over units.
 // Every mbarrier wait is bounded by a clock budget; on expiry the kernel records a fault in
 // g_tc_fault and stops issuing work.
@@ -57,7 +61,7 @@ enum { TC_GENERIC = 0, TC_CE_FWD = 1, TC_CE_BWD = 2 };
 // the single all-modes kernel spent a measurable share of its issue slots on instruction-cache misses):
 //   PLAIN: generic, no activation (bias / addend / accumulate);  ACT: GELU or ReLU (+ pre-activation);
 //   DACT: GELU' or ReLU' with the saved pre-activation;  CE_FWD / CE_BWD: the cross-entropy modes.
-enum { EK_PLAIN = 0, EK_ACT = 1, EK_DACT = 2, EK_CE_FWD = 3, EK_CE_BWD = 4 };
+enum { EK_PLAIN = 0, EK_ACT = 1, EK_DACT = 2, EK_CE_FWD = 3, EK_CE_BWD = 4, EK_DUAL = 5 };
 
 // The bf16-output GELU and GELU' (tanh form) on a pair of columns with packed float32 instructions:
 // GELU(x) = hx + hx tanh(u) with hx = x/2, u = C x (1 + A x^2);
@@ -77,11 +81,24 @@ __device__ __forceinline__ float2 gelu_prime2_bf(float2 x) {
   const float2 hs = mul2(mul2(x, f2(0.5f)), fma2(t, f2(-t.x, -t.y), f2(1.0f)));
   return fma2(hs, w, fma2(t, f2(0.5f), f2(0.5f)));
 }
+// GELU(x) and GELU'(x) from one tanh per element.
+__device__ __forceinline__ void gelu_and_prime2(float2 x, float2& g, float2& gp) {
+  const float2 x2 = mul2(x, x);
+  const float2 u = mul2(mul2(x, f2(PGF_GELU_C)), fma2(x2, f2(PGF_GELU_A), f2(1.0f)));
+  const float2 t = f2(tanh_approx(u.x), tanh_approx(u.y));
+  const float2 hx = mul2(x, f2(0.5f));
+  g = fma2(hx, t, hx);
+  const float2 w = fma2(x2, f2(3.0f * PGF_GELU_A * PGF_GELU_C), f2(PGF_GELU_C));
+  const float2 hs = mul2(hx, fma2(t, f2(-t.x, -t.y), f2(1.0f)));
+  gp = fma2(hs, w, fma2(t, f2(0.5f), f2(0.5f)));
+}
 
 
 struct TcParams {
   int64_t M, N, K;
   int a_mn, b_mn;
+  int64_t K2;          // DUAL: depth of the second product (operands tmA2 / tmB2)
+  int a2_mn, b2_mn;
   int mode;
   int ng;              // 128-column tiles per work unit
   int n_groups;        // work units per row block
@@ -108,8 +125,13 @@ struct TcParams {
 template <int BN, int EK>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmZ, const TcParams p) {
+               const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmZ,
+               const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, const TcParams p) {
   using C = TcCfg<BN>;
+  static_assert(EK != EK_DUAL || BN == 128, "the dual product runs 128-column tiles");
+  constexpr int NPROD = EK == EK_DUAL ? 2 : 1;        // products per output tile
+  constexpr uint32_t ABUF = uint32_t(NPROD * BN);     // TMEM columns of one accumulator set
+  constexpr uint32_t NCOL = 2 * ABUF;                 // two sets: the MMA fills one while the epilogue drains the other
   constexpr int MODE = EK == EK_CE_FWD ? TC_CE_FWD : (EK == EK_CE_BWD ? TC_CE_BWD : TC_GENERIC);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -123,6 +145,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = int((p.K + TC_BK - 1) / TC_BK);
+  const int nk2 = EK == EK_DUAL ? int((p.K2 + TC_BK - 1) / TC_BK) : 0;
   const int n_tiles = int((p.N + BN - 1) / BN);
 
   if (threadIdx.x == 0) {
@@ -137,10 +160,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    if (EK == EK_DUAL) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA2)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB2)) : "memory");
+    }
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(tslot)), "r"(C::TMEM));
+                 ::"r"(smem_u32(tslot)), "r"(NCOL));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -149,61 +176,73 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---- TMA producer
-      uint32_t it = 0;
-      bool ok = true;
-      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const int ks = int(u / p.tiles), ut = int(u % p.tiles);
-        const int mb = ut / p.n_groups, ng = ut % p.n_groups;
-        const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
-        const int m0 = mb * TC_BM;
-        const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
-        for (int nt = nt0; nt < nt1 && ok; ++nt) {
-          const int n0 = nt * BN;
-          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+    // ---- TMA producer: the whole warp runs the loop and waits, one elected lane issues the copies
+    const bool leader = elect_one();
+    uint32_t it = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      const int ks = int(u / p.tiles), ut = int(u % p.tiles);
+      const int mb = ut / p.n_groups, ng = ut % p.n_groups;
+      const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
+      const int m0 = mb * TC_BM;
+      const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
+      for (int nt = nt0; nt < nt1 && ok; ++nt) {
+        const int n0 = nt * BN;
+        for (int pr = 0; pr < NPROD && ok; ++pr) {
+          const CUtensorMap* mA = pr ? &tmA2 : &tmA;
+          const CUtensorMap* mB = pr ? &tmB2 : &tmB;
+          const int amn = pr ? p.a2_mn : p.a_mn, bmn = pr ? p.b2_mn : p.b_mn;
+          const int kbs = pr ? 0 : kb0, kbe = pr ? nk2 : kb1;
+          for (int kb = kbs; kb < kbe; ++kb, ++it) {
             const int s = int(it % C::STAGES), r = int(it / C::STAGES);
-            if (r > 0 && !mbar_wait(&empty[s], uint32_t((r - 1) & 1))) { ok = false; break; }
-            mbar_expect_tx(&full[s], C::STAGE);
-            uint8_t* sa = tiles + s * C::STAGE;
-            uint8_t* sb = sa + TILE_A_BYTES;
-            const int k0 = kb * TC_BK;
-            if (!p.a_mn) {
-              tma_load_2d(sa, &tmA, &full[s], k0, m0);
-            } else {
-              tma_load_2d(sa, &tmA, &full[s], m0, k0);
-              tma_load_2d(sa + TILE_A_BYTES / 2, &tmA, &full[s], m0 + 64, k0);
-            }
-            if (!p.b_mn) {
-              tma_load_2d(sb, &tmB, &full[s], k0, n0);
-            } else {
+            if (r > 0 && !mbar_wait_warp(&empty[s], uint32_t((r - 1) & 1))) { ok = false; break; }
+            if (leader) {
+              mbar_expect_tx(&full[s], C::STAGE);
+              uint8_t* sa = tiles + s * C::STAGE;
+              uint8_t* sb = sa + TILE_A_BYTES;
+              const int k0 = kb * TC_BK;
+              if (!amn) {
+                tma_load_2d(sa, mA, &full[s], k0, m0);
+              } else {
+                tma_load_2d(sa, mA, &full[s], m0, k0);
+                tma_load_2d(sa + TILE_A_BYTES / 2, mA, &full[s], m0 + 64, k0);
+              }
+              if (!bmn) {
+                tma_load_2d(sb, mB, &full[s], k0, n0);
+              } else {
 #pragma unroll
-              for (int i = 0; i < BN / 64; ++i) tma_load_2d(sb + i * 8192, &tmB, &full[s], n0 + 64 * i, k0);
+                for (int i = 0; i < BN / 64; ++i) tma_load_2d(sb + i * 8192, mB, &full[s], n0 + 64 * i, k0);
+              }
             }
+            __syncwarp();
           }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---- MMA issuer
-      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(p.a_mn) << 15) |
-                             (uint32_t(p.b_mn) << 16) | (uint32_t(BN >> 3) << 17) |
-                             (uint32_t(TC_BM >> 4) << 24);
-      uint32_t it = 0, tt = 0;
-      bool ok = true;
-      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const int ks = int(u / p.tiles), ng = int(u % p.tiles) % p.n_groups;
-        const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
-        const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
-        for (int nt = nt0; nt < nt1 && ok; ++nt, ++tt) {
-          const uint32_t buf = tt & 1, use = tt >> 1;
-          if (use > 0 && !mbar_wait(&tempty[buf], (use - 1) & 1)) { ok = false; break; }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t dcol = tmem + buf * BN;
-          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+    // ---- MMA issuer: the whole warp runs the loop and waits (descriptors stay warp-uniform), one
+    //      elected lane issues every tcgen05.mma and tcgen05.commit (commits track that lane's MMAs)
+    const bool leader = elect_one();
+    const uint32_t idesc_base = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
+                                (uint32_t(TC_BM >> 4) << 24);
+    uint32_t it = 0, tt = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      const int ks = int(u / p.tiles), ng = int(u % p.tiles) % p.n_groups;
+      const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
+      const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
+      for (int nt = nt0; nt < nt1 && ok; ++nt, ++tt) {
+        const uint32_t buf = tt & 1, use = tt >> 1;
+        if (use > 0 && !mbar_wait_warp(&tempty[buf], (use - 1) & 1)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int pr = 0; pr < NPROD && ok; ++pr) {
+          const uint32_t dcol = tmem + buf * ABUF + uint32_t(pr * BN);
+          const int amn = pr ? p.a2_mn : p.a_mn, bmn = pr ? p.b2_mn : p.b_mn;
+          const uint32_t idesc = idesc_base | (uint32_t(amn) << 15) | (uint32_t(bmn) << 16);
+          const int kbs = pr ? 0 : kb0, kbe = pr ? nk2 : kb1;
+          for (int kb = kbs; kb < kbe; ++kb, ++it) {
             const int s = int(it % C::STAGES), r = int(it / C::STAGES);
-            if (!mbar_wait(&full[s], uint32_t(r & 1))) { ok = false; break; }
+            if (!mbar_wait_warp(&full[s], uint32_t(r & 1))) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t a_base = smem_u32(tiles + s * C::STAGE);
             const uint32_t b_base = a_base + TILE_A_BYTES;
@@ -211,16 +250,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int kk = 0; kk < TC_BK / 16; ++kk) {
               // K-major: advance 16 elements (32 B) inside the 128B swizzle row;
               // MN-major: advance 16 k-rows (2 KB), two 8-row atoms apart by SBO = 1 KB.
-              const uint64_t ad = p.a_mn ? sdesc(a_base + kk * 2048, TILE_A_BYTES / 2, 1024)
-                                         : sdesc(a_base + kk * 32, 16, 1024);
-              const uint64_t bd = p.b_mn ? sdesc(b_base + kk * 2048, 8192, 1024)
-                                         : sdesc(b_base + kk * 32, 16, 1024);
-              umma_bf16(dcol, ad, bd, idesc, (kb != kb0) || (kk != 0));
+              const uint64_t ad = amn ? sdesc(a_base + kk * 2048, TILE_A_BYTES / 2, 1024)
+                                      : sdesc(a_base + kk * 32, 16, 1024);
+              const uint64_t bd = bmn ? sdesc(b_base + kk * 2048, 8192, 1024)
+                                      : sdesc(b_base + kk * 32, 16, 1024);
+              if (leader) umma_bf16(dcol, ad, bd, idesc, (kb != kbs) || (kk != 0));
             }
-            umma_commit(&empty[s]);
+            if (leader) umma_commit(&empty[s]);
+            __syncwarp();
           }
-          umma_commit(&tfull[buf]);
         }
+        if (!ok) break;
+        if (leader) umma_commit(&tfull[buf]);
+        __syncwarp();
       }
     }
   } else {
@@ -250,9 +292,74 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       for (int nt = nt0; nt < nt1; ++nt, ++tt) {
         const uint32_t buf = tt & 1, use = tt >> 1;
+        // DUAL: the tile's 64 bias values of this warp's columns, loaded while the MMA runs
+        float bias_pre[64];
+        if (EK == EK_DUAL) {
+          const int64_t nh = int64_t(nt) * BN + hf * 64;
+          const float* bias = p.epi.bias;
+          if (bias && nh + 64 <= p.N && ((reinterpret_cast<uintptr_t>(bias + nh) & 15) == 0)) {
+            const float4* bq = reinterpret_cast<const float4*>(bias + nh);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float4 b4 = __ldg(bq + j);
+              bias_pre[4 * j] = b4.x; bias_pre[4 * j + 1] = b4.y; bias_pre[4 * j + 2] = b4.z; bias_pre[4 * j + 3] = b4.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) bias_pre[j] = (bias && nh + j < p.N) ? __ldg(bias + nh + j) : 0.f;
+          }
+        }
         if (!mbar_wait_warp(&tfull[buf], use & 1)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int64_t n0 = int64_t(nt) * BN;
+        if (EK == EK_DUAL) {
+          // ---- two accumulators per tile: z (columns 0..127 of the set) and d (128..255); this
+          //      thread owns row `row` and the warp's 64 columns nh .. nh+63 of both
+          const int64_t row0 = int64_t(mb) * TC_BM + q * 32;
+          const bool box_live = row0 < p.M;
+          const int64_t nh = n0 + hf * 64;
+          const uint32_t tq = tmem + buf * ABUF + (uint32_t(q * 32) << 16) + uint32_t(hf * 64);
+          uint32_t hpk[32], dpk[32];  // bf16 pairs of act(z) and d * act'(z)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t rz[32], rd[32];
+            tmem_ld32_nowait(tq + uint32_t(c * 32), rz);
+            tmem_ld32_nowait(tq + uint32_t(BN + c * 32), rd);
+            tmem_wait_ld();
+            if (c == 1) {
+              asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&tempty[buf]);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float2 z = add2(f2(__uint_as_float(rz[2 * j]), __uint_as_float(rz[2 * j + 1])),
+                                    f2(bias_pre[c * 32 + 2 * j], bias_pre[c * 32 + 2 * j + 1]));
+              const float2 d = f2(__uint_as_float(rd[2 * j]), __uint_as_float(rd[2 * j + 1]));
+              float2 h, gz;
+              if (p.epi.kind == PGF_EPI_GELU) {
+                float2 gp;
+                gelu_and_prime2(z, h, gp);
+                gz = mul2(d, gp);
+              } else {
+                h = f2(fmaxf(z.x, 0.f), fmaxf(z.y, 0.f));
+                gz = f2(z.x > 0.f ? d.x : 0.f, z.y > 0.f ? d.y : 0.f);
+              }
+              hpk[c * 16 + j] = pack_bf16(h.x, h.y);
+              dpk[c * 16 + j] = pack_bf16(gz.x, gz.y);
+            }
+          }
+          // boxes start inside the output (the TMA clips their far edges)
+          if (box_live && nh < p.N) {
+            uint8_t* b = stage_acquire(stg, sq, lane);
+            stage_row(b, lane, hpk);
+            stage_store(b, &tmD, nh, row0, 0, lane);
+            b = stage_acquire(stg, sq, lane);
+            stage_row(b, lane, dpk);
+            stage_store(b, &tmZ, nh, row0, 0, lane);
+          }
+          continue;
+        }
         if (EK != EK_CE_FWD && p.fast) {
           // ---- row-per-thread epilogue: this thread owns row `row` and the warp's BN/2 columns,
           //      taken 64 at a time (nh .. nh+63)
@@ -266,7 +373,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t r[32];
-            tmem_ld32(tmem + buf * BN + (uint32_t(q * 32) << 16) + tcol + uint32_t(c * 32), r);
+            tmem_ld32(tmem + buf * ABUF + (uint32_t(q * 32) << 16) + tcol + uint32_t(c * 32), r);
             if (c == 1 && g64 == BN / 128 - 1) {
               // both chunks are in registers: hand the accumulator back to the MMA warp
               asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -398,7 +505,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll 1
         for (int c = hf * (BN / 64); c < (BN == 128 || EK == EK_CE_FWD ? (hf + 1) * (BN / 64) : 0); ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + buf * BN + (uint32_t(q * 32) << 16) + uint32_t(c * 32), r);
+          tmem_ld32(tmem + buf * ABUF + (uint32_t(q * 32) << 16) + uint32_t(c * 32), r);
           const int64_t nc = n0 + c * 32;
           if (MODE == TC_CE_FWD) {
             // online log-sum-exp in base 2: exp(v - m) = exp2(v log2e - m log2e)
@@ -481,7 +588,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NCOL));
   }
 }
 
@@ -549,13 +656,15 @@ static int ek_of(const TcParams& p) {
   }
 }
 
+// ma2 / mb2: the second product's operands (DUAL; other modes pass copies of ma / mb, unused).
 template <int BN, int EK>
 static int launch_tc_kernel(unsigned grid, cudaStream_t s, const CUtensorMap& ma, const CUtensorMap& mb,
-                            const CUtensorMap& md, const CUtensorMap& mz, const TcParams& p) {
+                            const CUtensorMap& md, const CUtensorMap& mz, const TcParams& p,
+                            const CUtensorMap* ma2 = nullptr, const CUtensorMap* mb2 = nullptr) {
   using C = TcCfg<BN>;
   static int smem_limit = 0;
   PGF_CUDA(ensure_dynamic_smem(gemm_tc_kernel<BN, EK>, C::SMEM, smem_limit));
-  gemm_tc_kernel<BN, EK><<<grid, TC_THREADS, C::SMEM, s>>>(ma, mb, md, mz, p);
+  gemm_tc_kernel<BN, EK><<<grid, TC_THREADS, C::SMEM, s>>>(ma, mb, md, mz, ma2 ? *ma2 : ma, mb2 ? *mb2 : mb, p);
   return PGF_OK;
 }
 
@@ -638,6 +747,52 @@ int run_gemm_tc(const Gemm& g, cudaStream_t s) {
   p.D = g.D; p.d_bf16 = g.d_bf16; p.ldd = g.ldd;
   p.epi = g.epi;
   return launch_tc(g, p, s, PROF_GEMM_TC);
+}
+
+int run_gemm_tc_dual(const DualGemm& g, cudaStream_t s) {
+  if (g.M == 0 || g.N == 0) return PGF_OK;
+  if (g.kind != PGF_EPI_GELU && g.kind != PGF_EPI_RELU) return PGF_ERR_UNSUPPORTED;
+  // both products must suit the engine on their own (bf16 operands, 16-byte aligned rows)
+  const Gemm p1 = gemm_make(g.M, g.N, g.K1, g.A1, 1, g.lda1, 0, g.B1, 1, g.ldb1, g.b1_trans, g.H, 1, g.ldh);
+  const Gemm p2 = gemm_make(g.M, g.N, g.K2, g.A2, 1, g.lda2, 0, g.B2, 1, g.ldb2, g.b2_trans, g.DZ, 1, g.lddz);
+  if (!tc_usable(p1) || !tc_usable(p2) || fast_epilogue_disabled()) return PGF_ERR_UNSUPPORTED;
+  if (!aligned(g.H, 16) || !aligned(g.DZ, 16) || (g.ldh * 2) % 16 || (g.lddz * 2) % 16) return PGF_ERR_UNSUPPORTED;
+  CUtensorMap ma, mb, ma2, mb2, md, mz;
+  memset(&md, 0, sizeof md);
+  memset(&mz, 0, sizeof mz);
+  const bool ok = make_map(&ma, g.A1, g.K1, g.M, g.lda1, 64, TC_BM) &&
+                  (g.b1_trans ? make_map(&mb, g.B1, g.N, g.K1, g.ldb1, 64, 64)
+                              : make_map(&mb, g.B1, g.K1, g.N, g.ldb1, 64, TC_BN)) &&
+                  make_map(&ma2, g.A2, g.K2, g.M, g.lda2, 64, TC_BM) &&
+                  (g.b2_trans ? make_map(&mb2, g.B2, g.N, g.K2, g.ldb2, 64, 64)
+                              : make_map(&mb2, g.B2, g.K2, g.N, g.ldb2, 64, TC_BN)) &&
+                  make_out_map(&md, g.H, 1, g.N, g.M, g.ldh, 1, 0) &&
+                  make_out_map(&mz, g.DZ, 1, g.N, g.M, g.lddz, 1, 0);
+  if (!ok) return PGF_ERR_UNSUPPORTED;
+  TcParams p = {};
+  p.mode = TC_GENERIC;
+  p.M = g.M; p.N = g.N; p.K = g.K1; p.K2 = g.K2;
+  p.a_mn = 0; p.b_mn = g.b1_trans;
+  p.a2_mn = 0; p.b2_mn = g.b2_trans;
+  p.ng = 1;
+  const int64_t n_tiles = (g.N + TC_BN - 1) / TC_BN;
+  p.n_groups = int(n_tiles);
+  p.tiles = ((g.M + TC_BM - 1) / TC_BM) * n_tiles;
+  p.ksplit = 1;
+  p.kper = int((g.K1 + TC_BK - 1) / TC_BK);
+  p.units = p.tiles;
+  p.fast = 1;
+  p.z_bf16 = 1;
+  p.D = g.H; p.d_bf16 = 1; p.ldd = g.ldh;
+  p.epi = epi_default();
+  p.epi.kind = g.kind;
+  p.epi.bias = g.bias;
+  const unsigned grid = unsigned(p.units < sm_count() ? p.units : sm_count());
+  prof_begin(PROF_GEMM_TC, s);
+  PGF_TRY((launch_tc_kernel<TC_BN, EK_DUAL>(grid, s, ma, mb, md, mz, p, &ma2, &mb2)));
+  prof_end(PROF_GEMM_TC, s, 2.0 * double(g.M) * double(g.N) * double(g.K1 + g.K2));
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
 }
 
 int split_slices_tc(int64_t M, int64_t N, int64_t K) {

@@ -93,6 +93,39 @@ def test_lm_step_matches_autograd_golden():
         assert_close(grads[k], v, atol=5e-5, name=k)
 
 
+def _oracle_lm_f64(G):
+    n = G["n_layers"]
+    blocks = [{k[len(f"layers.{i}."):]: v.double() for k, v in G["params"].items() if k.startswith(f"layers.{i}.")}
+              for i in range(n)]
+    return O.lm_pgf_step(G["emb"].double(), G["lm_head"].double(), blocks, G["ids"], G["targets"], G["block_size"])
+
+
+def test_lm_step_f32_within_f32_bound_of_f64_oracle():
+    """The whole float32 PGF LM step (embedding, 2 layers, LM head + CE) against the float64 oracle at
+    the float32 bound: max-abs error <= 1e-5 + 1e-4 max|ref| for every gradient, loss within 1e-5."""
+    G = golden("lm.pt")
+    lm = _lm_from_golden(G)
+    loss, grads = lm.forward_backward(G["ids"].to(DEV), G["targets"].to(DEV))
+    rloss, ref = _oracle_lm_f64(G)
+    assert abs(loss.item() - rloss.item()) < 1e-5
+    assert set(grads) == set(ref)
+    for k, v in ref.items():
+        assert_close(grads[k], v, name=k)
+
+
+def test_lm_step_bf16_every_gradient_close_to_f64_oracle():
+    """bf16 activations (float32 weights and gradients): every gradient within 5e-2 relative L2 of the
+    float64 oracle, the loss within 2e-2 relative."""
+    G = golden("lm.pt")
+    lm = _lm_from_golden(G, act_dtype=torch.bfloat16)
+    loss, grads = lm.forward_backward(G["ids"].to(DEV), G["targets"].to(DEV))
+    rloss, ref = _oracle_lm_f64(G)
+    assert abs(loss.item() - rloss.item()) < 2e-2 * abs(rloss.item())
+    errs = {k: rel_err(grads[k], v) for k, v in ref.items()}
+    bad = {k: e for k, e in errs.items() if not e < 5e-2}
+    assert not bad, bad
+
+
 def test_block_config1_reference_variant_f64_oracle():
     """Config-1 shapes on the reference variant (d=128, N=16, B=2, L=512), bs=128, float64 truth."""
     g = torch.Generator().manual_seed(40)

@@ -225,6 +225,29 @@ def test_ffn_row_tiles(ops, act, rows, dtype):
             assert rel_err(r[k], ref[k]) < BF16_RTOL, (k, rel_err(r[k], ref[k]))
 
 
+@pytest.mark.parametrize("act", ["gelu", "relu"])
+@pytest.mark.parametrize("rows,d,dh", [(4096, 256, 1024), (5000 + 77, 256, 1024), (1000, 1024, 4096)])
+def test_ffn_bwd_bf16_model_shape(ops, act, rows, d, dh):
+    """bf16 FFN backward at the LM's widths: 256 -> 1024 -> 256, where the recomputed hidden
+    activation and the pre-activation gradient come from one two-product tensor-core kernel (the
+    pre-activation stays in tensor memory), and 1024 -> 4096 -> 1024, which keeps the separate
+    products; against the float64 oracle on the same bf16-rounded inputs and weights, ragged row
+    counts included."""
+    g = _gen(13)
+    x = torch.randn(rows, d, generator=g).bfloat16()
+    gy = torch.randn(rows, d, generator=g).bfloat16()
+    a1 = math.sqrt(6 / (d + dh))
+    W1 = (torch.rand(dh, d, generator=g) * 2 - 1) * a1
+    W2 = (torch.rand(d, dh, generator=g) * 2 - 1) * a1
+    b1, b2 = 0.1 * torch.randn(dh, generator=g), 0.1 * torch.randn(d, generator=g)
+    args = [t.to(DEV) for t in (W1, b1, W2, b2)]
+    r = ops.ffn_bwd(x.to(DEV), gy.to(DEV), args[0], args[1], args[2], activation=act)
+    ref = O.ffn_grad(x.double(), gy.double(), W1.bfloat16().double(), b1.double(), W2.bfloat16().double(),
+                     b2.double(), act)
+    for k in ("grad_W1", "grad_b1", "grad_W2", "grad_b2", "grad_x"):
+        assert rel_err(r[k], ref[k]) < 1e-2, (k, rel_err(r[k], ref[k]))
+
+
 def test_ffn_golden(ops):
     for act in ("gelu", "relu"):
         c = golden("components.pt")[f"ffn_{act}"]
