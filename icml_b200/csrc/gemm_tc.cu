@@ -40,19 +40,22 @@ namespace pgf {
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64;  // TC_BN: the CE modes' (and narrow outputs') tile width
 constexpr int TC_THREADS = 320;  // TMA warp, MMA warp, 8 epilogue warps
 constexpr int TILE_A_BYTES = TC_BM * TC_BK * 2;
-constexpr int EPI_WARP_BYTES = 8192;        // per epilogue warp: two 4 KB staging rows-of-128B buffers
-constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;  // (the transpose path uses the first 32x33 floats)
 
 // Tile width BN = 128 or 256 output columns.  At N = 256 a K = 16 MMA reads 12 KB of operands for
 // 1 MFLOP (8 KB for 0.5 MFLOP at N = 128), which keeps the tensor pipe ahead of the operand reads;
-// the price is three stages instead of four and all 512 TMEM columns (two accumulators).
+// the price is all 512 TMEM columns (two accumulators).  Four operand stages either way: at N = 256
+// they leave room for one 4 KB epilogue staging buffer per warp instead of two (measured: the fourth
+// stage, which hides more of the operand fetch latency, is worth more than the second buffer).
+// Every epilogue warp has at least 4 KB (the transpose path uses the first 32 x 33 floats).
 template <int BN>
 struct TcCfg {
   static constexpr int TILE_B = BN * TC_BK * 2;
-  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr int STAGES = 4;
   static constexpr int STAGE = TILE_A_BYTES + TILE_B;
-  static constexpr uint32_t TMEM = 2 * BN;
-  static constexpr size_t SMEM = size_t(STAGES) * STAGE + EPI_BYTES + 256 /* barriers */ + 1024 /* align */;
+  static constexpr int NBUF = BN == 256 ? 1 : 2;      // epilogue staging buffers per warp
+  static constexpr int EPI_WARP = NBUF * 4096;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE + 8 * EPI_WARP + 256 /* barriers */ + 1024 /* align */;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 enum { TC_GENERIC = 0, TC_CE_FWD = 1, TC_CE_BWD = 2 };
@@ -137,7 +140,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
   float* epi_buf = reinterpret_cast<float*>(tiles + C::STAGES * C::STAGE);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi_buf) + EPI_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi_buf) + 8 * C::EPI_WARP);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -270,7 +273,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     //      hf = (warp - 2) / 4 (columns 64hf..64hf+63 of the 128-column tile)
     const int q = warp & 3;
     const int hf = (warp - 2) >> 2;
-    uint8_t* stg = reinterpret_cast<uint8_t*>(epi_buf) + (warp - 2) * EPI_WARP_BYTES;
+    uint8_t* stg = reinterpret_cast<uint8_t*>(epi_buf) + (warp - 2) * C::EPI_WARP;
     float* tb = reinterpret_cast<float*>(stg);
     uint32_t sq = 0;  // staging buffers taken by this warp
     uint32_t tt = 0;
@@ -351,10 +354,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
           // boxes start inside the output (the TMA clips their far edges)
           if (box_live && nh < p.N) {
-            uint8_t* b = stage_acquire(stg, sq, lane);
+            uint8_t* b = stage_acquire<C::NBUF>(stg, sq, lane);
             stage_row(b, lane, hpk);
             stage_store(b, &tmD, nh, row0, 0, lane);
-            b = stage_acquire(stg, sq, lane);
+            b = stage_acquire<C::NBUF>(stg, sq, lane);
             stage_row(b, lane, dpk);
             stage_store(b, &tmZ, nh, row0, 0, lane);
           }
@@ -423,7 +426,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     uint32_t w[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
-                    uint8_t* b = stage_acquire(stg, sq, lane);
+                    uint8_t* b = stage_acquire<C::NBUF>(stg, sq, lane);
                     stage_row(b, lane, w);
                     stage_store(b, &tmZ, nb, row0, 0, lane);
                   }
@@ -480,20 +483,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               uint32_t w[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
-              uint8_t* b = stage_acquire(stg, sq, lane);
+              uint8_t* b = stage_acquire<C::NBUF>(stg, sq, lane);
               stage_row(b, lane, w);
               stage_store(b, &tmD, nb, row0, ks, lane);
             }
           }
           // boxes start inside the output (the TMA clips their far edges)
           if (box_live && nh < p.N && p.d_bf16) {
-            uint8_t* b = stage_acquire(stg, sq, lane);
+            uint8_t* b = stage_acquire<C::NBUF>(stg, sq, lane);
             stage_row(b, lane, dpk);
             stage_store(b, &tmD, nh, row0, ks, lane);
           }
           if (box_live && nh < p.N && MODE == TC_GENERIC && p.epi.aux_out && p.z_bf16 &&
               (EK == EK_ACT)) {
-            uint8_t* b = stage_acquire(stg, sq, lane);
+            uint8_t* b = stage_acquire<C::NBUF>(stg, sq, lane);
             stage_row(b, lane, zpk);
             stage_store(b, &tmZ, nh, row0, 0, lane);
           }

@@ -339,22 +339,26 @@ ce_bwd_dh3_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   const uint32_t tmem_h = tmem + BV + 256;         // h rows, d/2 columns
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---- TMA producer: W tiles through the three slots
-      uint32_t jj = 0;
-      bool ok = true;
-      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        for (int j = 0; j < p.n_tiles; ++j, ++jj) {
-          const uint32_t s = jj % NSLOT3, r = jj / NSLOT3;
-          if (r > 0 && !mbar_wait(&wempty[s], (r - 1) & 1)) { ok = false; break; }
+    // ---- TMA producer: W tiles through the three slots (the whole warp waits, one lane issues)
+    const bool leader = elect_one();
+    uint32_t jj = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      for (int j = 0; j < p.n_tiles; ++j, ++jj) {
+        const uint32_t s = jj % NSLOT3, r = jj / NSLOT3;
+        if (r > 0 && !mbar_wait_warp(&wempty[s], (r - 1) & 1)) { ok = false; break; }
+        if (leader) {
           mbar_expect_tx(&wfull[s], HB);
           for (int c = 0; c < dch; ++c) tma_load_2d(sW + s * HB + c * 16384, &tmW, &wfull[s], c * 64, j * BV);
         }
+        __syncwarp();
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---- MMA issuer: logits of tile j (A = h rows in TMEM), then dh of tile j-1
+    {
+      // ---- MMA issuer: logits of tile j (A = h rows in TMEM), then dh of tile j-1; the whole warp
+      //      runs the loop and waits, one elected lane issues every MMA and commit
+      const bool leader = elect_one();
       const uint32_t idesc_l = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BV >> 3) << 17) |
                                (uint32_t(BM >> 4) << 24);
       const uint32_t idesc_d = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (uint32_t(p.d >> 3) << 17) |
@@ -362,43 +366,51 @@ ce_bwd_dh3_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       uint32_t jj = 0, tt = 0, uu = 0;
       bool ok = true;
       auto issue_dh = [&](uint32_t t, uint32_t s, bool first) -> bool {
-        if (!mbar_wait(gready, t & 1)) return false;
-        if (first && uu > 0 && !mbar_wait(dhfree, (uu - 1) & 1)) return false;
+        if (!mbar_wait_warp(gready, t & 1)) return false;
+        if (first && uu > 0 && !mbar_wait_warp(dhfree, (uu - 1) & 1)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t g_base = smem_u32(sG), w_base = smem_u32(sW + s * HB);
 #pragma unroll
         for (int kk = 0; kk < BV / 16; ++kk) {
           const uint64_t ad = sdesc(g_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc(w_base + kk * 2048, 16384, 1024);
-          umma_bf16(tmem_dh, ad, bd, idesc_d, (!first || kk > 0) ? 1u : 0u);
+          if (leader) umma_bf16(tmem_dh, ad, bd, idesc_d, (!first || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&wempty[s]);
-        umma_commit(gfree);
+        if (leader) {
+          umma_commit(&wempty[s]);
+          umma_commit(gfree);
+        }
+        __syncwarp();
         return true;
       };
       for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uu) {
-        if (!mbar_wait(hready, uu & 1)) { ok = false; break; }
+        if (!mbar_wait_warp(hready, uu & 1)) { ok = false; break; }
         uint32_t prev_t = 0, prev_s = 0;
         for (int j = 0; j < p.n_tiles && ok; ++j, ++jj, ++tt) {
           const uint32_t s = jj % NSLOT3, r = jj / NSLOT3;
-          if (!mbar_wait(&wfull[s], r & 1)) { ok = false; break; }
-          if (tt > 0 && !mbar_wait(tempty, (tt - 1) & 1)) { ok = false; break; }
+          if (!mbar_wait_warp(&wfull[s], r & 1)) { ok = false; break; }
+          if (tt > 0 && !mbar_wait_warp(tempty, (tt - 1) & 1)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t w_base = smem_u32(sW + s * HB);
           for (int kk = 0; kk < 4 * dch; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_bf16_ta(tmem_l, tmem_h + uint32_t(8 * kk), sdesc(w_base + off, 16, 1024), idesc_l,
-                         kk > 0 ? 1u : 0u);
+            if (leader)
+              umma_bf16_ta(tmem_l, tmem_h + uint32_t(8 * kk), sdesc(w_base + off, 16, 1024), idesc_l,
+                           kk > 0 ? 1u : 0u);
           }
-          umma_commit(tfull);
-          if (j == p.n_tiles - 1) umma_commit(hfree);  // the unit's h rows are no longer read
+          if (leader) {
+            umma_commit(tfull);
+            if (j == p.n_tiles - 1) umma_commit(hfree);  // the unit's h rows are no longer read
+          }
+          __syncwarp();
           if (j > 0 && !issue_dh(prev_t, prev_s, j == 1)) { ok = false; break; }
           prev_t = tt;
           prev_s = s;
         }
         if (!ok) break;
         if (!issue_dh(prev_t, prev_s, p.n_tiles == 1)) { ok = false; break; }
-        umma_commit(dhdone);
+        if (leader) umma_commit(dhdone);
+        __syncwarp();
       }
     }
   } else {

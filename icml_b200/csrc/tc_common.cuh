@@ -164,10 +164,18 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // ---- epilogue staging: 32 rows x 128 B, 128B-swizzled (16-byte chunk j of row r at j ^ (r % 8)),
 //      written by the warp and stored to global memory by one TMA bulk-tensor store.
+// NB = 2: two 4 KB buffers taken in turn (the store issued from a buffer two stagings ago must have
+// finished reading it); NB = 1: one buffer (the previous store must have finished reading it).
+template <int NB = 2>
 __device__ __forceinline__ uint8_t* stage_acquire(uint8_t* stg, uint32_t& sq, int lane) {
-  uint8_t* b = stg + (sq & 1u) * 4096u;
-  // the store issued from this buffer two stagings ago must have finished reading it
-  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  static_assert(NB == 1 || NB == 2, "one or two staging buffers");
+  uint8_t* b = stg + (sq % uint32_t(NB)) * 4096u;
+  if (lane == 0) {
+    if (NB == 2)
+      asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    else
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
   __syncwarp();
   ++sq;
   return b;
