@@ -646,11 +646,12 @@ __global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const
 }
 
 // Gradient of the halo rows: dxi_halo[b, K-1+j, e] = sum_k w[e, k] dxc[j + K-1-k] over the tokens
-// 0 <= j + K-1-k < L that read halo row j (j = -(K-1) .. -1), float32 (Bsz, K-1, E).
+// 0 <= j + K-1-k < L that read halo row j (j = -(K-1) .. -1), (Bsz, K-1, E) in the activation dtype
+// (bf16 runs take its two products on the tensor cores).
 template <int K>
 __global__ void conv_halo_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const void* __restrict__ halo,
                                      const float* __restrict__ w, const float* __restrict__ bias,
-                                     const float* __restrict__ du, float* __restrict__ dhalo, int64_t Bsz,
+                                     const float* __restrict__ du, void* __restrict__ dhalo, int64_t Bsz,
                                      int64_t L, int64_t E, int abf) {
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t b = blockIdx.y;
@@ -675,7 +676,7 @@ __global__ void conv_halo_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, 
       const int t = j + (K - 1) - k;
       if (t >= 0) acc = fmaf(wk[k], dxc[t], acc);
     }
-    dhalo[(b * (K - 1) + (K - 1) + j) * E + e] = acc;
+    stv(dhalo, abf, (b * (K - 1) + (K - 1) + j) * E + e, acc);
   }
 }
 
@@ -687,7 +688,7 @@ static void launch_conv_fwd(dim3 grid, cudaStream_t s, const void* xi, int64_t l
 template <int K>
 static void launch_conv_bwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo,
                             const float* w, const float* bias, const float* du, void* dxi, int64_t ld_dx, float* part,
-                            int64_t Bsz, int64_t L, int64_t E, int abf, float* dhalo) {
+                            int64_t Bsz, int64_t L, int64_t E, int abf, void* dhalo) {
   conv_bwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf);
   if (dhalo && K > 1)
     conv_halo_bwd_kernel<K><<<dim3(grid.x, unsigned(Bsz)), 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dhalo, Bsz, L,
@@ -710,7 +711,7 @@ static int conv_fwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld
 
 static int conv_bwd(int K, dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo, const float* w,
                     const float* bias, const float* du, void* dxi, int64_t ld_dx, float* part, int64_t Bsz, int64_t L,
-                    int64_t E, int abf, float* dhalo) {
+                    int64_t E, int abf, void* dhalo) {
   switch (K) {
 #define PGF_CONV_BWD(k) \
     case k: launch_conv_bwd<k>(grid, s, xi, ld_x, halo, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf, dhalo); break;
@@ -753,7 +754,7 @@ struct Bufs {
   void* split;  // split-K partials of the weight gradients
   size_t split_bytes;
   void* xi_halo;     // pre-conv projection of the halo rows (Bsz, K-1, E), activation dtype
-  float* dxi_halo;   // its gradient (Bsz, K-1, E)
+  float* dxi_halo;   // its gradient (Bsz, K-1, E), activation dtype
 };
 
 // column-sum scratch: grad dt_b over tokens and the conv parameter partials over slabs
@@ -1246,10 +1247,11 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
       // the halo rows fed this segment's conv through W_in[:E]: grad W_in[:E] += dxi_halo^T x_halo,
       // and their own gradient g_x_halo = dxi_halo W_in[:E] goes back to the segment they belong to
       const int64_t Th = p.Bsz * (p.K - 1);
-      Gemm gh = mstd::G_(E, d, Th, B.dxi_halo, 0, E, 1, c.x_halo, dtype, d, 1, g_in_w, 0, d);
+      Gemm gh = mstd::G_(E, d, Th, B.dxi_halo, dtype, E, 1, c.x_halo, dtype, d, 1, g_in_w, 0, d);
       gh.epi.accumulate = 1;
       PGF_TRY(run_gemm(gh, s));
-      if (c.g_x_halo) PGF_TRY(run_gemm(mstd::G_(Th, d, E, B.dxi_halo, 0, E, 0, in_w, 0, d, 1, c.g_x_halo, dtype, d), s));
+      if (c.g_x_halo)
+        PGF_TRY(run_gemm(mstd::G_(Th, d, E, B.dxi_halo, dtype, E, 0, iw, dtype, d, 1, c.g_x_halo, dtype, d), s));
     }
   }
   return PGF_OK;
