@@ -8,6 +8,11 @@ block size 4096, synthetic Zipf(1.1) token ids, bf16 activations, fp32 weights a
 boundary-state hand-off between segments, one gradient all-reduce): the total work is fixed (strong
 scaling).  --parallel dp runs one such sequence per GPU instead (weak scaling).
 
+The same line carries, under "mamba_standard", the same measurement of the Mamba-standard model of
+the benchmark configurations (d_inner 512, d_conv 4, dt_rank 16, per-channel A, final RMSNorm, tied
+head) on the same sequence and GPUs, which the reference has no code for (--no-std-companion skips
+it; --variant std makes it the headline).
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--seq-len L] [--impl b200|reference]
 
 --impl reference times the reference's PGF step restated on the CPU (the oracle, float32, all host
@@ -66,6 +71,8 @@ def parse():
     ap.add_argument("--stash", default="device", choices=["device", "host", "scan"],
                     help="where layer inputs wait for the backward: device memory, pinned host memory, or "
                          "device memory together with each layer's scan states (no scan recompute)")
+    ap.add_argument("--no-std-companion", action="store_true",
+                    help="skip the Mamba-standard model measured after the reference variant (key mamba_standard)")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of the CUDA-graph captured step (1 GPU)")
     ap.add_argument("--parallel", default="sp", choices=["sp", "dp"],
@@ -490,9 +497,7 @@ PROF_NAMES = {0: "ssm_chunk_fwd", 1: "ssm_compose", 2: "ssm_out_fwd", 3: "ssm_ch
 
 
 def run_gpu(a, rank, world, local_rank):
-    import ctypes
     from icml_b200 import _lib
-    from icml_b200.lm import PGFLanguageModel
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -503,6 +508,37 @@ def run_gpu(a, rank, world, local_rank):
                                              device_id=dev)
         pg = torch.distributed.group.WORLD
     L = _lib.lib()
+    r = _measure_model(a, rank, world, local_rank, dev, pg, L)
+    line = None
+    if rank == 0:
+        line = _line_of(a, world, r)
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(a)
+    # the model of the benchmark configurations (Mamba-standard block) on the same sequence, when the
+    # headline runs the reference's own SSM variant
+    if a.variant == "reference" and not a.no_std_companion:
+        b = argparse.Namespace(**vars(a))
+        b.variant = "std"
+        r2 = _measure_model(b, rank, world, local_rank, dev, pg, L)
+        if rank == 0:
+            l2 = _line_of(b, world, r2)
+            line["mamba_standard"] = {k: l2[k] for k in ("metric", "value", "unit", "ms_per_step", "scaling",
+                                                         "config", "peak_hbm_gb", "clocks", "e2e",
+                                                         "gpu_launches", "cuda_graph", "kernels",
+                                                         "dominant_kernel", "roofline")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def _measure_model(a, rank, world, local_rank, dev, pg, L):
+    """Build the LM of `a`, run its warm-up, profiled, timed and end-to-end steps; returns the
+    measurements (max over ranks) and releases the model's graph and memory."""
+    import ctypes
+    from icml_b200.lm import PGFLanguageModel
+
     act = torch.bfloat16 if a.dtype == "bf16" else torch.float32
     torch.manual_seed(1234)
     if a.variant == "std":
@@ -682,44 +718,49 @@ def run_gpu(a, rank, world, local_rank):
         torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
     e2e = tokens / (te.item() / 1e3)
 
-    if rank == 0:
-        dom = max(prof_ms, key=prof_ms.get) if prof_ms else None
-        # per-kernel figures come from the eager profiled steps (graph replays carry no timers)
-        traffic = TRAFFIC_DEFAULT if default_workload(a, world) else {}
-        kernels = {k: {"launches_per_step": prof_n[k], "ms_per_step": prof_ms[k],
-                       "share_of_step": prof_ms[k] / ms_step if ms_step else None,
-                       "roofline": roofline_entry(k, prof_ms[k], prof_n[k], prof_w[k], traffic.get(k))}
-                   for k in prof_ms}
-        compute_roofline = None
-        if "ssm_main_bwd" in kernels and default_workload(a, world):
-            mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
-            compute_roofline = issue_roofline(kernels["ssm_main_bwd"]["roofline"]["ms_per_launch"], mhz)
-        line = {
-            "metric": metric_of(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling_of(a, world),
-            "vs_baseline": None, "dtype": a.dtype, "data": "synthetic (Zipf 1.1 token ids, random init)",
-            "config": dict(config_of(a, world), launch=(
-                "whole step (with its collectives) captured once as a CUDA graph, replayed each step"
-                if graphed is not None else "eager launches")), "impl": "b200",
-            "peak_hbm_gb": peak_gb, "loss": loss_val, "clocks": clocks,
-            "e2e": {"value": e2e, "unit": UNIT,
-                    "h2d_bytes_per_step": inp_host.numel() * 8 * 2, "d2h_bytes_per_step": 4},
-            "gpu_launches": int(launches),
-            "cuda_graph": graphed is not None,
-            "kernels": kernels, "dominant_kernel": dom,
-            "roofline": kernels[dom]["roofline"] if dom else None,
-            "compute_roofline": compute_roofline,
-        }
-        if world == 1 and not a.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(a)
-        print(json.dumps(line), flush=True)
+    r = {"value": value, "ms_step": ms_step, "e2e": e2e, "peak_gb": peak_gb, "clocks": clocks,
+         "launches": launches, "graphed": graphed is not None, "loss": loss_val,
+         "prof_ms": prof_ms, "prof_n": prof_n, "prof_w": prof_w, "h2d": inp_host.numel() * 8 * 2}
     if graphed is not None:
         torch.cuda.synchronize()
         graphed.release()  # the graph holds NCCL work on N GPUs: release it before the process group
         del graphed
-    if pg is not None:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    del model, reducer, inp, tgt
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return r
+
+
+def _line_of(a, world, r):
+    """The JSON line of one measured model (rank 0)."""
+    prof_ms, prof_n, prof_w, ms_step = r["prof_ms"], r["prof_n"], r["prof_w"], r["ms_step"]
+    dom = max(prof_ms, key=prof_ms.get) if prof_ms else None
+    # per-kernel figures come from the eager profiled steps (graph replays carry no timers)
+    traffic = TRAFFIC_DEFAULT if default_workload(a, world) else {}
+    kernels = {k: {"launches_per_step": prof_n[k], "ms_per_step": prof_ms[k],
+                   "share_of_step": prof_ms[k] / ms_step if ms_step else None,
+                   "roofline": roofline_entry(k, prof_ms[k], prof_n[k], prof_w[k], traffic.get(k))}
+               for k in prof_ms}
+    clocks = r["clocks"]
+    compute_roofline = None
+    if "ssm_main_bwd" in kernels and default_workload(a, world):
+        mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
+        compute_roofline = issue_roofline(kernels["ssm_main_bwd"]["roofline"]["ms_per_launch"], mhz)
+    return {
+        "metric": metric_of(a), "value": r["value"], "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling_of(a, world),
+        "vs_baseline": None, "dtype": a.dtype, "data": "synthetic (Zipf 1.1 token ids, random init)",
+        "config": dict(config_of(a, world), launch=(
+            "whole step (with its collectives) captured once as a CUDA graph, replayed each step"
+            if r["graphed"] else "eager launches")), "impl": "b200",
+        "peak_hbm_gb": r["peak_gb"], "loss": r["loss"], "clocks": clocks,
+        "e2e": {"value": r["e2e"], "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": 4},
+        "gpu_launches": int(r["launches"]),
+        "cuda_graph": r["graphed"],
+        "kernels": kernels, "dominant_kernel": dom,
+        "roofline": kernels[dom]["roofline"] if dom else None,
+        "compute_roofline": compute_roofline,
+    }
 
 
 if __name__ == "__main__":
