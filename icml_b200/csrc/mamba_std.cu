@@ -392,10 +392,14 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
   const float Dd = l.ch ? a.Dp[l.d] : 0.f;
   const int64_t cb = l.b * a.nC + l.c;
   const int nsub = int((l.e - l.s + ST - 1) / ST);
-  float carry[NS];
-#pragma unroll
-  for (int j = 0; j < NS; ++j) carry[j] = l.ch ? a.X[(cb * a.E + l.d) * NST + l.nq * NS + j] : 0.f;
-  float accA[NS] = {0.f, 0.f, 0.f, 0.f};
+  // the thread's NS states as NP packed float32 pairs
+  float2 A2p[NP], Ap[NP];
+  a2_pairs(K, A2p);
+  Ap[0] = f2(K.A[0], K.A[1]);
+  Ap[1] = f2(K.A[2], K.A[3]);
+  float2 carry[NP] = {f2(0.f), f2(0.f)};
+  if (l.ch) ld_pairs(a.X + (cb * a.E + l.d) * NST + l.nq * NS, carry);
+  float2 accA[NP] = {f2(0.f), f2(0.f)};
   float accD = 0.f;
   const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
   Pref r;
@@ -403,58 +407,74 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
   pref_store(r, l, true, stg[(nsub - 1) & 1]);
   __syncthreads();
   // sub-chunk start states, loaded one sub-chunk ahead so the re-run never waits on memory
-  auto ckpt_at = [&](int k, float (&dst)[NS]) {
-    const float4 v = l.ch ? *reinterpret_cast<const float4*>(
-                                a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-    dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+  auto ckpt_at = [&](int k, float2 (&dst)[NP]) {
+    if (l.ch) {
+      ld_pairs(a.ckpt_g + (((l.b * a.nC + l.c) * KS + k) * a.E + l.d) * NST + l.nq * NS, dst);
+    } else {
+      dst[0] = dst[1] = f2(0.f);
+    }
   };
-  float ck_next[NS];
+  float2 ck_next[NP];
   ckpt_at(nsub - 1, ck_next);
   for (int k = nsub - 1; k >= 0; --k) {
     if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
     const Stage& S = stg[k & 1];
     float* gb = gbuf + (k & 1) * (3 * ST * DC);
-    float tr[ST + 1][NS], ex[ST][NS];
-#pragma unroll
-    for (int j = 0; j < NS; ++j) tr[0][j] = ck_next[j];
+    // re-run the sub-chunk into registers: tr[i] = state before token i, ex[i] = exp(delta_i A)
+    float2 tr[ST + 1][NP], ex[ST][NP];
+    tr[0][0] = ck_next[0];
+    tr[0][1] = ck_next[1];
     if (k > 0) ckpt_at(k - 1, ck_next);
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
+      if (l.s + int64_t(k) * ST + i < l.e) {
+        const float dt = S.dt[i][l.dl];
+        const float2 dt2 = f2(dt), du = f2(dt * S.u[i][l.dl]);
+        const float4 Bq = S.B[i][l.nq];
+        const float2 Bv[NP] = {lo2(Bq), hi2(Bq)};
 #pragma unroll
-      for (int j = 0; j < NS; ++j) tr[i + 1][j] = tr[i][j];
-      if (l.s + int64_t(k) * ST + i < l.e) step_fwd(S, i, l.dl, l.nq, K, tr[i + 1], ex[i]);
-      else {
+        for (int p = 0; p < NP; ++p) {
+          ex[i][p] = ex2_2(mul2(dt2, A2p[p]));
+          tr[i + 1][p] = fma2(ex[i][p], tr[i][p], mul2(du, Bv[p]));
+        }
+      } else {
 #pragma unroll
-        for (int j = 0; j < NS; ++j) ex[i][j] = 1.f;
+        for (int p = 0; p < NP; ++p) {
+          ex[i][p] = f2(1.f);
+          tr[i + 1][p] = tr[i][p];
+        }
       }
     }
 #pragma unroll
     for (int i = ST - 1; i >= 0; --i) {
       const bool valid = l.s + int64_t(k) * ST + i < l.e;
-      float v8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      float gdt = 0.f, gur = 0.f, hc = 0.f;
-      const float dt = S.dt[i][l.dl], uu = S.u[i][l.dl], dy = S.zs[i][l.dl];
+      float2 vB[NP] = {f2(0.f), f2(0.f)}, vC[NP] = {f2(0.f), f2(0.f)};
+      float2 gdt2 = f2(0.f), gur2 = f2(0.f), hc2 = f2(0.f);
+      const float uu = S.u[i][l.dl];
       if (valid) {
+        const float dt = S.dt[i][l.dl], dy = S.zs[i][l.dl];
+        const float2 dt2 = f2(dt), uu2 = f2(uu), dy2 = f2(dy), du2 = f2(dt * uu);
         const float4 Bq = S.B[i][l.nq], Cq = S.C[i][l.nq];
-        const float Bv[NS] = {Bq.x, Bq.y, Bq.z, Bq.w};
-        const float Cv[NS] = {Cq.x, Cq.y, Cq.z, Cq.w};
-        const float du = dt * uu;
+        const float2 Bv[NP] = {lo2(Bq), hi2(Bq)};
+        const float2 Cv[NP] = {lo2(Cq), hi2(Cq)};
 #pragma unroll
-        for (int j = 0; j < NS; ++j) {
-          hc = fmaf(Cv[j], tr[i + 1][j], hc);
-          const float dlt = carry[j] + dy * Cv[j];
-          const float ez = ex[i][j];
-          const float eh = ez * tr[i][j];
+        for (int p = 0; p < NP; ++p) {
+          hc2 = fma2(Cv[p], tr[i + 1][p], hc2);
+          const float2 dlt = fma2(dy2, Cv[p], carry[p]);
+          const float2 ez = ex[i][p];
+          const float2 eh = mul2(ez, tr[i][p]);
           // dh_t/d delta = A e h_{t-1} + B u ;  dh_t/dA = delta e h_{t-1}
-          gdt = fmaf(dlt, fmaf(K.A[j], eh, Bv[j] * uu), gdt);
-          accA[j] = fmaf(dlt * dt, eh, accA[j]);
-          gur = fmaf(dlt * dt, Bv[j], gur);
-          v8[j] = dlt * du;
-          v8[NS + j] = dy * tr[i + 1][j];
-          carry[j] = ez * dlt;
+          gdt2 = fma2(dlt, fma2(Ap[p], eh, mul2(Bv[p], uu2)), gdt2);
+          const float2 ddt = mul2(dlt, dt2);
+          accA[p] = fma2(ddt, eh, accA[p]);
+          gur2 = fma2(ddt, Bv[p], gur2);
+          vB[p] = mul2(dlt, du2);
+          vC[p] = mul2(dy2, tr[i + 1][p]);
+          carry[p] = mul2(ez, dlt);
         }
       }
+      float gdt = hsum2(gdt2), gur = hsum2(gur2), hc = hsum2(hc2);
+      const float dy = S.zs[i][l.dl];
       gdt += __shfl_xor_sync(0xffffffffu, gdt, 1);
       gdt += __shfl_xor_sync(0xffffffffu, gdt, 2);
       gur += __shfl_xor_sync(0xffffffffu, gur, 1);
@@ -467,6 +487,7 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
         gb[2 * ST * DC + i * DC + l.dl] = S.gs[i][l.dl] * (hc + Dd * uu);    // grad z
         accD = fmaf(dy, uu, accD);
       }
+      const float v8[8] = {vB[0].x, vB[0].y, vB[1].x, vB[1].y, vC[0].x, vC[0].y, vC[1].x, vC[1].y};
       float w4[4], w2[2];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -515,9 +536,10 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
     __syncthreads();
   }
   if (l.ch) {
+    const float accs[NS] = {accA[0].x, accA[0].y, accA[1].x, accA[1].y};
 #pragma unroll
     for (int j = 0; j < NS; ++j)
-      a.partA[((l.c * a.Bsz + l.b) * a.E + l.d) * NST + l.nq * NS + j] = accA[j] * K.A[j];  // d/dA_log
+      a.partA[((l.c * a.Bsz + l.b) * a.E + l.d) * NST + l.nq * NS + j] = accs[j] * K.A[j];  // d/dA_log
     if (l.nq == 0) a.partD[(l.c * a.Bsz + l.b) * a.E + l.d] = accD;
   }
 }
