@@ -380,13 +380,112 @@ __global__ void __launch_bounds__(32 * CSEG) compose_bwd_kernel(const Args a) {
 
 // Main backward: checkpoints from the forward output pass (ckpt_g) are required.
 // Dynamic shared memory: red [ST][WARPS][32], gbuf [2][3][ST][DC].
+// Untransformed inputs of one backward sub-chunk, copied global -> shared by cp.async in 16-byte
+// pieces a sub-chunk ahead of their use (no register holds them and no thread waits on them while it
+// computes): dt_raw and [B | C] (float32), u, z and g (bf16 rows fill the first half of each row) and
+// the sub-chunk's start states of the 64 channels.
+struct Raw {
+  float dtr[ST][DC];
+  float bc[ST][32];
+  float u[ST][DC];
+  float z[ST][DC];
+  float g[ST][DC];
+  float ck[DC * NST];
+};
+
+__device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Issue the copies of sub-chunk k into R (every thread takes every THREADS-th 16-byte piece).
+// Pieces of tokens past the chunk or channels past E are zero-filled (nothing is read for them).
+// Needs E, ld_dt, ld_bc and ld_z multiples of 8 and 16-byte aligned bases (the host checks).
+__device__ __forceinline__ void raw_issue(const Args& a, const Lane& l, int k, Raw& R) {
+  const int es = a.abf ? 2 : 4;
+  const int pu = DC * es / 16;  // pieces per token row of u, z and g
+  const int n_dt = ST * 16, n_bc = ST * 8, n_act = 3 * ST * pu, n_ck = DC * NST / 4;
+  const int total = n_dt + n_bc + n_act + n_ck;
+  const int64_t t0 = l.s + int64_t(k) * ST, c0 = int64_t(l.grp) * DC;
+  const int KS = int((a.Tc + ST - 1) / ST);
+  const int64_t ck = (l.b * a.nC + l.c) * KS + k;
+  for (int pc = l.tid; pc < total; pc += THREADS) {
+    int q = pc;
+    if (q < n_dt) {
+      const int t = q >> 4, c = (q & 15) * 4;
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e && c0 + c < a.E;
+      cp16(&R.dtr[t][c], v ? a.dt + (l.b * a.L + tok) * a.ld_dt + c0 + c : a.dt, v);
+      continue;
+    }
+    q -= n_dt;
+    if (q < n_bc) {
+      const int t = q >> 3, c = (q & 7) * 4;
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e;
+      cp16(&R.bc[t][c], v ? a.bc + (l.b * a.L + tok) * a.ld_bc + c : a.bc, v);
+      continue;
+    }
+    q -= n_bc;
+    if (q < n_act) {
+      const int which = q / (ST * pu);  // 0: u, 1: z, 2: g
+      q -= which * ST * pu;
+      const int t = q / pu, c = (q % pu) * (16 / es);
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e && c0 + c < a.E;
+      const char* base = static_cast<const char*>(which == 0 ? a.u : which == 1 ? a.zg : a.g);
+      const int64_t ld = which == 1 ? a.ld_z : a.E;
+      float* dst = which == 0 ? &R.u[t][0] : which == 1 ? &R.z[t][0] : &R.g[t][0];
+      cp16(reinterpret_cast<char*>(dst) + c * es, v ? base + ((l.b * a.L + tok) * ld + c0 + c) * es : base, v);
+      continue;
+    }
+    q -= n_act;
+    {
+      const int c = q >> 2;  // channel; four pieces of four states each
+      const bool v = c0 + c < a.E;
+      cp16(&R.ck[q * 4], v ? a.ckpt_g + (ck * a.E + c0) * NST + q * 4 : a.ckpt_g, v);
+    }
+  }
+  cp_commit();
+}
+
+// The stage of a backward sub-chunk from its raw inputs (the transform of pref_store).
+__device__ __forceinline__ void raw_store(const Args& a, const Raw& R, const Lane& l, Stage& st) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    const float x = R.dtr[t][dl];
+    const float uu = a.abf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.u[t][0])[dl]) : R.u[t][dl];
+    const float zz = a.abf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.z[t][0])[dl]) : R.z[t][dl];
+    const float gg = a.abf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.g[t][0])[dl]) : R.g[t][dl];
+    const float y = exp_neg_abs(x);
+    st.dt[t][dl] = softplus_from(x, y);
+    st.u[t][dl] = uu;
+    st.zs[t][dl] = gg * silu_f(zz);
+    st.gs[t][dl] = gg * silu_prime_f(zz);
+    st.sig[t][dl] = sigmoid_from(x, y);
+  }
+  const int t = l.tid >> 5, j = l.tid & 31;
+  if (t < ST) {
+    float* dst = j < NST ? reinterpret_cast<float*>(&st.B[t][0]) + j : reinterpret_cast<float*>(&st.C[t][0]) + (j - NST);
+    *dst = R.bc[t][j];
+  }
+}
+
+// ASYNC: inputs staged by cp.async through two Raw buffers after the kernel's other shared memory;
+// otherwise through registers one sub-chunk ahead.
+template <bool ASYNC>
 __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   __shared__ Stage stg[2];
   const Lane l = lane_of(a);
   const int KS = int((a.Tc + ST - 1) / ST);
   float* red = sm;
   float* gbuf = red + ST * WARPS * 32;
+  Raw* raw = reinterpret_cast<Raw*>(gbuf + 2 * 3 * ST * DC);  // [2], ASYNC only
   const int lane = l.tid & 31, warp = l.tid >> 5;
   const AConst K = load_A(a, l);
   const float Dd = l.ch ? a.Dp[l.d] : 0.f;
@@ -402,10 +501,6 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
   float2 accA[NP] = {f2(0.f), f2(0.f)};
   float accD = 0.f;
   const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
-  Pref r;
-  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
-  pref_store(r, l, true, stg[(nsub - 1) & 1]);
-  __syncthreads();
   // sub-chunk start states, loaded one sub-chunk ahead so the re-run never waits on memory
   auto ckpt_at = [&](int k, float2 (&dst)[NP]) {
     if (l.ch) {
@@ -415,16 +510,39 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
     }
   };
   float2 ck_next[NP];
-  ckpt_at(nsub - 1, ck_next);
+  // ASYNC: stage kk and the start state of sub-chunk kk from raw buffer kk & 1
+  auto fill = [&](int kk) {
+    const Raw& R = raw[kk & 1];
+    raw_store(a, R, l, stg[kk & 1]);
+    if (l.ch) {
+      ld_pairs(&R.ck[l.dl * NST + l.nq * NS], ck_next);
+    } else {
+      ck_next[0] = ck_next[1] = f2(0.f);
+    }
+  };
+  Pref r;
+  if (ASYNC) {
+    raw_issue(a, l, nsub - 1, raw[(nsub - 1) & 1]);
+    cp_wait_all();
+    __syncthreads();
+    fill(nsub - 1);
+    __syncthreads();
+    if (nsub > 1) raw_issue(a, l, nsub - 2, raw[(nsub - 2) & 1]);
+  } else {
+    pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+    pref_store(r, l, true, stg[(nsub - 1) & 1]);
+    __syncthreads();
+    ckpt_at(nsub - 1, ck_next);
+  }
   for (int k = nsub - 1; k >= 0; --k) {
-    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    if (!ASYNC && k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
     const Stage& S = stg[k & 1];
     float* gb = gbuf + (k & 1) * (3 * ST * DC);
     // re-run the sub-chunk into registers: tr[i] = state before token i, ex[i] = exp(delta_i A)
     float2 tr[ST + 1][NP], ex[ST][NP];
     tr[0][0] = ck_next[0];
     tr[0][1] = ck_next[1];
-    if (k > 0) ckpt_at(k - 1, ck_next);
+    if (!ASYNC && k > 0) ckpt_at(k - 1, ck_next);
 #pragma unroll
     for (int i = 0; i < ST; ++i) {
       if (l.s + int64_t(k) * ST + i < l.e) {
@@ -505,8 +623,14 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
       const float send = b2 ? w2[0] : w2[1];
       red[(i * WARPS + warp) * 32 + lane] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
     }
-    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
-    __syncthreads();
+    if (ASYNC) {
+      if (k > 0) cp_wait_all();  // sub-chunk k-1's raw inputs (issued a sub-chunk ago) have landed
+      __syncthreads();
+      if (k > 0) fill(k - 1);
+    } else {
+      if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
+      __syncthreads();
+    }
     {
       const int i = l.tid >> 5, ln = l.tid & 31;
       const int64_t t = l.s + int64_t(k) * ST + i;
@@ -534,6 +658,8 @@ __global__ void __launch_bounds__(THREADS, 2) main_bwd_kernel(const Args a) {
       }
     }
     __syncthreads();
+    // raw buffer k & 1 held sub-chunk k, whose stage was filled a sub-chunk ago
+    if (ASYNC && k > 1) raw_issue(a, l, k - 2, raw[k & 1]);
   }
   if (l.ch) {
     const float accs[NS] = {accA[0].x, accA[0].y, accA[1].x, accA[1].y};
@@ -1216,8 +1342,19 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
   a.dh_end = a.dA_end = nullptr;
   a.dh_start = a.dA_start = nullptr;
   const size_t smem = size_t(mstd::ST * mstd::WARPS * 32 + 2 * 3 * mstd::ST * mstd::DC) * 4;
+  // cp.async staging of the inputs when every row and base is 16-byte aligned
+  const bool async = E % 8 == 0 && a.ld_dt % 8 == 0 && a.ld_bc % 8 == 0 && a.ld_z % 8 == 0 && aligned(a.u, 16) &&
+                     aligned(a.dt, 16) && aligned(a.bc, 16) && aligned(a.zg, 16) && aligned(a.g, 16) &&
+                     aligned(a.ckpt_g, 16);
   prof_begin(PROF_SSM_MAIN_BWD, s);
-  mstd::main_bwd_kernel<<<grid, mstd::THREADS, smem, s>>>(a);
+  if (async) {
+    const size_t smem_a = smem + 2 * sizeof(mstd::Raw);
+    static int smem_limit_async = 0;
+    PGF_CUDA(ensure_dynamic_smem(mstd::main_bwd_kernel<true>, smem_a, smem_limit_async));
+    mstd::main_bwd_kernel<true><<<grid, mstd::THREADS, smem_a, s>>>(a);
+  } else {
+    mstd::main_bwd_kernel<false><<<grid, mstd::THREADS, smem, s>>>(a);
+  }
   prof_end(PROF_SSM_MAIN_BWD, s, double(T) * es * (7.0 * E + 2 * mstd::NST) + double(T) * 8 * mstd::NST);
   PGF_LAUNCH_CHECK();
   mstd::bc_reduce_kernel<<<ceil_div(T * 32, 256), 256, 0, s>>>(a);
