@@ -685,6 +685,7 @@ __global__ void bc_reduce_kernel(const Args a) {
 // causal depthwise conv1d + SiLU
 // ---------------------------------------------------------------------------------------------
 constexpr int CONV_T = 64;  // tokens per thread block row
+constexpr int CONV_G = 8;   // tokens whose inputs a thread loads together
 constexpr int KMAX = 8;
 
 // u[t, e] = SiLU(b[e] + sum_k w[e, k] xi[t - (K-1) + k, e]); xi rows have pitch ld_x.
@@ -715,15 +716,22 @@ __global__ void conv_fwd_kernel(const void* __restrict__ xi, int64_t ld_x, const
 #pragma unroll
   for (int k = 0; k < K - 1; ++k) win[k] = xi_at(xi, ld_x, halo, abf, b, L, E, K, t0 - (K - 1) + k, e);
   const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
-#pragma unroll 4
-  for (int64_t t = t0; t < t1; ++t) {
-    win[K - 1] = ldv(xi, abf, (b * L + t) * ld_x + e);
-    float acc = be;
+  for (int64_t tg = t0; tg < t1; tg += CONV_G) {
+    float xn[CONV_G];  // the group's inputs, loaded before any of its tokens runs
 #pragma unroll
-    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], win[k], acc);
-    stv(u, abf, (b * L + t) * E + e, silu_f(acc));
+    for (int j = 0; j < CONV_G; ++j) xn[j] = tg + j < t1 ? ldv(xi, abf, (b * L + tg + j) * ld_x + e) : 0.f;
 #pragma unroll
-    for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
+    for (int j = 0; j < CONV_G; ++j) {
+      if (tg + j < t1) {
+        win[K - 1] = xn[j];
+        float acc = be;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(wk[k], win[k], acc);
+        stv(u, abf, (b * L + tg + j) * E + e, silu_f(acc));
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
+      }
+    }
   }
 }
 
@@ -764,27 +772,39 @@ __global__ void conv_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, const
 #pragma unroll
   for (int k = 0; k < K; ++k) gw[k] = 0.f;
   float gb = 0.f;
-  for (int64_t t = t0; t < t1; ++t) {
-    xs[2 * K - 2] = xin(t + K - 1);
-    {
-      const int64_t tt = t + K - 1;
-      float acc = be;
+  // tokens in groups of CONV_G: the group's inputs are loaded first (2 CONV_G loads in flight per
+  // thread), then its tokens run from registers
+  for (int64_t tg = t0; tg < t1; tg += CONV_G) {
+    float xn[CONV_G], dn[CONV_G];
 #pragma unroll
-      for (int k = 0; k < K; ++k) acc = fmaf(wk[k], xs[K - 1 + k], acc);
-      fwin[K - 1] = tt < L ? du[(b * L + tt) * E + e] * silu_prime_f(acc) : 0.f;
+    for (int j = 0; j < CONV_G; ++j) {
+      const int64_t tt = tg + j + K - 1;
+      xn[j] = tt < L ? ldv(xi, abf, (b * L + tt) * ld_x + e) : 0.f;
+      dn[j] = tt < L ? du[(b * L + tt) * E + e] : 0.f;
     }
-    float acc = 0.f;
 #pragma unroll
-    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], fwin[K - 1 - k], acc);
-    stv(dxi, abf, (b * L + t) * ld_dx + e, acc);
-    const float g0 = fwin[0];
-    gb += g0;
+    for (int j = 0; j < CONV_G; ++j) {
+      const int64_t t = tg + j;
+      if (t < t1) {
+        xs[2 * K - 2] = xn[j];
+        float pre = be;
 #pragma unroll
-    for (int k = 0; k < K; ++k) gw[k] = fmaf(g0, xs[k], gw[k]);
+        for (int k = 0; k < K; ++k) pre = fmaf(wk[k], xs[K - 1 + k], pre);
+        fwin[K - 1] = dn[j] * silu_prime_f(pre);  // zero past L (dn = 0 there)
+        float acc = 0.f;
 #pragma unroll
-    for (int j = 0; j < K - 1; ++j) fwin[j] = fwin[j + 1];
+        for (int k = 0; k < K; ++k) acc = fmaf(wk[k], fwin[K - 1 - k], acc);
+        stv(dxi, abf, (b * L + t) * ld_dx + e, acc);
+        const float g0 = fwin[0];
+        gb += g0;
 #pragma unroll
-    for (int j = 0; j < 2 * K - 2; ++j) xs[j] = xs[j + 1];
+        for (int k = 0; k < K; ++k) gw[k] = fmaf(g0, xs[k], gw[k]);
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i) fwin[i] = fwin[i + 1];
+#pragma unroll
+        for (int i = 0; i < 2 * K - 2; ++i) xs[i] = xs[i + 1];
+      }
+    }
   }
   const int64_t nb = (L + CONV_T - 1) / CONV_T;
   float* row = part + (b * nb + tb) * (E * (K + 1));
