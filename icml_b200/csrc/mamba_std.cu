@@ -294,47 +294,6 @@ __global__ void __launch_bounds__(THREADS) out_fwd_kernel(const Args a) {
 // ---------------------------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
-  __shared__ Stage stg[2];
-  const Lane l = lane_of(a);
-  const AConst K = load_A(a, l);
-  float2 A2p[NP], dlt[NP] = {f2(0.f), f2(0.f)}, anext[NP] = {f2(1.f), f2(1.f)};
-  a2_pairs(K, A2p);
-  float sdt2 = 0.f, dt_first = 0.f;
-  const int nsub = int((l.e - l.s + ST - 1) / ST);
-  Pref r;
-  pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
-  pref_store(r, l, true, stg[(nsub - 1) & 1]);
-  __syncthreads();
-  for (int k = nsub - 1; k >= 0; --k) {
-    if (k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
-    const Stage& S = stg[k & 1];
-#pragma unroll
-    for (int i = ST - 1; i >= 0; --i) {
-      const int64_t t = l.s + int64_t(k) * ST + i;
-      if (t < l.e) {
-        const float dt = S.dt[i][l.dl];
-        const float2 dy = f2(S.zs[i][l.dl]), dt2 = f2(dt);
-        const float4 Cq = S.C[i][l.nq];
-        dlt[0] = fma2(anext[0], dlt[0], mul2(dy, lo2(Cq)));
-        dlt[1] = fma2(anext[1], dlt[1], mul2(dy, hi2(Cq)));
-        anext[0] = ex2_2(mul2(dt2, A2p[0]));
-        anext[1] = ex2_2(mul2(dt2, A2p[1]));
-        if (t > l.s) sdt2 += dt;
-        dt_first = dt;
-      }
-    }
-    if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
-    __syncthreads();
-  }
-  if (!l.ch) return;
-  const int64_t cb = l.b * a.nC + l.c;
-  st_pairs(a.dloc + (cb * a.E + l.d) * NST + l.nq * NS, dlt);
-  if (l.nq == 0) {
-    a.sdt2[cb * a.E + l.d] = sdt2;
-    a.dt0[cb * a.E + l.d] = dt_first;
-  }
-}
 
 // Adjoint carries X entering each chunk from the right (zero final carry), segmented over warps.
 __global__ void __launch_bounds__(32 * CSEG) compose_bwd_kernel(const Args a) {
@@ -472,6 +431,127 @@ __device__ __forceinline__ void raw_store(const Args& a, const Raw& R, const Lan
   if (t < ST) {
     float* dst = j < NST ? reinterpret_cast<float*>(&st.B[t][0]) + j : reinterpret_cast<float*>(&st.C[t][0]) + (j - NST);
     *dst = R.bc[t][j];
+  }
+}
+
+// The adjoint-only inputs of a sub-chunk (dt_raw, [B | C], z and g; not u or the start states).
+__device__ __forceinline__ void raw_issue_adj(const Args& a, const Lane& l, int k, Raw& R) {
+  const int es = a.abf ? 2 : 4;
+  const int pu = DC * es / 16;
+  const int n_dt = ST * 16, n_bc = ST * 8, n_act = 2 * ST * pu;
+  const int total = n_dt + n_bc + n_act;
+  const int64_t t0 = l.s + int64_t(k) * ST, c0 = int64_t(l.grp) * DC;
+  for (int pc = l.tid; pc < total; pc += THREADS) {
+    int q = pc;
+    if (q < n_dt) {
+      const int t = q >> 4, c = (q & 15) * 4;
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e && c0 + c < a.E;
+      cp16(&R.dtr[t][c], v ? a.dt + (l.b * a.L + tok) * a.ld_dt + c0 + c : a.dt, v);
+      continue;
+    }
+    q -= n_dt;
+    if (q < n_bc) {
+      const int t = q >> 3, c = (q & 7) * 4;
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e;
+      cp16(&R.bc[t][c], v ? a.bc + (l.b * a.L + tok) * a.ld_bc + c : a.bc, v);
+      continue;
+    }
+    q -= n_bc;
+    {
+      const bool isg = q >= ST * pu;
+      if (isg) q -= ST * pu;
+      const int t = q / pu, c = (q % pu) * (16 / es);
+      const int64_t tok = t0 + t;
+      const bool v = tok < l.e && c0 + c < a.E;
+      const char* base = static_cast<const char*>(isg ? a.g : a.zg);
+      const int64_t ld = isg ? a.E : a.ld_z;
+      float* dst = isg ? &R.g[t][0] : &R.z[t][0];
+      cp16(reinterpret_cast<char*>(dst) + c * es, v ? base + ((l.b * a.L + tok) * ld + c0 + c) * es : base, v);
+    }
+  }
+  cp_commit();
+}
+
+// The adjoint pass's stage of a sub-chunk: delta, dy = g SiLU(z) and C.
+__device__ __forceinline__ void raw_store_adj(const Args& a, const Raw& R, const Lane& l, Stage& st) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int idx = l.tid + q * THREADS;
+    const int t = idx / DC, dl = idx % DC;
+    const float zz = a.abf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.z[t][0])[dl]) : R.z[t][dl];
+    const float gg = a.abf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&R.g[t][0])[dl]) : R.g[t][dl];
+    st.dt[t][dl] = softplus_fast(R.dtr[t][dl]);
+    st.zs[t][dl] = gg * silu_f(zz);
+  }
+  const int t = l.tid >> 5, j = l.tid & 31;
+  if (t < ST && j >= NST) reinterpret_cast<float*>(&st.C[t][0])[j - NST] = R.bc[t][j];
+}
+
+// Reverse chunk summaries of the adjoint from a zero carry.  ASYNC: inputs staged by cp.async into
+// two Raw buffers in dynamic shared memory, three sub-chunks ahead of their use, one barrier per
+// sub-chunk; otherwise through registers one sub-chunk ahead.
+template <bool ASYNC>
+__global__ void __launch_bounds__(THREADS) chunk_bwd_kernel(const Args a) {
+  extern __shared__ __align__(16) float smr[];
+  __shared__ Stage stg[2];
+  Raw* raw = reinterpret_cast<Raw*>(smr);
+  const Lane l = lane_of(a);
+  const AConst K = load_A(a, l);
+  float2 A2p[NP], dlt[NP] = {f2(0.f), f2(0.f)}, anext[NP] = {f2(1.f), f2(1.f)};
+  a2_pairs(K, A2p);
+  float sdt2 = 0.f, dt_first = 0.f;
+  const int nsub = int((l.e - l.s + ST - 1) / ST);
+  Pref r;
+  if (ASYNC) {
+    raw_issue_adj(a, l, nsub - 1, raw[(nsub - 1) & 1]);
+    if (nsub > 1) raw_issue_adj(a, l, nsub - 2, raw[(nsub - 2) & 1]);
+    cp_wait_all();
+    __syncthreads();
+    raw_store_adj(a, raw[(nsub - 1) & 1], l, stg[(nsub - 1) & 1]);
+    __syncthreads();
+    if (nsub > 2) raw_issue_adj(a, l, nsub - 3, raw[(nsub - 3) & 1]);
+  } else {
+    pref_load(a, l, l.s + int64_t(nsub - 1) * ST, true, r);
+    pref_store(r, l, true, stg[(nsub - 1) & 1]);
+    __syncthreads();
+  }
+  for (int k = nsub - 1; k >= 0; --k) {
+    if (!ASYNC && k > 0) pref_load(a, l, l.s + int64_t(k - 1) * ST, true, r);
+    const Stage& S = stg[k & 1];
+#pragma unroll
+    for (int i = ST - 1; i >= 0; --i) {
+      const int64_t t = l.s + int64_t(k) * ST + i;
+      if (t < l.e) {
+        const float dt = S.dt[i][l.dl];
+        const float2 dy = f2(S.zs[i][l.dl]), dt2 = f2(dt);
+        const float4 Cq = S.C[i][l.nq];
+        dlt[0] = fma2(anext[0], dlt[0], mul2(dy, lo2(Cq)));
+        dlt[1] = fma2(anext[1], dlt[1], mul2(dy, hi2(Cq)));
+        anext[0] = ex2_2(mul2(dt2, A2p[0]));
+        anext[1] = ex2_2(mul2(dt2, A2p[1]));
+        if (t > l.s) sdt2 += dt;
+        dt_first = dt;
+      }
+    }
+    if (ASYNC) {
+      // stage k-1 from its raw inputs (landed by the previous barrier); raw k-2 lands by this one
+      if (k > 0) raw_store_adj(a, raw[(k - 1) & 1], l, stg[(k - 1) & 1]);
+      cp_wait_all();
+      __syncthreads();
+      if (k > 2) raw_issue_adj(a, l, k - 3, raw[(k - 3) & 1]);
+    } else {
+      if (k > 0) pref_store(r, l, true, stg[(k - 1) & 1]);
+      __syncthreads();
+    }
+  }
+  if (!l.ch) return;
+  const int64_t cb = l.b * a.nC + l.c;
+  st_pairs(a.dloc + (cb * a.E + l.d) * NST + l.nq * NS, dlt);
+  if (l.nq == 0) {
+    a.sdt2[cb * a.E + l.d] = sdt2;
+    a.dt0[cb * a.E + l.d] = dt_first;
   }
 }
 
@@ -1345,7 +1425,15 @@ static int mixer_bwd_impl(const void* x, const void* g_out, const Params& P, flo
   a.ckpt_write = 0;
   dim3 grid(unsigned(p.nC), unsigned(p.Bsz), unsigned(p.G));
   if (stage != MSTAGE_FINISH) {
-    mstd::chunk_bwd_kernel<<<grid, mstd::THREADS, 0, s>>>(a);
+    const bool async_c = E % 8 == 0 && a.ld_dt % 8 == 0 && a.ld_bc % 8 == 0 && a.ld_z % 8 == 0 &&
+                         aligned(a.dt, 16) && aligned(a.bc, 16) && aligned(a.zg, 16) && aligned(a.g, 16);
+    if (async_c) {
+      static int lim_c = 0;
+      PGF_CUDA(ensure_dynamic_smem(mstd::chunk_bwd_kernel<true>, 2 * sizeof(mstd::Raw), lim_c));
+      mstd::chunk_bwd_kernel<true><<<grid, mstd::THREADS, 2 * sizeof(mstd::Raw), s>>>(a);
+    } else {
+      mstd::chunk_bwd_kernel<false><<<grid, mstd::THREADS, 0, s>>>(a);
+    }
     PGF_LAUNCH_CHECK();
   }
   const int64_t nth = p.Bsz * E * mstd::NST;
