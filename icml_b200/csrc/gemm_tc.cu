@@ -47,10 +47,12 @@ constexpr int TILE_A_BYTES = TC_BM * TC_BK * 2;
 // they leave room for one 4 KB epilogue staging buffer per warp instead of two (measured: the fourth
 // stage, which hides more of the operand fetch latency, is worth more than the second buffer).
 // Every epilogue warp has at least 4 KB (the transpose path uses the first 32 x 33 floats).
-template <int BN>
+// PAIR: a cluster of two CTAs computes a 256-row tile with tcgen05.mma.cta_group::2; each CTA holds
+// its 128 rows of A and half of the tile's B columns, so a stage is 32 KB and six fit.
+template <int BN, bool PAIR = false>
 struct TcCfg {
-  static constexpr int TILE_B = BN * TC_BK * 2;
-  static constexpr int STAGES = 4;
+  static constexpr int TILE_B = (PAIR ? BN / 2 : BN) * TC_BK * 2;
+  static constexpr int STAGES = PAIR ? 6 : 4;
   static constexpr int STAGE = TILE_A_BYTES + TILE_B;
   static constexpr int NBUF = BN == 256 ? 1 : 2;      // epilogue staging buffers per warp
   static constexpr int EPI_WARP = NBUF * 4096;
@@ -125,13 +127,21 @@ struct TcParams {
   float* tgt_logit;        // (M,)  CE_FWD
 };
 
-template <int BN, int EK>
+template <int BN, int EK, bool PAIR = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmZ,
                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, const TcParams p) {
-  using C = TcCfg<BN>;
+  using C = TcCfg<BN, PAIR>;
   static_assert(EK != EK_DUAL || BN == 128, "the dual product runs 128-column tiles");
+  static_assert(!PAIR || (BN == 256 && (EK == EK_PLAIN || EK == EK_ACT || EK == EK_DACT)),
+                "CTA pairs run 256-column generic products");
+  // PAIR: rank 0 of the pair (the leader) holds the stage barriers and issues the MMAs
+  const uint32_t crank = PAIR ? cluster_rank() : 0u;
+  const int64_t u_first = PAIR ? int64_t(blockIdx.x >> 1) : int64_t(blockIdx.x);
+  const int64_t u_step = PAIR ? int64_t(gridDim.x >> 1) : int64_t(gridDim.x);
+  constexpr int BMU = PAIR ? 2 * TC_BM : TC_BM;        // rows of one work unit
+  const int64_t row_off = int64_t(crank) * TC_BM;      // this CTA's rows within the unit
   constexpr int NPROD = EK == EK_DUAL ? 2 : 1;        // products per output tile
   constexpr uint32_t ABUF = uint32_t(NPROD * BN);     // TMEM columns of one accumulator set
   constexpr uint32_t NCOL = 2 * ABUF;                 // two sets: the MMA fills one while the epilogue drains the other
@@ -158,7 +168,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);
+      mbar_init(&tempty[b], PAIR ? 16 : 8);  // the epilogue warps of both CTAs arrive on the leader's
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
@@ -168,10 +178,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB2)) : "memory");
     }
   }
+  if (PAIR) cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(tslot)), "r"(NCOL));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                   ::"r"(smem_u32(tslot)), "r"(NCOL));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                   ::"r"(smem_u32(tslot)), "r"(NCOL));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -183,11 +200,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const bool leader = elect_one();
     uint32_t it = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+    for (int64_t u = u_first; u < p.units && ok; u += u_step) {
       const int ks = int(u / p.tiles), ut = int(u % p.tiles);
       const int mb = ut / p.n_groups, ng = ut % p.n_groups;
       const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
-      const int m0 = mb * TC_BM;
+      const int m0 = int(int64_t(mb) * BMU + row_off);
       const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
       for (int nt = nt0; nt < nt1 && ok; ++nt) {
         const int n0 = nt * BN;
@@ -199,7 +216,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           for (int kb = kbs; kb < kbe; ++kb, ++it) {
             const int s = int(it % C::STAGES), r = int(it / C::STAGES);
             if (r > 0 && !mbar_wait_warp(&empty[s], uint32_t((r - 1) & 1))) { ok = false; break; }
-            if (leader) {
+            if (PAIR) {
+              // both CTAs' copies complete on the leader's barrier; the leader expects both
+              if (leader) {
+                if (crank == 0) mbar_expect_tx(&full[s], 2 * C::STAGE);
+                const uint32_t fb = cluster_addr(&full[s], 0);
+                uint8_t* sa = tiles + s * C::STAGE;
+                uint8_t* sb = sa + TILE_A_BYTES;
+                const int k0 = kb * TC_BK;
+                const int nb0 = n0 + int(crank) * (BN / 2);
+                if (!amn) {
+                  tma_load_2d_pair(sa, mA, fb, k0, m0);
+                } else {
+                  tma_load_2d_pair(sa, mA, fb, m0, k0);
+                  tma_load_2d_pair(sa + TILE_A_BYTES / 2, mA, fb, m0 + 64, k0);
+                }
+                if (!bmn) {
+                  tma_load_2d_pair(sb, mB, fb, k0, nb0);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < BN / 128; ++i) tma_load_2d_pair(sb + i * 8192, mB, fb, nb0 + 64 * i, k0);
+                }
+              }
+            } else if (leader) {
               mbar_expect_tx(&full[s], C::STAGE);
               uint8_t* sa = tiles + s * C::STAGE;
               uint8_t* sb = sa + TILE_A_BYTES;
@@ -222,15 +261,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 && (!PAIR || crank == 0)) {
     // ---- MMA issuer: the whole warp runs the loop and waits (descriptors stay warp-uniform), one
-    //      elected lane issues every tcgen05.mma and tcgen05.commit (commits track that lane's MMAs)
+    //      elected lane issues every tcgen05.mma and tcgen05.commit (commits track that lane's MMAs).
+    //      PAIR: the leader's warp issues the pair's MMAs (M = 256) and signals both CTAs' barriers.
     const bool leader = elect_one();
     const uint32_t idesc_base = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
-                                (uint32_t(TC_BM >> 4) << 24);
+                                (uint32_t(BMU >> 4) << 24);
+    // commit: this CTA's barrier, and in a pair the peer's too
+    auto commit = [&](uint64_t* bar) {
+      if (PAIR) {
+        umma_commit_pair(cluster_addr(bar, 0));
+        umma_commit_pair(cluster_addr(bar, 1));
+      } else {
+        umma_commit(bar);
+      }
+    };
     uint32_t it = 0, tt = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+    for (int64_t u = u_first; u < p.units && ok; u += u_step) {
       const int ks = int(u / p.tiles), ng = int(u % p.tiles) % p.n_groups;
       const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
       const int kb0 = ks * p.kper, kb1 = min(nk, kb0 + p.kper);
@@ -257,34 +306,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                       : sdesc(a_base + kk * 32, 16, 1024);
               const uint64_t bd = bmn ? sdesc(b_base + kk * 2048, 8192, 1024)
                                       : sdesc(b_base + kk * 32, 16, 1024);
-              if (leader) umma_bf16(dcol, ad, bd, idesc, (kb != kbs) || (kk != 0));
+              if (leader) {
+                if (PAIR) umma_bf16_pair(dcol, ad, bd, idesc, (kb != kbs) || (kk != 0));
+                else umma_bf16(dcol, ad, bd, idesc, (kb != kbs) || (kk != 0));
+              }
             }
-            if (leader) umma_commit(&empty[s]);
+            if (leader) commit(&empty[s]);
             __syncwarp();
           }
         }
         if (!ok) break;
-        if (leader) umma_commit(&tfull[buf]);
+        if (leader) commit(&tfull[buf]);
         __syncwarp();
       }
     }
-  } else {
+  } else if (warp >= 2) {
     // ---- epilogue warps 2..9: TMEM lane quarter q = warp % 4 (rows 32q..32q+31), column half
     //      hf = (warp - 2) / 4 (columns 64hf..64hf+63 of the 128-column tile)
     const int q = warp & 3;
     const int hf = (warp - 2) >> 2;
+    // the accumulator buffer is drained: tell the MMA warp (the leader's, in a pair)
+    auto release_acc = [&](uint32_t b) {
+      if (PAIR) mbar_arrive_cluster(cluster_addr(&tempty[b], 0));
+      else mbar_arrive(&tempty[b]);
+    };
     uint8_t* stg = reinterpret_cast<uint8_t*>(epi_buf) + (warp - 2) * C::EPI_WARP;
     float* tb = reinterpret_cast<float*>(stg);
     uint32_t sq = 0;  // staging buffers taken by this warp
     uint32_t tt = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+    for (int64_t u = u_first; u < p.units && ok; u += u_step) {
       const int ks = int(u / p.tiles), ut = int(u % p.tiles);
       const int mb = ut / p.n_groups, ng = ut % p.n_groups;
       const int nt0 = ng * p.ng, nt1 = min(nt0 + p.ng, n_tiles);
       // a K slice stores its plain float32 partial product; the reduction applies the epilogue
       void* Dst = p.ksplit > 1 ? static_cast<void*>(static_cast<float*>(p.D) + ks * p.split_stride) : p.D;
-      const int64_t row = int64_t(mb) * TC_BM + q * 32 + lane;  // this thread's row (CE modes)
+      const int64_t row = (int64_t(mb) * BMU + row_off) + q * 32 + lane;  // this thread's row (CE modes)
       const bool row_ok = row < p.M;
       float run_m = -INFINITY, run_s = 0.f;
       int64_t tgt = -1;
@@ -318,7 +375,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (EK == EK_DUAL) {
           // ---- two accumulators per tile: z (columns 0..127 of the set) and d (128..255); this
           //      thread owns row `row` and the warp's 64 columns nh .. nh+63 of both
-          const int64_t row0 = int64_t(mb) * TC_BM + q * 32;
+          const int64_t row0 = (int64_t(mb) * BMU + row_off) + q * 32;
           const bool box_live = row0 < p.M;
           const int64_t nh = n0 + hf * 64;
           const uint32_t tq = tmem + buf * ABUF + (uint32_t(q * 32) << 16) + uint32_t(hf * 64);
@@ -332,7 +389,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (c == 1) {
               asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
               __syncwarp();
-              if (lane == 0) mbar_arrive(&tempty[buf]);
+              if (lane == 0) release_acc(buf);
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -366,7 +423,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (EK != EK_CE_FWD && p.fast) {
           // ---- row-per-thread epilogue: this thread owns row `row` and the warp's BN/2 columns,
           //      taken 64 at a time (nh .. nh+63)
-          const int64_t row0 = int64_t(mb) * TC_BM + q * 32;
+          const int64_t row0 = (int64_t(mb) * BMU + row_off) + q * 32;
           const bool box_live = row0 < p.M;  // rows of this quarter exist (TMA clips the rest)
 #pragma unroll 1
           for (int g64 = 0; g64 < BN / 128; ++g64) {
@@ -381,7 +438,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               // both chunks are in registers: hand the accumulator back to the MMA warp
               asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
               __syncwarp();
-              if (lane == 0) mbar_arrive(&tempty[buf]);
+              if (lane == 0) release_acc(buf);
             }
             const int64_t nb = nh + c * 32;
             float v[32];
@@ -558,7 +615,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           __syncwarp();
           const int64_t n = nc + lane;
           const bool n_ok = n < p.N;
-          const int64_t mbase = int64_t(mb) * TC_BM + q * 32;
+          const int64_t mbase = (int64_t(mb) * BMU + row_off) + q * 32;
           if (MODE == TC_GENERIC) {
             const float bias_n = (p.epi.bias && n_ok) ? p.epi.bias[n] : 0.f;
 #pragma unroll 8
@@ -578,7 +635,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
+        if (lane == 0) release_acc(buf);
       }
       if (MODE == TC_CE_FWD && row_ok && ok) {
         p.part_m[row * (2 * p.n_groups) + 2 * ng + hf] = run_m;
@@ -589,9 +646,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (p.fast && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 0) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NCOL));
+  if (PAIR) {
+    // neither CTA leaves (or frees its tensor memory) while the other may still signal its barriers
+    // or the pair's MMAs may still write it
+    cluster_sync();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NCOL));
+  } else {
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NCOL));
   }
 }
 
@@ -671,6 +733,38 @@ static int launch_tc_kernel(unsigned grid, cudaStream_t s, const CUtensorMap& ma
   return PGF_OK;
 }
 
+static bool pair_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PGF_TC_NO_PAIR");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// A 256-column generic product on CTA pairs: `pairs` clusters of two CTAs.
+template <int EK>
+static int launch_tc_pair_kernel(unsigned pairs, cudaStream_t s, const CUtensorMap& ma, const CUtensorMap& mb,
+                                 const CUtensorMap& md, const CUtensorMap& mz, const TcParams& p) {
+  using C = TcCfg<256, true>;
+  static int smem_limit = 0;
+  PGF_CUDA(ensure_dynamic_smem(gemm_tc_kernel<256, EK, true>, C::SMEM, smem_limit));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  PGF_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256, EK, true>, ma, mb, md, mz, ma, mb, p));
+  return PGF_OK;
+}
+
 template <int BN>
 static int launch_tc_bn(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id) {
   using C = TcCfg<BN>;
@@ -715,10 +809,38 @@ static int launch_tc_bn(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id)
   // 256-wide tiles: generic products through the TMA-store epilogue, and the CE forward (no stored
   // output); the transpose epilogue is only used at 128
   if (BN == 256 && ((p.mode == TC_GENERIC && !p.fast) || p.mode == TC_CE_BWD)) return PGF_ERR_UNSUPPORTED;
+  const int ek = ek_of(p);
+  // CTA pairs: 256-column generic products of at least two 128-row blocks and a depth of at least
+  // 512 per unit (at shallower depths the two CTAs' epilogues, which must both drain an accumulator
+  // before it is reused, bound the product and the pair was measured slower: FFN up at K = 256
+  // 74 -> 84 us; at K = 1024 133 -> 119 us, the LM-head weight gradient 121 -> 102 us)
+  if (BN == 256 && p.mode == TC_GENERIC && p.fast && m_blocks >= 2 && !pair_disabled() &&
+      int64_t(p.kper) * TC_BK >= 512 &&
+      (ek == EK_PLAIN || ek == EK_ACT || ek == EK_DACT)) {
+    CUtensorMap mbp;  // a K-major B operand is loaded in halves of BN / 2 rows
+    const bool okp = g.b_trans ? true : make_map(&mbp, g.B, g.K, g.N, g.ldb, 64, BN / 2);
+    if (okp) {
+      if (g.b_trans) mbp = mb;
+      TcParams q = p;
+      q.tiles = ((g.M + 2 * TC_BM - 1) / (2 * TC_BM)) * q.n_groups;
+      q.units = q.tiles * q.ksplit;
+      const int64_t max_pairs = sm_count() / 2;
+      const unsigned pairs = unsigned(q.units < max_pairs ? q.units : max_pairs);
+      prof_begin(prof_id, s);
+      int rc = PGF_OK;
+      if (ek == EK_PLAIN) rc = launch_tc_pair_kernel<EK_PLAIN>(pairs, s, ma, mbp, md, mz, q);
+      else if (ek == EK_ACT) rc = launch_tc_pair_kernel<EK_ACT>(pairs, s, ma, mbp, md, mz, q);
+      else rc = launch_tc_pair_kernel<EK_DACT>(pairs, s, ma, mbp, md, mz, q);
+      PGF_TRY(rc);
+      prof_end(prof_id, s, 2.0 * double(g.M) * double(g.N) * double(g.K));
+      PGF_LAUNCH_CHECK();
+      return PGF_OK;
+    }
+  }
   const unsigned grid = unsigned(p.units < sm_count() ? p.units : sm_count());
   prof_begin(prof_id, s);
   int rc = PGF_OK;
-  switch (ek_of(p)) {
+  switch (ek) {
     case EK_PLAIN: rc = launch_tc_kernel<BN, EK_PLAIN>(grid, s, ma, mb, md, mz, p); break;
     case EK_ACT: rc = launch_tc_kernel<BN, EK_ACT>(grid, s, ma, mb, md, mz, p); break;
     case EK_DACT: rc = launch_tc_kernel<BN, EK_DACT>(grid, s, ma, mb, md, mz, p); break;

@@ -31,8 +31,10 @@ def _tc_launches(fn):
 
 @pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 512), (200, 72, 40), (1000, 304, 1024),
-                                   (64, 1000, 8), (4096, 1024, 256)])
+                                   (64, 1000, 8), (4096, 1024, 256), (1000, 512, 320), (136, 768, 192)])
 def test_tc_gemm_layouts(ops, at, bt, M, N, K):
+    """256-column outputs of two or more 128-row blocks run on CTA pairs (one 256-row MMA per pair);
+    ragged last blocks included."""
     g = torch.Generator().manual_seed(M + N + K + 7 * at + 3 * bt)
     A = (torch.randn(K, M, generator=g) if at else torch.randn(M, K, generator=g)).bfloat16()
     B = (torch.randn(K, N, generator=g) if bt else torch.randn(N, K, generator=g)).bfloat16()
