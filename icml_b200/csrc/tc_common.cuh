@@ -112,7 +112,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 // 2-D tile load into this CTA's shared memory whose completion is counted on a barrier of either
-// CTA of the pair (`cluster_bar`, a shared::cluster address).  No multicast.
+// CTA of the pair (`cluster_bar`, a shared::cluster address); the data lands in this CTA only.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t cluster_bar, int c0,
                                                  int c1) {
   asm volatile(
