@@ -236,11 +236,11 @@ def run_reference(a, rank, world):
 
 # ----------------------------------------------------------------------------- GPU arm
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant kernels, from
-# ncu captures of one launch each on the 65536-token segment every launch of the default workload
-# covers (8-layer reference variant, d 256, d_ff 1024, vocab 50257, bf16; the scan kernels from
-# `bench.py --component scan`, the others from the 65536-token step).  Reported as `traffic` only
-# for that workload.
-TRAFFIC_DEFAULT = {"gemm_tc": 194818014, "ssm_main_bwd": 496966144, "ce": 1316616857, "ssm_chunk_fwd": 288500000,
+# ncu captures on the 65536-token segment every launch of the default workload covers (8-layer
+# reference variant, d 256, d_ff 1024, vocab 50257, bf16): the scan kernels one launch each from
+# `bench.py --component scan`; gemm_tc and ce the mean over one step's launches of the group, the
+# others one launch each, from the 65536-token step.  Reported as `traffic` only for that workload.
+TRAFFIC_DEFAULT = {"gemm_tc": 194297962, "ssm_main_bwd": 496966144, "ce": 1316357018, "ssm_chunk_fwd": 288500000,
                    "ssm_out_fwd": 230101748, "ssm_chunk_bwd": 114800000, "ssm_compose": 8940480,
                    "rmsnorm_fwd": 58914490, "rmsnorm_bwd": 110329568, "adamw": 395415392}
 # Warp instructions per launch of the scan backward on that segment (smsp__inst_executed.sum, same
