@@ -928,16 +928,158 @@ __global__ void conv_halo_bwd_kernel(const void* __restrict__ xi, int64_t ld_x, 
   }
 }
 
+// bf16 activations, two channels per thread (4-byte loads and stores of channel pairs): the same
+// arithmetic as conv_fwd_kernel / conv_bwd_kernel on float2 pairs.  Needs E, ld_x, ld_dx even.
+__device__ __forceinline__ float2 ld2_bf(const void* base, int64_t i) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(base) + i));
+}
+__device__ __forceinline__ void st2_bf(void* base, int64_t i, float2 v) {
+  *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(base) + i) = __floats2bfloat162_rn(v.x, v.y);
+}
+__device__ __forceinline__ float2 xi2_at(const void* xi, int64_t ld_x, const void* halo, int64_t b, int64_t L,
+                                         int64_t E, int K, int64_t tt, int64_t e) {
+  if (tt >= 0) return tt < L ? ld2_bf(xi, (b * L + tt) * ld_x + e) : f2(0.f);
+  return halo ? ld2_bf(halo, (b * (K - 1) + (K - 1) + tt) * E + e) : f2(0.f);
+}
+
+template <int K>
+__global__ void conv_fwd2_kernel(const void* __restrict__ xi, int64_t ld_x, const void* __restrict__ halo,
+                                 const float* __restrict__ w, const float* __restrict__ bias, void* __restrict__ u,
+                                 int64_t Bsz, int64_t L, int64_t E) {
+  const int64_t e = 2 * (int64_t(blockIdx.x) * blockDim.x + threadIdx.x);
+  const int64_t b = blockIdx.z;
+  const int64_t t0 = int64_t(blockIdx.y) * CONV_T;
+  if (e >= E) return;
+  float2 wk[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) wk[k] = f2(w[e * K + k], w[(e + 1) * K + k]);
+  const float2 be = f2(bias[e], bias[e + 1]);
+  float2 win[K];
+#pragma unroll
+  for (int k = 0; k < K - 1; ++k) win[k] = xi2_at(xi, ld_x, halo, b, L, E, K, t0 - (K - 1) + k, e);
+  const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
+  for (int64_t tg = t0; tg < t1; tg += CONV_G) {
+    float2 xn[CONV_G];
+#pragma unroll
+    for (int j = 0; j < CONV_G; ++j) xn[j] = tg + j < t1 ? ld2_bf(xi, (b * L + tg + j) * ld_x + e) : f2(0.f);
+#pragma unroll
+    for (int j = 0; j < CONV_G; ++j) {
+      if (tg + j < t1) {
+        win[K - 1] = xn[j];
+        float2 acc = be;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fma2(wk[k], win[k], acc);
+        st2_bf(u, (b * L + tg + j) * E + e, f2(silu_f(acc.x), silu_f(acc.y)));
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
+      }
+    }
+  }
+}
+
+template <int K>
+__global__ void conv_bwd2_kernel(const void* __restrict__ xi, int64_t ld_x, const void* __restrict__ halo,
+                                 const float* __restrict__ w, const float* __restrict__ bias,
+                                 const float* __restrict__ du, void* __restrict__ dxi, int64_t ld_dx,
+                                 float* __restrict__ part, int64_t Bsz, int64_t L, int64_t E) {
+  constexpr int G = CONV_G / 2;  // tokens whose inputs a thread loads together (two channels each)
+  const int64_t e = 2 * (int64_t(blockIdx.x) * blockDim.x + threadIdx.x);
+  const int64_t b = blockIdx.z;
+  const int64_t tb = blockIdx.y;
+  const int64_t t0 = tb * CONV_T;
+  if (e >= E) return;
+  float2 wk[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) wk[k] = f2(w[e * K + k], w[(e + 1) * K + k]);
+  const float2 be = f2(bias[e], bias[e + 1]);
+  const int64_t t1 = t0 + CONV_T < L ? t0 + CONV_T : L;
+  float2 xs[2 * K - 1];
+#pragma unroll
+  for (int j = 0; j < 2 * K - 2; ++j) xs[j] = xi2_at(xi, ld_x, halo, b, L, E, K, t0 - (K - 1) + j, e);
+  float2 fwin[K];
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) {
+    const int64_t tt = t0 + j;
+    float2 pre = be;
+#pragma unroll
+    for (int k = 0; k < K; ++k) pre = fma2(wk[k], xs[j + k], pre);
+    const float2 d = tt < L ? *reinterpret_cast<const float2*>(du + (b * L + tt) * E + e) : f2(0.f);
+    fwin[j] = f2(d.x * silu_prime_f(pre.x), d.y * silu_prime_f(pre.y));
+  }
+  float2 gw[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) gw[k] = f2(0.f);
+  float2 gb = f2(0.f);
+  for (int64_t tg = t0; tg < t1; tg += G) {
+    float2 xn[G], dn[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int64_t tt = tg + j + K - 1;
+      xn[j] = tt < L ? ld2_bf(xi, (b * L + tt) * ld_x + e) : f2(0.f);
+      dn[j] = tt < L ? *reinterpret_cast<const float2*>(du + (b * L + tt) * E + e) : f2(0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int64_t t = tg + j;
+      if (t < t1) {
+        xs[2 * K - 2] = xn[j];
+        float2 pre = be;
+#pragma unroll
+        for (int k = 0; k < K; ++k) pre = fma2(wk[k], xs[K - 1 + k], pre);
+        fwin[K - 1] = f2(dn[j].x * silu_prime_f(pre.x), dn[j].y * silu_prime_f(pre.y));  // zero past L
+        float2 acc = f2(0.f);
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fma2(wk[k], fwin[K - 1 - k], acc);
+        st2_bf(dxi, (b * L + t) * ld_dx + e, acc);
+        const float2 g0 = fwin[0];
+        gb = add2(gb, g0);
+#pragma unroll
+        for (int k = 0; k < K; ++k) gw[k] = fma2(g0, xs[k], gw[k]);
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i) fwin[i] = fwin[i + 1];
+#pragma unroll
+        for (int i = 0; i < 2 * K - 2; ++i) xs[i] = xs[i + 1];
+      }
+    }
+  }
+  const int64_t nb = (L + CONV_T - 1) / CONV_T;
+  float* row = part + (b * nb + tb) * (E * (K + 1));
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    row[e * K + k] = gw[k].x;
+    row[(e + 1) * K + k] = gw[k].y;
+  }
+  row[E * K + e] = gb.x;
+  row[E * K + e + 1] = gb.y;
+}
+
+// Channel pairs (bf16, even widths and pitches, 4-byte aligned bases) take the two-channel kernels.
+static bool conv_pairs(int abf, int64_t E, int64_t ld_a, int64_t ld_b, const void* p, const void* halo,
+                       const void* q) {
+  return abf && E % 2 == 0 && ld_a % 2 == 0 && ld_b % 2 == 0 && aligned(p, 4) && aligned(q, 4) &&
+         (!halo || aligned(halo, 4));
+}
+
 template <int K>
 static void launch_conv_fwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo, const float* w,
                             const float* bias, void* u, int64_t Bsz, int64_t L, int64_t E, int abf) {
-  conv_fwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, halo, w, bias, u, Bsz, L, E, abf);
+  if (conv_pairs(abf, E, ld_x, E, xi, halo, u)) {
+    const dim3 g2(unsigned(ceil_div(E / 2, 128)), grid.y, grid.z);
+    conv_fwd2_kernel<K><<<g2, 128, 0, s>>>(xi, ld_x, halo, w, bias, u, Bsz, L, E);
+  } else {
+    conv_fwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, halo, w, bias, u, Bsz, L, E, abf);
+  }
 }
 template <int K>
 static void launch_conv_bwd(dim3 grid, cudaStream_t s, const void* xi, int64_t ld_x, const void* halo,
                             const float* w, const float* bias, const float* du, void* dxi, int64_t ld_dx, float* part,
                             int64_t Bsz, int64_t L, int64_t E, int abf, void* dhalo) {
-  conv_bwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf);
+  if (conv_pairs(abf, E, ld_x, ld_dx, xi, halo, dxi) && aligned(du, 8)) {
+    const dim3 g2(unsigned(ceil_div(E / 2, 128)), grid.y, grid.z);
+    conv_bwd2_kernel<K><<<g2, 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dxi, ld_dx, part, Bsz, L, E);
+  } else {
+    conv_bwd_kernel<K><<<grid, 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dxi, ld_dx, part, Bsz, L, E, abf);
+  }
   if (dhalo && K > 1)
     conv_halo_bwd_kernel<K><<<dim3(grid.x, unsigned(Bsz)), 128, 0, s>>>(xi, ld_x, halo, w, bias, du, dhalo, Bsz, L,
                                                                          E, abf);
