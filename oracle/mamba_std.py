@@ -13,9 +13,11 @@ Linear-Time Sequence Modeling with Selective State Spaces", 2023, Algorithm 2 / 
     h_t = exp(delta_t A) * h_{t-1} + delta_t B_t u_t,   A = -exp(A_log)  (per channel, E x N)
     y_t = C_t . h_t + D u_t;  y = y * silu(z);  out = y W_out^T   (no bias)
 
-restated here from that published description in plain PyTorch; parity for this variant is
-pinned only against autograd of this restatement ("parity unpinned" with respect to the
-reference, which has no such code).  The block around it is the reference's PGFMambaBlock
+restated here from that published description in plain PyTorch.  The reference has no such code,
+so the restatement cannot be pinned to it; instead tests/test_oracle_mamba_std.py checks it against
+an independent implementation of the same mixer, the pure-PyTorch path of transformers'
+MambaMixer (`slow_forward`, transformers 5.5.0): outputs and every gradient agree to float32
+rounding (relative 2e-7 to 7e-7) at the single-block configuration.  The block around it is the reference's PGFMambaBlock
 (pgf_mamba_block.py:51-68): x -> RMSNorm -> mixer -> +x -> RMSNorm -> FFN -> +x.
 """
 from __future__ import annotations
