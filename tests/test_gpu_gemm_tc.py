@@ -31,10 +31,11 @@ def _tc_launches(fn):
 
 @pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 512), (200, 72, 40), (1000, 304, 1024),
-                                   (64, 1000, 8), (4096, 1024, 256), (1000, 512, 320), (136, 768, 192)])
+                                   (64, 1000, 8), (4096, 1024, 256), (1000, 512, 640), (136, 768, 192),
+                                   (520, 256, 1024), (4096, 1024, 512)])
 def test_tc_gemm_layouts(ops, at, bt, M, N, K):
-    """256-column outputs of two or more 128-row blocks run on CTA pairs (one 256-row MMA per pair);
-    ragged last blocks included."""
+    """256-column outputs of two or more 128-row blocks and depth >= 512 run on CTA pairs (one
+    256-row MMA per pair, each CTA loading half of B); ragged last blocks included."""
     g = torch.Generator().manual_seed(M + N + K + 7 * at + 3 * bt)
     A = (torch.randn(K, M, generator=g) if at else torch.randn(M, K, generator=g)).bfloat16()
     B = (torch.randn(K, N, generator=g) if bt else torch.randn(N, K, generator=g)).bfloat16()
@@ -44,9 +45,12 @@ def test_tc_gemm_layouts(ops, at, bt, M, N, K):
     assert_close(D, ref, atol=1e-4, rtol=1e-5)
 
 
-def test_tc_gemm_epilogue_and_bf16_out(ops):
+@pytest.mark.parametrize("K", [256, 768])
+def test_tc_gemm_epilogue_and_bf16_out(ops, K):
+    """Bias + GELU with the pre-activation stored, bf16 output, and accumulation into float32; at
+    K = 768 on CTA pairs with a ragged last pair (M = 300) and a ragged column tile (N = 500)."""
     g = torch.Generator().manual_seed(3)
-    M, N, K = 300, 500, 256
+    M, N = 300, 500
     A = torch.randn(M, K, generator=g).bfloat16()
     B = torch.randn(N, K, generator=g).bfloat16()
     bias = torch.randn(N, generator=g)
