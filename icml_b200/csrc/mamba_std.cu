@@ -982,7 +982,7 @@ __global__ void conv_bwd2_kernel(const void* __restrict__ xi, int64_t ld_x, cons
                                  const float* __restrict__ w, const float* __restrict__ bias,
                                  const float* __restrict__ du, void* __restrict__ dxi, int64_t ld_dx,
                                  float* __restrict__ part, int64_t Bsz, int64_t L, int64_t E) {
-  constexpr int G = CONV_G / 2;  // tokens whose inputs a thread loads together (two channels each)
+  constexpr int G = CONV_G;  // tokens whose inputs a thread loads together (two channels each)
   const int64_t e = 2 * (int64_t(blockIdx.x) * blockDim.x + threadIdx.x);
   const int64_t b = blockIdx.z;
   const int64_t tb = blockIdx.y;
