@@ -519,13 +519,17 @@ def run_gpu(a, rank, world, local_rank):
     if a.variant == "reference" and not a.no_std_companion:
         b = argparse.Namespace(**vars(a))
         b.variant = "std"
-        r2 = _measure_model(b, rank, world, local_rank, dev, pg, L)
-        if rank == 0:
-            l2 = _line_of(b, world, r2)
-            line["mamba_standard"] = {k: l2[k] for k in ("metric", "value", "unit", "ms_per_step", "scaling",
-                                                         "config", "peak_hbm_gb", "clocks", "e2e",
-                                                         "gpu_launches", "cuda_graph", "kernels",
-                                                         "dominant_kernel", "roofline")}
+        try:
+            r2 = _measure_model(b, rank, world, local_rank, dev, pg, L)
+            if rank == 0:
+                l2 = _line_of(b, world, r2)
+                line["mamba_standard"] = {k: l2[k] for k in ("metric", "value", "unit", "ms_per_step", "scaling",
+                                                             "config", "peak_hbm_gb", "clocks", "e2e",
+                                                             "gpu_launches", "cuda_graph", "kernels",
+                                                             "dominant_kernel", "roofline")}
+        except Exception as e:  # the headline line is printed whatever happens to the companion
+            if rank == 0:
+                line["mamba_standard"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
