@@ -813,7 +813,8 @@ static int launch_tc_bn(const Gemm& g, TcParams& p, cudaStream_t s, int prof_id)
   // CTA pairs: 256-column generic products of at least two 128-row blocks and a depth of at least
   // 512 per unit (at shallower depths the two CTAs' epilogues, which must both drain an accumulator
   // before it is reused, bound the product and the pair was measured slower: FFN up at K = 256
-  // 74 -> 84 us; at K = 1024 133 -> 119 us, the LM-head weight gradient 121 -> 102 us)
+  // 74 -> 84 us; at K = 1024 133 -> 119 us; the FFN 1024 -> 4096 weight gradients, depth 16384,
+  // 121 -> 102 us)
   if (BN == 256 && p.mode == TC_GENERIC && p.fast && m_blocks >= 2 && !pair_disabled() &&
       int64_t(p.kper) * TC_BK >= 512 &&
       (ek == EK_PLAIN || ek == EK_ACT || ek == EK_DACT)) {
