@@ -217,7 +217,7 @@ rmsnorm_fwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ res, T* __
 }
 
 template <int CPL, class T>
-__global__ void __launch_bounds__(RMS_WARPS * 32)
+__global__ void __launch_bounds__(RMS_WARPS * 32, CPL == 1 ? 3 : 1)  // 1 chunk per lane: 3 CTAs per SM
 rmsnorm_bwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ g, const float* __restrict__ w,
                        const T* __restrict__ gadd, T* __restrict__ gx, float* __restrict__ gw_part, int64_t rows,
                        int dim, float eps) {
@@ -234,6 +234,16 @@ rmsnorm_bwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ g, const f
 #pragma unroll
     for (int e = 0; e < VW; ++e) acc[k][e] = 0.f;
   const int64_t row0 = (int64_t(blockIdx.x) * RMS_WARPS + warp) * RMS_ROWS_PER_WARP;
+  // the weight slice of this lane, once per warp where it fits beside the row group's loads;
+  // at 4 chunks per lane it is re-read (from L1) per row
+  constexpr bool HOIST_W = CPL <= 2;
+  float wh[HOIST_W ? CPL : 1][VW];
+  if (HOIST_W) {
+#pragma unroll
+    for (int k = 0; k < (HOIST_W ? CPL : 1); ++k)
+#pragma unroll
+      for (int e = 0; e < VW; ++e) wh[k][e] = __ldg(w + (k * 32 + lane) * VW + e);
+  }
 #pragma unroll 1
   for (int rb = 0; rb < RMS_ROWS_PER_WARP; rb += RB) {
   uint4 qx[RB][CPL], qg[RB][CPL], qa[RB][CPL];
@@ -247,31 +257,64 @@ rmsnorm_bwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ g, const f
       qg[r][k] = ok ? __ldg(reinterpret_cast<const uint4*>(g + off)) : make_uint4(0, 0, 0, 0);
       qa[r][k] = (ok && gadd) ? __ldg(reinterpret_cast<const uint4*>(gadd + off)) : make_uint4(0, 0, 0, 0);
     }
+  // the group's sums (x.x and (g w).x) first, then their warp reductions side by side (each row's
+  // butterfly in the same order as a lone row's), then the per-row divides and outputs: the rows'
+  // shuffle and divide chains overlap instead of running one after another.  Rows past the end
+  // hold zeros and are reduced too, but write nothing.
+  float ss[RB], dot[RB];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    ss[r] = 0.f;
+    dot[r] = 0.f;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      float xv[VW], gv[VW];
+      V::unpack(qx[r][k], xv);
+      V::unpack(qg[r][k], gv);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        const float wk = HOIST_W ? wh[HOIST_W ? k : 0][e] : __ldg(w + (k * 32 + lane) * VW + e);
+        ss[r] = fmaf(xv[e], xv[e], ss[r]);
+        dot[r] = fmaf(gv[e] * wk, xv[e], dot[r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], o);
+      dot[r] += __shfl_xor_sync(0xffffffffu, dot[r], o);
+    }
+  // with several rows in the group, unpack again below rather than keep the unpacked rows alive
+  // across the reductions (twice the registers of the packed ones): an empty asm makes the packed
+  // words opaque to the compiler
+  if constexpr (RB > 1) {
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+#pragma unroll
+      for (int k = 0; k < CPL; ++k) {
+        asm volatile("" : "+r"(qx[r][k].x), "+r"(qx[r][k].y), "+r"(qx[r][k].z), "+r"(qx[r][k].w));
+        asm volatile("" : "+r"(qg[r][k].x), "+r"(qg[r][k].y), "+r"(qg[r][k].z), "+r"(qg[r][k].w));
+      }
+  }
 #pragma unroll
   for (int r = 0; r < RB; ++r) {
     const int64_t row = row0 + rb + r;
     if (row >= rows) break;
-    float wv[CPL][VW];  // the weight, from L1 (it is the same for every row)
+    float wv[CPL][VW];
 #pragma unroll
     for (int k = 0; k < CPL; ++k)
 #pragma unroll
-      for (int e = 0; e < VW; ++e) wv[k][e] = __ldg(w + (k * 32 + lane) * VW + e);
+      for (int e = 0; e < VW; ++e) wv[k][e] = HOIST_W ? wh[HOIST_W ? k : 0][e] : __ldg(w + (k * 32 + lane) * VW + e);
     float xv[CPL][VW], gv[CPL][VW];
-    float ss = 0.f, dot = 0.f;
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
       V::unpack(qx[r][k], xv[k]);
       V::unpack(qg[r][k], gv[k]);
-#pragma unroll
-      for (int e = 0; e < VW; ++e) {
-        ss = fmaf(xv[k][e], xv[k][e], ss);
-        dot = fmaf(gv[k][e] * wv[k][e], xv[k][e], dot);
-      }
     }
-    ss = warp_sum(ss);
-    dot = warp_sum(dot);
-    const float rinv = 1.0f / sqrtf(ss / float(dim) + eps);
-    const float kx = dot * (rinv * rinv * rinv) / float(dim);  // per row: no divide per element
+    const float rinv = 1.0f / sqrtf(ss[r] / float(dim) + eps);
+    const float kx = dot[r] * (rinv * rinv * rinv) / float(dim);  // per row: no divide per element
     if (gx) {
 #pragma unroll
       for (int k = 0; k < CPL; ++k) {
