@@ -239,10 +239,11 @@ def run_reference(a, rank, world):
 # ncu captures on the 65536-token segment every launch of the default workload covers (8-layer
 # reference variant, d 256, d_ff 1024, vocab 50257, bf16): the scan kernels one launch each from
 # `bench.py --component scan`; gemm_tc and ce the mean over one step's launches of the group, the
-# others one launch each, from the 65536-token step.  Reported as `traffic` only for that workload.
+# RMSNorm kernels the mean of two launches (the forward: one with and one without the residual),
+# the others one launch each, from the 65536-token step.  Reported as `traffic` only for that workload.
 TRAFFIC_DEFAULT = {"gemm_tc": 194297962, "ssm_main_bwd": 496966144, "ce": 1316357018, "ssm_chunk_fwd": 288500000,
                    "ssm_out_fwd": 230101748, "ssm_chunk_bwd": 114800000, "ssm_compose": 8940480,
-                   "rmsnorm_fwd": 58914490, "rmsnorm_bwd": 110329568, "adamw": 395415392}
+                   "rmsnorm_fwd": 60879232, "rmsnorm_bwd": 115444608, "adamw": 395415392}
 # Warp instructions per launch of the scan backward on that segment (smsp__inst_executed.sum, same
 # capture): the kernel is bound by instruction issue, so its compute roofline is issue rate.
 MAIN_BWD_WARP_INSTS = 517951488

@@ -226,8 +226,9 @@ rmsnorm_bwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ g, const f
   extern __shared__ float sm_gw[];  // [RMS_WARPS][dim]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  // rows whose loads are issued together: four 16-byte chunks of each tensor per lane in flight
-  constexpr int RB = CPL >= 4 ? 1 : 4 / CPL;
+  // rows whose loads are issued together: four 16-byte chunks of each tensor per lane in flight,
+  // eight at 4 chunks per lane (two rows: one CTA per SM either way, 222 registers)
+  constexpr int RB = CPL >= 4 ? 2 : 4 / CPL;
   float acc[CPL][VW];
 #pragma unroll
   for (int k = 0; k < CPL; ++k)
