@@ -138,8 +138,7 @@ static int ffn_fwd_impl(const void* x, const float* W1, const float* b1, const f
   const void* w1 = W1;
   const void* w2 = W2;
   if (dtype) {
-    PGF_TRY(to_bf16(W1, f.W1b, d_hidden * d_in, s));
-    PGF_TRY(to_bf16(W2, f.W2b, d_out * d_hidden, s));
+    PGF_TRY(to_bf16_multi(Bf16Casts{{W1, W2}, {f.W1b, f.W2b}, {d_hidden * d_in, d_out * d_hidden}, 2}, s));
     w1 = f.W1b;
     w2 = f.W2b;
   }
@@ -311,8 +310,7 @@ extern "C" int pgf_ffn_bwd(const void* x, const void* g, const float* W1, const 
   const void* w2 = W2;
   int wbf = 0;
   if (dtype) {
-    PGF_TRY(to_bf16(W1, f.W1b, d_h * d_in, s));
-    PGF_TRY(to_bf16(W2, f.W2b, d_out * d_h, s));
+    PGF_TRY(to_bf16_multi(Bf16Casts{{W1, W2}, {f.W1b, f.W2b}, {d_h * d_in, d_out * d_h}, 2}, s));
     w1 = f.W1b;
     w2 = f.W2b;
     wbf = 1;

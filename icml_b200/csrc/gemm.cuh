@@ -99,6 +99,15 @@ int column_reduce(const float* part, int64_t nparts, int64_t N, float* out, int 
 
 // dst[i] = bf16(src[i]) (weights to the tensor-core operand type)
 int to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s);
+// the same for up to MAX tensors in one launch (tensor t: src[t] -> dst[t], n[t] elements)
+struct Bf16Casts {
+  static constexpr int MAX = 4;
+  const float* src[MAX];
+  __nv_bfloat16* dst[MAX];
+  int64_t n[MAX];
+  int count;
+};
+int to_bf16_multi(const Bf16Casts& c, cudaStream_t s);
 
 // GELU / GELU' with the hardware tanh approximation (tanh.approx.f32, relative error ~2^-11): used
 // only where the result is rounded to bf16 (8-bit mantissa) anyway.

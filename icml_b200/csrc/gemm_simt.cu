@@ -366,6 +366,33 @@ int to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t s) {
   return PGF_OK;
 }
 
+// Several tensors in one launch: grid row blockIdx.y converts tensor blockIdx.y (the per-element
+// loop of to_bf16_kernel), so a call's weight copies cost one launch instead of one each.
+__global__ void to_bf16_multi_kernel(Bf16Casts c) {
+  const int t = blockIdx.y;
+  const float* __restrict__ src = c.src[t];
+  __nv_bfloat16* __restrict__ dst = c.dst[t];
+  const int64_t n = c.n[t];
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (; i < n; i += stride) dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+int to_bf16_multi(const Bf16Casts& c, cudaStream_t s) {
+  if (c.count < 1 || c.count > Bf16Casts::MAX) {
+    set_error("to_bf16_multi: %d tensors (1..%d)", c.count, Bf16Casts::MAX);
+    return PGF_ERR_INVALID;
+  }
+  int64_t most = 0;
+  for (int t = 0; t < c.count; ++t) most = c.n[t] > most ? c.n[t] : most;
+  if (most == 0) return PGF_OK;
+  int blocks = ceil_div(most, 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  to_bf16_multi_kernel<<<dim3(unsigned(blocks), unsigned(c.count)), 256, 0, s>>>(c);
+  PGF_LAUNCH_CHECK();
+  return PGF_OK;
+}
+
 }  // namespace pgf
 
 using namespace pgf;

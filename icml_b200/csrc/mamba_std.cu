@@ -1279,10 +1279,11 @@ struct Params {
 static int convert_weights(const Params& P, const Plan& p, Bufs& B, int dtype, cudaStream_t s) {
   if (!dtype) return PGF_OK;
   const int64_t E = p.E;
-  PGF_TRY(to_bf16(P.in_w, B.in_wb, 2 * E * p.d, s));
-  PGF_TRY(to_bf16(P.x_w, B.x_wb, p.XD * E, s));
-  PGF_TRY(to_bf16(P.dt_w, B.dt_wb, E * p.R, s));
-  return to_bf16(P.out_w, B.out_wb, p.d * E, s);
+  return to_bf16_multi(Bf16Casts{{P.in_w, P.x_w, P.dt_w, P.out_w},
+                                  {B.in_wb, B.x_wb, B.dt_wb, B.out_wb},
+                                  {2 * E * p.d, p.XD * E, E * p.R, p.d * E},
+                                  4},
+                       s);
 }
 
 // scan arguments over the forward buffers
