@@ -1,8 +1,8 @@
-"""Mamba-standard variant (BASELINE config 1 shapes) on the GPU against autograd of the float64 oracle.
+"""Mamba-standard variant on the GPU against autograd of the float64 oracle, at the small test
+shapes (B=2, L=512, d_model 128, d_inner 256, d_state 16) and ragged ones.
 
 The reference has no code for this variant, so the truth is autograd of the CPU restatement in
-oracle/mamba_std.py (the comparison config 1 asks for: "every parameter/input gradient of the PGF
-path against plain autograd").
+oracle/mamba_std.py: every parameter and input gradient of the PGF path against plain autograd.
 """
 import pytest
 import torch
