@@ -84,7 +84,7 @@ def test_std_block_bf16_activations():
 
 
 def test_std_lm_step_matches_autograd():
-    """8-layer shape family at small size: tied embedding / LM head and a final RMSNorm (config 3 layout)."""
+    """8-layer shape family at small size: tied embedding / LM head and a final RMSNorm."""
     from icml_b200.lm import PGFLanguageModel
     g = torch.Generator().manual_seed(72)
     V, d, E, R, nl, B, L = 97, 32, 64, 2, 2, 2, 40
