@@ -50,6 +50,26 @@ def test_reference_arm_prints_one_line_with_the_contract_keys():
     assert d["ms_per_step"] > 0
 
 
+def test_reference_arm_under_torchrun_prints_once_from_rank_0():
+    """Launched the way the multi-GPU runs launch both arms: rank 0 times and prints the one line,
+    the other rank exits 0 without work."""
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                          "--master-addr", "127.0.0.1", "--master-port", str(port), "bench.py", "--impl", "reference",
+                          "--gpus", "2", "--steps", "1", "--warmup", "1", "--cpu-sample-len", "64", "--layers", "2"],
+                         cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+    assert d["e2e"]["value"] == d["value"] and d["cpu_baseline"]["kind"] == "port"
+
+
 @pytest.mark.parametrize("world,par,expect", [(1, "sp", 1048576), (2, "sp", 524288), (8, "sp", 131072),
                                               (8, "dp", 1048576)])
 def test_sequence_split_over_ranks(world, par, expect):
