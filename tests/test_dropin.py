@@ -132,3 +132,23 @@ def test_layer_stash_policies():
                 st.prefetch(i - 1, "cpu")
             assert st.take(i, "cpu") is xs[i]
             assert st.items[i] is None
+
+
+def test_operators_refuse_cpu_tensors():
+    """No CPU path: every operator checks its tensors before any work and raises on host tensors,
+    rather than computing something on the CPU."""
+    import pytest
+    from icml_b200 import ops
+    x = torch.randn(4, 8)
+    w = torch.ones(8)
+    calls = [
+        lambda: ops.rmsnorm_fwd(x, w, 1e-6),
+        lambda: ops.embedding_fwd(torch.zeros(4, dtype=torch.long), torch.randn(10, 8)),
+        lambda: ops.ffn_fwd(x, torch.randn(16, 8), torch.zeros(16), torch.randn(8, 16), torch.zeros(8)),
+        lambda: ops.lm_head_ce_fwd(x, torch.randn(10, 8), torch.zeros(4, dtype=torch.long)),
+        lambda: ops.ssm_fwd(x.view(1, 4, 8), torch.randn(8 + 32, 8), torch.zeros(8 + 32), torch.zeros(8, 16),
+                            torch.ones(8), 1.0),
+    ]
+    for call in calls:
+        with pytest.raises(RuntimeError, match="CUDA tensors only"):
+            call()
