@@ -38,3 +38,19 @@ def test_calls_without_gpu_return_errors_not_crashes():
     rc = L.pgf_rmsnorm_fwd(None, None, None, 4, 16, 1e-6, 0, None)  # rows > 0
     assert rc != 0 and "null" in _lib.last_error()
     assert L.pgf_version() >= 100
+
+
+def test_boundary_rejects_bad_arguments_before_any_cuda_call():
+    """Shape and dtype checks run on the host before any CUDA call, with the reason in
+    pgf_last_error; an empty input is a no-op that touches nothing."""
+    from icml_b200 import _lib
+    L = _lib.lib()
+    dummy = 256  # never dereferenced: each call below returns before touching memory or the GPU
+    assert L.pgf_rmsnorm_fwd(dummy, dummy, dummy, 4, 5000, 1e-6, 0, None) != 0
+    assert "bad shape" in _lib.last_error()
+    assert L.pgf_rmsnorm_fwd(dummy, dummy, dummy, 4, 256, 1e-6, 7, None) != 0
+    assert "dtype" in _lib.last_error()
+    assert L.pgf_rmsnorm_fwd(None, None, None, 0, 256, 1e-6, 0, None) == 0
+    assert L.pgf_embedding_fwd(None, None, None, 0, 10, 8, 0, None) != 0  # null before the empty check
+    assert "null" in _lib.last_error()
+    assert L.pgf_embedding_fwd(dummy, dummy, dummy, 0, 10, 8, 0, None) == 0
